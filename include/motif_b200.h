@@ -1,0 +1,217 @@
+/*
+ * motif_b200 — C ABI of the B200 (sm_100a) kernels behind the Motif Chord inference path.
+ *
+ * Every entry point takes plain device pointers, sizes and element strides, launches on
+ * the given CUDA stream (passed as `void*`, i.e. a `cudaStream_t`; NULL = legacy default
+ * stream), never allocates, never synchronises, and returns an `MB_*` status code.  On a
+ * nonzero code nothing was launched and `motif_b200_last_error()` holds a message.
+ *
+ * Dtype codes: MB_F32 / MB_F16 / MB_BF16 name the element type of the tensors marked
+ * "dtype" in each signature; recurrent states, log-decays, write strengths, `log_n` and
+ * the per-head GGD parameters are always fp32.
+ *
+ * Each declaration cites the reference interface it replaces (paths relative to the
+ * reference project, CodonProject/codon-motif).  The Python shim `motif_b200/_lib.py`
+ * binds these with ctypes and maps the codes onto the reference's exception types
+ * (ValueError for MB_ERR_ARG/SHAPE/DTYPE/ALIGN, NotImplementedError for
+ * MB_ERR_UNSUPPORTED, RuntimeError for MB_ERR_CUDA).
+ */
+#ifndef MOTIF_B200_H
+#define MOTIF_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MB_API __attribute__((visibility("default")))
+#else
+#define MB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MB_OK = 0,
+  MB_ERR_ARG = 1,         /* null pointer or invalid scalar argument */
+  MB_ERR_SHAPE = 2,       /* inconsistent sizes */
+  MB_ERR_DTYPE = 3,       /* unsupported dtype code */
+  MB_ERR_ALIGN = 4,       /* pointer / stride not aligned as required */
+  MB_ERR_UNSUPPORTED = 5, /* valid call this build has no kernel for (e.g. head dim) */
+  MB_ERR_CUDA = 6         /* the CUDA runtime reported an error at launch */
+};
+
+enum { MB_F32 = 0, MB_F16 = 1, MB_BF16 = 2 };
+
+/* Message of the last failing call on this host thread ("" if none). */
+MB_API const char* motif_b200_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+MB_API int motif_b200_abi_version(void);
+
+/* ------------------------------------------------------------------ gated delta rule
+ * Layout of `strides` (elements), [18]:
+ *   q(b,h,l) k(b,h,l) v(b,h,l) o(b,h,l) beta(b,h,l) g(b,h,l)
+ * q,k: [B,H,L,Dk] dtype, last dim contiguous; v,o: [B,H,L,Dv] dtype; beta,g: [B,H,L] fp32;
+ * state_in / state_out: [B,H,Dk,Dv] fp32 contiguous; state_in may be NULL (zeros) and may
+ * equal state_out (updated in place).
+ */
+
+/* Token-by-token recurrence. Replaces recurrent_gated_delta_rule,
+ * motif/ops/gated_deltanet.py:26-59 (Dk <= 128, Dv <= 256). */
+MB_API int motif_b200_gdn_recurrent(const void* q, const void* k, const void* v, const float* beta,
+                             const float* g, const float* state_in, float* state_out, void* o,
+                             int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                             const int64_t* strides, int dtype, void* stream);
+
+/* Chunked form (chunk 64) fused in one kernel per (batch, head): intra-chunk UT transform,
+ * inter-chunk state scan and output combine.  Replaces chunk_gated_delta_rule /
+ * chunk_gated_delta_rule_triton, motif/ops/gated_deltanet.py:287-321 and :796-834
+ * (Dk in {16,32,64}, Dv in {32,64,128}, Dv >= Dk). */
+MB_API int motif_b200_gdn_chunk(const void* q, const void* k, const void* v, const float* beta,
+                         const float* g, const float* state_in, float* state_out, void* o,
+                         int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                         const int64_t* strides, int dtype, void* stream);
+
+/* motif_b200_gdn_chunk with GatedRMSNorm fused into the output: each output row (token l
+ * of head h) becomes rmsnorm(o) * onorm_w * silu(gate) with gate row
+ * gate + (b*L + l)*gate_row_stride + h*gate_head_stride (token-major, Dv contiguous).
+ * Replaces gdn_attn.py:197-209 (delta rule, o.to(dtype), o_norm(cat[o, gate])). */
+MB_API int motif_b200_gdn_chunk_gated(const void* q, const void* k, const void* v, const float* beta,
+                               const float* g, const float* state_in, float* state_out, void* o,
+                               int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                               const int64_t* strides, const void* gate, int64_t gate_row_stride,
+                               int64_t gate_head_stride, const void* onorm_w, float eps, int dtype,
+                               void* stream);
+
+/* ------------------------------------------------------------------ chord attention
+ * Causal softmax attention with the gated geometric-decay bias
+ *   logit(i,j) = (q_i.k_j * scale - alpha_h (|j - (q_start+i) - mu_h| + eps)^beta_h)
+ *                * ssmax_h * log_n[b,i],   j <= q_start + i.
+ * q,out: [B,H,L,D] dtype; k,v: [B,Hkv,S,D] dtype (H % Hkv == 0, head h reads kv head
+ * h / (H/Hkv)); alpha,beta,mu,ssmax: [H] fp32; log_n: [B,L] fp32.
+ * `strides` (elements), [14]: q(b,h,l) k(b,h,s) v(b,h,s) out(b,h,l) log_n(b,l).
+ * `workspace` must hold motif_b200_chord_workspace_bytes(...) bytes (may be 0).
+ * Replaces apply_chord_attention, motif/ops/chord_attention.py:1557-1625 (forward,
+ * no autograd; D <= 128: tensor-core kernel for 16-bit dtypes and D in {16,32,64}, a
+ * CUDA-core kernel otherwise). */
+MB_API int64_t motif_b200_chord_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t L, int64_t S,
+                                         int64_t D, int dtype);
+MB_API int motif_b200_chord_attention(const void* q, const void* k, const void* v, const float* alpha,
+                               const float* beta, const float* mu, const float* ssmax,
+                               const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
+                               int64_t L, int64_t S, int64_t D, int64_t q_start,
+                               float softmax_scale, float eps, const int64_t* strides, int dtype,
+                               void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ attn-res / norms
+ * Depth softmax over n_src (1..8) aligned [B,T,D] sources: logit_s = query . (weight *
+ * rmsnorm(x_s)), h = sum_s softmax_s * x_s.  `src_strides` holds (batch, time) element
+ * strides per source, [2*n_src]; weight, query: [D] dtype.
+ * Replaces attn_res_block / _read_sources, motif/ops/attn_res.py:518-593. */
+MB_API int motif_b200_attn_res(const void* const* sources, int n_src, const int64_t* src_strides,
+                        const void* weight, const void* query, void* out, int64_t out_sb,
+                        int64_t out_st, int64_t B, int64_t T, int64_t D, float eps, int dtype,
+                        void* stream);
+
+/* y = x * rsqrt(mean(x^2) + eps) * w over rows of N.  w may be NULL.
+ * Replaces RMSNorm.forward, motif/ops/rms_norm.py:461-486. */
+MB_API int motif_b200_rms_norm(const void* x, const void* w, void* y, int64_t M, int64_t N,
+                        int64_t x_stride, int64_t y_stride, float eps, int dtype, void* stream);
+
+/* y = rmsnorm(x[:, :N]) * w * silu(x[:, N:2N]) over rows of 2N.  w may be NULL.
+ * Replaces GatedRMSNorm.forward, motif/ops/rms_norm.py:530-553. */
+MB_API int motif_b200_gated_rms_norm(const void* x, const void* w, void* y, int64_t M, int64_t N,
+                              int64_t x_stride, int64_t y_stride, float eps, int dtype,
+                              void* stream);
+
+/* y = x[:, :N] * silu(x[:, N:2N]).  Replaces SwiGLU.forward, motif/ops/swiglu.py:239-253. */
+MB_API int motif_b200_swiglu(const void* x, void* y, int64_t M, int64_t N, int64_t x_stride,
+                      int64_t y_stride, int dtype, void* stream);
+
+/* ------------------------------------------------------------------ fused model kernels
+ * These replace sequences of reference statements inside one layer; each cites them.
+ * Token-major activations: row r = b*T + t, element stride 1 within a row.
+ */
+
+/* Attn-res read fused with the next RMSNorm: from n_src (1..8) aligned sources compute
+ * h (softmax-weighted as motif_b200_attn_res when `query` != NULL, else the plain sum of
+ * the sources), optionally store h to `h_out` (NULL = skip), and store
+ * hn = h * rsqrt(mean(h^2) + eps) (no weight; norm weights are folded into the
+ * following projection) to `hn_out`.  weight/query dtype.
+ * Replaces decoder.py:189-207 (apply_block_attn_res + attn_norm / mlp_norm inputs) and
+ * decoder.py:215 + motif.py:613 (block sum + final norm). */
+MB_API int motif_b200_attn_res_norm(const void* const* sources, int n_src, int64_t src_row_stride,
+                             const void* weight, const void* query, void* h_out,
+                             void* hn_out, int64_t out_row_stride, int64_t rows, int64_t D,
+                             float eps_src, float eps_out, int dtype, void* stream);
+
+/* GDN input preparation over a [B,T] token block.  `proj` rows hold the concatenated
+ * projections [q (H*Dk) | k (H*Dk) | v (H*Dv) | a (H) | b (H) | ...] (row stride
+ * proj_stride).  Computes the causal depthwise conv (taps 4, weights [C][4] for the
+ * C = H*(2Dk+Dv) q|k|v channels) over time with `conv_in` ([B,3,C] previous raw inputs,
+ * NULL = zeros), SiLU, L2-normalised q*Dk^-0.5 and k, beta = sigmoid(b),
+ * g = -exp(A_log) * softplus(a + dt_bias); writes q,k,v token-major ([B*T, H*D]),
+ * beta/g as [B,T,H] fp32, and the last 3 raw inputs to `conv_out` ([B,3,C]; may alias
+ * conv_in).  Replaces gdn_attn.py:116-136 and :183-197. */
+MB_API int motif_b200_gdn_prep(const void* proj, int64_t proj_stride, const void* conv_w,
+                        const void* A_log, const void* dt_bias, const void* conv_in,
+                        void* conv_out, void* q, void* k, void* v, float* beta, float* g,
+                        int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int dtype,
+                        void* stream);
+
+/* One GDN decode step (T == 1) for a whole layer, fused: conv with the carried state,
+ * SiLU, L2 norms, beta/g, the recurrent update of `state` ([B,H,Dk,Dv] fp32, in place)
+ * and the gated RMSNorm of the output with gate columns `gate` (row stride proj_stride),
+ * weight `onorm_w` [Dv]: writes out[B, H*Dv] (row stride out_stride).
+ * Replaces gdn_attn.py:176-209 on the L == 1 path (recurrent_gated_delta_rule). */
+MB_API int motif_b200_gdn_decode(const void* proj, int64_t proj_stride, const void* conv_w,
+                          const void* A_log, const void* dt_bias, void* conv_state,
+                          float* state, const void* gate, const void* onorm_w, void* out,
+                          int64_t out_stride, int64_t B, int64_t H, int64_t Dk, int64_t Dv,
+                          float eps, int dtype, void* stream);
+
+/* Chord input preparation: per token, RMSNorm each q head (weight qn_w [D]) and each k
+ * head (kn_w [D]) of `proj` rows [q (H*D) | k (Hkv*D) | v (Hkv*D) | ...]; writes q
+ * token-major [B*T, H*D] and appends k, v into the cache buffers k_cache/v_cache
+ * ([B,Hkv,cap,D]) at positions pos .. pos+T-1, where pos = *pos_dev if pos_dev != NULL
+ * else pos_host.  Replaces chord_attn.py:256-270 (projections' norms + KVLayerCache.update). */
+MB_API int motif_b200_chord_prep(const void* proj, int64_t proj_stride, const void* qn_w,
+                          const void* kn_w, void* q, void* k_cache, void* v_cache, int64_t cap,
+                          const int32_t* pos_dev, int64_t pos_host, int64_t B, int64_t T,
+                          int64_t H, int64_t Hkv, int64_t D, float eps, int dtype, void* stream);
+
+/* Chord decode/short-query attention over a cache whose length is read on the device:
+ * S = *len_dev (+ T new tokens already appended), q_start = S - T.  Same math as
+ * motif_b200_chord_attention; q token-major [B*T, H*D], out token-major (out_stride).
+ * `workspace` >= motif_b200_chord_decode_workspace_bytes(B,H,T,D,max_splits).
+ * Replaces the L <= 8 use of apply_chord_attention from chord_attn.py:295-313. */
+MB_API int64_t motif_b200_chord_decode_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t D,
+                                                int max_splits);
+MB_API int motif_b200_chord_decode(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                            const int32_t* len_dev, int64_t len_host, const float* alpha,
+                            const float* beta, const float* mu, const float* ssmax,
+                            void* out, int64_t out_stride, int64_t B, int64_t H, int64_t Hkv,
+                            int64_t T, int64_t D, float softmax_scale, float eps,
+                            int max_splits, void* workspace, int64_t workspace_bytes, int dtype,
+                            void* stream);
+
+/* out = a * sigmoid(gate) + m over [rows, N] (row strides given).
+ * Replaces chord_attn.py:254,313 (o_proj(out) * G) + decoder.py:208 (attn + mlp). */
+MB_API int motif_b200_gate_residual(const void* a, int64_t a_stride, const void* gate,
+                             int64_t gate_stride, const void* m, int64_t m_stride, void* out,
+                             int64_t out_stride, int64_t rows, int64_t N, int dtype, void* stream);
+
+/* Greedy next token: ids[r] = argmax over V of logits row r (first maximum), int64.
+ * Replaces ModelOutput.next_token's argmax, motif/model/motif.py:92-98. */
+MB_API int motif_b200_argmax(const void* logits, int64_t rows, int64_t V, int64_t row_stride,
+                      int64_t* ids, int dtype, void* stream);
+
+/* Token embedding gather: out[r] = table[ids[r]] ([V, D] rows), motif/model/motif.py:604. */
+MB_API int motif_b200_embed(const int64_t* ids, const void* table, void* out, int64_t rows, int64_t D,
+                     int64_t V, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOTIF_B200_H */

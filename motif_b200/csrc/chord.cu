@@ -1,0 +1,671 @@
+// Chord attention: causal softmax attention with the gated geometric-decay (GGD) bias
+//   logit(i, j) = (q_i . k_j * scale - alpha_h (|j - (q_start + i) - mu_h| + eps)^beta_h)
+//                 * ssmax_h * log_n[b, i],     visible iff j <= q_start + i
+// (motif/ops/chord_attention.py:145-244 and the eager body of chord_attn.py:316-361).
+//
+// Kernels:
+//   * chord_fwd_mma   — prefill / long-query flash kernel on bf16/fp16 mma.sync.  A CTA owns a
+//     kv head and G of its query heads, so each K/V tile staged in shared memory serves G
+//     heads (the reference re-reads K/V once per query head).  The bias depends on (head,
+//     distance) only, so each warp tabulates it per K/V tile for the (BMQ + 63) distances the
+//     tile spans instead of evaluating pow() per score.
+//   * chord_fwd_simple — fp32 (and any-shape fallback) kernel: one warp per query row, lanes
+//     over keys, online softmax; used for fp32 parity runs.
+//   * chord_decode + chord_merge — split-KV decoding for few new tokens over a long cache,
+//     with the cache length read from device memory (so a captured CUDA graph replays at any
+//     position); one warp per (b, kv head, split) serves all G query heads of the group.
+//   * chord_prep — per-head RMSNorm of q and k and the append of k, v into the cache.
+#include "common.cuh"
+
+namespace mb {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Strides14 {
+  int64_t s[14];  // q(b,h,l) k(b,h,s) v(b,h,s) out(b,h,l) log_n(b,l)
+};
+
+__device__ __forceinline__ float ggd_bias(float alpha, float beta, float mu, float delta, float eps) {
+  // -alpha * (|d - mu| + eps)^beta with d = key - query = -delta
+  return -alpha * powf(fabsf(-delta - mu) + eps, beta);
+}
+
+// ------------------------------------------------------------------ tensor-core prefill
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(128) chord_fwd_mma_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ alpha,
+    const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
+    const float* __restrict__ log_n, T* __restrict__ out, int H, int Hkv, int L, int S, int q_start, float scale,
+    float eps, Strides14 sv) {
+  constexpr int BMQ = 64 / G;  // query positions per CTA
+  constexpr int BN = 64;       // keys per tile
+  constexpr int DS = D + 8;    // smem row stride (elements)
+  constexpr int DW = DS / 2;   // in 32-bit words
+  constexpr int TBL = 80;      // bias table entries per head slot (>= 16 + 63)
+  __shared__ __align__(16) T sQ[64 * DS];
+  __shared__ __align__(16) T sK[2][BN * DS];
+  __shared__ __align__(16) T sV[2][BN * DS];
+  __shared__ float sBias[4][2 * TBL];
+
+  const int64_t* st = sv.s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int GS = H / Hkv;
+  const int groups_per_kv = GS / G;
+  const int kvh = blockIdx.y / groups_per_kv;
+  const int h0 = kvh * GS + (blockIdx.y % groups_per_kv) * G;
+  const int b = blockIdx.z;
+  const int m0q = blockIdx.x * BMQ;
+
+  const T* kb = k + b * st[3] + kvh * st[4];
+  const T* vb = v + b * st[6] + kvh * st[7];
+
+  // rows of this CTA: r -> (head h0 + r / BMQ, position m0q + r % BMQ)
+  auto load_q = [&]() {
+    constexpr int VPR = D / 8;  // 16-byte vectors per row
+    for (int i = tid; i < 64 * VPR; i += 128) {
+      const int r = i / VPR, c = i % VPR;
+      const int hh = h0 + r / BMQ, pos = m0q + r % BMQ;
+      const bool ok = pos < L;
+      const T* src = q + b * st[0] + hh * st[1] + (int64_t)(ok ? pos : 0) * st[2] + c * 8;
+      cp_async16(&sQ[r * DS + c * 8], src, ok);
+    }
+  };
+  auto load_kv = [&](int tile, int stage) {
+    constexpr int VPR = D / 8;
+    const int k0 = tile * BN;
+    for (int i = tid; i < BN * VPR; i += 128) {
+      const int r = i / VPR, c = i % VPR;
+      const int key = k0 + r;
+      const bool ok = key < S;
+      const int64_t kk = ok ? key : 0;
+      cp_async16(&sK[stage][r * DS + c * 8], kb + kk * st[5] + c * 8, ok);
+      cp_async16(&sV[stage][r * DS + c * 8], vb + kk * st[8] + c * 8, ok);
+    }
+  };
+
+  const int last_pos = min(L, m0q + BMQ) - 1;
+  const int kv_end = min(S, q_start + last_pos + 1);  // keys [0, kv_end) are visible to some row
+  const int ntiles = (kv_end + BN - 1) / BN;
+
+  load_q();
+  if (ntiles > 0) load_kv(0, 0);
+  cp_async_commit();
+
+  // per-row constants for rows g8 and g8 + 8 of this warp
+  int rpos[2], rslot[2];
+  float rc[2], ral[2], rbe[2], rmu[2];
+  const int wr0 = warp * 16;
+  const int wpos0 = m0q + (wr0 % BMQ);  // smallest position among this warp's rows
+  const int whead0 = h0 + wr0 / BMQ;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int r = wr0 + g8 + 8 * e;
+    const int hh = h0 + r / BMQ;
+    rpos[e] = m0q + r % BMQ;
+    rslot[e] = hh - whead0;  // 0 or 1 (two heads per warp only when G == 8)
+    const float ln = rpos[e] < L ? log_n[b * st[12] + (int64_t)rpos[e] * st[13]] : 0.f;
+    rc[e] = ssmax[hh] * ln * kLog2e;
+    ral[e] = alpha[hh];
+    rbe[e] = beta[hh];
+    rmu[e] = mu[hh];
+  }
+  const int nslots = (G == 8) ? 2 : 1;
+
+  float o_acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  uint32_t qa[D / 16][4];
+
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int stage = tile & 1;
+    if (tile + 1 < ntiles) load_kv(tile + 1, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (tile == 0) {
+      const uint32_t* Qw = reinterpret_cast<const uint32_t*>(sQ);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        qa[kk][0] = Qw[(wr0 + g8) * DW + kk * 8 + t4];
+        qa[kk][1] = Qw[(wr0 + g8 + 8) * DW + kk * 8 + t4];
+        qa[kk][2] = Qw[(wr0 + g8) * DW + kk * 8 + 4 + t4];
+        qa[kk][3] = Qw[(wr0 + g8 + 8) * DW + kk * 8 + 4 + t4];
+      }
+    }
+    const int k0 = tile * BN;
+    // bias table for this warp: slot s, entry e <-> delta = q_start + wpos0 - k0 + e - 63
+    for (int e = lane; e < nslots * TBL; e += 32) {
+      const int slot = e / TBL, ee = e % TBL;
+      const int hh = whead0 + slot;
+      const float delta = (float)(q_start + wpos0 - k0 + ee - 63);
+      sBias[warp][e] = ggd_bias(alpha[hh], beta[hh], mu[hh], delta, eps);
+    }
+    __syncwarp();
+
+    // S = Q K^T (16 x 64 per warp)
+    float s_acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s_acc[i][0] = s_acc[i][1] = s_acc[i][2] = s_acc[i][3] = 0.f;
+    const uint32_t* Kw = reinterpret_cast<const uint32_t*>(sK[stage]);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        uint32_t bb[2];
+        bb[0] = Kw[(nt * 8 + g8) * DW + kk * 8 + t4];
+        bb[1] = Kw[(nt * 8 + g8) * DW + kk * 8 + 4 + t4];
+        mma_16816<T>(s_acc[nt], qa[kk], bb);
+      }
+    }
+    // logits (log2 units), masking, online softmax
+    const bool need_mask = (k0 + BN > S) || (k0 + BN - 1 > q_start + wpos0);
+    float rmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ri = e >> 1;
+        const int kl = nt * 8 + 2 * t4 + (e & 1);  // key offset in tile
+        const int tb = rslot[ri] * TBL + (rpos[ri] - wpos0) + 63 - kl;
+        float x = (s_acc[nt][e] * scale + sBias[warp][tb]) * rc[ri];
+        if (need_mask) {
+          const int key = k0 + kl;
+          if (key >= S || key > q_start + rpos[ri]) x = -INFINITY;
+        }
+        s_acc[nt][e] = x;
+        rmax[ri] = fmaxf(rmax[ri], x);
+      }
+    }
+    float corr[2], mbase[2];
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      rmax[ri] = fmaxf(rmax[ri], __shfl_xor_sync(0xffffffffu, rmax[ri], 1));
+      rmax[ri] = fmaxf(rmax[ri], __shfl_xor_sync(0xffffffffu, rmax[ri], 2));
+      const float mn = fmaxf(m_run[ri], rmax[ri]);
+      mbase[ri] = mn == -INFINITY ? 0.f : mn;
+      corr[ri] = exp2f(m_run[ri] - mbase[ri]);
+      m_run[ri] = mn;
+      l_run[ri] *= corr[ri];
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o_acc[i][0] *= corr[0];
+      o_acc[i][1] *= corr[0];
+      o_acc[i][2] *= corr[1];
+      o_acc[i][3] *= corr[1];
+    }
+    uint32_t pa[4][4];  // P as A fragments for 4 k16 steps over the 64 keys
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float p0 = exp2f(s_acc[nt][0] - mbase[0]);
+      const float p1 = exp2f(s_acc[nt][1] - mbase[0]);
+      const float p2 = exp2f(s_acc[nt][2] - mbase[1]);
+      const float p3 = exp2f(s_acc[nt][3] - mbase[1]);
+      l_run[0] += p0 + p1;
+      l_run[1] += p2 + p3;
+      const int kk = nt >> 1, hi = nt & 1;
+      pa[kk][hi ? 2 : 0] = pack2<T>(p0, p1);
+      pa[kk][hi ? 3 : 1] = pack2<T>(p2, p3);
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int n0 = 0; n0 < D; n0 += 16) {
+        uint32_t vb4[4];
+        const T* src = &sV[stage][(kk * 16 + (lane & 15)) * DS + n0 + (lane >> 4) * 8];
+        ldmatrix_x4_trans(vb4, src);
+        mma_16816<T>(o_acc[n0 / 8], pa[kk], &vb4[0]);
+        mma_16816<T>(o_acc[n0 / 8 + 1], pa[kk], &vb4[2]);
+      }
+    }
+    __syncthreads();  // stage is overwritten by the prefetch two tiles later
+  }
+  cp_async_wait<0>();
+
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) {
+    l_run[ri] += __shfl_xor_sync(0xffffffffu, l_run[ri], 1);
+    l_run[ri] += __shfl_xor_sync(0xffffffffu, l_run[ri], 2);
+  }
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) {
+    if (rpos[ri] >= L) continue;
+    const int r = wr0 + g8 + 8 * ri;
+    const int hh = h0 + r / BMQ;
+    const float inv = 1.f / fmaxf(l_run[ri], 1e-20f);
+    T* orow = out + b * st[9] + hh * st[10] + (int64_t)rpos[ri] * st[11];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const int c = i * 8 + 2 * t4;
+      *reinterpret_cast<uint32_t*>(&orow[c]) = pack2<T>(o_acc[i][2 * ri] * inv, o_acc[i][2 * ri + 1] * inv);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ simple (fp32 / fallback)
+// One warp per (b, h, query row); lanes own keys in chunks of 32 and the D outputs in slices.
+template <typename T>
+__global__ void __launch_bounds__(128) chord_fwd_simple_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ alpha,
+    const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
+    const float* __restrict__ log_n, T* __restrict__ out, int H, int Hkv, int L, int S, int D, int q_start,
+    float scale, float eps, Strides14 sv) {
+  const int64_t* st = sv.s;
+  extern __shared__ float sq_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;  // over B * H * L
+  const int64_t total = (int64_t)gridDim.y * H * L;
+  (void)total;
+  const int b = blockIdx.y;
+  float* sq = sq_all + warp * D;
+  const bool valid = row < (int64_t)H * L;
+  const int h = valid ? (int)(row / L) : 0;
+  const int i = valid ? (int)(row % L) : 0;
+  const int kvh = h / (H / Hkv);
+  const T* qr = q + b * st[0] + h * st[1] + (int64_t)i * st[2];
+  for (int d = lane; d < D; d += 32) sq[d] = valid ? to_f(qr[d]) : 0.f;
+  __syncwarp();
+  if (!valid) return;
+  const float c = ssmax[h] * log_n[b * st[12] + (int64_t)i * st[13]] * kLog2e;
+  const float al = alpha[h], be = beta[h], m_u = mu[h];
+  const int qa = q_start + i;
+  const int kend = min(S, qa + 1);
+  const T* kb = k + b * st[3] + kvh * st[4];
+  const T* vb = v + b * st[6] + kvh * st[7];
+  constexpr int MAXD = 4;  // D <= 128
+  float o[MAXD] = {0.f, 0.f, 0.f, 0.f};
+  float m = -INFINITY, l = 0.f;
+  for (int j0 = 0; j0 < kend; j0 += 32) {
+    const int j = j0 + lane;
+    float x = -INFINITY;
+    if (j < kend) {
+      const T* kr = kb + (int64_t)j * st[5];
+      float s = 0.f;
+      for (int d = 0; d < D; ++d) s = fmaf(sq[d], to_f(kr[d]), s);
+      x = (s * scale + ggd_bias(al, be, m_u, (float)(qa - j), eps)) * c;
+    }
+    const float cm = warp_max(x);
+    const float mn = fmaxf(m, cm);
+    const float corr = exp2f(m - mn);
+    const float p = exp2f(x - mn);
+    l = l * corr + warp_sum(p);
+#pragma unroll
+    for (int r = 0; r < MAXD; ++r) o[r] *= corr;
+    const int nk = min(32, kend - j0);
+    for (int jj = 0; jj < nk; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);
+      const T* vr = vb + (int64_t)(j0 + jj) * st[8];
+#pragma unroll
+      for (int r = 0; r < MAXD; ++r) {
+        const int d = lane + 32 * r;
+        if (d < D) o[r] = fmaf(pj, to_f(vr[d]), o[r]);
+      }
+    }
+    m = mn;
+  }
+  T* orow = out + b * st[9] + h * st[10] + (int64_t)i * st[11];
+  const float inv = 1.f / fmaxf(l, 1e-20f);
+#pragma unroll
+  for (int r = 0; r < MAXD; ++r) {
+    const int d = lane + 32 * r;
+    if (d < D) orow[d] = from_f<T>(o[r] * inv);
+  }
+}
+
+// ------------------------------------------------------------------ split-KV decode
+// Rows R = G * T (query heads of the group x new tokens), R <= 16.  q token-major [B*T, H*D].
+template <typename T, int D>
+__global__ void __launch_bounds__(128) chord_decode_kernel(
+    const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int64_t cap,
+    const int32_t* __restrict__ len_dev, int len_host, const float* __restrict__ alpha,
+    const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
+    float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps) {
+  constexpr int MAXR = 16;
+  constexpr int DPL = D / 32;  // output dims per lane (D in {32, 64, 128})
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x * 4 + warp;
+  const int bk = blockIdx.y;  // b * Hkv + kvh
+  const int b = bk / Hkv, kvh = bk % Hkv;
+  const int G = H / Hkv;
+  const int R = G * Tn;
+  __shared__ float sq[4][MAXR][D];
+  if (split >= nsplit) return;
+  const int S = len_dev ? *len_dev : len_host;  // cache length including the new tokens
+  const int q_start = S - Tn;
+  // keys handled by this split (multiples of 32)
+  const int per = ((S + nsplit - 1) / nsplit + 31) & ~31;
+  const int kbeg = split * per, kend = min(S, kbeg + per);
+  for (int idx = lane; idx < R * D; idx += 32) {
+    const int r = idx / D, d = idx % D;
+    const int hg = r / Tn, t = r % Tn;
+    sq[warp][r][d] = to_f(q[((int64_t)b * Tn + t) * H * D + (kvh * G + hg) * D + d]);
+  }
+  __syncwarp();
+  float m[MAXR], l[MAXR], o[MAXR][DPL], rc[MAXR];
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[r][i] = 0.f;
+    rc[r] = 0.f;
+    if (r < R) {
+      const int h = kvh * G + r / Tn;
+      const int qa = q_start + r % Tn;
+      rc[r] = ssmax[h] * logf((float)(qa + 1)) * kLog2e;
+    }
+  }
+  const T* kb = kc + ((int64_t)b * Hkv + kvh) * cap * D;
+  const T* vb = vc + ((int64_t)b * Hkv + kvh) * cap * D;
+  for (int j0 = kbeg; j0 < kend; j0 += 32) {
+    const int j = j0 + lane;
+    float kr[D];
+    if (j < kend) {
+      const uint4* src = reinterpret_cast<const uint4*>(kb + (int64_t)j * D);
+#pragma unroll
+      for (int c = 0; c < D * (int)sizeof(T) / 16; ++c) {
+        uint4 raw = src[c];
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int x = 0; x < 16 / (int)sizeof(T); ++x) kr[c * (16 / sizeof(T)) + x] = to_f(e[x]);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < D; ++d) kr[d] = 0.f;
+    }
+    float p[MAXR];
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) {
+      if (r >= R) break;
+      const int h = kvh * G + r / Tn;
+      const int qa = q_start + r % Tn;
+      float x = -INFINITY;
+      if (j < kend && j <= qa) {
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) s = fmaf(sq[warp][r][d], kr[d], s);
+        x = (s * scale + ggd_bias(alpha[h], beta[h], mu[h], (float)(qa - j), eps)) * rc[r];
+      }
+      const float cm = warp_max(x);
+      const float mn = fmaxf(m[r], cm);
+      const float mb = mn == -INFINITY ? 0.f : mn;
+      const float corr = exp2f(m[r] - mb);
+      p[r] = exp2f(x - mb);
+      l[r] = l[r] * corr + p[r];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) o[r][i] *= corr;
+      m[r] = mn;
+    }
+    const int nk = min(32, kend - j0);
+    for (int jj = 0; jj < nk; ++jj) {
+      const T* vr = vb + (int64_t)(j0 + jj) * D;
+      float vv[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) vv[i] = to_f(vr[lane + 32 * i]);
+#pragma unroll
+      for (int r = 0; r < MAXR; ++r) {
+        if (r >= R) break;
+        const float pj = __shfl_sync(0xffffffffu, p[r], jj);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) o[r][i] = fmaf(pj, vv[i], o[r][i]);
+      }
+    }
+  }
+  // partials: ws[((split * B + b) * H + h) * Tn + t][D + 2] = (o[0..D), m, l)
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) {
+    if (r >= R) break;
+    const float lt = warp_sum(l[r]);
+    const int h = kvh * G + r / Tn, t = r % Tn;
+    float* dst = ws + ((((int64_t)split * B + b) * H + h) * Tn + t) * (D + 2);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) dst[lane + 32 * i] = o[r][i];
+    if (lane == 0) {
+      dst[D] = m[r];
+      dst[D + 1] = lt;
+    }
+  }
+}
+
+template <typename T>
+__global__ void chord_merge_kernel(const float* __restrict__ ws, T* __restrict__ out, int64_t os, int B, int H,
+                                   int Tn, int D, int nsplit) {
+  const int64_t row = blockIdx.x;  // (b * Tn + t) * H + h
+  const int h = (int)(row % H);
+  const int64_t bt = row / H;
+  const int t = (int)(bt % Tn), b = (int)(bt / Tn);
+  float mmax = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) {
+    const float* src = ws + ((((int64_t)s * B + b) * H + h) * Tn + t) * (D + 2);
+    mmax = fmaxf(mmax, src[D]);
+  }
+  const float mb = mmax == -INFINITY ? 0.f : mmax;
+  float den = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float* src = ws + ((((int64_t)s * B + b) * H + h) * Tn + t) * (D + 2);
+    den += src[D + 1] * exp2f(src[D] - mb);
+  }
+  const float inv = 1.f / fmaxf(den, 1e-20f);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float* src = ws + ((((int64_t)s * B + b) * H + h) * Tn + t) * (D + 2);
+      acc += src[d] * exp2f(src[D] - mb);
+    }
+    out[((int64_t)b * Tn + t) * os + (int64_t)h * D + d] = from_f<T>(acc * inv);
+  }
+}
+
+// ------------------------------------------------------------------ prep (q/k norms + append)
+template <typename T>
+__global__ void chord_prep_kernel(const T* __restrict__ proj, int64_t ps, const T* __restrict__ qn_w,
+                                  const T* __restrict__ kn_w, T* __restrict__ qo, T* __restrict__ kc,
+                                  T* __restrict__ vc, int64_t cap, const int32_t* __restrict__ pos_dev,
+                                  int64_t pos_host, int64_t rows, int Tn, int H, int Hkv, int D, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int slots = H + 2 * Hkv;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (wid >= rows * slots) return;
+  const int64_t tok = wid / slots;
+  const int slot = (int)(wid % slots);
+  const int b = (int)(tok / Tn), t = (int)(tok % Tn);
+  const int64_t pos = (pos_dev ? (int64_t)*pos_dev : pos_host) + t;
+  const T* src = proj + tok * ps + (int64_t)slot * D;  // q heads, then k heads, then v heads
+  if (slot >= H + Hkv) {  // value: plain copy into the cache
+    const int kvh = slot - H - Hkv;
+    T* dst = vc + (((int64_t)b * Hkv + kvh) * cap + pos) * D;
+    for (int d = lane; d < D; d += 32) dst[d] = src[d];
+    return;
+  }
+  const T* w = slot < H ? qn_w : kn_w;
+  float ss = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float x = to_f(src[d]);
+    ss += x * x;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)D + eps);
+  T* dst = slot < H ? qo + tok * H * D + (int64_t)slot * D
+                    : kc + (((int64_t)b * Hkv + (slot - H)) * cap + pos) * D;
+  for (int d = lane; d < D; d += 32) {
+    const float y = to_f(from_f<T>(to_f(src[d]) * r));
+    dst[d] = from_f<T>(y * to_f(w[d]));
+  }
+}
+
+template <typename T, int D>
+int launch_mma_d(int G, const void* q, const void* k, const void* v, const float* alpha, const float* beta,
+                 const float* mu, const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
+                 int64_t L, int64_t S, int64_t q_start, float scale, float eps, const Strides14& sv, cudaStream_t st) {
+  const int GS = (int)(H / Hkv);
+  auto go = [&](auto gc) {
+    constexpr int GG = decltype(gc)::value;
+    dim3 grid((unsigned)((L + 64 / GG - 1) / (64 / GG)), (unsigned)(Hkv * (GS / GG)), (unsigned)B);
+    chord_fwd_mma_kernel<T, D, GG><<<grid, 128, 0, st>>>((const T*)q, (const T*)k, (const T*)v, alpha, beta, mu,
+                                                         ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L, (int)S,
+                                                         (int)q_start, scale, eps, sv);
+    return check_launch("chord_fwd_mma");
+  };
+  switch (G) {
+    case 8: return go(std::integral_constant<int, 8>{});
+    case 4: return go(std::integral_constant<int, 4>{});
+    case 2: return go(std::integral_constant<int, 2>{});
+    default: return go(std::integral_constant<int, 1>{});
+  }
+}
+
+template <typename T>
+int launch_mma(int64_t D, int G, const void* q, const void* k, const void* v, const float* alpha, const float* beta,
+               const float* mu, const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
+               int64_t L, int64_t S, int64_t q_start, float scale, float eps, const Strides14& sv, cudaStream_t st) {
+  switch (D) {
+    case 16: return launch_mma_d<T, 16>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, sv, st);
+    case 32: return launch_mma_d<T, 32>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, sv, st);
+    case 64: return launch_mma_d<T, 64>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, sv, st);
+    default: return set_error(MB_ERR_UNSUPPORTED, "chord: head dim %lld", (long long)D);
+  }
+}
+
+template <typename T>
+int launch_simple(const void* q, const void* k, const void* v, const float* alpha, const float* beta, const float* mu,
+                  const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L,
+                  int64_t S, int64_t D, int64_t q_start, float scale, float eps, const Strides14& sv,
+                  cudaStream_t st) {
+  dim3 grid((unsigned)((H * L + 3) / 4), (unsigned)B);
+  chord_fwd_simple_kernel<T><<<grid, 128, 4 * D * sizeof(float), st>>>(
+      (const T*)q, (const T*)k, (const T*)v, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
+      (int)S, (int)D, (int)q_start, scale, eps, sv);
+  return check_launch("chord_fwd_simple");
+}
+
+template <typename F>
+int dispatch_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case MB_F32: return f(float{});
+    case MB_F16: return f(__half{});
+    case MB_BF16: return f(__nv_bfloat16{});
+    default: return set_error(MB_ERR_DTYPE, "unsupported dtype code %d", dtype);
+  }
+}
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int64_t motif_b200_chord_workspace_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int) {
+  return 0;
+}
+
+extern "C" int motif_b200_chord_attention(const void* q, const void* k, const void* v, const float* alpha,
+                                          const float* beta, const float* mu, const float* ssmax, const float* log_n,
+                                          void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L, int64_t S,
+                                          int64_t D, int64_t q_start, float scale, float eps, const int64_t* strides,
+                                          int dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  MB_REQUIRE(strides, MB_ERR_ARG, "chord: null strides");
+  MB_REQUIRE(B >= 0 && B < 65536 && H > 0 && Hkv > 0 && L >= 0 && S >= 0 && D > 0, MB_ERR_SHAPE,
+             "chord: bad shape");
+  MB_REQUIRE(H % Hkv == 0, MB_ERR_SHAPE, "chord: num_heads %lld not divisible by num_kv_heads %lld", (long long)H,
+             (long long)Hkv);
+  MB_REQUIRE(q_start >= 0 && L < (1LL << 30) && S < (1LL << 30), MB_ERR_SHAPE, "chord: bad q_start / lengths");
+  MB_REQUIRE(D <= 128, MB_ERR_UNSUPPORTED, "chord: head dim %lld > 128", (long long)D);
+  if (B == 0 || L == 0) return MB_OK;
+  MB_REQUIRE(q && k && v && alpha && beta && mu && ssmax && log_n && out, MB_ERR_ARG, "chord: null pointer");
+  Strides14 sv;
+  for (int i = 0; i < 14; ++i) sv.s[i] = strides[i];
+  cudaStream_t st = (cudaStream_t)stream;
+  const int GS = (int)(H / Hkv);
+  int G = 1;
+  for (int c : {8, 4, 2})
+    if (GS % c == 0) {
+      G = c;
+      break;
+    }
+  bool aligned = ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 == 0;
+  for (int i = 0; i < 9; ++i) aligned = aligned && strides[i] % 8 == 0;
+  aligned = aligned && (strides[9] % 2 == 0) && (strides[10] % 2 == 0) && (strides[11] % 2 == 0) &&
+            ((uintptr_t)out % 4 == 0);
+  const bool mma_ok = dtype != MB_F32 && aligned && (D == 16 || D == 32 || D == 64);
+  return dispatch_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    if constexpr (sizeof(T) == 2) {
+      if (mma_ok)
+        return launch_mma<T>(D, G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps,
+                             sv, st);
+    }
+    return launch_simple<T>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, D, q_start, scale, eps,
+                            sv, st);
+  });
+}
+
+extern "C" int64_t motif_b200_chord_decode_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t D,
+                                                           int max_splits) {
+  return (int64_t)max_splits * B * H * T * (D + 2) * (int64_t)sizeof(float);
+}
+
+extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                                       const int32_t* len_dev, int64_t len_host, const float* alpha,
+                                       const float* beta, const float* mu, const float* ssmax, void* out,
+                                       int64_t out_stride, int64_t B, int64_t H, int64_t Hkv, int64_t T, int64_t D,
+                                       float scale, float eps, int max_splits, void* workspace,
+                                       int64_t workspace_bytes, int dtype, void* stream) {
+  MB_REQUIRE(q && k_cache && v_cache && alpha && beta && mu && ssmax && out && workspace, MB_ERR_ARG,
+             "chord_decode: null pointer");
+  MB_REQUIRE(B > 0 && B < 65536 && H > 0 && Hkv > 0 && H % Hkv == 0 && T > 0 && cap > 0, MB_ERR_SHAPE,
+             "chord_decode: bad shape");
+  MB_REQUIRE((H / Hkv) * T <= 16, MB_ERR_UNSUPPORTED, "chord_decode: (H/Hkv)*T = %lld > 16",
+             (long long)((H / Hkv) * T));
+  MB_REQUIRE(max_splits >= 1 && max_splits <= 1024, MB_ERR_ARG, "chord_decode: max_splits %d", max_splits);
+  MB_REQUIRE(workspace_bytes >= motif_b200_chord_decode_workspace_bytes(B, H, T, D, max_splits), MB_ERR_ARG,
+             "chord_decode: workspace too small");
+  MB_REQUIRE(len_dev != nullptr || (len_host >= T && len_host <= cap), MB_ERR_ARG, "chord_decode: bad length");
+  MB_REQUIRE(((uintptr_t)k_cache | (uintptr_t)v_cache) % 16 == 0, MB_ERR_ALIGN, "chord_decode: cache alignment");
+  cudaStream_t st = (cudaStream_t)stream;
+  return dispatch_dtype(dtype, [&](auto t) {
+    using Tt = decltype(t);
+    auto go = [&](auto dc) {
+      constexpr int DD = decltype(dc)::value;
+      dim3 grid((unsigned)((max_splits + 3) / 4), (unsigned)(B * Hkv));
+      chord_decode_kernel<Tt, DD><<<grid, 128, 0, st>>>((const Tt*)q, (const Tt*)k_cache, (const Tt*)v_cache, cap,
+                                                        len_dev, (int)len_host, alpha, beta, mu, ssmax,
+                                                        (float*)workspace, (int)B, (int)H, (int)Hkv, (int)T,
+                                                        max_splits, scale, eps);
+      int rc = check_launch("chord_decode");
+      if (rc) return rc;
+      chord_merge_kernel<Tt><<<(unsigned)(B * T * H), 64, 0, st>>>((const float*)workspace, (Tt*)out, out_stride,
+                                                                    (int)B, (int)H, (int)T, (int)DD, max_splits);
+      return check_launch("chord_merge");
+    };
+    switch (D) {
+      case 32: return go(std::integral_constant<int, 32>{});
+      case 64: return go(std::integral_constant<int, 64>{});
+      default: return set_error(MB_ERR_UNSUPPORTED, "chord_decode: head dim %lld", (long long)D);
+    }
+  });
+}
+
+extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, const void* qn_w, const void* kn_w,
+                                     void* q, void* k_cache, void* v_cache, int64_t cap, const int32_t* pos_dev,
+                                     int64_t pos_host, int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t D,
+                                     float eps, int dtype, void* stream) {
+  MB_REQUIRE(proj && qn_w && kn_w && q && k_cache && v_cache, MB_ERR_ARG, "chord_prep: null pointer");
+  MB_REQUIRE(B >= 0 && T >= 0 && H > 0 && Hkv > 0 && D > 0, MB_ERR_SHAPE, "chord_prep: bad shape");
+  MB_REQUIRE(pos_dev != nullptr || pos_host + T <= cap, MB_ERR_SHAPE, "chord_prep: cache capacity %lld exceeded",
+             (long long)cap);
+  const int64_t rows = B * T;
+  if (rows == 0) return MB_OK;
+  return dispatch_dtype(dtype, [&](auto t) {
+    using Tt = decltype(t);
+    const int64_t warps = rows * (H + 2 * Hkv);
+    chord_prep_kernel<Tt><<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+        (const Tt*)proj, proj_stride, (const Tt*)qn_w, (const Tt*)kn_w, (Tt*)q, (Tt*)k_cache, (Tt*)v_cache, cap,
+        pos_dev, pos_host, rows, (int)T, (int)H, (int)Hkv, (int)D, eps);
+    return check_launch("chord_prep");
+  });
+}

@@ -1,0 +1,391 @@
+// Gated DeltaNet kernels other than the chunked prefill:
+//   * the token-by-token recurrence (op level, any L),
+//   * the fused single-token decode step of a whole GDN layer (model level),
+//   * the prefill input preparation (causal conv + SiLU + L2 norms + beta/g).
+//
+// State layout: S[b][h] is a row-major [Dk][Dv] fp32 block.  The recurrent kernels give
+// one CTA to each (b, h) and one thread to each value column j, which holds column j of
+// S in registers, so every step reads and writes S exactly once, coalesced across j.
+#include "common.cuh"
+
+namespace mb {
+namespace {
+
+// Element strides q(b,h,l) k(b,h,l) v(b,h,l) o(b,h,l) beta(b,h,l) g(b,h,l), by value.
+struct Strides18 {
+  int64_t s[18];
+};
+
+// --------------------------------------------------------------- recurrence (op level)
+// motif/ops/gated_deltanet.py:26-59.  blockDim.x == Dv (<= 256); DK <= 128.
+template <typename T, int DK>
+__global__ void __launch_bounds__(256) gdn_recurrent_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const float* __restrict__ beta, const float* __restrict__ g, const float* __restrict__ s_in,
+    float* __restrict__ s_out, T* __restrict__ o, int H, int L, int Dv, Strides18 sv) {
+  const int64_t* st = sv.s;
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const int j = threadIdx.x;
+  __shared__ float sq[DK], sk[DK];
+  float S[DK];
+  const size_t sbase = (size_t)bh * DK * Dv;
+#pragma unroll
+  for (int i = 0; i < DK; ++i) S[i] = s_in ? s_in[sbase + (size_t)i * Dv + j] : 0.f;
+  const int64_t qb = b * st[0] + h * st[1], kb = b * st[3] + h * st[4], vb = b * st[6] + h * st[7];
+  const int64_t ob = b * st[9] + h * st[10], bb = b * st[12] + h * st[13], gb = b * st[15] + h * st[16];
+  for (int t = 0; t < L; ++t) {
+    __syncthreads();
+    for (int i = j; i < DK; i += blockDim.x) {
+      sq[i] = to_f(q[qb + t * st[2] + i]);
+      sk[i] = to_f(k[kb + t * st[5] + i]);
+    }
+    __syncthreads();
+    const float e = expf(g[gb + t * st[17]]);
+    const float bt = beta[bb + t * st[14]];
+    float vo = 0.f;
+#pragma unroll
+    for (int i = 0; i < DK; ++i) {
+      S[i] *= e;
+      vo = fmaf(sk[i], S[i], vo);
+    }
+    const float delta = bt * (to_f(v[vb + t * st[8] + j]) - vo);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < DK; ++i) {
+      S[i] = fmaf(sk[i], delta, S[i]);
+      acc = fmaf(sq[i], S[i], acc);
+    }
+    o[ob + t * st[11] + j] = from_f<T>(acc);
+  }
+#pragma unroll
+  for (int i = 0; i < DK; ++i) s_out[sbase + (size_t)i * Dv + j] = S[i];
+}
+
+// ------------------------------------------------------------ block reduction helper
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  return s;
+}
+
+// ------------------------------------------------------- fused decode step (model level)
+// gdn_attn.py:176-209 at L == 1: conv (carried state) + SiLU, F.normalize(q)*Dk^-0.5,
+// F.normalize(k), beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias), the recurrent
+// step on S, then o_norm(cat[o, gate]) = rmsnorm(o) * w * silu(gate).
+// One CTA per (b, h), DV threads; thread j owns value column j (and q/k channel j < DK).
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(DV) gdn_decode_kernel(
+    const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
+    const T* __restrict__ dt_bias, T* __restrict__ conv_state, float* __restrict__ state,
+    const T* __restrict__ gate, const T* __restrict__ onw, T* __restrict__ out, int64_t os, int H,
+    float eps) {
+  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  const int j = threadIdx.x;
+  const int C = H * (2 * DK + DV);
+  const T* row = proj + (int64_t)b * ps;
+  T* cs = conv_state + (int64_t)b * 3 * C;
+  __shared__ float sq[DK], sk[DK], red[DV / 32];
+
+  auto conv = [&](int c) -> float {
+    const float x = to_f(row[c]);
+    const float s0 = to_f(cs[c]), s1 = to_f(cs[C + c]), s2 = to_f(cs[2 * C + c]);
+    const T* w = conv_w + (int64_t)c * 4;
+    float y = to_f(w[0]) * s0 + to_f(w[1]) * s1 + to_f(w[2]) * s2 + to_f(w[3]) * x;
+    cs[c] = from_f<T>(s1);
+    cs[C + c] = from_f<T>(s2);
+    cs[2 * C + c] = from_f<T>(x);
+    return siluf_(to_f(from_f<T>(y)));
+  };
+  float qv = 0.f, kv = 0.f;
+  if (j < DK) {
+    qv = conv(h * DK + j);
+    kv = conv(H * DK + h * DK + j);
+  }
+  const float vv = conv(2 * H * DK + h * DV + j);
+  const float qn = block_sum<DV>(qv * qv, red);
+  const float kn = block_sum<DV>(kv * kv, red);
+  if (j < DK) {
+    sq[j] = qv / fmaxf(sqrtf(qn), 1e-12f) * rsqrtf((float)DK);
+    sk[j] = kv / fmaxf(sqrtf(kn), 1e-12f);
+  }
+  const float a = to_f(row[2 * H * DK + H * DV + h]);
+  const float bsc = to_f(row[2 * H * DK + H * DV + H + h]);
+  const float bt = sigmoidf_(bsc);
+  const float gg = -expf(to_f(A_log[h])) * softplusf_(a + to_f(dt_bias[h]));
+  __syncthreads();
+  float* S = state + ((int64_t)b * H + h) * DK * DV;
+  float Sr[DK];
+  const float e = expf(gg);
+  float vo = 0.f;
+#pragma unroll
+  for (int i = 0; i < DK; ++i) {
+    Sr[i] = S[i * DV + j] * e;
+    vo = fmaf(sk[i], Sr[i], vo);
+  }
+  const float delta = bt * (vv - vo);
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < DK; ++i) {
+    Sr[i] = fmaf(sk[i], delta, Sr[i]);
+    acc = fmaf(sq[i], Sr[i], acc);
+    S[i * DV + j] = Sr[i];
+  }
+  // o.to(dtype) then GatedRMSNorm (rms_norm.py:547-553).
+  const float ov = to_f(from_f<T>(acc));
+  const float ss = block_sum<DV>(ov * ov, red);
+  const float r = rsqrtf(ss / (float)DV + eps);
+  float y = to_f(from_f<T>(ov * r));
+  y = to_f(from_f<T>(y * to_f(onw[j])));
+  const float gt = to_f(gate[(int64_t)b * ps + h * DV + j]);
+  out[(int64_t)b * os + h * DV + j] = from_f<T>(y * to_f(from_f<T>(siluf_(gt))));
+}
+
+// ------------------------------------------------------------- prefill preparation
+// gdn_attn.py:116-136 (conv over time with the carried state, SiLU) and :187-197.
+// One warp per (b, head, block of TB tokens); lanes own channels and keep a sliding window
+// of the last three raw inputs in registers, so each raw element is read once.
+template <typename T, int DK, int DV, int TB>
+__global__ void __launch_bounds__(128) gdn_prep_kernel(
+    const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
+    const T* __restrict__ dt_bias, const T* __restrict__ conv_in, T* __restrict__ conv_out,
+    T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, float* __restrict__ beta,
+    float* __restrict__ gout, int Tn, int H) {
+  constexpr int QPL = (DK + 31) / 32, VPL = (DV + 31) / 32;
+  const int lane = threadIdx.x & 31;
+  const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nblk = (Tn + TB - 1) / TB;
+  const int b = blockIdx.y;
+  const int h = warp / nblk, tb = warp % nblk;
+  if (h >= H) return;
+  const int t0 = tb * TB;
+  const int C = H * (2 * DK + DV);
+  const T* P = proj + (int64_t)b * Tn * ps;
+  // channel ids owned by this lane (-1 = none)
+  int cq[QPL], ck[QPL], cv[VPL];
+  float wq[QPL][4], wk[QPL][4], wv[VPL][4];
+  float hq[QPL][3], hk[QPL][3], hv[VPL][3];
+  auto load_w = [&](int c, float* w) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = c >= 0 ? to_f(conv_w[(int64_t)c * 4 + i]) : 0.f;
+  };
+  auto raw = [&](int c, int tau) -> float {  // raw input of channel c at time tau (may be < 0)
+    if (c < 0) return 0.f;
+    if (tau >= 0) return to_f(P[(int64_t)tau * ps + c]);
+    return conv_in ? to_f(conv_in[((int64_t)b * 3 + (3 + tau)) * C + c]) : 0.f;
+  };
+#pragma unroll
+  for (int r = 0; r < QPL; ++r) {
+    const int d = lane + 32 * r;
+    cq[r] = d < DK ? h * DK + d : -1;
+    ck[r] = d < DK ? H * DK + h * DK + d : -1;
+    load_w(cq[r], wq[r]);
+    load_w(ck[r], wk[r]);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      hq[r][i] = raw(cq[r], t0 - 3 + i);
+      hk[r][i] = raw(ck[r], t0 - 3 + i);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < VPL; ++r) {
+    const int d = lane + 32 * r;
+    cv[r] = d < DV ? 2 * H * DK + h * DV + d : -1;
+    load_w(cv[r], wv[r]);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) hv[r][i] = raw(cv[r], t0 - 3 + i);
+  }
+  const float qscale = rsqrtf((float)DK);
+  const float Aexp = -expf(to_f(A_log[h]));
+  const float dtb = to_f(dt_bias[h]);
+  const int t1 = min(t0 + TB, Tn);
+  for (int t = t0; t < t1; ++t) {
+    const T* row = P + (int64_t)t * ps;
+    float yq[QPL], yk[QPL], yv[VPL];
+    float nq = 0.f, nk = 0.f;
+#pragma unroll
+    for (int r = 0; r < QPL; ++r) {
+      const float xq = cq[r] >= 0 ? to_f(row[cq[r]]) : 0.f;
+      const float xk = ck[r] >= 0 ? to_f(row[ck[r]]) : 0.f;
+      float a = wq[r][0] * hq[r][0] + wq[r][1] * hq[r][1] + wq[r][2] * hq[r][2] + wq[r][3] * xq;
+      float c = wk[r][0] * hk[r][0] + wk[r][1] * hk[r][1] + wk[r][2] * hk[r][2] + wk[r][3] * xk;
+      hq[r][0] = hq[r][1]; hq[r][1] = hq[r][2]; hq[r][2] = xq;
+      hk[r][0] = hk[r][1]; hk[r][1] = hk[r][2]; hk[r][2] = xk;
+      yq[r] = cq[r] >= 0 ? to_f(from_f<T>(siluf_(to_f(from_f<T>(a))))) : 0.f;
+      yk[r] = ck[r] >= 0 ? to_f(from_f<T>(siluf_(to_f(from_f<T>(c))))) : 0.f;
+      nq += yq[r] * yq[r];
+      nk += yk[r] * yk[r];
+    }
+#pragma unroll
+    for (int r = 0; r < VPL; ++r) {
+      const float xv = cv[r] >= 0 ? to_f(row[cv[r]]) : 0.f;
+      float a = wv[r][0] * hv[r][0] + wv[r][1] * hv[r][1] + wv[r][2] * hv[r][2] + wv[r][3] * xv;
+      hv[r][0] = hv[r][1]; hv[r][1] = hv[r][2]; hv[r][2] = xv;
+      yv[r] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
+    }
+    nq = warp_sum(nq);
+    nk = warp_sum(nk);
+    const float iq = qscale / fmaxf(sqrtf(nq), 1e-12f);
+    const float ik = 1.f / fmaxf(sqrtf(nk), 1e-12f);
+    const int64_t tok = (int64_t)b * Tn + t;
+#pragma unroll
+    for (int r = 0; r < QPL; ++r) {
+      const int d = lane + 32 * r;
+      if (d < DK) {
+        qo[tok * H * DK + h * DK + d] = from_f<T>(yq[r] * iq);
+        ko[tok * H * DK + h * DK + d] = from_f<T>(yk[r] * ik);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < VPL; ++r) {
+      const int d = lane + 32 * r;
+      if (d < DV) vo[tok * H * DV + h * DV + d] = from_f<T>(yv[r]);
+    }
+    if (lane == 0) {
+      const float a = to_f(row[2 * H * DK + H * DV + h]);
+      const float bb = to_f(row[2 * H * DK + H * DV + H + h]);
+      beta[tok * H + h] = to_f(from_f<T>(sigmoidf_(bb)));
+      gout[tok * H + h] = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(a + dtb)))))));
+    }
+  }
+  // The last token block writes the new conv state (raw inputs at T-3 .. T-1).
+  if (t1 == Tn && conv_out) {
+    T* co = conv_out + (int64_t)b * 3 * C;
+#pragma unroll
+    for (int r = 0; r < QPL; ++r)
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        if (cq[r] >= 0) co[(int64_t)i * C + cq[r]] = from_f<T>(hq[r][i]);
+        if (ck[r] >= 0) co[(int64_t)i * C + ck[r]] = from_f<T>(hk[r][i]);
+      }
+#pragma unroll
+    for (int r = 0; r < VPL; ++r)
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+        if (cv[r] >= 0) co[(int64_t)i * C + cv[r]] = from_f<T>(hv[r][i]);
+  }
+}
+
+template <typename F>
+int dispatch_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case MB_F32: return f(float{});
+    case MB_F16: return f(__half{});
+    case MB_BF16: return f(__nv_bfloat16{});
+    default: return set_error(MB_ERR_DTYPE, "unsupported dtype code %d", dtype);
+  }
+}
+
+template <typename F>
+int dispatch_dk(int64_t dk, F&& f) {
+  switch (dk) {
+    case 16: return f(std::integral_constant<int, 16>{});
+    case 32: return f(std::integral_constant<int, 32>{});
+    case 64: return f(std::integral_constant<int, 64>{});
+    case 128: return f(std::integral_constant<int, 128>{});
+    default: return set_error(MB_ERR_UNSUPPORTED, "head_k_dim %lld not supported (16/32/64/128)", (long long)dk);
+  }
+}
+
+template <typename F>
+int dispatch_dv(int64_t dv, F&& f) {
+  switch (dv) {
+    case 32: return f(std::integral_constant<int, 32>{});
+    case 64: return f(std::integral_constant<int, 64>{});
+    case 128: return f(std::integral_constant<int, 128>{});
+    case 256: return f(std::integral_constant<int, 256>{});
+    default: return set_error(MB_ERR_UNSUPPORTED, "value head dim %lld not supported (32/64/128/256)", (long long)dv);
+  }
+}
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int motif_b200_gdn_recurrent(const void* q, const void* k, const void* v, const float* beta,
+                                        const float* g, const float* state_in, float* state_out, void* o,
+                                        int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                                        const int64_t* strides, int dtype, void* stream) {
+  MB_REQUIRE(state_out && strides, MB_ERR_ARG, "gdn_recurrent: null state_out/strides");
+  MB_REQUIRE(L == 0 || (q && k && v && beta && g && o), MB_ERR_ARG, "gdn_recurrent: null input");
+  MB_REQUIRE(B >= 0 && H > 0 && L >= 0 && L < 2147483647LL && B * H < 2147483647LL, MB_ERR_SHAPE,
+             "gdn_recurrent: bad shape");
+  MB_REQUIRE(Dv >= 32 && Dv <= 256 && Dv % 32 == 0, MB_ERR_UNSUPPORTED,
+             "gdn_recurrent: value dim %lld must be a multiple of 32 in [32, 256]", (long long)Dv);
+  if (B == 0) return MB_OK;
+  Strides18 sv;
+  for (int i = 0; i < 18; ++i) sv.s[i] = strides[i];
+  return dispatch_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return dispatch_dk(Dk, [&](auto dkc) {
+      constexpr int DK = decltype(dkc)::value;
+      gdn_recurrent_kernel<T, DK><<<(unsigned)(B * H), (unsigned)Dv, 0, (cudaStream_t)stream>>>(
+          (const T*)q, (const T*)k, (const T*)v, beta, g, state_in, state_out, (T*)o, (int)H, (int)L,
+          (int)Dv, sv);
+      return check_launch("gdn_recurrent");
+    });
+  });
+}
+
+extern "C" int motif_b200_gdn_decode(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
+                                     const void* dt_bias, void* conv_state, float* state, const void* gate,
+                                     const void* onorm_w, void* out, int64_t os, int64_t B, int64_t H,
+                                     int64_t Dk, int64_t Dv, float eps, int dtype, void* stream) {
+  MB_REQUIRE(proj && conv_w && A_log && dt_bias && conv_state && state && gate && onorm_w && out,
+             MB_ERR_ARG, "gdn_decode: null pointer");
+  MB_REQUIRE(B >= 0 && H > 0 && B * H < 2147483647LL, MB_ERR_SHAPE, "gdn_decode: bad shape");
+  MB_REQUIRE(Dv >= Dk, MB_ERR_UNSUPPORTED, "gdn_decode: needs Dv >= Dk");
+  if (B == 0) return MB_OK;
+  return dispatch_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return dispatch_dk(Dk, [&](auto dkc) {
+      constexpr int DK = decltype(dkc)::value;
+      return dispatch_dv(Dv, [&](auto dvc) {
+        constexpr int DV = decltype(dvc)::value;
+        if constexpr (DV < DK) {
+          return set_error(MB_ERR_UNSUPPORTED, "gdn_decode: needs Dv >= Dk");
+        } else {
+          gdn_decode_kernel<T, DK, DV><<<(unsigned)(B * H), DV, 0, (cudaStream_t)stream>>>(
+              (const T*)proj, ps, (const T*)conv_w, (const T*)A_log, (const T*)dt_bias, (T*)conv_state,
+              state, (const T*)gate, (const T*)onorm_w, (T*)out, os, (int)H, eps);
+          return check_launch("gdn_decode");
+        }
+      });
+    });
+  });
+}
+
+extern "C" int motif_b200_gdn_prep(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
+                                   const void* dt_bias, const void* conv_in, void* conv_out, void* q, void* k,
+                                   void* v, float* beta, float* g, int64_t B, int64_t T, int64_t H, int64_t Dk,
+                                   int64_t Dv, int dtype, void* stream) {
+  MB_REQUIRE(proj && conv_w && A_log && dt_bias && q && k && v && beta && g, MB_ERR_ARG,
+             "gdn_prep: null pointer");
+  MB_REQUIRE(conv_out == nullptr || conv_out != conv_in, MB_ERR_ARG, "gdn_prep: conv_out must not alias conv_in");
+  MB_REQUIRE(B >= 0 && B < 65536 && T >= 0 && T < (1LL << 30) && H > 0, MB_ERR_SHAPE, "gdn_prep: bad shape");
+  if (B == 0 || T == 0) return MB_OK;
+  constexpr int TB = 16;
+  return dispatch_dtype(dtype, [&](auto t) {
+    using Tt = decltype(t);
+    return dispatch_dk(Dk, [&](auto dkc) {
+      constexpr int DK = decltype(dkc)::value;
+      return dispatch_dv(Dv, [&](auto dvc) {
+        constexpr int DV = decltype(dvc)::value;
+        const int64_t warps = H * ((T + TB - 1) / TB);
+        dim3 grid((unsigned)((warps + 3) / 4), (unsigned)B);
+        gdn_prep_kernel<Tt, DK, DV, TB><<<grid, 128, 0, (cudaStream_t)stream>>>(
+            (const Tt*)proj, ps, (const Tt*)conv_w, (const Tt*)A_log, (const Tt*)dt_bias, (const Tt*)conv_in,
+            (Tt*)conv_out, (Tt*)q, (Tt*)k, (Tt*)v, beta, g, (int)T, (int)H);
+        return check_launch("gdn_prep");
+      });
+    });
+  });
+}

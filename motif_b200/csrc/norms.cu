@@ -1,0 +1,509 @@
+// Row-wise HBM-bound kernels: RMSNorm, GatedRMSNorm, SwiGLU, attn-res depth softmax
+// (with its fused RMSNorm), gated residual, argmax and the embedding gather.
+//
+// All are one warp per row: the row is streamed once from HBM into registers (fp32),
+// reduced with warp shuffles and written once.  Rows of up to 8 * 32 * MAXV elements stay
+// in registers; the generic path re-reads the row (it is L1-resident by then).
+#include "common.cuh"
+
+namespace mb {
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+
+inline int rows_grid(int64_t rows) { return (int)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock); }
+
+// ---------------------------------------------------------------------------- RMSNorm
+// motif/ops/rms_norm.py:481-486: y = (x * rsqrt(mean(x^2) + eps)) * w.
+template <typename T>
+__global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                                int64_t M, int N, int64_t xs, int64_t ys, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const T* xr = x + row * xs;
+  float ss = 0.f;
+  for (int i = lane; i < N; i += 32) {
+    float v = to_f(xr[i]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)N + eps);
+  T* yr = y + row * ys;
+  for (int i = lane; i < N; i += 32) {
+    // The reference rounds the normalised value to the input dtype before the weight.
+    float v = to_f(from_f<T>(to_f(xr[i]) * r));
+    if (w) v = to_f(from_f<T>(v * to_f(w[i])));
+    yr[i] = from_f<T>(v);
+  }
+}
+
+// motif/ops/rms_norm.py:547-553: rmsnorm(values) * w * silu(gate), values first.
+template <typename T>
+__global__ void gated_rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                      T* __restrict__ y, int64_t M, int N, int64_t xs, int64_t ys,
+                                      float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const T* xr = x + row * xs;
+  float ss = 0.f;
+  for (int i = lane; i < N; i += 32) {
+    float v = to_f(xr[i]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)N + eps);
+  T* yr = y + row * ys;
+  for (int i = lane; i < N; i += 32) {
+    float v = to_f(from_f<T>(to_f(xr[i]) * r));
+    if (w) v = to_f(from_f<T>(v * to_f(w[i])));
+    const float gt = to_f(xr[N + i]);
+    const float sg = to_f(from_f<T>(siluf_(gt)));
+    yr[i] = from_f<T>(v * sg);
+  }
+}
+
+// motif/ops/swiglu.py:252-253: values * silu(gate).
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N,
+                              int64_t xs, int64_t ys) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  for (int64_t row = blockIdx.y; row < M; row += gridDim.y) {
+    const T* xr = x + row * xs;
+    const float gt = to_f(xr[N + i]);
+    const float sg = to_f(from_f<T>(siluf_(gt)));
+    y[row * ys + i] = from_f<T>(to_f(xr[i]) * sg);
+  }
+}
+
+// ---------------------------------------------------------------------------- attn-res
+constexpr int kMaxSrc = 8;
+struct SrcPtrs {
+  const void* p[kMaxSrc];
+  int64_t sb[kMaxSrc];
+  int64_t st[kMaxSrc];
+};
+
+// motif/ops/attn_res.py:588-593 (eager) / :93-186 (fused): logit_s = q . (w * rmsnorm(x_s)),
+// h = sum_s softmax_s(logit) x_s.  Generic path: the sources are re-read from L1.
+template <typename T>
+__global__ void attn_res_kernel(SrcPtrs src, int n_src, const T* __restrict__ w,
+                                const T* __restrict__ q, T* __restrict__ out, int64_t osb,
+                                int64_t ost, int64_t B, int64_t Tn, int D, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= B * Tn) return;
+  const int64_t b = row / Tn, t = row % Tn;
+  float logit[kMaxSrc];
+  float mx = -INFINITY;
+  for (int s = 0; s < n_src; ++s) {
+    const T* xr = static_cast<const T*>(src.p[s]) + b * src.sb[s] + t * src.st[s];
+    float ss = 0.f, dot = 0.f;
+    for (int i = lane; i < D; i += 32) {
+      const float v = to_f(xr[i]);
+      ss += v * v;
+      dot += to_f(q[i]) * to_f(w[i]) * v;
+    }
+    ss = warp_sum(ss);
+    dot = warp_sum(dot);
+    logit[s] = dot * rsqrtf(ss / (float)D + eps);
+    mx = fmaxf(mx, logit[s]);
+  }
+  float den = 0.f;
+  for (int s = 0; s < n_src; ++s) {
+    logit[s] = expf(logit[s] - mx);
+    den += logit[s];
+  }
+  const float inv = 1.f / den;
+  T* orow = out + b * osb + t * ost;
+  for (int i = lane; i < D; i += 32) {
+    float h = 0.f;
+    for (int s = 0; s < n_src; ++s) {
+      const T* xr = static_cast<const T*>(src.p[s]) + b * src.sb[s] + t * src.st[s];
+      h += logit[s] * inv * to_f(xr[i]);
+    }
+    orow[i] = from_f<T>(h);
+  }
+}
+
+// Fused attn-res read + RMSNorm of the result for the model path (token-major rows, all
+// sources share one row stride).  NV 16-byte vectors of 8 elements per lane: D = 256 * NV.
+template <typename T, int NV>
+__global__ void attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, const T* __restrict__ w,
+                                         const T* __restrict__ q, T* __restrict__ h_out,
+                                         T* __restrict__ hn_out, int64_t ors, int64_t rows,
+                                         float eps_src, float eps_out) {
+  constexpr int D = 256 * NV;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float h[NV][8];
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[v][e] = 0.f;
+
+  if (q == nullptr || n_src == 1) {
+    for (int s = 0; s < n_src; ++s) {
+      const T* xr = static_cast<const T*>(src.p[s]) + row * srs;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        uint4 raw = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+        const T* e8 = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[v][e] += to_f(e8[e]);
+      }
+    }
+  } else {
+    float qw[NV][8];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      uint4 rq = *reinterpret_cast<const uint4*>(q + (v * 32 + lane) * 8);
+      uint4 rw = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
+      const T* q8 = reinterpret_cast<const T*>(&rq);
+      const T* w8 = reinterpret_cast<const T*>(&rw);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qw[v][e] = to_f(q8[e]) * to_f(w8[e]);
+    }
+    // Online softmax over the sources: h accumulates exp(l_s - m) x_s.
+    float m = -INFINITY, den = 0.f;
+    for (int s = 0; s < n_src; ++s) {
+      const T* xr = static_cast<const T*>(src.p[s]) + row * srs;
+      float x[NV][8];
+      float ss = 0.f, dot = 0.f;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        uint4 raw = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+        const T* e8 = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          x[v][e] = to_f(e8[e]);
+          ss += x[v][e] * x[v][e];
+          dot += qw[v][e] * x[v][e];
+        }
+      }
+      ss = warp_sum(ss);
+      dot = warp_sum(dot);
+      const float l = dot * rsqrtf(ss / (float)D + eps_src);
+      const float mn = fmaxf(m, l);
+      const float sc = expf(m - mn);  // 0 on the first source (m = -inf)
+      const float p = expf(l - mn);
+      den = den * sc + p;
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[v][e] = h[v][e] * sc + p * x[v][e];
+      m = mn;
+    }
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[v][e] *= inv;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += h[v][e] * h[v][e];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)D + eps_out);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    T o8[8], n8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o8[e] = from_f<T>(h[v][e]);
+      n8[e] = from_f<T>(h[v][e] * r);
+    }
+    if (h_out) *reinterpret_cast<uint4*>(h_out + row * ors + (v * 32 + lane) * 8) = *reinterpret_cast<uint4*>(o8);
+    *reinterpret_cast<uint4*>(hn_out + row * ors + (v * 32 + lane) * 8) = *reinterpret_cast<uint4*>(n8);
+  }
+}
+
+// Generic-D version of the fused read (scalar, two passes over L1-resident rows).
+template <typename T>
+__global__ void attn_res_norm_kernel(SrcPtrs src, int n_src, int64_t srs, const T* __restrict__ w,
+                                     const T* __restrict__ q, T* __restrict__ h_out,
+                                     T* __restrict__ hn_out, int64_t ors, int64_t rows, int D,
+                                     float eps_src, float eps_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float a[kMaxSrc];
+  if (q == nullptr || n_src == 1) {
+    for (int s = 0; s < n_src; ++s) a[s] = 1.f;
+  } else {
+    float mx = -INFINITY;
+    for (int s = 0; s < n_src; ++s) {
+      const T* xr = static_cast<const T*>(src.p[s]) + row * srs;
+      float ss = 0.f, dot = 0.f;
+      for (int i = lane; i < D; i += 32) {
+        const float v = to_f(xr[i]);
+        ss += v * v;
+        dot += to_f(q[i]) * to_f(w[i]) * v;
+      }
+      ss = warp_sum(ss);
+      dot = warp_sum(dot);
+      a[s] = dot * rsqrtf(ss / (float)D + eps_src);
+      mx = fmaxf(mx, a[s]);
+    }
+    float den = 0.f;
+    for (int s = 0; s < n_src; ++s) {
+      a[s] = expf(a[s] - mx);
+      den += a[s];
+    }
+    for (int s = 0; s < n_src; ++s) a[s] /= den;
+  }
+  float ss = 0.f;
+  for (int i = lane; i < D; i += 32) {
+    float h = 0.f;
+    for (int s = 0; s < n_src; ++s) h += a[s] * to_f(static_cast<const T*>(src.p[s])[row * srs + i]);
+    ss += h * h;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)D + eps_out);
+  for (int i = lane; i < D; i += 32) {
+    float h = 0.f;
+    for (int s = 0; s < n_src; ++s) h += a[s] * to_f(static_cast<const T*>(src.p[s])[row * srs + i]);
+    if (h_out) h_out[row * ors + i] = from_f<T>(h);
+    hn_out[row * ors + i] = from_f<T>(h * r);
+  }
+}
+
+// ---------------------------------------------------------------------------- misc
+template <typename T>
+__global__ void gate_residual_kernel(const T* __restrict__ a, int64_t as, const T* __restrict__ g,
+                                     int64_t gs, const T* __restrict__ m, int64_t ms,
+                                     T* __restrict__ out, int64_t os, int64_t rows, int N) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    // chord_attn.py:254,313 rounds o_proj(out) and sigmoid(g_proj) to the model dtype.
+    const float gate = to_f(from_f<T>(sigmoidf_(to_f(g[row * gs + i]))));
+    const float att = to_f(from_f<T>(to_f(a[row * as + i]) * gate));
+    out[row * os + i] = from_f<T>(att + to_f(m[row * ms + i]));
+  }
+}
+
+template <typename T>
+__global__ void argmax_kernel(const T* __restrict__ x, int64_t V, int64_t rs, int64_t* __restrict__ ids) {
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * rs;
+  float best = -INFINITY;
+  int64_t bi = 0x7fffffffffffffffLL;
+  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = to_f(xr[i]);
+    if (v > best || (v == best && i < bi) || (isnan(v) && !isnan(best))) {
+      best = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[wid] = best;
+    si[wid] = bi;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffffffffffffLL;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) ids[row] = bi;
+  }
+}
+
+template <typename T>
+__global__ void embed_kernel(const int64_t* __restrict__ ids, const T* __restrict__ table,
+                             T* __restrict__ out, int64_t rows, int D, int64_t V) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= D) return;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    int64_t id = ids[row];
+    id = id < 0 ? 0 : (id >= V ? V - 1 : id);  // out-of-range ids are clamped, never read OOB
+    out[row * D + i] = table[id * D + i];
+  }
+}
+
+template <typename F>
+int dispatch(int dtype, F&& f) {
+  switch (dtype) {
+    case MB_F32: return f(float{});
+    case MB_F16: return f(__half{});
+    case MB_BF16: return f(__nv_bfloat16{});
+    default: return set_error(MB_ERR_DTYPE, "unsupported dtype code %d", dtype);
+  }
+}
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int motif_b200_rms_norm(const void* x, const void* w, void* y, int64_t M, int64_t N,
+                                   int64_t xs, int64_t ys, float eps, int dtype, void* stream) {
+  MB_REQUIRE(x && y, MB_ERR_ARG, "rms_norm: null pointer");
+  MB_REQUIRE(M >= 0 && N > 0 && N <= (1 << 20), MB_ERR_SHAPE, "rms_norm: bad shape M=%lld N=%lld",
+             (long long)M, (long long)N);
+  if (M == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using T = decltype(t);
+    rms_norm_kernel<T><<<rows_grid(M), 32 * kWarpsPerBlock, 0, (cudaStream_t)stream>>>(
+        (const T*)x, (const T*)w, (T*)y, M, (int)N, xs, ys, eps);
+    return check_launch("rms_norm");
+  });
+}
+
+extern "C" int motif_b200_gated_rms_norm(const void* x, const void* w, void* y, int64_t M, int64_t N,
+                                         int64_t xs, int64_t ys, float eps, int dtype, void* stream) {
+  MB_REQUIRE(x && y, MB_ERR_ARG, "gated_rms_norm: null pointer");
+  MB_REQUIRE(M >= 0 && N > 0 && N <= (1 << 20), MB_ERR_SHAPE, "gated_rms_norm: bad shape");
+  if (M == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using T = decltype(t);
+    gated_rms_norm_kernel<T><<<rows_grid(M), 32 * kWarpsPerBlock, 0, (cudaStream_t)stream>>>(
+        (const T*)x, (const T*)w, (T*)y, M, (int)N, xs, ys, eps);
+    return check_launch("gated_rms_norm");
+  });
+}
+
+extern "C" int motif_b200_swiglu(const void* x, void* y, int64_t M, int64_t N, int64_t xs,
+                                 int64_t ys, int dtype, void* stream) {
+  MB_REQUIRE(x && y, MB_ERR_ARG, "swiglu: null pointer");
+  MB_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), MB_ERR_SHAPE, "swiglu: bad shape");
+  if (M == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using T = decltype(t);
+    dim3 grid((unsigned)((N + 255) / 256), (unsigned)(M < 65535 ? M : 65535));
+    swiglu_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>((const T*)x, (T*)y, M, (int)N, xs, ys);
+    return check_launch("swiglu");
+  });
+}
+
+extern "C" int motif_b200_attn_res(const void* const* sources, int n_src, const int64_t* src_strides,
+                                   const void* weight, const void* query, void* out, int64_t osb,
+                                   int64_t ost, int64_t B, int64_t T, int64_t D, float eps, int dtype,
+                                   void* stream) {
+  MB_REQUIRE(sources && src_strides && weight && query && out, MB_ERR_ARG, "attn_res: null pointer");
+  MB_REQUIRE(n_src >= 1 && n_src <= kMaxSrc, MB_ERR_UNSUPPORTED, "attn_res: %d sources (1..%d supported)",
+             n_src, kMaxSrc);
+  MB_REQUIRE(B >= 0 && T >= 0 && D > 0, MB_ERR_SHAPE, "attn_res: bad shape");
+  SrcPtrs sp{};
+  for (int s = 0; s < n_src; ++s) {
+    MB_REQUIRE(sources[s], MB_ERR_ARG, "attn_res: null source %d", s);
+    sp.p[s] = sources[s];
+    sp.sb[s] = src_strides[2 * s];
+    sp.st[s] = src_strides[2 * s + 1];
+  }
+  if (B * T == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using Tt = decltype(t);
+    attn_res_kernel<Tt><<<rows_grid(B * T), 32 * kWarpsPerBlock, 0, (cudaStream_t)stream>>>(
+        sp, n_src, (const Tt*)weight, (const Tt*)query, (Tt*)out, osb, ost, B, T, (int)D, eps);
+    return check_launch("attn_res");
+  });
+}
+
+extern "C" int motif_b200_attn_res_norm(const void* const* sources, int n_src, int64_t srs,
+                                        const void* weight, const void* query, void* h_out,
+                                        void* hn_out, int64_t ors, int64_t rows, int64_t D,
+                                        float eps_src, float eps_out, int dtype, void* stream) {
+  MB_REQUIRE(sources && hn_out, MB_ERR_ARG, "attn_res_norm: null pointer");
+  MB_REQUIRE(n_src >= 1 && n_src <= kMaxSrc, MB_ERR_UNSUPPORTED, "attn_res_norm: %d sources", n_src);
+  MB_REQUIRE(query == nullptr || weight != nullptr, MB_ERR_ARG, "attn_res_norm: query without weight");
+  MB_REQUIRE(rows >= 0 && D > 0, MB_ERR_SHAPE, "attn_res_norm: bad shape");
+  SrcPtrs sp{};
+  bool aligned = (srs % 8 == 0) && (ors % 8 == 0) && ((uintptr_t)hn_out % 16 == 0) &&
+                 ((uintptr_t)h_out % 16 == 0) && ((uintptr_t)weight % 16 == 0) && ((uintptr_t)query % 16 == 0);
+  for (int s = 0; s < n_src; ++s) {
+    MB_REQUIRE(sources[s], MB_ERR_ARG, "attn_res_norm: null source %d", s);
+    sp.p[s] = sources[s];
+    aligned = aligned && ((uintptr_t)sources[s] % 16 == 0);
+  }
+  if (rows == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using Tt = decltype(t);
+    const int grid = rows_grid(rows);
+    const int blk = 32 * kWarpsPerBlock;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool vec = aligned && sizeof(Tt) == 2 && D % 256 == 0 && D / 256 <= 4;
+    if (vec && D == 256)
+      attn_res_norm_vec_kernel<Tt, 1><<<grid, blk, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                             (Tt*)h_out, (Tt*)hn_out, ors, rows, eps_src, eps_out);
+    else if (vec && D == 512)
+      attn_res_norm_vec_kernel<Tt, 2><<<grid, blk, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                             (Tt*)h_out, (Tt*)hn_out, ors, rows, eps_src, eps_out);
+    else if (vec && D == 768)
+      attn_res_norm_vec_kernel<Tt, 3><<<grid, blk, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                             (Tt*)h_out, (Tt*)hn_out, ors, rows, eps_src, eps_out);
+    else if (vec && D == 1024)
+      attn_res_norm_vec_kernel<Tt, 4><<<grid, blk, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                             (Tt*)h_out, (Tt*)hn_out, ors, rows, eps_src, eps_out);
+    else
+      attn_res_norm_kernel<Tt><<<grid, blk, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                      (Tt*)h_out, (Tt*)hn_out, ors, rows, (int)D, eps_src, eps_out);
+    return check_launch("attn_res_norm");
+  });
+}
+
+extern "C" int motif_b200_gate_residual(const void* a, int64_t as, const void* g, int64_t gs,
+                                        const void* m, int64_t ms, void* out, int64_t os, int64_t rows,
+                                        int64_t N, int dtype, void* stream) {
+  MB_REQUIRE(a && g && m && out, MB_ERR_ARG, "gate_residual: null pointer");
+  MB_REQUIRE(rows >= 0 && N > 0 && N <= (1 << 24), MB_ERR_SHAPE, "gate_residual: bad shape");
+  if (rows == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using T = decltype(t);
+    dim3 grid((unsigned)((N + 255) / 256), (unsigned)(rows < 65535 ? rows : 65535));
+    gate_residual_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>((const T*)a, as, (const T*)g, gs,
+                                                                   (const T*)m, ms, (T*)out, os, rows, (int)N);
+    return check_launch("gate_residual");
+  });
+}
+
+extern "C" int motif_b200_argmax(const void* logits, int64_t rows, int64_t V, int64_t rs, int64_t* ids,
+                                 int dtype, void* stream) {
+  MB_REQUIRE(logits && ids, MB_ERR_ARG, "argmax: null pointer");
+  MB_REQUIRE(rows >= 0 && rows < 2147483647LL && V > 0, MB_ERR_SHAPE, "argmax: bad shape");
+  if (rows == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using T = decltype(t);
+    argmax_kernel<T><<<(unsigned)rows, 1024, 0, (cudaStream_t)stream>>>((const T*)logits, V, rs, ids);
+    return check_launch("argmax");
+  });
+}
+
+extern "C" int motif_b200_embed(const int64_t* ids, const void* table, void* out, int64_t rows,
+                                int64_t D, int64_t V, int dtype, void* stream) {
+  MB_REQUIRE(ids && table && out, MB_ERR_ARG, "embed: null pointer");
+  MB_REQUIRE(rows >= 0 && D > 0 && D <= (1 << 24) && V > 0, MB_ERR_SHAPE, "embed: bad shape");
+  if (rows == 0) return MB_OK;
+  return dispatch(dtype, [&](auto t) {
+    using T = decltype(t);
+    dim3 grid((unsigned)((D + 255) / 256), (unsigned)(rows < 65535 ? rows : 65535));
+    embed_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>(ids, (const T*)table, (T*)out, rows, (int)D, V);
+    return check_launch("embed");
+  });
+}
