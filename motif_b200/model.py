@@ -1,0 +1,615 @@
+"""`MotifChordModel` with the reference's module tree, parameter names, forward, cache and
+generation API (`motif/model/motif.py`, `motif/block/decoder.py`, `motif/block/mlp.py`,
+`motif/block/attention/{gdn_attn,chord_attn}.py`), computed by the sm_100a kernels.
+
+The parameters are stored exactly as the reference stores them, so `state_dict()` /
+`load_state_dict()` interoperate with the reference in both directions.  The forward does
+not walk the modules one by one; per decoder it runs
+
+    attn-res read + RMSNorm            motif_b200_attn_res_norm   (one pass over the sources)
+    one GEMM for every input projection  cuBLAS, norm weights folded into the packed weight
+    GDN:   conv + SiLU + L2 norms + beta/g   motif_b200_gdn_prep
+           delta rule + GatedRMSNorm          motif_b200_gdn_chunk_gated   (decode: gdn_decode)
+           SwiGLU                             motif_b200_swiglu
+           o_proj + down_proj as ONE GEMM over [o | act] (the parallel residual is a sum of
+           two products, so it is one product over the concatenated K dimension)
+    Chord: q/k RMSNorm + cache append         motif_b200_chord_prep
+           biased flash attention             motif_b200_chord_attention  (decode: chord_decode)
+           o_proj, down_proj GEMMs, then f = attn * sigmoid(g) + mlp   motif_b200_gate_residual
+
+and the block output / final norm with the same fused read (sum mode).  Packed weights
+are derived from the parameters on first use and rebuilt after `load_state_dict`, `.to()`
+or an explicit `invalidate_packed()` (call it after editing parameters in place).
+"""
+
+import builtins
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Union
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .cache import (AttnResCache, BasicLayerCache, DecoderBlockCache, GatedDeltaAttentionLayerCache,
+                    KVLayerCache, ModelCache, build_cache)
+from .config import CHUNK_SIZE, CONV_SIZE, EXPAND_V, GGD_EPS, NORM_EPS, MotifChordConfig
+from .ops import GatedRMSNorm, RMSNorm, SwiGLU as SwiGLUOp
+
+
+# ============================================================================ modules
+class BasicAttention(nn.Module):
+    """Head layout shared by the attention layers (`block/attention/base.py:10-118`)."""
+
+    def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: Optional[int] = None, **kwargs):
+        super().__init__()
+        num_kv_heads = num_kv_heads if num_kv_heads is not None else num_heads
+        assert hidden_size % num_heads == 0, f'hidden_size {hidden_size} must be divisible by num_heads {num_heads}'
+        assert num_heads % num_kv_heads == 0, f'num_heads {num_heads} must be divisible by num_kv_heads {num_kv_heads}'
+        self.hidden_size = hidden_size
+        self.num_heads = num_heads
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = hidden_size // num_heads
+        self.kv_dim = num_kv_heads * self.head_dim
+        self.num_kv_queries = num_heads // num_kv_heads
+
+
+class GatedDeltaAttention(BasicAttention):
+    """Gated delta-net attention parameters (`block/attention/gdn_attn.py:19-106`)."""
+
+    def __init__(self, hidden_size, num_heads, head_k_dim=None, expand_v=EXPAND_V, conv_size=CONV_SIZE,
+                 chunk_size=CHUNK_SIZE, bias=False, dropout=0.0, use_triton=True, **kwargs):
+        super().__init__(hidden_size=hidden_size, num_heads=num_heads, num_kv_heads=num_heads)
+        if bias:
+            raise NotImplementedError('projection biases are not part of this inference path')
+        self.dk = head_k_dim or self.head_dim
+        self.dv = int(self.dk * expand_v)
+        self.conv_size = conv_size
+        self.chunk_size = chunk_size
+        self.bias = bias
+        self.dropout = dropout
+        self.use_triton = True
+        dk_all, dv_all = self.num_heads * self.dk, self.num_heads * self.dv
+        self.q_proj = nn.Linear(hidden_size, dk_all, bias=False)
+        self.k_proj = nn.Linear(hidden_size, dk_all, bias=False)
+        self.v_proj = nn.Linear(hidden_size, dv_all, bias=False)
+        self.a_proj = nn.Linear(hidden_size, self.num_heads, bias=False)
+        self.b_proj = nn.Linear(hidden_size, self.num_heads, bias=False)
+        self.g_proj = nn.Linear(hidden_size, dv_all, bias=False)
+        self.o_proj = nn.Linear(dv_all, hidden_size, bias=False)
+        self.q_conv = nn.Conv1d(dk_all, dk_all, conv_size, groups=dk_all, bias=False)
+        self.k_conv = nn.Conv1d(dk_all, dk_all, conv_size, groups=dk_all, bias=False)
+        self.v_conv = nn.Conv1d(dv_all, dv_all, conv_size, groups=dv_all, bias=False)
+        A = torch.empty(self.num_heads).uniform_(1, 16)
+        self.A_log = nn.Parameter(A.log())
+        dt = torch.exp(torch.rand(self.num_heads) * (math.log(0.1) - math.log(0.001)) + math.log(0.001))
+        self.dt_bias = nn.Parameter(dt + torch.log(-torch.expm1(-dt)))
+        self.o_norm = GatedRMSNorm(self.dv)
+
+    @classmethod
+    def cache_type(cls):
+        return GatedDeltaAttentionLayerCache
+
+
+class ChordAttention(BasicAttention):
+    """Chord attention parameters (`block/attention/chord_attn.py:59-124`)."""
+
+    def __init__(self, hidden_size, num_heads, num_kv_heads=None, **kwargs):
+        super().__init__(hidden_size=hidden_size, num_heads=num_heads, num_kv_heads=num_kv_heads)
+        self.q_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.k_proj = nn.Linear(hidden_size, self.kv_dim, bias=False)
+        self.v_proj = nn.Linear(hidden_size, self.kv_dim, bias=False)
+        self.o_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.g_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.q_norm = RMSNorm(self.head_dim)
+        self.k_norm = RMSNorm(self.head_dim)
+        self.theta_alpha = nn.Parameter(torch.zeros(num_heads))
+        self.theta_beta = nn.Parameter(torch.zeros(num_heads))
+        self.theta_mu = nn.Parameter(torch.zeros(num_heads), requires_grad=False)
+        self.ssmax_s = nn.Parameter(torch.ones(num_heads))
+
+    @classmethod
+    def cache_type(cls):
+        return KVLayerCache
+
+    def _ggd_parameters(self):
+        """`(alpha, beta, mu)` in fp32 (`chord_attn.py:126-138`)."""
+        ta, tb, tm = (t.float() for t in (self.theta_alpha, self.theta_beta, self.theta_mu))
+        return torch.exp(ta), tb, torch.exp(tm) - torch.exp(-tm)
+
+    @torch.no_grad()
+    def relative_prior(self, max_distance: int, device=None, dtype=torch.float32):
+        """GGD bias as a function of signed distance (`chord_attn.py:178-202`)."""
+        alpha, beta, mu = self._ggd_parameters()
+        device = device if device is not None else self.theta_alpha.device
+        d = torch.arange(-max_distance, max_distance + 1, device=device, dtype=alpha.dtype)
+        b = torch.abs(d[None, :] - mu[:, None].to(device)) + GGD_EPS
+        return (-alpha[:, None].to(device) * b ** beta[:, None].to(device)).to(dtype)
+
+
+class SwiGLU(nn.Module):
+    """Gated MLP `down_proj(act(gate_up_proj(x)))` (`block/mlp.py:7-63`)."""
+
+    def __init__(self, in_features: int, hidden_features: int = None, out_features: int = None, bias: bool = False):
+        super().__init__()
+        if hidden_features is None:
+            h = int(in_features * 8 / 3)
+            hidden_features = (h + 127) // 128 * 128
+        out_features = out_features or in_features
+        self.hidden_features = hidden_features
+        self.gate_up_proj = nn.Linear(in_features, 2 * hidden_features, bias=bias)
+        self.down_proj = nn.Linear(hidden_features, out_features, bias=bias)
+        self.act = SwiGLUOp(dim=-1)
+
+    def forward(self, x):
+        return F.linear(self.act(F.linear(x, self.gate_up_proj.weight)), self.down_proj.weight)
+
+
+class Decoder(nn.Module):
+    """attn_norm, attn, mlp_norm, mlp (`block/decoder.py:44-104`)."""
+
+    def __init__(self, attn_type: str, config: MotifChordConfig):
+        super().__init__()
+        self.attn_type = attn_type.lower()
+        self.attn_norm = RMSNorm(config.model_dim)
+        if self.attn_type == 'chord':
+            self.attn = ChordAttention(hidden_size=config.model_dim, num_heads=config.num_heads,
+                                       num_kv_heads=config.num_kv_heads)
+        else:
+            self.attn = GatedDeltaAttention(hidden_size=config.model_dim, num_heads=config.num_heads,
+                                            head_k_dim=config.head_k_dim, expand_v=EXPAND_V,
+                                            chunk_size=CHUNK_SIZE, bias=False)
+        self.mlp_norm = RMSNorm(config.model_dim)
+        self.mlp = SwiGLU(in_features=config.model_dim)
+
+    @property
+    def cache_type(self):
+        return KVLayerCache if self.attn_type == 'chord' else GatedDeltaAttentionLayerCache
+
+
+class DecoderBlock(nn.Module):
+    """Decoders joined by the intra-block attention residual (`block/decoder.py:107-137`)."""
+
+    def __init__(self, config: MotifChordConfig):
+        super().__init__()
+        self.features = nn.ModuleList([Decoder(t, config) for t in config.block])
+        self.pseudo_queries = nn.ParameterList([nn.Parameter(torch.zeros(config.model_dim)) for _ in self.features])
+        self.attn_res_norms = nn.ModuleList([RMSNorm(config.model_dim) for _ in self.features])
+
+
+# ============================================================================ output
+class ModelOutput:
+    """Result of one forward (`model/motif.py:27-151`).
+
+    `hidden_states` (the final-normed states) is materialised on first access from the
+    pre-norm block output, so a decode step that only needs logits does not pay for it.
+    """
+
+    def __init__(self, hidden_states=None, logits=None, loss=None, cache=None, sampler=None, _final=None):
+        self._hidden = hidden_states
+        self._final = _final
+        self.logits = logits
+        self.loss = loss
+        self.cache = cache
+        self.sampler = sampler
+
+    @property
+    def hidden_states(self) -> torch.Tensor:
+        if self._hidden is None and self._final is not None:
+            x, norm = self._final
+            with torch.no_grad():
+                self._hidden = norm(x)
+        return self._hidden
+
+    @hidden_states.setter
+    def hidden_states(self, v):
+        self._hidden = v
+
+    @property
+    def last_hidden_state(self):
+        return self.hidden_states[:, -1, :]
+
+    @property
+    def last_logits(self):
+        return None if self.logits is None else self.logits[:, -1, :]
+
+    def next_token(self, temperature: float = 1.0, sampler=None, input_ids=None):
+        """Greedy argmax of the last position, or the given / bound sampler (`motif.py:68-98`)."""
+        if self.logits is None:
+            return None
+        last = self.logits[:, -1, :]
+        active = sampler if sampler is not None else self.sampler
+        if active is not None:
+            return active(last, input_ids)
+        return greedy_next(last)
+
+    def set_sampler(self, sampler=None, **kwargs):
+        if kwargs:
+            raise NotImplementedError('only a ready sampler callable can be bound (sampling kernels are not built)')
+        self.sampler = sampler
+        return self
+
+    def reset_caches(self):
+        if self.cache is not None:
+            self.cache.reset()
+
+    def __repr__(self):
+        lg = tuple(self.logits.shape) if self.logits is not None else None
+        return f'ModelOutput(logits={lg}, loss={self.loss is not None}, cache={self.cache!r})'
+
+
+def greedy_next(last_logits: torch.Tensor) -> torch.Tensor:
+    """`[B, V] -> [B, 1]` argmax (first maximum) on the argmax kernel."""
+    rows, V = last_logits.shape
+    x = last_logits if last_logits.stride(-1) == 1 else last_logits.contiguous()
+    ids = torch.empty((rows, 1), dtype=torch.int64, device=x.device)
+    _lib.call('motif_b200_argmax', _lib.ptr(x), rows, V, x.stride(0), _lib.ptr(ids), _lib.dtype_code(x.dtype),
+              _lib.stream_ptr(x.device))
+    return ids
+
+
+# ============================================================================ packing
+@dataclass
+class _GDNPack:
+    w_in: torch.Tensor      # [N_in, d]: q | k | v | a | b | g | gate_up, norm weights folded in
+    conv_w: torch.Tensor    # [C, 4] q | k | v channels
+    A_log: torch.Tensor
+    dt_bias: torch.Tensor
+    onorm_w: torch.Tensor
+    w_out: torch.Tensor     # [d, H*dv + hid]: o_proj | down_proj
+    H: int
+    dk: int
+    dv: int
+    hid: int
+    off_g: int
+    off_gu: int
+
+
+@dataclass
+class _ChordPack:
+    w_in: torch.Tensor      # [N_in, d]: q | k | v | g | gate_up
+    qn_w: torch.Tensor
+    kn_w: torch.Tensor
+    w_o: torch.Tensor
+    w_down: torch.Tensor
+    alpha: torch.Tensor
+    beta: torch.Tensor
+    mu: torch.Tensor
+    ssmax: torch.Tensor
+    H: int
+    Hkv: int
+    D: int
+    hid: int
+    off_g: int
+    off_gu: int
+
+
+@torch.no_grad()
+def _pack_decoder(dec: Decoder):
+    wa = dec.attn_norm.weight[None, :]
+    wm = dec.mlp_norm.weight[None, :]
+    a = dec.attn
+    hid = dec.mlp.hidden_features
+    gu = dec.mlp.gate_up_proj.weight * wm
+    if dec.attn_type == 'chord':
+        parts = [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.g_proj.weight]
+        off_g = a.hidden_size + 2 * a.kv_dim
+        w_in = torch.cat([p * wa for p in parts] + [gu], 0).contiguous()
+        al, be, mu = a._ggd_parameters()
+        return _ChordPack(w_in=w_in, qn_w=a.q_norm.weight.detach().contiguous(),
+                          kn_w=a.k_norm.weight.detach().contiguous(), w_o=a.o_proj.weight.detach().contiguous(),
+                          w_down=dec.mlp.down_proj.weight.detach().contiguous(), alpha=al.contiguous(),
+                          beta=be.contiguous(), mu=mu.contiguous(), ssmax=a.ssmax_s.detach().float().contiguous(),
+                          H=a.num_heads, Hkv=a.num_kv_heads, D=a.head_dim, hid=hid, off_g=off_g,
+                          off_gu=off_g + a.hidden_size)
+    H, dk, dv = a.num_heads, a.dk, a.dv
+    parts = [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.a_proj.weight, a.b_proj.weight, a.g_proj.weight]
+    off_g = 2 * H * dk + H * dv + 2 * H
+    w_in = torch.cat([p * wa for p in parts] + [gu], 0).contiguous()
+    conv_w = torch.cat([a.q_conv.weight.reshape(-1, CONV_SIZE), a.k_conv.weight.reshape(-1, CONV_SIZE),
+                        a.v_conv.weight.reshape(-1, CONV_SIZE)], 0).contiguous()
+    w_out = torch.cat([a.o_proj.weight, dec.mlp.down_proj.weight], 1).contiguous()
+    return _GDNPack(w_in=w_in, conv_w=conv_w, A_log=a.A_log.detach().contiguous(),
+                    dt_bias=a.dt_bias.detach().contiguous(), onorm_w=a.o_norm.weight.detach().contiguous(),
+                    w_out=w_out, H=H, dk=dk, dv=dv, hid=hid, off_g=off_g, off_gu=off_g + H * dv)
+
+
+# ============================================================================ model
+class MotifChordModel(nn.Module):
+    """The Motif Chord decoder-only LM (`model/motif.py:154-630`) on the sm_100a kernels."""
+
+    def __init__(self, config):
+        super().__init__()
+        config = MotifChordConfig.from_any(config)
+        self.config = config
+        self.embed = nn.Embedding(config.vocab_size, config.model_dim)
+        self.blocks = nn.ModuleList([DecoderBlock(config) for _ in range(config.block_n)])
+        self.norm = RMSNorm(config.model_dim)
+        self.lm_head = nn.Linear(config.model_dim, config.vocab_size, bias=False)
+        if config.tied_weight:
+            self.embed.weight = self.lm_head.weight
+        self.sampler = None
+        self._packed = None
+        self.decode_splits = None  # split-KV count override for the decode attention
+
+    # ------------------------------------------------------------------ bookkeeping
+    def invalidate_packed(self):
+        self._packed = None
+
+    def _apply(self, fn, *args, **kwargs):
+        self._packed = None
+        return super()._apply(fn, *args, **kwargs)
+
+    def load_state_dict(self, state_dict, strict: bool = True, assign: bool = False):
+        self._packed = None
+        return super().load_state_dict(state_dict, strict=strict, assign=assign)
+
+    def packed(self):
+        if self._packed is None:
+            with torch.no_grad():
+                decs = [[_pack_decoder(dec) for dec in blk.features] for blk in self.blocks]
+                lm = (self.lm_head.weight * self.norm.weight[None, :]).contiguous()
+            self._packed = (decs, lm)
+        return self._packed
+
+    def count_param(self, print: bool = False) -> int:
+        """Parameter count, tied weights once (`model/motif.py:377-400`)."""
+        total = int(sum(p.numel() for p in self.parameters()))
+        if print:
+            builtins.print(f'{type(self).__name__} params: {total:,}')
+        return total
+
+    def cache_types(self):
+        return [[d.cache_type for d in blk.features] for blk in self.blocks]
+
+    def create_cache(self, use_attn: Optional[bool] = None, functional: bool = False,
+                     wide_kv: bool = False) -> ModelCache:
+        """`create_cache` (`model/motif.py:413-455`)."""
+        return build_cache(self, use_attn=use_attn, functional=functional, wide_kv=wide_kv)
+
+    def set_sampler(self, sampler=None, **kwargs):
+        if kwargs:
+            raise NotImplementedError('only a ready sampler callable can be bound (sampling kernels are not built)')
+        self.sampler = sampler
+        return self
+
+    def generate(self, input_ids, max_new_tokens: int = 32, eos_token_id=None, sampler=None, cache=None,
+                 mask=None, tokenizer=None):
+        """`generate` (`model/motif.py:483-543`)."""
+        from .generate import Generation
+        active = sampler if sampler is not None else self.sampler
+        if eos_token_id is None and active is not None:
+            eos_token_id = getattr(active, 'eos_token_id', None)
+        if eos_token_id is None and tokenizer is not None:
+            eos_token_id = getattr(tokenizer, 'token_eos', None)
+        return Generation(self, input_ids, max_new_tokens, eos_token_id, sampler, cache, mask, tokenizer)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, input_ids: torch.Tensor, cache: Optional[ModelCache] = None, labels=None,
+                mask: Optional[torch.Tensor] = None, position: Optional[Union[int, torch.Tensor]] = None):
+        """`MotifChordModel.forward` (`model/motif.py:545-630`) on the fused kernels."""
+        if input_ids.dim() != 2:
+            raise ValueError(f'input_ids must be [B, T], got {tuple(input_ids.shape)}')
+        if not self.embed.weight.is_cuda:
+            raise ValueError('motif_b200 runs on CUDA only: move the model to a CUDA device')
+        cached = cache.seq_len if cache is not None else 0
+        if mask is not None:
+            width = cached + input_ids.shape[1]
+            if mask.dim() != 2:
+                raise ValueError(f'mask must be [B, T], got {tuple(mask.shape)}')
+            if mask.shape != (input_ids.shape[0], width):
+                raise ValueError(f'mask {tuple(mask.shape)} does not cover the {width} keys of a {cached}-position '
+                                 f'cache plus {input_ids.shape[1]} inputs')
+            if not bool(mask.all()):
+                raise NotImplementedError('attention masks are not supported by the fused path yet')
+        if isinstance(position, torch.Tensor):
+            position = int(position.reshape(-1)[0])
+        if cache is None:
+            cache = self.create_cache()
+        with torch.no_grad():
+            logits, x_final = _forward(self, input_ids.to(self.embed.weight.device), cache, position or 0)
+        loss = None
+        if labels is not None:
+            loss = F.cross_entropy(logits.view(-1, logits.size(-1)).float(), labels.view(-1).to(logits.device),
+                                   ignore_index=-100)
+        return ModelOutput(logits=logits, loss=loss, cache=cache, sampler=self.sampler,
+                           _final=(x_final, self.norm))
+
+
+# ============================================================================ engine
+def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """a [M, K] @ w[N, K]^T with cuBLAS (plain library GEMM)."""
+    return torch.mm(a, w.t(), out=out)
+
+
+def _norm_read(sources: List[torch.Tensor], query, weight, h_out, hn_out, eps_src=NORM_EPS, eps_out=NORM_EPS):
+    x0 = sources[0]
+    rows, d = x0.shape
+    _lib.call('motif_b200_attn_res_norm', _lib.ptr_array([s.data_ptr() for s in sources]), len(sources),
+              x0.stride(0), _lib.ptr(weight), _lib.ptr(query), _lib.ptr(h_out), _lib.ptr(hn_out), hn_out.stride(0),
+              rows, d, float(eps_src), float(eps_out), _lib.dtype_code(x0.dtype), _lib.stream_ptr(x0.device))
+
+
+def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, position: int):
+    cfg = model.config
+    decs, lm = model.packed()
+    B, T = ids.shape
+    M = B * T
+    d = cfg.model_dim
+    w = model.embed.weight
+    dt, dev = w.dtype, w.device
+    dc = _lib.dtype_code(dt)
+    st = _lib.stream_ptr(dev)
+    ids = ids.contiguous()
+
+    x = torch.empty((M, d), dtype=dt, device=dev)
+    _lib.call('motif_b200_embed', _lib.ptr(ids), _lib.ptr(w), _lib.ptr(x), M, d, cfg.vocab_size, dc, st)
+    hn = torch.empty((M, d), dtype=dt, device=dev)
+    _norm_read([x], None, None, None, hn)
+
+    for b, block in enumerate(model.blocks):
+        bc = cache[b]
+        ar = bc.attn_res
+        ar.init_embedding(x.view(B, T, d))
+        if len(bc.attn) == 0:
+            if not model.training:
+                bc.ensure_attn([dec.cache_type for dec in block.features])
+        elif len(bc.attn) != len(block.features):
+            raise ValueError(f'cache.attn has {len(bc.attn)} entries but the block has {len(block.features)} layers')
+        use_cache = len(bc.attn) == len(block.features)
+        fs: List[torch.Tensor] = []
+        for i, dec in enumerate(block.features):
+            if i > 0:
+                hn = torch.empty((M, d), dtype=dt, device=dev)
+                _norm_read([x] + fs, block.pseudo_queries[i].detach(), block.attn_res_norms[i].weight.detach(),
+                           None, hn, eps_src=block.attn_res_norms[i].eps)
+            pk = decs[b][i]
+            proj = _mm(hn, pk.w_in)
+            layer_cache = bc.attn[i] if use_cache else None
+            if dec.attn_type == 'chord':
+                if layer_cache is not None and not isinstance(layer_cache, KVLayerCache):
+                    raise TypeError(f'ChordAttention requires KVLayerCache, got {type(layer_cache).__name__}')
+                f = _chord_decoder(model, pk, proj, B, T, layer_cache, position, dt, dev, dc, st)
+            else:
+                if layer_cache is not None and not isinstance(layer_cache, GatedDeltaAttentionLayerCache):
+                    raise TypeError(f'GatedDeltaAttention requires GatedDeltaAttentionLayerCache, '
+                                    f'got {type(layer_cache).__name__}')
+                f = _gdn_decoder(pk, proj, B, T, layer_cache, dt, dev, dc, st)
+            fs.append(f)
+        # block output = sum of the increments (decoder.py:215-217), and its RMSNorm for the
+        # next block's first decoder (or the final norm before lm_head)
+        x_next = torch.empty((M, d), dtype=dt, device=dev)
+        hn = torch.empty((M, d), dtype=dt, device=dev)
+        _norm_read(fs, None, None, x_next, hn, eps_out=(model.norm.eps if b == len(model.blocks) - 1 else
+                                                         model.blocks[b + 1].features[0].attn_norm.eps))
+        ar.blocks.extend(f.view(B, T, d) for f in fs)
+        ar.partial_block = x_next.view(B, T, d)
+        ar.seq_len = max(ar.seq_len, T)
+        x = x_next
+    logits = _mm(hn, lm)
+    return logits.view(B, T, cfg.vocab_size), x.view(B, T, d)
+
+
+def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLayerCache], dt, dev, dc, st):
+    """`GatedDeltaAttention.forward` + the SwiGLU MLP + the parallel residual (decoder.py:203-208)."""
+    M = B * T
+    H, dk, dv, hid = pk.H, pk.dk, pk.dv, pk.hid
+    C = H * (2 * dk + dv)
+    N_in = proj.shape[1]
+    cat = torch.empty((M, H * dv + hid), dtype=dt, device=dev)  # [gated-normed o | act]
+    state_in = cache.state if cache is not None else None
+    conv_in = cache._conv if cache is not None else None
+    if state_in is not None and (state_in.dtype != torch.float32 or not state_in.is_contiguous()):
+        state_in = state_in.float().contiguous()
+    if conv_in is not None and (conv_in.dtype != dt or not conv_in.is_contiguous()):
+        conv_in = conv_in.to(dt).contiguous()
+    eps = NORM_EPS
+    if T == 1:
+        # gdn_attn.py:198-199: the L == 1 step is the recurrence, fused with conv and o_norm.
+        state = state_in if state_in is not None else torch.zeros((B, H, dk, dv), dtype=torch.float32, device=dev)
+        conv = conv_in if conv_in is not None else torch.zeros((B, 3, C), dtype=dt, device=dev)
+        _lib.call('motif_b200_gdn_decode', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+                  _lib.ptr(pk.dt_bias), _lib.ptr(conv), _lib.ptr(state), proj.data_ptr() + pk.off_g * proj.element_size(),
+                  _lib.ptr(pk.onorm_w), _lib.ptr(cat), cat.stride(0), B, H, dk, dv, eps, dc, st)
+        conv_out = conv
+    else:
+        qb = torch.empty((M, H * dk), dtype=dt, device=dev)
+        kb = torch.empty((M, H * dk), dtype=dt, device=dev)
+        vb = torch.empty((M, H * dv), dtype=dt, device=dev)
+        beta = torch.empty((M, H), dtype=torch.float32, device=dev)
+        g = torch.empty((M, H), dtype=torch.float32, device=dev)
+        conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)
+        _lib.call('motif_b200_gdn_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+                  _lib.ptr(pk.dt_bias), _lib.ptr(conv_in), _lib.ptr(conv_out), _lib.ptr(qb), _lib.ptr(kb),
+                  _lib.ptr(vb), _lib.ptr(beta), _lib.ptr(g), B, T, H, dk, dv, dc, st)
+        state = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+        cs = cat.stride(0)
+        strides = [T * H * dk, dk, H * dk, T * H * dk, dk, H * dk, T * H * dv, dv, H * dv,
+                   T * cs, dv, cs, T * H, 1, H, T * H, 1, H]
+        _lib.call('motif_b200_gdn_chunk_gated', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(beta), _lib.ptr(g),
+                  _lib.ptr(state_in), _lib.ptr(state), _lib.ptr(cat), B, H, T, dk, dv, _lib.i64_array(strides),
+                  proj.data_ptr() + pk.off_g * proj.element_size(), N_in, dv, _lib.ptr(pk.onorm_w), eps, dc, st)
+    _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
+              cat.data_ptr() + H * dv * cat.element_size(), M, hid, N_in, cat.stride(0), dc, st)
+    f = _mm(cat, pk.w_out)
+    if cache is not None:
+        cache._split = (H * dk, H * dk, H * dv)
+        cache.update(state, conv_out, steps=T)
+    return f
+
+
+_SMS: Dict[int, int] = {}
+
+
+def _decode_splits(model, B, Hkv, S):
+    if model.decode_splits:
+        return int(model.decode_splits)
+    dev = torch.cuda.current_device()
+    if dev not in _SMS:
+        _SMS[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    sms = _SMS[dev]
+    want = max(1, (sms * 16) // max(1, B * Hkv))
+    return int(max(1, min(want, 64, (S + 255) // 256)))
+
+
+def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCache], position, dt, dev, dc, st):
+    """`ChordAttention.forward` (fused path) + SwiGLU MLP + parallel residual."""
+    M = B * T
+    H, Hkv, D, hid = pk.H, pk.Hkv, pk.D, pk.hid
+    d = H * D
+    N_in = proj.shape[1]
+    if cache is None:
+        cache = KVLayerCache()  # no layer cache (training-mode forward): attend to this chunk only
+    if cache.wide:
+        raise NotImplementedError('wide KV caches (an export-only layout) are not used by the fused path')
+    if cache._kbuf is not None and (cache._kbuf.dtype != dt or cache._kbuf.device != dev):
+        cache.to(device=dev, dtype=dt)
+    cached = cache.length
+    q_start = position if position != 0 else cached
+    cache.reserve(cached + T, like=proj, shape=(B, Hkv, D))
+    cap = cache._kbuf.shape[2]
+    qb = torch.empty((M, d), dtype=dt, device=dev)
+    _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
+              _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cap, None, cached, B, T, H, Hkv, D, NORM_EPS, dc, st)
+    cache.length = cached + T
+    S = cache.length
+    attn = torch.empty((M, d), dtype=dt, device=dev)
+    scale = D ** -0.5
+    G = H // Hkv
+    if q_start == S - T and G * T <= 16 and D in (32, 64):
+        splits = _decode_splits(model, B, Hkv, S)
+        ws_bytes = _lib.load().motif_b200_chord_decode_workspace_bytes(B, H, T, D, splits)
+        ws = torch.empty((ws_bytes // 4,), dtype=torch.float32, device=dev)
+        _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cap, None,
+                  S, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax), _lib.ptr(attn), d,
+                  B, H, Hkv, T, D, scale, GGD_EPS, splits, _lib.ptr(ws), ws_bytes, dc, st)
+    else:
+        log_n = _log_n(q_start, T, dev)
+        strides = [T * d, D, d, Hkv * cap * D, cap * D, D, Hkv * cap * D, cap * D, D, T * d, D, d, 0, 1]
+        _lib.call('motif_b200_chord_attention', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf),
+                  _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax), _lib.ptr(log_n),
+                  _lib.ptr(attn), B, H, Hkv, T, S, D, q_start, scale, GGD_EPS, _lib.i64_array(strides), dc, None, 0, st)
+    act = torch.empty((M, hid), dtype=dt, device=dev)
+    _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid, N_in,
+              hid, dc, st)
+    f = _mm(act, pk.w_down)
+    a = _mm(attn, pk.w_o)
+    _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(), N_in,
+              _lib.ptr(f), d, _lib.ptr(f), d, M, d, dc, st)
+    return f
+
+
+_LOG_TABLE: Dict[str, torch.Tensor] = {}
+
+
+def _log_n(q_start: int, T: int, dev) -> torch.Tensor:
+    """`log(q_start + 1 .. q_start + T)` from a cached table (`chord_attn.py:21-43,282`)."""
+    key = str(dev)
+    n = q_start + T
+    table = _LOG_TABLE.get(key)
+    if table is None or table.numel() < n:
+        size = 1 << (max(n, 8192) - 1).bit_length()
+        table = torch.log(torch.arange(1, size + 1, device=dev, dtype=torch.float32))
+        _LOG_TABLE[key] = table
+    return table[q_start:q_start + T].view(1, T)

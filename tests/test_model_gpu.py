@@ -1,0 +1,144 @@
+"""Model-level parity of `motif_b200.model.MotifChordModel` (CUDA) against the reference.
+
+* fp32: logits within 1e-5 relative of the golden reference outputs / the CPU oracle;
+  greedy decode token ids bit-exact (config 1: 64 steps).
+* bf16: the reference's own bf16 torch path differs from its fp32 path by far more than
+  2e-2 on these random-init models (0.08 on the small model, 0.13 on config 1, measured
+  by the golden generator), so the bf16 bar is: our bf16 logits stay within
+  max(2e-2, that reference bf16 noise) of the fp32 oracle run on the same bf16 weights.
+"""
+
+import os
+
+import pytest
+import torch
+
+from motif_b200.config import MotifChordConfig, tiny_config
+from motif_b200.init import init_params
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
+SMALL = dict(vocab_size=512, model_dim=64, num_heads=4, num_kv_heads=2, head_k_dim=16,
+             block=('gdn', 'gdn', 'gdn', 'chord'), block_n=2)
+
+
+def load(name):
+    return torch.load(os.path.join(GOLD, f'{name}.pt'))
+
+
+def rel_err(a, b):
+    a, b = a.detach().double().cpu(), b.detach().double().cpu()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+def build(cfg, seed=0, jitter=0.0, dtype=torch.float32):
+    from motif_b200.model import MotifChordModel
+    torch.manual_seed(0)
+    m = MotifChordModel(cfg)
+    init_params(m, seed=seed, norm_jitter=jitter)
+    return m.to('cuda', dtype).eval()
+
+
+def test_small_fp32_golden():
+    d = load('small_fp32')
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    ids = d['ids'].cuda()
+    with torch.no_grad():
+        full = m(ids).logits
+        assert rel_err(full, d['logits']) < 1e-5, rel_err(full, d['logits'])
+        out = m(ids[:, :24])
+        steps = []
+        for t in range(24, 40):
+            out = m(ids[:, t:t + 1], cache=out.cache)
+            steps.append(out.logits[:, 0])
+        assert rel_err(torch.stack(steps, 1), d['decode_logits']) < 1e-5
+    gen = m.generate(ids[:, :16], max_new_tokens=24).run().generated
+    assert torch.equal(gen.cpu(), d['greedy'])
+
+
+def test_small_chunked_prefill_matches_full():
+    """`tests/test_unified_cache.py:173-188` on the fused path."""
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    ids = torch.randint(0, 512, (2, 200), generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad():
+        full = m(ids).logits
+        cache = m.create_cache()
+        for s in range(0, 200, 70):
+            out = m(ids[:, s:s + 70], cache=cache)
+            cache = out.cache
+            assert rel_err(out.logits, full[:, s:s + 70]) < 1e-5
+        assert cache.seq_len == 200
+
+
+def test_small_cache_structure_and_reset():
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    ids = torch.randint(0, 512, (2, 6), generator=torch.Generator().manual_seed(2)).cuda()
+    with torch.no_grad():
+        out = m(ids)
+        for bc in out.cache:
+            assert len(bc.attn) == 4 and bc.seq_len == 6 and len(bc.blocks) == 5
+            assert bc.blocks[0].shape == (2, 6, 64)
+            assert bc.attn[3].k.shape == (2, 2, 6, 16)
+            assert bc.attn[0].state.shape == (2, 4, 16, 32)
+            assert [c.shape for c in bc.attn[0].conv_state] == [(2, 64, 3), (2, 64, 3), (2, 128, 3)]
+        first = out.logits.clone()
+        out.reset_caches()
+        again = m(ids, cache=out.cache)
+        assert torch.allclose(again.logits, first, atol=1e-6)
+        # hidden_states = final RMSNorm output, like the reference
+        ref, hid, _ = om.forward(om.make_params(MotifChordConfig(**SMALL), 0, 0.1), MotifChordConfig(**SMALL),
+                                 ids.cpu())
+        assert rel_err(again.hidden_states, hid) < 1e-5
+
+
+def test_small_bf16_within_reference_noise():
+    d = load('small_bf16')
+    cfg = MotifChordConfig(**SMALL)
+    m = build(cfg, jitter=0.1, dtype=torch.bfloat16)
+    ids = d['ids'].cuda()
+    with torch.no_grad():
+        ours = m(ids).logits.float().cpu()
+    P = {k: v.to(torch.bfloat16).float() for k, v in om.make_params(cfg, 0, 0.1).items()}
+    fp32, _, _ = om.forward(P, cfg, d['ids'])
+    ref_noise = (d['logits'] - fp32).abs().max().item()
+    ours_err = (ours - fp32).abs().max().item()
+    print(f'bf16 logits: ours vs fp32 {ours_err:.4f}, reference bf16 vs fp32 {ref_noise:.4f}')
+    assert ours_err <= max(2e-2, ref_noise)
+
+
+def test_tiny_config_fp32_golden_and_greedy64():
+    """Config 1: logits vs the reference (rtol 1e-5) and 64 greedy tokens bit-exact."""
+    d = load('tiny')
+    m = build(tiny_config())
+    ids = d['ids'].cuda()
+    with torch.no_grad():
+        lg = m(ids).logits[0]
+    assert rel_err(lg[-2:], d['last_logits']) < 1e-5
+    assert rel_err(lg.max(-1).values, d['pos_max']) < 1e-5
+    assert torch.equal(lg.argmax(-1).cpu(), d['pos_argmax'])
+    gen = m.generate(ids, max_new_tokens=64).run().generated
+    assert torch.equal(gen.cpu(), d['greedy']), (gen.cpu() != d['greedy']).nonzero()
+
+
+def test_172m_bf16_prefill_and_decode_vs_oracle():
+    """172M-class architecture (kv=3, 12 heads, 4 blocks), bf16, B=2 x T=160 prefill + 4 steps."""
+    from motif_b200.config import config_172m
+    cfg = config_172m()
+    m = build(cfg, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (2, 164), generator=g)
+    with torch.no_grad():
+        full = m(ids[:, :160].cuda())
+        steps = []
+        cache = full.cache
+        for t in range(160, 164):
+            o = m(ids[:, t:t + 1].cuda(), cache=cache)
+            cache = o.cache
+            steps.append(o.logits[:, 0].float().cpu())
+    P = {k: v.to(torch.bfloat16).float() for k, v in om.make_params(cfg, 0).items()}
+    ref, _, _ = om.forward(P, cfg, ids)
+    e_pre = (full.logits.float().cpu() - ref[:, :160]).abs().max().item()
+    e_dec = (torch.stack(steps, 1) - ref[:, 160:]).abs().max().item()
+    print(f'172M bf16: prefill max-abs {e_pre:.4f}, decode max-abs {e_dec:.4f}, |logits| max {ref.abs().max():.3f}')
+    assert e_pre < 5e-2 and e_dec < 5e-2

@@ -2,8 +2,8 @@
 
 Tolerances (stated per the north-star): fp32 inputs -> max relative error 1e-5 against the
 fp32 oracle; 16-bit inputs -> the oracle is run in fp32 on the same (rounded) inputs and the
-kernel must stay within the 16-bit output rounding (rel 1e-2 for attention outputs, which
-are written in bf16; 2e-3 for the delta rule whose state stays fp32).
+kernel must stay within the 16-bit output rounding (rel 1e-2: outputs and the returned
+state are in the input dtype, as the reference returns them).
 """
 
 import os
@@ -92,9 +92,9 @@ def test_chunk_16bit_vs_oracle(ops, dtype, L):
     q, k, v = (t.to(dtype) for t in (q, k, v))
     ro, rS = oo.chunk_gated_delta_rule(q.float(), k.float(), v.float(), beta, g, S0)
     o, S = ops.chunk_gated_delta_rule(*cuda(q, k, v, beta, g, S0))
-    assert o.dtype == dtype
+    assert o.dtype == dtype and S.dtype == dtype  # the reference returns S in q's dtype
     assert rel_err(o.float(), ro) < 1e-2, rel_err(o.float(), ro)
-    assert rel_err(S.float(), rS) < 2e-3, rel_err(S.float(), rS)
+    assert rel_err(S.float(), rS) < 1e-2, rel_err(S.float(), rS)
 
 
 def test_chunk_split_sequence_property(ops):
@@ -132,7 +132,7 @@ def test_gdn_op_config_full_size(ops):
     ro, rS = oo.chunk_gated_delta_rule(q[:1, :2].float(), k[:1, :2].float(), v[:1, :2].float(),
                                        beta[:1, :2], g[:1, :2])
     assert rel_err(o[:1, :2].float(), ro) < 1e-2
-    assert rel_err(S[:1, :2].float(), rS) < 2e-3
+    assert rel_err(S[:1, :2].float(), rS) < 1e-2
     assert torch.isfinite(o).all() and torch.isfinite(S).all()
 
 
