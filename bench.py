@@ -1,0 +1,382 @@
+"""Benchmark of the Motif Chord hot path on B200: 172M-class bf16 prefill (config 4).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+One step = one `MotifChordModel.forward` over this rank's shard of the 32 x 4096 token
+batch (sequences split evenly across ranks; no collective on the hot path), logits over
+all positions included.  Prints ONE JSON line on rank 0.
+
+* `value`      — whole-job prefill tokens/s, inputs resident in HBM, device time (CUDA
+                 events on the launching stream), max over ranks.
+* `e2e`        — the same metric through the public API with host buffers: pinned int64
+                 ids -> device, forward, greedy next token -> host, every step.
+* `roofline`   — the dominant kernel of this library (by time), its algorithmic work per
+                 launch over its CUDA-event duration inside the timed region.
+* `kernels`    — per-kernel breakdown of one instrumented step (CUDA events per call).
+* `cpu_baseline` — the CPU oracle (the reference's torch algorithm restated) timed on this
+                 box's host cores on a bounded sample (B=1 x T=4096), rank 0 at N=1.
+* `--impl reference` times that CPU implementation alone on the same metric.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+GLOBAL_BATCH = 32
+SEQ_LEN = 4096
+METRIC = 'prefill_tokens_per_s'
+UNIT = 'tokens/s'
+FALLBACK_PEAKS = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {'hbm_gbs': float(d['hbm_gbs']), 'bf16_tflops': float(d['bf16_tflops']),
+                'bf16_tflops_sustained': float(d.get('bf16_tflops_sustained', d['bf16_tflops'])),
+                'source': 'measured'}
+    return dict(FALLBACK_PEAKS, bf16_tflops_sustained=1400.0, source='fallback')
+
+
+# ---------------------------------------------------------------- algorithmic work
+def kernel_work(name, cfg, B, T):
+    """(flops, bytes) one launch of `name` does on a [B, T] prefill of `cfg` (bf16)."""
+    d, H, Hkv = cfg.model_dim, cfg.num_heads, cfg.kv_heads
+    dk, dv, D, hid, V = cfg.gdn_dk, cfg.gdn_dv, cfg.head_dim, cfg.mlp_hidden, cfg.vocab_size
+    M = B * T
+    C = 64
+    if name == 'motif_b200_gdn_chunk_gated':
+        # per token per head: G1, QK, W (2*C*dk each), U (2*C*dv), WS, qS, K^T X (2*dk*dv each), Aq X (2*C*dv)
+        f_tok = 3 * 2 * C * dk + 2 * 2 * C * dv + 3 * 2 * dk * dv
+        by_tok = 2 * (2 * dk + dv) + 8 + 2 * dv + 2 * dv  # q,k,v in, beta+g, gate in, o out
+        return M * H * f_tok, M * H * by_tok + B * H * dk * dv * 4
+    if name == 'motif_b200_chord_attention':
+        pairs = T * (T + 1) / 2
+        return 4 * B * H * D * pairs, M * (2 * H + 2 * Hkv) * D * 2
+    if name == 'motif_b200_gdn_prep':
+        cin = H * (2 * dk + dv) + 2 * H
+        return 0, M * cin * 2 + M * H * (2 * dk + dv) * 2 + M * H * 8
+    if name == 'motif_b200_attn_res_norm':
+        return 0, None  # depends on the source count; filled by the caller
+    if name == 'motif_b200_swiglu':
+        return 0, M * hid * 3 * 2
+    if name == 'motif_b200_chord_prep':
+        return 0, M * (H + 2 * Hkv) * D * 2 * 2
+    if name == 'motif_b200_gate_residual':
+        return 0, M * d * 4 * 2
+    if name == 'motif_b200_embed':
+        return 0, M * d * 2 * 2 + M * 8
+    return 0, 0
+
+
+def gemm_flops(cfg, B, T):
+    """Total cuBLAS GEMM flops of one forward (packed projections, K-concat residual, lm_head)."""
+    d, H, Hkv = cfg.model_dim, cfg.num_heads, cfg.kv_heads
+    dk, dv, D, hid, V = cfg.gdn_dk, cfg.gdn_dv, cfg.head_dim, cfg.mlp_hidden, cfg.vocab_size
+    M = B * T
+    n_gdn = sum(t != 'chord' for t in cfg.block) * cfg.block_n
+    n_chord = sum(t == 'chord' for t in cfg.block) * cfg.block_n
+    gdn = 2 * M * d * (2 * H * dk + 2 * H * dv + 2 * H + 2 * hid) + 2 * M * d * (H * dv + hid)
+    chord = 2 * M * d * (2 * d + 2 * Hkv * D + 2 * hid) + 2 * M * d * d + 2 * M * d * hid
+    return n_gdn * gdn + n_chord * chord + 2 * M * d * V
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.idx = gpu_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200', '-i', str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(n)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': mx, 'reasons': ['unsampled'], 'samples': 0}
+        load = [s for s in sm if mx is None or s > 0.5 * mx] or sm
+        return {'sm_mhz': statistics.median(load), 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ---------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device('cuda', local))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------- CPU baseline
+_CPU_PARAMS = {}
+
+
+def cpu_oracle_rate(seq_len=SEQ_LEN, batch=1):
+    """The CPU oracle (reference torch algorithm) forward at batch x seq_len, fp32, all cores."""
+    from motif_b200.config import config_172m
+    from oracle import model as om
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = config_172m()
+    if 'P' not in _CPU_PARAMS:
+        _CPU_PARAMS['P'] = om.make_params(cfg, 0, dtype=torch.float32)
+    P = _CPU_PARAMS['P']
+    ids = torch.randint(0, cfg.vocab_size, (batch, seq_len), generator=torch.Generator().manual_seed(0))
+    t0 = time.perf_counter()
+    om.forward(P, cfg, ids)
+    dt = time.perf_counter() - t0
+    return batch * seq_len / dt, threads, dt
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    steps, warm = args.steps, args.warmup
+    rates = []
+    threads = os.cpu_count() or 1
+    t_all = time.perf_counter()
+    sample_len = args.ref_seq_len
+    for i in range(warm + steps):
+        r, threads, _ = cpu_oracle_rate(seq_len=sample_len)
+        if i >= warm:
+            rates.append(r)
+    value = statistics.mean(rates)
+    sample = f'B=1 x T={sample_len} prefill of the 172M config per step, fp32 CPU oracle (reference torch path)'
+    line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': steps, 'warmup': warm,
+            'ms_per_step': 1000.0 * sample_len / value, 'higher_is_better': True, 'scaling': 'strong',
+            'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic', 'impl': 'reference',
+            'config': {'workload': '172M prefill (bounded CPU sample)', 'global_batch': 1, 'seq_len': sample_len},
+            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample},
+            'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+            'wall_s': time.perf_counter() - t_all}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, world, rank, local):
+    from motif_b200 import _lib
+    from motif_b200.config import config_172m
+    from motif_b200.init import init_params
+    from motif_b200.model import MotifChordModel
+
+    dev = torch.device('cuda', local)
+    torch.cuda.set_device(dev)
+    cfg = config_172m()
+    if GLOBAL_BATCH % world:
+        raise SystemExit(f'global batch {GLOBAL_BATCH} is not divisible by {world} ranks')
+    B = GLOBAL_BATCH // world
+    T = args.seq_len
+    torch.manual_seed(0)
+    model = MotifChordModel(cfg)
+    init_params(model, seed=0)
+    model = model.to(dev, torch.bfloat16).eval()
+    ids_all = torch.randint(0, cfg.vocab_size, (GLOBAL_BATCH, T), generator=torch.Generator().manual_seed(0))
+    ids_host = ids_all[rank * B:(rank + 1) * B].contiguous().pin_memory()
+    ids_dev = ids_host.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return model(ids_dev).logits
+
+    # warm-up (also builds the packed weights and the cuBLAS handles)
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize(dev)
+    del out
+
+    # one instrumented step: per-kernel CUDA-event breakdown (outside the timed region)
+    tr = _lib.Tracker(timed=None)
+    _lib.set_tracker(tr)
+    out = step()
+    torch.cuda.synchronize(dev)
+    _lib.set_tracker(None)
+    del out
+    summ = tr.summary()
+    mine = {k: v for k, v in summ.items() if k.startswith('motif_b200_')}
+    dominant = max(mine, key=lambda k: mine[k][1])
+
+    # timed region: events only around the dominant kernel's launches
+    tr = _lib.Tracker(timed={dominant})
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        _lib.set_tracker(tr)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        _lib.set_tracker(None)
+    barrier(world)
+    del out
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+    dom = tr.summary().get(dominant, (0, 0.0))
+    launches = tr.launches
+
+    # end to end through the public API with host buffers
+    def e2e_step():
+        ids = ids_host.to(dev, non_blocking=True)
+        o = model(ids)
+        tok = o.next_token()
+        return tok.to('cpu')
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        tok = e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+
+    tokens = GLOBAL_BATCH * T * args.steps
+    value = tokens / (elapsed_ms / 1000.0)
+    pk = peaks()
+    kernels = {}
+    for name, (calls, tot) in sorted(summ.items(), key=lambda kv: -kv[1][1]):
+        kernels[name.replace('motif_b200_', '')] = {'calls': calls, 'ms': round(tot, 4)}
+    gf = gemm_flops(cfg, B, T)
+    if 'cublas_gemm' in summ:
+        kernels['cublas_gemm']['tflops'] = round(gf / (summ['cublas_gemm'][1] / 1000.0) / 1e12, 1)
+    flops, byts = kernel_work(dominant, cfg, B, T)
+    avg_s = dom[1] / max(dom[0], 1) / 1000.0
+    if flops and flops / max(byts, 1) > pk['bf16_tflops'] * 1e12 / (pk['hbm_gbs'] * 1e9):
+        roof = {'bound': 'tensor', 'achieved': flops / avg_s / 1e12, 'peak': pk['bf16_tflops'], 'unit': 'TFLOP/s'}
+    else:
+        roof = {'bound': 'hbm', 'achieved': byts / avg_s / 1e9, 'peak': pk['hbm_gbs'], 'unit': 'GB/s'}
+    roof['frac'] = roof['achieved'] / roof['peak']
+    roof['traffic'] = None
+    roof['kernel'] = dominant
+    roof['launches_timed'] = dom[0]
+    roof['avg_launch_ms'] = avg_s * 1000.0
+    if flops:
+        roof['tflops'] = flops / avg_s / 1e12
+        roof['tensor_frac_of_measured_bf16'] = roof['tflops'] / pk['bf16_tflops']
+    roof['gbs'] = byts / avg_s / 1e9
+    roof['hbm_frac_of_measured'] = roof['gbs'] / pk['hbm_gbs']
+    roof['peak_source'] = pk['source']
+
+    result = {
+        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': elapsed_ms / args.steps, 'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None,
+        'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': '172M-class MotifChord prefill, logits over all positions (config 4)',
+                   'global_batch': GLOBAL_BATCH, 'seq_len': T, 'per_rank_batch': B,
+                   'parallelism': f'sequence-sharded replicas x{world}, no hot-path collective',
+                   'l2': 'inputs larger than L2 (every activation >= 200 MB at B=32)'},
+        'e2e': {'value': tokens / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': ids_host.numel() * 8,
+                'd2h_bytes_per_step': int(tok.numel() * 8)},
+        'gpu_launches': launches,
+        'roofline': roof,
+        'kernels': kernels,
+        'clocks': clk.summary(),
+        'peaks': pk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, dt = cpu_oracle_rate(seq_len=args.ref_seq_len)
+        result['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': threads, 'kind': 'port',
+                                  'sample': f'one B=1 x T={args.ref_seq_len} forward of the fp32 CPU oracle '
+                                            f'(reference torch algorithm), {dt:.1f} s'}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    ap.add_argument('--seq-len', type=int, default=SEQ_LEN)
+    ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    world, rank, local = dist_setup() if args.impl == 'ours' else (
+        int(os.environ.get('WORLD_SIZE', '1')), int(os.environ.get('RANK', '0')), 0)
+    if world != args.gpus:
+        print(f'warning: --gpus {args.gpus} but WORLD_SIZE {world}', file=sys.stderr)
+    try:
+        if args.impl == 'reference':
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1 and args.impl == 'ours':
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

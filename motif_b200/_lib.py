@@ -109,10 +109,64 @@ def ptr(t):
     return None if t is None else t.data_ptr()
 
 
+# Kernels each entry point launches (for launch accounting); 0 = host-only query.
+KERNELS_PER_CALL = {n: 1 for n in SIGNATURES}
+KERNELS_PER_CALL.update({'motif_b200_last_error': 0, 'motif_b200_abi_version': 0,
+                         'motif_b200_chord_workspace_bytes': 0, 'motif_b200_chord_decode_workspace_bytes': 0,
+                         'motif_b200_chord_decode': 2})
+
+
+class Tracker:
+    """Counts kernel launches and (optionally) times calls with CUDA events on the
+    current stream.  `timed` names the entry points to bracket with events (None = all)."""
+
+    def __init__(self, timed=None, events=True):
+        self.launches = 0
+        self.timed = timed
+        self.events = events
+        self.records = []  # (name, start_event, end_event)
+
+    def start(self, name):
+        if self.events and (self.timed is None or name in self.timed):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            return ev
+        return None
+
+    def stop(self, name, ev):
+        self.launches += KERNELS_PER_CALL.get(name, 1)
+        if ev is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            self.records.append((name, ev, end))
+
+    def summary(self):
+        """`{name: (calls, total_ms)}` (call after synchronising)."""
+        out = {}
+        for name, a, b in self.records:
+            c, t = out.get(name, (0, 0.0))
+            out[name] = (c + 1, t + a.elapsed_time(b))
+        return out
+
+
+_tracker = None
+
+
+def set_tracker(tr):
+    """Install (or remove with None) the launch tracker; returns the previous one."""
+    global _tracker
+    prev, _tracker = _tracker, tr
+    return prev
+
+
 def call(name: str, *args) -> None:
     """Call one entry point and raise on a nonzero status."""
     lib = load()
+    tr = _tracker
+    ev = tr.start(name) if tr is not None else None
     rc = getattr(lib, name)(*args)
+    if tr is not None and rc == MB_OK:
+        tr.stop(name, ev)
     if rc != MB_OK:
         msg = lib.motif_b200_last_error().decode(errors='replace')
         if rc in (MB_ERR_ARG, MB_ERR_SHAPE, MB_ERR_DTYPE, MB_ERR_ALIGN):

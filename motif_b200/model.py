@@ -419,8 +419,17 @@ class MotifChordModel(nn.Module):
 
 # ============================================================================ engine
 def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
-    """a [M, K] @ w[N, K]^T with cuBLAS (plain library GEMM)."""
-    return torch.mm(a, w.t(), out=out)
+    """a [M, K] @ w[N, K]^T with cuBLAS (plain library GEMM; timed as 'cublas_gemm' when tracked)."""
+    tr = _lib._tracker
+    if tr is None:
+        return torch.mm(a, w.t(), out=out)
+    ev = tr.start('cublas_gemm')
+    r = torch.mm(a, w.t(), out=out)
+    if ev is not None:
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        tr.records.append(('cublas_gemm', ev, end))
+    return r
 
 
 def _norm_read(sources: List[torch.Tensor], query, weight, h_out, hn_out, eps_src=NORM_EPS, eps_out=NORM_EPS):

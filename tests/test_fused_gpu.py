@@ -1,0 +1,213 @@
+"""Parity of the fused model-level kernels (one C-ABI call each) against the CPU oracle.
+
+Each fused kernel replaces a run of reference statements (cited in `include/motif_b200.h`);
+here every one is checked on its own against the oracle statements it replaces.
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from motif_b200 import _lib
+from oracle import ops as oo
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a, b = a.detach().double().cpu(), b.detach().double().cpu()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+def st():
+    return _lib.stream_ptr()
+
+
+TOL = {torch.float32: 1e-5, torch.bfloat16: 1.5e-2}
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('D', [64, 256, 768])
+@pytest.mark.parametrize('n', [1, 2, 4, 5])
+@pytest.mark.parametrize('mode', ['softmax', 'sum'])
+def test_attn_res_norm(dtype, D, n, mode):
+    g = torch.Generator().manual_seed(D + n)
+    rows = 37
+    srcs = [torch.randn(rows, D, generator=g).to(dtype) for _ in range(n)]
+    w = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype)
+    qv = (torch.randn(D, generator=g) / D ** 0.5).to(dtype)
+    if mode == 'softmax':
+        h = oo.attn_res([s.float()[None] for s in srcs], qv.float(), w.float())[0] if n > 1 else srcs[0].float()
+    else:
+        h = sum(s.float() for s in srcs)
+    hn = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)
+    cs = [s.cuda() for s in srcs]
+    h_out = torch.empty(rows, D, dtype=dtype, device='cuda')
+    hn_out = torch.empty(rows, D, dtype=dtype, device='cuda')
+    wq = (w.cuda(), qv.cuda()) if mode == 'softmax' else (None, None)
+    _lib.call('motif_b200_attn_res_norm', _lib.ptr_array([t.data_ptr() for t in cs]), n, D, _lib.ptr(wq[0]),
+              _lib.ptr(wq[1]), _lib.ptr(h_out), _lib.ptr(hn_out), D, rows, D, 1e-6, 1e-6, _lib.dtype_code(dtype), st())
+    assert rel_err(h_out.float(), h) < TOL[dtype], rel_err(h_out.float(), h)
+    assert rel_err(hn_out.float(), hn) < TOL[dtype], rel_err(hn_out.float(), hn)
+
+
+def gdn_setup(B, T, H, dk, dv, dtype, seed, with_conv=True):
+    g = torch.Generator().manual_seed(seed)
+    C = H * (2 * dk + dv)
+    N = C + 2 * H + 40  # extra trailing columns, as in the packed projection
+    proj = (0.5 * torch.randn(B, T, N, generator=g)).to(dtype)
+    conv_w = (0.3 * torch.randn(C, 4, generator=g)).to(dtype)
+    A_log = torch.log(1 + 15 * torch.rand(H, generator=g)).to(dtype)
+    dt_bias = (0.1 * torch.randn(H, generator=g)).to(dtype)
+    conv_in = (0.5 * torch.randn(B, 3, C, generator=g)).to(dtype) if with_conv else None
+    return proj, conv_w, A_log, dt_bias, conv_in, C, N
+
+
+def gdn_prep_oracle(proj, conv_w, A_log, dt_bias, conv_in, B, T, H, dk, dv):
+    f = proj.float()
+    C = H * (2 * dk + dv)
+    x = f[..., :C]
+    cache = conv_in.float().transpose(1, 2) if conv_in is not None else None
+    y, new_cache = oo.causal_conv_silu(x, conv_w.float().view(C, 1, 4), cache)
+    q = y[..., :H * dk].view(B, T, H, dk)
+    k = y[..., H * dk:2 * H * dk].view(B, T, H, dk)
+    v = y[..., 2 * H * dk:].view(B, T, H, dv)
+    q = F.normalize(q, dim=-1) * dk ** -0.5
+    k = F.normalize(k, dim=-1)
+    a = f[..., C:C + H]
+    b = f[..., C + H:C + 2 * H]
+    beta = torch.sigmoid(b)
+    gg = -A_log.float().exp() * F.softplus(a + dt_bias.float())
+    return q, k, v, beta, gg, new_cache.transpose(1, 2)
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('B,T,H,dk,dv,with_conv', [(2, 37, 3, 64, 128, True), (1, 2, 12, 64, 128, False),
+                                                   (2, 70, 4, 16, 32, True), (1, 16, 2, 32, 64, True)])
+def test_gdn_prep(dtype, B, T, H, dk, dv, with_conv):
+    proj, conv_w, A_log, dt_bias, conv_in, C, N = gdn_setup(B, T, H, dk, dv, dtype, seed=T)
+    q, k, v, beta, gg, cout = gdn_prep_oracle(proj, conv_w, A_log, dt_bias, conv_in, B, T, H, dk, dv)
+    M = B * T
+    qb = torch.empty(M, H * dk, dtype=dtype, device='cuda')
+    kb = torch.empty_like(qb)
+    vb = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+    be = torch.empty(M, H, device='cuda')
+    ge = torch.empty(M, H, device='cuda')
+    co = torch.empty(B, 3, C, dtype=dtype, device='cuda')
+    p, cw, al, db = (t.cuda() for t in (proj, conv_w, A_log, dt_bias))
+    ci = conv_in.cuda() if conv_in is not None else None
+    _lib.call('motif_b200_gdn_prep', _lib.ptr(p), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db), _lib.ptr(ci),
+              _lib.ptr(co), _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(be), _lib.ptr(ge), B, T, H, dk, dv,
+              _lib.dtype_code(dtype), st())
+    tol = TOL[dtype]
+    assert rel_err(qb.view(B, T, H, dk).float(), q) < tol
+    assert rel_err(kb.view(B, T, H, dk).float(), k) < tol
+    assert rel_err(vb.view(B, T, H, dv).float(), v) < tol
+    assert rel_err(be.view(B, T, H), beta) < tol
+    assert rel_err(ge.view(B, T, H), gg) < tol
+    assert rel_err(co.float(), cout) < tol
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('B,H,dk,dv', [(3, 12, 64, 128), (2, 4, 16, 32)])
+def test_gdn_decode(dtype, B, H, dk, dv):
+    proj, conv_w, A_log, dt_bias, conv_in, C, _ = gdn_setup(B, 1, H, dk, dv, dtype, seed=B * H)
+    g = torch.Generator().manual_seed(11)
+    N = C + 2 * H + H * dv
+    proj = torch.cat([proj[..., :C + 2 * H], (0.5 * torch.randn(B, 1, H * dv, generator=g)).to(dtype)], -1)
+    state = 0.1 * torch.randn(B, H, dk, dv, generator=g)
+    onw = (1 + 0.1 * torch.randn(dv, generator=g)).to(dtype)
+    q, k, v, beta, gg, cout = gdn_prep_oracle(proj, conv_w, A_log, dt_bias, conv_in, B, 1, H, dk, dv)
+    o, S = oo.recurrent_gated_delta_rule(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                         beta.transpose(1, 2), gg.transpose(1, 2), state)
+    gate = proj[..., C + 2 * H:].float().view(B, 1, H, dv)
+    ref = oo.gated_rms_norm(torch.cat([o.transpose(1, 2), gate], -1), onw.float()).reshape(B, H * dv)
+    p, cw, al, db, ci, sd, ow = (t.cuda() for t in (proj, conv_w, A_log, dt_bias, conv_in, state, onw))
+    out = torch.empty(B, H * dv, dtype=dtype, device='cuda')
+    _lib.call('motif_b200_gdn_decode', _lib.ptr(p), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db), _lib.ptr(ci),
+              _lib.ptr(sd), p.data_ptr() + (C + 2 * H) * p.element_size(), _lib.ptr(ow), _lib.ptr(out), H * dv,
+              B, H, dk, dv, 1e-6, _lib.dtype_code(dtype), st())
+    tol = TOL[dtype]
+    assert rel_err(sd, S) < max(tol, 1e-5)
+    assert rel_err(ci.float(), cout) < tol
+    assert rel_err(out.float(), ref) < (1e-5 if dtype == torch.float32 else 3e-2)
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('B,T,H,Hkv,D,pos', [(2, 5, 12, 3, 64, 0), (3, 1, 4, 2, 16, 17), (1, 33, 8, 8, 32, 4)])
+def test_chord_prep(dtype, B, T, H, Hkv, D, pos):
+    g = torch.Generator().manual_seed(T + pos)
+    N = (H + 2 * Hkv) * D + 24
+    proj = torch.randn(B * T, N, generator=g).to(dtype)
+    qw = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype)
+    kw = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype)
+    cap = pos + T + 3
+    qo = torch.empty(B * T, H * D, dtype=dtype, device='cuda')
+    kc = torch.zeros(B, Hkv, cap, D, dtype=dtype, device='cuda')
+    vc = torch.zeros_like(kc)
+    # keep every device tensor alive across the call (a temporary's block could be reused)
+    pc, qwc, kwc = proj.cuda(), qw.cuda(), kw.cuda()
+    _lib.call('motif_b200_chord_prep', _lib.ptr(pc), N, _lib.ptr(qwc), _lib.ptr(kwc),
+              _lib.ptr(qo), _lib.ptr(kc), _lib.ptr(vc), cap, None, pos, B, T, H, Hkv, D, 1e-6,
+              _lib.dtype_code(dtype), st())
+    P = proj.view(B, T, N)
+    q = oo.rms_norm(P[..., :H * D].reshape(B, T, H, D), qw)
+    k = oo.rms_norm(P[..., H * D:(H + Hkv) * D].reshape(B, T, Hkv, D), kw)
+    v = P[..., (H + Hkv) * D:(H + 2 * Hkv) * D].reshape(B, T, Hkv, D)
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    assert rel_err(qo.view(B, T, H, D).float(), q.float()) < tol
+    assert rel_err(kc[:, :, pos:pos + T].float(), k.transpose(1, 2).float()) < tol
+    assert torch.equal(vc[:, :, pos:pos + T].cpu(), v.transpose(1, 2))
+    assert kc[:, :, :pos].abs().sum() == 0 and kc[:, :, pos + T:].abs().sum() == 0
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('B,H,Hkv,T,S,D,splits', [(2, 12, 3, 1, 1000, 64, 7), (3, 4, 2, 2, 33, 32, 4),
+                                                  (1, 8, 8, 1, 5000, 64, 64), (2, 4, 1, 4, 300, 32, 1)])
+def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits):
+    g = torch.Generator().manual_seed(S + T)
+    cap = S + 10
+    q = torch.randn(B, T, H, D, generator=g).to(dtype)
+    kc = torch.randn(B, Hkv, cap, D, generator=g).to(dtype)
+    vc = torch.randn(B, Hkv, cap, D, generator=g).to(dtype)
+    alpha = 0.5 + 1.5 * torch.rand(H, generator=g)
+    beta = torch.rand(H, generator=g)
+    mu = torch.ones(H)
+    ssmax = 0.8 + 0.4 * torch.rand(H, generator=g)
+    q_start = S - T
+    log_n = oo.log_n_table(q_start, T).view(1, T).expand(B, T)
+    ref = oo.chord_attention(q.transpose(1, 2).float(), kc[:, :, :S].float(), vc[:, :, :S].float(), alpha, beta, mu,
+                             ssmax, log_n, q_start)
+    out = torch.empty(B * T, H * D, dtype=dtype, device='cuda')
+    ws_bytes = _lib.load().motif_b200_chord_decode_workspace_bytes(B, H, T, D, splits)
+    ws = torch.empty(ws_bytes // 4, device='cuda')
+    length = torch.tensor([S], dtype=torch.int32, device='cuda')
+    a = [t.cuda() for t in (alpha, beta, mu, ssmax)]
+    qc, kcc, vcc = q.cuda(), kc.cuda(), vc.cuda()
+    _lib.call('motif_b200_chord_decode', _lib.ptr(qc), _lib.ptr(kcc), _lib.ptr(vcc), cap,
+              _lib.ptr(length), 0, *[_lib.ptr(t) for t in a], _lib.ptr(out), H * D, B, H, Hkv, T, D, D ** -0.5,
+              1e-5, splits, _lib.ptr(ws), ws_bytes, _lib.dtype_code(dtype), st())
+    got = out.view(B, T, H, D).transpose(1, 2).float()
+    assert rel_err(got, ref) < (1e-5 if dtype == torch.float32 else 1e-2), rel_err(got, ref)
+
+
+def test_gate_residual_argmax_embed():
+    g = torch.Generator().manual_seed(0)
+    a, gt, m = (torch.randn(70000, 24, generator=g) for _ in range(3))
+    out = torch.empty(70000, 24, device='cuda')
+    ac, gc, mc = a.cuda(), gt.cuda(), m.cuda()
+    _lib.call('motif_b200_gate_residual', _lib.ptr(ac), 24, _lib.ptr(gc), 24, _lib.ptr(mc), 24,
+              _lib.ptr(out), 24, 70000, 24, _lib.MB_F32, st())
+    assert rel_err(out, a * torch.sigmoid(gt) + m) < 1e-6
+    x = torch.randn(5, 32000, generator=g)
+    x[2, 7] = x[2, 9] = x[2].max() + 1  # tie: first index wins, like torch.argmax
+    ids = torch.empty(5, dtype=torch.int64, device='cuda')
+    xc = x.cuda()
+    _lib.call('motif_b200_argmax', _lib.ptr(xc), 5, 32000, 32000, _lib.ptr(ids), _lib.MB_F32, st())
+    assert torch.equal(ids.cpu(), x.argmax(-1))
+    table = torch.randn(100, 48, generator=g)
+    tok = torch.randint(0, 100, (70000,), generator=g)
+    out = torch.empty(70000, 48, device='cuda')
+    tc, tbc = tok.cuda(), table.cuda()
+    _lib.call('motif_b200_embed', _lib.ptr(tc), _lib.ptr(tbc), _lib.ptr(out), 70000, 48, 100, _lib.MB_F32, st())
+    assert torch.equal(out.cpu(), table[tok])
