@@ -273,6 +273,117 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(
   }
 }
 
+// Vectorised preparation: one CTA per (b, block of TBT tokens); thread c owns 8 consecutive
+// channels of the q | k | v projection (16-byte loads / stores), keeps their last three raw
+// inputs in registers and walks the token block.  L2 norms of q / k heads reduce over the
+// DK/8 threads that own one head (shuffles inside an aligned lane group).  Threads 0..H-1
+// also produce beta / g for head tid.  16-bit dtypes, DK >= 16.
+template <typename T, int DK, int DV, int TBT>
+__global__ void __launch_bounds__(512) gdn_prep_vec_kernel(
+    const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
+    const T* __restrict__ dt_bias, const T* __restrict__ conv_in, T* __restrict__ conv_out,
+    T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, float* __restrict__ beta,
+    float* __restrict__ gout, int Tn, int H) {
+  constexpr int GQ = DK / 8;  // threads per q / k head
+  const int C = H * (2 * DK + DV);
+  const int nthr = C / 8;
+  const int tid = threadIdx.x;
+  const bool active = tid < nthr;
+  const int b = blockIdx.y;
+  const int t0 = blockIdx.x * TBT;
+  const int t1 = min(t0 + TBT, Tn);
+  const int c0 = (active ? tid : 0) * 8;  // first channel of this thread
+  const int kind = c0 < H * DK ? 0 : (c0 < 2 * H * DK ? 1 : 2);  // q, k, v
+  const T* P = proj + (int64_t)b * Tn * ps;
+  float w[8][4], hist[8][3];
+  {
+    uint4 r0 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4);
+    uint4 r1 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4 + 8);
+    uint4 r2 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4 + 16);
+    uint4 r3 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4 + 24);
+    const T* e0 = reinterpret_cast<const T*>(&r0);
+    const T* e1 = reinterpret_cast<const T*>(&r1);
+    const T* e2 = reinterpret_cast<const T*>(&r2);
+    const T* e3 = reinterpret_cast<const T*>(&r3);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const T* src = i < 2 ? e0 : (i < 4 ? e1 : (i < 6 ? e2 : e3));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) w[i][j] = to_f(src[(i & 1) * 4 + j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int tau = t0 - 3 + j;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (tau >= 0)
+      raw = *reinterpret_cast<const uint4*>(P + (int64_t)tau * ps + c0);
+    else if (conv_in)
+      raw = *reinterpret_cast<const uint4*>(conv_in + ((int64_t)b * 3 + (3 + tau)) * C + c0);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hist[i][j] = to_f(e[i]);
+  }
+  const float qscale = rsqrtf((float)DK);
+  float Aexp = 0.f, dtb = 0.f;
+  if (tid < H) {
+    Aexp = -to_f(from_f<T>(expf(to_f(A_log[tid]))));
+    dtb = to_f(dt_bias[tid]);
+  }
+  for (int t = t0; t < t1; ++t) {
+    const T* row = P + (int64_t)t * ps;
+    uint4 raw = *reinterpret_cast<const uint4*>(row + c0);
+    const T* e = reinterpret_cast<const T*>(&raw);
+    float y[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = to_f(e[i]);
+      const float a = w[i][0] * hist[i][0] + w[i][1] * hist[i][1] + w[i][2] * hist[i][2] + w[i][3] * x;
+      hist[i][0] = hist[i][1];
+      hist[i][1] = hist[i][2];
+      hist[i][2] = x;
+      y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
+      ss += y[i] * y[i];
+    }
+    // group reduction over the GQ lanes of one q / k head (groups are lane-aligned)
+#pragma unroll
+    for (int o = 1; o < GQ; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int64_t tok = (int64_t)b * Tn + t;
+    T o8[8];
+    if (kind == 0) {
+      const float sc = qscale / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
+      if (active) *reinterpret_cast<uint4*>(qo + tok * H * DK + c0) = *reinterpret_cast<uint4*>(o8);
+    } else if (kind == 1) {
+      const float sc = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
+      if (active) *reinterpret_cast<uint4*>(ko + tok * H * DK + (c0 - H * DK)) = *reinterpret_cast<uint4*>(o8);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i]);
+      if (active) *reinterpret_cast<uint4*>(vo + tok * H * DV + (c0 - 2 * H * DK)) = *reinterpret_cast<uint4*>(o8);
+    }
+    if (tid < H) {
+      const float a = to_f(row[C + tid]);
+      const float bb = to_f(row[C + H + tid]);
+      beta[tok * H + tid] = to_f(from_f<T>(sigmoidf_(bb)));
+      gout[tok * H + tid] = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(a + dtb)))))));
+    }
+  }
+  if (t1 == Tn && conv_out && active) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      T o8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(hist[i][j]);
+      *reinterpret_cast<uint4*>(conv_out + ((int64_t)b * 3 + j) * C + c0) = *reinterpret_cast<uint4*>(o8);
+    }
+  }
+}
+
 template <typename F>
 int dispatch_dtype(int dtype, F&& f) {
   switch (dtype) {
@@ -379,6 +490,22 @@ extern "C" int motif_b200_gdn_prep(const void* proj, int64_t ps, const void* con
       constexpr int DK = decltype(dkc)::value;
       return dispatch_dv(Dv, [&](auto dvc) {
         constexpr int DV = decltype(dvc)::value;
+        const int64_t C = H * (2 * DK + DV);
+        const bool vec = sizeof(Tt) == 2 && ps % 8 == 0 && ((uintptr_t)proj | (uintptr_t)conv_w | (uintptr_t)q |
+                                                            (uintptr_t)k | (uintptr_t)v | (uintptr_t)conv_in |
+                                                            (uintptr_t)conv_out) % 16 == 0 &&
+                         C / 8 <= 512 && B < 65536;
+        if constexpr (sizeof(Tt) == 2) {
+          if (vec) {
+            constexpr int TBT = 64;
+            const int threads = (int)((C / 8 + 31) / 32 * 32);
+            dim3 grid((unsigned)((T + TBT - 1) / TBT), (unsigned)B);
+            gdn_prep_vec_kernel<Tt, DK, DV, TBT><<<grid, threads, 0, (cudaStream_t)stream>>>(
+                (const Tt*)proj, ps, (const Tt*)conv_w, (const Tt*)A_log, (const Tt*)dt_bias, (const Tt*)conv_in,
+                (Tt*)conv_out, (Tt*)q, (Tt*)k, (Tt*)v, beta, g, (int)T, (int)H);
+            return check_launch("gdn_prep");
+          }
+        }
         const int64_t warps = H * ((T + TB - 1) / TB);
         dim3 grid((unsigned)((warps + 3) / 4), (unsigned)B);
         gdn_prep_kernel<Tt, DK, DV, TB><<<grid, 128, 0, (cudaStream_t)stream>>>(

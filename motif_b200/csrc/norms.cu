@@ -78,6 +78,64 @@ __global__ void swiglu_kernel(const T* __restrict__ x, T* __restrict__ y, int64_
   }
 }
 
+// 16-byte vector variant: 8 elements per thread, flat grid-stride loop over [M, N/8].
+template <typename T>
+__global__ void swiglu_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int64_t xs,
+                                  int64_t ys) {
+  const int nv = N / 8;
+  const int64_t total = M * nv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / nv;
+    const int c = (int)(i % nv) * 8;
+    const T* xr = x + row * xs;
+    uint4 rv = *reinterpret_cast<const uint4*>(xr + c);
+    uint4 rg = *reinterpret_cast<const uint4*>(xr + N + c);
+    const T* v8 = reinterpret_cast<const T*>(&rv);
+    const T* g8 = reinterpret_cast<const T*>(&rg);
+    T o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float sg = to_f(from_f<T>(siluf_(to_f(g8[e]))));
+      o8[e] = from_f<T>(to_f(v8[e]) * sg);
+    }
+    *reinterpret_cast<uint4*>(y + row * ys + c) = *reinterpret_cast<const uint4*>(o8);
+  }
+}
+
+template <typename T>
+__global__ void gate_residual_vec_kernel(const T* __restrict__ a, int64_t as, const T* __restrict__ g, int64_t gs,
+                                         const T* __restrict__ m, int64_t ms, T* __restrict__ out, int64_t os,
+                                         int64_t rows, int N) {
+  const int nv = N / 8;
+  const int64_t total = rows * nv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / nv;
+    const int c = (int)(i % nv) * 8;
+    uint4 ra = *reinterpret_cast<const uint4*>(a + row * as + c);
+    uint4 rg = *reinterpret_cast<const uint4*>(g + row * gs + c);
+    uint4 rm = *reinterpret_cast<const uint4*>(m + row * ms + c);
+    const T* a8 = reinterpret_cast<const T*>(&ra);
+    const T* g8 = reinterpret_cast<const T*>(&rg);
+    const T* m8 = reinterpret_cast<const T*>(&rm);
+    T o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float gate = to_f(from_f<T>(sigmoidf_(to_f(g8[e]))));
+      const float att = to_f(from_f<T>(to_f(a8[e]) * gate));
+      o8[e] = from_f<T>(att + to_f(m8[e]));
+    }
+    *reinterpret_cast<uint4*>(out + row * os + c) = *reinterpret_cast<const uint4*>(o8);
+  }
+}
+
+inline bool vec16_ok(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+inline unsigned flat_grid(int64_t total, int threads) {
+  int64_t blocks = (total + threads - 1) / threads;
+  const int64_t cap = 148LL * 16;  // enough resident blocks to saturate HBM; grid-stride beyond
+  return (unsigned)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
 // ---------------------------------------------------------------------------- attn-res
 constexpr int kMaxSrc = 8;
 struct SrcPtrs {
@@ -396,6 +454,11 @@ extern "C" int motif_b200_swiglu(const void* x, void* y, int64_t M, int64_t N, i
   if (M == 0) return MB_OK;
   return dispatch(dtype, [&](auto t) {
     using T = decltype(t);
+    if (sizeof(T) == 2 && N % 8 == 0 && xs % 8 == 0 && ys % 8 == 0 && vec16_ok(x) && vec16_ok(y)) {
+      swiglu_vec_kernel<T><<<flat_grid(M * (N / 8), 256), 256, 0, (cudaStream_t)stream>>>((const T*)x, (T*)y, M,
+                                                                                          (int)N, xs, ys);
+      return check_launch("swiglu");
+    }
     dim3 grid((unsigned)((N + 255) / 256), (unsigned)(M < 65535 ? M : 65535));
     swiglu_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>((const T*)x, (T*)y, M, (int)N, xs, ys);
     return check_launch("swiglu");
@@ -476,6 +539,12 @@ extern "C" int motif_b200_gate_residual(const void* a, int64_t as, const void* g
   if (rows == 0) return MB_OK;
   return dispatch(dtype, [&](auto t) {
     using T = decltype(t);
+    if (sizeof(T) == 2 && N % 8 == 0 && as % 8 == 0 && gs % 8 == 0 && ms % 8 == 0 && os % 8 == 0 && vec16_ok(a) &&
+        vec16_ok(g) && vec16_ok(m) && vec16_ok(out)) {
+      gate_residual_vec_kernel<T><<<flat_grid(rows * (N / 8), 256), 256, 0, (cudaStream_t)stream>>>(
+          (const T*)a, as, (const T*)g, gs, (const T*)m, ms, (T*)out, os, rows, (int)N);
+      return check_launch("gate_residual");
+    }
     dim3 grid((unsigned)((N + 255) / 256), (unsigned)(rows < 65535 ? rows : 65535));
     gate_residual_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>((const T*)a, as, (const T*)g, gs,
                                                                    (const T*)m, ms, (T*)out, os, rows, (int)N);
