@@ -330,47 +330,65 @@ __global__ void __launch_bounds__(512) gdn_prep_vec_kernel(
     Aexp = -to_f(from_f<T>(expf(to_f(A_log[tid]))));
     dtb = to_f(dt_bias[tid]);
   }
-  for (int t = t0; t < t1; ++t) {
-    const T* row = P + (int64_t)t * ps;
-    uint4 raw = *reinterpret_cast<const uint4*>(row + c0);
-    const T* e = reinterpret_cast<const T*>(&raw);
-    float y[8];
-    float ss = 0.f;
+  // Rows are loaded PF at a time before any is used, so each thread keeps PF 16-byte loads
+  // in flight (one CTA covers all channels of a token, so the loads of a row are coalesced).
+  constexpr int PF = 4;
+  for (int tb = t0; tb < t1; tb += PF) {
+    uint4 rows[PF];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float x = to_f(e[i]);
-      const float a = w[i][0] * hist[i][0] + w[i][1] * hist[i][1] + w[i][2] * hist[i][2] + w[i][3] * x;
-      hist[i][0] = hist[i][1];
-      hist[i][1] = hist[i][2];
-      hist[i][2] = x;
-      y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
-      ss += y[i] * y[i];
-    }
-    // group reduction over the GQ lanes of one q / k head (groups are lane-aligned)
-#pragma unroll
-    for (int o = 1; o < GQ; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const int64_t tok = (int64_t)b * Tn + t;
-    T o8[8];
-    if (kind == 0) {
-      const float sc = qscale / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
-      if (active) *reinterpret_cast<uint4*>(qo + tok * H * DK + c0) = *reinterpret_cast<uint4*>(o8);
-    } else if (kind == 1) {
-      const float sc = 1.f / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
-      if (active) *reinterpret_cast<uint4*>(ko + tok * H * DK + (c0 - H * DK)) = *reinterpret_cast<uint4*>(o8);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i]);
-      if (active) *reinterpret_cast<uint4*>(vo + tok * H * DV + (c0 - 2 * H * DK)) = *reinterpret_cast<uint4*>(o8);
-    }
+    for (int u = 0; u < PF; ++u)
+      rows[u] = (tb + u < t1 && active) ? *reinterpret_cast<const uint4*>(P + (int64_t)(tb + u) * ps + c0)
+                                        : make_uint4(0, 0, 0, 0);
+    float ab[PF], bb[PF];
     if (tid < H) {
-      const float a = to_f(row[C + tid]);
-      const float bb = to_f(row[C + H + tid]);
-      beta[tok * H + tid] = to_f(from_f<T>(sigmoidf_(bb)));
-      gout[tok * H + tid] = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(a + dtb)))))));
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        const bool ok = tb + u < t1;
+        ab[u] = ok ? to_f(P[(int64_t)(tb + u) * ps + C + tid]) : 0.f;
+        bb[u] = ok ? to_f(P[(int64_t)(tb + u) * ps + C + H + tid]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < PF; ++u) {
+      const int t = tb + u;
+      if (t >= t1) break;
+      const T* e = reinterpret_cast<const T*>(&rows[u]);
+      float y[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = to_f(e[i]);
+        const float a = w[i][0] * hist[i][0] + w[i][1] * hist[i][1] + w[i][2] * hist[i][2] + w[i][3] * x;
+        hist[i][0] = hist[i][1];
+        hist[i][1] = hist[i][2];
+        hist[i][2] = x;
+        y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
+        ss += y[i] * y[i];
+      }
+      // group reduction over the GQ lanes of one q / k head (groups are lane-aligned)
+#pragma unroll
+      for (int o = 1; o < GQ; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const int64_t tok = (int64_t)b * Tn + t;
+      T o8[8];
+      if (kind == 0) {
+        const float sc = qscale / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
+        if (active) *reinterpret_cast<uint4*>(qo + tok * H * DK + c0) = *reinterpret_cast<uint4*>(o8);
+      } else if (kind == 1) {
+        const float sc = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
+        if (active) *reinterpret_cast<uint4*>(ko + tok * H * DK + (c0 - H * DK)) = *reinterpret_cast<uint4*>(o8);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i]);
+        if (active) *reinterpret_cast<uint4*>(vo + tok * H * DV + (c0 - 2 * H * DK)) = *reinterpret_cast<uint4*>(o8);
+      }
+      if (tid < H) {
+        beta[tok * H + tid] = to_f(from_f<T>(sigmoidf_(bb[u])));
+        gout[tok * H + tid] = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(ab[u] + dtb)))))));
+      }
     }
   }
   if (t1 == Tn && conv_out && active) {

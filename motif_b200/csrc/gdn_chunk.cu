@@ -18,9 +18,17 @@
 //
 // An optional epilogue applies GatedRMSNorm (rms_norm.py:547-553) to each output row with a
 // gate row read from global memory, replacing gdn_attn.py:206-209 (o_norm(cat[o, gate])).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace mb {
+
+int gdn_chunk_fast_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, const void* k, const void* v,
+                            const float* beta, const float* g, const float* s_in, float* s_out, void* o, int64_t B,
+                            int64_t H, int64_t L, const int64_t* strides, const void* gate, int64_t gate_rs,
+                            int64_t gate_hs, const void* onorm_w, float eps, cudaStream_t st, int* rc);
+
 namespace {
 
 constexpr int C = 64;
@@ -532,6 +540,15 @@ int launch_dims(int64_t Dk, int64_t Dv, const void* q, const void* k, const void
                    (long long)Dv);
 }
 
+// MOTIF_B200_GDN_PRECISE=1 routes 16-bit inputs through the 3xTF32 kernel (validation aid).
+bool force_precise() {
+  static const bool v = [] {
+    const char* e = getenv("MOTIF_B200_GDN_PRECISE");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 int gdn_chunk_impl(const void* q, const void* k, const void* v, const float* beta, const float* g,
                    const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, int64_t Dk,
                    int64_t Dv, const int64_t* strides, int dtype, const void* gate, int64_t gate_rs,
@@ -548,9 +565,13 @@ int gdn_chunk_impl(const void* q, const void* k, const void* v, const float* bet
   MB_REQUIRE(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 == 0, MB_ERR_ALIGN,
              "gdn_chunk: q/k/v must be 16-byte aligned");
   if (B == 0) return MB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = MB_OK;
+  if (!force_precise() && gdn_chunk_fast_dispatch(dtype, Dk, Dv, q, k, v, beta, g, s_in, s_out, o, B, H, L, strides,
+                                                  gate, gate_rs, gate_hs, onorm_w, eps, st, &rc))
+    return rc;
   Strides18 sv;
   for (int i = 0; i < 18; ++i) sv.s[i] = strides[i];
-  cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case MB_F32:
       return launch_dims<float>(Dk, Dv, q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs, gate_hs,
