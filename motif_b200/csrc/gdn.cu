@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(
 // DK/8 threads that own one head (shuffles inside an aligned lane group).  Threads 0..H-1
 // also produce beta / g for head tid.  16-bit dtypes, DK >= 16.
 template <typename T, int DK, int DV, int TBT>
-__global__ void __launch_bounds__(512) gdn_prep_vec_kernel(
+__global__ void __launch_bounds__(384) gdn_prep_vec_kernel(
     const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
     const T* __restrict__ dt_bias, const T* __restrict__ conv_in, T* __restrict__ conv_out,
     T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, float* __restrict__ beta,
@@ -512,7 +512,7 @@ extern "C" int motif_b200_gdn_prep(const void* proj, int64_t ps, const void* con
         const bool vec = sizeof(Tt) == 2 && ps % 8 == 0 && ((uintptr_t)proj | (uintptr_t)conv_w | (uintptr_t)q |
                                                             (uintptr_t)k | (uintptr_t)v | (uintptr_t)conv_in |
                                                             (uintptr_t)conv_out) % 16 == 0 &&
-                         C / 8 <= 512 && B < 65536;
+                         C / 8 <= 384 && B < 65536;
         if constexpr (sizeof(Tt) == 2) {
           if (vec) {
             constexpr int TBT = 64;
