@@ -48,7 +48,8 @@ struct FastLayout {
   static constexpr size_t off_td = off_s + 2ull * DK * VS * sizeof(T);
   static constexpr size_t off_ad = off_td + 4ull * 16 * TS * sizeof(T);
   static constexpr size_t off_vec = off_ad + 4ull * 16 * 17 * 4;
-  static constexpr size_t bytes = off_vec + 4ull * C * 4;
+  static constexpr size_t off_gate = off_vec + 4ull * C * 4;  // gate tiles, staged with q/k/v
+  static constexpr size_t bytes = off_gate + 2ull * C * VS * sizeof(T);
   static_assert(bytes <= 232448, "shared memory budget");
 };
 
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
   float* sEg = sGam + C;
   float* sDl = sEg + C;
   float* sBeta = sDl + C;
+  T* sG = reinterpret_cast<T*>(smem + Lay::off_gate);
 
   const int64_t* st = sv.s;
   const int bh = blockIdx.x;
@@ -141,6 +143,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
   const float* bg = beta + b * st[12] + h * st[13];
   const float* gg = g + b * st[15] + h * st[16];
   const int nchunks = (L + C - 1) / C;
+  // gate rows are token-major: row (b * L + l), head h at column offset h * gate_hs
+  const T* gbase = gate ? gate + (int64_t)b * L * gate_rs + h * gate_hs : nullptr;
+  const bool gate_async = gate && ((uintptr_t)gbase % 16 == 0) && (gate_rs % (16 / sizeof(T)) == 0);
 
   // ---- state: warps 4 .. 4+SM_T-1 hold S rows [16 (warp-4), +16) x all DV columns (fp32)
   const bool s_owner = warp >= 4 && warp < 4 + SM_T;
@@ -177,6 +182,15 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
         cp_async16(dk + r * QS + (c - QV) * E, kg + lc * st[5] + (c - QV) * E, ok);
       else
         cp_async16(dv + r * VS + (c - 2 * QV) * E, vg + lc * st[8] + (c - 2 * QV) * E, ok);
+    }
+    if (gate_async) {
+      T* dg = sG + (size_t)stage * C * VS;
+      for (int i = tid; i < C * VV; i += NT) {
+        const int r = i / VV, c = i % VV;
+        const int l = n * C + r;
+        const bool ok = l < L;
+        cp_async16(dg + r * VS + c * E, gbase + (int64_t)(ok ? l : 0) * gate_rs + c * E, ok);
+      }
     }
     cp_async_commit();
   };
@@ -453,8 +467,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
         ssb += __shfl_xor_sync(0xffffffffu, ssb, 1);
         ssb += __shfl_xor_sync(0xffffffffu, ssb, 2);
         const float rsa = rsqrtf(ssa / (float)DV + onorm_eps), rsb = rsqrtf(ssb / (float)DV + onorm_eps);
-        const T* ga = gate + ((int64_t)b * L + la) * gate_rs + h * gate_hs;
-        const T* gb = gate + ((int64_t)b * L + lb) * gate_rs + h * gate_hs;
+        const T* cG = sG + (size_t)stage * C * VS;
+        const T* ga = gate_async ? cG + ra * VS : gbase + (int64_t)la * gate_rs;
+        const T* gb = gate_async ? cG + rb * VS : gbase + (int64_t)lb * gate_rs;
 #pragma unroll
         for (int nt = 0; nt < DVT; ++nt) {
           const int c = nt * 8 + 2 * tq;

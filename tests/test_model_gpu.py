@@ -154,5 +154,9 @@ def test_172m_bf16_prefill_and_decode_vs_oracle():
     print(f'172M bf16: prefill max-abs {e_pre:.4f}, decode {e_dec:.4f}, reference bf16 drift {noise:.4f}')
     assert e_pre <= max(2e-2, noise) and e_dec <= max(2e-2, noise)
     _, _, rc0 = om.forward(P32, cfg, ids[:, :160])
-    for ours, theirs in zip(blk0, rc0.blocks[0].attn_res.blocks):
-        assert rel_err(ours, theirs) < 2e-2
+    _, _, rc16 = om.forward(P16, cfg, ids[:, :160])
+    for ours, theirs, ref16 in zip(blk0, rc0.blocks[0].attn_res.blocks, rc16.blocks[0].attn_res.blocks):
+        # first block, before the amplification: per increment no further from fp32 than the
+        # reference's own bf16 path (or 2e-2 relative, whichever is looser)
+        ref_drift = (ref16.float() - theirs).abs().max().item()
+        assert (ours - theirs).abs().max().item() <= max(2e-2 * theirs.abs().max().item(), 1.25 * ref_drift)
