@@ -195,6 +195,24 @@ MB_API int motif_b200_chord_decode(const void* q, const void* k_cache, const voi
                             int max_splits, void* workspace, int64_t workspace_bytes, int dtype,
                             void* stream);
 
+/* motif_b200_chord_decode without a caller-provided workspace: for callers that cannot
+ * allocate device memory (a runtime bound through a plain C FFI with no CUDA allocator of
+ * its own, or a serving loop that must not call cudaMalloc between steps).  The split
+ * partials go to one fixed 8 MiB device array inside the library instead; requests whose
+ * motif_b200_chord_decode_workspace_bytes(B, H, T, D, max_splits) exceeds 8 MiB fail with
+ * MB_ERR_SHAPE.  The array is shared by every call on a device: calls that overlap on the
+ * GPU (e.g. on two streams at once) race and must be serialised by the caller.  The first
+ * call on each device looks up the array's device address (with that device current); make
+ * that first call before any stream capture.  Allocates nothing.
+ * No counterpart in the reference: an addition of this library. */
+MB_API int motif_b200_chord_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                    int64_t cap, const int32_t* len_dev, int64_t len_host,
+                                    const float* alpha, const float* beta, const float* mu,
+                                    const float* ssmax, void* out, int64_t out_stride, int64_t B,
+                                    int64_t H, int64_t Hkv, int64_t T, int64_t D,
+                                    float softmax_scale, float eps, int max_splits, int dtype,
+                                    void* stream);
+
 /* out = a * sigmoid(gate) + m over [rows, N] (row strides given).
  * Replaces chord_attn.py:254,313 (o_proj(out) * G) + decoder.py:208 (attn + mlp). */
 MB_API int motif_b200_gate_residual(const void* a, int64_t a_stride, const void* gate,

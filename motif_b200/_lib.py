@@ -49,6 +49,8 @@ SIGNATURES = {
     'motif_b200_chord_decode_workspace_bytes': (_I64, [_I64, _I64, _I64, _I64, _I]),
     'motif_b200_chord_decode': (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                                      _I64, _I64, _F, _F, _I, _P, _I64, _I, _P]),
+    'motif_b200_chord_decode_noalloc': (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                                             _I64, _I64, _I64, _F, _F, _I, _I, _P]),
     'motif_b200_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
     'motif_b200_argmax': (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
     'motif_b200_embed': (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
@@ -113,7 +115,7 @@ def ptr(t):
 KERNELS_PER_CALL = {n: 1 for n in SIGNATURES}
 KERNELS_PER_CALL.update({'motif_b200_last_error': 0, 'motif_b200_abi_version': 0,
                          'motif_b200_chord_workspace_bytes': 0, 'motif_b200_chord_decode_workspace_bytes': 0,
-                         'motif_b200_chord_decode': 2})
+                         'motif_b200_chord_decode': 2, 'motif_b200_chord_decode_noalloc': 2})
 
 
 class Tracker:

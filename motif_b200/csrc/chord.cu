@@ -15,6 +15,8 @@
 //     with the cache length read from device memory (so a captured CUDA graph replays at any
 //     position); one warp per (b, kv head, split) serves all G query heads of the group.
 //   * chord_prep — per-head RMSNorm of q and k and the append of k, v into the cache.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mb {
@@ -668,4 +670,67 @@ extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, cons
         pos_dev, pos_host, rows, (int)T, (int)H, (int)Hkv, (int)D, eps);
     return check_launch("chord_prep");
   });
+}
+
+// ------------------------------------------------------------------ allocation-free decode
+// Some callers of the split-KV decode cannot allocate device memory for its workspace: a
+// host runtime that reaches this library through a plain C FFI and has no CUDA allocator
+// of its own, or a serving loop that must never call cudaMalloc mid-stream (it can stall
+// the whole device and can fail under memory pressure at an arbitrary step).  For them the
+// workspace lives in one fixed, file-scope device array.
+namespace mb {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 8LL << 20;  // 8 MiB, held by every GPU that loads the library
+__device__ __align__(256) float g_decode_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_dev[kMaxDevices] = {};
+
+// Device address of g_decode_scratch on the current device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per device (with
+// that device current) and cached.
+int scratch_on_current_device(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(MB_ERR_CUDA, "chord_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(MB_ERR_UNSUPPORTED, "chord_decode_noalloc: device ordinal %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_dev[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(MB_ERR_CUDA, "chord_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_dev[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_dev[dev];
+  return MB_OK;
+}
+
+}  // namespace
+}  // namespace mb
+
+extern "C" int motif_b200_chord_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                                               const int32_t* len_dev, int64_t len_host, const float* alpha,
+                                               const float* beta, const float* mu, const float* ssmax, void* out,
+                                               int64_t out_stride, int64_t B, int64_t H, int64_t Hkv, int64_t T,
+                                               int64_t D, float scale, float eps, int max_splits, int dtype,
+                                               void* stream) {
+  MB_REQUIRE(B > 0 && H > 0 && T > 0 && D > 0 && max_splits >= 1, MB_ERR_SHAPE, "chord_decode_noalloc: bad shape");
+  const int64_t need = motif_b200_chord_decode_workspace_bytes(B, H, T, D, max_splits);
+  MB_REQUIRE(need <= mb::kNoAllocScratchBytes, MB_ERR_SHAPE,
+             "chord_decode_noalloc: needs %lld bytes of scratch for B=%lld H=%lld T=%lld D=%lld splits=%d, above "
+             "the fixed %lld-byte limit (use fewer splits or motif_b200_chord_decode with a workspace)",
+             (long long)need, (long long)B, (long long)H, (long long)T, (long long)D, max_splits,
+             (long long)mb::kNoAllocScratchBytes);
+  float* ws = nullptr;
+  const int rc = mb::scratch_on_current_device(&ws);
+  if (rc != MB_OK) return rc;
+  // Every split writes all of its partial rows (empty splits write m = -inf, l = 0), so the
+  // scratch needs no clearing between calls.
+  return motif_b200_chord_decode(q, k_cache, v_cache, cap, len_dev, len_host, alpha, beta, mu, ssmax, out,
+                                 out_stride, B, H, Hkv, T, D, scale, eps, max_splits, ws, mb::kNoAllocScratchBytes,
+                                 dtype, stream);
 }
