@@ -159,6 +159,21 @@ MB_API int motif_b200_gdn_prep(const void* proj, int64_t proj_stride, const void
                         int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int dtype,
                         void* stream);
 
+/* GDN prefill of a whole layer in ONE kernel (16-bit dtypes): motif_b200_gdn_prep's conv +
+ * SiLU + L2 norms + beta/g computed on each chunk as it is staged, then the chunked delta
+ * rule and the GatedRMSNorm epilogue of motif_b200_gdn_chunk_gated.  `proj` rows hold
+ * [q | k | v | a | b | g | ...] (gate = g columns), row stride proj_stride (multiple of 8);
+ * writes out[(b*T + t)*out_stride + h*Dv + j].  conv_in / conv_out: [B,3,C] (conv_out must
+ * not alias conv_in); state_in may be NULL.  (Dk, Dv) in {(32,64), (64,64), (64,128)};
+ * other shapes return MB_ERR_UNSUPPORTED (use gdn_prep + gdn_chunk_gated).
+ * Replaces gdn_attn.py:183-209 for L > 1. */
+MB_API int motif_b200_gdn_prefill(const void* proj, int64_t proj_stride, const void* conv_w,
+                           const void* A_log, const void* dt_bias, const void* conv_in,
+                           void* conv_out, const float* state_in, float* state_out,
+                           const void* onorm_w, float eps, void* out, int64_t out_stride,
+                           int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int dtype,
+                           void* stream);
+
 /* One GDN decode step (T == 1) for a whole layer, fused: conv with the carried state,
  * SiLU, L2 norms, beta/g, the recurrent update of `state` ([B,H,Dk,Dv] fp32, in place)
  * and the gated RMSNorm of the output with gate columns `gate` (row stride proj_stride),

@@ -42,6 +42,8 @@ SIGNATURES = {
     'motif_b200_attn_res_norm': (_I, [_P, _I, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _F, _F, _I, _P]),
     'motif_b200_gdn_prep': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                                  _I64, _I, _P]),
+    'motif_b200_gdn_prefill': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64,
+                                    _I64, _I64, _I, _P]),
     'motif_b200_gdn_decode': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                    _F, _I, _P]),
     'motif_b200_chord_prep': (_I, [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64,

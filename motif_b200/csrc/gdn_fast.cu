@@ -102,12 +102,26 @@ __device__ __forceinline__ float2 ld2(const T* p) {
   return make_float2(to_f(e[0]), to_f(e[1]));
 }
 
-template <typename T, int DK, int DV>
+// Inputs of the fused preparation (PREP = true): q, k, v then point at the RAW projection
+// columns, and beta / g are computed from the raw a / b columns (gdn_attn.py:116-136,183-197).
+template <typename T>
+struct PrepArgs {
+  const T* conv_w;   // [C][4], C = H (2 Dk + Dv) channels q | k | v
+  const T* A_log;    // [H]
+  const T* dt_bias;  // [H]
+  const T* conv_in;  // [B][3][C] previous raw inputs or nullptr (zeros)
+  T* conv_out;       // [B][3][C] last three raw inputs (must not alias conv_in)
+  const T* a_col;    // raw a column of head 0 (row stride ps, head stride 1)
+  const T* b_col;    // raw b column of head 0
+  int64_t ps;        // projection row stride
+};
+
+template <typename T, int DK, int DV, bool PREP>
 __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ beta,
     const float* __restrict__ g, const float* __restrict__ s_in, float* __restrict__ s_out, T* __restrict__ o,
     int H, int L, Strides18 sv, const T* __restrict__ gate, int64_t gate_rs, int64_t gate_hs,
-    const T* __restrict__ onorm_w, float onorm_eps) {
+    const T* __restrict__ onorm_w, float onorm_eps, PrepArgs<T> pa) {
   using Lay = FastLayout<T, DK, DV>;
   constexpr int QS = Lay::QS, VS = Lay::VS, AS = Lay::AS, XS = Lay::XS, TS = Lay::TS;
   constexpr int NTILE = (DK + DV) / 8;  // n8 tiles of the solve
@@ -200,10 +214,35 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
     for (int e = 0; e < 2; ++e) {
       const int l = n * C + lane + 32 * e;
       const bool ok = l < L;
-      pg[e] = ok ? gg[(int64_t)l * st[17]] : 0.f;
-      pb[e] = ok ? bg[(int64_t)l * st[14]] : 0.f;
+      if constexpr (PREP) {
+        const int64_t row = ((int64_t)b * L + (ok ? l : 0)) * pa.ps + h;
+        pg[e] = ok ? to_f(pa.a_col[row]) : 0.f;  // raw a
+        pb[e] = ok ? to_f(pa.b_col[row]) : 0.f;  // raw b
+      } else {
+        pg[e] = ok ? gg[(int64_t)l * st[17]] : 0.f;
+        pb[e] = ok ? bg[(int64_t)l * st[14]] : 0.f;
+      }
     }
   };
+  // PREP: conv thread state (one q | k | v channel per thread, window carried across chunks)
+  constexpr int NCH = 2 * DK + DV;
+  float cw[4] = {0.f, 0.f, 0.f, 0.f}, hist[3] = {0.f, 0.f, 0.f};
+  int gch = 0;  // global channel index of this thread
+  float aexp = 0.f, dtb = 0.f;
+  if constexpr (PREP) {
+    if (tid < NCH) {
+      gch = tid < DK ? h * DK + tid : (tid < 2 * DK ? H * DK + h * DK + (tid - DK) : 2 * H * DK + h * DV + (tid - 2 * DK));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cw[i] = to_f(pa.conv_w[(int64_t)gch * 4 + i]);
+      const int Ct = H * (2 * DK + DV);
+      if (pa.conv_in) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) hist[i] = to_f(pa.conv_in[((int64_t)b * 3 + i) * Ct + gch]);
+      }
+    }
+    aexp = -to_f(from_f<T>(expf(to_f(pa.A_log[h]))));
+    dtb = to_f(pa.dt_bias[h]);
+  }
   if (nchunks > 0) {
     load_chunk(0, 0);
     if (warp == 0) fetch_gb(0);
@@ -225,6 +264,18 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
 
     // (a) gamma = inclusive cumsum(g), e^gamma, e^(gL - gamma), beta  (warp 0)
     if (warp == 0) {
+      if constexpr (PREP) {
+        // beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias), rounded like the reference's
+        // 16-bit ops; padded rows get beta = g = 0 (the reference pads with zeros)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool ok = n * C + lane + 32 * e < L;
+          const float bt = to_f(from_f<T>(sigmoidf_(pb[e])));
+          const float gt = to_f(from_f<T>(aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(pg[e] + dtb)))))));
+          pb[e] = ok ? bt : 0.f;
+          pg[e] = ok ? gt : 0.f;
+        }
+      }
       float x0 = pg[0], x1 = pg[1];
 #pragma unroll
       for (int o2 = 1; o2 < 32; o2 <<= 1) {
@@ -249,6 +300,45 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
     }
     __syncthreads();  // (1) chunk data + gamma visible
     const float eL = sEg[C - 1];
+
+    if constexpr (PREP) {
+      // causal depthwise conv (taps 4) + SiLU over this chunk's raw rows, in place; thread =
+      // channel, window of the previous three raw inputs carried in registers
+      if (tid < NCH) {
+        T* col = tid < DK ? const_cast<T*>(cQ) + tid
+                          : (tid < 2 * DK ? const_cast<T*>(cK) + (tid - DK) : const_cast<T*>(cV) + (tid - 2 * DK));
+        const int stride = tid < 2 * DK ? QS : VS;
+        const int Ct = H * (2 * DK + DV);
+        for (int r = 0; r < C; ++r) {
+          const int l = n * C + r;
+          const float x = to_f(col[r * stride]);
+          const float y = cw[0] * hist[0] + cw[1] * hist[1] + cw[2] * hist[2] + cw[3] * x;
+          hist[0] = hist[1];
+          hist[1] = hist[2];
+          hist[2] = x;
+          col[r * stride] = l < L ? from_f<T>(siluf_(to_f(from_f<T>(y)))) : from_f<T>(0.f);
+          if (l == L - 1 && pa.conv_out) {
+#pragma unroll
+            for (int i = 0; i < 3; ++i) pa.conv_out[((int64_t)b * 3 + i) * Ct + gch] = from_f<T>(hist[i]);
+          }
+        }
+      }
+      __syncthreads();
+      // L2-normalise q (times Dk^-1/2) and k per token (F.normalize, gdn_attn.py:190-191)
+      for (int task = warp; task < 2 * C; task += NW) {
+        const int r = task >> 1;
+        T* row = const_cast<T*>((task & 1) ? cK : cQ) + r * QS;
+        float ss = 0.f;
+        for (int c = lane; c < DK; c += 32) {
+          const float x = to_f(row[c]);
+          ss += x * x;
+        }
+        ss = warp_sum(ss);
+        const float sc = ((task & 1) ? 1.f : rsqrtf((float)DK)) / fmaxf(sqrtf(ss), 1e-12f);
+        for (int c = lane; c < DK; c += 32) row[c] = from_f<T>(to_f(row[c]) * sc);
+      }
+      __syncthreads();
+    }
 
     // (b) KK -> A (+ diagonal inverses) on warps 0-3, QK -> Aq on warps 4-7
     {
@@ -529,17 +619,18 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
   }
 }
 
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, bool PREP = false>
 int launch_fast(const void* q, const void* k, const void* v, const float* beta, const float* g, const float* s_in,
                 float* s_out, void* o, int64_t B, int64_t H, int64_t L, const Strides18& sv, const void* gate,
-                int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, cudaStream_t stream) {
+                int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, cudaStream_t stream,
+                PrepArgs<T> pa = PrepArgs<T>{}) {
   using Lay = FastLayout<T, DK, DV>;
-  auto kern = gdn_chunk_fast_kernel<T, DK, DV>;
+  auto kern = gdn_chunk_fast_kernel<T, DK, DV, PREP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Lay::bytes);
   if (e != cudaSuccess) return set_error(MB_ERR_CUDA, "gdn_chunk_fast: smem attribute: %s", cudaGetErrorString(e));
   kern<<<(unsigned)(B * H), NT, Lay::bytes, stream>>>((const T*)q, (const T*)k, (const T*)v, beta, g, s_in, s_out,
                                                       (T*)o, (int)H, (int)L, sv, (const T*)gate, gate_rs, gate_hs,
-                                                      (const T*)onorm_w, eps);
+                                                      (const T*)onorm_w, eps, pa);
   return check_launch("gdn_chunk_fast");
 }
 
@@ -558,10 +649,10 @@ int gdn_chunk_fast_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, co
 #define MB_FAST_CASE(DK_, DV_)                                                                               \
   if (Dk == DK_ && Dv == DV_) {                                                                              \
     if (dtype == MB_BF16)                                                                                    \
-      *rc = launch_fast<__nv_bfloat16, DK_, DV_>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs, \
+      *rc = launch_fast<__nv_bfloat16, DK_, DV_, false>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs, \
                                                  gate_hs, onorm_w, eps, st);                                 \
     else                                                                                                     \
-      *rc = launch_fast<__half, DK_, DV_>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs,      \
+      *rc = launch_fast<__half, DK_, DV_, false>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs,      \
                                           gate_hs, onorm_w, eps, st);                                        \
     return 1;                                                                                                \
   }
@@ -573,4 +664,52 @@ int gdn_chunk_fast_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, co
   return 0;
 }
 
+template <typename T, int DK, int DV>
+int prefill_typed(const void* proj, int64_t ps, const void* conv_w, const void* A_log, const void* dt_bias,
+                  const void* conv_in, void* conv_out, const float* s_in, float* s_out, const void* onorm_w, float eps,
+                  void* out, int64_t os, int64_t B, int64_t Tn, int64_t H, cudaStream_t st) {
+  const T* P = static_cast<const T*>(proj);
+  const int64_t C = H * (2 * DK + DV);
+  Strides18 sv;
+  const int64_t s9[18] = {Tn * ps, DK, ps, Tn * ps, DK, ps, Tn * ps, DV, ps, Tn * os, DV, os, 0, 0, 0, 0, 0, 0};
+  for (int i = 0; i < 18; ++i) sv.s[i] = s9[i];
+  PrepArgs<T> pa{static_cast<const T*>(conv_w), static_cast<const T*>(A_log), static_cast<const T*>(dt_bias),
+                 static_cast<const T*>(conv_in), static_cast<T*>(conv_out), P + C, P + C + H, ps};
+  const T* gate = P + C + 2 * H;
+  return launch_fast<T, DK, DV, true>(P, P + H * DK, P + 2 * H * DK, nullptr, nullptr, s_in, s_out, out, B, H, Tn,
+                                      sv, gate, ps, DV, onorm_w, eps, st, pa);
+}
+
 }  // namespace mb
+
+extern "C" int motif_b200_gdn_prefill(const void* proj, int64_t proj_stride, const void* conv_w, const void* A_log,
+                                      const void* dt_bias, const void* conv_in, void* conv_out, const float* state_in,
+                                      float* state_out, const void* onorm_w, float eps, void* out, int64_t out_stride,
+                                      int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int dtype,
+                                      void* stream) {
+  using namespace mb;
+  MB_REQUIRE(proj && conv_w && A_log && dt_bias && state_out && onorm_w && out, MB_ERR_ARG, "gdn_prefill: null pointer");
+  MB_REQUIRE(conv_out == nullptr || conv_out != conv_in, MB_ERR_ARG, "gdn_prefill: conv_out must not alias conv_in");
+  MB_REQUIRE(B >= 0 && T >= 0 && H > 0 && B * H < (1LL << 31) && T < (1LL << 31), MB_ERR_SHAPE, "gdn_prefill: bad shape");
+  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "gdn_prefill: 16-bit dtypes only");
+  const int64_t C = H * (2 * Dk + Dv);
+  MB_REQUIRE(proj_stride % 8 == 0 && out_stride % 2 == 0 && (uintptr_t)proj % 16 == 0 && (uintptr_t)out % 4 == 0 &&
+                 (C + 2 * H) % 8 == 0 && (uintptr_t)onorm_w % 4 == 0,
+             MB_ERR_ALIGN, "gdn_prefill: projection rows / gate columns must be 16-byte aligned");
+  if (B == 0 || T == 0) return set_error(MB_ERR_SHAPE, "gdn_prefill: empty input");
+  cudaStream_t st = (cudaStream_t)stream;
+#define MB_PREFILL_CASE(DK_, DV_)                                                                              \
+  if (Dk == DK_ && Dv == DV_)                                                                                  \
+    return dtype == MB_BF16                                                                                    \
+               ? prefill_typed<__nv_bfloat16, DK_, DV_>(proj, proj_stride, conv_w, A_log, dt_bias, conv_in,    \
+                                                        conv_out, state_in, state_out, onorm_w, eps, out,      \
+                                                        out_stride, B, T, H, st)                               \
+               : prefill_typed<__half, DK_, DV_>(proj, proj_stride, conv_w, A_log, dt_bias, conv_in, conv_out, \
+                                                 state_in, state_out, onorm_w, eps, out, out_stride, B, T, H,  \
+                                                 st);
+  MB_PREFILL_CASE(32, 64)
+  MB_PREFILL_CASE(64, 64)
+  MB_PREFILL_CASE(64, 128)
+#undef MB_PREFILL_CASE
+  return set_error(MB_ERR_UNSUPPORTED, "gdn_prefill: (Dk, Dv) = (%lld, %lld) not built", (long long)Dk, (long long)Dv);
+}

@@ -500,6 +500,9 @@ def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, posit
     return logits.view(B, T, cfg.vocab_size), x.view(B, T, d)
 
 
+_PREFILL_DIMS = ((32, 64), (64, 64), (64, 128))
+
+
 def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLayerCache], dt, dev, dc, st):
     """`GatedDeltaAttention.forward` + the SwiGLU MLP + the parallel residual (decoder.py:203-208)."""
     M = B * T
@@ -522,6 +525,13 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   _lib.ptr(pk.dt_bias), _lib.ptr(conv), _lib.ptr(state), proj.data_ptr() + pk.off_g * proj.element_size(),
                   _lib.ptr(pk.onorm_w), _lib.ptr(cat), cat.stride(0), B, H, dk, dv, eps, dc, st)
         conv_out = conv
+    elif dt != torch.float32 and (dk, dv) in _PREFILL_DIMS and N_in % 8 == 0:
+        # one kernel: conv + SiLU + norms + beta/g + chunked delta rule + GatedRMSNorm
+        conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)
+        state = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+        _lib.call('motif_b200_gdn_prefill', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+                  _lib.ptr(pk.dt_bias), _lib.ptr(conv_in), _lib.ptr(conv_out), _lib.ptr(state_in), _lib.ptr(state),
+                  _lib.ptr(pk.onorm_w), eps, _lib.ptr(cat), cat.stride(0), B, T, H, dk, dv, dc, st)
     else:
         qb = torch.empty((M, H * dk), dtype=dt, device=dev)
         kb = torch.empty((M, H * dk), dtype=dt, device=dev)

@@ -211,3 +211,59 @@ def test_gate_residual_argmax_embed():
     tc, tbc = tok.cuda(), table.cuda()
     _lib.call('motif_b200_embed', _lib.ptr(tc), _lib.ptr(tbc), _lib.ptr(out), 70000, 48, 100, _lib.MB_F32, st())
     assert torch.equal(out.cpu(), table[tok])
+
+
+@pytest.mark.parametrize('B,T,H,dk,dv,with_state', [(2, 150, 12, 64, 128, True), (1, 64, 4, 32, 64, False),
+                                                    (3, 2, 2, 64, 64, True), (1, 300, 3, 64, 128, False)])
+def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
+    """motif_b200_gdn_prefill == gdn_prep + gdn_chunk_gated, and both track the fp32 oracle."""
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(T + H)
+    C = H * (2 * dk + dv)
+    N = C + 2 * H + H * dv + 24
+    proj = (0.5 * torch.randn(B, T, N, generator=g)).to(dtype)
+    conv_w = (0.3 * torch.randn(C, 4, generator=g)).to(dtype)
+    A_log = torch.log(1 + 15 * torch.rand(H, generator=g)).to(dtype)
+    dt_bias = (0.1 * torch.randn(H, generator=g)).to(dtype)
+    conv_in = (0.5 * torch.randn(B, 3, C, generator=g)).to(dtype)
+    s_in = 0.1 * torch.randn(B, H, dk, dv, generator=g) if with_state else None
+    onw = (1 + 0.1 * torch.randn(dv, generator=g)).to(dtype)
+    p, cw, al, db, ci, ow = (t.cuda() for t in (proj, conv_w, A_log, dt_bias, conv_in, onw))
+    si = s_in.cuda() if s_in is not None else None
+    M = B * T
+    dc, s = _lib.MB_BF16, st()
+    # fused
+    out1 = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+    co1 = torch.empty(B, 3, C, dtype=dtype, device='cuda')
+    S1 = torch.empty(B, H, dk, dv, device='cuda')
+    _lib.call('motif_b200_gdn_prefill', _lib.ptr(p), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db), _lib.ptr(ci),
+              _lib.ptr(co1), _lib.ptr(si), _lib.ptr(S1), _lib.ptr(ow), 1e-6, _lib.ptr(out1), H * dv, B, T, H, dk, dv,
+              dc, s)
+    # two kernels
+    qb = torch.empty(M, H * dk, dtype=dtype, device='cuda')
+    kb = torch.empty_like(qb)
+    vb = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+    be = torch.empty(M, H, device='cuda')
+    ge = torch.empty(M, H, device='cuda')
+    co2 = torch.empty(B, 3, C, dtype=dtype, device='cuda')
+    _lib.call('motif_b200_gdn_prep', _lib.ptr(p), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db), _lib.ptr(ci),
+              _lib.ptr(co2), _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(be), _lib.ptr(ge), B, T, H, dk, dv, dc, s)
+    out2 = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+    S2 = torch.empty(B, H, dk, dv, device='cuda')
+    strides = [T * H * dk, dk, H * dk, T * H * dk, dk, H * dk, T * H * dv, dv, H * dv,
+               T * H * dv, dv, H * dv, T * H, 1, H, T * H, 1, H]
+    _lib.call('motif_b200_gdn_chunk_gated', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(be), _lib.ptr(ge),
+              _lib.ptr(si), _lib.ptr(S2), _lib.ptr(out2), B, H, T, dk, dv, _lib.i64_array(strides),
+              p.data_ptr() + (C + 2 * H) * 2, N, dv, _lib.ptr(ow), 1e-6, dc, s)
+    torch.cuda.synchronize()
+    assert torch.equal(co1, co2)
+    assert rel_err(out1.float(), out2.float()) < 1e-2, rel_err(out1.float(), out2.float())
+    assert rel_err(S1, S2) < 1e-3, rel_err(S1, S2)
+    # fp32 oracle on the prepared inputs (rounded like the kernels round them)
+    q, k, v, beta, gg, _ = gdn_prep_oracle(proj, conv_w, A_log, dt_bias, conv_in, B, T, H, dk, dv)
+    o, S = oo.chunk_gated_delta_rule(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), beta.transpose(1, 2),
+                                     gg.transpose(1, 2), s_in)
+    gate = proj[..., C + 2 * H:C + 2 * H + H * dv].float().view(B, T, H, dv)
+    ref = oo.gated_rms_norm(torch.cat([o.transpose(1, 2), gate], -1), onw.float()).reshape(M, H * dv)
+    assert rel_err(out1.float(), ref) < 3e-2, rel_err(out1.float(), ref)
+    assert rel_err(S1, S) < 2e-2, rel_err(S1, S)
