@@ -273,131 +273,123 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(
   }
 }
 
-// Vectorised preparation: one CTA per (b, block of TBT tokens); thread c owns 8 consecutive
-// channels of the q | k | v projection (16-byte loads / stores), keeps their last three raw
-// inputs in registers and walks the token block.  L2 norms of q / k heads reduce over the
-// DK/8 threads that own one head (shuffles inside an aligned lane group).  Threads 0..H-1
-// also produce beta / g for head tid.  16-bit dtypes, DK >= 16.
-template <typename T, int DK, int DV, int TBT>
-__global__ void __launch_bounds__(384) gdn_prep_vec_kernel(
+// Vectorised preparation for 16-bit dtypes.  A thread owns 8 consecutive q | k | v channels
+// (16-byte loads / stores) for a run of TR tokens: it issues the TR + 3 row loads it needs
+// (the 3 before the run are the conv window) up front, so every thread keeps TR + 3
+// independent 16-byte loads in flight, then produces the TR output rows.  Consecutive lanes
+// own consecutive channel groups, so the DK/8 lanes of one q / k head reduce the head's L2
+// norm with 3 xor-shuffles.  Threads whose channel group index is < H also produce beta / g
+// of head `group` for the run.
+template <typename T, int DK, int DV, int TR>
+__global__ void __launch_bounds__(256) gdn_prep_run_kernel(
     const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
     const T* __restrict__ dt_bias, const T* __restrict__ conv_in, T* __restrict__ conv_out,
     T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, float* __restrict__ beta,
     float* __restrict__ gout, int Tn, int H) {
-  constexpr int GQ = DK / 8;  // threads per q / k head
+  constexpr int GQ = DK / 8;  // lanes per q / k head
   const int C = H * (2 * DK + DV);
-  const int nthr = C / 8;
-  const int tid = threadIdx.x;
-  const bool active = tid < nthr;
+  const int ngrp = C / 8;
   const int b = blockIdx.y;
-  const int t0 = blockIdx.x * TBT;
-  const int t1 = min(t0 + TBT, Tn);
-  const int c0 = (active ? tid : 0) * 8;  // first channel of this thread
-  const int kind = c0 < H * DK ? 0 : (c0 < 2 * H * DK ? 1 : 2);  // q, k, v
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int nruns = (Tn + TR - 1) / TR;
+  const bool active = gid < (int64_t)ngrp * nruns;
+  const int grp = active ? (int)(gid % ngrp) : 0;
+  const int run = active ? (int)(gid / ngrp) : 0;
+  const int c0 = grp * 8;
+  const int kind = c0 < H * DK ? 0 : (c0 < 2 * H * DK ? 1 : 2);
+  const int t0 = run * TR;
   const T* P = proj + (int64_t)b * Tn * ps;
-  float w[8][4], hist[8][3];
-  {
-    uint4 r0 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4);
-    uint4 r1 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4 + 8);
-    uint4 r2 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4 + 16);
-    uint4 r3 = *reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4 + 24);
-    const T* e0 = reinterpret_cast<const T*>(&r0);
-    const T* e1 = reinterpret_cast<const T*>(&r1);
-    const T* e2 = reinterpret_cast<const T*>(&r2);
-    const T* e3 = reinterpret_cast<const T*>(&r3);
+  uint4 raw[TR + 3];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const T* src = i < 2 ? e0 : (i < 4 ? e1 : (i < 6 ? e2 : e3));
-#pragma unroll
-      for (int j = 0; j < 4; ++j) w[i][j] = to_f(src[(i & 1) * 4 + j]);
+  for (int j = 0; j < TR + 3; ++j) {
+    const int tau = t0 - 3 + j;
+    raw[j] = make_uint4(0, 0, 0, 0);
+    if (active) {
+      if (tau >= 0 && tau < Tn)
+        raw[j] = *reinterpret_cast<const uint4*>(P + (int64_t)tau * ps + c0);
+      else if (tau < 0 && conv_in)
+        raw[j] = *reinterpret_cast<const uint4*>(conv_in + ((int64_t)b * 3 + (3 + tau)) * C + c0);
     }
   }
+  float w[8][4];
+  {
+    const uint4* wp = reinterpret_cast<const uint4*>(conv_w + (int64_t)c0 * 4);
 #pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    const int tau = t0 - 3 + j;
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (tau >= 0)
-      raw = *reinterpret_cast<const uint4*>(P + (int64_t)tau * ps + c0);
-    else if (conv_in)
-      raw = *reinterpret_cast<const uint4*>(conv_in + ((int64_t)b * 3 + (3 + tau)) * C + c0);
-    const T* e = reinterpret_cast<const T*>(&raw);
+    for (int u = 0; u < 4; ++u) {
+      const uint4 r = active ? wp[u] : make_uint4(0, 0, 0, 0);
+      const T* e = reinterpret_cast<const T*>(&r);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) hist[i][j] = to_f(e[i]);
+      for (int i = 0; i < 8; ++i) w[2 * u + i / 4][i % 4] = to_f(e[i]);
+    }
   }
   const float qscale = rsqrtf((float)DK);
-  float Aexp = 0.f, dtb = 0.f;
-  if (tid < H) {
-    Aexp = -to_f(from_f<T>(expf(to_f(A_log[tid]))));
-    dtb = to_f(dt_bias[tid]);
-  }
-  // Rows are loaded PF at a time before any is used, so each thread keeps PF 16-byte loads
-  // in flight (one CTA covers all channels of a token, so the loads of a row are coalesced).
-  constexpr int PF = 4;
-  for (int tb = t0; tb < t1; tb += PF) {
-    uint4 rows[PF];
 #pragma unroll
-    for (int u = 0; u < PF; ++u)
-      rows[u] = (tb + u < t1 && active) ? *reinterpret_cast<const uint4*>(P + (int64_t)(tb + u) * ps + c0)
-                                        : make_uint4(0, 0, 0, 0);
-    float ab[PF], bb[PF];
-    if (tid < H) {
+  for (int r = 0; r < TR; ++r) {
+    const int t = t0 + r;
+    float y[8];
+    float ss = 0.f;
 #pragma unroll
-      for (int u = 0; u < PF; ++u) {
-        const bool ok = tb + u < t1;
-        ab[u] = ok ? to_f(P[(int64_t)(tb + u) * ps + C + tid]) : 0.f;
-        bb[u] = ok ? to_f(P[(int64_t)(tb + u) * ps + C + H + tid]) : 0.f;
-      }
+    for (int i = 0; i < 8; ++i) {
+      const float x0 = to_f(reinterpret_cast<const T*>(&raw[r])[i]);
+      const float x1 = to_f(reinterpret_cast<const T*>(&raw[r + 1])[i]);
+      const float x2 = to_f(reinterpret_cast<const T*>(&raw[r + 2])[i]);
+      const float x3 = to_f(reinterpret_cast<const T*>(&raw[r + 3])[i]);
+      const float a = w[i][0] * x0 + w[i][1] * x1 + w[i][2] * x2 + w[i][3] * x3;
+      y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
+      ss += y[i] * y[i];
     }
 #pragma unroll
-    for (int u = 0; u < PF; ++u) {
-      const int t = tb + u;
-      if (t >= t1) break;
-      const T* e = reinterpret_cast<const T*>(&rows[u]);
-      float y[8];
-      float ss = 0.f;
+    for (int o = 1; o < GQ; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (!active || t >= Tn) continue;
+    const int64_t tok = (int64_t)b * Tn + t;
+    T o8[8];
+    if (kind == 0) {
+      const float sc = qscale / fmaxf(sqrtf(ss), 1e-12f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float x = to_f(e[i]);
-        const float a = w[i][0] * hist[i][0] + w[i][1] * hist[i][1] + w[i][2] * hist[i][2] + w[i][3] * x;
-        hist[i][0] = hist[i][1];
-        hist[i][1] = hist[i][2];
-        hist[i][2] = x;
-        y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
-        ss += y[i] * y[i];
-      }
-      // group reduction over the GQ lanes of one q / k head (groups are lane-aligned)
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
+      *reinterpret_cast<uint4*>(qo + tok * H * DK + c0) = *reinterpret_cast<uint4*>(o8);
+    } else if (kind == 1) {
+      const float sc = 1.f / fmaxf(sqrtf(ss), 1e-12f);
 #pragma unroll
-      for (int o = 1; o < GQ; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
+      *reinterpret_cast<uint4*>(ko + tok * H * DK + (c0 - H * DK)) = *reinterpret_cast<uint4*>(o8);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i]);
+      *reinterpret_cast<uint4*>(vo + tok * H * DV + (c0 - 2 * H * DK)) = *reinterpret_cast<uint4*>(o8);
+    }
+  }
+  if (active && grp < H) {
+    const int hh = grp;
+    const float Aexp = -to_f(from_f<T>(expf(to_f(A_log[hh]))));
+    const float dtb = to_f(dt_bias[hh]);
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      const int t = t0 + r;
+      if (t >= Tn) break;
+      const T* row = P + (int64_t)t * ps;
       const int64_t tok = (int64_t)b * Tn + t;
-      T o8[8];
-      if (kind == 0) {
-        const float sc = qscale / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
-        if (active) *reinterpret_cast<uint4*>(qo + tok * H * DK + c0) = *reinterpret_cast<uint4*>(o8);
-      } else if (kind == 1) {
-        const float sc = 1.f / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
-        if (active) *reinterpret_cast<uint4*>(ko + tok * H * DK + (c0 - H * DK)) = *reinterpret_cast<uint4*>(o8);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i]);
-        if (active) *reinterpret_cast<uint4*>(vo + tok * H * DV + (c0 - 2 * H * DK)) = *reinterpret_cast<uint4*>(o8);
-      }
-      if (tid < H) {
-        beta[tok * H + tid] = to_f(from_f<T>(sigmoidf_(bb[u])));
-        gout[tok * H + tid] = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(ab[u] + dtb)))))));
-      }
+      beta[tok * H + hh] = to_f(from_f<T>(sigmoidf_(to_f(row[C + H + hh]))));
+      gout[tok * H + hh] =
+          to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(to_f(row[C + hh]) + dtb)))))));
     }
   }
-  if (t1 == Tn && conv_out && active) {
+  // the run holding T-1 writes the raw inputs at T-3 .. T-1 as the carried conv state
+  const int last = Tn - 1 - t0;
+  if (active && conv_out && last >= 0 && last < TR) {
 #pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      T o8[8];
+    for (int j = 3; j < TR + 3; ++j) {
+      const int slot = j - last - 1;  // raw[j] holds token t0 - 3 + j = Tn - 3 + slot
+      if (slot >= 0 && slot < 3)
+        *reinterpret_cast<uint4*>(conv_out + ((int64_t)b * 3 + slot) * C + c0) = raw[j];
+    }
+    if (Tn < 3) {  // positions before 0 come from conv_in (or zeros)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(hist[i][j]);
-      *reinterpret_cast<uint4*>(conv_out + ((int64_t)b * 3 + j) * C + c0) = *reinterpret_cast<uint4*>(o8);
+      for (int j = 0; j < 3; ++j) {
+        const int slot = j - last - 1;
+        if (slot >= 0 && slot < 3)
+          *reinterpret_cast<uint4*>(conv_out + ((int64_t)b * 3 + slot) * C + c0) = raw[j];
+      }
     }
   }
 }
@@ -512,13 +504,13 @@ extern "C" int motif_b200_gdn_prep(const void* proj, int64_t ps, const void* con
         const bool vec = sizeof(Tt) == 2 && ps % 8 == 0 && ((uintptr_t)proj | (uintptr_t)conv_w | (uintptr_t)q |
                                                             (uintptr_t)k | (uintptr_t)v | (uintptr_t)conv_in |
                                                             (uintptr_t)conv_out) % 16 == 0 &&
-                         C / 8 <= 384 && B < 65536;
+                         B < 65536;
         if constexpr (sizeof(Tt) == 2) {
-          if (vec) {
-            constexpr int TBT = 64;
-            const int threads = (int)((C / 8 + 31) / 32 * 32);
-            dim3 grid((unsigned)((T + TBT - 1) / TBT), (unsigned)B);
-            gdn_prep_vec_kernel<Tt, DK, DV, TBT><<<grid, threads, 0, (cudaStream_t)stream>>>(
+          if (vec && DK >= 8) {
+            constexpr int TR = 8;
+            const int64_t threads = (C / 8) * ((T + TR - 1) / TR);
+            dim3 grid((unsigned)((threads + 255) / 256), (unsigned)B);
+            gdn_prep_run_kernel<Tt, DK, DV, TR><<<grid, 256, 0, (cudaStream_t)stream>>>(
                 (const Tt*)proj, ps, (const Tt*)conv_w, (const Tt*)A_log, (const Tt*)dt_bias, (const Tt*)conv_in,
                 (Tt*)conv_out, (Tt*)q, (Tt*)k, (Tt*)v, beta, g, (int)T, (int)H);
             return check_launch("gdn_prep");

@@ -501,6 +501,10 @@ def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, posit
 
 
 _PREFILL_DIMS = ((32, 64), (64, 64), (64, 128))
+# motif_b200_gdn_prefill (conv / norms inside the chunk kernel) is correct but slower than the
+# separate high-occupancy prep kernel + chunk kernel, whose per-chunk critical path it would
+# lengthen; the model uses the two-kernel path unless this is switched on.
+FUSED_GDN_PREFILL = False
 
 
 def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLayerCache], dt, dev, dc, st):
@@ -525,7 +529,7 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   _lib.ptr(pk.dt_bias), _lib.ptr(conv), _lib.ptr(state), proj.data_ptr() + pk.off_g * proj.element_size(),
                   _lib.ptr(pk.onorm_w), _lib.ptr(cat), cat.stride(0), B, H, dk, dv, eps, dc, st)
         conv_out = conv
-    elif dt != torch.float32 and (dk, dv) in _PREFILL_DIMS and N_in % 8 == 0:
+    elif FUSED_GDN_PREFILL and dt != torch.float32 and (dk, dv) in _PREFILL_DIMS and N_in % 8 == 0:
         # one kernel: conv + SiLU + norms + beta/g + chunked delta rule + GatedRMSNorm
         conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)
         state = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)

@@ -220,7 +220,7 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
     dtype = torch.bfloat16
     g = torch.Generator().manual_seed(T + H)
     C = H * (2 * dk + dv)
-    N = C + 2 * H + H * dv + 24
+    N = (C + 2 * H + H * dv + 24 + 7) // 8 * 8  # projection rows are 16-byte aligned (as packed by the model)
     proj = (0.5 * torch.randn(B, T, N, generator=g)).to(dtype)
     conv_w = (0.3 * torch.randn(C, 4, generator=g)).to(dtype)
     A_log = torch.log(1 + 15 * torch.rand(H, generator=g)).to(dtype)
