@@ -229,15 +229,16 @@ def run_ours(args, world, rank, local):
     dev = torch.device('cuda', local)
     torch.cuda.set_device(dev)
     cfg = config_172m()
-    if GLOBAL_BATCH % world:
-        raise SystemExit(f'global batch {GLOBAL_BATCH} is not divisible by {world} ranks')
-    B = GLOBAL_BATCH // world
+    gb = args.global_batch
+    if gb % world:
+        raise SystemExit(f'global batch {gb} is not divisible by {world} ranks')
+    B = gb // world
     T = args.seq_len
     torch.manual_seed(0)
     model = MotifChordModel(cfg)
     init_params(model, seed=0)
     model = model.to(dev, torch.bfloat16).eval()
-    ids_all = torch.randint(0, cfg.vocab_size, (GLOBAL_BATCH, T), generator=torch.Generator().manual_seed(0))
+    ids_all = torch.randint(0, cfg.vocab_size, (gb, T), generator=torch.Generator().manual_seed(0))
     ids_host = ids_all[rank * B:(rank + 1) * B].contiguous().pin_memory()
     ids_dev = ids_host.to(dev)
     stream = torch.cuda.current_stream(dev)
@@ -301,7 +302,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
 
-    tokens = GLOBAL_BATCH * T * args.steps
+    tokens = gb * T * args.steps
     value = tokens / (elapsed_ms / 1000.0)
     pk = peaks()
     kernels = {}
@@ -333,7 +334,7 @@ def run_ours(args, world, rank, local):
         'ms_per_step': elapsed_ms / args.steps, 'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None,
         'dtype': 'bf16', 'data': 'synthetic',
         'config': {'workload': '172M-class MotifChord prefill, logits over all positions (config 4)',
-                   'global_batch': GLOBAL_BATCH, 'seq_len': T, 'per_rank_batch': B,
+                   'global_batch': gb, 'seq_len': T, 'per_rank_batch': B,
                    'parallelism': f'sequence-sharded replicas x{world}, no hot-path collective',
                    'l2': 'inputs larger than L2 (every activation >= 200 MB at B=32)'},
         'e2e': {'value': tokens / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': ids_host.numel() * 8,
@@ -360,6 +361,9 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--seq-len', type=int, default=SEQ_LEN)
+    ap.add_argument('--global-batch', type=int, default=GLOBAL_BATCH,
+                    help='sequences per step over all ranks (the benchmark config is 32; smaller values are for '
+                         'profiling captures)')
     ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     args = ap.parse_args()
