@@ -81,6 +81,25 @@ def kernel_work(name, cfg, B, T):
     return 0, 0
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per unit of work, from one ncu
+# capture of each kernel on a smaller case of the same layer; traffic grows in proportion to the
+# units, so a full launch's traffic is this figure times its units.
+#   gdn_chunk_gated : per token-head, profiles/gdn_chunk_fast_b4_t4096.txt (186.2 MB / 196608)
+#   chord_attention : per token,      profiles/chord_fwd_mma_b4_t4096.txt (39.6 MB / 16384)
+NCU_TRAFFIC = {
+    'motif_b200_gdn_chunk_gated': (186.15e6 / (4 * 4096 * 12), 'token_head'),
+    'motif_b200_chord_attention': (39.55e6 / (4 * 4096), 'token'),
+}
+
+
+def ncu_traffic(name, cfg, B, T):
+    if name not in NCU_TRAFFIC:
+        return None
+    per, unit = NCU_TRAFFIC[name]
+    units = B * T * (cfg.num_heads if unit == 'token_head' else 1)
+    return per * units
+
+
 def gemm_flops(cfg, B, T):
     """Total cuBLAS GEMM flops of one forward (packed projections, K-concat residual, lm_head)."""
     d, H, Hkv = cfg.model_dim, cfg.num_heads, cfg.kv_heads
@@ -260,7 +279,9 @@ def run_ours(args, world, rank, local):
     _lib.set_tracker(None)
     del out
     summ = tr.summary()
-    mine = {k: v for k, v in summ.items() if k.startswith('motif_b200_')}
+    # the roofline kernel: the slowest of this library's kernels whose work is known per launch
+    mine = {k: v for k, v in summ.items()
+            if k.startswith('motif_b200_') and kernel_work(k, cfg, B, T)[1]}
     dominant = max(mine, key=lambda k: mine[k][1])
 
     # timed region: events only around the dominant kernel's launches
@@ -318,7 +339,7 @@ def run_ours(args, world, rank, local):
     else:
         roof = {'bound': 'hbm', 'achieved': byts / avg_s / 1e9, 'peak': pk['hbm_gbs'], 'unit': 'GB/s'}
     roof['frac'] = roof['achieved'] / roof['peak']
-    roof['traffic'] = None
+    roof['traffic'] = ncu_traffic(dominant, cfg, B, T)
     roof['kernel'] = dominant
     roof['launches_timed'] = dom[0]
     roof['avg_launch_ms'] = avg_s * 1000.0
