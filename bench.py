@@ -3,9 +3,10 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
-One step = one `MotifChordModel.forward` over this rank's shard of the 32 x 4096 token
-batch (sequences split evenly across ranks; no collective on the hot path), logits over
-all positions included.  Prints ONE JSON line on rank 0.
+One step = one `MotifChordModel.forward` over this rank's 32 x 4096-token batch (weak
+scaling: N ranks process 32·N independent sequences, no collective on the hot path), logits
+over all positions included.  `--global-batch G` instead splits G sequences across the
+ranks (strong scaling).  Prints ONE JSON line on rank 0.
 
 * `value`      — whole-job prefill tokens/s, inputs resident in HBM, device time (CUDA
                  events on the launching stream), max over ranks.
@@ -32,7 +33,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-GLOBAL_BATCH = 32
+GLOBAL_BATCH = 32   # sequences per rank
 SEQ_LEN = 4096
 METRIC = 'prefill_tokens_per_s'
 UNIT = 'tokens/s'
@@ -165,32 +166,29 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- distributed
+# One process per GPU through motif_b200.runner: NCCL process group (short timeout), barrier,
+# max over ranks.  No collective inside a forward.
+_CTX = None
+
+
 def dist_setup():
-    world = int(os.environ.get('WORLD_SIZE', '1'))
-    rank = int(os.environ.get('RANK', '0'))
-    local = int(os.environ.get('LOCAL_RANK', '0'))
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device('cuda', local))
-    return world, rank, local
+    global _CTX
+    from motif_b200 import runner
+    _CTX = runner.init(timeout_s=300.0)
+    return _CTX.world, _CTX.rank, _CTX.local
 
 
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device='cuda')
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from motif_b200 import runner
+    return runner.max_over_ranks(x, _CTX)
 
 
 def barrier(world):
     if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
+        from motif_b200 import runner
+        runner.barrier(_CTX)
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -248,17 +246,20 @@ def run_ours(args, world, rank, local):
     dev = torch.device('cuda', local)
     torch.cuda.set_device(dev)
     cfg = config_172m()
-    gb = args.global_batch
-    if gb % world:
-        raise SystemExit(f'global batch {gb} is not divisible by {world} ranks')
-    B = gb // world
+    from motif_b200 import runner
+    weak = args.global_batch is None
+    gb = GLOBAL_BATCH * world if weak else args.global_batch
+    lo, hi = runner.shard_range(gb, world, rank)
+    B = hi - lo
+    if B == 0:
+        raise SystemExit(f'global batch {gb} leaves rank {rank} of {world} without a sequence')
     T = args.seq_len
     torch.manual_seed(0)
     model = MotifChordModel(cfg)
     init_params(model, seed=0)
     model = model.to(dev, torch.bfloat16).eval()
     ids_all = torch.randint(0, cfg.vocab_size, (gb, T), generator=torch.Generator().manual_seed(0))
-    ids_host = ids_all[rank * B:(rank + 1) * B].contiguous().pin_memory()
+    ids_host = ids_all[lo:hi].contiguous().pin_memory()
     ids_dev = ids_host.to(dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -352,7 +353,8 @@ def run_ours(args, world, rank, local):
 
     result = {
         'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
-        'ms_per_step': elapsed_ms / args.steps, 'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None,
+        'ms_per_step': elapsed_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak' if weak else 'strong',
+        'vs_baseline': None,
         'dtype': 'bf16', 'data': 'synthetic',
         'config': {'workload': '172M-class MotifChord prefill, logits over all positions (config 4)',
                    'global_batch': gb, 'seq_len': T, 'per_rank_batch': B,
@@ -382,9 +384,9 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--seq-len', type=int, default=SEQ_LEN)
-    ap.add_argument('--global-batch', type=int, default=GLOBAL_BATCH,
-                    help='sequences per step over all ranks (the benchmark config is 32; smaller values are for '
-                         'profiling captures)')
+    ap.add_argument('--global-batch', type=int, default=None,
+                    help='sequences per step over all ranks, split across them (strong scaling); the default is '
+                         f'{GLOBAL_BATCH} per rank (weak scaling); small values are for profiling captures')
     ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     args = ap.parse_args()
