@@ -368,6 +368,8 @@ def run_ours(args, world, rank, local):
         'clocks': clk.summary(),
         'peaks': pk,
     }
+    if args.decode_steps > 0:
+        result['decode'] = run_decode(model, cfg, args, world, rank, local, dev, stream, pk)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, threads, dt = cpu_oracle_rate(seq_len=args.ref_seq_len)
         result['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': threads, 'kind': 'port',
@@ -375,6 +377,98 @@ def run_ours(args, world, rank, local):
                                             f'(reference torch algorithm), {dt:.1f} s'}
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+# ---------------------------------------------------------------- decode (config 5)
+DECODE_BATCH = 64      # sequences per rank
+DECODE_CONTEXT = 8192
+
+
+def decode_step_bytes(model, B, S):
+    """HBM bytes one greedy decode step must move at cache length S (new token included):
+    every packed weight once, each Chord layer's K and V over S positions plus the new
+    row, each GDN layer's fp32 state read + written and conv window read + written, the
+    embedding rows, the logits written and read by the argmax."""
+    cfg = model.config
+    decs, lm = model.packed()
+    wb = lm.numel() * lm.element_size()
+    kv = gdn = 0
+    for blk in decs:
+        for pk in blk:
+            for name in ('w_in', 'w_out', 'w_o', 'w_down'):
+                t = getattr(pk, name, None)
+                if t is not None:
+                    wb += t.numel() * t.element_size()
+            if hasattr(pk, 'Hkv'):
+                kv += 2 * B * pk.Hkv * (S + 1) * pk.D * 2
+            else:
+                C = pk.H * (2 * pk.dk + pk.dv)
+                gdn += 2 * B * pk.H * pk.dk * pk.dv * 4 + 2 * B * 3 * C * 2
+    d = cfg.model_dim
+    return wb + kv + gdn + B * d * 2 + 2 * B * cfg.vocab_size * 2
+
+
+def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
+    """Config 5: B=64 sequences per GPU at context 8192, then `--decode-steps` greedy steps,
+    one CUDA-graph replay per step.  The caches are filled directly with seeded random
+    contents at length 8192 (decode speed does not depend on them), as a prefill of
+    64 x 8192 tokens would leave them."""
+    from motif_b200 import _lib
+    from motif_b200.decode import GraphDecoder, fill_cache_random
+    B, L, n = DECODE_BATCH, DECODE_CONTEXT, args.decode_steps
+    cache = fill_cache_random(model, model.create_cache(), B, L, L + 2 * n, seed=rank)
+    dec = GraphDecoder(model, cache, max_steps=2 * n)
+    g = torch.Generator().manual_seed(rank)
+    first_host = torch.randint(0, cfg.vocab_size, (B, 1), generator=g).pin_memory()
+    first = first_host.to(dev)
+    # warm-up replays (also the first touch of every cache page), then the caches' lengths
+    # are rewound so the timed steps start at context 8192
+    dec.run(first, min(3, n))
+    torch.cuda.synchronize(dev)
+    dec.taken = 0
+    dec.lens.copy_(torch.tensor([L, L + 1], dtype=torch.int32))
+    dec.step_idx.zero_()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        toks = dec.run(first, n)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = max_over_ranks(t0.elapsed_time(t1), world)
+    # end to end through the public API: host ids in, n graph steps, host tokens out
+    dec.taken = 0
+    dec.lens.copy_(torch.tensor([L, L + 1], dtype=torch.int32))
+    dec.step_idx.zero_()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    toks = dec.run(first_host.to(dev, non_blocking=True), n).to('cpu')
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    total_tok = B * n * world
+    byts = sum(decode_step_bytes(model, B, L + i) for i in range(n))
+    gbs = byts / (ms / 1000.0) / 1e9
+    out = {
+        'metric': 'decode_tokens_per_s', 'value': total_tok / (ms / 1000.0), 'unit': 'tokens/s',
+        'higher_is_better': True, 'scaling': 'weak', 'steps': n, 'ms_per_step': ms / n,
+        'config': {'workload': '172M-class greedy decode (config 5), one CUDA-graph replay per token',
+                   'per_rank_batch': B, 'global_batch': B * world, 'context': L,
+                   'cache_fill': 'seeded random KV / GDN states at length 8192 (stands in for the prefill)',
+                   'l2': 'working set per step > 2 GB, larger than L2'},
+        'hbm': {'achieved_gbs_per_gpu': gbs, 'peak': pk['hbm_gbs'], 'frac': gbs / pk['hbm_gbs'],
+                'algorithmic_bytes_per_step': byts / n},
+        'e2e': {'value': total_tok / (e2e_ms / 1000.0), 'unit': 'tokens/s',
+                'h2d_bytes_per_step': first_host.numel() * 8 / n, 'd2h_bytes_per_step': toks.numel() * 8 / n},
+        'gpu_launches': dec.launches_per_step * n,
+        'clocks': clk.summary(),
+    }
+    dec.release()
+    del cache
+    return out
 
 
 def main():
@@ -389,6 +483,8 @@ def main():
                          f'{GLOBAL_BATCH} per rank (weak scaling); small values are for profiling captures')
     ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--decode-steps', type=int, default=256,
+                    help='greedy decode steps of the config-5 decode measurement (0 skips it)')
     args = ap.parse_args()
     world, rank, local = dist_setup() if args.impl == 'ours' else (
         int(os.environ.get('WORLD_SIZE', '1')), int(os.environ.get('RANK', '0')), 0)

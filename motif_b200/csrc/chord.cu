@@ -336,7 +336,9 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
   const int R = G * Tn;
   __shared__ float sq[4][MAXR][D];
   if (split >= nsplit) return;
-  const int S = len_dev ? *len_dev : len_host;  // cache length including the new tokens
+  // cache length including the new tokens; a device-side length is clamped to [Tn, cap] so
+  // that a stale counter can only give wrong scores, never an access outside the cache
+  const int S = len_dev ? min(max(*len_dev, Tn), (int)cap) : len_host;
   const int q_start = S - Tn;
   // keys handled by this split (multiples of 32)
   const int per = ((S + nsplit - 1) / nsplit + 31) & ~31;
@@ -477,6 +479,9 @@ __global__ void chord_prep_kernel(const T* __restrict__ proj, int64_t ps, const 
   const int b = (int)(tok / Tn), t = (int)(tok % Tn);
   const int64_t pos = (pos_dev ? (int64_t)*pos_dev : pos_host) + t;
   const T* src = proj + tok * ps + (int64_t)slot * D;  // q heads, then k heads, then v heads
+  // a device-side position past the cache capacity skips the cache write (the host checks
+  // host-side positions before launch)
+  if (slot >= H && (pos < 0 || pos >= cap)) return;
   if (slot >= H + Hkv) {  // value: plain copy into the cache
     const int kvh = slot - H - Hkv;
     T* dst = vc + (((int64_t)b * Hkv + kvh) * cap + pos) * D;

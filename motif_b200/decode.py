@@ -1,0 +1,289 @@
+"""Batched greedy decode as a replayed CUDA graph.
+
+`Generation.step` (`motif/model/generate.py:138-171`) runs one `MotifChordModel.forward`
+per new token: at L = 1 every layer is a handful of small launches, so a Python-driven loop
+is launch-bound.  `GraphDecoder` captures ONE decode step — embed, for each decoder the
+attn-res read, packed projection GEMM, GDN recurrent update (`motif_b200_gdn_decode`) or
+Chord cache append + split-KV attention (`motif_b200_chord_prep` / `_chord_decode`), MLP,
+residual GEMMs, then lm_head and the greedy argmax — and replays it once per token.
+
+Positions live on the device: `lens = [pos, pos + 1]` (int32) is read by the Chord kernels
+(cache write position, attended length) and advanced by the graph itself, and the argmax
+writes the next input ids in place, so `run(n)` replays n steps back to back with no host
+synchronisation.  The KV buffers are grown to hold every step before capture (a graph
+cannot regrow them); the GDN recurrent and conv states are updated in place.
+
+The math is the eager T = 1 path's: the same kernels in the same order, except that the
+split-KV count is fixed at capture (from the cache capacity) instead of chosen per length;
+with `model.decode_splits` set, graph and eager decode give identical tokens.
+"""
+
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import _lib
+from .cache import GatedDeltaAttentionLayerCache, KVLayerCache, ModelCache
+from .config import GGD_EPS, NORM_EPS
+from .model import _decode_splits, _mm, _norm_read
+
+__all__ = ['GraphDecoder', 'fill_cache_random']
+
+
+class _GDNSlot:
+    """A GDN layer's in-place recurrent state (fp32 [B,H,dk,dv]) and conv state ([B,3,C])."""
+
+    def __init__(self, cache: GatedDeltaAttentionLayerCache):
+        self.cache = cache
+        self.state = cache.state
+        self.conv = cache._conv
+
+
+def _check_layer_caches(model, cache: ModelCache, B: int, need: int):
+    kv, gdn = [], []
+    dt = model.embed.weight.dtype
+    for b, block in enumerate(model.blocks):
+        bc = cache[b]
+        if len(bc.attn) != len(block.features):
+            raise ValueError('the cache must hold one layer cache per decoder (run a prefill first)')
+        for i, dec in enumerate(block.features):
+            lc = bc.attn[i]
+            if dec.attn_type == 'chord':
+                if not isinstance(lc, KVLayerCache) or lc._kbuf is None:
+                    raise ValueError(f'block {b} decoder {i}: an allocated KVLayerCache is required')
+                if lc.wide:
+                    raise NotImplementedError('wide KV caches are not used by the decode graph')
+                if lc._kbuf.shape[0] != B or lc._kbuf.dtype != dt:
+                    raise ValueError(f'block {b} decoder {i}: KV cache batch/dtype mismatch')
+                lc.reserve(need)   # room for every step before capture: a graph cannot regrow it
+                kv.append(lc)
+            else:
+                if not isinstance(lc, GatedDeltaAttentionLayerCache) or lc.state is None or lc._conv is None:
+                    raise ValueError(f'block {b} decoder {i}: a filled GatedDeltaAttentionLayerCache is required')
+                if lc.state.dtype != torch.float32 or not lc.state.is_contiguous():
+                    lc.state = lc.state.float().contiguous()
+                if lc._conv.dtype != dt or not lc._conv.is_contiguous():
+                    lc._conv = lc._conv.to(dt).contiguous()
+                gdn.append(_GDNSlot(lc))
+    lengths = {lc.length for lc in kv}
+    if len(lengths) > 1:
+        raise ValueError(f'Chord layer caches disagree on length: {sorted(lengths)}')
+    return kv, gdn
+
+
+class GraphDecoder:
+    """Greedy batched decode of `model` from `cache`, one CUDA-graph replay per token.
+
+    >>> dec = GraphDecoder(model, cache, max_steps=256)   # cache: prefilled, batch B
+    >>> toks = dec.run(first_ids, 256)                     # [B, 256] int64 on the device
+
+    `first_ids` [B, 1] (or [B]) is the token fed at the first step (the prefill's greedy
+    next token); the result holds the token produced by each step.  After `run` the cache's
+    host-side lengths are advanced by the steps taken, so the eager API can continue from it.
+    """
+
+    def __init__(self, model, cache: ModelCache, max_steps: int, splits: Optional[int] = None):
+        if model.training:
+            raise ValueError('GraphDecoder needs an eval-mode model')
+        w = model.embed.weight
+        if w.device.type != 'cuda':
+            raise ValueError('GraphDecoder runs on a CUDA device')
+        self.model = model
+        self.cache = cache
+        self.dev = w.device
+        self.dt = w.dtype
+        kv0 = None
+        for bc in cache:
+            for lc in bc.attn:
+                if isinstance(lc, KVLayerCache) and lc._kbuf is not None:
+                    kv0 = lc
+                    break
+            if kv0 is not None:
+                break
+        if kv0 is None:
+            raise ValueError('no allocated KV cache: prefill the cache before building the graph')
+        self.B = kv0._kbuf.shape[0]
+        self.start = kv0.length
+        self.max_steps = int(max_steps)
+        self.kv, self.gdn = _check_layer_caches(model, cache, self.B, self.start + self.max_steps)
+        self.cap = min(lc.capacity for lc in self.kv)
+        cfg = model.config
+        Hkv = cfg.kv_heads
+        self.splits = int(splits) if splits else _decode_splits(model, self.B, Hkv, self.cap)
+        self.decs, self.lm = model.packed()
+        self.lens = torch.tensor([self.start, self.start + 1], dtype=torch.int32, device=self.dev)
+        self.step_idx = torch.zeros((1,), dtype=torch.int64, device=self.dev)
+        self.ids = torch.zeros((self.B,), dtype=torch.int64, device=self.dev)
+        self.tokens = torch.zeros((self.max_steps, self.B), dtype=torch.int64, device=self.dev)
+        self.launches_per_step = 0
+        self.graph = None
+        self._capture()
+
+    # ------------------------------------------------------------------ one step
+    def _step(self):
+        """Every launch of one decode step; reads `ids`, `lens`, writes `ids`, `tokens[step]`."""
+        model, cfg = self.model, self.model.config
+        B, d, dt, dev = self.B, cfg.model_dim, self.dt, self.dev
+        dc = _lib.dtype_code(dt)
+        st = _lib.stream_ptr(dev)
+        w = model.embed.weight
+        x = torch.empty((B, d), dtype=dt, device=dev)
+        _lib.call('motif_b200_embed', _lib.ptr(self.ids), _lib.ptr(w), _lib.ptr(x), B, d, cfg.vocab_size, dc, st)
+        hn = torch.empty((B, d), dtype=dt, device=dev)
+        _norm_read([x], None, None, None, hn)
+        kv_i = gdn_i = 0
+        for b, block in enumerate(model.blocks):
+            fs: List[torch.Tensor] = []
+            for i, dec in enumerate(block.features):
+                if i > 0:
+                    hn = torch.empty((B, d), dtype=dt, device=dev)
+                    _norm_read([x] + fs, block.pseudo_queries[i].detach(), block.attn_res_norms[i].weight.detach(),
+                               None, hn, eps_src=block.attn_res_norms[i].eps)
+                pk = self.decs[b][i]
+                proj = _mm(hn, pk.w_in)
+                if dec.attn_type == 'chord':
+                    f = self._chord(pk, proj, self.kv[kv_i], dc, st)
+                    kv_i += 1
+                else:
+                    f = self._gdn(pk, proj, self.gdn[gdn_i], dc, st)
+                    gdn_i += 1
+                fs.append(f)
+            x_next = torch.empty((B, d), dtype=dt, device=dev)
+            hn = torch.empty((B, d), dtype=dt, device=dev)
+            _norm_read(fs, None, None, x_next, hn, eps_out=(model.norm.eps if b == len(model.blocks) - 1 else
+                                                             model.blocks[b + 1].features[0].attn_norm.eps))
+            x = x_next
+        logits = _mm(hn, self.lm)
+        _lib.call('motif_b200_argmax', _lib.ptr(logits), B, cfg.vocab_size, logits.stride(0), _lib.ptr(self.ids),
+                  dc, st)
+        self.tokens.index_copy_(0, self.step_idx, self.ids.view(1, B))
+        self.step_idx.add_(1)
+        self.lens.add_(1)
+
+    def _gdn(self, pk, proj, slot: _GDNSlot, dc, st):
+        B, dt, dev = self.B, self.dt, self.dev
+        H, dk, dv, hid = pk.H, pk.dk, pk.dv, pk.hid
+        N_in = proj.shape[1]
+        cat = torch.empty((B, H * dv + hid), dtype=dt, device=dev)
+        _lib.call('motif_b200_gdn_decode', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+                  _lib.ptr(pk.dt_bias), _lib.ptr(slot.conv), _lib.ptr(slot.state),
+                  proj.data_ptr() + pk.off_g * proj.element_size(), _lib.ptr(pk.onorm_w), _lib.ptr(cat),
+                  cat.stride(0), B, H, dk, dv, NORM_EPS, dc, st)
+        _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
+                  cat.data_ptr() + H * dv * cat.element_size(), B, hid, N_in, cat.stride(0), dc, st)
+        return _mm(cat, pk.w_out)
+
+    def _chord(self, pk, proj, lc: KVLayerCache, dc, st):
+        B, dt, dev = self.B, self.dt, self.dev
+        H, Hkv, D, hid = pk.H, pk.Hkv, pk.D, pk.hid
+        d = H * D
+        N_in = proj.shape[1]
+        cap = lc._kbuf.shape[2]
+        qb = torch.empty((B, d), dtype=dt, device=dev)
+        lens_ptr = self.lens.data_ptr()
+        _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
+                  _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap, lens_ptr, 0, B, 1, H, Hkv, D, NORM_EPS, dc, st)
+        attn = torch.empty((B, d), dtype=dt, device=dev)
+        ws_bytes = _lib.load().motif_b200_chord_decode_workspace_bytes(B, H, 1, D, self.splits)
+        ws = torch.empty((max(ws_bytes, 4) // 4,), dtype=torch.float32, device=dev)
+        _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap,
+                  lens_ptr + 4, 0, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax),
+                  _lib.ptr(attn), d, B, H, Hkv, 1, D, D ** -0.5, GGD_EPS, self.splits, _lib.ptr(ws), ws_bytes, dc, st)
+        act = torch.empty((B, hid), dtype=dt, device=dev)
+        _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), B, hid,
+                  N_in, hid, dc, st)
+        f = _mm(act, pk.w_down)
+        a = _mm(attn, pk.w_o)
+        _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(),
+                  N_in, _lib.ptr(f), d, _lib.ptr(f), d, B, d, dc, st)
+        return f
+
+    # ------------------------------------------------------------------ capture / replay
+    def _snapshot(self):
+        return [s.state.clone() for s in self.gdn], [s.conv.clone() for s in self.gdn]
+
+    def _restore(self, snap):
+        for s, st_, cv in zip(self.gdn, snap[0], snap[1]):
+            s.state.copy_(st_)
+            s.conv.copy_(cv)
+
+    def _capture(self):
+        # The warm-up step (required before capture: cuBLAS handles, lazy library load) and the
+        # captured step both execute, so the recurrent states are saved and put back, and the
+        # cache positions they wrote are rewritten by the first real step.
+        snap = self._snapshot()
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        tr = _lib.Tracker(timed=None, events=False)
+        with torch.cuda.stream(side):
+            _lib.set_tracker(tr)
+            try:
+                self._step()
+            finally:
+                _lib.set_tracker(None)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        self.launches_per_step = tr.launches
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        torch.cuda.synchronize(self.dev)
+        self._restore(snap)
+        self.lens.copy_(torch.tensor([self.start, self.start + 1], dtype=torch.int32))
+        self.step_idx.zero_()
+        self.taken = 0
+
+    def run(self, first_ids: torch.Tensor, steps: int) -> torch.Tensor:
+        """Replay `steps` decode steps from the current position; returns [B, steps] tokens."""
+        steps = int(steps)
+        if steps < 0 or self.taken + steps > self.max_steps:
+            raise ValueError(f'{steps} steps after {self.taken} exceed max_steps={self.max_steps}')
+        ids = first_ids.reshape(-1)
+        if ids.numel() != self.B:
+            raise ValueError(f'first_ids holds {ids.numel()} ids for a batch of {self.B}')
+        self.ids.copy_(ids.to(self.dev, torch.int64), non_blocking=True)
+        lo = self.taken
+        for _ in range(steps):
+            self.graph.replay()
+        self.taken += steps
+        for lc in self.kv:
+            lc.length = self.start + self.taken
+        for s in self.gdn:
+            s.cache.length = self.start + self.taken
+        return self.tokens[lo:self.taken].t()
+
+    def release(self):
+        """Free the graph (and its memory pool)."""
+        self.graph = None
+
+
+def fill_cache_random(model, cache: ModelCache, batch: int, length: int, capacity: int, seed: int = 0):
+    """Fill every layer cache of `cache` as if `length` tokens had been prefilled, with seeded
+    random contents: Chord K (unit-RMS rows, as after k_norm) / V, GDN recurrent states and
+    conv windows.  Decode speed does not depend on the values; this stands in for a prefill
+    of `batch` x `length` tokens (the benchmark's decode context) without its time or memory."""
+    cfg = model.config
+    w = model.embed.weight
+    dev, dt = w.device, w.dtype
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    for b, block in enumerate(model.blocks):
+        bc = cache[b]
+        bc.ensure_attn([dec.cache_type for dec in block.features])
+        for i, dec in enumerate(block.features):
+            lc = bc.attn[i]
+            if dec.attn_type == 'chord':
+                Hkv, D = cfg.kv_heads, cfg.head_dim
+                lc._kbuf = torch.empty((batch, Hkv, capacity, D), dtype=dt, device=dev)
+                lc._vbuf = torch.empty_like(lc._kbuf)
+                lc._kbuf.normal_(0.0, 1.0, generator=g)
+                lc._vbuf.normal_(0.0, 0.5, generator=g)
+                lc.length = length
+            else:
+                H, dk, dv = cfg.num_heads, cfg.gdn_dk, cfg.gdn_dv
+                C = H * (2 * dk + dv)
+                lc.state = torch.empty((batch, H, dk, dv), dtype=torch.float32, device=dev).normal_(0.0, 0.05,
+                                                                                                   generator=g)
+                lc._conv = torch.empty((batch, 3, C), dtype=dt, device=dev).normal_(0.0, 0.5, generator=g)
+                lc._split = (H * dk, H * dk, H * dv)
+                lc.length = length
+    return cache

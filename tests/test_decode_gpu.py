@@ -1,0 +1,136 @@
+"""CUDA-graph batched decode (`motif_b200.decode.GraphDecoder`) against the eager decode path
+and the reference's greedy tokens.
+
+The graph replays the eager T = 1 kernels with device-side positions, so with the split-KV
+count pinned (`model.decode_splits`) graph and eager decode must give identical token ids,
+recurrent states and KV caches; against the reference (config 1, fp32) the 64 greedy tokens
+must be bit-exact.
+"""
+
+import os
+
+import pytest
+import torch
+
+from motif_b200.config import MotifChordConfig, tiny_config
+from motif_b200.init import init_params
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
+SMALL = dict(vocab_size=512, model_dim=64, num_heads=4, num_kv_heads=2, head_k_dim=16,
+             block=('gdn', 'gdn', 'gdn', 'chord'), block_n=2)
+
+
+def build(cfg, dtype=torch.float32, jitter=0.0):
+    from motif_b200.model import MotifChordModel
+    torch.manual_seed(0)
+    m = MotifChordModel(cfg)
+    init_params(m, seed=0, norm_jitter=jitter)
+    return m.to('cuda', dtype).eval()
+
+
+def eager_decode(m, ids, steps):
+    out = m(ids)
+    cache, tok = out.cache, out.next_token()
+    first = tok
+    toks = []
+    for _ in range(steps):
+        out = m(tok, cache=cache)
+        tok = out.next_token()
+        toks.append(tok)
+    return first, torch.cat(toks, 1), cache
+
+
+def graph_decode(m, ids, steps, chunks=None):
+    from motif_b200.decode import GraphDecoder
+    out = m(ids)
+    first = out.next_token()
+    dec = GraphDecoder(m, out.cache, max_steps=steps)
+    parts, tok = [], first
+    for n in (chunks or [steps]):
+        t = dec.run(tok, n)
+        parts.append(t.clone())
+        tok = t[:, -1:]
+    return first, torch.cat(parts, 1), out.cache, dec
+
+
+def _gdn_states(cache):
+    from motif_b200.cache import GatedDeltaAttentionLayerCache
+    return [lc.state for bc in cache for lc in bc.attn if isinstance(lc, GatedDeltaAttentionLayerCache)]
+
+
+def _kv(cache):
+    from motif_b200.cache import KVLayerCache
+    return [(lc.k, lc.v) for bc in cache for lc in bc.attn if isinstance(lc, KVLayerCache)]
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_graph_matches_eager_small(dtype):
+    m = build(MotifChordConfig(**SMALL), dtype=dtype, jitter=0.1)
+    m.decode_splits = 2
+    ids = torch.randint(0, 512, (3, 40), generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad():
+        f_e, t_e, c_e = eager_decode(m, ids, 20)
+        f_g, t_g, c_g, dec = graph_decode(m, ids, 20)
+    assert torch.equal(f_e, f_g)
+    assert torch.equal(t_e, t_g), (t_e != t_g).nonzero()
+    for a, b in zip(_gdn_states(c_e), _gdn_states(c_g)):
+        assert torch.equal(a, b)
+    for (ka, va), (kb, vb) in zip(_kv(c_e), _kv(c_g)):
+        assert ka.shape == kb.shape and torch.equal(ka, kb) and torch.equal(va, vb)
+    assert dec.launches_per_step > 0
+
+
+def test_graph_run_in_parts_equals_one_run():
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    m.decode_splits = 2
+    ids = torch.randint(0, 512, (2, 33), generator=torch.Generator().manual_seed(2)).cuda()
+    with torch.no_grad():
+        _, whole, _, _ = graph_decode(m, ids, 12)
+        _, parts, cache, dec = graph_decode(m, ids, 12, chunks=[5, 7])
+    assert torch.equal(whole, parts)
+    assert all(lc.length == 33 + 12 for bc in cache for lc in bc.attn)
+    with pytest.raises(ValueError):
+        dec.run(parts[:, -1:], 1)   # past max_steps
+
+
+def test_graph_then_eager_continues():
+    """After a graph run the cache's host lengths are advanced: the eager path continues."""
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    m.decode_splits = 2
+    ids = torch.randint(0, 512, (2, 30), generator=torch.Generator().manual_seed(3)).cuda()
+    with torch.no_grad():
+        _, t_e, _ = eager_decode(m, ids, 10)
+        _, t_g, cache, _ = graph_decode(m, ids, 6)
+        tok = t_g[:, -1:]
+        rest = []
+        for _ in range(4):
+            out = m(tok, cache=cache)
+            tok = out.next_token()
+            rest.append(tok)
+    assert torch.equal(t_e, torch.cat([t_g] + rest, 1))
+
+
+def test_tiny_config_graph_greedy64_matches_reference():
+    d = torch.load(os.path.join(GOLD, 'tiny.pt'))
+    m = build(tiny_config())
+    ids = d['ids'].cuda()
+    with torch.no_grad():
+        first, toks, _, _ = graph_decode(m, ids, 63)
+    gen = torch.cat([first, toks], 1).cpu()
+    assert torch.equal(gen, d['greedy']), (gen != d['greedy']).nonzero()
+
+
+def test_random_filled_cache_decode_172m_shapes():
+    from motif_b200.config import config_172m
+    from motif_b200.decode import GraphDecoder, fill_cache_random
+    m = build(config_172m(), dtype=torch.bfloat16)
+    B, L, steps = 4, 1000, 8
+    cache = fill_cache_random(m, m.create_cache(), B, L, L + steps)
+    dec = GraphDecoder(m, cache, max_steps=steps)
+    first = torch.zeros((B, 1), dtype=torch.int64, device='cuda')
+    toks = dec.run(first, steps)
+    torch.cuda.synchronize()
+    assert toks.shape == (B, steps)
+    assert int(toks.min()) >= 0 and int(toks.max()) < m.config.vocab_size
+    assert all(lc.length == L + steps for bc in cache for lc in bc.attn)
