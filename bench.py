@@ -258,6 +258,16 @@ def run_ours(args, world, rank, local):
     model = MotifChordModel(cfg)
     init_params(model, seed=0)
     model = model.to(dev, torch.bfloat16).eval()
+    if args.mode == 'decode':
+        # decode measurement alone, printed as the line's headline (profiling captures)
+        d = run_decode(model, cfg, args, world, rank, local, dev, torch.cuda.current_stream(dev), peaks())
+        if rank == 0:
+            line = dict(d, n_gpus=world, warmup=3, dtype='bf16', data='synthetic', vs_baseline=None)
+            line['roofline'] = {'bound': 'hbm', 'achieved': d['hbm']['achieved_gbs_per_gpu'], 'peak': d['hbm']['peak'],
+                                'unit': 'GB/s', 'frac': d['hbm']['frac'], 'traffic': None,
+                                'kernel': 'whole decode step (all kernels)'}
+            print(json.dumps(line), flush=True)
+        return
     ids_all = torch.randint(0, cfg.vocab_size, (gb, T), generator=torch.Generator().manual_seed(0))
     ids_host = ids_all[lo:hi].contiguous().pin_memory()
     ids_dev = ids_host.to(dev)
@@ -415,12 +425,14 @@ def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
     64 x 8192 tokens would leave them."""
     from motif_b200 import _lib
     from motif_b200.decode import GraphDecoder, fill_cache_random
-    B, L, n = DECODE_BATCH, DECODE_CONTEXT, args.decode_steps
+    B, L, n = args.decode_batch, DECODE_CONTEXT, args.decode_steps
     cache = fill_cache_random(model, model.create_cache(), B, L, L + 2 * n, seed=rank)
     dec = GraphDecoder(model, cache, max_steps=2 * n)
     g = torch.Generator().manual_seed(rank)
     first_host = torch.randint(0, cfg.vocab_size, (B, 1), generator=g).pin_memory()
     first = first_host.to(dev)
+    # per-kernel breakdown of one step, run eagerly with events (outside the timed region)
+    brk = dec.breakdown(first)
     # warm-up replays (also the first touch of every cache page), then the caches' lengths
     # are rewound so the timed steps start at context 8192
     dec.run(first, min(3, n))
@@ -464,6 +476,8 @@ def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
         'e2e': {'value': total_tok / (e2e_ms / 1000.0), 'unit': 'tokens/s',
                 'h2d_bytes_per_step': first_host.numel() * 8 / n, 'd2h_bytes_per_step': toks.numel() * 8 / n},
         'gpu_launches': dec.launches_per_step * n,
+        'kernels': {k.replace('motif_b200_', ''): {'calls': c, 'ms': round(t, 4)}
+                    for k, (c, t) in sorted(brk.items(), key=lambda kv: -kv[1][1])},
         'clocks': clk.summary(),
     }
     dec.release()
@@ -483,6 +497,10 @@ def main():
                          f'{GLOBAL_BATCH} per rank (weak scaling); small values are for profiling captures')
     ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--mode', choices=['all', 'decode'], default='all',
+                    help="'decode' runs only the config-5 decode measurement (for profiling)")
+    ap.add_argument('--decode-batch', type=int, default=DECODE_BATCH,
+                    help=f'decode sequences per rank (the benchmark config is {DECODE_BATCH})')
     ap.add_argument('--decode-steps', type=int, default=256,
                     help='greedy decode steps of the config-5 decode measurement (0 skips it)')
     args = ap.parse_args()

@@ -319,149 +319,316 @@ __global__ void __launch_bounds__(128) chord_fwd_simple_kernel(
 }
 
 // ------------------------------------------------------------------ split-KV decode
-// Rows R = G * T (query heads of the group x new tokens), R <= 16.  q token-major [B*T, H*D].
-template <typename T, int D>
+// One CTA (4 warps) per (split, b * Hkv + kv head).  A split's keys are a contiguous run of
+// that (b, kv head)'s [cap, D] K and V arrays, streamed through a ring of kDecStages
+// 64-key tiles by one-dimensional bulk copies: thread 0 issues K and V of a tile onto the
+// stage's mbarrier, every thread waits on it (bounded), and the stage is refilled once the
+// whole CTA has finished with it.  Rows R = G * Tn (query heads of the group x new tokens),
+// R <= RM.
+//   scores       warp w scores keys 16w .. 16w+15 of the tile, four at a time: each 8-lane
+//                group takes one key, its lanes hold D/8 dims of every query row and reduce
+//                the partial dots with three xor-shuffles;
+//   softmax + PV warp w owns rows w, w+4, ...; online softmax over the tile, then each lane
+//                accumulates D/32 output dims over the tile's keys.
+// Partials: ws[((split * B + b) * H + h) * Tn + t][D + 2] = (o[0..D), m, l) for the merge.
+// GGD bias in the decode kernel: 16-bit inputs use exp2(beta * log2(x)) on the fast log2 (the
+// result's relative error, a few 1e-7, is far below bf16 / fp16 resolution); fp32 keeps powf.
+template <typename T>
+__device__ __forceinline__ float ggd_bias_decode(float alpha, float beta, float mu, float delta, float eps) {
+  if constexpr (sizeof(T) == 2) {
+    return -alpha * exp2f(beta * __log2f(fabsf(-delta - mu) + eps));
+  } else {
+    return ggd_bias(alpha, beta, mu, delta, eps);
+  }
+}
+
+constexpr int kDecTile = 64;
+constexpr int kDecStages = 4;
+constexpr uint32_t kDecWaitLimit = 1u << 22;
+// Count of decode CTAs whose bulk-copy wait ran out (never expected; read and cleared by
+// motif_b200_decode_wait_timeouts).
+__device__ unsigned int g_decode_wait_timeouts = 0;
+
+template <typename T, int D, int RM>
+struct DecodeSmem {
+  T k[kDecStages][kDecTile][D];
+  T v[kDecStages][kDecTile][D];
+  float p[RM][kDecTile];
+  uint64_t bar[kDecStages];
+};
+
+template <int N, typename T>
+__device__ __forceinline__ void load_vec_f(const T* src, float* dst) {
+  // N consecutive elements from shared memory, 16 / 8 / 4-byte vector loads where N allows
+  constexpr int BYTES = N * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+    for (int c = 0; c < BYTES / 16; ++c) {
+      const uint4 raw = reinterpret_cast<const uint4*>(src)[c];
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int x = 0; x < 16 / (int)sizeof(T); ++x) dst[c * (16 / sizeof(T)) + x] = to_f(e[x]);
+    }
+  } else if constexpr (BYTES == 8) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int x = 0; x < N; ++x) dst[x] = to_f(e[x]);
+  } else if constexpr (BYTES == 4) {
+    const uint32_t raw = *reinterpret_cast<const uint32_t*>(src);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int x = 0; x < N; ++x) dst[x] = to_f(e[x]);
+  } else {
+#pragma unroll
+    for (int x = 0; x < N; ++x) dst[x] = to_f(src[x]);
+  }
+}
+
+template <typename T, int D, int RM>
 __global__ void __launch_bounds__(128) chord_decode_kernel(
     const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int64_t cap,
     const int32_t* __restrict__ len_dev, int len_host, const float* __restrict__ alpha,
     const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
     float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps) {
-  constexpr int MAXR = 16;
-  constexpr int DPL = D / 32;  // output dims per lane (D in {32, 64, 128})
+  constexpr int QD = D / 8;   // dims per lane in the score phase
+  constexpr int OD = D / 32;  // output dims per lane
+  constexpr int RW = RM / 4;  // rows per warp in the softmax / PV phase
+  extern __shared__ __align__(128) unsigned char dec_smem_raw[];
+  auto& sm = *reinterpret_cast<DecodeSmem<T, D, RM>*>(dec_smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = blockIdx.x * 4 + warp;
+  const int sub = lane & 7, grp = lane >> 3;
+  const int split = blockIdx.x;
   const int bk = blockIdx.y;  // b * Hkv + kvh
   const int b = bk / Hkv, kvh = bk % Hkv;
   const int G = H / Hkv;
   const int R = G * Tn;
-  __shared__ float sq[4][MAXR][D];
-  if (split >= nsplit) return;
   // cache length including the new tokens; a device-side length is clamped to [Tn, cap] so
   // that a stale counter can only give wrong scores, never an access outside the cache
   const int S = len_dev ? min(max(*len_dev, Tn), (int)cap) : len_host;
   const int q_start = S - Tn;
-  // keys handled by this split (multiples of 32)
-  const int per = ((S + nsplit - 1) / nsplit + 31) & ~31;
-  const int kbeg = split * per, kend = min(S, kbeg + per);
-  for (int idx = lane; idx < R * D; idx += 32) {
-    const int r = idx / D, d = idx % D;
-    const int hg = r / Tn, t = r % Tn;
-    sq[warp][r][d] = to_f(q[((int64_t)b * Tn + t) * H * D + (kvh * G + hg) * D + d]);
-  }
-  __syncwarp();
-  float m[MAXR], l[MAXR], o[MAXR][DPL], rc[MAXR];
-#pragma unroll
-  for (int r = 0; r < MAXR; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) o[r][i] = 0.f;
-    rc[r] = 0.f;
-    if (r < R) {
-      const int h = kvh * G + r / Tn;
-      const int qa = q_start + r % Tn;
-      rc[r] = ssmax[h] * logf((float)(qa + 1)) * kLog2e;
-    }
-  }
+  const int per = ((S + nsplit - 1) / nsplit + kDecTile - 1) / kDecTile * kDecTile;
+  const int kbeg = min(S, split * per), kend = min(S, kbeg + per);
+  const int ntile = (kend - kbeg + kDecTile - 1) / kDecTile;
   const T* kb = kc + ((int64_t)b * Hkv + kvh) * cap * D;
   const T* vb = vc + ((int64_t)b * Hkv + kvh) * cap * D;
-  for (int j0 = kbeg; j0 < kend; j0 += 32) {
-    const int j = j0 + lane;
-    float kr[D];
-    if (j < kend) {
-      const uint4* src = reinterpret_cast<const uint4*>(kb + (int64_t)j * D);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDecStages; ++s) mbar_init(&sm.bar[s], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  auto issue = [&](int t) {  // thread 0: K and V rows of tile t into stage t % kDecStages
+    const int s = t % kDecStages;
+    const int j0 = kbeg + t * kDecTile;
+    const uint32_t bytes = (uint32_t)(min(kDecTile, kend - j0) * D * (int)sizeof(T));
+    mbar_arrive_expect_tx(&sm.bar[s], 2 * bytes);
+    bulk_load(&sm.k[s][0][0], kb + (int64_t)j0 * D, bytes, &sm.bar[s]);
+    bulk_load(&sm.v[s][0][0], vb + (int64_t)j0 * D, bytes, &sm.bar[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int t = 0; t < min(ntile, kDecStages); ++t) issue(t);
+
+  // this lane's D/8 slice of every query row; the rows whose scores this lane finalises are
+  // sub and sub + 8 (RO of them), with their log-n scaling, position and GGD parameters
+  constexpr int RO = (RM + 7) / 8;
+  float qr[RM][QD];
 #pragma unroll
-      for (int c = 0; c < D * (int)sizeof(T) / 16; ++c) {
-        uint4 raw = src[c];
-        const T* e = reinterpret_cast<const T*>(&raw);
+  for (int r = 0; r < RM; ++r) {
 #pragma unroll
-        for (int x = 0; x < 16 / (int)sizeof(T); ++x) kr[c * (16 / sizeof(T)) + x] = to_f(e[x]);
-      }
-    } else {
+    for (int i = 0; i < QD; ++i) qr[r][i] = 0.f;
+    if (r < R) {
+      const int h = kvh * G + r / Tn, t = r % Tn;
+      const T* qrow = q + ((int64_t)b * Tn + t) * H * D + (int64_t)h * D + sub * QD;
 #pragma unroll
-      for (int d = 0; d < D; ++d) kr[d] = 0.f;
-    }
-    float p[MAXR];
-#pragma unroll
-    for (int r = 0; r < MAXR; ++r) {
-      if (r >= R) break;
-      const int h = kvh * G + r / Tn;
-      const int qa = q_start + r % Tn;
-      float x = -INFINITY;
-      if (j < kend && j <= qa) {
-        float s = 0.f;
-#pragma unroll
-        for (int d = 0; d < D; ++d) s = fmaf(sq[warp][r][d], kr[d], s);
-        x = (s * scale + ggd_bias(alpha[h], beta[h], mu[h], (float)(qa - j), eps)) * rc[r];
-      }
-      const float cm = warp_max(x);
-      const float mn = fmaxf(m[r], cm);
-      const float mb = mn == -INFINITY ? 0.f : mn;
-      const float corr = exp2f(m[r] - mb);
-      p[r] = exp2f(x - mb);
-      l[r] = l[r] * corr + p[r];
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) o[r][i] *= corr;
-      m[r] = mn;
-    }
-    const int nk = min(32, kend - j0);
-    for (int jj = 0; jj < nk; ++jj) {
-      const T* vr = vb + (int64_t)(j0 + jj) * D;
-      float vv[DPL];
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) vv[i] = to_f(vr[lane + 32 * i]);
-#pragma unroll
-      for (int r = 0; r < MAXR; ++r) {
-        if (r >= R) break;
-        const float pj = __shfl_sync(0xffffffffu, p[r], jj);
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) o[r][i] = fmaf(pj, vv[i], o[r][i]);
-      }
+      for (int i = 0; i < QD; ++i) qr[r][i] = to_f(qrow[i]);
     }
   }
-  // partials: ws[((split * B + b) * H + h) * Tn + t][D + 2] = (o[0..D), m, l)
+  float rc[RO], pa[RO], pb[RO], pm[RO];
+  int qa[RO];
 #pragma unroll
-  for (int r = 0; r < MAXR; ++r) {
+  for (int u = 0; u < RO; ++u) {
+    const int r = sub + 8 * u;
+    rc[u] = pa[u] = pb[u] = pm[u] = 0.f;
+    qa[u] = -1;
+    if (r < R) {
+      const int h = kvh * G + r / Tn, t = r % Tn;
+      qa[u] = q_start + t;
+      rc[u] = ssmax[h] * logf((float)(qa[u] + 1)) * kLog2e;
+      pa[u] = alpha[h];
+      pb[u] = beta[h];
+      pm[u] = mu[h];
+    }
+  }
+  float m[RW], l[RW], o[RW][OD];
+#pragma unroll
+  for (int i = 0; i < RW; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int d = 0; d < OD; ++d) o[i][d] = 0.f;
+  }
+
+  int t = 0;
+  bool failed = false;
+  for (; t < ntile; ++t) {
+    const int s = t % kDecStages;
+    const int j0 = kbeg + t * kDecTile;
+    const int nk = min(kDecTile, kend - j0);
+    const bool ok = mbar_wait_bounded(&sm.bar[s], (uint32_t)((t / kDecStages) & 1), kDecWaitLimit);
+    // scores (a stage whose copy did not land is read anyway: in bounds, result discarded)
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int kk = warp * 16 + pass * 4 + grp;
+      const int j = j0 + kk;
+      float kf[QD];
+      load_vec_f<QD>(&sm.k[s][kk][sub * QD], kf);
+      float acc[RM];
+#pragma unroll
+      for (int r = 0; r < RM; ++r) {
+        acc[r] = 0.f;
+        if (r < R) {
+#pragma unroll
+          for (int i = 0; i < QD; ++i) acc[r] = fmaf(qr[r][i], kf[i], acc[r]);
+          acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
+          acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
+          acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 4);
+        }
+      }
+      // every lane of the group now holds every row's dot; lane sub finalises rows sub, sub + 8
+#pragma unroll
+      for (int u = 0; u < RO; ++u) {
+        const int r = sub + 8 * u;
+        float a = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < RM; ++rr)
+          if (rr == r) a = acc[rr];
+        if (r < R) {
+          float x = -INFINITY;
+          if (kk < nk && j <= qa[u])
+            x = (a * scale + ggd_bias_decode<T>(pa[u], pb[u], pm[u], (float)(qa[u] - j), eps)) * rc[u];
+          sm.p[r][kk] = x;
+        }
+      }
+    }
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+    // online softmax + PV for this warp's rows
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      const int r = warp + 4 * i;
+      if (r >= R) break;
+      const float x0 = sm.p[r][lane], x1 = sm.p[r][lane + 32];
+      const float cm = warp_max(fmaxf(x0, x1));
+      const float mn = fmaxf(m[i], cm);
+      const float mb = mn == -INFINITY ? 0.f : mn;
+      const float corr = exp2f(m[i] - mb);
+      const float p0 = exp2f(x0 - mb), p1 = exp2f(x1 - mb);
+      l[i] = l[i] * corr + p0 + p1;
+      m[i] = mn;
+      sm.p[r][lane] = p0;
+      sm.p[r][lane + 32] = p1;
+      __syncwarp();
+#pragma unroll
+      for (int d = 0; d < OD; ++d) o[i][d] *= corr;
+      int kk = 0;
+#pragma unroll 2
+      for (; kk + 4 <= nk; kk += 4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(&sm.p[r][kk]);
+        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float vf[OD];
+          load_vec_f<OD>(&sm.v[s][kk + e][lane * OD], vf);
+#pragma unroll
+          for (int d = 0; d < OD; ++d) o[i][d] = fmaf(pj[e], vf[d], o[i][d]);
+        }
+      }
+      for (; kk < nk; ++kk) {
+        const float pj = sm.p[r][kk];
+        float vf[OD];
+        load_vec_f<OD>(&sm.v[s][kk][lane * OD], vf);
+#pragma unroll
+        for (int d = 0; d < OD; ++d) o[i][d] = fmaf(pj, vf[d], o[i][d]);
+      }
+    }
+    __syncthreads();  // stage s and the score tile are free again
+    if (threadIdx.x == 0 && t + kDecStages < ntile) {
+      fence_proxy_async_smem();
+      issue(t + kDecStages);
+    }
+  }
+  if (failed) {
+    // record, then let the copies already issued land (bounded) before the CTA exits
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_decode_wait_timeouts, 1u);
+      for (int u = t; u < min(ntile, t + kDecStages); ++u)
+        mbar_wait_bounded(&sm.bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      m[i] = -INFINITY;
+      l[i] = 0.f;
+#pragma unroll
+      for (int d = 0; d < OD; ++d) o[i][d] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RW; ++i) {
+    const int r = warp + 4 * i;
     if (r >= R) break;
-    const float lt = warp_sum(l[r]);
-    const int h = kvh * G + r / Tn, t = r % Tn;
-    float* dst = ws + ((((int64_t)split * B + b) * H + h) * Tn + t) * (D + 2);
+    const float lt = warp_sum(l[i]);
+    const int h = kvh * G + r / Tn, tt = r % Tn;
+    float* dst = ws + ((((int64_t)split * B + b) * H + h) * Tn + tt) * (D + 2);
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) dst[lane + 32 * i] = o[r][i];
+    for (int d = 0; d < OD; ++d) dst[lane * OD + d] = o[i][d];
     if (lane == 0) {
-      dst[D] = m[r];
+      dst[D] = m[i];
       dst[D + 1] = lt;
     }
   }
 }
 
-template <typename T>
-__global__ void chord_merge_kernel(const float* __restrict__ ws, T* __restrict__ out, int64_t os, int B, int H,
-                                   int Tn, int D, int nsplit) {
-  const int64_t row = blockIdx.x;  // (b * Tn + t) * H + h
+// Merge of the split partials: one warp per (b, t, h) output row.  Lanes stride over the
+// splits for the global max and the denominator, then each lane combines D/32 dims.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) chord_merge_kernel(const float* __restrict__ ws, T* __restrict__ out,
+                                                          int64_t os, int B, int H, int Tn, int nsplit) {
+  constexpr int OD = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);  // (b * Tn + t) * H + h
+  if (row >= (int64_t)B * Tn * H) return;
   const int h = (int)(row % H);
   const int64_t bt = row / H;
   const int t = (int)(bt % Tn), b = (int)(bt / Tn);
+  const int64_t split_stride = (int64_t)B * H * Tn * (D + 2);
+  const float* base = ws + (((int64_t)b * H + h) * Tn + t) * (D + 2);
   float mmax = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) {
-    const float* src = ws + ((((int64_t)s * B + b) * H + h) * Tn + t) * (D + 2);
-    mmax = fmaxf(mmax, src[D]);
-  }
+  for (int sp = lane; sp < nsplit; sp += 32) mmax = fmaxf(mmax, base[sp * split_stride + D]);
+  mmax = warp_max(mmax);
   const float mb = mmax == -INFINITY ? 0.f : mmax;
   float den = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const float* src = ws + ((((int64_t)s * B + b) * H + h) * Tn + t) * (D + 2);
+  for (int sp = lane; sp < nsplit; sp += 32) {
+    const float* src = base + sp * split_stride;
     den += src[D + 1] * exp2f(src[D] - mb);
   }
-  const float inv = 1.f / fmaxf(den, 1e-20f);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float* src = ws + ((((int64_t)s * B + b) * H + h) * Tn + t) * (D + 2);
-      acc += src[d] * exp2f(src[D] - mb);
-    }
-    out[((int64_t)b * Tn + t) * os + (int64_t)h * D + d] = from_f<T>(acc * inv);
+  den = warp_sum(den);
+  float acc[OD];
+#pragma unroll
+  for (int d = 0; d < OD; ++d) acc[d] = 0.f;
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const float* src = base + sp * split_stride;
+    const float w = exp2f(src[D] - mb);
+#pragma unroll
+    for (int d = 0; d < OD; ++d) acc[d] = fmaf(w, src[lane * OD + d], acc[d]);
   }
+  const float inv = 1.f / fmaxf(den, 1e-20f);
+  T* dst = out + ((int64_t)b * Tn + t) * os + (int64_t)h * D;
+#pragma unroll
+  for (int d = 0; d < OD; ++d) dst[lane * OD + d] = from_f<T>(acc[d] * inv);
 }
 
 // ------------------------------------------------------------------ prep (q/k norms + append)
@@ -633,20 +800,36 @@ extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const
              "chord_decode: workspace too small");
   MB_REQUIRE(len_dev != nullptr || (len_host >= T && len_host <= cap), MB_ERR_ARG, "chord_decode: bad length");
   MB_REQUIRE(((uintptr_t)k_cache | (uintptr_t)v_cache) % 16 == 0, MB_ERR_ALIGN, "chord_decode: cache alignment");
+  MB_REQUIRE(B * Hkv < 65536 && cap < (1LL << 31), MB_ERR_SHAPE, "chord_decode: B*Hkv or cap too large");
   cudaStream_t st = (cudaStream_t)stream;
   return dispatch_dtype(dtype, [&](auto t) {
     using Tt = decltype(t);
     auto go = [&](auto dc) {
       constexpr int DD = decltype(dc)::value;
-      dim3 grid((unsigned)((max_splits + 3) / 4), (unsigned)(B * Hkv));
-      chord_decode_kernel<Tt, DD><<<grid, 128, 0, st>>>((const Tt*)q, (const Tt*)k_cache, (const Tt*)v_cache, cap,
-                                                        len_dev, (int)len_host, alpha, beta, mu, ssmax,
-                                                        (float*)workspace, (int)B, (int)H, (int)Hkv, (int)T,
-                                                        max_splits, scale, eps);
-      int rc = check_launch("chord_decode");
+      dim3 grid((unsigned)max_splits, (unsigned)(B * Hkv));
+      const int R = (int)((H / Hkv) * T);
+      auto launch = [&](auto rmc) {
+        constexpr int RM = decltype(rmc)::value;
+        auto kern = chord_decode_kernel<Tt, DD, RM>;
+        const int smem = (int)sizeof(DecodeSmem<Tt, DD, RM>);
+        static bool attr_set[64] = {};  // per instantiation and device
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+          if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_launch("chord_decode (shared memory attribute)");
+          if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        }
+        kern<<<grid, 128, smem, st>>>((const Tt*)q, (const Tt*)k_cache, (const Tt*)v_cache, cap, len_dev,
+                                      (int)len_host, alpha, beta, mu, ssmax, (float*)workspace, (int)B, (int)H,
+                                      (int)Hkv, (int)T, max_splits, scale, eps);
+        return check_launch("chord_decode");
+      };
+      int rc = R <= 4 ? launch(std::integral_constant<int, 4>{})
+                      : R <= 8 ? launch(std::integral_constant<int, 8>{}) : launch(std::integral_constant<int, 16>{});
       if (rc) return rc;
-      chord_merge_kernel<Tt><<<(unsigned)(B * T * H), 64, 0, st>>>((const float*)workspace, (Tt*)out, out_stride,
-                                                                    (int)B, (int)H, (int)T, (int)DD, max_splits);
+      chord_merge_kernel<Tt, DD><<<(unsigned)((B * T * H + 3) / 4), 128, 0, st>>>(
+          (const float*)workspace, (Tt*)out, out_stride, (int)B, (int)H, (int)T, max_splits);
       return check_launch("chord_merge");
     };
     switch (D) {
@@ -738,4 +921,14 @@ extern "C" int motif_b200_chord_decode_noalloc(const void* q, const void* k_cach
   return motif_b200_chord_decode(q, k_cache, v_cache, cap, len_dev, len_host, alpha, beta, mu, ssmax, out,
                                  out_stride, B, H, Hkv, T, D, scale, eps, max_splits, ws, mb::kNoAllocScratchBytes,
                                  dtype, stream);
+}
+
+extern "C" int motif_b200_decode_wait_timeouts(uint32_t* count) {
+  MB_REQUIRE(count != nullptr, MB_ERR_ARG, "decode_wait_timeouts: null pointer");
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_decode_wait_timeouts, sizeof(v)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_decode_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
+    return set_error(MB_ERR_CUDA, "decode_wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
+  *count = v;
+  return MB_OK;
 }

@@ -148,6 +148,110 @@ __global__ void __launch_bounds__(DV) gdn_decode_kernel(
   out[(int64_t)b * os + h * DV + j] = from_f<T>(y * to_f(from_f<T>(siluf_(gt))));
 }
 
+// The same step for the model's shape Dv == 2 * Dk with 2 * Dv threads per (b, head): the
+// 2*Dk + Dv conv channels of the head are one per thread (q: threads [0, Dk), k: [Dk, 2Dk),
+// v: [2Dk, 4Dk)), and each state column j is split between threads j (rows [0, Dk/2)) and
+// j + Dv (rows [Dk/2, Dk)), whose partial kᵀS and qᵀS meet in shared memory.  The state
+// loads are issued first, so their latency overlaps the conv, norms and gate math; half
+// the registers per thread of the one-column kernel, twice the threads in flight.
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
+    const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
+    const T* __restrict__ dt_bias, T* __restrict__ conv_state, float* __restrict__ state,
+    const T* __restrict__ gate, const T* __restrict__ onw, T* __restrict__ out, int64_t os, int H,
+    float eps) {
+  static_assert(DV == 2 * DK, "one conv channel per thread needs Dv == 2 Dk");
+  constexpr int NT = 2 * DV, HR = DK / 2;
+  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  const int tid = threadIdx.x;
+  const int j = tid % DV, half = tid / DV;
+  const int C = H * (2 * DK + DV);
+  const T* row = proj + (int64_t)b * ps;
+  T* cs = conv_state + (int64_t)b * 3 * C;
+  __shared__ float sq[DK], sk[DK], sv[DV], part[2][DV], red[NT / 32];
+  __shared__ float norms[2];
+
+  float* S = state + ((int64_t)b * H + h) * DK * DV + (int64_t)half * HR * DV + j;
+  float Sr[HR];
+#pragma unroll
+  for (int i = 0; i < HR; ++i) Sr[i] = S[i * DV];
+
+  // conv + SiLU of this thread's channel (gdn_attn.py:116-136)
+  const int c = tid < DK ? h * DK + tid : tid < 2 * DK ? H * DK + h * DK + (tid - DK) : 2 * H * DK + h * DV + (tid - 2 * DK);
+  float y;
+  {
+    const float x = to_f(row[c]);
+    const float s0 = to_f(cs[c]), s1 = to_f(cs[C + c]), s2 = to_f(cs[2 * C + c]);
+    const T* w = conv_w + (int64_t)c * 4;
+    const float acc = to_f(w[0]) * s0 + to_f(w[1]) * s1 + to_f(w[2]) * s2 + to_f(w[3]) * x;
+    cs[c] = from_f<T>(s1);
+    cs[C + c] = from_f<T>(s2);
+    cs[2 * C + c] = from_f<T>(x);
+    y = siluf_(to_f(from_f<T>(acc)));
+  }
+  // L2 norms of q (warps of threads [0, DK)) and k (threads [DK, 2DK))
+  {
+    const float sq2 = warp_sum(tid < 2 * DK ? y * y : 0.f);
+    if ((tid & 31) == 0) red[tid >> 5] = sq2;
+  }
+  __syncthreads();
+  if (tid < 2) {
+    float acc = 0.f;
+    for (int w = tid * (DK / 32); w < (tid + 1) * (DK / 32); ++w) acc += red[w];
+    norms[tid] = acc;
+  }
+  __syncthreads();
+  if (tid < DK) {
+    sq[tid] = y / fmaxf(sqrtf(norms[0]), 1e-12f) * rsqrtf((float)DK);
+  } else if (tid < 2 * DK) {
+    sk[tid - DK] = y / fmaxf(sqrtf(norms[1]), 1e-12f);
+  } else {
+    sv[tid - 2 * DK] = y;
+  }
+  const float a = to_f(row[2 * H * DK + H * DV + h]);
+  const float bsc = to_f(row[2 * H * DK + H * DV + H + h]);
+  const float bt = sigmoidf_(bsc);
+  const float gg = -expf(to_f(A_log[h])) * softplusf_(a + to_f(dt_bias[h]));
+  const float e = expf(gg);
+  __syncthreads();
+
+  // delta rule on the split column: S <- e S;  delta = beta (v - kᵀS);  S += k deltaᵀ;  o = qᵀS
+  float vo = 0.f;
+#pragma unroll
+  for (int i = 0; i < HR; ++i) {
+    Sr[i] *= e;
+    vo = fmaf(sk[half * HR + i], Sr[i], vo);
+  }
+  part[half][j] = vo;
+  __syncthreads();
+  const float delta = bt * (sv[j] - (part[0][j] + part[1][j]));
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < HR; ++i) {
+    Sr[i] = fmaf(sk[half * HR + i], delta, Sr[i]);
+    acc = fmaf(sq[half * HR + i], Sr[i], acc);
+    S[i * DV] = Sr[i];
+  }
+  __syncthreads();  // every thread has read part[] for its delta
+  part[half][j] = acc;
+  __syncthreads();
+  // o.to(dtype) then GatedRMSNorm over the Dv outputs (rms_norm.py:547-553): threads [0, DV)
+  const float ov = to_f(from_f<T>(part[0][j] + part[1][j]));
+  const float ss2 = warp_sum(half == 0 ? ov * ov : 0.f);
+  if ((tid & 31) == 0) red[tid >> 5] = ss2;
+  __syncthreads();
+  if (half == 0) {
+    float ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < DV / 32; ++w) ss += red[w];
+    const float r = rsqrtf(ss / (float)DV + eps);
+    float yo = to_f(from_f<T>(ov * r));
+    yo = to_f(from_f<T>(yo * to_f(onw[j])));
+    const float gt = to_f(gate[(int64_t)b * ps + h * DV + j]);
+    out[(int64_t)b * os + h * DV + j] = from_f<T>(yo * to_f(from_f<T>(siluf_(gt))));
+  }
+}
+
 // ------------------------------------------------------------- prefill preparation
 // gdn_attn.py:116-136 (conv over time with the carried state, SiLU) and :187-197.
 // One warp per (b, head, block of TB tokens); lanes own channels and keep a sliding window
@@ -473,6 +577,11 @@ extern "C" int motif_b200_gdn_decode(const void* proj, int64_t ps, const void* c
         constexpr int DV = decltype(dvc)::value;
         if constexpr (DV < DK) {
           return set_error(MB_ERR_UNSUPPORTED, "gdn_decode: needs Dv >= Dk");
+        } else if constexpr (DV == 2 * DK && DK % 32 == 0 && 2 * DV <= 512) {
+          gdn_decode_split_kernel<T, DK, DV><<<(unsigned)(B * H), 2 * DV, 0, (cudaStream_t)stream>>>(
+              (const T*)proj, ps, (const T*)conv_w, (const T*)A_log, (const T*)dt_bias, (T*)conv_state,
+              state, (const T*)gate, (const T*)onorm_w, (T*)out, os, (int)H, eps);
+          return check_launch("gdn_decode");
         } else {
           gdn_decode_kernel<T, DK, DV><<<(unsigned)(B * H), DV, 0, (cudaStream_t)stream>>>(
               (const T*)proj, ps, (const T*)conv_w, (const T*)A_log, (const T*)dt_bias, (T*)conv_state,

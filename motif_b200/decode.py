@@ -109,6 +109,9 @@ class GraphDecoder:
         self.cap = min(lc.capacity for lc in self.kv)
         cfg = model.config
         Hkv = cfg.kv_heads
+        if self.kv and cfg.head_dim not in (32, 64):
+            raise NotImplementedError(f'the decode graph uses the split-KV kernel (head dim 32 or 64), '
+                                      f'got head dim {cfg.head_dim}')
         self.splits = int(splits) if splits else _decode_splits(model, self.B, Hkv, self.cap)
         self.decs, self.lm = model.packed()
         self.lens = torch.tensor([self.start, self.start + 1], dtype=torch.int32, device=self.dev)
@@ -250,6 +253,27 @@ class GraphDecoder:
         for s in self.gdn:
             s.cache.length = self.start + self.taken
         return self.tokens[lo:self.taken].t()
+
+    def breakdown(self, first_ids: torch.Tensor):
+        """Run one step eagerly (outside the graph) with CUDA events around every launch and
+        return `{entry point or 'cublas_gemm': (calls, ms)}`; the states, positions and
+        step counter are put back afterwards, so the decoder is unchanged."""
+        snap = self._snapshot()
+        lens = self.lens.clone()
+        step_idx = self.step_idx.clone()
+        self.ids.copy_(first_ids.reshape(-1).to(self.dev, torch.int64))
+        tr = _lib.Tracker(timed=None)
+        torch.cuda.synchronize(self.dev)
+        _lib.set_tracker(tr)
+        try:
+            self._step()
+        finally:
+            _lib.set_tracker(None)
+        torch.cuda.synchronize(self.dev)
+        self._restore(snap)
+        self.lens.copy_(lens)
+        self.step_idx.copy_(step_idx)
+        return tr.summary()
 
     def release(self):
         """Free the graph (and its memory pool)."""

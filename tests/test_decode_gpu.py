@@ -17,7 +17,8 @@ from motif_b200.init import init_params
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
-SMALL = dict(vocab_size=512, model_dim=64, num_heads=4, num_kv_heads=2, head_k_dim=16,
+# head dim 32: the split-KV decode kernel serves head dims 32 and 64
+SMALL = dict(vocab_size=512, model_dim=128, num_heads=4, num_kv_heads=2, head_k_dim=16,
              block=('gdn', 'gdn', 'gdn', 'chord'), block_n=2)
 
 

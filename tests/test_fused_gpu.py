@@ -109,7 +109,7 @@ def test_gdn_prep(dtype, B, T, H, dk, dv, with_conv):
 
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize('B,H,dk,dv', [(3, 12, 64, 128), (2, 4, 16, 32)])
+@pytest.mark.parametrize('B,H,dk,dv', [(3, 12, 64, 128), (2, 4, 16, 32), (2, 3, 32, 64), (1, 2, 128, 256), (2, 2, 64, 64)])
 def test_gdn_decode(dtype, B, H, dk, dv):
     proj, conv_w, A_log, dt_bias, conv_in, C, _ = gdn_setup(B, 1, H, dk, dv, dtype, seed=B * H)
     g = torch.Generator().manual_seed(11)
@@ -163,7 +163,8 @@ def test_chord_prep(dtype, B, T, H, Hkv, D, pos):
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize('B,H,Hkv,T,S,D,splits', [(2, 12, 3, 1, 1000, 64, 7), (3, 4, 2, 2, 33, 32, 4),
-                                                  (1, 8, 8, 1, 5000, 64, 64), (2, 4, 1, 4, 300, 32, 1)])
+                                                  (1, 8, 8, 1, 5000, 64, 64), (2, 4, 1, 4, 300, 32, 1),
+                                                  (2, 8, 2, 2, 8448, 64, 12), (1, 12, 3, 1, 64, 64, 3)])
 def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits):
     g = torch.Generator().manual_seed(S + T)
     cap = S + 10
@@ -189,6 +190,7 @@ def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits):
               1e-5, splits, _lib.ptr(ws), ws_bytes, _lib.dtype_code(dtype), st())
     got = out.view(B, T, H, D).transpose(1, 2).float()
     assert rel_err(got, ref) < (1e-5 if dtype == torch.float32 else 1e-2), rel_err(got, ref)
+    assert _lib.decode_wait_timeouts() == 0
 
 
 def test_gate_residual_argmax_embed():
