@@ -343,6 +343,12 @@ __device__ __forceinline__ float ggd_bias_decode(float alpha, float beta, float 
 }
 
 constexpr int kDecTile = 64;
+// MOTIF_B200_DECODE_SCALAR=1 routes 16-bit D = 64 decode through the CUDA-core kernel (the
+// tensor-core kernel is the default); used to cross-check the two in tests.
+static bool force_scalar_decode() {
+  const char* e = getenv("MOTIF_B200_DECODE_SCALAR");
+  return e && e[0] == '1';
+}
 constexpr int kDecStages = 4;
 constexpr uint32_t kDecWaitLimit = 1u << 22;
 // Count of decode CTAs whose bulk-copy wait ran out (never expected; read and cleared by
@@ -426,8 +432,9 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
     bulk_load(&sm.k[s][0][0], kb + (int64_t)j0 * D, bytes, &sm.bar[s]);
     bulk_load(&sm.v[s][0][0], vb + (int64_t)j0 * D, bytes, &sm.bar[s]);
   };
+  int nissued = 0;  // tiles issued so far (meaningful in thread 0, the only issuer)
   if (threadIdx.x == 0)
-    for (int t = 0; t < min(ntile, kDecStages); ++t) issue(t);
+    for (; nissued < min(ntile, kDecStages); ++nissued) issue(nissued);
 
   // this lane's D/8 slice of every query row; the rows whose scores this lane finalises are
   // sub and sub + 8 (RO of them), with their log-n scaling, position and GGD parameters
@@ -558,13 +565,14 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
     if (threadIdx.x == 0 && t + kDecStages < ntile) {
       fence_proxy_async_smem();
       issue(t + kDecStages);
+      ++nissued;
     }
   }
   if (failed) {
     // record, then let the copies already issued land (bounded) before the CTA exits
     if (threadIdx.x == 0) {
       atomicAdd(&g_decode_wait_timeouts, 1u);
-      for (int u = t; u < min(ntile, t + kDecStages); ++u)
+      for (int u = t; u < nissued; ++u)
         mbar_wait_bounded(&sm.bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit);
     }
     __syncthreads();
@@ -587,6 +595,237 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
     for (int d = 0; d < OD; ++d) dst[lane * OD + d] = o[i][d];
     if (lane == 0) {
       dst[D] = m[i];
+      dst[D + 1] = lt;
+    }
+  }
+}
+
+// Tensor-core variant for 16-bit caches with D = 64.  The MMA rows are the R <= 16 query
+// rows; K and V tiles arrive by tiled tensor copies with the 128-byte swizzle (16-byte
+// chunk c of key row r lands at chunk c ^ (r & 7)), which makes the K fragment loads and the
+// transposed V ldmatrix below bank-conflict free.  Warp w takes keys 16w .. 16w+15 of every
+// tile (QKᵀ: 2 x 4 m16n8k16, PV: 8 m16n8k16) and keeps its own online-softmax state; the
+// four warps' states are combined through shared memory at the end.  The barrier at the top
+// of each tile also tells thread 0 that the previous tile's stage is free to refill.
+template <typename T>
+__global__ void __launch_bounds__(128) chord_decode_mma_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const T* __restrict__ q,
+    int64_t cap, const int32_t* __restrict__ len_dev, int len_host, const float* __restrict__ alpha,
+    const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
+    float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps) {
+  constexpr int D = 64;
+  constexpr int TILE_BYTES = kDecTile * D * 2;  // 8 KB, rows of 128 bytes
+  extern __shared__ unsigned char dec_mma_smem[];
+  unsigned char* base = dec_mma_smem + ((1024u - (smem_u32(dec_mma_smem) & 1023u)) & 1023u);
+  unsigned char* sK = base;
+  unsigned char* sV = base + kDecStages * TILE_BYTES;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 2 * kDecStages * TILE_BYTES);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int split = blockIdx.x;
+  const int bk = blockIdx.y;
+  const int b = bk / Hkv, kvh = bk % Hkv;
+  const int G = H / Hkv;
+  const int R = G * Tn;
+  const int S = len_dev ? min(max(*len_dev, Tn), (int)cap) : len_host;
+  const int q_start = S - Tn;
+  const int per = ((S + nsplit - 1) / nsplit + kDecTile - 1) / kDecTile * kDecTile;
+  const int kbeg = min(S, split * per), kend = min(S, kbeg + per);
+  const int ntile = (kend - kbeg + kDecTile - 1) / kDecTile;
+  const int row0 = bk * (int)cap;  // tensor row of this (b, kv head)'s key 0 (host: B*Hkv*cap < 2^31)
+
+  if (tid == 0) {
+    for (int s = 0; s < kDecStages; ++s) mbar_init(&bar[s], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  auto issue = [&](int t) {
+    const int s = t % kDecStages;
+    const int y = row0 + kbeg + t * kDecTile;
+    mbar_arrive_expect_tx(&bar[s], 2 * TILE_BYTES);
+    tma_load_2d(sK + s * TILE_BYTES, &tmK, 0, y, &bar[s]);
+    tma_load_2d(sV + s * TILE_BYTES, &tmV, 0, y, &bar[s]);
+  };
+  int nissued = 0;  // tiles issued so far (meaningful in thread 0, the only issuer)
+  if (tid == 0)
+    for (; nissued < min(ntile, kDecStages); ++nissued) issue(nissued);
+
+  // rows g8 and g8 + 8 of the MMA tile
+  bool rv[2];
+  int rqa[2];
+  float rrc[2], ral[2], rbe[2], rmu[2];
+  uint32_t qf[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) qf[kk][0] = qf[kk][1] = qf[kk][2] = qf[kk][3] = 0u;
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) {
+    const int r = g8 + 8 * ri;
+    rv[ri] = r < R;
+    rqa[ri] = -1;
+    rrc[ri] = ral[ri] = rbe[ri] = rmu[ri] = 0.f;
+    if (rv[ri]) {
+      const int h = kvh * G + r / Tn, t = r % Tn;
+      rqa[ri] = q_start + t;
+      rrc[ri] = ssmax[h] * logf((float)(rqa[ri] + 1)) * kLog2e;
+      ral[ri] = alpha[h];
+      rbe[ri] = beta[h];
+      rmu[ri] = mu[h];
+      const uint32_t* qw = reinterpret_cast<const uint32_t*>(q + (((int64_t)b * Tn + t) * H + h) * D);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        qf[kk][ri] = qw[kk * 8 + t4];
+        qf[kk][2 + ri] = qw[kk * 8 + 4 + t4];
+      }
+    }
+  }
+
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+
+  int t = 0;
+  bool failed = false;
+  for (; t < ntile; ++t) {
+    const int s = t % kDecStages;
+    const bool ok = mbar_wait_bounded(&bar[s], (uint32_t)((t / kDecStages) & 1), kDecWaitLimit);
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+    if (tid == 0 && t >= 1 && t - 1 + kDecStages < ntile) {
+      fence_proxy_async_smem();
+      issue(t - 1 + kDecStages);  // refills the stage tile t - 1 used; every warp is past it
+      ++nissued;
+    }
+    const int j0 = kbeg + t * kDecTile;
+    const int nk = min(kDecTile, kend - j0);
+    // S = Q Kᵀ over this warp's 16 keys
+    float sacc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+    const uint32_t* Kw = reinterpret_cast<const uint32_t*>(sK + s * TILE_BYTES);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int kr = warp * 16 + nt * 8 + g8;
+      const uint32_t* krow = Kw + kr * 32;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t bb[2];
+        bb[0] = krow[(((2 * kk) ^ (kr & 7)) << 2) + t4];
+        bb[1] = krow[(((2 * kk + 1) ^ (kr & 7)) << 2) + t4];
+        mma_16816<T>(sacc[nt], qf[kk], bb);
+      }
+    }
+    // logits in log2 units with the GGD bias, masking, online softmax
+    float rmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ri = e >> 1;
+        const int kl = warp * 16 + nt * 8 + 2 * t4 + (e & 1);
+        const int j = j0 + kl;
+        float x = -INFINITY;
+        if (rv[ri] && kl < nk && j <= rqa[ri])
+          x = (sacc[nt][e] * scale + ggd_bias_decode<T>(ral[ri], rbe[ri], rmu[ri], (float)(rqa[ri] - j), eps)) *
+              rrc[ri];
+        sacc[nt][e] = x;
+        rmax[ri] = fmaxf(rmax[ri], x);
+      }
+    }
+    float mb[2];
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      rmax[ri] = fmaxf(rmax[ri], __shfl_xor_sync(0xffffffffu, rmax[ri], 1));
+      rmax[ri] = fmaxf(rmax[ri], __shfl_xor_sync(0xffffffffu, rmax[ri], 2));
+      const float mn = fmaxf(m[ri], rmax[ri]);
+      mb[ri] = mn == -INFINITY ? 0.f : mn;
+      const float corr = exp2f(m[ri] - mb[ri]);
+      m[ri] = mn;
+      l[ri] *= corr;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][2 * ri] *= corr;
+        o[i][2 * ri + 1] *= corr;
+      }
+    }
+    uint32_t pa[4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = exp2f(sacc[nt][0] - mb[0]), p1 = exp2f(sacc[nt][1] - mb[0]);
+      const float p2 = exp2f(sacc[nt][2] - mb[1]), p3 = exp2f(sacc[nt][3] - mb[1]);
+      l[0] += p0 + p1;
+      l[1] += p2 + p3;
+      pa[2 * nt] = pack2<T>(p0, p1);
+      pa[2 * nt + 1] = pack2<T>(p2, p3);
+    }
+    // O += P V over the same 16 keys (V rows 16w .. 16w+15, transposed by ldmatrix)
+    const int vr = warp * 16 + (lane & 15);
+    const unsigned char* vrow = sV + s * TILE_BYTES + vr * 128;
+#pragma unroll
+    for (int n0 = 0; n0 < D; n0 += 16) {
+      uint32_t vb4[4];
+      const int chunk = n0 / 8 + (lane >> 4);
+      ldmatrix_x4_trans(vb4, vrow + ((chunk ^ (vr & 7)) << 4));
+      mma_16816<T>(o[n0 / 8], pa, &vb4[0]);
+      mma_16816<T>(o[n0 / 8 + 1], pa, &vb4[2]);
+    }
+  }
+  __syncthreads();  // all tiles consumed (every issued copy was waited on): reuse the K stages
+  float* sM = reinterpret_cast<float*>(sK);  // [4][16]
+  float* sL = sM + 64;                       // [4][16]
+  float* sO = sL + 64;                       // [4][16][64]
+  if (failed) {
+    if (tid == 0) {
+      atomicAdd(&g_decode_wait_timeouts, 1u);
+      for (int u = t; u < nissued; ++u)
+        mbar_wait_bounded(&bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      m[ri] = -INFINITY;
+      l[ri] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  }
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) {
+    l[ri] += __shfl_xor_sync(0xffffffffu, l[ri], 1);
+    l[ri] += __shfl_xor_sync(0xffffffffu, l[ri], 2);
+    const int r = g8 + 8 * ri;
+    if (t4 == 0) {
+      sM[warp * 16 + r] = m[ri];
+      sL[warp * 16 + r] = l[ri];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sO[(warp * 16 + r) * D + i * 8 + 2 * t4] = o[i][2 * ri];
+      sO[(warp * 16 + r) * D + i * 8 + 2 * t4 + 1] = o[i][2 * ri + 1];
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < R * D; idx += 128) {
+    const int r = idx / D, d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sM[w * 16 + r]);
+    const float Mb = M == -INFINITY ? 0.f : M;
+    float val = 0.f, lt = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float f = exp2f(sM[w * 16 + r] - Mb);
+      val = fmaf(sO[(w * 16 + r) * D + d], f, val);
+      lt = fmaf(sL[w * 16 + r], f, lt);
+    }
+    const int h = kvh * G + r / Tn, tt = r % Tn;
+    float* dst = ws + ((((int64_t)split * B + b) * H + h) * Tn + tt) * (D + 2);
+    dst[d] = val;
+    if (d == 0) {
+      dst[D] = M;
       dst[D + 1] = lt;
     }
   }
@@ -808,6 +1047,32 @@ extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const
       constexpr int DD = decltype(dc)::value;
       dim3 grid((unsigned)max_splits, (unsigned)(B * Hkv));
       const int R = (int)((H / Hkv) * T);
+      if constexpr (sizeof(Tt) == 2 && DD == 64) {
+        if (B * Hkv * cap < (1LL << 31) && (uintptr_t)q % 4 == 0 && !force_scalar_decode()) {
+          CUtensorMap tmK, tmV;
+          const uint64_t rows = (uint64_t)(B * Hkv * cap);
+          int rc = encode_tile_map_2d(&tmK, k_cache, 2, DD, rows, DD * 2, DD, kDecTile, 128);
+          if (!rc) rc = encode_tile_map_2d(&tmV, v_cache, 2, DD, rows, DD * 2, DD, kDecTile, 128);
+          if (rc) return rc;
+          auto kern = chord_decode_mma_kernel<Tt>;
+          const int smem = 2 * kDecStages * kDecTile * DD * 2 + kDecStages * 8 + 1024;
+          static bool attr_set[64] = {};
+          int dev = 0;
+          cudaGetDevice(&dev);
+          if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+              return check_launch("chord_decode (shared memory attribute)");
+            if (dev >= 0 && dev < 64) attr_set[dev] = true;
+          }
+          kern<<<grid, 128, smem, st>>>(tmK, tmV, (const Tt*)q, cap, len_dev, (int)len_host, alpha, beta, mu, ssmax,
+                                        (float*)workspace, (int)B, (int)H, (int)Hkv, (int)T, max_splits, scale, eps);
+          rc = check_launch("chord_decode");
+          if (rc) return rc;
+          chord_merge_kernel<Tt, DD><<<(unsigned)((B * T * H + 3) / 4), 128, 0, st>>>(
+              (const float*)workspace, (Tt*)out, out_stride, (int)B, (int)H, (int)T, max_splits);
+          return check_launch("chord_merge");
+        }
+      }
       auto launch = [&](auto rmc) {
         constexpr int RM = decltype(rmc)::value;
         auto kern = chord_decode_kernel<Tt, DD, RM>;

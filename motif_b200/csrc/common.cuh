@@ -1,6 +1,7 @@
 // Shared device helpers for the Motif Chord sm_100a kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -14,6 +15,10 @@ namespace mb {
 // Records a message for motif_b200_last_error() and returns the code.
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
+// 2-D tiled tensor map over a row-major [rows, inner] array (16-bit elements are encoded as
+// bf16: the bulk tensor copy only moves bytes, so fp16 data is carried unchanged).
+int encode_tile_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes);
 
 #define MB_REQUIRE(cond, code, ...)                  \
   do {                                               \
@@ -156,6 +161,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+// Tiled tensor copy of one box at coordinates (x = inner element index, y = row); x * element
+// size must be a multiple of 16 bytes.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;

@@ -164,8 +164,15 @@ def test_chord_prep(dtype, B, T, H, Hkv, D, pos):
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize('B,H,Hkv,T,S,D,splits', [(2, 12, 3, 1, 1000, 64, 7), (3, 4, 2, 2, 33, 32, 4),
                                                   (1, 8, 8, 1, 5000, 64, 64), (2, 4, 1, 4, 300, 32, 1),
-                                                  (2, 8, 2, 2, 8448, 64, 12), (1, 12, 3, 1, 64, 64, 3)])
-def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits):
+                                                  (2, 8, 2, 2, 8448, 64, 12), (1, 12, 3, 1, 64, 64, 3),
+                                                  (1, 16, 2, 2, 777, 64, 5)])
+@pytest.mark.parametrize('scalar', [False, True])
+def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, monkeypatch):
+    # 16-bit D = 64 runs the tensor-core kernel unless MOTIF_B200_DECODE_SCALAR=1
+    if scalar:
+        if dtype == torch.float32 or D != 64:
+            pytest.skip('the CUDA-core kernel is the only path for this case')
+        monkeypatch.setenv('MOTIF_B200_DECODE_SCALAR', '1')
     g = torch.Generator().manual_seed(S + T)
     cap = S + 10
     q = torch.randn(B, T, H, D, generator=g).to(dtype)
