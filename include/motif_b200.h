@@ -228,11 +228,13 @@ MB_API int motif_b200_chord_decode_noalloc(const void* q, const void* k_cache, c
                                     float softmax_scale, float eps, int max_splits, int dtype,
                                     void* stream);
 
-/* Number of decode attention CTAs (motif_b200_chord_decode / _noalloc) whose bounded wait
- * for a bulk copy ran out since the last call (each such CTA writes an empty partial, so
- * its split contributes nothing); the counter is cleared.  Synchronous (copies from device
- * memory).  Expected to stay 0.  No counterpart in the reference. */
-MB_API int motif_b200_decode_wait_timeouts(uint32_t* count);
+/* Number of Chord attention CTAs (decode: motif_b200_chord_decode / _noalloc; tensor-core
+ * prefill: motif_b200_chord_attention) whose bounded wait for a tensor copy or an MMA ran out
+ * since the last call; such a CTA abandons its work (a decode split contributes nothing, a
+ * prefill tile's rows are left unwritten) instead of hanging.  The counter is cleared.
+ * Synchronous (copies from device memory).  Expected to stay 0.  No counterpart in the
+ * reference. */
+MB_API int motif_b200_wait_timeouts(uint32_t* count);
 
 /* out = a * sigmoid(gate) + m over [rows, N] (row strides given).
  * Replaces chord_attn.py:254,313 (o_proj(out) * G) + decoder.py:208 (attn + mlp). */

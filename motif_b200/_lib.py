@@ -56,7 +56,7 @@ SIGNATURES = {
     'motif_b200_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
     'motif_b200_argmax': (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
     'motif_b200_embed': (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
-    'motif_b200_decode_wait_timeouts': (_I, [_P]),
+    'motif_b200_wait_timeouts': (_I, [_P]),
 }
 
 _lock = threading.Lock()
@@ -181,8 +181,8 @@ def call(name: str, *args) -> None:
         raise RuntimeError(f'{name}: {msg}')
 
 
-def decode_wait_timeouts() -> int:
-    """Decode-attention CTAs whose bulk-copy wait ran out since the last call (clears it)."""
+def wait_timeouts() -> int:
+    """Chord-attention CTAs whose bounded copy / MMA wait ran out since the last call (clears it)."""
     n = ctypes.c_uint32(0)
-    call('motif_b200_decode_wait_timeouts', ctypes.addressof(n))
+    call('motif_b200_wait_timeouts', ctypes.addressof(n))
     return int(n.value)

@@ -30,8 +30,8 @@ int check_launch(const char* what) {
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 static std::once_flag g_encode_once;
 
-int encode_tile_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
-                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes) {
+int encode_tile_map(CUtensorMap* map, const void* base, int elem_bytes, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -45,15 +45,28 @@ int encode_tile_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
                           : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                           : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                 : CU_TENSOR_MAP_SWIZZLE_NONE;
-  const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {row_stride_bytes};
-  const cuuint32_t box[2] = {box_inner, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode_tiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+  if (rank < 1 || rank > 5) return set_error(MB_ERR_ARG, "tensor map rank %d", rank);
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    estr[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = g_encode_tiled(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(MB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return MB_OK;
+}
+
+int encode_tile_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes) {
+  const uint64_t dims[2] = {inner, rows};
+  const uint64_t strides[1] = {row_stride_bytes};
+  const uint32_t box[2] = {box_inner, box_rows};
+  return encode_tile_map(map, base, elem_bytes, 2, dims, strides, box, swizzle_bytes);
 }
 
 }  // namespace mb

@@ -16,6 +16,7 @@
 //     position); one warp per (b, kv head, split) serves all G query heads of the group.
 //   * chord_prep — per-head RMSNorm of q and k and the append of k, v into the cache.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -23,6 +24,10 @@ namespace mb {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
+
+// Count of Chord attention CTAs whose bounded copy / MMA wait ran out (never expected; read
+// and cleared by motif_b200_wait_timeouts).
+__device__ unsigned int g_wait_timeouts = 0;
 
 struct Strides14 {
   int64_t s[14];  // q(b,h,l) k(b,h,s) v(b,h,s) out(b,h,l) log_n(b,l)
@@ -248,6 +253,291 @@ __global__ void __launch_bounds__(128) chord_fwd_mma_kernel(
   }
 }
 
+// ------------------------------------------------------------------ tcgen05 prefill (16-bit, D = 64)
+// One CTA = 128 query rows = G heads of one GQA group x 128/G positions (row r <-> position
+// t0 + r / G, head h0 + r % G), sharing every K/V tile.  Four warps; thread r owns row r,
+// which is TMEM lane r of both accumulators.
+//   loads   Q once and 128-key K/V tiles (two stages) by tiled TMA with the 128-byte swizzle;
+//   S = Q Kᵀ  tcgen05.mma M=128 N=128 K=64 (4 x K16) into one of two TMEM S buffers, issued
+//           one tile ahead, so it runs while the rows work on the previous tile;
+//   softmax each thread reads its row of S (tcgen05.ld), applies scale, the GGD bias (from a
+//           per-tile table over the 128/G + 127 distances the tile spans, per head), the
+//           causal / length mask and log-n scaling, updates its online max / sum, and writes
+//           P (bf16 / fp16) into shared memory in the swizzled K-major layout;
+//   O_t = P V tcgen05.mma M=128 N=64 K=128 (8 x K16) into TMEM; the rows read it back and
+//           accumulate o = o * corr + O_t in registers (no TMEM rescaling).
+// Thread 0 issues every copy and MMA; MMA completion reaches the rows through
+// tcgen05.commit on mbarriers.  All waits are bounded: a CTA whose wait runs out records it in
+// g_wait_timeouts, drains what it issued, frees its TMEM and leaves its rows unwritten.
+namespace tc {
+constexpr int kRows = 128, kKeys = 128, kD = 64;
+constexpr int kTileBytes = kRows * kD * 2;  // 16 KB: 128 rows of 128 bytes
+constexpr uint32_t kWait = 1u << 22;
+constexpr uint32_t kTmemCols = 512;  // S: 2 x 128, O_t: 64
+constexpr uint32_t kColS = 0, kColO = 256;
+}  // namespace tc
+
+template <int G>
+struct TcSmemLayout {
+  static constexpr int BMQ = 128 / G;
+  static constexpr int TBL = BMQ + 127;               // distances one tile spans per head
+  static constexpr int TBLS = (TBL + 31) / 32 * 32 + 8;  // padded: the G tables start on distinct banks
+  static constexpr int offQ = 0;
+  static constexpr int offK = offQ + tc::kTileBytes;        // 2 stages
+  static constexpr int offV = offK + 2 * tc::kTileBytes;    // 2 stages
+  static constexpr int offP = offV + 2 * tc::kTileBytes;    // 2 swizzle atoms of 64 keys
+  static constexpr int offBias = offP + 2 * tc::kTileBytes;
+  static constexpr int offBar = offBias + 2 * G * TBLS * 4;
+  static constexpr int nBar = 7;  // q, kv[2], s[2], o, drain
+  static constexpr int offTmem = offBar + nBar * 8;
+  static constexpr int bytes = offTmem + 16;
+  static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
+};
+
+template <typename T, int G>
+__global__ void __launch_bounds__(128, 1) chord_tc_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmV, const float* __restrict__ alpha, const float* __restrict__ beta,
+    const float* __restrict__ mu, const float* __restrict__ ssmax, const float* __restrict__ log_n,
+    T* __restrict__ out, int H, int Hkv, int L, int S, int q_start, float scale, float eps, Strides14 sv) {
+  using Lay = TcSmemLayout<G>;
+  constexpr int BMQ = Lay::BMQ, TBL = Lay::TBL, TBLS = Lay::TBLS;
+  constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr uint32_t idS = umma_idesc_f16(ab_fmt, 128, tc::kKeys, 0, 0);
+  constexpr uint32_t idO = umma_idesc_f16(ab_fmt, 128, tc::kD, 0, 1);
+  extern __shared__ unsigned char tc_smem_raw[];
+  unsigned char* sm = tc_smem_raw + ((1024u - (smem_u32(tc_smem_raw) & 1023u)) & 1023u);
+  unsigned char* sQ = sm + Lay::offQ;
+  unsigned char* sK = sm + Lay::offK;
+  unsigned char* sV = sm + Lay::offV;
+  unsigned char* sP = sm + Lay::offP;
+  float* sBias = reinterpret_cast<float*>(sm + Lay::offBias);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Lay::offBar);
+  uint64_t *barQ = bar, *barKV = bar + 1, *barS = bar + 3, *barO = bar + 5, *barDrain = bar + 6;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + Lay::offTmem);
+
+  const int64_t* st = sv.s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int GS = H / Hkv;
+  const int groups_per_kv = GS / G;
+  const int kvh = blockIdx.y / groups_per_kv;
+  const int h0 = kvh * GS + (blockIdx.y % groups_per_kv) * G;
+  const int b = blockIdx.z;
+  const int t0 = (gridDim.x - 1 - blockIdx.x) * BMQ;  // longest rows first
+  const int last_pos = min(L, t0 + BMQ) - 1;
+  const int kv_end = min(S, q_start + last_pos + 1);
+  const int ntile = (kv_end + tc::kKeys - 1) / tc::kKeys;
+
+  // this thread's row
+  const int tl = tid / G, hg = tid % G;
+  const int pos = t0 + tl, h = h0 + hg;
+  const bool row_ok = pos < L;
+  const int qpos = q_start + pos;
+  const float rc = row_ok ? ssmax[h] * log_n[b * st[12] + (int64_t)pos * st[13]] * kLog2e : 0.f;
+
+  if (warp == 0) tmem_alloc(sTmem, tc::kTmemCols);
+  if (tid == 0) {
+    for (int i = 0; i < Lay::nBar; ++i) mbar_init(&bar[i], 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+
+  auto issue_kv = [&](int j) {  // thread 0
+    const int s = j & 1;
+    mbar_arrive_expect_tx(&barKV[s], 2 * tc::kTileBytes);
+    tma_load_4d(sK + s * tc::kTileBytes, &tmK, 0, j * tc::kKeys, kvh, b, &barKV[s]);
+    tma_load_4d(sV + s * tc::kTileBytes, &tmV, 0, j * tc::kKeys, kvh, b, &barKV[s]);
+  };
+  auto issue_s = [&](int j) {  // thread 0: S buffer j & 1 = Q K_jᵀ
+    const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + (j & 1) * tc::kTileBytes);
+#pragma unroll
+    for (int ks = 0; ks < tc::kD / 16; ++ks)
+      umma_f16_ss(tmem + tc::kColS + (j & 1) * tc::kKeys, umma_desc_sw128(qa + ks * 32, 16, 1024),
+                  umma_desc_sw128(ka + ks * 32, 16, 1024), idS, ks > 0);
+    umma_commit(&barS[j & 1]);
+  };
+  auto issue_o = [&](int j) {  // thread 0: O_t = P V_j
+    const uint32_t pa = smem_u32(sP), va = smem_u32(sV + (j & 1) * tc::kTileBytes);
+#pragma unroll
+    for (int ks = 0; ks < tc::kKeys / 16; ++ks)
+      umma_f16_ss(tmem + tc::kColO, umma_desc_sw128(pa + (ks >> 2) * tc::kTileBytes + (ks & 3) * 32, 16, 1024),
+                  umma_desc_sw128(va + ks * 16 * 128, tc::kTileBytes, 1024), idO, ks > 0);
+    umma_commit(barO);
+  };
+  auto fill_bias = [&](int j) {  // all threads: table of tile j into buffer j & 1
+    float* tb = sBias + (j & 1) * G * TBLS;
+    const int base = q_start + t0 - j * tc::kKeys - 127;  // distance of entry 0
+    for (int e = tid; e < G * TBL; e += 128) {
+      const int g = e / TBL, ee = e % TBL;
+      const int hh = h0 + g;
+      tb[g * TBLS + ee] = ggd_bias(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
+    }
+  };
+
+  int nissued = 0, nwaited = 0;  // K/V tiles issued / seen complete (thread 0)
+  bool q_waited = false;
+  if (tid == 0 && ntile > 0) {
+    mbar_arrive_expect_tx(barQ, tc::kTileBytes);
+    tma_load_4d(sQ, &tmQ, 0, h0, t0, b, barQ);
+    for (; nissued < min(ntile, 2); ++nissued) issue_kv(nissued);
+  }
+  if (ntile > 0) fill_bias(0);
+  __syncthreads();
+  bool failed = false;
+  if (tid == 0 && ntile > 0) {
+    q_waited = mbar_wait_bounded(barQ, 0, tc::kWait);
+    const bool ok = q_waited && mbar_wait_bounded(&barKV[0], 0, tc::kWait);
+    if (ok) {
+      nwaited = 1;
+      tc_fence_after();
+      issue_s(0);
+    } else {
+      failed = true;
+    }
+  }
+
+  float o[tc::kD];
+#pragma unroll
+  for (int i = 0; i < tc::kD; ++i) o[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+  int j = 0;
+  for (; j < ntile; ++j) {
+    const int sb = j & 1;
+    if (tid == 0 && !failed && j + 1 < ntile) {
+      if (mbar_wait_bounded(&barKV[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1), tc::kWait)) {
+        nwaited = j + 2;
+        tc_fence_after();
+        issue_s(j + 1);
+      } else {
+        failed = true;
+      }
+    }
+    if (j + 1 < ntile) fill_bias(j + 1);
+    bool ok = failed ? false : mbar_wait_bounded(&barS[sb], (uint32_t)((j >> 1) & 1), tc::kWait);
+    tc_fence_after();
+    // this row of S, scaled / biased / masked, in log2 units
+    float x[tc::kKeys];
+    {
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      const uint32_t ta = tmem + lane_base + tc::kColS + sb * tc::kKeys;
+      tmem_ld32(ta, r0);
+      tmem_ld32(ta + 32, r1);
+      tmem_ld32(ta + 64, r2);
+      tmem_ld32(ta + 96, r3);
+      tmem_wait_ld(r0);
+      tmem_wait_ld(r1);
+      tmem_wait_ld(r2);
+      tmem_wait_ld(r3);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        x[i] = __uint_as_float(r0[i]);
+        x[32 + i] = __uint_as_float(r1[i]);
+        x[64 + i] = __uint_as_float(r2[i]);
+        x[96 + i] = __uint_as_float(r3[i]);
+      }
+    }
+    const int k0 = j * tc::kKeys;
+    const float* tb = sBias + sb * G * TBLS + hg * TBLS + tl + 127;  // entry for key offset c: tb[-c]
+    const bool need_mask = (k0 + tc::kKeys > S) || (k0 + tc::kKeys - 1 > q_start + t0);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < tc::kKeys; ++c) {
+      float v = fmaf(x[c], scale, tb[-c]) * rc;
+      if (need_mask && (k0 + c >= S || k0 + c > qpos)) v = -INFINITY;
+      x[c] = v;
+      mx = fmaxf(mx, v);
+    }
+    const float mn = fmaxf(m, mx);
+    const float mb = mn == -INFINITY ? 0.f : mn;
+    const float corr = exp2f(m - mb);
+    m = mn;
+    float ps = 0.f;
+    // P row -> shared memory, swizzled: key chunk cc (8 keys) of row tid in atom cc / 8 at
+    // 16-byte slot (cc % 8) ^ (tid % 8)
+#pragma unroll
+    for (int cc = 0; cc < tc::kKeys / 8; ++cc) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p0 = exp2f(x[cc * 8 + 2 * e] - mb), p1 = exp2f(x[cc * 8 + 2 * e + 1] - mb);
+        ps += p0 + p1;
+        w[e] = pack2<T>(p0, p1);
+      }
+      unsigned char* dst = sP + (cc >> 3) * tc::kTileBytes + tid * 128 + (((cc & 7) ^ (tid & 7)) << 4);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    l = l * corr + ps;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+    if (tid == 0) {
+      tc_fence_after();
+      issue_o(j);
+    }
+    ok = mbar_wait_bounded(barO, (uint32_t)(j & 1), tc::kWait);
+    tc_fence_after();
+    {
+      uint32_t r0[32], r1[32];
+      const uint32_t ta = tmem + lane_base + tc::kColO;
+      tmem_ld32(ta, r0);
+      tmem_ld32(ta + 32, r1);
+      tmem_wait_ld(r0);
+      tmem_wait_ld(r1);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        o[i] = fmaf(o[i], corr, __uint_as_float(r0[i]));
+        o[32 + i] = fmaf(o[32 + i], corr, __uint_as_float(r1[i]));
+      }
+    }
+    tc_fence_before();
+    if (!ok) failed = true;  // reported at the next barrier
+    // K/V stage j & 1 is free (every MMA up to O_t(j) has completed): refill it
+    if (tid == 0 && !failed && nissued < ntile) {
+      issue_kv(nissued);
+      ++nissued;
+    }
+  }
+  // agree on failure (a wait that ran out after the last barrier)
+  failed = __syncthreads_or(failed);
+  if (failed) {
+    if (tid == 0) {
+      atomicAdd(&g_wait_timeouts, 1u);
+      // every MMA issued so far, then every K/V copy not yet consumed (bounded)
+      umma_commit(barDrain);
+      mbar_wait_bounded(barDrain, 0, tc::kWait);
+      if (ntile > 0 && !q_waited) mbar_wait_bounded(barQ, 0, tc::kWait);
+      for (int u = nwaited; u < nissued; ++u)
+        mbar_wait_bounded(&barKV[u & 1], (uint32_t)((u >> 1) & 1), tc::kWait);
+    }
+  } else if (row_ok) {
+    const float inv = 1.f / fmaxf(l, 1e-20f);
+    T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11];
+#pragma unroll
+    for (int c8 = 0; c8 < tc::kD / 8; ++c8) {
+      uint4 v;
+      v.x = pack2<T>(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+      v.y = pack2<T>(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+      v.z = pack2<T>(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+      v.w = pack2<T>(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+      *reinterpret_cast<uint4*>(orow + c8 * 8) = v;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tc::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ simple (fp32 / fallback)
 // One warp per (b, h, query row); lanes own keys in chunks of 32 and the D outputs in slices.
 template <typename T>
@@ -351,9 +641,6 @@ static bool force_scalar_decode() {
 }
 constexpr int kDecStages = 4;
 constexpr uint32_t kDecWaitLimit = 1u << 22;
-// Count of decode CTAs whose bulk-copy wait ran out (never expected; read and cleared by
-// motif_b200_decode_wait_timeouts).
-__device__ unsigned int g_decode_wait_timeouts = 0;
 
 template <typename T, int D, int RM>
 struct DecodeSmem {
@@ -571,7 +858,7 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
   if (failed) {
     // record, then let the copies already issued land (bounded) before the CTA exits
     if (threadIdx.x == 0) {
-      atomicAdd(&g_decode_wait_timeouts, 1u);
+      atomicAdd(&g_wait_timeouts, 1u);
       for (int u = t; u < nissued; ++u)
         mbar_wait_bounded(&sm.bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit);
     }
@@ -779,7 +1066,7 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
   float* sO = sL + 64;                       // [4][16][64]
   if (failed) {
     if (tid == 0) {
-      atomicAdd(&g_decode_wait_timeouts, 1u);
+      atomicAdd(&g_wait_timeouts, 1u);
       for (int u = t; u < nissued; ++u)
         mbar_wait_bounded(&bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit);
     }
@@ -974,6 +1261,65 @@ extern "C" int64_t motif_b200_chord_workspace_bytes(int64_t, int64_t, int64_t, i
   return 0;
 }
 
+// MOTIF_B200_CHORD_TC=0 keeps 16-bit D = 64 prefill on the mma.sync kernel (the tcgen05
+// kernel is the default); used to cross-check the two in tests.
+static bool chord_tc_disabled() {
+  const char* e = getenv("MOTIF_B200_CHORD_TC");
+  return e && e[0] == '0';
+}
+
+template <typename T, int G>
+int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha, const float* beta, const float* mu,
+                const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L,
+                int64_t S, int64_t q_start, float scale, float eps, const int64_t* strides, const Strides14& sv,
+                cudaStream_t st) {
+  using Lay = TcSmemLayout<G>;
+  CUtensorMap tmQ, tmK, tmV;
+  {
+    const uint64_t dims[4] = {64, (uint64_t)H, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)strides[1] * 2, (uint64_t)strides[2] * 2, (uint64_t)strides[0] * 2};
+    const uint32_t box[4] = {64, (uint32_t)G, (uint32_t)Lay::BMQ, 1};
+    int rc = encode_tile_map(&tmQ, q, 2, 4, dims, str, box, 128);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[4] = {64, (uint64_t)S, (uint64_t)Hkv, (uint64_t)B};
+    const uint32_t box[4] = {64, (uint32_t)tc::kKeys, 1, 1};
+    const uint64_t sk[3] = {(uint64_t)strides[5] * 2, (uint64_t)strides[4] * 2, (uint64_t)strides[3] * 2};
+    const uint64_t svv[3] = {(uint64_t)strides[8] * 2, (uint64_t)strides[7] * 2, (uint64_t)strides[6] * 2};
+    int rc = encode_tile_map(&tmK, k, 2, 4, dims, sk, box, 128);
+    if (!rc) rc = encode_tile_map(&tmV, v, 2, 4, dims, svv, box, 128);
+    if (rc) return rc;
+  }
+  auto kern = chord_tc_kernel<T, G>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::alloc) != cudaSuccess)
+      return check_launch("chord_attention (shared memory attribute)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int GS = (int)(H / Hkv);
+  dim3 grid((unsigned)((L + Lay::BMQ - 1) / Lay::BMQ), (unsigned)(Hkv * (GS / G)), (unsigned)B);
+  kern<<<grid, 128, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
+                                     (int)S, (int)q_start, scale, eps, sv);
+  return check_launch("chord_attention (tcgen05)");
+}
+
+template <typename T>
+int launch_tc(int G, const void* q, const void* k, const void* v, const float* alpha, const float* beta,
+              const float* mu, const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
+              int64_t L, int64_t S, int64_t q_start, float scale, float eps, const int64_t* strides,
+              const Strides14& sv, cudaStream_t st) {
+  switch (G) {
+    case 8: return launch_tc_g<T, 8>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
+    case 4: return launch_tc_g<T, 4>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
+    case 2: return launch_tc_g<T, 2>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
+    default: return launch_tc_g<T, 1>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
+  }
+}
+
 extern "C" int motif_b200_chord_attention(const void* q, const void* k, const void* v, const float* alpha,
                                           const float* beta, const float* mu, const float* ssmax, const float* log_n,
                                           void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L, int64_t S,
@@ -1005,9 +1351,16 @@ extern "C" int motif_b200_chord_attention(const void* q, const void* k, const vo
   aligned = aligned && (strides[9] % 2 == 0) && (strides[10] % 2 == 0) && (strides[11] % 2 == 0) &&
             ((uintptr_t)out % 4 == 0);
   const bool mma_ok = dtype != MB_F32 && aligned && (D == 16 || D == 32 || D == 64);
+  // tensor-core (tcgen05) path: 16-bit, D = 64, 16-byte aligned rows for the tensor maps and
+  // the row stores, key positions within the 32-bit tensor-map coordinate range
+  bool tc_ok = dtype != MB_F32 && D == 64 && ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) % 16 == 0;
+  for (int i = 0; i < 12; ++i) tc_ok = tc_ok && strides[i] % 8 == 0 && strides[i] > 0;
+  tc_ok = tc_ok && S >= 1 && S < (1LL << 31) && L < (1LL << 31) && !chord_tc_disabled();
   return dispatch_dtype(dtype, [&](auto t) {
     using T = decltype(t);
     if constexpr (sizeof(T) == 2) {
+      if (tc_ok) return launch_tc<T>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale,
+                                     eps, strides, sv, st);
       if (mma_ok)
         return launch_mma<T>(D, G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps,
                              sv, st);
@@ -1188,12 +1541,12 @@ extern "C" int motif_b200_chord_decode_noalloc(const void* q, const void* k_cach
                                  dtype, stream);
 }
 
-extern "C" int motif_b200_decode_wait_timeouts(uint32_t* count) {
-  MB_REQUIRE(count != nullptr, MB_ERR_ARG, "decode_wait_timeouts: null pointer");
+extern "C" int motif_b200_wait_timeouts(uint32_t* count) {
+  MB_REQUIRE(count != nullptr, MB_ERR_ARG, "wait_timeouts: null pointer");
   unsigned int v = 0, zero = 0;
-  if (cudaMemcpyFromSymbol(&v, g_decode_wait_timeouts, sizeof(v)) != cudaSuccess ||
-      cudaMemcpyToSymbol(g_decode_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
-    return set_error(MB_ERR_CUDA, "decode_wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
+  if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
+    return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
   *count = v;
   return MB_OK;
 }

@@ -197,7 +197,7 @@ def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, monkeypatch):
               1e-5, splits, _lib.ptr(ws), ws_bytes, _lib.dtype_code(dtype), st())
     got = out.view(B, T, H, D).transpose(1, 2).float()
     assert rel_err(got, ref) < (1e-5 if dtype == torch.float32 else 1e-2), rel_err(got, ref)
-    assert _lib.decode_wait_timeouts() == 0
+    assert _lib.wait_timeouts() == 0
 
 
 def test_gate_residual_argmax_embed():

@@ -172,13 +172,31 @@ def test_chord_fp32_vs_oracle(ops, B, H, Hkv, L, S, D):
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize('B,H,Hkv,L,S,D', [(1, 4, 4, 200, 200, 64), (2, 12, 3, 300, 300, 64),
                                            (1, 8, 1, 65, 100, 32), (2, 4, 2, 1, 513, 16),
-                                           (1, 16, 2, 129, 129, 64), (1, 12, 3, 1000, 1000, 64)])
+                                           (1, 16, 2, 129, 129, 64), (1, 12, 3, 1000, 1000, 64),
+                                           (2, 12, 3, 100, 350, 64), (1, 4, 2, 3, 5, 64), (3, 8, 4, 257, 600, 64),
+                                           (1, 2, 2, 128, 128, 64)])
 def test_chord_16bit_vs_oracle(ops, dtype, B, H, Hkv, L, S, D):
     q, k, v, alpha, beta, mu, ssmax, log_n, qs = chord_inputs(B, H, Hkv, L, S, D, seed=3 * L + S, dtype=dtype)
     ref = oo.chord_attention(q.float(), k.float(), v.float(), alpha, beta, mu, ssmax, log_n, qs)
     out = ops.apply_chord_attention(*cuda(q, k, v, alpha, beta, mu, ssmax, log_n))
     assert out.dtype == dtype
     assert rel_err(out.float(), ref) < 1e-2, rel_err(out.float(), ref)
+
+
+@pytest.mark.parametrize('B,H,Hkv,L,S', [(2, 12, 3, 300, 300), (1, 8, 8, 70, 500), (2, 16, 2, 200, 260)])
+def test_chord_tcgen05_matches_mma_sync(ops, monkeypatch, B, H, Hkv, L, S):
+    """16-bit D = 64 prefill: the tcgen05 kernel (default) against the mma.sync kernel."""
+    q, k, v, alpha, beta, mu, ssmax, log_n, qs = chord_inputs(B, H, Hkv, L, S, 64, seed=L + 7 * S,
+                                                              dtype=torch.bfloat16)
+    args = cuda(q, k, v, alpha, beta, mu, ssmax, log_n)
+    tc = ops.apply_chord_attention(*args)
+    monkeypatch.setenv('MOTIF_B200_CHORD_TC', '0')
+    ms = ops.apply_chord_attention(*args)
+    from motif_b200 import _lib
+    assert _lib.wait_timeouts() == 0
+    ref = oo.chord_attention(q.float(), k.float(), v.float(), alpha, beta, mu, ssmax, log_n, qs)
+    assert rel_err(tc.float(), ref) < 1e-2 and rel_err(ms.float(), ref) < 1e-2
+    assert rel_err(tc.float(), ms.float()) < 1e-2
 
 
 def test_chord_op_config_subset(ops):
