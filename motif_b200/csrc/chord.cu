@@ -254,54 +254,76 @@ __global__ void __launch_bounds__(128) chord_fwd_mma_kernel(
 }
 
 // ------------------------------------------------------------------ tcgen05 prefill (16-bit, D = 64)
-// One CTA = 128 query rows = G heads of one GQA group x 128/G positions (row r <-> position
-// t0 + r / G, head h0 + r % G), sharing every K/V tile.  Four warps; thread r owns row r,
-// which is TMEM lane r of both accumulators.
-//   loads   Q once and 128-key K/V tiles (two stages) by tiled TMA with the 128-byte swizzle;
-//   S = Q Kᵀ  tcgen05.mma M=128 N=128 K=64 (4 x K16) into one of two TMEM S buffers, issued
-//           one tile ahead, so it runs while the rows work on the previous tile;
-//   softmax each thread reads its row of S (tcgen05.ld), applies scale, the GGD bias (from a
-//           per-tile table over the 128/G + 127 distances the tile spans, per head), the
-//           causal / length mask and log-n scaling, updates its online max / sum, and writes
-//           P (bf16 / fp16) into shared memory in the swizzled K-major layout;
-//   O_t = P V tcgen05.mma M=128 N=64 K=128 (8 x K16) into TMEM; the rows read it back and
-//           accumulate o = o * corr + O_t in registers (no TMEM rescaling).
-// Thread 0 issues every copy and MMA; MMA completion reaches the rows through
-// tcgen05.commit on mbarriers.  All waits are bounded: a CTA whose wait runs out records it in
-// g_wait_timeouts, drains what it issued, frees its TMEM and leaves its rows unwritten.
+// One CTA = two warpgroups, each owning a tile of 128 query rows = G heads of one GQA group x
+// BMQ = 128/G positions (row r of warpgroup w <-> position t0 + w*BMQ + r / G, head
+// h0 + r % G; thread r of the warpgroup owns that row, which is TMEM lane r of its
+// accumulators).  Both tiles read the same 128-key K/V tiles, loaded once per CTA by tiled
+// TMA (128-byte swizzle) into a ring of kStages stages; each warpgroup runs its own loop and
+// the two interleave on the tensor core (while one does its softmax, the other's MMAs run).
+// Per warpgroup and key tile j:
+//   S = Q Kᵀ   tcgen05.mma M=128 N=128 K=64 into the warpgroup's S columns, issued for tile
+//              j+1 as soon as every row has read S(j), so it overlaps the softmax of tile j;
+//   softmax    each row reads its S (tcgen05.ld), applies scale, the GGD bias (per-tile table
+//              over the BMQ + 127 distances the tile spans, per head), mask and log-n scaling,
+//              updates its running max / sum and writes P (16-bit) into shared memory in the
+//              swizzled K-major layout;
+//   O_t = P V  tcgen05.mma M=128 N=64 K=128; the rows read it back and accumulate
+//              o = o * corr + O_t in registers.
+// The warpgroup's first thread issues its MMAs; a K/V stage is refilled by whichever
+// warpgroup finishes with it last.  All waits are bounded: a CTA whose wait runs out counts
+// itself in g_wait_timeouts, drains what it issued, frees its TMEM and leaves its rows
+// unwritten.
 namespace tc {
-constexpr int kRows = 128, kKeys = 128, kD = 64;
-constexpr int kTileBytes = kRows * kD * 2;  // 16 KB: 128 rows of 128 bytes
+constexpr int kKeys = 128, kD = 64;
+constexpr int kTileBytes = 128 * kD * 2;  // 16 KB: 128 rows of 128 bytes
+constexpr int kStages = 3;
 constexpr uint32_t kWait = 1u << 22;
-constexpr uint32_t kTmemCols = 512;  // S: 2 x 128, O_t: 64
-constexpr uint32_t kColS = 0, kColO = 256;
+constexpr uint32_t kTmemCols = 512;  // S: 2 x 128 columns, O: 2 x 64
 }  // namespace tc
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+// Barrier over the 128 threads of one warpgroup (ids 1 and 2; 0 is __syncthreads).
+__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;\n" ::"r"(id) : "memory"); }
+__device__ __forceinline__ bool wg_sync_or(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred ip, op;\n setp.ne.u32 ip, %1, 0;\n bar.red.or.pred op, %2, 128, ip;\n selp.u32 %0, 1, 0, op;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id)
+      : "memory");
+  return r != 0;
+}
 
 template <int G>
 struct TcSmemLayout {
   static constexpr int BMQ = 128 / G;
-  static constexpr int TBL = BMQ + 127;               // distances one tile spans per head
+  static constexpr int TBL = BMQ + 127;                  // distances one tile spans per head
   static constexpr int TBLS = (TBL + 31) / 32 * 32 + 8;  // padded: the G tables start on distinct banks
-  static constexpr int offQ = 0;
-  static constexpr int offK = offQ + tc::kTileBytes;        // 2 stages
-  static constexpr int offV = offK + 2 * tc::kTileBytes;    // 2 stages
-  static constexpr int offP = offV + 2 * tc::kTileBytes;    // 2 swizzle atoms of 64 keys
-  static constexpr int offBias = offP + 2 * tc::kTileBytes;
-  static constexpr int offBar = offBias + 2 * G * TBLS * 4;
-  static constexpr int nBar = 7;  // q, kv[2], s[2], o, drain
-  static constexpr int offTmem = offBar + nBar * 8;
+  static constexpr int offQ = 0;                          // 2 warpgroup tiles
+  static constexpr int offK = offQ + 2 * tc::kTileBytes;  // kStages
+  static constexpr int offV = offK + tc::kStages * tc::kTileBytes;
+  static constexpr int offP = offV + tc::kStages * tc::kTileBytes;  // 2 warpgroups x 2 atoms of 64 keys
+  static constexpr int offBias = offP + 4 * tc::kTileBytes;         // 2 warpgroups x 2 tiles
+  static constexpr int offBar = offBias + 4 * G * TBLS * 4;
+  static constexpr int nBar = 1 + tc::kStages + 6;  // q, kv[], s[2], o[2], drain[2]
+  static constexpr int offCnt = offBar + nBar * 8;   // per-stage release count, last tile issued
+  static constexpr int offTmem = offCnt + 2 * tc::kStages * 4;
   static constexpr int bytes = offTmem + 16;
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
 
 template <typename T, int G>
-__global__ void __launch_bounds__(128, 1) chord_tc_kernel(
+__global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const float* __restrict__ alpha, const float* __restrict__ beta,
     const float* __restrict__ mu, const float* __restrict__ ssmax, const float* __restrict__ log_n,
     T* __restrict__ out, int H, int Hkv, int L, int S, int q_start, float scale, float eps, Strides14 sv) {
   using Lay = TcSmemLayout<G>;
-  constexpr int BMQ = Lay::BMQ, TBL = Lay::TBL, TBLS = Lay::TBLS;
+  constexpr int BMQ = Lay::BMQ, TBL = Lay::TBL, TBLS = Lay::TBLS, NS = tc::kStages;
   constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t idS = umma_idesc_f16(ab_fmt, 128, tc::kKeys, 0, 0);
   constexpr uint32_t idO = umma_idesc_f16(ab_fmt, 128, tc::kD, 0, 1);
@@ -310,88 +332,103 @@ __global__ void __launch_bounds__(128, 1) chord_tc_kernel(
   unsigned char* sQ = sm + Lay::offQ;
   unsigned char* sK = sm + Lay::offK;
   unsigned char* sV = sm + Lay::offV;
-  unsigned char* sP = sm + Lay::offP;
-  float* sBias = reinterpret_cast<float*>(sm + Lay::offBias);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Lay::offBar);
-  uint64_t *barQ = bar, *barKV = bar + 1, *barS = bar + 3, *barO = bar + 5, *barDrain = bar + 6;
+  uint64_t *barQ = bar, *barKV = bar + 1, *barS = bar + 1 + NS, *barO = bar + 3 + NS, *barDrain = bar + 5 + NS;
+  int* cnt = reinterpret_cast<int*>(sm + Lay::offCnt);  // [NS] releases, [NS] last tile issued
+  int* stage_tile = cnt + NS;
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + Lay::offTmem);
 
   const int64_t* st = sv.s;
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int wg = tid >> 7, wt = tid & 127;
+  const bool issuer = wt == 0;
   const int GS = H / Hkv;
   const int groups_per_kv = GS / G;
   const int kvh = blockIdx.y / groups_per_kv;
   const int h0 = kvh * GS + (blockIdx.y % groups_per_kv) * G;
   const int b = blockIdx.z;
-  const int t0 = (gridDim.x - 1 - blockIdx.x) * BMQ;  // longest rows first
-  const int last_pos = min(L, t0 + BMQ) - 1;
-  const int kv_end = min(S, q_start + last_pos + 1);
-  const int ntile = (kv_end + tc::kKeys - 1) / tc::kKeys;
+  const int tpair = (gridDim.x - 1 - blockIdx.x) * 2 * BMQ;  // longest rows first
+  auto tiles_from = [&](int t0x) {
+    if (t0x >= L) return 0;
+    const int kv_end = min(S, q_start + min(L, t0x + BMQ));
+    return (kv_end + tc::kKeys - 1) / tc::kKeys;
+  };
+  const int nA = tiles_from(tpair), nB = tiles_from(tpair + BMQ);
+  const int nall = max(nA, nB);
+  const int t0w = tpair + wg * BMQ;
+  const int nmine = wg ? nB : nA;
 
   // this thread's row
-  const int tl = tid / G, hg = tid % G;
-  const int pos = t0 + tl, h = h0 + hg;
+  const int tl = wt / G, hg = wt % G;
+  const int pos = t0w + tl, h = h0 + hg;
   const bool row_ok = pos < L;
   const int qpos = q_start + pos;
   const float rc = row_ok ? ssmax[h] * log_n[b * st[12] + (int64_t)pos * st[13]] * kLog2e : 0.f;
+  const float sr = scale * rc;
+
+  unsigned char* sQw = sQ + wg * tc::kTileBytes;
+  unsigned char* sPw = sm + Lay::offP + wg * 2 * tc::kTileBytes;
+  float* sBw = reinterpret_cast<float*>(sm + Lay::offBias) + wg * 2 * G * TBLS;
 
   if (warp == 0) tmem_alloc(sTmem, tc::kTmemCols);
   if (tid == 0) {
     for (int i = 0; i < Lay::nBar; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < NS; ++i) {
+      cnt[i] = 0;
+      stage_tile[i] = -1;
+    }
     mbar_init_fence();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sTmem;
+  const uint32_t colS = wg * tc::kKeys, colO = 2 * tc::kKeys + wg * tc::kD;
 
-  auto issue_kv = [&](int j) {  // thread 0
-    const int s = j & 1;
+  auto issue_kv = [&](int j) {  // one thread
+    const int s = j % NS;
+    stage_tile[s] = j;
     mbar_arrive_expect_tx(&barKV[s], 2 * tc::kTileBytes);
     tma_load_4d(sK + s * tc::kTileBytes, &tmK, 0, j * tc::kKeys, kvh, b, &barKV[s]);
     tma_load_4d(sV + s * tc::kTileBytes, &tmV, 0, j * tc::kKeys, kvh, b, &barKV[s]);
   };
-  auto issue_s = [&](int j) {  // thread 0: S buffer j & 1 = Q K_jᵀ
-    const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + (j & 1) * tc::kTileBytes);
+  auto issue_s = [&](int j) {  // warpgroup issuer: S = Q_w K_jᵀ
+    const uint32_t qa = smem_u32(sQw), ka = smem_u32(sK + (j % NS) * tc::kTileBytes);
 #pragma unroll
     for (int ks = 0; ks < tc::kD / 16; ++ks)
-      umma_f16_ss(tmem + tc::kColS + (j & 1) * tc::kKeys, umma_desc_sw128(qa + ks * 32, 16, 1024),
-                  umma_desc_sw128(ka + ks * 32, 16, 1024), idS, ks > 0);
-    umma_commit(&barS[j & 1]);
+      umma_f16_ss(tmem + colS, umma_desc_sw128(qa + ks * 32, 16, 1024), umma_desc_sw128(ka + ks * 32, 16, 1024),
+                  idS, ks > 0);
+    umma_commit(&barS[wg]);
   };
-  auto issue_o = [&](int j) {  // thread 0: O_t = P V_j
-    const uint32_t pa = smem_u32(sP), va = smem_u32(sV + (j & 1) * tc::kTileBytes);
+  auto issue_o = [&](int j) {  // warpgroup issuer: O_t = P_w V_j
+    const uint32_t pa = smem_u32(sPw), va = smem_u32(sV + (j % NS) * tc::kTileBytes);
 #pragma unroll
     for (int ks = 0; ks < tc::kKeys / 16; ++ks)
-      umma_f16_ss(tmem + tc::kColO, umma_desc_sw128(pa + (ks >> 2) * tc::kTileBytes + (ks & 3) * 32, 16, 1024),
+      umma_f16_ss(tmem + colO, umma_desc_sw128(pa + (ks >> 2) * tc::kTileBytes + (ks & 3) * 32, 16, 1024),
                   umma_desc_sw128(va + ks * 16 * 128, tc::kTileBytes, 1024), idO, ks > 0);
-    umma_commit(barO);
+    umma_commit(&barO[wg]);
   };
-  auto fill_bias = [&](int j) {  // all threads: table of tile j into buffer j & 1
-    float* tb = sBias + (j & 1) * G * TBLS;
-    const int base = q_start + t0 - j * tc::kKeys - 127;  // distance of entry 0
-    for (int e = tid; e < G * TBL; e += 128) {
+  auto fill_bias = [&](int j) {  // warpgroup: table of tile j into buffer j & 1
+    float* tb = sBw + (j & 1) * G * TBLS;
+    const int base = q_start + t0w - j * tc::kKeys - 127;  // distance of entry 0
+    for (int e = wt; e < G * TBL; e += 128) {
       const int g = e / TBL, ee = e % TBL;
       const int hh = h0 + g;
       tb[g * TBLS + ee] = ggd_bias(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
     }
   };
 
-  int nissued = 0, nwaited = 0;  // K/V tiles issued / seen complete (thread 0)
-  bool q_waited = false;
-  if (tid == 0 && ntile > 0) {
-    mbar_arrive_expect_tx(barQ, tc::kTileBytes);
-    tma_load_4d(sQ, &tmQ, 0, h0, t0, b, barQ);
-    for (; nissued < min(ntile, 2); ++nissued) issue_kv(nissued);
+  if (tid == 0 && nall > 0) {
+    mbar_arrive_expect_tx(barQ, 2 * tc::kTileBytes);
+    tma_load_4d(sQ, &tmQ, 0, h0, tpair, b, barQ);
+    tma_load_4d(sQ + tc::kTileBytes, &tmQ, 0, h0, tpair + BMQ, b, barQ);
+    for (int t = 0; t < min(nall, NS); ++t) issue_kv(t);
   }
-  if (ntile > 0) fill_bias(0);
+  if (nmine > 0) fill_bias(0);
   __syncthreads();
   bool failed = false;
-  if (tid == 0 && ntile > 0) {
-    q_waited = mbar_wait_bounded(barQ, 0, tc::kWait);
-    const bool ok = q_waited && mbar_wait_bounded(&barKV[0], 0, tc::kWait);
-    if (ok) {
-      nwaited = 1;
+  if (issuer && nmine > 0) {
+    if (mbar_wait_bounded(barQ, 0, tc::kWait) && mbar_wait_bounded(&barKV[0], 0, tc::kWait)) {
       tc_fence_after();
       issue_s(0);
     } else {
@@ -403,28 +440,15 @@ __global__ void __launch_bounds__(128, 1) chord_tc_kernel(
 #pragma unroll
   for (int i = 0; i < tc::kD; ++i) o[i] = 0.f;
   float m = -INFINITY, l = 0.f;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
 
-  int j = 0;
-  for (; j < ntile; ++j) {
-    const int sb = j & 1;
-    if (tid == 0 && !failed && j + 1 < ntile) {
-      if (mbar_wait_bounded(&barKV[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1), tc::kWait)) {
-        nwaited = j + 2;
-        tc_fence_after();
-        issue_s(j + 1);
-      } else {
-        failed = true;
-      }
-    }
-    if (j + 1 < ntile) fill_bias(j + 1);
-    bool ok = failed ? false : mbar_wait_bounded(&barS[sb], (uint32_t)((j >> 1) & 1), tc::kWait);
+  for (int j = 0; j < nmine; ++j) {
+    bool ok = failed ? false : mbar_wait_bounded(&barS[wg], (uint32_t)(j & 1), tc::kWait);
     tc_fence_after();
-    // this row of S, scaled / biased / masked, in log2 units
     float x[tc::kKeys];
     {
       uint32_t r0[32], r1[32], r2[32], r3[32];
-      const uint32_t ta = tmem + lane_base + tc::kColS + sb * tc::kKeys;
+      const uint32_t ta = tmem + lane_base + colS;
       tmem_ld32(ta, r0);
       tmem_ld32(ta + 32, r1);
       tmem_ld32(ta + 64, r2);
@@ -441,52 +465,65 @@ __global__ void __launch_bounds__(128, 1) chord_tc_kernel(
         x[96 + i] = __uint_as_float(r3[i]);
       }
     }
+    tc_fence_before();
+    wg_sync(1 + wg);  // every row holds S(j): the columns may take S(j + 1)
+    if (issuer && !failed && j + 1 < nmine) {
+      const int jn = j + 1;
+      if (mbar_wait_bounded(&barKV[jn % NS], (uint32_t)((jn / NS) & 1), tc::kWait)) {
+        tc_fence_after();
+        issue_s(jn);
+      } else {
+        failed = true;
+      }
+    }
+    if (j + 1 < nmine) fill_bias(j + 1);
+
+    // logits (log2 units): x = (s * scale + bias) * rc for keys c <= cmax, else -inf
     const int k0 = j * tc::kKeys;
-    const float* tb = sBias + sb * G * TBLS + hg * TBLS + tl + 127;  // entry for key offset c: tb[-c]
-    const bool need_mask = (k0 + tc::kKeys > S) || (k0 + tc::kKeys - 1 > q_start + t0);
-    float mx = -INFINITY;
+    const int cmax = min(127, min(S - 1 - k0, qpos - k0));
+    const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127;  // key offset c -> tb[-c]
+    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int c = 0; c < tc::kKeys; ++c) {
-      float v = fmaf(x[c], scale, tb[-c]) * rc;
-      if (need_mask && (k0 + c >= S || k0 + c > qpos)) v = -INFINITY;
-      x[c] = v;
-      mx = fmaxf(mx, v);
+      const float v = fmaf(x[c], sr, tb[-c] * rc);
+      x[c] = c <= cmax ? v : -INFINITY;
+      mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
     }
-    const float mn = fmaxf(m, mx);
+    const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
     const float mb = mn == -INFINITY ? 0.f : mn;
-    const float corr = exp2f(m - mb);
+    const float corr = ex2_approx(m - mb);
     m = mn;
-    float ps = 0.f;
-    // P row -> shared memory, swizzled: key chunk cc (8 keys) of row tid in atom cc / 8 at
-    // 16-byte slot (cc % 8) ^ (tid % 8)
+    float ps4[4] = {0.f, 0.f, 0.f, 0.f};
+    // P row -> shared memory, swizzled: key chunk cc (8 keys) in atom cc / 8 at 16-byte slot
+    // (cc % 8) ^ (row % 8)
 #pragma unroll
     for (int cc = 0; cc < tc::kKeys / 8; ++cc) {
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float p0 = exp2f(x[cc * 8 + 2 * e] - mb), p1 = exp2f(x[cc * 8 + 2 * e + 1] - mb);
-        ps += p0 + p1;
+        const float p0 = ex2_approx(x[cc * 8 + 2 * e] - mb), p1 = ex2_approx(x[cc * 8 + 2 * e + 1] - mb);
+        ps4[e] += p0 + p1;
         w[e] = pack2<T>(p0, p1);
       }
-      unsigned char* dst = sP + (cc >> 3) * tc::kTileBytes + tid * 128 + (((cc & 7) ^ (tid & 7)) << 4);
+      unsigned char* dst = sPw + (cc >> 3) * tc::kTileBytes + wt * 128 + (((cc & 7) ^ (wt & 7)) << 4);
       *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    l = l * corr + ps;
+    l = l * corr + ((ps4[0] + ps4[1]) + (ps4[2] + ps4[3]));
     fence_proxy_async_smem();
     tc_fence_before();
-    if (__syncthreads_or(!ok)) {
+    if (wg_sync_or(1 + wg, !ok || failed)) {
       failed = true;
       break;
     }
-    if (tid == 0) {
+    if (issuer) {
       tc_fence_after();
       issue_o(j);
     }
-    ok = mbar_wait_bounded(barO, (uint32_t)(j & 1), tc::kWait);
+    ok = mbar_wait_bounded(&barO[wg], (uint32_t)(j & 1), tc::kWait);
     tc_fence_after();
     {
       uint32_t r0[32], r1[32];
-      const uint32_t ta = tmem + lane_base + tc::kColO;
+      const uint32_t ta = tmem + lane_base + colO;
       tmem_ld32(ta, r0);
       tmem_ld32(ta + 32, r1);
       tmem_wait_ld(r0);
@@ -499,23 +536,33 @@ __global__ void __launch_bounds__(128, 1) chord_tc_kernel(
     }
     tc_fence_before();
     if (!ok) failed = true;  // reported at the next barrier
-    // K/V stage j & 1 is free (every MMA up to O_t(j) has completed): refill it
-    if (tid == 0 && !failed && nissued < ntile) {
-      issue_kv(nissued);
-      ++nissued;
+    // this warpgroup is done with stage j % NS (its MMAs up to O_t(j) have completed); the
+    // last of the warpgroups that use tile j refills the stage
+    if (issuer && !failed) {
+      const int s = j % NS;
+      const int need = (j < nA) + (j < nB);
+      __threadfence_block();
+      const int prev = atomicAdd(&cnt[s], 1);
+      __threadfence_block();
+      if (prev + 1 == need) {
+        cnt[s] = 0;
+        if (j + NS < nall) issue_kv(j + NS);
+      }
     }
   }
-  // agree on failure (a wait that ran out after the last barrier)
   failed = __syncthreads_or(failed);
   if (failed) {
-    if (tid == 0) {
+    if (issuer) {  // every MMA this warpgroup issued
+      umma_commit(&barDrain[wg]);
+      mbar_wait_bounded(&barDrain[wg], 0, tc::kWait);
+    }
+    __syncthreads();
+    if (tid == 0) {  // every copy issued (the latest into each stage is the only one pending)
       atomicAdd(&g_wait_timeouts, 1u);
-      // every MMA issued so far, then every K/V copy not yet consumed (bounded)
-      umma_commit(barDrain);
-      mbar_wait_bounded(barDrain, 0, tc::kWait);
-      if (ntile > 0 && !q_waited) mbar_wait_bounded(barQ, 0, tc::kWait);
-      for (int u = nwaited; u < nissued; ++u)
-        mbar_wait_bounded(&barKV[u & 1], (uint32_t)((u >> 1) & 1), tc::kWait);
+      if (nall > 0) mbar_wait_bounded(barQ, 0, tc::kWait);
+      for (int s = 0; s < NS; ++s)
+        if (stage_tile[s] >= 0)
+          mbar_wait_bounded(&barKV[s], (uint32_t)((stage_tile[s] / NS) & 1), tc::kWait);
     }
   } else if (row_ok) {
     const float inv = 1.f / fmaxf(l, 1e-20f);
@@ -1301,8 +1348,8 @@ int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha,
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int GS = (int)(H / Hkv);
-  dim3 grid((unsigned)((L + Lay::BMQ - 1) / Lay::BMQ), (unsigned)(Hkv * (GS / G)), (unsigned)B);
-  kern<<<grid, 128, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
+  dim3 grid((unsigned)((L + 2 * Lay::BMQ - 1) / (2 * Lay::BMQ)), (unsigned)(Hkv * (GS / G)), (unsigned)B);
+  kern<<<grid, 256, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
                                      (int)S, (int)q_start, scale, eps, sv);
   return check_launch("chord_attention (tcgen05)");
 }
