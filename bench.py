@@ -58,7 +58,7 @@ def kernel_work(name, cfg, B, T):
     dk, dv, D, hid, V = cfg.gdn_dk, cfg.gdn_dv, cfg.head_dim, cfg.mlp_hidden, cfg.vocab_size
     M = B * T
     C = 64
-    if name == 'motif_b200_gdn_chunk_gated':
+    if name in ('motif_b200_gdn_chunk_gated', 'motif_b200_gdn_chunk_gated_ws'):
         # per token per head: G1, QK, W (2*C*dk each), U (2*C*dv), WS, qS, K^T X (2*dk*dv each), Aq X (2*C*dv)
         f_tok = 3 * 2 * C * dk + 2 * 2 * C * dv + 3 * 2 * dk * dv
         by_tok = 2 * (2 * dk + dv) + 8 + 2 * dv + 2 * dv  # q,k,v in, beta+g, gate in, o out

@@ -83,6 +83,26 @@ MB_API int motif_b200_gdn_chunk_gated(const void* q, const void* k, const void* 
                                int64_t gate_head_stride, const void* onorm_w, float eps, int dtype,
                                void* stream);
 
+/* Workspace bytes motif_b200_gdn_chunk_gated_ws needs for its two-kernel path (16-bit dtypes,
+ * (Dk, Dv) in {(32,64), (64,64), (64,128)}); 0 when that path does not exist for the shape
+ * (the call then runs the single fused kernel and needs no workspace). */
+MB_API int64_t motif_b200_gdn_chunk_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                                             int dtype);
+
+/* motif_b200_gdn_chunk_gated (gate may be NULL: plain motif_b200_gdn_chunk) with a
+ * caller-provided device workspace of at least motif_b200_gdn_chunk_workspace_bytes bytes
+ * (16-byte aligned).  With it the state-independent part of every chunk (gamma, the UT
+ * transform W, U and the intra-chunk attention Aq) runs as one fully parallel kernel that
+ * writes to the workspace, and only X = U - W S, the output and the state update walk the
+ * chunks in order (motif/ops/gated_deltanet.py:137-177 + :287-321 split the same way).
+ * workspace == NULL runs the fused kernel.  Same results contract as motif_b200_gdn_chunk_gated. */
+MB_API int motif_b200_gdn_chunk_gated_ws(const void* q, const void* k, const void* v, const float* beta,
+                                  const float* g, const float* state_in, float* state_out, void* o,
+                                  int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                                  const int64_t* strides, const void* gate, int64_t gate_row_stride,
+                                  int64_t gate_head_stride, const void* onorm_w, float eps, int dtype,
+                                  void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ chord attention
  * Causal softmax attention with the gated geometric-decay bias
  *   logit(i,j) = (q_i.k_j * scale - alpha_h (|j - (q_start+i) - mu_h| + eps)^beta_h)

@@ -28,6 +28,12 @@ int gdn_chunk_fast_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, co
                             const float* beta, const float* g, const float* s_in, float* s_out, void* o, int64_t B,
                             int64_t H, int64_t L, const int64_t* strides, const void* gate, int64_t gate_rs,
                             int64_t gate_hs, const void* onorm_w, float eps, cudaStream_t st, int* rc);
+int64_t gdn_split_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv, int dtype);
+int gdn_split_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, const void* k, const void* v,
+                       const float* beta, const float* g, const float* s_in, float* s_out, void* o, int64_t B,
+                       int64_t H, int64_t L, const int64_t* strides, const void* gate, int64_t gate_rs,
+                       int64_t gate_hs, const void* onorm_w, float eps, void* ws, int64_t ws_bytes, cudaStream_t st,
+                       int* rc);
 
 namespace {
 
@@ -549,10 +555,18 @@ bool force_precise() {
   return v;
 }
 
+// MOTIF_B200_GDN_FUSED=1 keeps 16-bit calls that bring a workspace on the single fused kernel
+// (the two-kernel split is the default when a workspace is given); used to cross-check them.
+bool force_fused() {
+  const char* e = getenv("MOTIF_B200_GDN_FUSED");
+  return e && e[0] == '1';
+}
+
 int gdn_chunk_impl(const void* q, const void* k, const void* v, const float* beta, const float* g,
                    const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, int64_t Dk,
                    int64_t Dv, const int64_t* strides, int dtype, const void* gate, int64_t gate_rs,
-                   int64_t gate_hs, const void* onorm_w, float eps, void* stream) {
+                   int64_t gate_hs, const void* onorm_w, float eps, void* stream, void* ws = nullptr,
+                   int64_t ws_bytes = 0) {
   MB_REQUIRE(s_out && strides, MB_ERR_ARG, "gdn_chunk: null state_out/strides");
   MB_REQUIRE(L == 0 || (q && k && v && beta && g && o), MB_ERR_ARG, "gdn_chunk: null input");
   MB_REQUIRE(B >= 0 && H > 0 && L >= 0 && L < (1LL << 31) && B * H < (1LL << 31), MB_ERR_SHAPE,
@@ -567,6 +581,10 @@ int gdn_chunk_impl(const void* q, const void* k, const void* v, const float* bet
   if (B == 0) return MB_OK;
   cudaStream_t st = (cudaStream_t)stream;
   int rc = MB_OK;
+  if (!force_precise() && !force_fused() && ws &&
+      gdn_split_dispatch(dtype, Dk, Dv, q, k, v, beta, g, s_in, s_out, o, B, H, L, strides, gate, gate_rs, gate_hs,
+                         onorm_w, eps, ws, ws_bytes, st, &rc))
+    return rc;
   if (!force_precise() && gdn_chunk_fast_dispatch(dtype, Dk, Dv, q, k, v, beta, g, s_in, s_out, o, B, H, L, strides,
                                                   gate, gate_rs, gate_hs, onorm_w, eps, st, &rc))
     return rc;
@@ -607,4 +625,24 @@ extern "C" int motif_b200_gdn_chunk_gated(const void* q, const void* k, const vo
   MB_REQUIRE(gate && onorm_w, MB_ERR_ARG, "gdn_chunk_gated: null gate / weight");
   return mb::gdn_chunk_impl(q, k, v, beta, g, state_in, state_out, o, B, H, L, Dk, Dv, strides, dtype, gate,
                             gate_row_stride, gate_head_stride, onorm_w, eps, stream);
+}
+
+extern "C" int64_t motif_b200_gdn_chunk_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                                                        int dtype) {
+  if (B < 0 || H <= 0 || L < 0) return 0;
+  return mb::gdn_split_workspace_bytes(B, H, L, Dk, Dv, dtype);
+}
+
+extern "C" int motif_b200_gdn_chunk_gated_ws(const void* q, const void* k, const void* v, const float* beta,
+                                             const float* g, const float* state_in, float* state_out, void* o,
+                                             int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv,
+                                             const int64_t* strides, const void* gate, int64_t gate_row_stride,
+                                             int64_t gate_head_stride, const void* onorm_w, float eps, int dtype,
+                                             void* workspace, int64_t workspace_bytes, void* stream) {
+  MB_REQUIRE(gate == nullptr || onorm_w != nullptr, MB_ERR_ARG, "gdn_chunk_gated_ws: gate without weight");
+  MB_REQUIRE(workspace == nullptr ||
+                 workspace_bytes >= mb::gdn_split_workspace_bytes(B, H, L, Dk, Dv, dtype),
+             MB_ERR_ARG, "gdn_chunk_gated_ws: workspace too small");
+  return mb::gdn_chunk_impl(q, k, v, beta, g, state_in, state_out, o, B, H, L, Dk, Dv, strides, dtype, gate,
+                            gate_row_stride, gate_head_stride, onorm_w, eps, stream, workspace, workspace_bytes);
 }

@@ -1,0 +1,660 @@
+// Chunked gated delta rule for 16-bit inputs as two kernels, so that only the part of the
+// chunk computation that depends on the recurrent state S runs sequentially.
+//
+// motif/ops/gated_deltanet.py:137-177 (_PrepareChunksFunction) and :287-321 split the chunk
+// math the same way: everything built from one chunk's q, k, v, beta, g alone (the UT
+// transform) is independent of the state; only X = U - W S, the output and the state update
+// walk the chunks in order.
+//
+//   gdn_wy_kernel   grid (chunks, B*H), fully parallel.  Per chunk: gamma = cumsum(g),
+//                   A = -(beta_i k_i.k_j e^{gamma_i - gamma_j}) (j < i), the 16x16 diagonal
+//                   inverses of (I - A) and the blocked forward substitution
+//                   [W | U] = (I - A)^-1 [k beta e^gamma | v beta]; Aq = (q k^T)_ij
+//                   e^{gamma_i - gamma_j} (j <= i).  Writes W, U, Aq (input dtype) and gamma
+//                   (fp32) to the workspace.
+//   gdn_rec_kernel  grid B*H, one CTA per (b, h) walking its chunks with S resident in fp32
+//                   registers; W, U, Aq, gamma, q, k and the gate tile of chunk n+1 stream in
+//                   (cp.async) while chunk n computes X = U - W S, o = e^gamma (q S) + Aq X,
+//                   the GatedRMSNorm epilogue, and S = e^{gamma_L} S + k^T (e^{gamma_L -
+//                   gamma} X).
+//
+// Products are 16-bit m16n8k16 tensor-core MMAs with fp32 accumulation, the same operand
+// roundings as the fused kernel (gdn_fast.cu), which stays the path without a workspace.
+#include <type_traits>
+
+#include "common.cuh"
+#include "gdn_mma.cuh"
+
+namespace mb {
+namespace {
+using namespace gdnk;
+
+// Per-chunk workspace record: W [C][DK] | U [C][DV] | Aq [C][C] (T) | gamma [C] (fp32).
+template <typename T, int DK, int DV>
+struct WsRec {
+  static constexpr size_t off_w = 0;
+  static constexpr size_t off_u = off_w + (size_t)C * DK * sizeof(T);
+  static constexpr size_t off_aq = off_u + (size_t)C * DV * sizeof(T);
+  static constexpr size_t off_gam = off_aq + (size_t)C * C * sizeof(T);
+  static constexpr size_t bytes = off_gam + (size_t)C * 4;
+  static_assert(bytes % 16 == 0, "records stay 16-byte aligned");
+};
+
+template <typename T, int DK, int DV>
+struct WyLayout {
+  static constexpr int QS = DK + 8, VS = DV + 8, AS = C + 8, XS = DK + DV + 8, TS = 16 + 8;
+  static constexpr size_t off_q = 0;
+  static constexpr size_t off_k = off_q + (size_t)C * QS * sizeof(T);
+  static constexpr size_t off_v = off_k + (size_t)C * QS * sizeof(T);
+  static constexpr size_t off_a = off_v + (size_t)C * VS * sizeof(T);
+  static constexpr size_t off_aq = off_a + (size_t)C * AS * sizeof(T);
+  static constexpr size_t off_x = off_aq + (size_t)C * AS * sizeof(T);
+  static constexpr size_t off_td = off_x + (size_t)C * XS * sizeof(T);
+  static constexpr size_t off_ad = off_td + 4ull * 16 * TS * sizeof(T);
+  static constexpr size_t off_vec = off_ad + 4ull * 16 * 17 * 4;
+  static constexpr size_t bytes = off_vec + 3ull * C * 4;
+};
+
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(NT) gdn_wy_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                    const T* __restrict__ v, const float* __restrict__ beta,
+                                                    const float* __restrict__ g, int H, int L, Strides18 sv,
+                                                    unsigned char* __restrict__ ws) {
+  using Lay = WyLayout<T, DK, DV>;
+  using Rec = WsRec<T, DK, DV>;
+  constexpr int QS = Lay::QS, VS = Lay::VS, AS = Lay::AS, XS = Lay::XS, TS = Lay::TS;
+  constexpr int NTILE = (DK + DV) / 8;
+  constexpr int SOLVE_T = (NTILE + NW - 1) / NW;
+  extern __shared__ __align__(16) unsigned char smem[];
+  T* cQ = reinterpret_cast<T*>(smem + Lay::off_q);
+  T* cK = reinterpret_cast<T*>(smem + Lay::off_k);
+  T* cV = reinterpret_cast<T*>(smem + Lay::off_v);
+  T* sA = reinterpret_cast<T*>(smem + Lay::off_a);
+  T* sAq = reinterpret_cast<T*>(smem + Lay::off_aq);
+  T* sX = reinterpret_cast<T*>(smem + Lay::off_x);
+  T* sTd = reinterpret_cast<T*>(smem + Lay::off_td);
+  float* sAd = reinterpret_cast<float*>(smem + Lay::off_ad);
+  float* sGam = reinterpret_cast<float*>(smem + Lay::off_vec);
+  float* sEg = sGam + C;
+  float* sBeta = sEg + C;
+
+  const int64_t* st = sv.s;
+  const int n = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const T* qg = q + b * st[0] + h * st[1];
+  const T* kg = k + b * st[3] + h * st[4];
+  const T* vg = v + b * st[6] + h * st[7];
+  const float* bg = beta + b * st[12] + h * st[13];
+  const float* gg = g + b * st[15] + h * st[16];
+
+  {  // q, k, v rows of the chunk (zeros past L)
+    constexpr int QV = DK * (int)sizeof(T) / 16, VV = DV * (int)sizeof(T) / 16;
+    constexpr int E = 16 / sizeof(T);
+    for (int i = tid; i < C * (2 * QV + VV); i += NT) {
+      const int r = i / (2 * QV + VV), c = i % (2 * QV + VV);
+      const int l = n * C + r;
+      const bool ok = l < L;
+      const int64_t lc = ok ? l : 0;
+      if (c < QV)
+        cp_async16(cQ + r * QS + c * E, qg + lc * st[2] + c * E, ok);
+      else if (c < 2 * QV)
+        cp_async16(cK + r * QS + (c - QV) * E, kg + lc * st[5] + (c - QV) * E, ok);
+      else
+        cp_async16(cV + r * VS + (c - 2 * QV) * E, vg + lc * st[8] + (c - 2 * QV) * E, ok);
+    }
+    cp_async_commit();
+  }
+  if (warp == 0) {  // gamma = inclusive cumsum(g), e^gamma, beta (padded rows: g = beta = 0)
+    float x0, x1, b0, b1;
+    {
+      const int l0 = n * C + lane, l1 = l0 + 32;
+      x0 = l0 < L ? gg[(int64_t)l0 * st[17]] : 0.f;
+      x1 = l1 < L ? gg[(int64_t)l1 * st[17]] : 0.f;
+      b0 = l0 < L ? bg[(int64_t)l0 * st[14]] : 0.f;
+      b1 = l1 < L ? bg[(int64_t)l1 * st[14]] : 0.f;
+    }
+#pragma unroll
+    for (int o2 = 1; o2 < 32; o2 <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o2);
+      const float y1 = __shfl_up_sync(0xffffffffu, x1, o2);
+      if (lane >= o2) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    sGam[lane] = x0;
+    sGam[lane + 32] = x1;
+    sEg[lane] = expf(x0);
+    sEg[lane + 32] = expf(x1);
+    sBeta[lane] = b0;
+    sBeta[lane + 32] = b1;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // KK -> A (+ diagonal inverses) on warps 0-3, QK -> Aq on warps 4-7
+  {
+    const int m0 = (warp & 3) * 16;
+    const T* left = warp < 4 ? cK : cQ;
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < DK; k0 += 16) {
+      uint32_t a[4];
+      lda(a, left, QS, m0, k0);
+#pragma unroll
+      for (int n0 = 0; n0 < 64; n0 += 16) {
+        uint32_t bb[4];
+        ldb_n(bb, cK, QS, k0, n0);
+        mma_16816<T>(acc[n0 / 8], a, &bb[0]);
+        mma_16816<T>(acc[n0 / 8 + 1], a, &bb[2]);
+      }
+    }
+    const int i0 = m0 + gq, i1 = i0 + 8;
+    const float gi0 = sGam[i0], gi1 = sGam[i1];
+    if (warp < 4) {
+      const float b0 = -sBeta[i0], b1 = -sBeta[i1];
+      float* ad = sAd + warp * 16 * 17;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int j = nt * 8 + 2 * tq;
+        const float gj0 = sGam[j], gj1 = sGam[j + 1];
+        const float a00 = j < i0 ? b0 * acc[nt][0] * expf(gi0 - gj0) : 0.f;
+        const float a01 = j + 1 < i0 ? b0 * acc[nt][1] * expf(gi0 - gj1) : 0.f;
+        const float a10 = j < i1 ? b1 * acc[nt][2] * expf(gi1 - gj0) : 0.f;
+        const float a11 = j + 1 < i1 ? b1 * acc[nt][3] * expf(gi1 - gj1) : 0.f;
+        st2(&sA[i0 * AS + j], a00, a01);
+        st2(&sA[i1 * AS + j], a10, a11);
+        if ((nt >> 1) == warp) {  // this warp's diagonal block, kept in fp32
+          const int jj = j - m0;
+          ad[gq * 17 + jj] = a00;
+          ad[gq * 17 + jj + 1] = a01;
+          ad[(gq + 8) * 17 + jj] = a10;
+          ad[(gq + 8) * 17 + jj + 1] = a11;
+        }
+      }
+      __syncwarp();
+      // T_ww = (I - A_ww)^-1: lane c < 16 owns column c; rows by forward substitution
+      if (lane < 16) {
+        float col[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          float s = (r == lane) ? 1.f : 0.f;
+#pragma unroll
+          for (int j = 0; j < r; ++j) s = fmaf(ad[r * 17 + j], col[j], s);
+          col[r] = s;
+        }
+        T* td = sTd + warp * 16 * TS;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) td[r * TS + lane] = from_f<T>(col[r]);
+      }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int j = nt * 8 + 2 * tq;
+        const float gj0 = sGam[j], gj1 = sGam[j + 1];
+        st2(&sAq[i0 * AS + j], j <= i0 ? acc[nt][0] * expf(gi0 - gj0) : 0.f,
+            j + 1 <= i0 ? acc[nt][1] * expf(gi0 - gj1) : 0.f);
+        st2(&sAq[i1 * AS + j], j <= i1 ? acc[nt][2] * expf(gi1 - gj0) : 0.f,
+            j + 1 <= i1 ? acc[nt][3] * expf(gi1 - gj1) : 0.f);
+      }
+    }
+  }
+  __syncthreads();
+
+  // blocked forward substitution, warp-local in its column tiles
+#pragma unroll
+  for (int bi = 0; bi < 4; ++bi) {
+    const int r0 = bi * 16;
+#pragma unroll
+    for (int ti = 0; ti < SOLVE_T; ++ti) {
+      const int tile = warp + NW * ti;
+      if (tile >= NTILE) break;
+      const int c0 = tile * 8;
+      float acc[4];
+      {
+        const int ra = r0 + gq, rb = ra + 8, c = c0 + 2 * tq;
+        if (c0 < DK) {
+          const float sa = sBeta[ra] * sEg[ra], sb = sBeta[rb] * sEg[rb];
+          const float2 xa = ld2(&cK[ra * QS + c]), xb = ld2(&cK[rb * QS + c]);
+          acc[0] = xa.x * sa; acc[1] = xa.y * sa; acc[2] = xb.x * sb; acc[3] = xb.y * sb;
+        } else {
+          const float sa = sBeta[ra], sb = sBeta[rb];
+          const float2 xa = ld2(&cV[ra * VS + c - DK]), xb = ld2(&cV[rb * VS + c - DK]);
+          acc[0] = xa.x * sa; acc[1] = xa.y * sa; acc[2] = xb.x * sb; acc[3] = xb.y * sb;
+        }
+      }
+      for (int bj = 0; bj < bi; ++bj) {  // + A_ij X_j
+        uint32_t a[4], bb[2];
+        lda(a, sA, AS, r0, bj * 16);
+        ldb_t1(bb, sX, XS, bj * 16, c0);
+        mma_16816<T>(acc, a, bb);
+      }
+      {
+        const int ra = r0 + gq, c = c0 + 2 * tq;
+        st2(&sX[ra * XS + c], acc[0], acc[1]);
+        st2(&sX[(ra + 8) * XS + c], acc[2], acc[3]);
+      }
+      __syncwarp();
+      {
+        uint32_t a[4], bb[2];
+        lda(a, sTd + bi * 16 * TS, TS, 0, 0);
+        ldb_t1(bb, sX, XS, r0, c0);
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_16816<T>(x, a, bb);
+        __syncwarp();
+        const int ra = r0 + gq, c = c0 + 2 * tq;
+        st2(&sX[ra * XS + c], x[0], x[1]);
+        st2(&sX[(ra + 8) * XS + c], x[2], x[3]);
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+
+  // record: W | U | Aq | gamma
+  unsigned char* rec = ws + ((size_t)bh * gridDim.x + n) * Rec::bytes;
+  {
+    constexpr int E = 16 / sizeof(T);
+    constexpr int WV = DK / E, UV = DV / E, AV = C / E;
+    for (int i = tid; i < C * (WV + UV + AV); i += NT) {
+      const int r = i / (WV + UV + AV), c = i % (WV + UV + AV);
+      uint4 val;
+      T* dst;
+      if (c < WV) {
+        val = *reinterpret_cast<const uint4*>(&sX[r * XS + c * E]);
+        dst = reinterpret_cast<T*>(rec + Rec::off_w) + r * DK + c * E;
+      } else if (c < WV + UV) {
+        val = *reinterpret_cast<const uint4*>(&sX[r * XS + DK + (c - WV) * E]);
+        dst = reinterpret_cast<T*>(rec + Rec::off_u) + r * DV + (c - WV) * E;
+      } else {
+        val = *reinterpret_cast<const uint4*>(&sAq[r * AS + (c - WV - UV) * E]);
+        dst = reinterpret_cast<T*>(rec + Rec::off_aq) + r * C + (c - WV - UV) * E;
+      }
+      *reinterpret_cast<uint4*>(dst) = val;
+    }
+    if (tid < C) reinterpret_cast<float*>(rec + Rec::off_gam)[tid] = sGam[tid];
+  }
+}
+
+template <typename T, int DK, int DV>
+struct RecLayout {
+  static constexpr int QS = DK + 8, VS = DV + 8, AS = C + 8, XS = DK + DV + 8;
+  static constexpr size_t q_b = (size_t)C * QS * sizeof(T);
+  static constexpr size_t wu_b = (size_t)C * XS * sizeof(T);
+  static constexpr size_t aq_b = (size_t)C * AS * sizeof(T);
+  static constexpr size_t g_b = (size_t)C * VS * sizeof(T);
+  static constexpr size_t stage_b = 2 * q_b + wu_b + aq_b + g_b + (size_t)C * 4;
+  // per stage: q | k | [W | U] | Aq | gate | gamma
+  static constexpr size_t o_q = 0, o_k = q_b, o_wu = 2 * q_b, o_aq = o_wu + wu_b, o_g = o_aq + aq_b,
+                          o_gam = o_g + g_b;
+  static constexpr size_t off_s = 2 * stage_b;
+  static constexpr size_t off_xd = off_s + 2ull * DK * VS * sizeof(T);
+  static constexpr size_t off_vec = off_xd + (size_t)C * VS * sizeof(T);
+  static constexpr size_t off_part = off_vec + 2ull * C * 4;
+  static constexpr size_t bytes = off_part + 2ull * C * 4;
+  static_assert(bytes <= 232448, "shared memory budget");
+};
+
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const unsigned char* __restrict__ ws,
+    const float* __restrict__ s_in, float* __restrict__ s_out, T* __restrict__ o, int H, int L, Strides18 sv,
+    const T* __restrict__ gate, int64_t gate_rs, int64_t gate_hs, const T* __restrict__ onorm_w,
+    float onorm_eps) {
+  using Lay = RecLayout<T, DK, DV>;
+  using Rec = WsRec<T, DK, DV>;
+  constexpr int QS = Lay::QS, VS = Lay::VS, AS = Lay::AS, XS = Lay::XS;
+  constexpr int SM_T = DK / 16;
+  constexpr int DVT = DV / 8;
+  constexpr int HT = DVT / 2;
+  extern __shared__ __align__(16) unsigned char smem[];
+  T* sS = reinterpret_cast<T*>(smem + Lay::off_s);
+  T* sXd = reinterpret_cast<T*>(smem + Lay::off_xd);
+  float* sEg = reinterpret_cast<float*>(smem + Lay::off_vec);
+  float* sDl = sEg + C;
+  float* sPart = reinterpret_cast<float*>(smem + Lay::off_part);
+
+  const int64_t* st = sv.s;
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const T* qg = q + b * st[0] + h * st[1];
+  const T* kg = k + b * st[3] + h * st[4];
+  T* og = o + b * st[9] + h * st[10];
+  const int nchunks = (L + C - 1) / C;
+  const unsigned char* recs = ws + (size_t)bh * nchunks * Rec::bytes;
+  const T* gbase = gate ? gate + (int64_t)b * L * gate_rs + h * gate_hs : nullptr;
+  const bool gate_async = gate && ((uintptr_t)gbase % 16 == 0) && (gate_rs % (16 / sizeof(T)) == 0);
+
+  // state: warp w holds S rows [16 (w % 4), +16) x value columns [DV/2 (w / 4), +DV/2) (fp32)
+  const bool s_owner = (warp & 3) < SM_T;
+  const int sm0 = (warp & 3) * 16;
+  const int sc0 = (warp >> 2) * (DV / 2);
+  float Sr[HT][4];
+  const float* s0 = s_in ? s_in + (size_t)bh * DK * DV : nullptr;
+  if (s_owner) {
+#pragma unroll
+    for (int nt = 0; nt < HT; ++nt) {
+      const int r = sm0 + gq, c = sc0 + nt * 8 + 2 * tq;
+      Sr[nt][0] = s0 ? s0[r * DV + c] : 0.f;
+      Sr[nt][1] = s0 ? s0[r * DV + c + 1] : 0.f;
+      Sr[nt][2] = s0 ? s0[(r + 8) * DV + c] : 0.f;
+      Sr[nt][3] = s0 ? s0[(r + 8) * DV + c + 1] : 0.f;
+      st2(&sS[r * VS + c], Sr[nt][0], Sr[nt][1]);
+      st2(&sS[(r + 8) * VS + c], Sr[nt][2], Sr[nt][3]);
+    }
+  }
+
+  auto stage_ptr = [&](int s) { return smem + (size_t)s * Lay::stage_b; };
+  auto load_chunk = [&](int n, int s) {
+    constexpr int E = 16 / sizeof(T);
+    constexpr int QV = DK / E, WV = DK / E, UV = DV / E, AV = C / E, GV = DV / E;
+    unsigned char* sp = stage_ptr(s);
+    T* dq = reinterpret_cast<T*>(sp + Lay::o_q);
+    T* dk = reinterpret_cast<T*>(sp + Lay::o_k);
+    T* dwu = reinterpret_cast<T*>(sp + Lay::o_wu);
+    T* daq = reinterpret_cast<T*>(sp + Lay::o_aq);
+    const unsigned char* rec = recs + (size_t)n * Rec::bytes;
+    const T* rw = reinterpret_cast<const T*>(rec + Rec::off_w);
+    const T* ru = reinterpret_cast<const T*>(rec + Rec::off_u);
+    const T* raq = reinterpret_cast<const T*>(rec + Rec::off_aq);
+    constexpr int PER = 2 * QV + WV + UV + AV;
+    for (int i = tid; i < C * PER; i += NT) {
+      const int r = i / PER, c = i % PER;
+      const int l = n * C + r;
+      const bool ok = l < L;
+      const int64_t lc = ok ? l : 0;
+      if (c < QV)
+        cp_async16(dq + r * QS + c * E, qg + lc * st[2] + c * E, ok);
+      else if (c < 2 * QV)
+        cp_async16(dk + r * QS + (c - QV) * E, kg + lc * st[5] + (c - QV) * E, ok);
+      else if (c < 2 * QV + WV)
+        cp_async16(dwu + r * XS + (c - 2 * QV) * E, rw + r * DK + (c - 2 * QV) * E, true);
+      else if (c < 2 * QV + WV + UV)
+        cp_async16(dwu + r * XS + DK + (c - 2 * QV - WV) * E, ru + r * DV + (c - 2 * QV - WV) * E, true);
+      else
+        cp_async16(daq + r * AS + (c - 2 * QV - WV - UV) * E, raq + r * C + (c - 2 * QV - WV - UV) * E, true);
+    }
+    if (tid < C / 4)
+      cp_async16(sp + Lay::o_gam + tid * 16, rec + Rec::off_gam + tid * 16, true);
+    if (gate_async) {
+      T* dg = reinterpret_cast<T*>(sp + Lay::o_g);
+      for (int i = tid; i < C * GV; i += NT) {
+        const int r = i / GV, c = i % GV;
+        const int l = n * C + r;
+        const bool ok = l < L;
+        cp_async16(dg + r * VS + c * E, gbase + (int64_t)(ok ? l : 0) * gate_rs + c * E, ok);
+      }
+    }
+    cp_async_commit();
+  };
+
+  if (nchunks > 0) load_chunk(0, 0);
+  for (int n = 0; n < nchunks; ++n) {
+    const int stage = n & 1;
+    if (n + 1 < nchunks) {
+      load_chunk(n + 1, stage ^ 1);  // that stage was last read in iteration n-1 (ended by a barrier)
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    unsigned char* sp = stage_ptr(stage);
+    const T* cQ = reinterpret_cast<const T*>(sp + Lay::o_q);
+    const T* cK = reinterpret_cast<const T*>(sp + Lay::o_k);
+    T* sX = reinterpret_cast<T*>(sp + Lay::o_wu);
+    const T* sAq = reinterpret_cast<const T*>(sp + Lay::o_aq);
+    const T* sG = reinterpret_cast<const T*>(sp + Lay::o_g);
+    const float* sGam = reinterpret_cast<const float*>(sp + Lay::o_gam);
+    const T* cS = sS + (size_t)(n & 1) * DK * VS;
+    T* nS = sS + (size_t)((n + 1) & 1) * DK * VS;
+    __syncthreads();  // (1) chunk n visible to every thread
+    if (tid < C) {
+      const float gl = sGam[C - 1];
+      sEg[tid] = expf(sGam[tid]);
+      sDl[tid] = expf(gl - sGam[tid]);
+    }
+    __syncthreads();  // (2) e^gamma, e^(gL - gamma)
+    const float eL = sEg[C - 1];
+
+    // X = U - W S  (warp: m-tile w%4, value-column half w/4); also Xd = e^(gL - g) X
+    {
+      const int m0 = (warp & 3) * 16;
+      const int nbase = (warp >> 2) * (DV / 2);
+      float acc[HT][4];
+#pragma unroll
+      for (int i = 0; i < HT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll
+      for (int k0 = 0; k0 < DK; k0 += 16) {
+        uint32_t a[4];
+        lda(a, sX, XS, m0, k0);
+#pragma unroll
+        for (int nn = 0; nn < DV / 2; nn += 16) {
+          uint32_t bb[4];
+          ldb_t(bb, cS, VS, k0, nbase + nn);
+          mma_16816<T>(acc[nn / 8], a, &bb[0]);
+          mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
+        }
+      }
+      const int ra = m0 + gq, rb = ra + 8;
+      const float da = sDl[ra], db = sDl[rb];
+#pragma unroll
+      for (int nt = 0; nt < HT; ++nt) {
+        const int c = nbase + nt * 8 + 2 * tq;
+        const float2 ua = ld2(&sX[ra * XS + DK + c]), ub = ld2(&sX[rb * XS + DK + c]);
+        const float x0 = ua.x - acc[nt][0], x1 = ua.y - acc[nt][1];
+        const float x2 = ub.x - acc[nt][2], x3 = ub.y - acc[nt][3];
+        st2(&sX[ra * XS + DK + c], x0, x1);
+        st2(&sX[rb * XS + DK + c], x2, x3);
+        st2(&sXd[ra * VS + c], x0 * da, x1 * da);
+        st2(&sXd[rb * VS + c], x2 * db, x3 * db);
+      }
+    }
+    __syncthreads();  // (3) X, Xd complete
+
+    // every warp: rows [16 (w % 4), +16) x value columns [DV/2 (w / 4), +DV/2) of
+    // o = e^g (q S) + Aq X  and  S = e^gL S + k^T Xd
+    {
+      const int m0 = (warp & 3) * 16, c0 = (warp >> 2) * (DV / 2);
+      float acc[HT][4];
+#pragma unroll
+      for (int i = 0; i < HT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll
+      for (int k0 = 0; k0 < DK; k0 += 16) {
+        uint32_t a[4];
+        lda(a, cQ, QS, m0, k0);
+#pragma unroll
+        for (int nn = 0; nn < DV / 2; nn += 16) {
+          uint32_t bb[4];
+          ldb_t(bb, cS, VS, k0, c0 + nn);
+          mma_16816<T>(acc[nn / 8], a, &bb[0]);
+          mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
+        }
+      }
+      const int ra = m0 + gq, rb = ra + 8;
+      const float ea = sEg[ra], eb = sEg[rb];
+#pragma unroll
+      for (int i = 0; i < HT; ++i) {
+        acc[i][0] *= ea; acc[i][1] *= ea; acc[i][2] *= eb; acc[i][3] *= eb;
+      }
+      for (int k0 = 0; k0 <= m0; k0 += 16) {  // Aq lower triangular: k < m0 + 16
+        uint32_t a[4];
+        lda(a, sAq, AS, m0, k0);
+#pragma unroll
+        for (int nn = 0; nn < DV / 2; nn += 16) {
+          uint32_t bb[4];
+          ldb_t(bb, sX + DK, XS, k0, c0 + nn);
+          mma_16816<T>(acc[nn / 8], a, &bb[0]);
+          mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
+        }
+      }
+      const int la = n * C + ra, lb = n * C + rb;
+      float ssa = 0.f, ssb = 0.f;
+      if (gate == nullptr) {
+#pragma unroll
+        for (int nt = 0; nt < HT; ++nt) {
+          const int c = c0 + nt * 8 + 2 * tq;
+          if (la < L) st2(&og[(int64_t)la * st[11] + c], acc[nt][0], acc[nt][1]);
+          if (lb < L) st2(&og[(int64_t)lb * st[11] + c], acc[nt][2], acc[nt][3]);
+        }
+      } else {
+        // partial sums of squares of this half-row (after the reference's o.to(dtype))
+#pragma unroll
+        for (int nt = 0; nt < HT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[nt][e] = to_f(from_f<T>(acc[nt][e]));
+          ssa += acc[nt][0] * acc[nt][0] + acc[nt][1] * acc[nt][1];
+          ssb += acc[nt][2] * acc[nt][2] + acc[nt][3] * acc[nt][3];
+        }
+        ssa += __shfl_xor_sync(0xffffffffu, ssa, 1);
+        ssa += __shfl_xor_sync(0xffffffffu, ssa, 2);
+        ssb += __shfl_xor_sync(0xffffffffu, ssb, 1);
+        ssb += __shfl_xor_sync(0xffffffffu, ssb, 2);
+        if (tq == 0) {
+          sPart[ra * 2 + (warp >> 2)] = ssa;
+          sPart[rb * 2 + (warp >> 2)] = ssb;
+        }
+      }
+      if (s_owner) {  // state update for this warp's S block
+#pragma unroll
+        for (int i = 0; i < HT; ++i) {
+          Sr[i][0] *= eL; Sr[i][1] *= eL; Sr[i][2] *= eL; Sr[i][3] *= eL;
+        }
+#pragma unroll
+        for (int k0 = 0; k0 < C; k0 += 16) {
+          uint32_t a[4];
+          lda_t(a, cK, QS, sm0, k0);
+#pragma unroll
+          for (int nn = 0; nn < DV / 2; nn += 16) {
+            uint32_t bb[4];
+            ldb_t(bb, sXd, VS, k0, sc0 + nn);
+            mma_16816<T>(Sr[nn / 8], a, &bb[0]);
+            mma_16816<T>(Sr[nn / 8 + 1], a, &bb[2]);
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < HT; ++nt) {
+          const int r = sm0 + gq, c = sc0 + nt * 8 + 2 * tq;
+          st2(&nS[r * VS + c], Sr[nt][0], Sr[nt][1]);
+          st2(&nS[(r + 8) * VS + c], Sr[nt][2], Sr[nt][3]);
+        }
+      }
+      if (gate != nullptr) {
+        __syncthreads();  // (4) both halves' partial row sums visible
+        ssa = sPart[ra * 2] + sPart[ra * 2 + 1];
+        ssb = sPart[rb * 2] + sPart[rb * 2 + 1];
+        const float rsa = rsqrtf(ssa / (float)DV + onorm_eps), rsb = rsqrtf(ssb / (float)DV + onorm_eps);
+        const T* ga = gate_async ? sG + ra * VS : gbase + (int64_t)la * gate_rs;
+        const T* gb = gate_async ? sG + rb * VS : gbase + (int64_t)lb * gate_rs;
+#pragma unroll
+        for (int nt = 0; nt < HT; ++nt) {
+          const int c = c0 + nt * 8 + 2 * tq;
+          const float2 w = ld2(&onorm_w[c]);
+          if (la < L) {
+            const float2 gt = ld2(&ga[c]);
+            const float y0 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][0] * rsa)) * w.x));
+            const float y1 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][1] * rsa)) * w.y));
+            st2(&og[(int64_t)la * st[11] + c], y0 * to_f(from_f<T>(siluf_(gt.x))),
+                y1 * to_f(from_f<T>(siluf_(gt.y))));
+          }
+          if (lb < L) {
+            const float2 gt = ld2(&gb[c]);
+            const float y0 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][2] * rsb)) * w.x));
+            const float y1 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][3] * rsb)) * w.y));
+            st2(&og[(int64_t)lb * st[11] + c], y0 * to_f(from_f<T>(siluf_(gt.x))),
+                y1 * to_f(from_f<T>(siluf_(gt.y))));
+          }
+        }
+      }
+    }
+    __syncthreads();  // (5) end of chunk: the stage and nS are reusable
+  }
+
+  if (s_owner) {
+    float* so = s_out + (size_t)bh * DK * DV;
+#pragma unroll
+    for (int nt = 0; nt < HT; ++nt) {
+      const int r = sm0 + gq, c = sc0 + nt * 8 + 2 * tq;
+      *reinterpret_cast<float2*>(&so[r * DV + c]) = make_float2(Sr[nt][0], Sr[nt][1]);
+      *reinterpret_cast<float2*>(&so[(r + 8) * DV + c]) = make_float2(Sr[nt][2], Sr[nt][3]);
+    }
+  }
+}
+
+template <typename T, int DK, int DV>
+int launch_split(const void* q, const void* k, const void* v, const float* beta, const float* g,
+                 const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, const Strides18& sv,
+                 const void* gate, int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, void* ws,
+                 cudaStream_t stream) {
+  using WL = WyLayout<T, DK, DV>;
+  using RL = RecLayout<T, DK, DV>;
+  auto k1 = gdn_wy_kernel<T, DK, DV>;
+  auto k2 = gdn_rec_kernel<T, DK, DV>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WL::bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RL::bytes);
+    if (e != cudaSuccess) return set_error(MB_ERR_CUDA, "gdn_chunk (split): smem attribute: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t nchunks = (L + C - 1) / C;
+  if (nchunks > 0) {
+    k1<<<dim3((unsigned)nchunks, (unsigned)(B * H)), NT, WL::bytes, stream>>>(
+        (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws);
+    int rc = check_launch("gdn_chunk (UT transform)");
+    if (rc) return rc;
+  }
+  k2<<<(unsigned)(B * H), NT, RL::bytes, stream>>>((const T*)q, (const T*)k, (const unsigned char*)ws, s_in, s_out,
+                                                   (T*)o, (int)H, (int)L, sv, (const T*)gate, gate_rs, gate_hs,
+                                                   (const T*)onorm_w, eps);
+  return check_launch("gdn_chunk (state scan)");
+}
+
+}  // namespace
+
+// Workspace bytes of the split path for (Dk, Dv), or 0 when no split kernel exists.
+int64_t gdn_split_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv, int dtype) {
+  if (dtype != MB_BF16 && dtype != MB_F16) return 0;
+  const int64_t nchunks = (L + C - 1) / C;
+  int64_t rec = 0;
+  if (Dk == 32 && Dv == 64) rec = WsRec<__nv_bfloat16, 32, 64>::bytes;
+  if (Dk == 64 && Dv == 64) rec = WsRec<__nv_bfloat16, 64, 64>::bytes;
+  if (Dk == 64 && Dv == 128) rec = WsRec<__nv_bfloat16, 64, 128>::bytes;
+  return B * H * nchunks * rec;
+}
+
+// Returns 1 (and launches) when the split path serves this call, else 0.
+int gdn_split_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, const void* k, const void* v,
+                       const float* beta, const float* g, const float* s_in, float* s_out, void* o, int64_t B,
+                       int64_t H, int64_t L, const int64_t* strides, const void* gate, int64_t gate_rs,
+                       int64_t gate_hs, const void* onorm_w, float eps, void* ws, int64_t ws_bytes, cudaStream_t st,
+                       int* rc) {
+  const int64_t need = gdn_split_workspace_bytes(B, H, L, Dk, Dv, dtype);
+  if (need == 0 || ws == nullptr || ws_bytes < need || ((uintptr_t)ws & 15) || L == 0) return 0;
+  if (strides[11] % 2 || strides[9] % 2 || strides[10] % 2 || ((uintptr_t)o & 3)) return 0;
+  if (gate && (gate_rs % 2 || gate_hs % 2 || ((uintptr_t)gate & 3) || ((uintptr_t)onorm_w & 3))) return 0;
+  Strides18 sv;
+  for (int i = 0; i < 18; ++i) sv.s[i] = strides[i];
+#define MB_SPLIT_CASE(DK_, DV_)                                                                                     \
+  if (Dk == DK_ && Dv == DV_) {                                                                                     \
+    *rc = dtype == MB_BF16 ? launch_split<__nv_bfloat16, DK_, DV_>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv,    \
+                                                                   gate, gate_rs, gate_hs, onorm_w, eps, ws, st)    \
+                           : launch_split<__half, DK_, DV_>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate,    \
+                                                            gate_rs, gate_hs, onorm_w, eps, ws, st);                \
+    return 1;                                                                                                       \
+  }
+  MB_SPLIT_CASE(32, 64)
+  MB_SPLIT_CASE(64, 64)
+  MB_SPLIT_CASE(64, 128)
+#undef MB_SPLIT_CASE
+  return 0;
+}
+
+}  // namespace mb

@@ -550,9 +550,13 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
         cs = cat.stride(0)
         strides = [T * H * dk, dk, H * dk, T * H * dk, dk, H * dk, T * H * dv, dv, H * dv,
                    T * cs, dv, cs, T * H, 1, H, T * H, 1, H]
-        _lib.call('motif_b200_gdn_chunk_gated', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(beta), _lib.ptr(g),
-                  _lib.ptr(state_in), _lib.ptr(state), _lib.ptr(cat), B, H, T, dk, dv, _lib.i64_array(strides),
-                  proj.data_ptr() + pk.off_g * proj.element_size(), N_in, dv, _lib.ptr(pk.onorm_w), eps, dc, st)
+        # two-kernel chunked delta rule: parallel UT transform into a workspace, then the scan
+        ws_bytes = _lib.load().motif_b200_gdn_chunk_workspace_bytes(B, H, T, dk, dv, dc)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+        _lib.call('motif_b200_gdn_chunk_gated_ws', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(beta),
+                  _lib.ptr(g), _lib.ptr(state_in), _lib.ptr(state), _lib.ptr(cat), B, H, T, dk, dv,
+                  _lib.i64_array(strides), proj.data_ptr() + pk.off_g * proj.element_size(), N_in, dv,
+                  _lib.ptr(pk.onorm_w), eps, dc, _lib.ptr(ws), max(ws_bytes, 0), st)
     _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
               cat.data_ptr() + H * dv * cat.element_size(), M, hid, N_in, cat.stride(0), dc, st)
     f = _mm(cat, pk.w_out)

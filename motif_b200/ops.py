@@ -74,9 +74,19 @@ def _delta_call(entry, q, k, v, beta, g, S):
     o = torch.empty(B, H, L, Dv, dtype=q.dtype, device=q.device)
     S_out = torch.empty(B, H, Dk, Dv, dtype=torch.float32, device=q.device)
     strides += [*o.stride()[:3], *beta.stride(), *g.stride()]
+    dc = _lib.dtype_code(q.dtype)
+    if entry == 'motif_b200_gdn_chunk':
+        # the two-kernel path (parallel UT transform, then the state scan) when it exists for
+        # this dtype / shape; its workspace comes from torch's caching allocator
+        ws_bytes = _lib.load().motif_b200_gdn_chunk_workspace_bytes(B, H, L, Dk, Dv, dc)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes > 0 else None
+        _lib.call('motif_b200_gdn_chunk_gated_ws', _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta),
+                  _lib.ptr(g), _lib.ptr(S), _lib.ptr(S_out), _lib.ptr(o), B, H, L, Dk, Dv, _lib.i64_array(strides),
+                  None, 0, 0, None, 0.0, dc, _lib.ptr(ws), max(ws_bytes, 0), _lib.stream_ptr(q.device))
+        return o, S_out.to(q.dtype)
     _lib.call(entry, _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta), _lib.ptr(g), _lib.ptr(S),
-              _lib.ptr(S_out), _lib.ptr(o), B, H, L, Dk, Dv, _lib.i64_array(strides),
-              _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device))
+              _lib.ptr(S_out), _lib.ptr(o), B, H, L, Dk, Dv, _lib.i64_array(strides), dc,
+              _lib.stream_ptr(q.device))
     return o, S_out.to(q.dtype)
 
 

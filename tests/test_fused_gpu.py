@@ -264,8 +264,20 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
     _lib.call('motif_b200_gdn_chunk_gated', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(be), _lib.ptr(ge),
               _lib.ptr(si), _lib.ptr(S2), _lib.ptr(out2), B, H, T, dk, dv, _lib.i64_array(strides),
               p.data_ptr() + (C + 2 * H) * 2, N, dv, _lib.ptr(ow), 1e-6, dc, s)
+    # the same call with a workspace: parallel UT-transform kernel + state-scan kernel
+    ws_bytes = _lib.load().motif_b200_gdn_chunk_workspace_bytes(B, H, T, dk, dv, dc)
+    assert ws_bytes > 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda')
+    out3 = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+    S3 = torch.empty(B, H, dk, dv, device='cuda')
+    _lib.call('motif_b200_gdn_chunk_gated_ws', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(be), _lib.ptr(ge),
+              _lib.ptr(si), _lib.ptr(S3), _lib.ptr(out3), B, H, T, dk, dv, _lib.i64_array(strides),
+              p.data_ptr() + (C + 2 * H) * 2, N, dv, _lib.ptr(ow), 1e-6, dc, _lib.ptr(ws), ws_bytes, s)
     torch.cuda.synchronize()
     assert torch.equal(co1, co2)
+    # same operand roundings in the same order: the split path reproduces the fused kernel
+    assert rel_err(out3.float(), out2.float()) < 1e-6, rel_err(out3.float(), out2.float())
+    assert rel_err(S3, S2) < 1e-6, rel_err(S3, S2)
     assert rel_err(out1.float(), out2.float()) < 1e-2, rel_err(out1.float(), out2.float())
     assert rel_err(S1, S2) < 1e-3, rel_err(S1, S2)
     # fp32 oracle on the prepared inputs (rounded like the kernels round them)
