@@ -248,10 +248,11 @@ MB_API int motif_b200_chord_decode_noalloc(const void* q, const void* k_cache, c
                                     float softmax_scale, float eps, int max_splits, int dtype,
                                     void* stream);
 
-/* Number of Chord attention CTAs (decode: motif_b200_chord_decode / _noalloc; tensor-core
- * prefill: motif_b200_chord_attention) whose bounded wait for a tensor copy or an MMA ran out
- * since the last call; such a CTA abandons its work (a decode split contributes nothing, a
- * prefill tile's rows are left unwritten) instead of hanging.  The counter is cleared.
+/* Number of CTAs whose bounded wait for a tensor / bulk copy or an MMA ran out since the last
+ * call (Chord decode: motif_b200_chord_decode / _noalloc; tensor-core Chord prefill:
+ * motif_b200_chord_attention; the GDN state scan of motif_b200_gdn_chunk_gated_ws); such a
+ * CTA abandons its work (a decode split contributes nothing, a prefill tile's rows or a
+ * scan's outputs are left unwritten) instead of hanging.  The counter is cleared.
  * Synchronous (copies from device memory).  Expected to stay 0.  No counterpart in the
  * reference. */
 MB_API int motif_b200_wait_timeouts(uint32_t* count);

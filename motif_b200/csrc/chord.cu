@@ -1588,12 +1588,18 @@ extern "C" int motif_b200_chord_decode_noalloc(const void* q, const void* k_cach
                                  dtype, stream);
 }
 
+namespace mb {
+int read_and_clear_gdn_timeouts(unsigned int* count);
+}
+
 extern "C" int motif_b200_wait_timeouts(uint32_t* count) {
   MB_REQUIRE(count != nullptr, MB_ERR_ARG, "wait_timeouts: null pointer");
-  unsigned int v = 0, zero = 0;
+  unsigned int v = 0, zero = 0, gdn = 0;
   if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess ||
       cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
     return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
-  *count = v;
+  const int rc = mb::read_and_clear_gdn_timeouts(&gdn);
+  if (rc) return rc;
+  *count = v + gdn;
   return MB_OK;
 }

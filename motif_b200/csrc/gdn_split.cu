@@ -10,13 +10,15 @@
 //                   A = -(beta_i k_i.k_j e^{gamma_i - gamma_j}) (j < i), the 16x16 diagonal
 //                   inverses of (I - A) and the blocked forward substitution
 //                   [W | U] = (I - A)^-1 [k beta e^gamma | v beta]; Aq = (q k^T)_ij
-//                   e^{gamma_i - gamma_j} (j <= i).  Writes W, U, Aq (input dtype) and gamma
-//                   (fp32) to the workspace.
+//                   e^{gamma_i - gamma_j} (j <= i); q e^gamma and k e^{gamma_L - gamma}.  The
+//                   chunk's record is written as the exact shared-memory image the scan uses
+//                   (padded rows), so the scan fetches it with one bulk copy.
 //   gdn_rec_kernel  grid B*H, one CTA per (b, h) walking its chunks with S resident in fp32
-//                   registers; W, U, Aq, gamma, q, k and the gate tile of chunk n+1 stream in
-//                   (cp.async) while chunk n computes X = U - W S, o = e^gamma (q S) + Aq X,
-//                   the GatedRMSNorm epilogue, and S = e^{gamma_L} S + k^T (e^{gamma_L -
-//                   gamma} X).
+//                   registers; the record of chunk n+2 streams in (cp.async.bulk + mbarrier)
+//                   while chunk n computes X = U - W S, o = (q e^gamma) S + Aq X and
+//                   S = e^{gamma_L} S + (k e^{gamma_L - gamma})^T X.
+//   gdn_gate_norm   (gated calls) o <- rmsnorm(o) * w * silu(gate) per (token, head) row,
+//                   in place: the GatedRMSNorm of gdn_attn.py:197-209, fully parallel.
 //
 // Products are 16-bit m16n8k16 tensor-core MMAs with fp32 accumulation, the same operand
 // roundings as the fused kernel (gdn_fast.cu), which stays the path without a workspace.
@@ -29,14 +31,19 @@ namespace mb {
 namespace {
 using namespace gdnk;
 
-// Per-chunk workspace record: W [C][DK] | U [C][DV] | Aq [C][C] (T) | gamma [C] (fp32).
+// Per-chunk workspace record = the scan's shared-memory image of one chunk (rows padded by 8
+// elements so that ldmatrix rows fall on distinct banks):
+//   Qs [C][QS] = q e^gamma | Kd [C][QS] = k e^{gamma_L - gamma} | WU [C][XS] = [W | U] |
+//   Aq [C][AS] (T) | e^{gamma_L} (fp32, padded to 16 bytes)
 template <typename T, int DK, int DV>
 struct WsRec {
-  static constexpr size_t off_w = 0;
-  static constexpr size_t off_u = off_w + (size_t)C * DK * sizeof(T);
-  static constexpr size_t off_aq = off_u + (size_t)C * DV * sizeof(T);
-  static constexpr size_t off_gam = off_aq + (size_t)C * C * sizeof(T);
-  static constexpr size_t bytes = off_gam + (size_t)C * 4;
+  static constexpr int QS = DK + 8, VS = DV + 8, AS = C + 8, XS = DK + DV + 8;
+  static constexpr size_t off_qs = 0;
+  static constexpr size_t off_kd = off_qs + (size_t)C * QS * sizeof(T);
+  static constexpr size_t off_wu = off_kd + (size_t)C * QS * sizeof(T);
+  static constexpr size_t off_aq = off_wu + (size_t)C * XS * sizeof(T);
+  static constexpr size_t off_el = off_aq + (size_t)C * AS * sizeof(T);
+  static constexpr size_t bytes = off_el + 16;
   static_assert(bytes % 16 == 0, "records stay 16-byte aligned");
 };
 
@@ -163,10 +170,10 @@ __global__ void __launch_bounds__(NT) gdn_wy_kernel(const T* __restrict__ q, con
       for (int nt = 0; nt < 8; ++nt) {
         const int j = nt * 8 + 2 * tq;
         const float gj0 = sGam[j], gj1 = sGam[j + 1];
-        const float a00 = j < i0 ? b0 * acc[nt][0] * expf(gi0 - gj0) : 0.f;
-        const float a01 = j + 1 < i0 ? b0 * acc[nt][1] * expf(gi0 - gj1) : 0.f;
-        const float a10 = j < i1 ? b1 * acc[nt][2] * expf(gi1 - gj0) : 0.f;
-        const float a11 = j + 1 < i1 ? b1 * acc[nt][3] * expf(gi1 - gj1) : 0.f;
+        const float a00 = j < i0 ? b0 * acc[nt][0] * __expf(gi0 - gj0) : 0.f;
+        const float a01 = j + 1 < i0 ? b0 * acc[nt][1] * __expf(gi0 - gj1) : 0.f;
+        const float a10 = j < i1 ? b1 * acc[nt][2] * __expf(gi1 - gj0) : 0.f;
+        const float a11 = j + 1 < i1 ? b1 * acc[nt][3] * __expf(gi1 - gj1) : 0.f;
         st2(&sA[i0 * AS + j], a00, a01);
         st2(&sA[i1 * AS + j], a10, a11);
         if ((nt >> 1) == warp) {  // this warp's diagonal block, kept in fp32
@@ -197,10 +204,10 @@ __global__ void __launch_bounds__(NT) gdn_wy_kernel(const T* __restrict__ q, con
       for (int nt = 0; nt < 8; ++nt) {
         const int j = nt * 8 + 2 * tq;
         const float gj0 = sGam[j], gj1 = sGam[j + 1];
-        st2(&sAq[i0 * AS + j], j <= i0 ? acc[nt][0] * expf(gi0 - gj0) : 0.f,
-            j + 1 <= i0 ? acc[nt][1] * expf(gi0 - gj1) : 0.f);
-        st2(&sAq[i1 * AS + j], j <= i1 ? acc[nt][2] * expf(gi1 - gj0) : 0.f,
-            j + 1 <= i1 ? acc[nt][3] * expf(gi1 - gj1) : 0.f);
+        st2(&sAq[i0 * AS + j], j <= i0 ? acc[nt][0] * __expf(gi0 - gj0) : 0.f,
+            j + 1 <= i0 ? acc[nt][1] * __expf(gi0 - gj1) : 0.f);
+        st2(&sAq[i1 * AS + j], j <= i1 ? acc[nt][2] * __expf(gi1 - gj0) : 0.f,
+            j + 1 <= i1 ? acc[nt][3] * __expf(gi1 - gj1) : 0.f);
       }
     }
   }
@@ -256,81 +263,72 @@ __global__ void __launch_bounds__(NT) gdn_wy_kernel(const T* __restrict__ q, con
   }
   __syncthreads();
 
-  // record: W | U | Aq | gamma
+  // the record: padded images of q e^gamma, k e^{gamma_L - gamma}, [W | U], Aq, e^{gamma_L}
   unsigned char* rec = ws + ((size_t)bh * gridDim.x + n) * Rec::bytes;
   {
     constexpr int E = 16 / sizeof(T);
-    constexpr int WV = DK / E, UV = DV / E, AV = C / E;
-    for (int i = tid; i < C * (WV + UV + AV); i += NT) {
-      const int r = i / (WV + UV + AV), c = i % (WV + UV + AV);
-      uint4 val;
-      T* dst;
-      if (c < WV) {
-        val = *reinterpret_cast<const uint4*>(&sX[r * XS + c * E]);
-        dst = reinterpret_cast<T*>(rec + Rec::off_w) + r * DK + c * E;
-      } else if (c < WV + UV) {
-        val = *reinterpret_cast<const uint4*>(&sX[r * XS + DK + (c - WV) * E]);
-        dst = reinterpret_cast<T*>(rec + Rec::off_u) + r * DV + (c - WV) * E;
-      } else {
-        val = *reinterpret_cast<const uint4*>(&sAq[r * AS + (c - WV - UV) * E]);
-        dst = reinterpret_cast<T*>(rec + Rec::off_aq) + r * C + (c - WV - UV) * E;
-      }
-      *reinterpret_cast<uint4*>(dst) = val;
+    T* rqs = reinterpret_cast<T*>(rec + Rec::off_qs);
+    T* rkd = reinterpret_cast<T*>(rec + Rec::off_kd);
+    constexpr int QP = DK / 2;  // element pairs per q / k row
+    const float gl = sGam[C - 1];
+    for (int i = tid; i < C * QP; i += NT) {
+      const int r = i / QP, c = 2 * (i % QP);
+      const float eq = sEg[r], ek = __expf(gl - sGam[r]);
+      const float2 xq = ld2(&cQ[r * QS + c]), xk = ld2(&cK[r * QS + c]);
+      st2(&rqs[r * QS + c], xq.x * eq, xq.y * eq);
+      st2(&rkd[r * QS + c], xk.x * ek, xk.y * ek);
     }
-    if (tid < C) reinterpret_cast<float*>(rec + Rec::off_gam)[tid] = sGam[tid];
+    constexpr int XV = (DK + DV) / E, AV = C / E;
+    T* rwu = reinterpret_cast<T*>(rec + Rec::off_wu);
+    T* raq = reinterpret_cast<T*>(rec + Rec::off_aq);
+    for (int i = tid; i < C * (XV + AV); i += NT) {
+      const int r = i / (XV + AV), c = i % (XV + AV);
+      if (c < XV)
+        *reinterpret_cast<uint4*>(&rwu[r * XS + c * E]) = *reinterpret_cast<const uint4*>(&sX[r * XS + c * E]);
+      else
+        *reinterpret_cast<uint4*>(&raq[r * AS + (c - XV) * E]) =
+            *reinterpret_cast<const uint4*>(&sAq[r * AS + (c - XV) * E]);
+    }
+    if (tid == 0) *reinterpret_cast<float*>(rec + Rec::off_el) = sEg[C - 1];
   }
 }
 
 template <typename T, int DK, int DV>
 struct RecLayout {
-  static constexpr int QS = DK + 8, VS = DV + 8, AS = C + 8, XS = DK + DV + 8;
-  static constexpr size_t q_b = (size_t)C * QS * sizeof(T);
-  static constexpr size_t wu_b = (size_t)C * XS * sizeof(T);
-  static constexpr size_t aq_b = (size_t)C * AS * sizeof(T);
-  static constexpr size_t g_b = (size_t)C * VS * sizeof(T);
-  static constexpr size_t stage_b = 2 * q_b + wu_b + aq_b + g_b + (size_t)C * 4;
-  // per stage: q | k | [W | U] | Aq | gate | gamma
-  static constexpr size_t o_q = 0, o_k = q_b, o_wu = 2 * q_b, o_aq = o_wu + wu_b, o_g = o_aq + aq_b,
-                          o_gam = o_g + g_b;
-  static constexpr size_t off_s = 2 * stage_b;
-  static constexpr size_t off_xd = off_s + 2ull * DK * VS * sizeof(T);
-  static constexpr size_t off_vec = off_xd + (size_t)C * VS * sizeof(T);
-  static constexpr size_t off_part = off_vec + 2ull * C * 4;
-  static constexpr size_t bytes = off_part + 2ull * C * 4;
+  using Rec = WsRec<T, DK, DV>;
+  static constexpr int VS = DV + 8;
+  static constexpr size_t off_stage = 0;  // 2 record images
+  static constexpr size_t off_s = off_stage + 2 * Rec::bytes;
+  static constexpr size_t off_bar = off_s + 2ull * DK * VS * sizeof(T);
+  static constexpr size_t bytes = off_bar + 16;
   static_assert(bytes <= 232448, "shared memory budget");
 };
 
+constexpr uint32_t kRecWait = 1u << 22;
+// Count of state-scan CTAs whose bounded record-copy wait ran out (never expected).
+__device__ unsigned int g_gdn_wait_timeouts = 0;
+
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
-    const T* __restrict__ q, const T* __restrict__ k, const unsigned char* __restrict__ ws,
-    const float* __restrict__ s_in, float* __restrict__ s_out, T* __restrict__ o, int H, int L, Strides18 sv,
-    const T* __restrict__ gate, int64_t gate_rs, int64_t gate_hs, const T* __restrict__ onorm_w,
-    float onorm_eps) {
+__global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __restrict__ ws,
+                                                        const float* __restrict__ s_in, float* __restrict__ s_out,
+                                                        T* __restrict__ o, int H, int L, Strides18 sv) {
   using Lay = RecLayout<T, DK, DV>;
   using Rec = WsRec<T, DK, DV>;
-  constexpr int QS = Lay::QS, VS = Lay::VS, AS = Lay::AS, XS = Lay::XS;
+  constexpr int QS = Rec::QS, VS = Rec::VS, AS = Rec::AS, XS = Rec::XS;
   constexpr int SM_T = DK / 16;
-  constexpr int DVT = DV / 8;
-  constexpr int HT = DVT / 2;
-  extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int HT = DV / 16;  // n8 tiles per column half
+  extern __shared__ __align__(128) unsigned char smem[];
   T* sS = reinterpret_cast<T*>(smem + Lay::off_s);
-  T* sXd = reinterpret_cast<T*>(smem + Lay::off_xd);
-  float* sEg = reinterpret_cast<float*>(smem + Lay::off_vec);
-  float* sDl = sEg + C;
-  float* sPart = reinterpret_cast<float*>(smem + Lay::off_part);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Lay::off_bar);
 
   const int64_t* st = sv.s;
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
-  const T* qg = q + b * st[0] + h * st[1];
-  const T* kg = k + b * st[3] + h * st[4];
   T* og = o + b * st[9] + h * st[10];
   const int nchunks = (L + C - 1) / C;
   const unsigned char* recs = ws + (size_t)bh * nchunks * Rec::bytes;
-  const T* gbase = gate ? gate + (int64_t)b * L * gate_rs + h * gate_hs : nullptr;
-  const bool gate_async = gate && ((uintptr_t)gbase % 16 == 0) && (gate_rs % (16 / sizeof(T)) == 0);
 
   // state: warp w holds S rows [16 (w % 4), +16) x value columns [DV/2 (w / 4), +DV/2) (fp32)
   const bool s_owner = (warp & 3) < SM_T;
@@ -350,79 +348,40 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
       st2(&sS[(r + 8) * VS + c], Sr[nt][2], Sr[nt][3]);
     }
   }
-
-  auto stage_ptr = [&](int s) { return smem + (size_t)s * Lay::stage_b; };
-  auto load_chunk = [&](int n, int s) {
-    constexpr int E = 16 / sizeof(T);
-    constexpr int QV = DK / E, WV = DK / E, UV = DV / E, AV = C / E, GV = DV / E;
-    unsigned char* sp = stage_ptr(s);
-    T* dq = reinterpret_cast<T*>(sp + Lay::o_q);
-    T* dk = reinterpret_cast<T*>(sp + Lay::o_k);
-    T* dwu = reinterpret_cast<T*>(sp + Lay::o_wu);
-    T* daq = reinterpret_cast<T*>(sp + Lay::o_aq);
-    const unsigned char* rec = recs + (size_t)n * Rec::bytes;
-    const T* rw = reinterpret_cast<const T*>(rec + Rec::off_w);
-    const T* ru = reinterpret_cast<const T*>(rec + Rec::off_u);
-    const T* raq = reinterpret_cast<const T*>(rec + Rec::off_aq);
-    constexpr int PER = 2 * QV + WV + UV + AV;
-    for (int i = tid; i < C * PER; i += NT) {
-      const int r = i / PER, c = i % PER;
-      const int l = n * C + r;
-      const bool ok = l < L;
-      const int64_t lc = ok ? l : 0;
-      if (c < QV)
-        cp_async16(dq + r * QS + c * E, qg + lc * st[2] + c * E, ok);
-      else if (c < 2 * QV)
-        cp_async16(dk + r * QS + (c - QV) * E, kg + lc * st[5] + (c - QV) * E, ok);
-      else if (c < 2 * QV + WV)
-        cp_async16(dwu + r * XS + (c - 2 * QV) * E, rw + r * DK + (c - 2 * QV) * E, true);
-      else if (c < 2 * QV + WV + UV)
-        cp_async16(dwu + r * XS + DK + (c - 2 * QV - WV) * E, ru + r * DV + (c - 2 * QV - WV) * E, true);
-      else
-        cp_async16(daq + r * AS + (c - 2 * QV - WV - UV) * E, raq + r * C + (c - 2 * QV - WV - UV) * E, true);
-    }
-    if (tid < C / 4)
-      cp_async16(sp + Lay::o_gam + tid * 16, rec + Rec::off_gam + tid * 16, true);
-    if (gate_async) {
-      T* dg = reinterpret_cast<T*>(sp + Lay::o_g);
-      for (int i = tid; i < C * GV; i += NT) {
-        const int r = i / GV, c = i % GV;
-        const int l = n * C + r;
-        const bool ok = l < L;
-        cp_async16(dg + r * VS + c * E, gbase + (int64_t)(ok ? l : 0) * gate_rs + c * E, ok);
-      }
-    }
-    cp_async_commit();
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  auto issue = [&](int n) {  // thread 0: record n -> stage n & 1
+    mbar_arrive_expect_tx(&bar[n & 1], (uint32_t)Rec::bytes);
+    bulk_load(smem + Lay::off_stage + (size_t)(n & 1) * Rec::bytes, recs + (size_t)n * Rec::bytes,
+              (uint32_t)Rec::bytes, &bar[n & 1]);
   };
+  int nissued = 0;
+  if (tid == 0)
+    for (; nissued < min(nchunks, 2); ++nissued) issue(nissued);
 
-  if (nchunks > 0) load_chunk(0, 0);
-  for (int n = 0; n < nchunks; ++n) {
+  bool failed = false;
+  int n = 0;
+  for (; n < nchunks; ++n) {
     const int stage = n & 1;
-    if (n + 1 < nchunks) {
-      load_chunk(n + 1, stage ^ 1);  // that stage was last read in iteration n-1 (ended by a barrier)
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    const bool ok = mbar_wait_bounded(&bar[stage], (uint32_t)((n >> 1) & 1), kRecWait);
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
     }
-    unsigned char* sp = stage_ptr(stage);
-    const T* cQ = reinterpret_cast<const T*>(sp + Lay::o_q);
-    const T* cK = reinterpret_cast<const T*>(sp + Lay::o_k);
-    T* sX = reinterpret_cast<T*>(sp + Lay::o_wu);
-    const T* sAq = reinterpret_cast<const T*>(sp + Lay::o_aq);
-    const T* sG = reinterpret_cast<const T*>(sp + Lay::o_g);
-    const float* sGam = reinterpret_cast<const float*>(sp + Lay::o_gam);
+    unsigned char* sp = smem + Lay::off_stage + (size_t)stage * Rec::bytes;
+    const T* cQ = reinterpret_cast<const T*>(sp + Rec::off_qs);
+    const T* cK = reinterpret_cast<const T*>(sp + Rec::off_kd);
+    T* sX = reinterpret_cast<T*>(sp + Rec::off_wu);
+    const T* sAq = reinterpret_cast<const T*>(sp + Rec::off_aq);
+    const float eL = *reinterpret_cast<const float*>(sp + Rec::off_el);
     const T* cS = sS + (size_t)(n & 1) * DK * VS;
     T* nS = sS + (size_t)((n + 1) & 1) * DK * VS;
-    __syncthreads();  // (1) chunk n visible to every thread
-    if (tid < C) {
-      const float gl = sGam[C - 1];
-      sEg[tid] = expf(sGam[tid]);
-      sDl[tid] = expf(gl - sGam[tid]);
-    }
-    __syncthreads();  // (2) e^gamma, e^(gL - gamma)
-    const float eL = sEg[C - 1];
 
-    // X = U - W S  (warp: m-tile w%4, value-column half w/4); also Xd = e^(gL - g) X
+    // X = U - W S  (warp: m-tile w%4, value-column half w/4), in place of U
     {
       const int m0 = (warp & 3) * 16;
       const int nbase = (warp >> 2) * (DV / 2);
@@ -442,23 +401,17 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
         }
       }
       const int ra = m0 + gq, rb = ra + 8;
-      const float da = sDl[ra], db = sDl[rb];
 #pragma unroll
       for (int nt = 0; nt < HT; ++nt) {
         const int c = nbase + nt * 8 + 2 * tq;
         const float2 ua = ld2(&sX[ra * XS + DK + c]), ub = ld2(&sX[rb * XS + DK + c]);
-        const float x0 = ua.x - acc[nt][0], x1 = ua.y - acc[nt][1];
-        const float x2 = ub.x - acc[nt][2], x3 = ub.y - acc[nt][3];
-        st2(&sX[ra * XS + DK + c], x0, x1);
-        st2(&sX[rb * XS + DK + c], x2, x3);
-        st2(&sXd[ra * VS + c], x0 * da, x1 * da);
-        st2(&sXd[rb * VS + c], x2 * db, x3 * db);
+        st2(&sX[ra * XS + DK + c], ua.x - acc[nt][0], ua.y - acc[nt][1]);
+        st2(&sX[rb * XS + DK + c], ub.x - acc[nt][2], ub.y - acc[nt][3]);
       }
     }
-    __syncthreads();  // (3) X, Xd complete
+    __syncthreads();  // X complete
 
-    // every warp: rows [16 (w % 4), +16) x value columns [DV/2 (w / 4), +DV/2) of
-    // o = e^g (q S) + Aq X  and  S = e^gL S + k^T Xd
+    // o = (q e^g) S + Aq X  and  S = e^gL S + (k e^(gL - g))^T X for this warp's block
     {
       const int m0 = (warp & 3) * 16, c0 = (warp >> 2) * (DV / 2);
       float acc[HT][4];
@@ -476,12 +429,6 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
           mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
         }
       }
-      const int ra = m0 + gq, rb = ra + 8;
-      const float ea = sEg[ra], eb = sEg[rb];
-#pragma unroll
-      for (int i = 0; i < HT; ++i) {
-        acc[i][0] *= ea; acc[i][1] *= ea; acc[i][2] *= eb; acc[i][3] *= eb;
-      }
       for (int k0 = 0; k0 <= m0; k0 += 16) {  // Aq lower triangular: k < m0 + 16
         uint32_t a[4];
         lda(a, sAq, AS, m0, k0);
@@ -493,34 +440,15 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
           mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
         }
       }
+      const int ra = m0 + gq, rb = ra + 8;
       const int la = n * C + ra, lb = n * C + rb;
-      float ssa = 0.f, ssb = 0.f;
-      if (gate == nullptr) {
 #pragma unroll
-        for (int nt = 0; nt < HT; ++nt) {
-          const int c = c0 + nt * 8 + 2 * tq;
-          if (la < L) st2(&og[(int64_t)la * st[11] + c], acc[nt][0], acc[nt][1]);
-          if (lb < L) st2(&og[(int64_t)lb * st[11] + c], acc[nt][2], acc[nt][3]);
-        }
-      } else {
-        // partial sums of squares of this half-row (after the reference's o.to(dtype))
-#pragma unroll
-        for (int nt = 0; nt < HT; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[nt][e] = to_f(from_f<T>(acc[nt][e]));
-          ssa += acc[nt][0] * acc[nt][0] + acc[nt][1] * acc[nt][1];
-          ssb += acc[nt][2] * acc[nt][2] + acc[nt][3] * acc[nt][3];
-        }
-        ssa += __shfl_xor_sync(0xffffffffu, ssa, 1);
-        ssa += __shfl_xor_sync(0xffffffffu, ssa, 2);
-        ssb += __shfl_xor_sync(0xffffffffu, ssb, 1);
-        ssb += __shfl_xor_sync(0xffffffffu, ssb, 2);
-        if (tq == 0) {
-          sPart[ra * 2 + (warp >> 2)] = ssa;
-          sPart[rb * 2 + (warp >> 2)] = ssb;
-        }
+      for (int nt = 0; nt < HT; ++nt) {
+        const int c = c0 + nt * 8 + 2 * tq;
+        if (la < L) st2(&og[(int64_t)la * st[11] + c], acc[nt][0], acc[nt][1]);
+        if (lb < L) st2(&og[(int64_t)lb * st[11] + c], acc[nt][2], acc[nt][3]);
       }
-      if (s_owner) {  // state update for this warp's S block
+      if (s_owner) {
 #pragma unroll
         for (int i = 0; i < HT; ++i) {
           Sr[i][0] *= eL; Sr[i][1] *= eL; Sr[i][2] *= eL; Sr[i][3] *= eL;
@@ -532,7 +460,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
 #pragma unroll
           for (int nn = 0; nn < DV / 2; nn += 16) {
             uint32_t bb[4];
-            ldb_t(bb, sXd, VS, k0, sc0 + nn);
+            ldb_t(bb, sX + DK, XS, k0, sc0 + nn);
             mma_16816<T>(Sr[nn / 8], a, &bb[0]);
             mma_16816<T>(Sr[nn / 8 + 1], a, &bb[2]);
           }
@@ -544,37 +472,21 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
           st2(&nS[(r + 8) * VS + c], Sr[nt][2], Sr[nt][3]);
         }
       }
-      if (gate != nullptr) {
-        __syncthreads();  // (4) both halves' partial row sums visible
-        ssa = sPart[ra * 2] + sPart[ra * 2 + 1];
-        ssb = sPart[rb * 2] + sPart[rb * 2 + 1];
-        const float rsa = rsqrtf(ssa / (float)DV + onorm_eps), rsb = rsqrtf(ssb / (float)DV + onorm_eps);
-        const T* ga = gate_async ? sG + ra * VS : gbase + (int64_t)la * gate_rs;
-        const T* gb = gate_async ? sG + rb * VS : gbase + (int64_t)lb * gate_rs;
-#pragma unroll
-        for (int nt = 0; nt < HT; ++nt) {
-          const int c = c0 + nt * 8 + 2 * tq;
-          const float2 w = ld2(&onorm_w[c]);
-          if (la < L) {
-            const float2 gt = ld2(&ga[c]);
-            const float y0 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][0] * rsa)) * w.x));
-            const float y1 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][1] * rsa)) * w.y));
-            st2(&og[(int64_t)la * st[11] + c], y0 * to_f(from_f<T>(siluf_(gt.x))),
-                y1 * to_f(from_f<T>(siluf_(gt.y))));
-          }
-          if (lb < L) {
-            const float2 gt = ld2(&gb[c]);
-            const float y0 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][2] * rsb)) * w.x));
-            const float y1 = to_f(from_f<T>(to_f(from_f<T>(acc[nt][3] * rsb)) * w.y));
-            st2(&og[(int64_t)lb * st[11] + c], y0 * to_f(from_f<T>(siluf_(gt.x))),
-                y1 * to_f(from_f<T>(siluf_(gt.y))));
-          }
-        }
-      }
     }
-    __syncthreads();  // (5) end of chunk: the stage and nS are reusable
+    __syncthreads();  // end of chunk: the stage and nS are reusable
+    if (tid == 0 && nissued < nchunks) {  // record n + 2 into the stage chunk n used
+      fence_proxy_async_smem();
+      issue(nissued);
+      ++nissued;
+    }
   }
-
+  if (failed) {
+    if (tid == 0) {  // let the copies in flight land (bounded), then report
+      atomicAdd(&g_gdn_wait_timeouts, 1u);
+      for (int u = n; u < nissued; ++u) mbar_wait_bounded(&bar[u & 1], (uint32_t)((u >> 1) & 1), kRecWait);
+    }
+    return;
+  }
   if (s_owner) {
     float* so = s_out + (size_t)bh * DK * DV;
 #pragma unroll
@@ -583,6 +495,42 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(
       *reinterpret_cast<float2*>(&so[r * DV + c]) = make_float2(Sr[nt][0], Sr[nt][1]);
       *reinterpret_cast<float2*>(&so[(r + 8) * DV + c]) = make_float2(Sr[nt][2], Sr[nt][3]);
     }
+  }
+}
+
+// GatedRMSNorm on the scan's output rows, in place: o <- rmsnorm(o) * w * silu(gate) for each
+// (token, head) row of DV values (gdn_attn.py:197-209 with rms_norm.py:547-553 roundings).
+// One warp per row; lanes own DV/32 consecutive values.
+template <typename T, int DV>
+__global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, int64_t ob, int64_t oh, int64_t ol,
+                                                            const T* __restrict__ gate, int64_t gate_rs,
+                                                            int64_t gate_hs, const T* __restrict__ w, float eps, int H,
+                                                            int L, int64_t rows) {
+  constexpr int PL = DV / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);  // (b * L + l) * H + h
+  if (row >= rows) return;
+  const int h = (int)(row % H);
+  const int64_t bl = row / H;
+  const int l = (int)(bl % L), b = (int)(bl / L);
+  T* orow = o + b * ob + h * oh + (int64_t)l * ol + lane * PL;
+  const T* grow = gate + bl * gate_rs + h * gate_hs + lane * PL;
+  float x[PL], gt[PL], wt[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    x[i] = to_f(orow[i]);
+    gt[i] = to_f(grow[i]);
+    wt[i] = to_f(w[lane * PL + i]);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PL; ++i) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)DV + eps);
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * wt[i]));
+    orow[i] = from_f<T>(y * to_f(from_f<T>(siluf_(gt[i]))));
   }
 }
 
@@ -605,16 +553,18 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int64_t nchunks = (L + C - 1) / C;
-  if (nchunks > 0) {
-    k1<<<dim3((unsigned)nchunks, (unsigned)(B * H)), NT, WL::bytes, stream>>>(
-        (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws);
-    int rc = check_launch("gdn_chunk (UT transform)");
-    if (rc) return rc;
-  }
-  k2<<<(unsigned)(B * H), NT, RL::bytes, stream>>>((const T*)q, (const T*)k, (const unsigned char*)ws, s_in, s_out,
-                                                   (T*)o, (int)H, (int)L, sv, (const T*)gate, gate_rs, gate_hs,
-                                                   (const T*)onorm_w, eps);
-  return check_launch("gdn_chunk (state scan)");
+  k1<<<dim3((unsigned)nchunks, (unsigned)(B * H)), NT, WL::bytes, stream>>>(
+      (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws);
+  int rc = check_launch("gdn_chunk (UT transform)");
+  if (rc) return rc;
+  k2<<<(unsigned)(B * H), NT, RL::bytes, stream>>>((const unsigned char*)ws, s_in, s_out, (T*)o, (int)H, (int)L, sv);
+  rc = check_launch("gdn_chunk (state scan)");
+  if (rc || gate == nullptr) return rc;
+  const int64_t rows = B * L * H;
+  const int64_t* st = sv.s;
+  gdn_gate_norm_kernel<T, DV><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(
+      (T*)o, st[9], st[10], st[11], (const T*)gate, gate_rs, gate_hs, (const T*)onorm_w, eps, (int)H, (int)L, rows);
+  return check_launch("gdn_chunk (gated norm)");
 }
 
 }  // namespace
@@ -628,6 +578,15 @@ int64_t gdn_split_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, i
   if (Dk == 64 && Dv == 64) rec = WsRec<__nv_bfloat16, 64, 64>::bytes;
   if (Dk == 64 && Dv == 128) rec = WsRec<__nv_bfloat16, 64, 128>::bytes;
   return B * H * nchunks * rec;
+}
+
+int read_and_clear_gdn_timeouts(unsigned int* count) {
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gdn_wait_timeouts, sizeof(v)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_gdn_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
+    return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
+  *count = v;
+  return MB_OK;
 }
 
 // Returns 1 (and launches) when the split path serves this call, else 0.

@@ -275,9 +275,11 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
               p.data_ptr() + (C + 2 * H) * 2, N, dv, _lib.ptr(ow), 1e-6, dc, _lib.ptr(ws), ws_bytes, s)
     torch.cuda.synchronize()
     assert torch.equal(co1, co2)
-    # same operand roundings in the same order: the split path reproduces the fused kernel
-    assert rel_err(out3.float(), out2.float()) < 1e-6, rel_err(out3.float(), out2.float())
-    assert rel_err(S3, S2) < 1e-6, rel_err(S3, S2)
+    # the split path rounds q e^gamma and k e^(gL - gamma) where the fused kernel rounds the
+    # products instead: agreement to the 16-bit operand rounding
+    assert rel_err(out3.float(), out2.float()) < 1e-2, rel_err(out3.float(), out2.float())
+    assert rel_err(S3, S2) < 5e-3, rel_err(S3, S2)
+    assert _lib.wait_timeouts() == 0
     assert rel_err(out1.float(), out2.float()) < 1e-2, rel_err(out1.float(), out2.float())
     assert rel_err(S1, S2) < 1e-3, rel_err(S1, S2)
     # fp32 oracle on the prepared inputs (rounded like the kernels round them)
