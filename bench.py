@@ -126,7 +126,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200', '-i', str(self.idx)], stdout=subprocess.PIPE,
+                                          '-lms', '50', '-i', str(self.idx)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None

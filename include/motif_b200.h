@@ -194,6 +194,18 @@ MB_API int motif_b200_gdn_prefill(const void* proj, int64_t proj_stride, const v
                            int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int dtype,
                            void* stream);
 
+/* motif_b200_gdn_prefill with a caller-provided device workspace of at least
+ * motif_b200_gdn_chunk_workspace_bytes(B, H, T, Dk, Dv, dtype) bytes (16-byte aligned).  With
+ * it, (Dk, Dv) = (64, 128) runs as three kernels: the preparation (conv, SiLU, norms, beta, g)
+ * fused into the fully parallel per-chunk UT transform, the state scan, and the gated norm;
+ * other shapes (or workspace == NULL) run motif_b200_gdn_prefill.  Same results contract. */
+MB_API int motif_b200_gdn_prefill_ws(const void* proj, int64_t proj_stride, const void* conv_w,
+                              const void* A_log, const void* dt_bias, const void* conv_in,
+                              void* conv_out, const float* state_in, float* state_out,
+                              const void* onorm_w, float eps, void* out, int64_t out_stride,
+                              int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int dtype,
+                              void* workspace, int64_t workspace_bytes, void* stream);
+
 /* One GDN decode step (T == 1) for a whole layer, fused: conv with the carried state,
  * SiLU, L2 norms, beta/g, the recurrent update of `state` ([B,H,Dk,Dv] fp32, in place)
  * and the gated RMSNorm of the output with gate columns `gate` (row stride proj_stride),

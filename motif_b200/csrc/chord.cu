@@ -1095,6 +1095,17 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
       pa[2 * nt] = pack2<T>(p0, p1);
       pa[2 * nt + 1] = pack2<T>(p2, p3);
     }
+    // Key rows at or past nk hold whatever the cache slots (or the next head's rows) contain,
+    // possibly non-finite: P is 0 there, but 0 * NaN would still poison the MMA, so this warp
+    // zeroes its rows of the V tile that lie past the split's last key (full 128-byte rows,
+    // swizzle-independent).  The proxy fence orders these writes before the stage's refill.
+    if (warp * 16 + 16 > nk) {
+      uint4* vz = reinterpret_cast<uint4*>(sV + s * TILE_BYTES + warp * 16 * 128);
+      for (int i = lane; i < 16 * 8; i += 32)
+        if (warp * 16 + (i >> 3) >= nk) vz[i] = make_uint4(0, 0, 0, 0);
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
     // O += P V over the same 16 keys (V rows 16w .. 16w+15, transposed by ldmatrix)
     const int vr = warp * 16 + (lane & 15);
     const unsigned char* vrow = sV + s * TILE_BYTES + vr * 128;

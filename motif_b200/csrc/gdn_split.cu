@@ -59,14 +59,50 @@ struct WyLayout {
   static constexpr size_t off_td = off_x + (size_t)C * XS * sizeof(T);
   static constexpr size_t off_ad = off_td + 4ull * 16 * TS * sizeof(T);
   static constexpr size_t off_vec = off_ad + 4ull * 16 * 17 * 4;
-  static constexpr size_t bytes = off_vec + 3ull * C * 4;
+  static constexpr size_t bytes = off_vec + 4ull * C * 4;
 };
 
-template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(NT) gdn_wy_kernel(const T* __restrict__ q, const T* __restrict__ k,
+// Inputs of the fused preparation (PREP = true): the raw projection rows [q | k | v | a | b | ...]
+// (row stride ps, token-major), the conv weights / carried conv state and the decay parameters
+// (gdn_attn.py:116-136, :183-197), with the roundings of motif_b200_gdn_prep.
+template <typename T>
+struct PrepIn {
+  const T* proj = nullptr;
+  int64_t ps = 0;
+  const T* conv_w = nullptr;   // [C][4], C = H (2 Dk + Dv): q | k | v channels
+  const T* A_log = nullptr;    // [H]
+  const T* dt_bias = nullptr;  // [H]
+  const T* conv_in = nullptr;  // [B][3][C] raw inputs before token 0, or nullptr (zeros)
+  T* conv_out = nullptr;       // [B][3][C] raw inputs at L-3 .. L-1, or nullptr
+};
+
+// Warp 0: gamma = inclusive cumsum of the chunk's g (two values per lane), e^gamma, beta.
+__device__ __forceinline__ void wy_gamma(int lane, float x0, float x1, float b0, float b1, float* sGam, float* sEg,
+                                         float* sBeta) {
+#pragma unroll
+  for (int o2 = 1; o2 < 32; o2 <<= 1) {
+    const float y0 = __shfl_up_sync(0xffffffffu, x0, o2);
+    const float y1 = __shfl_up_sync(0xffffffffu, x1, o2);
+    if (lane >= o2) {
+      x0 += y0;
+      x1 += y1;
+    }
+  }
+  x1 += __shfl_sync(0xffffffffu, x0, 31);
+  sGam[lane] = x0;
+  sGam[lane + 32] = x1;
+  sEg[lane] = expf(x0);
+  sEg[lane + 32] = expf(x1);
+  __syncwarp();
+  sBeta[lane] = b0;
+  sBeta[lane + 32] = b1;
+}
+
+template <typename T, int DK, int DV, bool PREP>
+__global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                     const T* __restrict__ v, const float* __restrict__ beta,
                                                     const float* __restrict__ g, int H, int L, Strides18 sv,
-                                                    unsigned char* __restrict__ ws) {
+                                                    unsigned char* __restrict__ ws, PrepIn<T> pin) {
   using Lay = WyLayout<T, DK, DV>;
   using Rec = WsRec<T, DK, DV>;
   constexpr int QS = Lay::QS, VS = Lay::VS, AS = Lay::AS, XS = Lay::XS, TS = Lay::TS;
@@ -90,54 +126,130 @@ __global__ void __launch_bounds__(NT) gdn_wy_kernel(const T* __restrict__ q, con
   const int b = bh / H, h = bh % H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
-  const T* qg = q + b * st[0] + h * st[1];
-  const T* kg = k + b * st[3] + h * st[4];
-  const T* vg = v + b * st[6] + h * st[7];
-  const float* bg = beta + b * st[12] + h * st[13];
-  const float* gg = g + b * st[15] + h * st[16];
+  const T* qg = PREP ? nullptr : q + b * st[0] + h * st[1];
+  const T* kg = PREP ? nullptr : k + b * st[3] + h * st[4];
+  const T* vg = PREP ? nullptr : v + b * st[6] + h * st[7];
+  const float* bg = PREP ? nullptr : beta + b * st[12] + h * st[13];
+  const float* gg = PREP ? nullptr : g + b * st[15] + h * st[16];
 
-  {  // q, k, v rows of the chunk (zeros past L)
-    constexpr int QV = DK * (int)sizeof(T) / 16, VV = DV * (int)sizeof(T) / 16;
-    constexpr int E = 16 / sizeof(T);
-    for (int i = tid; i < C * (2 * QV + VV); i += NT) {
-      const int r = i / (2 * QV + VV), c = i % (2 * QV + VV);
-      const int l = n * C + r;
-      const bool ok = l < L;
-      const int64_t lc = ok ? l : 0;
-      if (c < QV)
-        cp_async16(cQ + r * QS + c * E, qg + lc * st[2] + c * E, ok);
-      else if (c < 2 * QV)
-        cp_async16(cK + r * QS + (c - QV) * E, kg + lc * st[5] + (c - QV) * E, ok);
-      else
-        cp_async16(cV + r * VS + (c - 2 * QV) * E, vg + lc * st[8] + (c - 2 * QV) * E, ok);
+  if constexpr (!PREP) {
+    {  // q, k, v rows of the chunk (zeros past L)
+      constexpr int QV = DK * (int)sizeof(T) / 16, VV = DV * (int)sizeof(T) / 16;
+      constexpr int E = 16 / sizeof(T);
+      for (int i = tid; i < C * (2 * QV + VV); i += NT) {
+        const int r = i / (2 * QV + VV), c = i % (2 * QV + VV);
+        const int l = n * C + r;
+        const bool ok = l < L;
+        const int64_t lc = ok ? l : 0;
+        if (c < QV)
+          cp_async16(cQ + r * QS + c * E, qg + lc * st[2] + c * E, ok);
+        else if (c < 2 * QV)
+          cp_async16(cK + r * QS + (c - QV) * E, kg + lc * st[5] + (c - QV) * E, ok);
+        else
+          cp_async16(cV + r * VS + (c - 2 * QV) * E, vg + lc * st[8] + (c - 2 * QV) * E, ok);
+      }
+      cp_async_commit();
     }
-    cp_async_commit();
-  }
-  if (warp == 0) {  // gamma = inclusive cumsum(g), e^gamma, beta (padded rows: g = beta = 0)
-    float x0, x1, b0, b1;
-    {
-      const int l0 = n * C + lane, l1 = l0 + 32;
-      x0 = l0 < L ? gg[(int64_t)l0 * st[17]] : 0.f;
-      x1 = l1 < L ? gg[(int64_t)l1 * st[17]] : 0.f;
-      b0 = l0 < L ? bg[(int64_t)l0 * st[14]] : 0.f;
-      b1 = l1 < L ? bg[(int64_t)l1 * st[14]] : 0.f;
+    if (warp == 0) {  // gamma = inclusive cumsum(g), e^gamma, beta (padded rows: g = beta = 0)
+      float x0, x1, b0, b1;
+      {
+        const int l0 = n * C + lane, l1 = l0 + 32;
+        x0 = l0 < L ? gg[(int64_t)l0 * st[17]] : 0.f;
+        x1 = l1 < L ? gg[(int64_t)l1 * st[17]] : 0.f;
+        b0 = l0 < L ? bg[(int64_t)l0 * st[14]] : 0.f;
+        b1 = l1 < L ? bg[(int64_t)l1 * st[14]] : 0.f;
+      }
+      wy_gamma(lane, x0, x1, b0, b1, sGam, sEg, sBeta);
     }
+  } else {
+    // causal depthwise conv (4 taps, carried state) + SiLU, L2-normalised q * Dk^-0.5 and k,
+    // beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias): motif_b200_gdn_prep's math.
+    // Thread = (8-channel group of this head's q | k | v = lane, 8-row run = warp); the q / k
+    // norms reduce over the 8 lanes of a head's group.
+    constexpr int NG = (2 * DK + DV) / 8;  // channel groups of one head
+    static_assert(NG == 32 && C / 8 == NW, "one group per lane, one 8-row run per warp");
+    const int Ct = H * (2 * DK + DV);
+    const int grp = lane, run = warp;
+    const int kind = grp < DK / 8 ? 0 : (grp < 2 * DK / 8 ? 1 : 2);
+    const int cl = grp * 8;  // local channel
+    const int cg = kind == 0 ? h * DK + cl
+                             : (kind == 1 ? H * DK + h * DK + (cl - DK) : 2 * H * DK + h * DV + (cl - 2 * DK));
+    const T* P = pin.proj + (int64_t)b * L * pin.ps;
+    const int t0 = n * C + run * 8;
+    uint4 raw[11];
 #pragma unroll
-    for (int o2 = 1; o2 < 32; o2 <<= 1) {
-      const float y0 = __shfl_up_sync(0xffffffffu, x0, o2);
-      const float y1 = __shfl_up_sync(0xffffffffu, x1, o2);
-      if (lane >= o2) {
-        x0 += y0;
-        x1 += y1;
+    for (int j = 0; j < 11; ++j) {
+      const int tau = t0 - 3 + j;
+      raw[j] = make_uint4(0, 0, 0, 0);
+      if (tau >= 0 && tau < L)
+        raw[j] = *reinterpret_cast<const uint4*>(P + (int64_t)tau * pin.ps + cg);
+      else if (tau < 0 && pin.conv_in)
+        raw[j] = *reinterpret_cast<const uint4*>(pin.conv_in + ((int64_t)b * 3 + (3 + tau)) * Ct + cg);
+    }
+    float w[8][4];
+    {
+      const uint4* wp = reinterpret_cast<const uint4*>(pin.conv_w + (int64_t)cg * 4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 r = wp[u];
+        const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[2 * u + i / 4][i % 4] = to_f(e[i]);
       }
     }
-    x1 += __shfl_sync(0xffffffffu, x0, 31);
-    sGam[lane] = x0;
-    sGam[lane + 32] = x1;
-    sEg[lane] = expf(x0);
-    sEg[lane + 32] = expf(x1);
-    sBeta[lane] = b0;
-    sBeta[lane + 32] = b1;
+    const float qscale = rsqrtf((float)DK);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int row = run * 8 + r;
+      const bool ok = t0 + r < L;
+      float y[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x0 = to_f(reinterpret_cast<const T*>(&raw[r])[i]);
+        const float x1 = to_f(reinterpret_cast<const T*>(&raw[r + 1])[i]);
+        const float x2 = to_f(reinterpret_cast<const T*>(&raw[r + 2])[i]);
+        const float x3 = to_f(reinterpret_cast<const T*>(&raw[r + 3])[i]);
+        const float a = w[i][0] * x0 + w[i][1] * x1 + w[i][2] * x2 + w[i][3] * x3;
+        y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
+        ss += y[i] * y[i];
+      }
+#pragma unroll
+      for (int o2 = 1; o2 < 8; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+      const float sc = kind == 0 ? qscale / fmaxf(sqrtf(ss), 1e-12f) : (kind == 1 ? 1.f / fmaxf(sqrtf(ss), 1e-12f) : 1.f);
+      uint4 pk;
+      T* o8 = reinterpret_cast<T*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(ok ? y[i] * sc : 0.f);
+      T* dst = kind == 0 ? cQ + row * QS + cl : (kind == 1 ? cK + row * QS + (cl - DK) : cV + row * VS + (cl - 2 * DK));
+      *reinterpret_cast<uint4*>(dst) = pk;
+    }
+    // the run holding L-1 writes the raw inputs at L-3 .. L-1 as the carried conv state
+    const int last = L - 1 - t0;
+    if (pin.conv_out && last >= 0 && last < 8) {
+#pragma unroll
+      for (int j = 0; j < 11; ++j) {
+        const int slot = j - last - 1;  // raw[j] holds token t0 - 3 + j = L - 3 + slot
+        if (slot >= 0 && slot < 3 && (j >= 3 || L < 3))
+          *reinterpret_cast<uint4*>(pin.conv_out + ((int64_t)b * 3 + slot) * Ct + cg) = raw[j];
+      }
+    }
+    float* sGin = sGam + 3 * C;  // raw g values before the cumsum
+    if (tid < C) {
+      const int l = n * C + tid;
+      float bt = 0.f, gt = 0.f;
+      if (l < L) {
+        const T* row = P + (int64_t)l * pin.ps;
+        const float Aexp = -to_f(from_f<T>(expf(to_f(pin.A_log[h]))));
+        const float dtb = to_f(pin.dt_bias[h]);
+        bt = to_f(from_f<T>(sigmoidf_(to_f(row[Ct + H + h]))));
+        gt = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(to_f(row[Ct + h]) + dtb)))))));
+      }
+      sBeta[tid] = bt;
+      sGin[tid] = gt;
+    }
+    __syncthreads();
+    if (warp == 0) wy_gamma(lane, sGin[lane], sGin[lane + 32], sBeta[lane], sBeta[lane + 32], sGam, sEg, sBeta);
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -500,48 +612,56 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
 
 // GatedRMSNorm on the scan's output rows, in place: o <- rmsnorm(o) * w * silu(gate) for each
 // (token, head) row of DV values (gdn_attn.py:197-209 with rms_norm.py:547-553 roundings).
-// One warp per row; lanes own DV/32 consecutive values.
+// One warp per row; lanes own DV/32 consecutive values, moved as one vector.
 template <typename T, int DV>
 __global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, int64_t ob, int64_t oh, int64_t ol,
                                                             const T* __restrict__ gate, int64_t gate_rs,
                                                             int64_t gate_hs, const T* __restrict__ w, float eps, int H,
                                                             int L, int64_t rows) {
   constexpr int PL = DV / 32;
+  using V = typename std::conditional<PL * sizeof(T) == 8, uint2, typename std::conditional<PL * sizeof(T) == 4,
+                                                                                             uint32_t, uint4>::type>::type;
+  static_assert(sizeof(V) == PL * sizeof(T), "one vector per lane");
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);  // (b * L + l) * H + h
   if (row >= rows) return;
   const int h = (int)(row % H);
   const int64_t bl = row / H;
   const int l = (int)(bl % L), b = (int)(bl / L);
-  T* orow = o + b * ob + h * oh + (int64_t)l * ol + lane * PL;
-  const T* grow = gate + bl * gate_rs + h * gate_hs + lane * PL;
-  float x[PL], gt[PL], wt[PL];
-#pragma unroll
-  for (int i = 0; i < PL; ++i) {
-    x[i] = to_f(orow[i]);
-    gt[i] = to_f(grow[i]);
-    wt[i] = to_f(w[lane * PL + i]);
-  }
+  V* orow = reinterpret_cast<V*>(o + b * ob + h * oh + (int64_t)l * ol) + lane;
+  const V gv = reinterpret_cast<const V*>(gate + bl * gate_rs + h * gate_hs)[lane];
+  const V wv = reinterpret_cast<const V*>(w)[lane];
+  V ov = *orow;
+  const T* oe = reinterpret_cast<const T*>(&ov);
+  const T* ge = reinterpret_cast<const T*>(&gv);
+  const T* we = reinterpret_cast<const T*>(&wv);
+  float x[PL];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < PL; ++i) ss += x[i] * x[i];
+  for (int i = 0; i < PL; ++i) {
+    x[i] = to_f(oe[i]);
+    ss += x[i] * x[i];
+  }
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / (float)DV + eps);
+  V res;
+  T* re = reinterpret_cast<T*>(&res);
 #pragma unroll
   for (int i = 0; i < PL; ++i) {
-    const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * wt[i]));
-    orow[i] = from_f<T>(y * to_f(from_f<T>(siluf_(gt[i]))));
+    const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * to_f(we[i])));
+    re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
   }
+  *orow = res;
 }
 
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, bool PREP = false>
 int launch_split(const void* q, const void* k, const void* v, const float* beta, const float* g,
                  const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, const Strides18& sv,
                  const void* gate, int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, void* ws,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, PrepIn<T> pin = PrepIn<T>{}) {
   using WL = WyLayout<T, DK, DV>;
   using RL = RecLayout<T, DK, DV>;
-  auto k1 = gdn_wy_kernel<T, DK, DV>;
+  auto k1 = gdn_wy_kernel<T, DK, DV, PREP>;
   auto k2 = gdn_rec_kernel<T, DK, DV>;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -554,7 +674,7 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
   }
   const int64_t nchunks = (L + C - 1) / C;
   k1<<<dim3((unsigned)nchunks, (unsigned)(B * H)), NT, WL::bytes, stream>>>(
-      (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws);
+      (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws, pin);
   int rc = check_launch("gdn_chunk (UT transform)");
   if (rc) return rc;
   k2<<<(unsigned)(B * H), NT, RL::bytes, stream>>>((const unsigned char*)ws, s_in, s_out, (T*)o, (int)H, (int)L, sv);
@@ -598,7 +718,12 @@ int gdn_split_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, const v
   const int64_t need = gdn_split_workspace_bytes(B, H, L, Dk, Dv, dtype);
   if (need == 0 || ws == nullptr || ws_bytes < need || ((uintptr_t)ws & 15) || L == 0) return 0;
   if (strides[11] % 2 || strides[9] % 2 || strides[10] % 2 || ((uintptr_t)o & 3)) return 0;
-  if (gate && (gate_rs % 2 || gate_hs % 2 || ((uintptr_t)gate & 3) || ((uintptr_t)onorm_w & 3))) return 0;
+  {  // the gated norm moves Dv / 32 values per lane as one vector
+    const int64_t vec = Dv / 32, vb = vec * 2;
+    if (gate && (gate_rs % vec || gate_hs % vec || strides[9] % vec || strides[10] % vec || strides[11] % vec ||
+                 (uintptr_t)gate % vb || (uintptr_t)o % vb || (uintptr_t)onorm_w % vb))
+      return 0;
+  }
   Strides18 sv;
   for (int i = 0; i < 18; ++i) sv.s[i] = strides[i];
 #define MB_SPLIT_CASE(DK_, DV_)                                                                                     \
@@ -616,4 +741,68 @@ int gdn_split_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, const v
   return 0;
 }
 
+// Whole-layer prefill (16-bit, Dk = 64 or 32 with Dv = 2 Dk... see the dispatch below): the
+// preparation fused into the UT-transform kernel, the state scan, the gated norm.
+int gdn_prefill_split_dispatch(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
+                               const void* dt_bias, const void* conv_in, void* conv_out, const float* s_in,
+                               float* s_out, const void* onorm_w, float eps, void* out, int64_t os, int64_t B,
+                               int64_t Tn, int64_t H, int64_t Dk, int64_t Dv, int dtype, void* ws, int64_t ws_bytes,
+                               cudaStream_t st, int* rc) {
+  const int64_t need = gdn_split_workspace_bytes(B, H, Tn, Dk, Dv, dtype);
+  if (need == 0 || ws == nullptr || ws_bytes < need || ((uintptr_t)ws & 15) || Tn == 0) return 0;
+  // one channel group per lane / one 8-row run per warp needs 2 Dk + Dv = 256 channels per head
+  if (!(Dk == 64 && Dv == 128)) return 0;
+  const int64_t C = H * (2 * Dk + Dv);
+  if (ps % 8 || (uintptr_t)proj % 16 || (uintptr_t)conv_w % 16 || (conv_in && (uintptr_t)conv_in % 16) ||
+      (conv_out && (uintptr_t)conv_out % 16) || os % 4 || (uintptr_t)out % 8 || (uintptr_t)onorm_w % 8 || C % 8 ||
+      (C + 2 * H) % 4)
+    return 0;
+  Strides18 sv;
+  for (int i = 0; i < 18; ++i) sv.s[i] = 0;
+  sv.s[9] = Tn * os;
+  sv.s[10] = Dv;
+  sv.s[11] = os;
+  auto go = [&](auto t) {
+    using T = decltype(t);
+    PrepIn<T> pin;
+    pin.proj = (const T*)proj;
+    pin.ps = ps;
+    pin.conv_w = (const T*)conv_w;
+    pin.A_log = (const T*)A_log;
+    pin.dt_bias = (const T*)dt_bias;
+    pin.conv_in = (const T*)conv_in;
+    pin.conv_out = (T*)conv_out;
+    const T* gate = (const T*)proj + C + 2 * H;
+    return launch_split<T, 64, 128, true>(nullptr, nullptr, nullptr, nullptr, nullptr, s_in, s_out, out, B, H, Tn, sv,
+                                          gate, ps, Dv, onorm_w, eps, ws, st, pin);
+  };
+  *rc = dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+  return 1;
+}
+
 }  // namespace mb
+
+extern "C" int motif_b200_gdn_prefill_ws(const void* proj, int64_t proj_stride, const void* conv_w, const void* A_log,
+                                         const void* dt_bias, const void* conv_in, void* conv_out,
+                                         const float* state_in, float* state_out, const void* onorm_w, float eps,
+                                         void* out, int64_t out_stride, int64_t B, int64_t T, int64_t H, int64_t Dk,
+                                         int64_t Dv, int dtype, void* workspace, int64_t workspace_bytes,
+                                         void* stream) {
+  using namespace mb;
+  MB_REQUIRE(proj && conv_w && A_log && dt_bias && state_out && onorm_w && out, MB_ERR_ARG,
+             "gdn_prefill_ws: null pointer");
+  MB_REQUIRE(conv_out == nullptr || conv_out != conv_in, MB_ERR_ARG, "gdn_prefill_ws: conv_out must not alias conv_in");
+  MB_REQUIRE(B >= 0 && T >= 0 && H > 0 && B * H < (1LL << 31) && T < (1LL << 31), MB_ERR_SHAPE,
+             "gdn_prefill_ws: bad shape");
+  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "gdn_prefill_ws: 16-bit dtypes only");
+  MB_REQUIRE(workspace == nullptr || workspace_bytes >= gdn_split_workspace_bytes(B, H, T, Dk, Dv, dtype),
+             MB_ERR_ARG, "gdn_prefill_ws: workspace too small");
+  if (B == 0 || T == 0) return set_error(MB_ERR_SHAPE, "gdn_prefill_ws: empty input");
+  int rc = MB_OK;
+  if (gdn_prefill_split_dispatch(proj, proj_stride, conv_w, A_log, dt_bias, conv_in, conv_out, state_in, state_out,
+                                 onorm_w, eps, out, out_stride, B, T, H, Dk, Dv, dtype, workspace, workspace_bytes,
+                                 (cudaStream_t)stream, &rc))
+    return rc;
+  return motif_b200_gdn_prefill(proj, proj_stride, conv_w, A_log, dt_bias, conv_in, conv_out, state_in, state_out,
+                                onorm_w, eps, out, out_stride, B, T, H, Dk, Dv, dtype, stream);
+}

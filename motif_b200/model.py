@@ -529,6 +529,17 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   _lib.ptr(pk.dt_bias), _lib.ptr(conv), _lib.ptr(state), proj.data_ptr() + pk.off_g * proj.element_size(),
                   _lib.ptr(pk.onorm_w), _lib.ptr(cat), cat.stride(0), B, H, dk, dv, eps, dc, st)
         conv_out = conv
+    elif dt != torch.float32 and (dk, dv) == (64, 128) and N_in % 8 == 0 and not FUSED_GDN_PREFILL:
+        # three kernels: preparation fused into the parallel per-chunk UT transform (records in a
+        # workspace), the state scan, the gated norm
+        conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)
+        state = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+        ws_bytes = _lib.load().motif_b200_gdn_chunk_workspace_bytes(B, H, T, dk, dv, dc)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        _lib.call('motif_b200_gdn_prefill_ws', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+                  _lib.ptr(pk.dt_bias), _lib.ptr(conv_in), _lib.ptr(conv_out), _lib.ptr(state_in), _lib.ptr(state),
+                  _lib.ptr(pk.onorm_w), eps, _lib.ptr(cat), cat.stride(0), B, T, H, dk, dv, dc, _lib.ptr(ws), ws_bytes,
+                  st)
     elif FUSED_GDN_PREFILL and dt != torch.float32 and (dk, dv) in _PREFILL_DIMS and N_in % 8 == 0:
         # one kernel: conv + SiLU + norms + beta/g + chunked delta rule + GatedRMSNorm
         conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)

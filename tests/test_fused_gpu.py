@@ -178,6 +178,9 @@ def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, monkeypatch):
     q = torch.randn(B, T, H, D, generator=g).to(dtype)
     kc = torch.randn(B, Hkv, cap, D, generator=g).to(dtype)
     vc = torch.randn(B, Hkv, cap, D, generator=g).to(dtype)
+    # cache slots past the length hold stale data, possibly non-finite: must not leak in
+    kc[:, :, S:] = float('nan')
+    vc[:, :, S:] = float('nan')
     alpha = 0.5 + 1.5 * torch.rand(H, generator=g)
     beta = torch.rand(H, generator=g)
     mu = torch.ones(H)
@@ -273,7 +276,21 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
     _lib.call('motif_b200_gdn_chunk_gated_ws', _lib.ptr(qb), _lib.ptr(kb), _lib.ptr(vb), _lib.ptr(be), _lib.ptr(ge),
               _lib.ptr(si), _lib.ptr(S3), _lib.ptr(out3), B, H, T, dk, dv, _lib.i64_array(strides),
               p.data_ptr() + (C + 2 * H) * 2, N, dv, _lib.ptr(ow), 1e-6, dc, _lib.ptr(ws), ws_bytes, s)
+    # whole layer with a workspace: preparation fused into the UT-transform kernel
+    out4 = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+    co4 = torch.empty(B, 3, C, dtype=dtype, device='cuda')
+    S4 = torch.empty(B, H, dk, dv, device='cuda')
+    _lib.call('motif_b200_gdn_prefill_ws', _lib.ptr(p), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db), _lib.ptr(ci),
+              _lib.ptr(co4), _lib.ptr(si), _lib.ptr(S4), _lib.ptr(ow), 1e-6, _lib.ptr(out4), H * dv, B, T, H, dk, dv,
+              dc, _lib.ptr(ws), ws_bytes, s)
     torch.cuda.synchronize()
+    assert torch.equal(co4, co2)
+    if (dk, dv) == (64, 128):
+        # same preparation roundings, same split kernels: equal to the split call on prepared inputs
+        assert rel_err(out4.float(), out3.float()) < 1e-6, rel_err(out4.float(), out3.float())
+        assert rel_err(S4, S3) < 1e-6, rel_err(S4, S3)
+    else:  # other shapes run the single fused prefill kernel
+        assert torch.equal(out4, out1) and torch.equal(S4, S1)
     assert torch.equal(co1, co2)
     # the split path rounds q e^gamma and k e^(gL - gamma) where the fused kernel rounds the
     # products instead: agreement to the 16-bit operand rounding
