@@ -140,7 +140,7 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t* r, const void* smem)
 // ------------------------------------------------------------------ mbarrier + bulk copy
 // One-dimensional bulk copies (cp.async.bulk, the untiled TMA path) global -> shared with
 // completion counted on an mbarrier by transaction bytes.  Source and destination must be
-// 16-byte aligned and the size a multiple of 16.  No multicast.
+// 16-byte aligned and the size a multiple of 16.  The destination is this CTA only.
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -167,7 +167,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 // Tiled tensor copy of one box at coordinates (x = inner element index, y = row); x * element
-// size must be a multiple of 16 bytes.  No multicast.
+// size must be a multiple of 16 bytes.  The destination is this CTA only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
