@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   const int pos = t0w + tl, h = h0 + hg;
   const bool row_ok = pos < L;
   const int qpos = q_start + pos;
+  // log-n scaling in log2 units (0 for rows past L, which are never stored)
   const float rc = row_ok ? ssmax[h] * log_n[b * st[12] + (int64_t)pos * st[13]] * kLog2e : 0.f;
   const float sr = scale * rc;
 
@@ -478,17 +479,21 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
     if (j + 1 < nmine) fill_bias(j + 1);
 
-    // logits (log2 units): x = (s * scale + bias) * rc for keys c <= cmax, else -inf
+    // logits (log2 units): x = (s * scale + bias) * rc; keys past the row's last visible key
+    // (causal, or at / past S) are set to -inf only on the tiles that contain such keys
     const int k0 = j * tc::kKeys;
-    const int cmax = min(127, min(S - 1 - k0, qpos - k0));
+    const int cmax = min(tc::kKeys - 1, min(S - 1 - k0, qpos - k0));
     const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127;  // key offset c -> tb[-c]
+#pragma unroll
+    for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(x[c], sr, tb[-c] * rc);
+    if (cmax < tc::kKeys - 1) {
+#pragma unroll
+      for (int c = 0; c < tc::kKeys; ++c)
+        if (c > cmax) x[c] = -INFINITY;
+    }
     float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int c = 0; c < tc::kKeys; ++c) {
-      const float v = fmaf(x[c], sr, tb[-c] * rc);
-      x[c] = c <= cmax ? v : -INFINITY;
-      mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
-    }
+    for (int c = 0; c < tc::kKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
     const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
     const float mb = mn == -INFINITY ? 0.f : mn;
     const float corr = ex2_approx(m - mb);
@@ -1516,6 +1521,66 @@ extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const
   });
 }
 
+// Vectorised preparation for 16-bit rows with D in {32, 64, 128}: a group of D/8 lanes owns
+// one (token, slot) row (slot = q head | k head | v head) as 16-byte vectors; the q / k RMS
+// norms reduce over the group's lanes.  A warp walks one token's H + 2 Hkv slots.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) chord_prep_vec_kernel(const T* __restrict__ proj, int64_t ps,
+                                                             const T* __restrict__ qn_w, const T* __restrict__ kn_w,
+                                                             T* __restrict__ qo, T* __restrict__ kc, T* __restrict__ vc,
+                                                             int64_t cap, const int32_t* __restrict__ pos_dev,
+                                                             int64_t pos_host, int64_t rows, int Tn, int H, int Hkv,
+                                                             float eps) {
+  constexpr int LPS = D / 8;       // lanes per slot
+  constexpr int SPI = 32 / LPS;    // slots per warp iteration
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LPS, grp = lane / LPS;
+  const int64_t tok = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (tok >= rows) return;
+  const int b = (int)(tok / Tn), t = (int)(tok % Tn);
+  const int64_t pos = (pos_dev ? (int64_t)*pos_dev : pos_host) + t;
+  const bool pos_ok = pos >= 0 && pos < cap;  // a device-side position past the capacity skips the cache write
+  const int slots = H + 2 * Hkv;
+  const T* src_row = proj + tok * ps;
+  for (int s0 = 0; s0 < slots; s0 += SPI) {
+    const int slot = s0 + grp;
+    const bool act = slot < slots;  // lanes past the last slot still join the reductions
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (act) raw = *reinterpret_cast<const uint4*>(src_row + (int64_t)slot * D + sub * 8);
+    const T* e = reinterpret_cast<const T*>(&raw);
+    float x[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      x[i] = to_f(e[i]);
+      ss += x[i] * x[i];
+    }
+#pragma unroll
+    for (int o2 = 1; o2 < LPS; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+    if (!act) continue;
+    if (slot >= H + Hkv) {  // value: plain copy into the cache
+      if (pos_ok) {
+        const int kvh = slot - H - Hkv;
+        *reinterpret_cast<uint4*>(vc + (((int64_t)b * Hkv + kvh) * cap + pos) * D + sub * 8) = raw;
+      }
+      continue;
+    }
+    const float r = rsqrtf(ss / (float)D + eps);
+    const T* w = (slot < H ? qn_w : kn_w) + sub * 8;
+    const uint4 wr = *reinterpret_cast<const uint4*>(w);
+    const T* we = reinterpret_cast<const T*>(&wr);
+    uint4 outv;
+    T* oe = reinterpret_cast<T*>(&outv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) oe[i] = from_f<T>(to_f(from_f<T>(x[i] * r)) * to_f(we[i]));
+    if (slot < H) {
+      *reinterpret_cast<uint4*>(qo + tok * H * D + (int64_t)slot * D + sub * 8) = outv;
+    } else if (pos_ok) {
+      *reinterpret_cast<uint4*>(kc + (((int64_t)b * Hkv + (slot - H)) * cap + pos) * D + sub * 8) = outv;
+    }
+  }
+}
+
 extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, const void* qn_w, const void* kn_w,
                                      void* q, void* k_cache, void* v_cache, int64_t cap, const int32_t* pos_dev,
                                      int64_t pos_host, int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t D,
@@ -1526,8 +1591,25 @@ extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, cons
              (long long)cap);
   const int64_t rows = B * T;
   if (rows == 0) return MB_OK;
+  const bool vec = dtype != MB_F32 && (D == 32 || D == 64 || D == 128) && proj_stride % 8 == 0 &&
+                   ((uintptr_t)proj | (uintptr_t)qn_w | (uintptr_t)kn_w | (uintptr_t)q | (uintptr_t)k_cache |
+                    (uintptr_t)v_cache) % 16 == 0;
   return dispatch_dtype(dtype, [&](auto t) {
     using Tt = decltype(t);
+    if constexpr (sizeof(Tt) == 2) {
+      if (vec) {
+        auto go = [&](auto dc) {
+          constexpr int DD = decltype(dc)::value;
+          chord_prep_vec_kernel<Tt, DD><<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+              (const Tt*)proj, proj_stride, (const Tt*)qn_w, (const Tt*)kn_w, (Tt*)q, (Tt*)k_cache, (Tt*)v_cache,
+              cap, pos_dev, pos_host, rows, (int)T, (int)H, (int)Hkv, eps);
+          return check_launch("chord_prep");
+        };
+        if (D == 32) return go(std::integral_constant<int, 32>{});
+        if (D == 64) return go(std::integral_constant<int, 64>{});
+        return go(std::integral_constant<int, 128>{});
+      }
+    }
     const int64_t warps = rows * (H + 2 * Hkv);
     chord_prep_kernel<Tt><<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
         (const Tt*)proj, proj_stride, (const Tt*)qn_w, (const Tt*)kn_w, (Tt*)q, (Tt*)k_cache, (Tt*)v_cache, cap,

@@ -612,46 +612,60 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
 
 // GatedRMSNorm on the scan's output rows, in place: o <- rmsnorm(o) * w * silu(gate) for each
 // (token, head) row of DV values (gdn_attn.py:197-209 with rms_norm.py:547-553 roundings).
-// One warp per row; lanes own DV/32 consecutive values, moved as one vector.
+// A warp takes RPW consecutive rows (heads of one token, then the next token), issues all their
+// loads before any arithmetic, and gives each lane DV/32 consecutive values of every row.
 template <typename T, int DV>
 __global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, int64_t ob, int64_t oh, int64_t ol,
                                                             const T* __restrict__ gate, int64_t gate_rs,
                                                             int64_t gate_hs, const T* __restrict__ w, float eps, int H,
                                                             int L, int64_t rows) {
   constexpr int PL = DV / 32;
+  constexpr int RPW = 4;
   using V = typename std::conditional<PL * sizeof(T) == 8, uint2, typename std::conditional<PL * sizeof(T) == 4,
                                                                                              uint32_t, uint4>::type>::type;
   static_assert(sizeof(V) == PL * sizeof(T), "one vector per lane");
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);  // (b * L + l) * H + h
-  if (row >= rows) return;
-  const int h = (int)(row % H);
-  const int64_t bl = row / H;
-  const int l = (int)(bl % L), b = (int)(bl / L);
-  V* orow = reinterpret_cast<V*>(o + b * ob + h * oh + (int64_t)l * ol) + lane;
-  const V gv = reinterpret_cast<const V*>(gate + bl * gate_rs + h * gate_hs)[lane];
+  const int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW;  // (b * L + l) * H + h
   const V wv = reinterpret_cast<const V*>(w)[lane];
-  V ov = *orow;
-  const T* oe = reinterpret_cast<const T*>(&ov);
-  const T* ge = reinterpret_cast<const T*>(&gv);
+  V ov[RPW], gv[RPW];
+  V* op[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    const int64_t row = row0 + j;
+    op[j] = nullptr;
+    if (row < rows) {
+      const int h = (int)(row % H);
+      const int64_t bl = row / H;
+      const int l = (int)(bl % L), b = (int)(bl / L);
+      op[j] = reinterpret_cast<V*>(o + b * ob + h * oh + (int64_t)l * ol) + lane;
+      ov[j] = *op[j];
+      gv[j] = reinterpret_cast<const V*>(gate + bl * gate_rs + h * gate_hs)[lane];
+    }
+  }
   const T* we = reinterpret_cast<const T*>(&wv);
-  float x[PL];
-  float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < PL; ++i) {
-    x[i] = to_f(oe[i]);
-    ss += x[i] * x[i];
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)DV + eps);
-  V res;
-  T* re = reinterpret_cast<T*>(&res);
+  for (int j = 0; j < RPW; ++j) {
+    if (row0 + j >= rows) break;  // warp-uniform
+    const T* oe = reinterpret_cast<const T*>(&ov[j]);
+    const T* ge = reinterpret_cast<const T*>(&gv[j]);
+    float x[PL];
+    float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < PL; ++i) {
-    const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * to_f(we[i])));
-    re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
+    for (int i = 0; i < PL; ++i) {
+      x[i] = to_f(oe[i]);
+      ss += x[i] * x[i];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)DV + eps);
+    V res;
+    T* re = reinterpret_cast<T*>(&res);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * to_f(we[i])));
+      re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
+    }
+    *op[j] = res;
   }
-  *orow = res;
 }
 
 template <typename T, int DK, int DV, bool PREP = false>
@@ -682,7 +696,7 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
   if (rc || gate == nullptr) return rc;
   const int64_t rows = B * L * H;
   const int64_t* st = sv.s;
-  gdn_gate_norm_kernel<T, DV><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(
+  gdn_gate_norm_kernel<T, DV><<<(unsigned)((rows + 31) / 32), 256, 0, stream>>>(
       (T*)o, st[9], st[10], st[11], (const T*)gate, gate_rs, gate_hs, (const T*)onorm_w, eps, (int)H, (int)L, rows);
   return check_launch("gdn_chunk (gated norm)");
 }
