@@ -58,6 +58,12 @@ def kernel_work(name, cfg, B, T):
     dk, dv, D, hid, V = cfg.gdn_dk, cfg.gdn_dv, cfg.head_dim, cfg.mlp_hidden, cfg.vocab_size
     M = B * T
     C = 64
+    if name == 'motif_b200_gdn_prefill_ws':
+        # whole GDN layer from the projections: per token per head the chunked delta rule's
+        # flops; bytes = q, k, v, a, b projection columns in, gate in, gated o out, + state out
+        f_tok = 3 * 2 * C * dk + 2 * 2 * C * dv + 3 * 2 * dk * dv
+        by_tok = 2 * (2 * dk + dv) + 2 * 2 + 2 * dv + 2 * dv
+        return M * H * f_tok, M * H * by_tok + B * H * dk * dv * 4
     if name in ('motif_b200_gdn_chunk_gated', 'motif_b200_gdn_chunk_gated_ws'):
         # per token per head: G1, QK, W (2*C*dk each), U (2*C*dv), WS, qS, K^T X (2*dk*dv each), Aq X (2*C*dv)
         f_tok = 3 * 2 * C * dk + 2 * 2 * C * dv + 3 * 2 * dk * dv
@@ -86,10 +92,14 @@ def kernel_work(name, cfg, B, T):
 # capture of each kernel on a smaller case of the same layer; traffic grows in proportion to the
 # units, so a full launch's traffic is this figure times its units.
 #   gdn_chunk_gated : per token-head, profiles/gdn_chunk_fast_b4_t4096.txt (186.2 MB / 196608)
-#   chord_attention : per token,      profiles/chord_fwd_mma_b4_t4096.txt (39.6 MB / 16384)
+#   gdn_prefill_ws  : per token-head, profiles/gdn_split_b32_t4096.txt, the three kernels of
+#                     one launch at B = 32 (5158 MB / 1572864: the chunk records written and
+#                     read back are most of the excess over the algorithmic bytes)
+#   chord_attention : per token,      profiles/chord_tc_b4_t4096.txt (38.2 MB / 16384)
 NCU_TRAFFIC = {
     'motif_b200_gdn_chunk_gated': (186.15e6 / (4 * 4096 * 12), 'token_head'),
-    'motif_b200_chord_attention': (39.55e6 / (4 * 4096), 'token'),
+    'motif_b200_gdn_prefill_ws': (5158.0e6 / (32 * 4096 * 12), 'token_head'),
+    'motif_b200_chord_attention': (38.19e6 / (4 * 4096), 'token'),
 }
 
 
