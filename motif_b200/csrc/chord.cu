@@ -38,6 +38,17 @@ __device__ __forceinline__ float ggd_bias(float alpha, float beta, float mu, flo
   return -alpha * powf(fabsf(-delta - mu) + eps, beta);
 }
 
+// GGD bias in the tensor-core kernels: 16-bit inputs use exp2(beta * log2(x)) on the fast log2 (the
+// result's relative error, a few 1e-7, is far below bf16 / fp16 resolution); fp32 keeps powf.
+template <typename T>
+__device__ __forceinline__ float ggd_bias_decode(float alpha, float beta, float mu, float delta, float eps) {
+  if constexpr (sizeof(T) == 2) {
+    return -alpha * exp2f(beta * __log2f(fabsf(-delta - mu) + eps));
+  } else {
+    return ggd_bias(alpha, beta, mu, delta, eps);
+  }
+}
+
 // ------------------------------------------------------------------ tensor-core prefill
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(128) chord_fwd_mma_kernel(
@@ -415,7 +426,7 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     for (int e = wt; e < G * TBL; e += 128) {
       const int g = e / TBL, ee = e % TBL;
       const int hh = h0 + g;
-      tb[g * TBLS + ee] = ggd_bias(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
+      tb[g * TBLS + ee] = ggd_bias_decode<T>(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
     }
   };
 
@@ -673,17 +684,6 @@ __global__ void __launch_bounds__(128) chord_fwd_simple_kernel(
 //   softmax + PV warp w owns rows w, w+4, ...; online softmax over the tile, then each lane
 //                accumulates D/32 output dims over the tile's keys.
 // Partials: ws[((split * B + b) * H + h) * Tn + t][D + 2] = (o[0..D), m, l) for the merge.
-// GGD bias in the decode kernel: 16-bit inputs use exp2(beta * log2(x)) on the fast log2 (the
-// result's relative error, a few 1e-7, is far below bf16 / fp16 resolution); fp32 keeps powf.
-template <typename T>
-__device__ __forceinline__ float ggd_bias_decode(float alpha, float beta, float mu, float delta, float eps) {
-  if constexpr (sizeof(T) == 2) {
-    return -alpha * exp2f(beta * __log2f(fabsf(-delta - mu) + eps));
-  } else {
-    return ggd_bias(alpha, beta, mu, delta, eps);
-  }
-}
-
 constexpr int kDecTile = 64;
 // MOTIF_B200_DECODE_SCALAR=1 routes 16-bit D = 64 decode through the CUDA-core kernel (the
 // tensor-core kernel is the default); used to cross-check the two in tests.

@@ -22,6 +22,7 @@
 //
 // Products are 16-bit m16n8k16 tensor-core MMAs with fp32 accumulation, the same operand
 // roundings as the fused kernel (gdn_fast.cu), which stays the path without a workspace.
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -612,59 +613,55 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
 
 // GatedRMSNorm on the scan's output rows, in place: o <- rmsnorm(o) * w * silu(gate) for each
 // (token, head) row of DV values (gdn_attn.py:197-209 with rms_norm.py:547-553 roundings).
-// A warp takes RPW consecutive rows (heads of one token, then the next token), issues all their
-// loads before any arithmetic, and gives each lane DV/32 consecutive values of every row.
+// A group of DV/8 lanes owns a row as 16-byte vectors (the row's sum of squares reduces over
+// the group); a grid-stride loop walks the rows, so each thread keeps several rows of loads in
+// flight across iterations.
 template <typename T, int DV>
 __global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, int64_t ob, int64_t oh, int64_t ol,
                                                             const T* __restrict__ gate, int64_t gate_rs,
                                                             int64_t gate_hs, const T* __restrict__ w, float eps, int H,
                                                             int L, int64_t rows) {
-  constexpr int PL = DV / 32;
-  constexpr int RPW = 4;
-  using V = typename std::conditional<PL * sizeof(T) == 8, uint2, typename std::conditional<PL * sizeof(T) == 4,
-                                                                                             uint32_t, uint4>::type>::type;
-  static_assert(sizeof(V) == PL * sizeof(T), "one vector per lane");
+  constexpr int LPR = DV / 8;  // lanes per row
+  constexpr int RPW = 32 / LPR;
   const int lane = threadIdx.x & 31;
-  const int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW;  // (b * L + l) * H + h
-  const V wv = reinterpret_cast<const V*>(w)[lane];
-  V ov[RPW], gv[RPW];
-  V* op[RPW];
-#pragma unroll
-  for (int j = 0; j < RPW; ++j) {
-    const int64_t row = row0 + j;
-    op[j] = nullptr;
-    if (row < rows) {
+  const int sub = lane % LPR;
+  const uint4 wv = reinterpret_cast<const uint4*>(w)[sub];
+  const T* we = reinterpret_cast<const T*>(&wv);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t wi = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi * RPW < rows; wi += warps) {
+    const int64_t row = wi * RPW + lane / LPR;  // (b * L + l) * H + h
+    const bool ok = row < rows;
+    uint4* op = nullptr;
+    uint4 ov = make_uint4(0, 0, 0, 0), gv = make_uint4(0, 0, 0, 0);
+    if (ok) {
       const int h = (int)(row % H);
       const int64_t bl = row / H;
       const int l = (int)(bl % L), b = (int)(bl / L);
-      op[j] = reinterpret_cast<V*>(o + b * ob + h * oh + (int64_t)l * ol) + lane;
-      ov[j] = *op[j];
-      gv[j] = reinterpret_cast<const V*>(gate + bl * gate_rs + h * gate_hs)[lane];
+      op = reinterpret_cast<uint4*>(o + b * ob + h * oh + (int64_t)l * ol) + sub;
+      ov = *op;
+      gv = reinterpret_cast<const uint4*>(gate + bl * gate_rs + h * gate_hs)[sub];
     }
-  }
-  const T* we = reinterpret_cast<const T*>(&wv);
-#pragma unroll
-  for (int j = 0; j < RPW; ++j) {
-    if (row0 + j >= rows) break;  // warp-uniform
-    const T* oe = reinterpret_cast<const T*>(&ov[j]);
-    const T* ge = reinterpret_cast<const T*>(&gv[j]);
-    float x[PL];
+    const T* oe = reinterpret_cast<const T*>(&ov);
+    const T* ge = reinterpret_cast<const T*>(&gv);
+    float x[8];
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < PL; ++i) {
+    for (int i = 0; i < 8; ++i) {
       x[i] = to_f(oe[i]);
       ss += x[i] * x[i];
     }
-    ss = warp_sum(ss);
+#pragma unroll
+    for (int o2 = 1; o2 < LPR; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+    if (!ok) continue;
     const float r = rsqrtf(ss / (float)DV + eps);
-    V res;
+    uint4 res;
     T* re = reinterpret_cast<T*>(&res);
 #pragma unroll
-    for (int i = 0; i < PL; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * to_f(we[i])));
       re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
     }
-    *op[j] = res;
+    *op = res;
   }
 }
 
@@ -696,7 +693,9 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
   if (rc || gate == nullptr) return rc;
   const int64_t rows = B * L * H;
   const int64_t* st = sv.s;
-  gdn_gate_norm_kernel<T, DV><<<(unsigned)((rows + 31) / 32), 256, 0, stream>>>(
+  const int64_t warps_needed = (rows + (256 / DV) - 1) / (256 / DV);  // DV/8 lanes per row
+  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, 148 * 16);
+  gdn_gate_norm_kernel<T, DV><<<(unsigned)blocks, 256, 0, stream>>>(
       (T*)o, st[9], st[10], st[11], (const T*)gate, gate_rs, gate_hs, (const T*)onorm_w, eps, (int)H, (int)L, rows);
   return check_launch("gdn_chunk (gated norm)");
 }
@@ -733,7 +732,7 @@ int gdn_split_dispatch(int dtype, int64_t Dk, int64_t Dv, const void* q, const v
   if (need == 0 || ws == nullptr || ws_bytes < need || ((uintptr_t)ws & 15) || L == 0) return 0;
   if (strides[11] % 2 || strides[9] % 2 || strides[10] % 2 || ((uintptr_t)o & 3)) return 0;
   {  // the gated norm moves Dv / 32 values per lane as one vector
-    const int64_t vec = Dv / 32, vb = vec * 2;
+    const int64_t vec = 8, vb = 16;
     if (gate && (gate_rs % vec || gate_hs % vec || strides[9] % vec || strides[10] % vec || strides[11] % vec ||
                  (uintptr_t)gate % vb || (uintptr_t)o % vb || (uintptr_t)onorm_w % vb))
       return 0;
@@ -768,8 +767,8 @@ int gdn_prefill_split_dispatch(const void* proj, int64_t ps, const void* conv_w,
   if (!(Dk == 64 && Dv == 128)) return 0;
   const int64_t C = H * (2 * Dk + Dv);
   if (ps % 8 || (uintptr_t)proj % 16 || (uintptr_t)conv_w % 16 || (conv_in && (uintptr_t)conv_in % 16) ||
-      (conv_out && (uintptr_t)conv_out % 16) || os % 4 || (uintptr_t)out % 8 || (uintptr_t)onorm_w % 8 || C % 8 ||
-      (C + 2 * H) % 4)
+      (conv_out && (uintptr_t)conv_out % 16) || os % 8 || (uintptr_t)out % 16 || (uintptr_t)onorm_w % 16 ||
+      C % 8 || (C + 2 * H) % 8)
     return 0;
   Strides18 sv;
   for (int i = 0; i < 18; ++i) sv.s[i] = 0;

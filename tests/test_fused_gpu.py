@@ -285,11 +285,13 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
               dc, _lib.ptr(ws), ws_bytes, s)
     torch.cuda.synchronize()
     assert torch.equal(co4, co2)
-    if (dk, dv) == (64, 128):
+    if (dk, dv) == (64, 128) and (C + 2 * H) % 8 == 0:
         # same preparation roundings, same split kernels: equal to the split call on prepared inputs
+        # (the split prefill takes gate columns on 16-byte boundaries; otherwise it runs the
+        # single fused kernel)
         assert rel_err(out4.float(), out3.float()) < 1e-6, rel_err(out4.float(), out3.float())
         assert rel_err(S4, S3) < 1e-6, rel_err(S4, S3)
-    else:  # other shapes run the single fused prefill kernel
+    else:  # other shapes / alignments run the single fused prefill kernel
         assert torch.equal(out4, out1) and torch.equal(S4, S1)
     assert torch.equal(co1, co2)
     # the split path rounds q e^gamma and k e^(gL - gamma) where the fused kernel rounds the
