@@ -382,14 +382,25 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
     constexpr int E = 16 / sizeof(T);
     T* rqs = reinterpret_cast<T*>(rec + Rec::off_qs);
     T* rkd = reinterpret_cast<T*>(rec + Rec::off_kd);
-    constexpr int QP = DK / 2;  // element pairs per q / k row
+    constexpr int QV = DK / E;  // 16-byte vectors per q / k row
     const float gl = sGam[C - 1];
-    for (int i = tid; i < C * QP; i += NT) {
-      const int r = i / QP, c = 2 * (i % QP);
+    for (int i = tid; i < C * QV; i += NT) {
+      const int r = i / QV, c = (i % QV) * E;
       const float eq = sEg[r], ek = __expf(gl - sGam[r]);
-      const float2 xq = ld2(&cQ[r * QS + c]), xk = ld2(&cK[r * QS + c]);
-      st2(&rqs[r * QS + c], xq.x * eq, xq.y * eq);
-      st2(&rkd[r * QS + c], xk.x * ek, xk.y * ek);
+      const uint4 vq = *reinterpret_cast<const uint4*>(&cQ[r * QS + c]);
+      const uint4 vk = *reinterpret_cast<const uint4*>(&cK[r * QS + c]);
+      const T* eqv = reinterpret_cast<const T*>(&vq);
+      const T* ekv = reinterpret_cast<const T*>(&vk);
+      uint4 oq, ok;
+      T* oqe = reinterpret_cast<T*>(&oq);
+      T* oke = reinterpret_cast<T*>(&ok);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        oqe[e] = from_f<T>(to_f(eqv[e]) * eq);
+        oke[e] = from_f<T>(to_f(ekv[e]) * ek);
+      }
+      *reinterpret_cast<uint4*>(&rqs[r * QS + c]) = oq;
+      *reinterpret_cast<uint4*>(&rkd[r * QS + c]) = ok;
     }
     constexpr int XV = (DK + DV) / E, AV = C / E;
     T* rwu = reinterpret_cast<T*>(rec + Rec::off_wu);
