@@ -309,3 +309,46 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
     ref = oo.gated_rms_norm(torch.cat([o.transpose(1, 2), gate], -1), onw.float()).reshape(M, H * dv)
     assert rel_err(out1.float(), ref) < 3e-2, rel_err(out1.float(), ref)
     assert rel_err(S1, S) < 2e-2, rel_err(S1, S)
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize('M,N,K', [(1, 768, 768), (7, 8728, 768), (64, 768, 3584), (64, 6016, 768),
+                                   (33, 768, 2048), (64, 32000, 768), (5, 100, 40)])
+def test_skinny_gemm_vs_torch(dtype, M, N, K):
+    g = torch.Generator().manual_seed(M + N + K)
+    x = (0.5 * torch.randn(M, K, generator=g)).to(dtype).cuda()
+    w = (0.05 * torch.randn(N, K, generator=g)).to(dtype).cuda()
+    ref = x.float() @ w.float().t()
+    nbytes = _lib.load().motif_b200_skinny_gemm_workspace_bytes(M, N, K)
+    ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device='cuda')
+    for _ in range(2):  # the workspace counters must come back to zero
+        y = torch.empty(M, N, dtype=dtype, device='cuda')
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K,
+                  _lib.dtype_code(dtype), ws.data_ptr(), nbytes, st())
+        assert rel_err(y.float(), ref) < 1e-2, rel_err(y.float(), ref)
+    if nbytes:
+        assert int(ws[:32768].sum()) == 0  # the counter region is left zeroed
+
+
+def test_skinny_gemm_shared_workspace_across_shapes():
+    """Calls of different shapes share one workspace (as the model's decode step does)."""
+    g = torch.Generator().manual_seed(3)
+    shapes = [(2, 768, 3584), (2, 6016, 768), (2, 768, 2048), (2, 8728, 768), (2, 768, 3584)]
+    nbytes = max(_lib.load().motif_b200_skinny_gemm_workspace_bytes(*s) for s in shapes)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device='cuda')
+    for M, N, K in shapes * 2:
+        x = torch.randn(M, K, generator=g).bfloat16().cuda()
+        w = (0.05 * torch.randn(N, K, generator=g)).bfloat16().cuda()
+        y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K,
+                  _lib.MB_BF16, ws.data_ptr(), nbytes, st())
+        assert rel_err(y.float(), x.float() @ w.float().t()) < 1e-2
+
+
+def test_skinny_gemm_rejects_bad_shapes():
+    x = torch.zeros(65, 64, dtype=torch.bfloat16, device='cuda')
+    w = torch.zeros(64, 64, dtype=torch.bfloat16, device='cuda')
+    y = torch.zeros(65, 64, dtype=torch.bfloat16, device='cuda')
+    with pytest.raises(ValueError):  # M > 64
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, w.data_ptr(), 64, y.data_ptr(), 64, 65, 64, 64,
+                  _lib.MB_BF16, None, 0, st())
