@@ -418,7 +418,10 @@ class MotifChordModel(nn.Module):
 
 
 # ============================================================================ engine
-SKINNY_MAX_M = 64
+# Largest M routed to motif_b200_skinny_gemm.  0: every product runs on cuBLAS — the skinny
+# kernel is correct (tests) but measured slower than cuBLAS at decode sizes (30-48 us vs
+# ~8 us per product at M = 64), so the model does not use it.
+SKINNY_MAX_M = 0
 _SKINNY_WS: Dict[int, torch.Tensor] = {}
 
 
