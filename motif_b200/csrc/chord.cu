@@ -375,8 +375,15 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   const bool row_ok = pos < L;
   const int qpos = q_start + pos;
   // log-n scaling in log2 units (0 for rows past L, which are never stored)
-  const float rc = row_ok ? ssmax[h] * log_n[b * st[12] + (int64_t)pos * st[13]] * kLog2e : 0.f;
-  const float sr = scale * rc;
+  // logit (log2 units) = (s * scale + bias) * rc with rc = ssmax * log n * log2 e.  The sign of
+  // ssmax (per head) is folded into scale and the bias table, so the row keeps x = +-(s * scale
+  // + bias), its running max in those units, and applies |rc| inside the exponent.  |rc| = 0
+  // (log 1 = 0 at the first position, or a row past L) becomes 1e-30: every visible key then
+  // gets the same weight, and masked keys (-inf) still get none.
+  const float ssh = ssmax[h];
+  const float sgn = ssh < 0.f ? -1.f : 1.f;
+  const float rcs = row_ok ? fmaxf(fabsf(ssh * log_n[b * st[12] + (int64_t)pos * st[13]] * kLog2e), 1e-30f) : 1e-30f;
+  const float scale_s = sgn * scale;
 
   unsigned char* sQw = sQ + wg * tc::kTileBytes;
   unsigned char* sPw = sm + Lay::offP + wg * 2 * tc::kTileBytes;
@@ -426,7 +433,8 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     for (int e = wt; e < G * TBL; e += 128) {
       const int g = e / TBL, ee = e % TBL;
       const int hh = h0 + g;
-      tb[g * TBLS + ee] = ggd_bias_decode<T>(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
+      const float b0 = ggd_bias_decode<T>(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
+      tb[g * TBLS + ee] = ssmax[hh] < 0.f ? -b0 : b0;
     }
   };
 
@@ -490,13 +498,13 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
     if (j + 1 < nmine) fill_bias(j + 1);
 
-    // logits (log2 units): x = (s * scale + bias) * rc; keys past the row's last visible key
+    // x = +-(s * scale + bias) (sign of ssmax folded in); keys past the row's last visible key
     // (causal, or at / past S) are set to -inf only on the tiles that contain such keys
     const int k0 = j * tc::kKeys;
     const int cmax = min(tc::kKeys - 1, min(S - 1 - k0, qpos - k0));
     const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127;  // key offset c -> tb[-c]
 #pragma unroll
-    for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(x[c], sr, tb[-c] * rc);
+    for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(x[c], scale_s, tb[-c]);
     if (cmax < tc::kKeys - 1) {
 #pragma unroll
       for (int c = 0; c < tc::kKeys; ++c)
@@ -507,7 +515,8 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     for (int c = 0; c < tc::kKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
     const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
     const float mb = mn == -INFINITY ? 0.f : mn;
-    const float corr = ex2_approx(m - mb);
+    const float corr = ex2_approx((m - mb) * rcs);
+    const float nb = -mb * rcs;
     m = mn;
     float ps4[4] = {0.f, 0.f, 0.f, 0.f};
     // P row -> shared memory, swizzled: key chunk cc (8 keys) in atom cc / 8 at 16-byte slot
@@ -517,7 +526,8 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float p0 = ex2_approx(x[cc * 8 + 2 * e] - mb), p1 = ex2_approx(x[cc * 8 + 2 * e + 1] - mb);
+        const float p0 = ex2_approx(fmaf(x[cc * 8 + 2 * e], rcs, nb));
+        const float p1 = ex2_approx(fmaf(x[cc * 8 + 2 * e + 1], rcs, nb));
         ps4[e] += p0 + p1;
         w[e] = pack2<T>(p0, p1);
       }

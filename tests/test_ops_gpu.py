@@ -199,6 +199,17 @@ def test_chord_tcgen05_matches_mma_sync(ops, monkeypatch, B, H, Hkv, L, S):
     assert rel_err(tc.float(), ms.float()) < 1e-2
 
 
+@pytest.mark.parametrize('L,S', [(200, 200), (70, 330)])
+def test_chord_16bit_negative_ssmax(ops, L, S):
+    """ssmax < 0 on some heads flips those heads' logits; first positions have log n = 0."""
+    q, k, v, alpha, beta, mu, ssmax, log_n, qs = chord_inputs(2, 12, 3, L, S, 64, seed=L + S, dtype=torch.bfloat16)
+    ssmax = ssmax.clone()
+    ssmax[::3] *= -1.0
+    ref = oo.chord_attention(q.float(), k.float(), v.float(), alpha, beta, mu, ssmax, log_n, qs)
+    out = ops.apply_chord_attention(*cuda(q, k, v, alpha, beta, mu, ssmax, log_n))
+    assert rel_err(out.float(), ref) < 1e-2, rel_err(out.float(), ref)
+
+
 def test_chord_op_config_subset(ops):
     """Config 3 (B=8, H=12, T=4096, D=64, bf16): full-size kernel, oracle on two (b, h) slices."""
     B, H, L, D = 8, 12, 4096, 64
