@@ -293,6 +293,22 @@ MB_API int motif_b200_gate_residual(const void* a, int64_t a_stride, const void*
 MB_API int motif_b200_argmax(const void* logits, int64_t rows, int64_t V, int64_t row_stride,
                       int64_t* ids, int dtype, void* stream);
 
+/* One sampled token per row (Sampler.__call__, motif/model/sampler.py:151-219, without the
+ * grammar constraint, whose mask the caller applies to the logits first): repetition penalty
+ * over the distinct ids of history[r, :hist_len] (negative ids ignored) -> temperature
+ * (x / max(T, 1e-5) when T != 1) -> top-k (top_k <= 0: off) -> top-p (p outside (0, 1):
+ * off) -> softmax -> draw.  The draw takes uniforms[r] in [0, 1) when `uniforms` is given,
+ * else Philox4x32-10 with key `seed` and counter (r, 0, offset + *offset_dev) (offset_dev may
+ * be NULL); the token is the first index whose inclusive cumulative probability exceeds
+ * u * total.  out: B int64 (-1 for a row with no finite logit); probs_out (optional, fp32
+ * [B, probs_ld]) receives the final distribution.  V <= 53248 (MB_ERR_UNSUPPORTED above).
+ * `logits` has row stride ld (elements) and dtype `dtype`. */
+MB_API int motif_b200_sample(const void* logits, int64_t ld, int64_t B, int64_t V, const int64_t* history,
+                      int64_t hist_ld, int64_t hist_len, float repetition_penalty, float temperature,
+                      int64_t top_k, float top_p, const float* uniforms, uint64_t seed, uint64_t offset,
+                      const int64_t* offset_dev, int64_t* out, float* probs_out, int64_t probs_ld,
+                      int dtype, void* stream);
+
 /* Token embedding gather: out[r] = table[ids[r]] ([V, D] rows), motif/model/motif.py:604. */
 MB_API int motif_b200_embed(const int64_t* ids, const void* table, void* out, int64_t rows, int64_t D,
                      int64_t V, int dtype, void* stream);

@@ -56,6 +56,8 @@ SIGNATURES = {
     'motif_b200_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
     'motif_b200_argmax': (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
     'motif_b200_embed': (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    'motif_b200_sample': (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _F, _F, _I64, _F, _P, ctypes.c_uint64,
+                               ctypes.c_uint64, _P, _P, _P, _I64, _I, _P]),
     'motif_b200_wait_timeouts': (_I, [_P]),
     'motif_b200_skinny_gemm_workspace_bytes': (_I64, [_I64, _I64, _I64]),
     'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _I64, _P]),

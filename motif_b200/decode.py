@@ -1,11 +1,12 @@
-"""Batched greedy decode as a replayed CUDA graph.
+"""Batched decode as a replayed CUDA graph (greedy, or sampled on the device).
 
 `Generation.step` (`motif/model/generate.py:138-171`) runs one `MotifChordModel.forward`
 per new token: at L = 1 every layer is a handful of small launches, so a Python-driven loop
 is launch-bound.  `GraphDecoder` captures ONE decode step — embed, for each decoder the
 attn-res read, packed projection GEMM, GDN recurrent update (`motif_b200_gdn_decode`) or
 Chord cache append + split-KV attention (`motif_b200_chord_prep` / `_chord_decode`), MLP,
-residual GEMMs, then lm_head and the greedy argmax — and replays it once per token.
+residual GEMMs, then lm_head and the greedy argmax (or the sampling kernel) — and replays it
+once per token.
 
 Positions live on the device: `lens = [pos, pos + 1]` (int32) is read by the Chord kernels
 (cache write position, attended length) and advanced by the graph itself, and the argmax
@@ -16,6 +17,13 @@ cannot regrow them); the GDN recurrent and conv states are updated in place.
 The math is the eager T = 1 path's: the same kernels in the same order, except that the
 split-KV count is fixed at capture (from the cache capacity) instead of chosen per length;
 with `model.decode_splits` set, graph and eager decode give identical tokens.
+
+With a `motif_b200.sampler.Sampler` (no grammar constraint: its hooks run on the host), the
+argmax is replaced by `motif_b200_sample`: the Philox offset is the sampler's offset plus the
+device step counter, and the repetition-penalty history is a device buffer [B, start + 1 +
+max_steps] holding the sequence so far (-1 past its end; the kernel ignores negative ids),
+into which each step writes the token it feeds.  The sampled stream is the one the eager
+`Generation` loop draws with the same sampler.
 """
 
 from typing import List, Optional, Tuple
@@ -82,7 +90,7 @@ class GraphDecoder:
     host-side lengths are advanced by the steps taken, so the eager API can continue from it.
     """
 
-    def __init__(self, model, cache: ModelCache, max_steps: int, splits: Optional[int] = None):
+    def __init__(self, model, cache: ModelCache, max_steps: int, splits: Optional[int] = None, sampler=None):
         if model.training:
             raise ValueError('GraphDecoder needs an eval-mode model')
         w = model.embed.weight
@@ -118,6 +126,20 @@ class GraphDecoder:
         self.step_idx = torch.zeros((1,), dtype=torch.int64, device=self.dev)
         self.ids = torch.zeros((self.B,), dtype=torch.int64, device=self.dev)
         self.tokens = torch.zeros((self.max_steps, self.B), dtype=torch.int64, device=self.dev)
+        self.sampler = None
+        self.hist = None
+        if sampler is not None:
+            from .sampler import Sampler
+            if not isinstance(sampler, Sampler):
+                raise TypeError('GraphDecoder samples with a motif_b200.sampler.Sampler')
+            if sampler.constraint is not None:
+                raise NotImplementedError('a grammar constraint runs host hooks every step: use the eager loop')
+            self.sampler = sampler
+            self.sample_base = sampler.offset
+            if sampler.repetition_penalty != 1.0:
+                self.hist = torch.full((self.B, self.start + 1 + self.max_steps), -1, dtype=torch.int64,
+                                       device=self.dev)
+                self.hist_col = torch.tensor([self.start], dtype=torch.int64, device=self.dev)
         self.launches_per_step = 0
         self.graph = None
         self._capture()
@@ -157,8 +179,22 @@ class GraphDecoder:
                                                              model.blocks[b + 1].features[0].attn_norm.eps))
             x = x_next
         logits = _mm(hn, self.lm)
-        _lib.call('motif_b200_argmax', _lib.ptr(logits), B, cfg.vocab_size, logits.stride(0), _lib.ptr(self.ids),
-                  dc, st)
+        sp = self.sampler
+        if sp is None:
+            _lib.call('motif_b200_argmax', _lib.ptr(logits), B, cfg.vocab_size, logits.stride(0),
+                      _lib.ptr(self.ids), dc, st)
+        else:
+            hist_len = 0
+            if self.hist is not None:
+                self.hist.index_copy_(1, self.hist_col, self.ids.view(B, 1))
+                self.hist_col.add_(1)
+                hist_len = self.hist.shape[1]
+            _lib.call('motif_b200_sample', _lib.ptr(logits), logits.stride(0), B, cfg.vocab_size,
+                      _lib.ptr(self.hist), hist_len, hist_len, float(sp.repetition_penalty), float(sp.temperature),
+                      int(sp.top_k) if sp.top_k is not None else 0,
+                      float(sp.top_p) if sp.top_p is not None else 1.0, None, sp.seed & (2 ** 64 - 1),
+                      self.sample_base & (2 ** 64 - 1), _lib.ptr(self.step_idx), _lib.ptr(self.ids), None, 0,
+                      dc, st)
         self.tokens.index_copy_(0, self.step_idx, self.ids.view(1, B))
         self.step_idx.add_(1)
         self.lens.add_(1)
@@ -203,12 +239,16 @@ class GraphDecoder:
 
     # ------------------------------------------------------------------ capture / replay
     def _snapshot(self):
-        return [s.state.clone() for s in self.gdn], [s.conv.clone() for s in self.gdn]
+        hist = None if self.hist is None else (self.hist.clone(), self.hist_col.clone())
+        return [s.state.clone() for s in self.gdn], [s.conv.clone() for s in self.gdn], hist
 
     def _restore(self, snap):
         for s, st_, cv in zip(self.gdn, snap[0], snap[1]):
             s.state.copy_(st_)
             s.conv.copy_(cv)
+        if snap[2] is not None:
+            self.hist.copy_(snap[2][0])
+            self.hist_col.copy_(snap[2][1])
 
     def _capture(self):
         # The warm-up step (required before capture: cuBLAS handles, lazy library load) and the
@@ -235,19 +275,31 @@ class GraphDecoder:
         self.step_idx.zero_()
         self.taken = 0
 
-    def run(self, first_ids: torch.Tensor, steps: int) -> torch.Tensor:
-        """Replay `steps` decode steps from the current position; returns [B, steps] tokens."""
+    def run(self, first_ids: torch.Tensor, steps: int, history: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Replay `steps` decode steps from the current position; returns [B, steps] tokens.
+
+        With a sampler that applies a repetition penalty, `history` ([B, start + 1], the
+        sequence so far ending with `first_ids`, as `Generation.sequences`) seeds the penalty
+        on the first run; without it the penalty sees only the tokens fed by the graph."""
         steps = int(steps)
         if steps < 0 or self.taken + steps > self.max_steps:
             raise ValueError(f'{steps} steps after {self.taken} exceed max_steps={self.max_steps}')
         ids = first_ids.reshape(-1)
         if ids.numel() != self.B:
             raise ValueError(f'first_ids holds {ids.numel()} ids for a batch of {self.B}')
+        if history is not None and self.hist is not None:
+            if self.taken:
+                raise ValueError('history seeds the first run only')
+            if tuple(history.shape) != (self.B, self.start + 1):
+                raise ValueError(f'history must be [{self.B}, {self.start + 1}], got {tuple(history.shape)}')
+            self.hist[:, :self.start + 1].copy_(history.to(self.dev, torch.int64))
         self.ids.copy_(ids.to(self.dev, torch.int64), non_blocking=True)
         lo = self.taken
         for _ in range(steps):
             self.graph.replay()
         self.taken += steps
+        if self.sampler is not None:
+            self.sampler.offset = self.sample_base + self.taken
         for lc in self.kv:
             lc.length = self.start + self.taken
         for s in self.gdn:

@@ -9,7 +9,8 @@ changes nothing for an already-imported layer: the patch targets are the importi
                                                chunk_gated_delta_rule_triton, GatedRMSNorm
     motif/block/decoder.py:12-13               apply_block_attn_res, RMSNorm
     motif/block/mlp.py:4                       SwiGLU (bound as SwiGLUOp)
-    motif/model/motif.py:23                    RMSNorm
+    motif/model/motif.py:22-23                 Sampler, make_sampler, RMSNorm
+    motif/model/sampler.py                     Sampler, make_sampler (the device sampler)
     motif/ops/__init__.py                      every name above, for later importers
 
 Functions take effect at once for existing layers; classes (RMSNorm, GatedRMSNorm, SwiGLU)
@@ -43,6 +44,10 @@ TARGETS: List[Tuple[str, str, str]] = [
     ('motif.block.decoder', 'RMSNorm', 'RMSNorm'),
     ('motif.block.mlp', 'SwiGLUOp', 'SwiGLU'),
     ('motif.model.motif', 'RMSNorm', 'RMSNorm'),
+    ('motif.model.motif', 'Sampler', 'Sampler'),
+    ('motif.model.motif', 'make_sampler', 'make_sampler'),
+    ('motif.model.sampler', 'Sampler', 'Sampler'),
+    ('motif.model.sampler', 'make_sampler', 'make_sampler'),
 ]
 
 _saved: Dict[Tuple[str, str], object] = {}

@@ -36,6 +36,7 @@ from .cache import (AttnResCache, BasicLayerCache, DecoderBlockCache, GatedDelta
                     KVLayerCache, ModelCache, build_cache)
 from .config import CHUNK_SIZE, CONV_SIZE, EXPAND_V, GGD_EPS, NORM_EPS, MotifChordConfig
 from .ops import GatedRMSNorm, RMSNorm, SwiGLU as SwiGLUOp
+from .sampler import Sampler, make_sampler
 
 
 # ============================================================================ modules
@@ -225,9 +226,9 @@ class ModelOutput:
         return greedy_next(last)
 
     def set_sampler(self, sampler=None, **kwargs):
-        if kwargs:
-            raise NotImplementedError('only a ready sampler callable can be bound (sampling kernels are not built)')
-        self.sampler = sampler
+        """Bind a sampler to this output (`motif.py:100-131`): a ready one, or one built from
+        `Sampler` keyword arguments; no arguments unbinds (greedy)."""
+        self.sampler = make_sampler(sampler, **kwargs)
         return self
 
     def reset_caches(self):
@@ -369,9 +370,8 @@ class MotifChordModel(nn.Module):
         return build_cache(self, use_attn=use_attn, functional=functional, wide_kv=wide_kv)
 
     def set_sampler(self, sampler=None, **kwargs):
-        if kwargs:
-            raise NotImplementedError('only a ready sampler callable can be bound (sampling kernels are not built)')
-        self.sampler = sampler
+        """Model-level sampler carried by every later `ModelOutput` (`motif.py:457-482`)."""
+        self.sampler = make_sampler(sampler, **kwargs)
         return self
 
     def generate(self, input_ids, max_new_tokens: int = 32, eos_token_id=None, sampler=None, cache=None,

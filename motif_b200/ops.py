@@ -13,6 +13,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
+from .sampler import Sampler, make_sampler  # noqa: F401  (install targets)
 
 __all__ = [
     'RMSNorm', 'GatedRMSNorm', 'SwiGLU', 'apply_chord_attention', 'HAS_TRITON',

@@ -94,6 +94,7 @@ def eager_chord_reference(q, k, v, alpha, beta, mu, ssmax, q_start):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True, help='reference source tree (contains motif/)')
+    ap.add_argument('--only', nargs='*', default=None, help='write only these fixtures (default: all)')
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     sys.path.insert(0, REPO)
@@ -175,7 +176,38 @@ def main():
                        pos_argmax=lg[0].argmax(-1), pos_lse=torch.logsumexp(lg[0], -1),
                        pos_sumsq=lg[0].pow(2).sum(-1), greedy=gen_ids)
 
+    # --- sampler: the filtered distribution the reference draws from -------------------
+    # (repetition penalty -> temperature -> top-k -> top-p -> softmax, model/sampler.py:151-219);
+    # torch.multinomial is wrapped to record the probabilities it is given.
+    from motif.model.sampler import Sampler
+    gen = _gen(40)
+    V = 1000
+    logits = torch.randn(4, V, generator=gen) * 3.0
+    hist = torch.randint(0, V, (4, 50), generator=gen)
+    cases = [(0.7, 50, 0.9, 1.15), (1.0, -1, 0.5, 1.0), (1.3, 10, -1.0, 1.3), (0.5, -1, -1.0, 1.15),
+             (1.0, 1, -1.0, 1.0), (0.9, 200, 0.95, 1.05)]
+    seen = {}
+    real_multinomial = torch.multinomial
+
+    def recording_multinomial(p, num_samples, *a, **kw):
+        seen['p'] = p.detach().clone()
+        return real_multinomial(p, num_samples, *a, **kw)
+
+    torch.multinomial = recording_multinomial
+    try:
+        probs = []
+        for t, k, p_, rp in cases:
+            Sampler(temperature=t, top_k=None if k < 0 else k, top_p=None if p_ < 0 else p_,
+                    repetition_penalty=rp)(logits, hist)
+            probs.append(seen['p'])
+    finally:
+        torch.multinomial = real_multinomial
+    out['sampler'] = dict(logits=logits, hist=hist, cases=torch.tensor(cases, dtype=torch.float64),
+                          probs=torch.stack(probs))
+
     for name, d in out.items():
+        if args.only is not None and name not in args.only:
+            continue
         path = os.path.join(HERE, f'{name}.pt')
         torch.save({k: (v.contiguous() if isinstance(v, torch.Tensor) else v) for k, v in d.items()}, path)
         print(f'wrote {path} ({os.path.getsize(path) / 1024:.1f} KiB)')

@@ -135,3 +135,32 @@ def test_random_filled_cache_decode_172m_shapes():
     assert toks.shape == (B, steps)
     assert int(toks.min()) >= 0 and int(toks.max()) < m.config.vocab_size
     assert all(lc.length == L + steps for bc in cache for lc in bc.attn)
+
+
+@pytest.mark.parametrize('rp', [1.0, 1.3])
+def test_graph_sampled_matches_eager_generation(rp):
+    """Sampled decode: the graph (Philox offset = sampler offset + device step counter, device
+    history buffer for the penalty) draws the same tokens as the eager `Generation` loop with
+    an identically seeded sampler."""
+    from motif_b200.decode import GraphDecoder
+    from motif_b200.generate import Generation
+    from motif_b200.sampler import Sampler
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    m.decode_splits = 2
+    ids = torch.randint(0, 512, (3, 24), generator=torch.Generator().manual_seed(4)).cuda()
+    kw = dict(temperature=0.9, top_k=40, top_p=0.95, repetition_penalty=rp, seed=21)
+    steps = 12
+    with torch.no_grad():
+        gen = Generation(m, ids, max_new_tokens=steps + 1, sampler=Sampler(**kw)).run()
+        s = Sampler(**kw)
+        out = m(ids)
+        first = out.next_token(sampler=s, input_ids=ids)
+        seq = torch.cat([ids, first], 1)
+        dec = GraphDecoder(m, out.cache, max_steps=steps, sampler=s)
+        a = dec.run(first, 5, history=seq)
+        b = dec.run(a[:, -1:], steps - 5)
+    got = torch.cat([first, a, b], 1)
+    assert torch.equal(got, gen.generated), (got != gen.generated).nonzero()
+    assert s.offset == 1 + steps
+    with pytest.raises(NotImplementedError):
+        GraphDecoder(m, out.cache, max_steps=1, sampler=Sampler(**kw).with_constraint(object()))

@@ -2,7 +2,7 @@
 
 Runs on CPU against a stand-in `motif` package tree with the same module paths and names
 as the reference (`motif/block/attention/{chord_attn,gdn_attn}.py`, `motif/block/decoder.py`,
-`motif/block/mlp.py`, `motif/model/motif.py`, `motif/ops`), so no reference checkout is needed.
+`motif/block/mlp.py`, `motif/model/{motif,sampler}.py`, `motif/ops`), so no reference checkout is needed.
 """
 
 import sys
@@ -28,7 +28,8 @@ def fake_motif(monkeypatch):
         'motif.block.decoder': ['apply_block_attn_res', 'RMSNorm'],
         'motif.block.mlp': ['SwiGLUOp'],
         'motif.model': [],
-        'motif.model.motif': ['RMSNorm'],
+        'motif.model.motif': ['RMSNorm', 'Sampler', 'make_sampler'],
+        'motif.model.sampler': ['Sampler', 'make_sampler'],
     }
     originals = {}
     for mod_name, attrs in names.items():

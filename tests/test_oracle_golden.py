@@ -103,3 +103,39 @@ def test_tiny_config():
     close(torch.logsumexp(lg, -1), d['pos_lse'], rtol=1e-5, atol=1e-5)
     toks, margins = om.greedy(P, cfg, d['ids'], 64)
     assert torch.equal(toks, d['greedy'])
+
+
+def test_sampler_oracle_matches_reference_distribution():
+    """oracle/sampler.py's filtered distribution == the probabilities the reference Sampler
+    hands to torch.multinomial (model/sampler.py:151-219), for six settings."""
+    from oracle import sampler as osm
+    d = torch.load(os.path.join(GOLD, 'sampler.pt'))
+    for case, ref in zip(d['cases'].tolist(), d['probs']):
+        t, k, p, rp = case
+        got = osm.filtered_probs(d['logits'], d['hist'], t, None if k < 0 else int(k), None if p < 0 else p, rp)
+        assert torch.allclose(got, ref.float(), atol=1e-6, rtol=1e-5), case
+        assert torch.equal(got > 0, ref > 0), case  # the same support
+
+
+def test_philox_known_answers():
+    """Philox4x32-10 restatement against the Random123 known-answer vectors."""
+    from oracle import sampler as osm
+    M = 0xFFFFFFFF
+    assert osm.philox4x32_10([0, 0, 0, 0], [0, 0]) == [0x6627e8d5, 0xe169c58d, 0xbc57ac4c, 0x9b00dbd8]
+    assert osm.philox4x32_10([M, M, M, M], [M, M]) == [0x408f276d, 0x41c83b0e, 0xa20bc7c6, 0x6d5451fd]
+    assert osm.philox4x32_10([0x243f6a88, 0x85a308d3, 0x13198a2e, 0x03707344], [0xa4093822, 0x299f31d0]) == \
+        [0xd16cfe09, 0x94fdcceb, 0x5001e420, 0x24126ea1]
+    u = osm.philox_uniforms(1234, 7, 64)
+    assert u.dtype == torch.float32 and bool((u >= 0).all()) and bool((u < 1).all())
+
+
+def test_sampler_oracle_draw_is_inverse_cdf():
+    """The oracle's draw: first index whose inclusive cumulative mass exceeds u * total."""
+    from oracle import sampler as osm
+    logits = torch.tensor([[0.0, 1.0, -float('inf'), 2.0]])
+    p = torch.softmax(logits, -1)[0]
+    c = torch.cumsum(p, 0)
+    for u, want in [(0.0, 0), (float(c[0]) * 0.999, 0), (float(c[0]) * 1.001, 1), (float(c[1]) * 1.0001, 3),
+                    (0.999999, 3)]:
+        got = osm.sample(logits, None, 1.0, None, None, 1.0, torch.tensor([u]))
+        assert int(got[0]) == want, (u, int(got[0]))
