@@ -60,9 +60,17 @@ def filtered_logits(logits: torch.Tensor, hist: Optional[torch.Tensor], temperat
     if top_p is not None and 0.0 < top_p < 1.0:  # :189-199; ties at the boundary are all kept here
         p = torch.softmax(x, -1)
         keep = torch.zeros_like(x, dtype=torch.bool)
-        for i in range(x.shape[0]):  # mass of the strictly larger values before each token
-            before = (p[i][None, :] * (x[i][None, :] > x[i][:, None])).sum(1)
-            keep[i] = (before <= top_p) & (x[i] > float('-inf'))
+        for i in range(x.shape[0]):
+            # mass of the strictly larger values before each token: the exclusive cumulative
+            # mass (float64) at the first sorted position of the token's group of equal values
+            xs, order = torch.sort(x[i], descending=True, stable=True)
+            ps = p[i][order].double()
+            excl = torch.cumsum(ps, 0) - ps
+            _, inv, counts = torch.unique_consecutive(xs, return_inverse=True, return_counts=True)
+            starts = torch.cumsum(counts, 0) - counts
+            before = excl[starts][inv]
+            k_sorted = (before <= top_p) & (xs > float('-inf'))
+            keep[i, order] = k_sorted
         x = x.masked_fill(~keep, float('-inf'))
     return x
 

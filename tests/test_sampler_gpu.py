@@ -73,6 +73,43 @@ def test_sampler_matches_oracle(V, B, dt, t, k, p, rp, S):
     assert torch.equal(tok, ref_t)
 
 
+def _wide(g, B, V):
+    return torch.randn(B, V, generator=g) * 20
+
+
+def _ties(g, B, V):
+    x = torch.zeros(B, V)
+    x[:, :3] = torch.tensor([4.0, 3.0, 3.0])
+    return x
+
+
+def _coarse(g, B, V):
+    return torch.randint(-3, 4, (B, V), generator=g).float()
+
+
+# Inputs that defeat the window search (cut far below the row maximum, or thousands of equal
+# values in the cut bin) and take the exact radix descent.
+@pytest.mark.parametrize('make,V,dt,k,p', [
+    (_wide, 32000, torch.float32, 20000, None),
+    (_wide, 32000, torch.float32, 20000, 0.999),
+    (_ties, 4096, torch.float32, 100, None),
+    (_ties, 4096, torch.float32, None, 0.5),
+    (_ties, 4096, torch.float32, 2, 0.3),
+    (_coarse, 40960, torch.bfloat16, None, 0.7),
+    (_coarse, 40960, torch.bfloat16, 9000, 0.95),
+])
+def test_sampler_fallback_paths_match_oracle(make, V, dt, k, p):
+    g = torch.Generator().manual_seed(V + (k or 0))
+    B = 4
+    logits = make(g, B, V).to(dt)
+    u = torch.rand(B, generator=g)
+    tok, probs = _kernel(logits.cuda(), None, 1.0, k, p, 1.0, uniforms=u)
+    ref_p = _oracle_probs(logits, None, 1.0, k, p, 1.0)
+    assert torch.equal(probs > 0, ref_p > 0)
+    assert torch.allclose(probs, ref_p, atol=1e-6, rtol=1e-5), (probs - ref_p).abs().max()
+    assert torch.equal(tok, _oracle_draw(ref_p, u))
+
+
 def _oracle_probs(logits, hist_rows, t, k, p, rp):
     rows = []
     for i in range(logits.shape[0]):
