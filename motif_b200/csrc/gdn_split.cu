@@ -33,19 +33,25 @@ namespace {
 using namespace gdnk;
 
 // Per-chunk workspace record = the scan's shared-memory image of one chunk (rows padded by 8
-// elements so that ldmatrix rows fall on distinct banks):
-//   Qs [C][QS] = q e^gamma | Kd [C][QS] = k e^{gamma_L - gamma} | WU [C][XS] = [W | U] |
-//   Aq [C][AS] (T) | e^{gamma_L} (fp32, padded to 16 bytes)
+// elements so that ldmatrix rows fall on distinct banks).  A shared part every value-column
+// slice of the scan reads, then one U plane per slice of SW value columns:
+//   Qs [C][QS] = q e^gamma | Kd [C][QS] = k e^{gamma_L - gamma} | W [C][QS] | Aq [C][AS] (T) |
+//   e^{gamma_L} (fp32, padded to 16 bytes) | U_0 [C][US] | U_1 [C][US] | ...
 template <typename T, int DK, int DV>
 struct WsRec {
-  static constexpr int QS = DK + 8, VS = DV + 8, AS = C + 8, XS = DK + DV + 8;
+  static constexpr int SW = DV < 64 ? DV : 64;  // value columns per scan slice
+  static constexpr int NSL = DV / SW;
+  static_assert(DV % SW == 0, "value columns split into equal slices");
+  static constexpr int QS = DK + 8, AS = C + 8, US = SW + 8;
   static constexpr size_t off_qs = 0;
   static constexpr size_t off_kd = off_qs + (size_t)C * QS * sizeof(T);
-  static constexpr size_t off_wu = off_kd + (size_t)C * QS * sizeof(T);
-  static constexpr size_t off_aq = off_wu + (size_t)C * XS * sizeof(T);
+  static constexpr size_t off_w = off_kd + (size_t)C * QS * sizeof(T);
+  static constexpr size_t off_aq = off_w + (size_t)C * QS * sizeof(T);
   static constexpr size_t off_el = off_aq + (size_t)C * AS * sizeof(T);
-  static constexpr size_t bytes = off_el + 16;
-  static_assert(bytes % 16 == 0, "records stay 16-byte aligned");
+  static constexpr size_t shared_bytes = off_el + 16;
+  static constexpr size_t u_bytes = (size_t)C * US * sizeof(T);
+  static constexpr size_t bytes = shared_bytes + NSL * u_bytes;
+  static_assert(shared_bytes % 16 == 0 && u_bytes % 16 == 0, "records stay 16-byte aligned");
 };
 
 template <typename T, int DK, int DV>
@@ -402,16 +408,24 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       *reinterpret_cast<uint4*>(&rqs[r * QS + c]) = oq;
       *reinterpret_cast<uint4*>(&rkd[r * QS + c]) = ok;
     }
-    constexpr int XV = (DK + DV) / E, AV = C / E;
-    T* rwu = reinterpret_cast<T*>(rec + Rec::off_wu);
+    // [W | U] row r, vector c: W -> the W plane, U columns -> their slice's plane
+    constexpr int XV = (DK + DV) / E, AV = C / E, WV = DK / E, UV = Rec::SW / E;
+    T* rw = reinterpret_cast<T*>(rec + Rec::off_w);
     T* raq = reinterpret_cast<T*>(rec + Rec::off_aq);
     for (int i = tid; i < C * (XV + AV); i += NT) {
       const int r = i / (XV + AV), c = i % (XV + AV);
-      if (c < XV)
-        *reinterpret_cast<uint4*>(&rwu[r * XS + c * E]) = *reinterpret_cast<const uint4*>(&sX[r * XS + c * E]);
-      else
-        *reinterpret_cast<uint4*>(&raq[r * AS + (c - XV) * E]) =
-            *reinterpret_cast<const uint4*>(&sAq[r * AS + (c - XV) * E]);
+      const uint4 val = c < XV ? *reinterpret_cast<const uint4*>(&sX[r * XS + c * E])
+                               : *reinterpret_cast<const uint4*>(&sAq[r * AS + (c - XV) * E]);
+      T* dst;
+      if (c < WV) {
+        dst = &rw[r * QS + c * E];
+      } else if (c < XV) {
+        const int j = (c - WV) / UV, cu = (c - WV) % UV;
+        dst = reinterpret_cast<T*>(rec + Rec::shared_bytes + j * Rec::u_bytes) + r * Rec::US + cu * E;
+      } else {
+        dst = &raq[r * AS + (c - XV) * E];
+      }
+      *reinterpret_cast<uint4*>(dst) = val;
     }
     if (tid == 0) *reinterpret_cast<float*>(rec + Rec::off_el) = sEg[C - 1];
   }
@@ -420,10 +434,11 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
 template <typename T, int DK, int DV>
 struct RecLayout {
   using Rec = WsRec<T, DK, DV>;
-  static constexpr int VS = DV + 8;
-  static constexpr size_t off_stage = 0;  // 2 record images
-  static constexpr size_t off_s = off_stage + 2 * Rec::bytes;
-  static constexpr size_t off_bar = off_s + 2ull * DK * VS * sizeof(T);
+  static constexpr int SS = Rec::SW + 8;  // state slice row stride (elements)
+  static constexpr size_t stage_bytes = Rec::shared_bytes + Rec::u_bytes;
+  static constexpr size_t off_stage = 0;  // 2 stages: the shared part + this slice's U plane
+  static constexpr size_t off_s = off_stage + 2 * stage_bytes;
+  static constexpr size_t off_bar = off_s + 2ull * DK * SS * sizeof(T);
   static constexpr size_t bytes = off_bar + 16;
   static_assert(bytes <= 232448, "shared memory budget");
 };
@@ -432,34 +447,38 @@ constexpr uint32_t kRecWait = 1u << 22;
 // Count of state-scan CTAs whose bounded record-copy wait ran out (never expected).
 __device__ unsigned int g_gdn_wait_timeouts = 0;
 
+// One CTA per (sequence, head, slice of SW value columns): the columns of S evolve
+// independently (X = U - W S, o = Qs S + Aq X and S' = e^gL S + Kd^T X act column by column),
+// so each slice scans its own DK x SW block of the state.  Adjacent CTAs are the slices of one
+// (sequence, head) and read the record's shared part at about the same time, from L2.
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __restrict__ ws,
+__global__ void __launch_bounds__(NT, 2) gdn_rec_kernel(const unsigned char* __restrict__ ws,
                                                         const float* __restrict__ s_in, float* __restrict__ s_out,
                                                         T* __restrict__ o, int H, int L, Strides18 sv) {
   using Lay = RecLayout<T, DK, DV>;
   using Rec = WsRec<T, DK, DV>;
-  constexpr int QS = Rec::QS, VS = Rec::VS, AS = Rec::AS, XS = Rec::XS;
+  constexpr int QS = Rec::QS, AS = Rec::AS, US = Rec::US, SW = Rec::SW, SS = Lay::SS;
   constexpr int SM_T = DK / 16;
-  constexpr int HT = DV / 16;  // n8 tiles per column half
+  constexpr int HT = SW / 16;  // n8 tiles per warp (two column groups of SW / 2)
   extern __shared__ __align__(128) unsigned char smem[];
   T* sS = reinterpret_cast<T*>(smem + Lay::off_s);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Lay::off_bar);
 
   const int64_t* st = sv.s;
-  const int bh = blockIdx.x;
+  const int bh = blockIdx.x / Rec::NSL, slice = blockIdx.x % Rec::NSL;
   const int b = bh / H, h = bh % H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
-  T* og = o + b * st[9] + h * st[10];
+  T* og = o + b * st[9] + h * st[10] + slice * SW;
   const int nchunks = (L + C - 1) / C;
   const unsigned char* recs = ws + (size_t)bh * nchunks * Rec::bytes;
 
-  // state: warp w holds S rows [16 (w % 4), +16) x value columns [DV/2 (w / 4), +DV/2) (fp32)
+  // state: warp w holds S rows [16 (w % 4), +16) x slice columns [SW/2 (w / 4), +SW/2) (fp32)
   const bool s_owner = (warp & 3) < SM_T;
   const int sm0 = (warp & 3) * 16;
-  const int sc0 = (warp >> 2) * (DV / 2);
+  const int sc0 = (warp >> 2) * (SW / 2);
   float Sr[HT][4];
-  const float* s0 = s_in ? s_in + (size_t)bh * DK * DV : nullptr;
+  const float* s0 = s_in ? s_in + (size_t)bh * DK * DV + slice * SW : nullptr;
   if (s_owner) {
 #pragma unroll
     for (int nt = 0; nt < HT; ++nt) {
@@ -468,8 +487,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
       Sr[nt][1] = s0 ? s0[r * DV + c + 1] : 0.f;
       Sr[nt][2] = s0 ? s0[(r + 8) * DV + c] : 0.f;
       Sr[nt][3] = s0 ? s0[(r + 8) * DV + c + 1] : 0.f;
-      st2(&sS[r * VS + c], Sr[nt][0], Sr[nt][1]);
-      st2(&sS[(r + 8) * VS + c], Sr[nt][2], Sr[nt][3]);
+      st2(&sS[r * SS + c], Sr[nt][0], Sr[nt][1]);
+      st2(&sS[(r + 8) * SS + c], Sr[nt][2], Sr[nt][3]);
     }
   }
   if (tid == 0) {
@@ -478,10 +497,13 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
     mbar_init_fence();
   }
   __syncthreads();
-  auto issue = [&](int n) {  // thread 0: record n -> stage n & 1
-    mbar_arrive_expect_tx(&bar[n & 1], (uint32_t)Rec::bytes);
-    bulk_load(smem + Lay::off_stage + (size_t)(n & 1) * Rec::bytes, recs + (size_t)n * Rec::bytes,
-              (uint32_t)Rec::bytes, &bar[n & 1]);
+  auto issue = [&](int n) {  // thread 0: record n (shared part + this slice's U) -> stage n & 1
+    unsigned char* dst = smem + Lay::off_stage + (size_t)(n & 1) * Lay::stage_bytes;
+    const unsigned char* src = recs + (size_t)n * Rec::bytes;
+    mbar_arrive_expect_tx(&bar[n & 1], (uint32_t)Lay::stage_bytes);
+    bulk_load(dst, src, (uint32_t)Rec::shared_bytes, &bar[n & 1]);
+    bulk_load(dst + Rec::shared_bytes, src + Rec::shared_bytes + slice * Rec::u_bytes, (uint32_t)Rec::u_bytes,
+              &bar[n & 1]);
   };
   int nissued = 0;
   if (tid == 0)
@@ -496,30 +518,30 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
       failed = true;
       break;
     }
-    unsigned char* sp = smem + Lay::off_stage + (size_t)stage * Rec::bytes;
+    unsigned char* sp = smem + Lay::off_stage + (size_t)stage * Lay::stage_bytes;
     const T* cQ = reinterpret_cast<const T*>(sp + Rec::off_qs);
     const T* cK = reinterpret_cast<const T*>(sp + Rec::off_kd);
-    T* sX = reinterpret_cast<T*>(sp + Rec::off_wu);
+    const T* cW = reinterpret_cast<const T*>(sp + Rec::off_w);
     const T* sAq = reinterpret_cast<const T*>(sp + Rec::off_aq);
+    T* sX = reinterpret_cast<T*>(sp + Rec::shared_bytes);  // U, then X in place
     const float eL = *reinterpret_cast<const float*>(sp + Rec::off_el);
-    const T* cS = sS + (size_t)(n & 1) * DK * VS;
-    T* nS = sS + (size_t)((n + 1) & 1) * DK * VS;
+    const T* cS = sS + (size_t)(n & 1) * DK * SS;
+    T* nS = sS + (size_t)((n + 1) & 1) * DK * SS;
+    const int m0 = (warp & 3) * 16, c0 = (warp >> 2) * (SW / 2);
 
-    // X = U - W S  (warp: m-tile w%4, value-column half w/4), in place of U
+    // X = U - W S  (warp: m-tile w%4, column group w/4), in place of U
     {
-      const int m0 = (warp & 3) * 16;
-      const int nbase = (warp >> 2) * (DV / 2);
       float acc[HT][4];
 #pragma unroll
       for (int i = 0; i < HT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll
       for (int k0 = 0; k0 < DK; k0 += 16) {
         uint32_t a[4];
-        lda(a, sX, XS, m0, k0);
+        lda(a, cW, QS, m0, k0);
 #pragma unroll
-        for (int nn = 0; nn < DV / 2; nn += 16) {
+        for (int nn = 0; nn < SW / 2; nn += 16) {
           uint32_t bb[4];
-          ldb_t(bb, cS, VS, k0, nbase + nn);
+          ldb_t(bb, cS, SS, k0, c0 + nn);
           mma_16816<T>(acc[nn / 8], a, &bb[0]);
           mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
         }
@@ -527,17 +549,16 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
       const int ra = m0 + gq, rb = ra + 8;
 #pragma unroll
       for (int nt = 0; nt < HT; ++nt) {
-        const int c = nbase + nt * 8 + 2 * tq;
-        const float2 ua = ld2(&sX[ra * XS + DK + c]), ub = ld2(&sX[rb * XS + DK + c]);
-        st2(&sX[ra * XS + DK + c], ua.x - acc[nt][0], ua.y - acc[nt][1]);
-        st2(&sX[rb * XS + DK + c], ub.x - acc[nt][2], ub.y - acc[nt][3]);
+        const int c = c0 + nt * 8 + 2 * tq;
+        const float2 ua = ld2(&sX[ra * US + c]), ub = ld2(&sX[rb * US + c]);
+        st2(&sX[ra * US + c], ua.x - acc[nt][0], ua.y - acc[nt][1]);
+        st2(&sX[rb * US + c], ub.x - acc[nt][2], ub.y - acc[nt][3]);
       }
     }
     __syncthreads();  // X complete
 
     // o = (q e^g) S + Aq X  and  S = e^gL S + (k e^(gL - g))^T X for this warp's block
     {
-      const int m0 = (warp & 3) * 16, c0 = (warp >> 2) * (DV / 2);
       float acc[HT][4];
 #pragma unroll
       for (int i = 0; i < HT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -546,9 +567,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
         uint32_t a[4];
         lda(a, cQ, QS, m0, k0);
 #pragma unroll
-        for (int nn = 0; nn < DV / 2; nn += 16) {
+        for (int nn = 0; nn < SW / 2; nn += 16) {
           uint32_t bb[4];
-          ldb_t(bb, cS, VS, k0, c0 + nn);
+          ldb_t(bb, cS, SS, k0, c0 + nn);
           mma_16816<T>(acc[nn / 8], a, &bb[0]);
           mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
         }
@@ -557,9 +578,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
         uint32_t a[4];
         lda(a, sAq, AS, m0, k0);
 #pragma unroll
-        for (int nn = 0; nn < DV / 2; nn += 16) {
+        for (int nn = 0; nn < SW / 2; nn += 16) {
           uint32_t bb[4];
-          ldb_t(bb, sX + DK, XS, k0, c0 + nn);
+          ldb_t(bb, sX, US, k0, c0 + nn);
           mma_16816<T>(acc[nn / 8], a, &bb[0]);
           mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
         }
@@ -582,9 +603,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
           uint32_t a[4];
           lda_t(a, cK, QS, sm0, k0);
 #pragma unroll
-          for (int nn = 0; nn < DV / 2; nn += 16) {
+          for (int nn = 0; nn < SW / 2; nn += 16) {
             uint32_t bb[4];
-            ldb_t(bb, sX + DK, XS, k0, sc0 + nn);
+            ldb_t(bb, sX, US, k0, sc0 + nn);
             mma_16816<T>(Sr[nn / 8], a, &bb[0]);
             mma_16816<T>(Sr[nn / 8 + 1], a, &bb[2]);
           }
@@ -592,8 +613,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
 #pragma unroll
         for (int nt = 0; nt < HT; ++nt) {
           const int r = sm0 + gq, c = sc0 + nt * 8 + 2 * tq;
-          st2(&nS[r * VS + c], Sr[nt][0], Sr[nt][1]);
-          st2(&nS[(r + 8) * VS + c], Sr[nt][2], Sr[nt][3]);
+          st2(&nS[r * SS + c], Sr[nt][0], Sr[nt][1]);
+          st2(&nS[(r + 8) * SS + c], Sr[nt][2], Sr[nt][3]);
         }
       }
     }
@@ -612,7 +633,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
     return;
   }
   if (s_owner) {
-    float* so = s_out + (size_t)bh * DK * DV;
+    float* so = s_out + (size_t)bh * DK * DV + slice * SW;
 #pragma unroll
     for (int nt = 0; nt < HT; ++nt) {
       const int r = sm0 + gq, c = sc0 + nt * 8 + 2 * tq;
@@ -625,54 +646,67 @@ __global__ void __launch_bounds__(NT, 1) gdn_rec_kernel(const unsigned char* __r
 // GatedRMSNorm on the scan's output rows, in place: o <- rmsnorm(o) * w * silu(gate) for each
 // (token, head) row of DV values (gdn_attn.py:197-209 with rms_norm.py:547-553 roundings).
 // A group of DV/8 lanes owns a row as 16-byte vectors (the row's sum of squares reduces over
-// the group); a grid-stride loop walks the rows, so each thread keeps several rows of loads in
-// flight across iterations.
+// the group); each warp takes two groups of rows per iteration of a grid-stride loop, so every
+// thread has four 16-byte loads in flight.  Row coordinates use 32-bit arithmetic (the host
+// checks rows < 2^31).
 template <typename T, int DV>
 __global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, int64_t ob, int64_t oh, int64_t ol,
                                                             const T* __restrict__ gate, int64_t gate_rs,
                                                             int64_t gate_hs, const T* __restrict__ w, float eps, int H,
-                                                            int L, int64_t rows) {
+                                                            int L, int rows) {
   constexpr int LPR = DV / 8;  // lanes per row
   constexpr int RPW = 32 / LPR;
+  constexpr int U = 2;         // row groups per warp iteration
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;
   const uint4 wv = reinterpret_cast<const uint4*>(w)[sub];
   const T* we = reinterpret_cast<const T*>(&wv);
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t wi = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi * RPW < rows; wi += warps) {
-    const int64_t row = wi * RPW + lane / LPR;  // (b * L + l) * H + h
-    const bool ok = row < rows;
-    uint4* op = nullptr;
-    uint4 ov = make_uint4(0, 0, 0, 0), gv = make_uint4(0, 0, 0, 0);
-    if (ok) {
-      const int h = (int)(row % H);
-      const int64_t bl = row / H;
-      const int l = (int)(bl % L), b = (int)(bl / L);
-      op = reinterpret_cast<uint4*>(o + b * ob + h * oh + (int64_t)l * ol) + sub;
-      ov = *op;
-      gv = reinterpret_cast<const uint4*>(gate + bl * gate_rs + h * gate_hs)[sub];
-    }
-    const T* oe = reinterpret_cast<const T*>(&ov);
-    const T* ge = reinterpret_cast<const T*>(&gv);
-    float x[8];
-    float ss = 0.f;
+  float wf[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x[i] = to_f(oe[i]);
-      ss += x[i] * x[i];
+  for (int i = 0; i < 8; ++i) wf[i] = to_f(we[i]);
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int wi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi * RPW * U < rows; wi += warps) {
+    uint4* op[U];
+    uint4 ov[U], gv[U];
+    bool ok[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int row = (wi * U + u) * RPW + lane / LPR;  // (b * L + l) * H + h
+      ok[u] = row < rows;
+      ov[u] = gv[u] = make_uint4(0, 0, 0, 0);
+      op[u] = nullptr;
+      if (ok[u]) {
+        const unsigned bl = (unsigned)row / (unsigned)H, h = (unsigned)row - bl * (unsigned)H;
+        const unsigned b = bl / (unsigned)L, l = bl - b * (unsigned)L;
+        op[u] = reinterpret_cast<uint4*>(o + (int64_t)b * ob + (int64_t)h * oh + (int64_t)l * ol) + sub;
+        ov[u] = *op[u];
+        gv[u] = reinterpret_cast<const uint4*>(gate + (int64_t)bl * gate_rs + (int64_t)h * gate_hs)[sub];
+      }
     }
 #pragma unroll
-    for (int o2 = 1; o2 < LPR; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
-    if (!ok) continue;
-    const float r = rsqrtf(ss / (float)DV + eps);
-    uint4 res;
-    T* re = reinterpret_cast<T*>(&res);
+    for (int u = 0; u < U; ++u) {
+      const T* oe = reinterpret_cast<const T*>(&ov[u]);
+      const T* ge = reinterpret_cast<const T*>(&gv[u]);
+      float x[8];
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * to_f(we[i])));
-      re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
+      for (int i = 0; i < 8; ++i) {
+        x[i] = to_f(oe[i]);
+        ss += x[i] * x[i];
+      }
+#pragma unroll
+      for (int o2 = 1; o2 < LPR; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+      if (!ok[u]) continue;
+      const float r = rsqrtf(ss / (float)DV + eps);
+      uint4 res;
+      T* re = reinterpret_cast<T*>(&res);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * wf[i]));
+        re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
+      }
+      *op[u] = res;
     }
-    *op = res;
   }
 }
 
@@ -699,15 +733,18 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
       (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws, pin);
   int rc = check_launch("gdn_chunk (UT transform)");
   if (rc) return rc;
-  k2<<<(unsigned)(B * H), NT, RL::bytes, stream>>>((const unsigned char*)ws, s_in, s_out, (T*)o, (int)H, (int)L, sv);
+  k2<<<(unsigned)(B * H * WsRec<T, DK, DV>::NSL), NT, RL::bytes, stream>>>((const unsigned char*)ws, s_in, s_out,
+                                                                             (T*)o, (int)H, (int)L, sv);
   rc = check_launch("gdn_chunk (state scan)");
   if (rc || gate == nullptr) return rc;
   const int64_t rows = B * L * H;
+  if (rows >= (1LL << 31) - 64) return set_error(MB_ERR_SHAPE, "gdn_chunk (gated norm): %lld rows", (long long)rows);
   const int64_t* st = sv.s;
-  const int64_t warps_needed = (rows + (256 / DV) - 1) / (256 / DV);  // DV/8 lanes per row
-  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, 148 * 16);
+  const int64_t warps_needed = (rows + 2 * (256 / DV) - 1) / (2 * (256 / DV));  // DV/8 lanes per row, 2 groups
+  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, 148 * 8);
   gdn_gate_norm_kernel<T, DV><<<(unsigned)blocks, 256, 0, stream>>>(
-      (T*)o, st[9], st[10], st[11], (const T*)gate, gate_rs, gate_hs, (const T*)onorm_w, eps, (int)H, (int)L, rows);
+      (T*)o, st[9], st[10], st[11], (const T*)gate, gate_rs, gate_hs, (const T*)onorm_w, eps, (int)H, (int)L,
+      (int)rows);
   return check_launch("gdn_chunk (gated norm)");
 }
 
