@@ -183,6 +183,14 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
                              : (kind == 1 ? H * DK + h * DK + (cl - DK) : 2 * H * DK + h * DV + (cl - 2 * DK));
     const T* P = pin.proj + (int64_t)b * L * pin.ps;
     const int t0 = n * C + run * 8;
+    // this chunk's a / b scalars (beta and g below), requested first so that their latency
+    // overlaps the row loads instead of following them
+    T a_raw = from_f<T>(0.f), b_raw = from_f<T>(0.f);
+    if (tid < C && n * C + tid < L) {
+      const T* row = P + (int64_t)(n * C + tid) * pin.ps;
+      a_raw = row[Ct + h];
+      b_raw = row[Ct + H + h];
+    }
     uint4 raw[11];
 #pragma unroll
     for (int j = 0; j < 11; ++j) {
@@ -246,11 +254,10 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       const int l = n * C + tid;
       float bt = 0.f, gt = 0.f;
       if (l < L) {
-        const T* row = P + (int64_t)l * pin.ps;
         const float Aexp = -to_f(from_f<T>(expf(to_f(pin.A_log[h]))));
         const float dtb = to_f(pin.dt_bias[h]);
-        bt = to_f(from_f<T>(sigmoidf_(to_f(row[Ct + H + h]))));
-        gt = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(to_f(row[Ct + h]) + dtb)))))));
+        bt = to_f(from_f<T>(sigmoidf_(to_f(b_raw))));
+        gt = to_f(from_f<T>(Aexp * to_f(from_f<T>(softplusf_(to_f(from_f<T>(to_f(a_raw) + dtb)))))));
       }
       sBeta[tid] = bt;
       sGin[tid] = gt;
@@ -388,10 +395,17 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
     constexpr int E = 16 / sizeof(T);
     T* rqs = reinterpret_cast<T*>(rec + Rec::off_qs);
     T* rkd = reinterpret_cast<T*>(rec + Rec::off_kd);
+    // Every 16-byte vector of the record is written, the row pads included (as zeros), so that
+    // no L2 sector is left partly written (a partial sector is read back from DRAM to merge).
     constexpr int QV = DK / E;  // 16-byte vectors per q / k row
     const float gl = sGam[C - 1];
-    for (int i = tid; i < C * QV; i += NT) {
-      const int r = i / QV, c = (i % QV) * E;
+    for (int i = tid; i < C * (QV + 1); i += NT) {
+      const int r = i / (QV + 1), c = (i % (QV + 1)) * E;
+      if (c == DK) {
+        *reinterpret_cast<uint4*>(&rqs[r * QS + c]) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(&rkd[r * QS + c]) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
       const float eq = sEg[r], ek = __expf(gl - sGam[r]);
       const uint4 vq = *reinterpret_cast<const uint4*>(&cQ[r * QS + c]);
       const uint4 vk = *reinterpret_cast<const uint4*>(&cK[r * QS + c]);
@@ -408,26 +422,30 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       *reinterpret_cast<uint4*>(&rqs[r * QS + c]) = oq;
       *reinterpret_cast<uint4*>(&rkd[r * QS + c]) = ok;
     }
-    // [W | U] row r, vector c: W -> the W plane, U columns -> their slice's plane
-    constexpr int XV = (DK + DV) / E, AV = C / E, WV = DK / E, UV = Rec::SW / E;
+    // per row: the W plane (WV vectors + pad), each U plane (UV + pad), Aq (AV + pad)
+    constexpr int AV = C / E, WV = DK / E, UV = Rec::SW / E;
+    constexpr int RV = (WV + 1) + Rec::NSL * (UV + 1) + (AV + 1);
     T* rw = reinterpret_cast<T*>(rec + Rec::off_w);
     T* raq = reinterpret_cast<T*>(rec + Rec::off_aq);
-    for (int i = tid; i < C * (XV + AV); i += NT) {
-      const int r = i / (XV + AV), c = i % (XV + AV);
-      const uint4 val = c < XV ? *reinterpret_cast<const uint4*>(&sX[r * XS + c * E])
-                               : *reinterpret_cast<const uint4*>(&sAq[r * AS + (c - XV) * E]);
+    for (int i = tid; i < C * RV; i += NT) {
+      const int r = i / RV, c = i % RV;
+      uint4 val = make_uint4(0, 0, 0, 0);
       T* dst;
-      if (c < WV) {
+      if (c <= WV) {
         dst = &rw[r * QS + c * E];
-      } else if (c < XV) {
-        const int j = (c - WV) / UV, cu = (c - WV) % UV;
+        if (c < WV) val = *reinterpret_cast<const uint4*>(&sX[r * XS + c * E]);
+      } else if (c < (WV + 1) + Rec::NSL * (UV + 1)) {
+        const int j = (c - WV - 1) / (UV + 1), cu = (c - WV - 1) % (UV + 1);
         dst = reinterpret_cast<T*>(rec + Rec::shared_bytes + j * Rec::u_bytes) + r * Rec::US + cu * E;
+        if (cu < UV) val = *reinterpret_cast<const uint4*>(&sX[r * XS + DK + j * Rec::SW + cu * E]);
       } else {
-        dst = &raq[r * AS + (c - XV) * E];
+        const int ca = c - (WV + 1) - Rec::NSL * (UV + 1);
+        dst = &raq[r * AS + ca * E];
+        if (ca < AV) val = *reinterpret_cast<const uint4*>(&sAq[r * AS + ca * E]);
       }
       *reinterpret_cast<uint4*>(dst) = val;
     }
-    if (tid == 0) *reinterpret_cast<float*>(rec + Rec::off_el) = sEg[C - 1];
+    if (tid == 0) *reinterpret_cast<float4*>(rec + Rec::off_el) = make_float4(sEg[C - 1], 0.f, 0.f, 0.f);
   }
 }
 

@@ -90,7 +90,9 @@ class GraphDecoder:
     host-side lengths are advanced by the steps taken, so the eager API can continue from it.
     """
 
-    def __init__(self, model, cache: ModelCache, max_steps: int, splits: Optional[int] = None, sampler=None):
+    def __init__(self, model, cache: ModelCache, max_steps: int, splits: Optional[int] = None, sampler=None,
+                 eos_ids: Optional[List[int]] = None, fill_id: Optional[int] = None,
+                 finished: Optional[torch.Tensor] = None):
         if model.training:
             raise ValueError('GraphDecoder needs an eval-mode model')
         w = model.embed.weight
@@ -112,6 +114,7 @@ class GraphDecoder:
             raise ValueError('no allocated KV cache: prefill the cache before building the graph')
         self.B = kv0._kbuf.shape[0]
         self.start = kv0.length
+        self.seq_start = cache.seq_len  # the block histories' token count (`ModelCache.seq_len`)
         self.max_steps = int(max_steps)
         self.kv, self.gdn = _check_layer_caches(model, cache, self.B, self.start + self.max_steps)
         self.cap = min(lc.capacity for lc in self.kv)
@@ -140,6 +143,18 @@ class GraphDecoder:
                 self.hist = torch.full((self.B, self.start + 1 + self.max_steps), -1, dtype=torch.int64,
                                        device=self.dev)
                 self.hist_col = torch.tensor([self.start], dtype=torch.int64, device=self.dev)
+        # end-of-sequence bookkeeping of `Generation.step` on the device: rows that already
+        # produced an eos id receive `fill_id`; `all_done[i]` records whether every row has
+        # finished after step i (read by the host once per chunk of steps)
+        self.eos = None
+        if eos_ids:
+            self.eos = torch.tensor([int(e) for e in eos_ids], dtype=torch.int64, device=self.dev)
+            self.fill = torch.tensor(int(fill_id if fill_id is not None else min(eos_ids)), dtype=torch.int64,
+                                     device=self.dev)
+            self.finished = torch.zeros((self.B,), dtype=torch.bool, device=self.dev)
+            if finished is not None:
+                self.finished.copy_(finished.reshape(-1).to(self.dev, torch.bool))
+            self.all_done = torch.zeros((self.max_steps,), dtype=torch.bool, device=self.dev)
         self.launches_per_step = 0
         self.graph = None
         self._capture()
@@ -195,6 +210,10 @@ class GraphDecoder:
                       float(sp.top_p) if sp.top_p is not None else 1.0, None, sp.seed & (2 ** 64 - 1),
                       self.sample_base & (2 ** 64 - 1), _lib.ptr(self.step_idx), _lib.ptr(self.ids), None, 0,
                       dc, st)
+        if self.eos is not None:
+            self.ids.copy_(torch.where(self.finished, self.fill, self.ids))
+            self.finished.logical_or_(torch.isin(self.ids, self.eos))
+            self.all_done.index_copy_(0, self.step_idx, self.finished.all().view(1))
         self.tokens.index_copy_(0, self.step_idx, self.ids.view(1, B))
         self.step_idx.add_(1)
         self.lens.add_(1)
@@ -240,7 +259,8 @@ class GraphDecoder:
     # ------------------------------------------------------------------ capture / replay
     def _snapshot(self):
         hist = None if self.hist is None else (self.hist.clone(), self.hist_col.clone())
-        return [s.state.clone() for s in self.gdn], [s.conv.clone() for s in self.gdn], hist
+        fin = None if self.eos is None else self.finished.clone()
+        return [s.state.clone() for s in self.gdn], [s.conv.clone() for s in self.gdn], hist, fin
 
     def _restore(self, snap):
         for s, st_, cv in zip(self.gdn, snap[0], snap[1]):
@@ -249,6 +269,36 @@ class GraphDecoder:
         if snap[2] is not None:
             self.hist.copy_(snap[2][0])
             self.hist_col.copy_(snap[2][1])
+        if snap[3] is not None:
+            self.finished.copy_(snap[3])
+
+    def set_history(self, history: torch.Tensor):
+        """Seed the repetition-penalty history with the sequence so far ([B, start + 1], ending
+        with the first token fed); a no-op for samplers without the penalty."""
+        if self.hist is None:
+            return
+        if self.taken:
+            raise ValueError('history seeds the first run only')
+        if tuple(history.shape) != (self.B, self.start + 1):
+            raise ValueError(f'history must be [{self.B}, {self.start + 1}], got {tuple(history.shape)}')
+        self.hist[:, :self.start + 1].copy_(history.to(self.dev, torch.int64))
+
+    def save(self):
+        """Everything a later `run` reads or writes, so that `load(save())` rewinds the decoder
+        (and the cache's recurrent states and lengths) to this point.  KV entries written after
+        the save lie past the restored lengths and are overwritten by the next steps."""
+        return (self._snapshot(), self.lens.clone(), self.step_idx.clone(), self.ids.clone(), self.taken)
+
+    def load(self, saved):
+        snap, lens, step_idx, ids, taken = saved
+        self._restore(snap)
+        self.lens.copy_(lens)
+        self.step_idx.copy_(step_idx)
+        self.ids.copy_(ids)
+        self.taken = taken
+        if self.sampler is not None:
+            self.sampler.offset = self.sample_base + taken
+        self._sync_lengths()
 
     def _capture(self):
         # The warm-up step (required before capture: cuBLAS handles, lazy library load) and the
@@ -287,12 +337,8 @@ class GraphDecoder:
         ids = first_ids.reshape(-1)
         if ids.numel() != self.B:
             raise ValueError(f'first_ids holds {ids.numel()} ids for a batch of {self.B}')
-        if history is not None and self.hist is not None:
-            if self.taken:
-                raise ValueError('history seeds the first run only')
-            if tuple(history.shape) != (self.B, self.start + 1):
-                raise ValueError(f'history must be [{self.B}, {self.start + 1}], got {tuple(history.shape)}')
-            self.hist[:, :self.start + 1].copy_(history.to(self.dev, torch.int64))
+        if history is not None:
+            self.set_history(history)
         self.ids.copy_(ids.to(self.dev, torch.int64), non_blocking=True)
         lo = self.taken
         for _ in range(steps):
@@ -300,11 +346,18 @@ class GraphDecoder:
         self.taken += steps
         if self.sampler is not None:
             self.sampler.offset = self.sample_base + self.taken
+        self._sync_lengths()
+        return self.tokens[lo:self.taken].t()
+
+    def _sync_lengths(self):
+        """Host-side lengths after `taken` graph steps: KV / GDN layer caches and the block
+        histories' `seq_len` (each step feeds one token)."""
         for lc in self.kv:
             lc.length = self.start + self.taken
         for s in self.gdn:
             s.cache.length = self.start + self.taken
-        return self.tokens[lo:self.taken].t()
+        for bc in self.cache:
+            bc.attn_res.seq_len = self.seq_start + self.taken
 
     def breakdown(self, first_ids: torch.Tensor):
         """Run one step eagerly (outside the graph) with CUDA events around every launch and

@@ -4,6 +4,16 @@ Each step: forward with the cache -> `next_token` (greedy argmax kernel, or a bo
 sampler callable) -> append.  The first forward feeds the whole prompt (prefill); later
 steps feed the previous token.  Rows that produced an eos keep receiving the eos
 placeholder; iteration stops when every row finished or `max_new_tokens` is reached.
+
+`graph=True` runs the decode steps of `run()` as replays of one captured CUDA graph
+(`motif_b200.decode.GraphDecoder`): the eos placeholder and the finished flags are kept on
+the device, and the host reads the all-finished flags once per `sync_every` steps instead
+of once per step (`generate.py:127`).  When every row finished inside a chunk, the
+recurrent states saved at the chunk's start are restored and exactly the steps up to the
+stop are replayed, so the tokens, the finished flags and the cache are those of the
+step-by-step loop.  Graph mode needs a Chord layer (the graph reads its positions from the
+KV cache), no attention mask, and either greedy decoding or a `motif_b200.sampler.Sampler`
+without a grammar constraint; otherwise `run()` steps eagerly.
 """
 
 from typing import Sequence, Union
@@ -30,7 +40,7 @@ def _resolve_eos(eos_token_id, tokenizer):
 
 class Generation:
     def __init__(self, model, input_ids, max_new_tokens=32, eos_token_id: EosTokenId = None, sampler=None,
-                 cache=None, mask=None, tokenizer=None):
+                 cache=None, mask=None, tokenizer=None, graph: bool = False, sync_every: int = 16):
         if input_ids.dim() != 2:
             raise ValueError(f'input_ids must be [B, T], got {tuple(input_ids.shape)}')
         if int(max_new_tokens) < 0:
@@ -51,6 +61,9 @@ class Generation:
         self.fill_id = min(self.eos_ids) if self.eos_ids else None
         self.finished = torch.zeros(input_ids.shape[0], dtype=torch.bool, device=input_ids.device)
         self.steps = 0
+        self.graph = bool(graph)
+        self.sync_every = max(1, int(sync_every))
+        self.graph_steps = 0  # steps taken by graph replays (the rest ran eagerly)
 
     @property
     def done(self) -> bool:
@@ -89,6 +102,59 @@ class Generation:
         return self.step()
 
     def run(self):
+        if self.graph and not self.done:
+            if self.steps == 0:
+                self.step()  # the prefill (and the first token) run eagerly
+            if not self.done and self._graph_ok():
+                self._run_graph()
         for _ in self:
             pass
         return self
+
+    def _graph_ok(self) -> bool:
+        from .model import MotifChordModel
+        from .sampler import Sampler
+        if not isinstance(self.model, MotifChordModel) or self._key_mask is not None or self.cache is None:
+            return False
+        s = self.sampler if self.sampler is not None else self.model.sampler
+        if s is not None and (not isinstance(s, Sampler) or s.constraint is not None):
+            return False
+        cfg = self.model.config
+        has_chord = any(d.attn_type == 'chord' for blk in self.model.blocks for d in blk.features)
+        return has_chord and cfg.head_dim in (32, 64)
+
+    def _run_graph(self):
+        from .decode import GraphDecoder
+        s = self.sampler if self.sampler is not None else self.model.sampler
+        remaining = self.max_new_tokens - self.steps
+        dec = GraphDecoder(self.model, self.cache, max_steps=remaining, sampler=s, eos_ids=self.eos_ids or None,
+                           fill_id=self.fill_id, finished=self.finished)
+        first = self._next_input
+        try:
+            dec.set_history(self.sequences)
+            while remaining > 0:
+                k = min(self.sync_every, remaining)
+                saved = dec.save() if dec.eos is not None else None
+                toks = dec.run(first, k)
+                stop = k
+                if dec.eos is not None:
+                    flags = dec.all_done[dec.taken - k:dec.taken].cpu()  # the one host sync per chunk
+                    hit = torch.nonzero(flags).flatten()
+                    if hit.numel():
+                        stop = int(hit[0]) + 1
+                        if stop < k:  # rewind to the chunk's start and take exactly `stop` steps
+                            dec.load(saved)
+                            toks = dec.run(first, stop)
+                toks = toks.to(self.sequences.device)
+                self.sequences = torch.cat([self.sequences, toks], dim=1)
+                self.steps += stop
+                self.graph_steps += stop
+                remaining -= stop
+                first = toks[:, -1:]
+                if dec.eos is not None and bool(dec.finished.all()):
+                    break
+            self._next_input = first
+            if dec.eos is not None:
+                self.finished = dec.finished.to(self.finished.device).clone()
+        finally:
+            dec.release()

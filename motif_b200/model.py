@@ -375,7 +375,7 @@ class MotifChordModel(nn.Module):
         return self
 
     def generate(self, input_ids, max_new_tokens: int = 32, eos_token_id=None, sampler=None, cache=None,
-                 mask=None, tokenizer=None):
+                 mask=None, tokenizer=None, graph: bool = False, sync_every: int = 16):
         """`generate` (`model/motif.py:483-543`)."""
         from .generate import Generation
         active = sampler if sampler is not None else self.sampler
@@ -383,7 +383,8 @@ class MotifChordModel(nn.Module):
             eos_token_id = getattr(active, 'eos_token_id', None)
         if eos_token_id is None and tokenizer is not None:
             eos_token_id = getattr(tokenizer, 'token_eos', None)
-        return Generation(self, input_ids, max_new_tokens, eos_token_id, sampler, cache, mask, tokenizer)
+        return Generation(self, input_ids, max_new_tokens, eos_token_id, sampler, cache, mask, tokenizer,
+                          graph=graph, sync_every=sync_every)
 
     # ------------------------------------------------------------------ forward
     def forward(self, input_ids: torch.Tensor, cache: Optional[ModelCache] = None, labels=None,

@@ -164,3 +164,52 @@ def test_graph_sampled_matches_eager_generation(rp):
     assert s.offset == 1 + steps
     with pytest.raises(NotImplementedError):
         GraphDecoder(m, out.cache, max_steps=1, sampler=Sampler(**kw).with_constraint(object()))
+
+
+def _gdn_and_lengths(cache):
+    from motif_b200.cache import GatedDeltaAttentionLayerCache
+    states = [lc.state.clone() for bc in cache for lc in bc.attn if isinstance(lc, GatedDeltaAttentionLayerCache)]
+    return states, [lc.length for bc in cache for lc in bc.attn]
+
+
+@pytest.mark.parametrize('sampled,sync_every', [(False, 16), (False, 3), (True, 5), (True, 1)])
+def test_generation_graph_mode_matches_eager(sampled, sync_every):
+    """`generate(graph=True)`: device-side eos bookkeeping, one host read per chunk, and a
+    rewind when every row finished inside a chunk — the tokens, finished flags, recurrent
+    states and cache lengths equal the step-by-step loop's."""
+    from motif_b200.sampler import Sampler
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    m.decode_splits = 2
+    ids = torch.randint(0, 512, (3, 20), generator=torch.Generator().manual_seed(5)).cuda()
+    kw = dict(temperature=0.9, top_k=30, repetition_penalty=1.2, seed=3) if sampled else None
+    mk = (lambda: Sampler(**kw)) if sampled else (lambda: None)
+    with torch.no_grad():
+        probe = m.generate(ids, max_new_tokens=24, sampler=mk()).run().generated
+        # eos ids that end each row at a different step, the last one inside a chunk
+        eos = sorted({int(probe[0, 4]), int(probe[1, 9]), int(probe[2, 13])})
+        ref = m.generate(ids, max_new_tokens=24, eos_token_id=eos, sampler=mk()).run()
+        got = m.generate(ids, max_new_tokens=24, eos_token_id=eos, sampler=mk(), graph=True,
+                         sync_every=sync_every).run()
+    assert got.graph_steps > 0
+    assert torch.equal(got.sequences, ref.sequences), (got.generated, ref.generated)
+    assert torch.equal(got.finished, ref.finished) and got.steps == ref.steps
+    s_ref, l_ref = _gdn_and_lengths(ref.cache)
+    s_got, l_got = _gdn_and_lengths(got.cache)
+    assert l_got == l_ref
+    for a, b in zip(s_got, s_ref):
+        assert torch.equal(a, b)
+
+
+def test_generation_graph_mode_runs_to_max_tokens():
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    m.decode_splits = 2
+    ids = torch.randint(0, 512, (2, 17), generator=torch.Generator().manual_seed(6)).cuda()
+    with torch.no_grad():
+        ref = m.generate(ids, max_new_tokens=21).run()
+        got = m.generate(ids, max_new_tokens=21, graph=True, sync_every=8).run()
+    assert got.graph_steps == 20 and torch.equal(got.sequences, ref.sequences)
+    # continuing eagerly from the graph's cache gives the eager continuation
+    with torch.no_grad():
+        a = m.generate(ref.sequences, max_new_tokens=4, cache=ref.cache).run().generated
+        b = m.generate(got.sequences, max_new_tokens=4, cache=got.cache).run().generated
+    assert torch.equal(a, b)
