@@ -397,15 +397,14 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
     T* rkd = reinterpret_cast<T*>(rec + Rec::off_kd);
     // Every 16-byte vector of the record is written, the row pads included (as zeros), so that
     // no L2 sector is left partly written (a partial sector is read back from DRAM to merge).
-    constexpr int QV = DK / E;  // 16-byte vectors per q / k row
+    // One loop per plane over (row, vector) with a power-of-two vector count per row keeps the
+    // index arithmetic to shifts and masks.
+    constexpr int QV = DK / E;  // 16-byte vectors per q / k / W row
+    constexpr int UV = Rec::SW / E, AV = C / E;
+    static_assert((QV & (QV - 1)) == 0 && (UV & (UV - 1)) == 0 && (AV & (AV - 1)) == 0, "power-of-two rows");
     const float gl = sGam[C - 1];
-    for (int i = tid; i < C * (QV + 1); i += NT) {
-      const int r = i / (QV + 1), c = (i % (QV + 1)) * E;
-      if (c == DK) {
-        *reinterpret_cast<uint4*>(&rqs[r * QS + c]) = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(&rkd[r * QS + c]) = make_uint4(0, 0, 0, 0);
-        continue;
-      }
+    for (int i = tid; i < C * QV; i += NT) {  // q e^gamma, k e^{gamma_L - gamma}
+      const int r = i / QV, c = (i % QV) * E;
       const float eq = sEg[r], ek = __expf(gl - sGam[r]);
       const uint4 vq = *reinterpret_cast<const uint4*>(&cQ[r * QS + c]);
       const uint4 vk = *reinterpret_cast<const uint4*>(&cK[r * QS + c]);
@@ -422,28 +421,35 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       *reinterpret_cast<uint4*>(&rqs[r * QS + c]) = oq;
       *reinterpret_cast<uint4*>(&rkd[r * QS + c]) = ok;
     }
-    // per row: the W plane (WV vectors + pad), each U plane (UV + pad), Aq (AV + pad)
-    constexpr int AV = C / E, WV = DK / E, UV = Rec::SW / E;
-    constexpr int RV = (WV + 1) + Rec::NSL * (UV + 1) + (AV + 1);
     T* rw = reinterpret_cast<T*>(rec + Rec::off_w);
     T* raq = reinterpret_cast<T*>(rec + Rec::off_aq);
-    for (int i = tid; i < C * RV; i += NT) {
-      const int r = i / RV, c = i % RV;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      T* dst;
-      if (c <= WV) {
-        dst = &rw[r * QS + c * E];
-        if (c < WV) val = *reinterpret_cast<const uint4*>(&sX[r * XS + c * E]);
-      } else if (c < (WV + 1) + Rec::NSL * (UV + 1)) {
-        const int j = (c - WV - 1) / (UV + 1), cu = (c - WV - 1) % (UV + 1);
-        dst = reinterpret_cast<T*>(rec + Rec::shared_bytes + j * Rec::u_bytes) + r * Rec::US + cu * E;
-        if (cu < UV) val = *reinterpret_cast<const uint4*>(&sX[r * XS + DK + j * Rec::SW + cu * E]);
-      } else {
-        const int ca = c - (WV + 1) - Rec::NSL * (UV + 1);
-        dst = &raq[r * AS + ca * E];
-        if (ca < AV) val = *reinterpret_cast<const uint4*>(&sAq[r * AS + ca * E]);
+    for (int i = tid; i < C * QV; i += NT) {  // W = the first DK columns of [W | U]
+      const int r = i / QV, c = (i % QV) * E;
+      *reinterpret_cast<uint4*>(&rw[r * QS + c]) = *reinterpret_cast<const uint4*>(&sX[r * XS + c]);
+    }
+#pragma unroll
+    for (int j = 0; j < Rec::NSL; ++j) {  // U, one plane per slice of SW value columns
+      T* ru = reinterpret_cast<T*>(rec + Rec::shared_bytes + j * Rec::u_bytes);
+      for (int i = tid; i < C * UV; i += NT) {
+        const int r = i / UV, c = (i % UV) * E;
+        *reinterpret_cast<uint4*>(&ru[r * Rec::US + c]) =
+            *reinterpret_cast<const uint4*>(&sX[r * XS + DK + j * Rec::SW + c]);
       }
-      *reinterpret_cast<uint4*>(dst) = val;
+    }
+    for (int i = tid; i < C * AV; i += NT) {  // Aq
+      const int r = i / AV, c = (i % AV) * E;
+      *reinterpret_cast<uint4*>(&raq[r * AS + c]) = *reinterpret_cast<const uint4*>(&sAq[r * AS + c]);
+    }
+    // the pads: one 16-byte vector at the end of every row of every plane
+    constexpr int NPAD = 4 + Rec::NSL;  // Qs, Kd, W, Aq, U planes
+    for (int i = tid; i < C * NPAD; i += NT) {
+      const int r = i % C, p = i / C;
+      T* dst = p == 0 ? &rqs[r * QS + DK]
+             : p == 1 ? &rkd[r * QS + DK]
+             : p == 2 ? &rw[r * QS + DK]
+             : p == 3 ? &raq[r * AS + C]
+                      : reinterpret_cast<T*>(rec + Rec::shared_bytes + (p - 4) * Rec::u_bytes) + r * Rec::US + Rec::SW;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
     if (tid == 0) *reinterpret_cast<float4*>(rec + Rec::off_el) = make_float4(sEg[C - 1], 0.f, 0.f, 0.f);
   }
