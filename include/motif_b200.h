@@ -123,6 +123,18 @@ MB_API int motif_b200_chord_attention(const void* q, const void* k, const void* 
                                float softmax_scale, float eps, const int64_t* strides, int dtype,
                                void* workspace, int64_t workspace_bytes, void* stream);
 
+/* motif_b200_chord_attention with an additive key bias: key_bias[b * key_bias_stride + s]
+ * (fp32, natural-log units, -inf drops key s of sequence b) is added to every logit after the
+ * ssmax * log n scaling, as ChordAttention applies `attention_mask` (a bool keep-mask as
+ * 0 / -inf, or a float mask as is; motif/block/attention/chord_attn.py:347-356).  A row whose
+ * keys are all dropped yields zeros (the reference's softmax yields NaN there). */
+MB_API int motif_b200_chord_attention_masked(const void* q, const void* k, const void* v, const float* alpha,
+                                      const float* beta, const float* mu, const float* ssmax,
+                                      const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
+                                      int64_t L, int64_t S, int64_t D, int64_t q_start, float scale,
+                                      float eps, const int64_t* strides, const float* key_bias,
+                                      int64_t key_bias_stride, int dtype, void* stream);
+
 /* ------------------------------------------------------------------ attn-res / norms
  * Depth softmax over n_src (1..8) aligned [B,T,D] sources: logit_s = query . (weight *
  * rmsnorm(x_s)), h = sum_s softmax_s * x_s.  `src_strides` holds (batch, time) element
@@ -241,6 +253,16 @@ MB_API int motif_b200_chord_decode(const void* q, const void* k_cache, const voi
                             int64_t T, int64_t D, float softmax_scale, float eps,
                             int max_splits, void* workspace, int64_t workspace_bytes, int dtype,
                             void* stream);
+
+/* motif_b200_chord_decode with the additive key bias of motif_b200_chord_attention_masked
+ * (row stride key_bias_stride >= the attended length). */
+MB_API int motif_b200_chord_decode_masked(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                                   const int32_t* len_dev, int64_t len_host, const float* alpha,
+                                   const float* beta, const float* mu, const float* ssmax, void* out,
+                                   int64_t out_stride, int64_t B, int64_t H, int64_t Hkv, int64_t T, int64_t D,
+                                   float scale, float eps, int max_splits, const float* key_bias,
+                                   int64_t key_bias_stride, void* workspace, int64_t workspace_bytes,
+                                   int dtype, void* stream);
 
 /* motif_b200_chord_decode without a caller-provided workspace: for callers that cannot
  * allocate device memory (a runtime bound through a plain C FFI with no CUDA allocator of

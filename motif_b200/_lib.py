@@ -51,6 +51,10 @@ SIGNATURES = {
     'motif_b200_chord_decode_workspace_bytes': (_I64, [_I64, _I64, _I64, _I64, _I]),
     'motif_b200_chord_decode': (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                                      _I64, _I64, _F, _F, _I, _P, _I64, _I, _P]),
+    'motif_b200_chord_attention_masked': (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                                               _I64, _I64, _F, _F, _P, _P, _I64, _I, _P]),
+    'motif_b200_chord_decode_masked': (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                            _I64, _I64, _F, _F, _I, _P, _I64, _P, _I64, _I, _P]),
     'motif_b200_chord_decode_noalloc': (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                                              _I64, _I64, _I64, _F, _F, _I, _I, _P]),
     'motif_b200_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
@@ -130,6 +134,7 @@ KERNELS_PER_CALL.update({'motif_b200_last_error': 0, 'motif_b200_abi_version': 0
                          'motif_b200_skinny_gemm_workspace_bytes': 0, 'motif_b200_gdn_chunk_workspace_bytes': 0,
                          'motif_b200_wait_timeouts': 0,
                          'motif_b200_chord_decode': 2, 'motif_b200_chord_decode_noalloc': 2,
+                         'motif_b200_chord_decode_masked': 2,
                          'motif_b200_gdn_chunk_gated_ws': 3, 'motif_b200_gdn_prefill_ws': 3})
 
 

@@ -319,7 +319,8 @@ struct TcSmemLayout {
   static constexpr int offV = offK + tc::kStages * tc::kTileBytes;
   static constexpr int offP = offV + tc::kStages * tc::kTileBytes;  // 2 warpgroups x 2 atoms of 64 keys
   static constexpr int offBias = offP + 4 * tc::kTileBytes;         // 2 warpgroups x 2 tiles
-  static constexpr int offBar = offBias + 4 * G * TBLS * 4;
+  static constexpr int offKm = offBias + 4 * G * TBLS * 4;          // key bias: 2 warpgroups x 2 tiles
+  static constexpr int offBar = offKm + 4 * tc::kKeys * 4;
   static constexpr int nBar = 1 + tc::kStages + 6;  // q, kv[], s[2], o[2], drain[2]
   static constexpr int offCnt = offBar + nBar * 8;   // per-stage release count, last tile issued
   static constexpr int offTmem = offCnt + 2 * tc::kStages * 4;
@@ -327,12 +328,15 @@ struct TcSmemLayout {
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
 
-template <typename T, int G>
+// KM: an additive key bias kmask[b * kms + key] (natural-log units, -inf drops the key) is
+// added to every logit, as the attention mask of chord_attn.py:347-356.
+template <typename T, int G, bool KM>
 __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const float* __restrict__ alpha, const float* __restrict__ beta,
     const float* __restrict__ mu, const float* __restrict__ ssmax, const float* __restrict__ log_n,
-    T* __restrict__ out, int H, int Hkv, int L, int S, int q_start, float scale, float eps, Strides14 sv) {
+    T* __restrict__ out, int H, int Hkv, int L, int S, int q_start, float scale, float eps, Strides14 sv,
+    const float* __restrict__ kmask, int64_t kms) {
   using Lay = TcSmemLayout<G>;
   constexpr int BMQ = Lay::BMQ, TBL = Lay::TBL, TBLS = Lay::TBLS, NS = tc::kStages;
   constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
@@ -384,10 +388,12 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   const float sgn = ssh < 0.f ? -1.f : 1.f;
   const float rcs = row_ok ? fmaxf(fabsf(ssh * log_n[b * st[12] + (int64_t)pos * st[13]] * kLog2e), 1e-30f) : 1e-30f;
   const float scale_s = sgn * scale;
+  const float inv_rcs = 1.f / rcs;  // a key bias m (natural log) enters x as m log2(e) / |rc|
 
   unsigned char* sQw = sQ + wg * tc::kTileBytes;
   unsigned char* sPw = sm + Lay::offP + wg * 2 * tc::kTileBytes;
   float* sBw = reinterpret_cast<float*>(sm + Lay::offBias) + wg * 2 * G * TBLS;
+  float* sKmw = reinterpret_cast<float*>(sm + Lay::offKm) + wg * 2 * tc::kKeys;
 
   if (warp == 0) tmem_alloc(sTmem, tc::kTmemCols);
   if (tid == 0) {
@@ -435,6 +441,10 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       const int hh = h0 + g;
       const float b0 = ggd_bias_decode<T>(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
       tb[g * TBLS + ee] = ssmax[hh] < 0.f ? -b0 : b0;
+    }
+    if constexpr (KM) {  // the tile's key bias in log2 units
+      const int key = j * tc::kKeys + wt;
+      sKmw[(j & 1) * tc::kKeys + wt] = key < S ? kmask[(int64_t)b * kms + key] * kLog2e : 0.f;
     }
   };
 
@@ -505,6 +515,11 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127;  // key offset c -> tb[-c]
 #pragma unroll
     for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(x[c], scale_s, tb[-c]);
+    if constexpr (KM) {
+      const float* km = sKmw + (j & 1) * tc::kKeys;
+#pragma unroll
+      for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(km[c], inv_rcs, x[c]);
+    }
     if (cmax < tc::kKeys - 1) {
 #pragma unroll
       for (int c = 0; c < tc::kKeys; ++c)
@@ -618,7 +633,7 @@ __global__ void __launch_bounds__(128) chord_fwd_simple_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ alpha,
     const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
     const float* __restrict__ log_n, T* __restrict__ out, int H, int Hkv, int L, int S, int D, int q_start,
-    float scale, float eps, Strides14 sv) {
+    float scale, float eps, Strides14 sv, const float* __restrict__ kmask, int64_t kms) {
   const int64_t* st = sv.s;
   extern __shared__ float sq_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -652,11 +667,13 @@ __global__ void __launch_bounds__(128) chord_fwd_simple_kernel(
       float s = 0.f;
       for (int d = 0; d < D; ++d) s = fmaf(sq[d], to_f(kr[d]), s);
       x = (s * scale + ggd_bias(al, be, m_u, (float)(qa - j), eps)) * c;
+      if (kmask) x = fmaf(kmask[(int64_t)b * kms + j], kLog2e, x);
     }
     const float cm = warp_max(x);
     const float mn = fmaxf(m, cm);
-    const float corr = exp2f(m - mn);
-    const float p = exp2f(x - mn);
+    const float mb = mn == -INFINITY ? 0.f : mn;  // every key so far dropped by the mask
+    const float corr = exp2f(m - mb);
+    const float p = exp2f(x - mb);
     l = l * corr + warp_sum(p);
 #pragma unroll
     for (int r = 0; r < MAXD; ++r) o[r] *= corr;
@@ -745,7 +762,8 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
     const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int64_t cap,
     const int32_t* __restrict__ len_dev, int len_host, const float* __restrict__ alpha,
     const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
-    float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps) {
+    float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps,
+    const float* __restrict__ kmask, int64_t kms) {
   constexpr int QD = D / 8;   // dims per lane in the score phase
   constexpr int OD = D / 32;  // output dims per lane
   constexpr int RW = RM / 4;  // rows per warp in the softmax / PV phase
@@ -861,8 +879,10 @@ __global__ void __launch_bounds__(128) chord_decode_kernel(
           if (rr == r) a = acc[rr];
         if (r < R) {
           float x = -INFINITY;
-          if (kk < nk && j <= qa[u])
+          if (kk < nk && j <= qa[u]) {
             x = (a * scale + ggd_bias_decode<T>(pa[u], pb[u], pm[u], (float)(qa[u] - j), eps)) * rc[u];
+            if (kmask) x = fmaf(kmask[(int64_t)b * kms + j], kLog2e, x);  // key bias (mask)
+          }
           sm.p[r][kk] = x;
         }
       }
@@ -961,7 +981,8 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const T* __restrict__ q,
     int64_t cap, const int32_t* __restrict__ len_dev, int len_host, const float* __restrict__ alpha,
     const float* __restrict__ beta, const float* __restrict__ mu, const float* __restrict__ ssmax,
-    float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps) {
+    float* __restrict__ ws, int B, int H, int Hkv, int Tn, int nsplit, float scale, float eps,
+    const float* __restrict__ kmask, int64_t kms) {
   constexpr int D = 64;
   constexpr int TILE_BYTES = kDecTile * D * 2;  // 8 KB, rows of 128 bytes
   extern __shared__ unsigned char dec_mma_smem[];
@@ -1077,9 +1098,11 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
         const int kl = warp * 16 + nt * 8 + 2 * t4 + (e & 1);
         const int j = j0 + kl;
         float x = -INFINITY;
-        if (rv[ri] && kl < nk && j <= rqa[ri])
+        if (rv[ri] && kl < nk && j <= rqa[ri]) {
           x = (sacc[nt][e] * scale + ggd_bias_decode<T>(ral[ri], rbe[ri], rmu[ri], (float)(rqa[ri] - j), eps)) *
               rrc[ri];
+          if (kmask) x = fmaf(kmask[(int64_t)b * kms + j], kLog2e, x);  // key bias (mask)
+        }
         sacc[nt][e] = x;
         rmax[ri] = fmaxf(rmax[ri], x);
       }
@@ -1307,11 +1330,11 @@ template <typename T>
 int launch_simple(const void* q, const void* k, const void* v, const float* alpha, const float* beta, const float* mu,
                   const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L,
                   int64_t S, int64_t D, int64_t q_start, float scale, float eps, const Strides14& sv,
-                  cudaStream_t st) {
+                  cudaStream_t st, const float* kmask = nullptr, int64_t kms = 0) {
   dim3 grid((unsigned)((H * L + 3) / 4), (unsigned)B);
   chord_fwd_simple_kernel<T><<<grid, 128, 4 * D * sizeof(float), st>>>(
       (const T*)q, (const T*)k, (const T*)v, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
-      (int)S, (int)D, (int)q_start, scale, eps, sv);
+      (int)S, (int)D, (int)q_start, scale, eps, sv, kmask, kms);
   return check_launch("chord_fwd_simple");
 }
 
@@ -1341,11 +1364,11 @@ static bool chord_tc_disabled() {
   return e && e[0] == '0';
 }
 
-template <typename T, int G>
+template <typename T, int G, bool KM>
 int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha, const float* beta, const float* mu,
                 const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L,
                 int64_t S, int64_t q_start, float scale, float eps, const int64_t* strides, const Strides14& sv,
-                cudaStream_t st) {
+                cudaStream_t st, const float* kmask, int64_t kms) {
   using Lay = TcSmemLayout<G>;
   CUtensorMap tmQ, tmK, tmV;
   {
@@ -1364,7 +1387,7 @@ int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha,
     if (!rc) rc = encode_tile_map(&tmV, v, 2, 4, dims, svv, box, 128);
     if (rc) return rc;
   }
-  auto kern = chord_tc_kernel<T, G>;
+  auto kern = chord_tc_kernel<T, G, KM>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1376,30 +1399,40 @@ int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha,
   const int GS = (int)(H / Hkv);
   dim3 grid((unsigned)((L + 2 * Lay::BMQ - 1) / (2 * Lay::BMQ)), (unsigned)(Hkv * (GS / G)), (unsigned)B);
   kern<<<grid, 256, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
-                                     (int)S, (int)q_start, scale, eps, sv);
+                                     (int)S, (int)q_start, scale, eps, sv, kmask, kms);
   return check_launch("chord_attention (tcgen05)");
+}
+
+template <typename T, bool KM>
+int launch_tc_km(int G, const void* q, const void* k, const void* v, const float* alpha, const float* beta,
+                 const float* mu, const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H,
+                 int64_t Hkv, int64_t L, int64_t S, int64_t q_start, float scale, float eps, const int64_t* strides,
+                 const Strides14& sv, cudaStream_t st, const float* kmask, int64_t kms) {
+  switch (G) {
+    case 8: return launch_tc_g<T, 8, KM>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st, kmask, kms);
+    case 4: return launch_tc_g<T, 4, KM>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st, kmask, kms);
+    case 2: return launch_tc_g<T, 2, KM>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st, kmask, kms);
+    default: return launch_tc_g<T, 1, KM>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st, kmask, kms);
+  }
 }
 
 template <typename T>
 int launch_tc(int G, const void* q, const void* k, const void* v, const float* alpha, const float* beta,
               const float* mu, const float* ssmax, const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
               int64_t L, int64_t S, int64_t q_start, float scale, float eps, const int64_t* strides,
-              const Strides14& sv, cudaStream_t st) {
-  switch (G) {
-    case 8: return launch_tc_g<T, 8>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
-    case 4: return launch_tc_g<T, 4>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
-    case 2: return launch_tc_g<T, 2>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
-    default: return launch_tc_g<T, 1>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps, strides, sv, st);
-  }
+              const Strides14& sv, cudaStream_t st, const float* kmask = nullptr, int64_t kms = 0) {
+  if (kmask)
+    return launch_tc_km<T, true>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale,
+                                 eps, strides, sv, st, kmask, kms);
+  return launch_tc_km<T, false>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps,
+                                strides, sv, st, nullptr, 0);
 }
 
-extern "C" int motif_b200_chord_attention(const void* q, const void* k, const void* v, const float* alpha,
-                                          const float* beta, const float* mu, const float* ssmax, const float* log_n,
-                                          void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L, int64_t S,
-                                          int64_t D, int64_t q_start, float scale, float eps, const int64_t* strides,
-                                          int dtype, void* workspace, int64_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
+static int chord_attention_impl(const void* q, const void* k, const void* v, const float* alpha, const float* beta,
+                                const float* mu, const float* ssmax, const float* log_n, void* out, int64_t B,
+                                int64_t H, int64_t Hkv, int64_t L, int64_t S, int64_t D, int64_t q_start, float scale,
+                                float eps, const int64_t* strides, int dtype, const float* kmask, int64_t kms,
+                                void* stream) {
   MB_REQUIRE(strides, MB_ERR_ARG, "chord: null strides");
   MB_REQUIRE(B >= 0 && B < 65536 && H > 0 && Hkv > 0 && L >= 0 && S >= 0 && D > 0, MB_ERR_SHAPE,
              "chord: bad shape");
@@ -1433,14 +1466,38 @@ extern "C" int motif_b200_chord_attention(const void* q, const void* k, const vo
     using T = decltype(t);
     if constexpr (sizeof(T) == 2) {
       if (tc_ok) return launch_tc<T>(G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale,
-                                     eps, strides, sv, st);
-      if (mma_ok)
+                                     eps, strides, sv, st, kmask, kms);
+      if (mma_ok && kmask == nullptr)  // the mma.sync kernel takes no key bias: masked calls use the simple one
         return launch_mma<T>(D, G, q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, q_start, scale, eps,
                              sv, st);
     }
     return launch_simple<T>(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, D, q_start, scale, eps,
-                            sv, st);
+                            sv, st, kmask, kms);
   });
+}
+
+extern "C" int motif_b200_chord_attention(const void* q, const void* k, const void* v, const float* alpha,
+                                          const float* beta, const float* mu, const float* ssmax, const float* log_n,
+                                          void* out, int64_t B, int64_t H, int64_t Hkv, int64_t L, int64_t S,
+                                          int64_t D, int64_t q_start, float scale, float eps, const int64_t* strides,
+                                          int dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  return chord_attention_impl(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, D, q_start, scale, eps,
+                              strides, dtype, nullptr, 0, stream);
+}
+
+extern "C" int motif_b200_chord_attention_masked(const void* q, const void* k, const void* v, const float* alpha,
+                                                 const float* beta, const float* mu, const float* ssmax,
+                                                 const float* log_n, void* out, int64_t B, int64_t H, int64_t Hkv,
+                                                 int64_t L, int64_t S, int64_t D, int64_t q_start, float scale,
+                                                 float eps, const int64_t* strides, const float* key_bias,
+                                                 int64_t key_bias_stride, int dtype, void* stream) {
+  MB_REQUIRE(key_bias != nullptr || B == 0 || L == 0, MB_ERR_ARG, "chord (masked): null key bias");
+  MB_REQUIRE(key_bias_stride >= S, MB_ERR_SHAPE, "chord (masked): key bias row stride %lld below S %lld",
+             (long long)key_bias_stride, (long long)S);
+  return chord_attention_impl(q, k, v, alpha, beta, mu, ssmax, log_n, out, B, H, Hkv, L, S, D, q_start, scale, eps,
+                              strides, dtype, key_bias, key_bias_stride, stream);
 }
 
 extern "C" int64_t motif_b200_chord_decode_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t D,
@@ -1448,12 +1505,12 @@ extern "C" int64_t motif_b200_chord_decode_workspace_bytes(int64_t B, int64_t H,
   return (int64_t)max_splits * B * H * T * (D + 2) * (int64_t)sizeof(float);
 }
 
-extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
-                                       const int32_t* len_dev, int64_t len_host, const float* alpha,
-                                       const float* beta, const float* mu, const float* ssmax, void* out,
-                                       int64_t out_stride, int64_t B, int64_t H, int64_t Hkv, int64_t T, int64_t D,
-                                       float scale, float eps, int max_splits, void* workspace,
-                                       int64_t workspace_bytes, int dtype, void* stream) {
+static int chord_decode_impl(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                             const int32_t* len_dev, int64_t len_host, const float* alpha, const float* beta,
+                             const float* mu, const float* ssmax, void* out, int64_t out_stride, int64_t B, int64_t H,
+                             int64_t Hkv, int64_t T, int64_t D, float scale, float eps, int max_splits,
+                             void* workspace, int64_t workspace_bytes, int dtype, const float* kmask, int64_t kms,
+                             void* stream) {
   MB_REQUIRE(q && k_cache && v_cache && alpha && beta && mu && ssmax && out && workspace, MB_ERR_ARG,
              "chord_decode: null pointer");
   MB_REQUIRE(B > 0 && B < 65536 && H > 0 && Hkv > 0 && H % Hkv == 0 && T > 0 && cap > 0, MB_ERR_SHAPE,
@@ -1491,7 +1548,8 @@ extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const
             if (dev >= 0 && dev < 64) attr_set[dev] = true;
           }
           kern<<<grid, 128, smem, st>>>(tmK, tmV, (const Tt*)q, cap, len_dev, (int)len_host, alpha, beta, mu, ssmax,
-                                        (float*)workspace, (int)B, (int)H, (int)Hkv, (int)T, max_splits, scale, eps);
+                                        (float*)workspace, (int)B, (int)H, (int)Hkv, (int)T, max_splits, scale, eps,
+                                        kmask, kms);
           rc = check_launch("chord_decode");
           if (rc) return rc;
           chord_merge_kernel<Tt, DD><<<(unsigned)((B * T * H + 3) / 4), 128, 0, st>>>(
@@ -1513,7 +1571,7 @@ extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const
         }
         kern<<<grid, 128, smem, st>>>((const Tt*)q, (const Tt*)k_cache, (const Tt*)v_cache, cap, len_dev,
                                       (int)len_host, alpha, beta, mu, ssmax, (float*)workspace, (int)B, (int)H,
-                                      (int)Hkv, (int)T, max_splits, scale, eps);
+                                      (int)Hkv, (int)T, max_splits, scale, eps, kmask, kms);
         return check_launch("chord_decode");
       };
       int rc = R <= 4 ? launch(std::integral_constant<int, 4>{})
@@ -1529,6 +1587,31 @@ extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const
       default: return set_error(MB_ERR_UNSUPPORTED, "chord_decode: head dim %lld", (long long)D);
     }
   });
+}
+
+extern "C" int motif_b200_chord_decode(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                                       const int32_t* len_dev, int64_t len_host, const float* alpha,
+                                       const float* beta, const float* mu, const float* ssmax, void* out,
+                                       int64_t out_stride, int64_t B, int64_t H, int64_t Hkv, int64_t T, int64_t D,
+                                       float scale, float eps, int max_splits, void* workspace,
+                                       int64_t workspace_bytes, int dtype, void* stream) {
+  return chord_decode_impl(q, k_cache, v_cache, cap, len_dev, len_host, alpha, beta, mu, ssmax, out, out_stride, B, H,
+                           Hkv, T, D, scale, eps, max_splits, workspace, workspace_bytes, dtype, nullptr, 0, stream);
+}
+
+extern "C" int motif_b200_chord_decode_masked(const void* q, const void* k_cache, const void* v_cache, int64_t cap,
+                                              const int32_t* len_dev, int64_t len_host, const float* alpha,
+                                              const float* beta, const float* mu, const float* ssmax, void* out,
+                                              int64_t out_stride, int64_t B, int64_t H, int64_t Hkv, int64_t T,
+                                              int64_t D, float scale, float eps, int max_splits,
+                                              const float* key_bias, int64_t key_bias_stride, void* workspace,
+                                              int64_t workspace_bytes, int dtype, void* stream) {
+  MB_REQUIRE(key_bias != nullptr, MB_ERR_ARG, "chord_decode (masked): null key bias");
+  MB_REQUIRE(key_bias_stride >= (len_dev ? cap : len_host), MB_ERR_SHAPE,
+             "chord_decode (masked): key bias row stride %lld below the attended length", (long long)key_bias_stride);
+  return chord_decode_impl(q, k_cache, v_cache, cap, len_dev, len_host, alpha, beta, mu, ssmax, out, out_stride, B, H,
+                           Hkv, T, D, scale, eps, max_splits, workspace, workspace_bytes, dtype, key_bias,
+                           key_bias_stride, stream);
 }
 
 // Vectorised preparation for 16-bit rows with D in {32, 64, 128}: a group of D/8 lanes owns

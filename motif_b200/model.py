@@ -402,14 +402,14 @@ class MotifChordModel(nn.Module):
             if mask.shape != (input_ids.shape[0], width):
                 raise ValueError(f'mask {tuple(mask.shape)} does not cover the {width} keys of a {cached}-position '
                                  f'cache plus {input_ids.shape[1]} inputs')
-            if not bool(mask.all()):
-                raise NotImplementedError('attention masks are not supported by the fused path yet')
+            key_bias = _key_bias(mask, self.embed.weight.device)
         if isinstance(position, torch.Tensor):
             position = int(position.reshape(-1)[0])
         if cache is None:
             cache = self.create_cache()
         with torch.no_grad():
-            logits, x_final = _forward(self, input_ids.to(self.embed.weight.device), cache, position or 0)
+            logits, x_final = _forward(self, input_ids.to(self.embed.weight.device), cache, position or 0,
+                                       key_bias if mask is not None else None)
         loss = None
         if labels is not None:
             loss = F.cross_entropy(logits.view(-1, logits.size(-1)).float(), labels.view(-1).to(logits.device),
@@ -473,7 +473,8 @@ def _norm_read(sources: List[torch.Tensor], query, weight, h_out, hn_out, eps_sr
               rows, d, float(eps_src), float(eps_out), _lib.dtype_code(x0.dtype), _lib.stream_ptr(x0.device))
 
 
-def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, position: int):
+def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, position: int,
+             key_bias: Optional[torch.Tensor] = None):
     cfg = model.config
     decs, lm = model.packed()
     B, T = ids.shape
@@ -512,7 +513,7 @@ def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, posit
             if dec.attn_type == 'chord':
                 if layer_cache is not None and not isinstance(layer_cache, KVLayerCache):
                     raise TypeError(f'ChordAttention requires KVLayerCache, got {type(layer_cache).__name__}')
-                f = _chord_decoder(model, pk, proj, B, T, layer_cache, position, dt, dev, dc, st)
+                f = _chord_decoder(model, pk, proj, B, T, layer_cache, position, dt, dev, dc, st, key_bias)
             else:
                 if layer_cache is not None and not isinstance(layer_cache, GatedDeltaAttentionLayerCache):
                     raise TypeError(f'GatedDeltaAttention requires GatedDeltaAttentionLayerCache, '
@@ -624,8 +625,10 @@ def _decode_splits(model, B, Hkv, S):
     return int(max(1, min(want, 64, (S + 255) // 256)))
 
 
-def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCache], position, dt, dev, dc, st):
-    """`ChordAttention.forward` (fused path) + SwiGLU MLP + parallel residual."""
+def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCache], position, dt, dev, dc, st,
+                   key_bias: Optional[torch.Tensor] = None):
+    """`ChordAttention.forward` (fused path) + SwiGLU MLP + parallel residual.  `key_bias`
+    ([B, S] fp32, natural-log units) is the attention mask as an additive key bias."""
     M = B * T
     H, Hkv, D, hid = pk.H, pk.Hkv, pk.D, pk.hid
     d = H * D
@@ -652,15 +655,28 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
         splits = _decode_splits(model, B, Hkv, S)
         ws_bytes = _lib.load().motif_b200_chord_decode_workspace_bytes(B, H, T, D, splits)
         ws = torch.empty((ws_bytes // 4,), dtype=torch.float32, device=dev)
-        _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cap, None,
-                  S, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax), _lib.ptr(attn), d,
-                  B, H, Hkv, T, D, scale, GGD_EPS, splits, _lib.ptr(ws), ws_bytes, dc, st)
+        if key_bias is None:
+            _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cap,
+                      None, S, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax),
+                      _lib.ptr(attn), d, B, H, Hkv, T, D, scale, GGD_EPS, splits, _lib.ptr(ws), ws_bytes, dc, st)
+        else:
+            _lib.call('motif_b200_chord_decode_masked', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf),
+                      cap, None, S, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax),
+                      _lib.ptr(attn), d, B, H, Hkv, T, D, scale, GGD_EPS, splits, _lib.ptr(key_bias),
+                      key_bias.stride(0), _lib.ptr(ws), ws_bytes, dc, st)
     else:
         log_n = _log_n(q_start, T, dev)
         strides = [T * d, D, d, Hkv * cap * D, cap * D, D, Hkv * cap * D, cap * D, D, T * d, D, d, 0, 1]
-        _lib.call('motif_b200_chord_attention', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf),
-                  _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax), _lib.ptr(log_n),
-                  _lib.ptr(attn), B, H, Hkv, T, S, D, q_start, scale, GGD_EPS, _lib.i64_array(strides), dc, None, 0, st)
+        if key_bias is None:
+            _lib.call('motif_b200_chord_attention', _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf),
+                      _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax), _lib.ptr(log_n),
+                      _lib.ptr(attn), B, H, Hkv, T, S, D, q_start, scale, GGD_EPS, _lib.i64_array(strides), dc, None,
+                      0, st)
+        else:
+            _lib.call('motif_b200_chord_attention_masked', _lib.ptr(qb), _lib.ptr(cache._kbuf),
+                      _lib.ptr(cache._vbuf), _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu),
+                      _lib.ptr(pk.ssmax), _lib.ptr(log_n), _lib.ptr(attn), B, H, Hkv, T, S, D, q_start, scale,
+                      GGD_EPS, _lib.i64_array(strides), _lib.ptr(key_bias), key_bias.stride(0), dc, st)
     act = torch.empty((M, hid), dtype=dt, device=dev)
     _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid, N_in,
               hid, dc, st)
@@ -669,6 +685,19 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
     _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(), N_in,
               _lib.ptr(f), d, _lib.ptr(f), d, M, d, dc, st)
     return f
+
+
+def _key_bias(mask: torch.Tensor, dev) -> Optional[torch.Tensor]:
+    """The model's `[B, cached + T]` key mask (`motif.py:592-602`) as the Chord kernels' additive
+    key bias ([B, S] fp32): a bool keep-mask becomes 0 / -inf, a float mask is added as is
+    (`chord_attn.py:347-356`).  None when it changes nothing (all True, or all zeros)."""
+    if mask.dtype == torch.bool:
+        if bool(mask.all()):
+            return None
+        kb = torch.zeros(mask.shape, dtype=torch.float32, device=dev)
+        return kb.masked_fill_(~mask.to(dev), float('-inf'))
+    kb = mask.to(device=dev, dtype=torch.float32).contiguous()
+    return None if not bool(kb.any()) else kb
 
 
 _LOG_TABLE: Dict[str, torch.Tensor] = {}

@@ -246,14 +246,18 @@ def forward(P, cfg, input_ids, cache: Optional[ModelCache] = None, position=None
 
 
 @torch.no_grad()
-def greedy(P, cfg, input_ids, steps):
-    """Prefill then `steps` greedy tokens, `model/generate.py:138-171` + `motif.py:92-98`."""
-    logits, _, cache = forward(P, cfg, input_ids)
+def greedy(P, cfg, input_ids, steps, mask=None):
+    """Prefill then `steps` greedy tokens, `model/generate.py:138-171` + `motif.py:92-98`.  A key
+    `mask` over the prompt is widened by one True column per token fed, as `Generation.step`
+    does (`torch.cat` with a bool column: a float mask gains 1.0 columns by type promotion)."""
+    logits, _, cache = forward(P, cfg, input_ids, mask=mask)
     tok = logits[:, -1].argmax(-1, keepdim=True)
     toks = [tok]
     margins = []
     for _ in range(steps - 1):
-        logits, _, cache = forward(P, cfg, tok, cache)
+        if mask is not None:
+            mask = torch.cat([mask, torch.ones_like(tok, dtype=torch.bool)], dim=1)
+        logits, _, cache = forward(P, cfg, tok, cache, mask=mask)
         top2 = logits[:, -1].float().topk(2, dim=-1).values
         margins.append((top2[:, 0] - top2[:, 1]).min().item())
         tok = logits[:, -1].argmax(-1, keepdim=True)

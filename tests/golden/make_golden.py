@@ -163,6 +163,38 @@ def main():
         out[f'small_{dtype_name}'] = dict(ids=ids, logits=full, decode_logits=torch.stack(steps, 1),
                                           greedy=gen_ids)
 
+    # --- small model with attention masks (chord_attn.py:347-356, motif.py:592-602): a bool
+    # keep-mask with a hole and right padding, and an additive float mask; prefill logits,
+    # chunked prefill + decode with the mask widened every step, masked greedy generation
+    torch.manual_seed(0)
+    model = MotifChordModel(MotifChordConfig(**SMALL))
+    init_params(model, seed=0, norm_jitter=0.1)
+    model = model.eval()
+    ids = torch.randint(0, SMALL['vocab_size'], (2, 40), generator=_gen(31))
+    keep = torch.ones(2, 40, dtype=torch.bool)
+    keep[0, 5:8] = False
+    keep[1, 32:] = False
+    gm = _gen(32)
+    additive = -2.0 * torch.rand(2, 40, generator=gm)
+    additive[0, 10] = float('-inf')
+    additive[1, 3:5] = float('-inf')
+    masked = {}
+    with torch.no_grad():
+        for mname, mask in (('bool', keep), ('float', additive)):
+            full = model(ids, mask=mask).logits.float()
+            pre = model(ids[:, :24], mask=mask[:, :24])
+            steps, cache = [], pre.cache
+            for t in range(24, 40):
+                o = model(ids[:, t:t + 1], cache=cache, mask=mask[:, :t + 1])
+                cache = o.cache
+                steps.append(o.logits[:, 0].float())
+            gen_ids = model.generate(ids[:, :16], max_new_tokens=8, mask=mask[:, :16]).run().generated
+            masked[f'{mname}_mask'] = mask
+            masked[f'{mname}_logits'] = full
+            masked[f'{mname}_decode_logits'] = torch.stack(steps, 1)
+            masked[f'{mname}_greedy'] = gen_ids
+    out['masked'] = dict(ids=ids, **masked)
+
     # --- config 1 (tiny): last-position logits, per-position stats, 64-step greedy
     torch.manual_seed(0)
     model = MotifChordModel(MotifChordConfig(**TINY))

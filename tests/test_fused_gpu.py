@@ -352,3 +352,110 @@ def test_skinny_gemm_rejects_bad_shapes():
     with pytest.raises(ValueError):  # M > 64
         _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, w.data_ptr(), 64, y.data_ptr(), 64, 65, 64, 64,
                   _lib.MB_BF16, None, 0, st())
+
+
+# ------------------------------------------------------------------ attention masks
+def _key_bias(B, S, seed, kind):
+    """[B, S] fp32 key bias: 'bool' -> 0 / -inf with a dropped run, 'float' -> random additive
+    values with some -inf (key 0 is never dropped, so no row loses every key)."""
+    g = torch.Generator().manual_seed(seed)
+    if kind == 'bool':
+        keep = torch.rand(B, S, generator=g) > 0.3
+        keep[:, 0] = True
+        return torch.zeros(B, S).masked_fill(~keep, float('-inf')), keep
+    kb = -3.0 * torch.rand(B, S, generator=g)
+    kb[:, 1::7] = float('-inf')
+    return kb, kb
+
+
+def _oracle_masked(q, k, v, alpha, beta, mu, ssmax, q_start, mask):
+    from oracle import model as om
+    B, H, L, D = q.shape
+    log_n = oo.log_n_table(q_start, L)
+    m4 = mask[:, None, None, :]
+    return om._chord_masked(q, k, v, alpha, beta, mu, ssmax, log_n, q_start, D, m4)
+
+
+@pytest.mark.parametrize('kind', ['bool', 'float'])
+@pytest.mark.parametrize('dtype,B,H,Hkv,L,S,D', [
+    (torch.bfloat16, 2, 12, 3, 300, 300, 64),    # tcgen05 kernel
+    (torch.bfloat16, 1, 8, 2, 130, 400, 64),     # tcgen05, q_start > 0
+    (torch.float16, 2, 4, 2, 70, 70, 32),        # 16-bit D = 32: the simple kernel takes masks
+    (torch.float32, 2, 4, 4, 50, 90, 64),        # fp32
+])
+def test_chord_prefill_masked(kind, dtype, B, H, Hkv, L, S, D):
+    g = torch.Generator().manual_seed(L + S + D)
+    q = torch.randn(B, H, L, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, S, D, generator=g).to(dtype)
+    v = torch.randn(B, Hkv, S, D, generator=g).to(dtype)
+    alpha = 0.5 + 1.5 * torch.rand(H, generator=g)
+    beta = torch.rand(H, generator=g)
+    mu = torch.ones(H) + 0.5 * torch.randn(H, generator=g)
+    ssmax = 0.8 + 0.4 * torch.rand(H, generator=g)
+    ssmax[::3] *= -1.0
+    qs = S - L
+    kb, mask = _key_bias(B, S, seed=S, kind=kind)
+    ref = _oracle_masked(q.float(), k.float(), v.float(), alpha, beta, mu, ssmax, qs, mask)
+    log_n = oo.log_n_table(qs, L).view(1, L).expand(B, L).contiguous()
+    qc, kc, vc, lc, kbc = q.cuda(), k.cuda(), v.cuda(), log_n.cuda(), kb.cuda()
+    a = [t.cuda() for t in (alpha, beta, mu, ssmax)]
+    out = torch.empty_like(qc)
+    strides = [*qc.stride()[:3], *kc.stride()[:3], *vc.stride()[:3], *out.stride()[:3], *lc.stride()]
+    _lib.call('motif_b200_chord_attention_masked', _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(vc),
+              *[_lib.ptr(t) for t in a], _lib.ptr(lc), _lib.ptr(out), B, H, Hkv, L, S, D, qs, D ** -0.5, 1e-5,
+              _lib.i64_array(strides), _lib.ptr(kbc), S, _lib.dtype_code(dtype), st())
+    assert torch.isfinite(out).all()
+    assert rel_err(out.float(), ref) < (1e-5 if dtype == torch.float32 else 1e-2), rel_err(out.float(), ref)
+    assert _lib.wait_timeouts() == 0
+
+
+@pytest.mark.parametrize('kind', ['bool', 'float'])
+@pytest.mark.parametrize('dtype,B,H,Hkv,T,S,D', [
+    (torch.bfloat16, 3, 12, 3, 1, 700, 64),   # tensor-core decode
+    (torch.bfloat16, 2, 8, 2, 2, 300, 32),    # CUDA-core decode
+    (torch.float32, 2, 4, 2, 1, 257, 64),
+])
+def test_chord_decode_masked(kind, dtype, B, H, Hkv, T, S, D):
+    g = torch.Generator().manual_seed(S + T)
+    cap = S + 10
+    q = torch.randn(B, T, H, D, generator=g).to(dtype)
+    kc = torch.randn(B, Hkv, cap, D, generator=g).to(dtype)
+    vc = torch.randn(B, Hkv, cap, D, generator=g).to(dtype)
+    alpha = 0.5 + 1.5 * torch.rand(H, generator=g)
+    beta = torch.rand(H, generator=g)
+    mu = torch.ones(H)
+    ssmax = 0.8 + 0.4 * torch.rand(H, generator=g)
+    qs = S - T
+    kb, mask = _key_bias(B, S, seed=S + 1, kind=kind)
+    ref = _oracle_masked(q.transpose(1, 2).float(), kc[:, :, :S].float(), vc[:, :, :S].float(), alpha, beta, mu,
+                         ssmax, qs, mask)
+    splits = 4
+    out = torch.empty(B * T, H * D, dtype=dtype, device='cuda')
+    ws_bytes = _lib.load().motif_b200_chord_decode_workspace_bytes(B, H, T, D, splits)
+    ws = torch.empty(ws_bytes // 4, device='cuda')
+    a = [t.cuda() for t in (alpha, beta, mu, ssmax)]
+    qc, kcc, vcc, kbc = q.cuda(), kc.cuda(), vc.cuda(), kb.cuda()
+    _lib.call('motif_b200_chord_decode_masked', _lib.ptr(qc), _lib.ptr(kcc), _lib.ptr(vcc), cap, None, S,
+              *[_lib.ptr(t) for t in a], _lib.ptr(out), H * D, B, H, Hkv, T, D, D ** -0.5, 1e-5, splits,
+              _lib.ptr(kbc), S, _lib.ptr(ws), ws_bytes, _lib.dtype_code(dtype), st())
+    got = out.view(B, T, H, D).transpose(1, 2).float()
+    assert rel_err(got, ref) < (1e-5 if dtype == torch.float32 else 1e-2), rel_err(got, ref)
+    assert _lib.wait_timeouts() == 0
+
+
+def test_chord_masked_all_keys_dropped_gives_zeros():
+    """A row whose every visible key is dropped yields zeros (the reference's softmax gives NaN)."""
+    B, H, Hkv, L, S, D = 1, 4, 4, 8, 8, 64
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(B, n, L, D, generator=g).bfloat16().cuda() for n in (H, Hkv, Hkv))
+    kb = torch.zeros(B, S)
+    kb[0, :4] = float('-inf')  # rows 0..3 see only keys 0..their own position
+    a = [t.cuda() for t in (torch.ones(H), torch.full((H,), 0.5), torch.ones(H), torch.ones(H))]
+    log_n = oo.log_n_table(0, L).view(1, L).contiguous().cuda()
+    out = torch.full_like(q, 7.0)
+    strides = [*q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out.stride()[:3], *log_n.stride()]
+    _lib.call('motif_b200_chord_attention_masked', _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), *[_lib.ptr(t) for t in a],
+              _lib.ptr(log_n), _lib.ptr(out), B, H, Hkv, L, S, D, 0, D ** -0.5, 1e-5, _lib.i64_array(strides),
+              _lib.ptr(kb.cuda()), S, _lib.dtype_code(torch.bfloat16), st())
+    assert bool((out[:, :, :4] == 0).all()) and torch.isfinite(out).all()
+    assert bool((out[:, :, 4:].abs().sum(-1) > 0).all())

@@ -139,3 +139,24 @@ def test_sampler_oracle_draw_is_inverse_cdf():
                     (0.999999, 3)]:
         got = osm.sample(logits, None, 1.0, None, None, 1.0, torch.tensor([u]))
         assert int(got[0]) == want, (u, int(got[0]))
+
+
+@pytest.mark.parametrize('kind', ['bool', 'float'])
+def test_small_model_masked(kind):
+    """The oracle's masked forward (keep-mask with a hole and right padding, additive float
+    mask) against the reference: prefill logits, chunked prefill + decode with the mask widened
+    every step, and masked greedy generation."""
+    d = load('masked')
+    cfg = MotifChordConfig(**SMALL)
+    P = om.make_params(cfg, seed=0, norm_jitter=0.1, dtype=torch.float32)
+    mask = d[f'{kind}_mask']
+    logits, _, _ = om.forward(P, cfg, d['ids'], mask=mask)
+    close(logits.float(), d[f'{kind}_logits'], rtol=1e-5, atol=1e-5)
+    _, _, cache = om.forward(P, cfg, d['ids'][:, :24], mask=mask[:, :24])
+    steps = []
+    for t in range(24, 40):
+        lg, _, cache = om.forward(P, cfg, d['ids'][:, t:t + 1], cache, mask=mask[:, :t + 1])
+        steps.append(lg[:, 0].float())
+    close(torch.stack(steps, 1), d[f'{kind}_decode_logits'], rtol=1e-5, atol=1e-5)
+    toks, _ = om.greedy(P, cfg, d['ids'][:, :16], 8, mask=mask[:, :16])
+    assert torch.equal(toks, d[f'{kind}_greedy'])
