@@ -354,6 +354,80 @@ class MotifChordModel(nn.Module):
             self._packed = (decs, lm)
         return self._packed
 
+    @classmethod
+    def from_pretrained(cls, path, config=None, map_location='cpu', device=None, strict: bool = False,
+                        verbose: bool = True, **overrides) -> 'MotifChordModel':
+        """Build the model from a checkpoint (`model/motif.py:237-360`): a bare state_dict, a
+        pipeline checkpoint or safetensors (file, shard directory, index).  The config is the
+        `config` argument (a config, a mapping or a JSON file path), else the file's, else the one
+        the tensor shapes imply; `**overrides` replace fields of it.  Tied models take a missing
+        `lm_head.weight` from `embed.weight`.  Returns the model in eval mode."""
+        import dataclasses
+        import json
+        import os
+        from .checkpoint import config_from_mapping, config_from_state_dict, load_checkpoint
+        loaded = load_checkpoint(path, map_location=map_location)
+        sd = loaded.state_dict
+        if config is not None:
+            if isinstance(config, (str, os.PathLike)):
+                with open(config, 'r', encoding='utf-8') as f:
+                    resolved = config_from_mapping(json.load(f))
+            elif isinstance(config, dict):
+                resolved = config_from_mapping(config)
+            else:
+                resolved = MotifChordConfig.from_any(config)
+        elif loaded.config is not None:
+            resolved = loaded.config
+        else:
+            try:
+                resolved = config_from_state_dict(sd)
+            except ValueError:
+                resolved = MotifChordConfig()
+        if overrides:
+            known = {f.name for f in dataclasses.fields(MotifChordConfig)}
+            unknown = sorted(set(overrides) - known)
+            if unknown:
+                raise TypeError(f'unknown MotifChordConfig override(s): {unknown}; valid names are {sorted(known)}.')
+            resolved = dataclasses.replace(resolved, **overrides)
+        model = cls(resolved)
+        emb, head = sd.get('embed.weight'), sd.get('lm_head.weight')
+        note = None
+        if resolved.tied_weight:
+            if head is None and emb is not None:
+                sd['lm_head.weight'] = emb
+                note = 'lm_head.weight taken from embed.weight (tied weights)'
+            elif head is not None and emb is not None and head is not emb and not torch.equal(head, emb):
+                note = ('the checkpoint is untied but the config has tied_weight=True: lm_head.weight and '
+                        'embed.weight disagree, the last one loaded wins.')
+        try:
+            incompatible = model.load_state_dict(sd, strict=False)
+        except RuntimeError as e:
+            raise RuntimeError(f'{os.fspath(path)!r} does not match the model built from {resolved!r}: {e}') from e
+        missing, unexpected = list(incompatible.missing_keys), list(incompatible.unexpected_keys)
+        if strict and (missing or unexpected):
+            raise RuntimeError(f'{os.fspath(path)!r} does not match the model exactly: {len(missing)} missing key(s) '
+                               f'{missing[:8]}, {len(unexpected)} unexpected key(s) {unexpected[:8]}.')
+        if device is not None:
+            model = model.to(device)
+        model.eval()
+        if verbose:
+            builtins.print(f'[MotifChordModel] {os.fspath(path)} -> {loaded.source}: {len(sd):,} tensors, '
+                           f'{model.count_param():,} params')
+            builtins.print(f'  config: {resolved}')
+            if note:
+                builtins.print(f'  note: {note}')
+            if missing:
+                builtins.print(f'  missing ({len(missing)}): {missing[:8]}' + (' ...' if len(missing) > 8 else ''))
+            if unexpected:
+                builtins.print(f'  unexpected ({len(unexpected)}): {unexpected[:8]}'
+                               + (' ...' if len(unexpected) > 8 else ''))
+        return model
+
+    def save_pretrained(self, path: str, metadata=None):
+        """Write the weights and config as one `.safetensors` file (`save_safetensors`)."""
+        from .checkpoint import save_safetensors
+        return save_safetensors(self, path, metadata=metadata)
+
     def count_param(self, print: bool = False) -> int:
         """Parameter count, tied weights once (`model/motif.py:377-400`)."""
         total = int(sum(p.numel() for p in self.parameters()))

@@ -14,6 +14,7 @@ rebuild bit-identical weights from the same seed without storing them.
 """
 
 import argparse
+import json
 import os
 import sys
 
@@ -236,6 +237,37 @@ def main():
         torch.multinomial = real_multinomial
     out['sampler'] = dict(logits=logits, hist=hist, cases=torch.tensor(cases, dtype=torch.float64),
                           probs=torch.stack(probs))
+
+    # --- checkpoints written by the reference's own writers (model/checkpoint.py): its
+    # safetensors writer, a wrapper-prefixed bare state_dict and a pipeline-style mapping;
+    # plus the logits of those weights and the config the reference resolves from each file
+    if args.only is None or 'checkpoints' in args.only:
+        from motif.model.checkpoint import save_safetensors, config_to_dict, load_checkpoint
+        ck_dir = os.path.join(HERE, 'ckpt')
+        os.makedirs(ck_dir, exist_ok=True)
+        ccfg = MotifChordConfig(vocab_size=64, model_dim=32, num_heads=2, num_kv_heads=1, head_k_dim=16,
+                                block=('gdn', 'chord'), block_n=1)
+        torch.manual_seed(0)
+        model = MotifChordModel(ccfg)
+        init_params(model, seed=0, norm_jitter=0.1)
+        model.eval()
+        save_safetensors(model, os.path.join(ck_dir, 'model.safetensors'))
+        sd = model.state_dict()
+        torch.save({'module.' + k: v.clone() for k, v in sd.items() if k != 'lm_head.weight'},
+                   os.path.join(ck_dir, 'bare_module.pt'))
+        torch.save({'__pipeline__': 'PretrainPipeline',
+                    'payload': {'model': {k: v.clone() for k, v in sd.items()}, 'config': config_to_dict(ccfg)}},
+                   os.path.join(ck_dir, 'pipeline.pt'))
+        ids = torch.randint(0, 64, (2, 12), generator=_gen(33))
+        with torch.no_grad():
+            lg = model(ids).logits.float()
+        resolved = {}
+        for f in ('model.safetensors', 'bare_module.pt', 'pipeline.pt'):
+            ld = load_checkpoint(os.path.join(ck_dir, f))
+            cfg = MotifChordModel._resolve_pretrained_config(None, ld)
+            resolved[f] = json.dumps(config_to_dict(cfg))
+        out['checkpoints'] = dict(ids=ids, logits=lg, resolved=resolved,
+                                  state_dict={k: v.clone() for k, v in sd.items()})
 
     for name, d in out.items():
         if args.only is not None and name not in args.only:
