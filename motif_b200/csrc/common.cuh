@@ -60,6 +60,9 @@ __device__ __forceinline__ float warp_max(float v) {
 // softplus keeps the accurate expf / log1pf.
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// scale / max(||x||, 1e-12) from ss = ||x||^2 (F.normalize's clamp), as one reciprocal square
+// root: the q / k L2 norms of the gated delta-net preparation.
+__device__ __forceinline__ float l2_scale(float ss, float scale) { return scale * rsqrtf(fmaxf(ss, 1e-24f)); }
 // torch.nn.functional.softplus with beta=1, threshold=20.
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
@@ -124,6 +127,17 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Two fp32 values rounded to T and back (one packed conversion instead of two).
+template <typename T> __device__ __forceinline__ float2 round2(float a, float b);
+template <>
+__device__ __forceinline__ float2 round2<__nv_bfloat16>(float a, float b) {
+  return __bfloat1622float2(__floats2bfloat162_rn(a, b));
+}
+template <>
+__device__ __forceinline__ float2 round2<__half>(float a, float b) {
+  return __half22float2(__floats2half2_rn(a, b));
 }
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t* r, const void* smem) {

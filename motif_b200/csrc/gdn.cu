@@ -448,12 +448,12 @@ __global__ void __launch_bounds__(256) gdn_prep_run_kernel(
     const int64_t tok = (int64_t)b * Tn + t;
     T o8[8];
     if (kind == 0) {
-      const float sc = qscale / fmaxf(sqrtf(ss), 1e-12f);
+      const float sc = l2_scale(ss, qscale);
 #pragma unroll
       for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
       *reinterpret_cast<uint4*>(qo + tok * H * DK + c0) = *reinterpret_cast<uint4*>(o8);
     } else if (kind == 1) {
-      const float sc = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+      const float sc = l2_scale(ss, 1.f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(y[i] * sc);
       *reinterpret_cast<uint4*>(ko + tok * H * DK + (c0 - H * DK)) = *reinterpret_cast<uint4*>(o8);

@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
             }
           }
           if constexpr (NORM) {  // second pass over the lane's own row: apply the L2 scale
-            const float sc = (cbase == 0 ? rsqrtf((float)DK) : 1.f) / fmaxf(sqrtf(ss), 1e-12f);
+            const float sc = l2_scale(ss, cbase == 0 ? rsqrtf((float)DK) : 1.f);
 #pragma unroll 4
             for (int p = 0; p < W / 2; ++p) {
               uint32_t* at = reinterpret_cast<uint32_t*>(colbase + r * stride + 2 * p);

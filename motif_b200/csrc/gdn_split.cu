@@ -220,22 +220,31 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       float y[8];
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float x0 = to_f(reinterpret_cast<const T*>(&raw[r])[i]);
-        const float x1 = to_f(reinterpret_cast<const T*>(&raw[r + 1])[i]);
-        const float x2 = to_f(reinterpret_cast<const T*>(&raw[r + 2])[i]);
-        const float x3 = to_f(reinterpret_cast<const T*>(&raw[r + 3])[i]);
-        const float a = w[i][0] * x0 + w[i][1] * x1 + w[i][2] * x2 + w[i][3] * x3;
-        y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
-        ss += y[i] * y[i];
+      for (int i = 0; i < 8; i += 2) {  // channel pairs: packed roundings
+        float a[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x0 = to_f(reinterpret_cast<const T*>(&raw[r])[i + e]);
+          const float x1 = to_f(reinterpret_cast<const T*>(&raw[r + 1])[i + e]);
+          const float x2 = to_f(reinterpret_cast<const T*>(&raw[r + 2])[i + e]);
+          const float x3 = to_f(reinterpret_cast<const T*>(&raw[r + 3])[i + e]);
+          a[e] = w[i + e][0] * x0 + w[i + e][1] * x1 + w[i + e][2] * x2 + w[i + e][3] * x3;
+        }
+        const float2 t = round2<T>(a[0], a[1]);
+        const float2 yy = round2<T>(siluf_(t.x), siluf_(t.y));
+        y[i] = yy.x;
+        y[i + 1] = yy.y;
+        ss += yy.x * yy.x;
+        ss += yy.y * yy.y;
       }
 #pragma unroll
       for (int o2 = 1; o2 < 8; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
-      const float sc = kind == 0 ? qscale / fmaxf(sqrtf(ss), 1e-12f) : (kind == 1 ? 1.f / fmaxf(sqrtf(ss), 1e-12f) : 1.f);
+      const float sc = (kind == 2 ? 1.f : l2_scale(ss, kind == 0 ? qscale : 1.f)) * (ok ? 1.f : 0.f);
       uint4 pk;
-      T* o8 = reinterpret_cast<T*>(&pk);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = from_f<T>(ok ? y[i] * sc : 0.f);
+      pk.x = pack2<T>(y[0] * sc, y[1] * sc);
+      pk.y = pack2<T>(y[2] * sc, y[3] * sc);
+      pk.z = pack2<T>(y[4] * sc, y[5] * sc);
+      pk.w = pack2<T>(y[6] * sc, y[7] * sc);
       T* dst = kind == 0 ? cQ + row * QS + cl : (kind == 1 ? cK + row * QS + (cl - DK) : cV + row * VS + (cl - 2 * DK));
       *reinterpret_cast<uint4*>(dst) = pk;
     }
