@@ -562,21 +562,30 @@ __global__ void __launch_bounds__(NT, 2) gdn_rec_kernel(const unsigned char* __r
     T* nS = sS + (size_t)((n + 1) & 1) * DK * SS;
     const int m0 = (warp & 3) * 16, c0 = (warp >> 2) * (SW / 2);
 
-    // X = U - W S  (warp: m-tile w%4, column group w/4), in place of U
+    // X = U - W S in place of U, and the first term of o = (q e^g) S + Aq X: both products
+    // read the same S fragments, and (q e^g) S does not wait for X
+    // (warp: m-tile w%4, column group w/4)
+    float acc[HT][4];  // o accumulator
     {
-      float acc[HT][4];
+      float accx[HT][4];
 #pragma unroll
-      for (int i = 0; i < HT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      for (int i = 0; i < HT; ++i) {
+        acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        accx[i][0] = accx[i][1] = accx[i][2] = accx[i][3] = 0.f;
+      }
 #pragma unroll
       for (int k0 = 0; k0 < DK; k0 += 16) {
-        uint32_t a[4];
-        lda(a, cW, QS, m0, k0);
+        uint32_t aw[4], aq[4];
+        lda(aw, cW, QS, m0, k0);
+        lda(aq, cQ, QS, m0, k0);
 #pragma unroll
         for (int nn = 0; nn < SW / 2; nn += 16) {
           uint32_t bb[4];
           ldb_t(bb, cS, SS, k0, c0 + nn);
-          mma_16816<T>(acc[nn / 8], a, &bb[0]);
-          mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
+          mma_16816<T>(accx[nn / 8], aw, &bb[0]);
+          mma_16816<T>(accx[nn / 8 + 1], aw, &bb[2]);
+          mma_16816<T>(acc[nn / 8], aq, &bb[0]);
+          mma_16816<T>(acc[nn / 8 + 1], aq, &bb[2]);
         }
       }
       const int ra = m0 + gq, rb = ra + 8;
@@ -584,29 +593,14 @@ __global__ void __launch_bounds__(NT, 2) gdn_rec_kernel(const unsigned char* __r
       for (int nt = 0; nt < HT; ++nt) {
         const int c = c0 + nt * 8 + 2 * tq;
         const float2 ua = ld2(&sX[ra * US + c]), ub = ld2(&sX[rb * US + c]);
-        st2(&sX[ra * US + c], ua.x - acc[nt][0], ua.y - acc[nt][1]);
-        st2(&sX[rb * US + c], ub.x - acc[nt][2], ub.y - acc[nt][3]);
+        st2(&sX[ra * US + c], ua.x - accx[nt][0], ua.y - accx[nt][1]);
+        st2(&sX[rb * US + c], ub.x - accx[nt][2], ub.y - accx[nt][3]);
       }
     }
     __syncthreads();  // X complete
 
-    // o = (q e^g) S + Aq X  and  S = e^gL S + (k e^(gL - g))^T X for this warp's block
+    // o += Aq X, and S = e^gL S + (k e^(gL - g))^T X for this warp's block
     {
-      float acc[HT][4];
-#pragma unroll
-      for (int i = 0; i < HT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-#pragma unroll
-      for (int k0 = 0; k0 < DK; k0 += 16) {
-        uint32_t a[4];
-        lda(a, cQ, QS, m0, k0);
-#pragma unroll
-        for (int nn = 0; nn < SW / 2; nn += 16) {
-          uint32_t bb[4];
-          ldb_t(bb, cS, SS, k0, c0 + nn);
-          mma_16816<T>(acc[nn / 8], a, &bb[0]);
-          mma_16816<T>(acc[nn / 8 + 1], a, &bb[2]);
-        }
-      }
       for (int k0 = 0; k0 <= m0; k0 += 16) {  // Aq lower triangular: k < m0 + 16
         uint32_t a[4];
         lda(a, sAq, AS, m0, k0);
