@@ -348,53 +348,73 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
   }
   __syncthreads();
 
-  // blocked forward substitution, warp-local in its column tiles
+  // blocked forward substitution, warp-local in its column tiles: the warp's SOLVE_T tiles
+  // advance together, sharing each A / T fragment and giving the MMA chains independent work
 #pragma unroll
   for (int bi = 0; bi < 4; ++bi) {
     const int r0 = bi * 16;
+    const int ra = r0 + gq, rb = ra + 8;
+    float acc[SOLVE_T][4];
 #pragma unroll
     for (int ti = 0; ti < SOLVE_T; ++ti) {
       const int tile = warp + NW * ti;
       if (tile >= NTILE) break;
-      const int c0 = tile * 8;
-      float acc[4];
-      {
-        const int ra = r0 + gq, rb = ra + 8, c = c0 + 2 * tq;
-        if (c0 < DK) {
-          const float sa = sBeta[ra] * sEg[ra], sb = sBeta[rb] * sEg[rb];
-          const float2 xa = ld2(&cK[ra * QS + c]), xb = ld2(&cK[rb * QS + c]);
-          acc[0] = xa.x * sa; acc[1] = xa.y * sa; acc[2] = xb.x * sb; acc[3] = xb.y * sb;
-        } else {
-          const float sa = sBeta[ra], sb = sBeta[rb];
-          const float2 xa = ld2(&cV[ra * VS + c - DK]), xb = ld2(&cV[rb * VS + c - DK]);
-          acc[0] = xa.x * sa; acc[1] = xa.y * sa; acc[2] = xb.x * sb; acc[3] = xb.y * sb;
-        }
+      const int c = tile * 8 + 2 * tq;
+      if (c < DK) {
+        const float sa = sBeta[ra] * sEg[ra], sb = sBeta[rb] * sEg[rb];
+        const float2 xa = ld2(&cK[ra * QS + c]), xb = ld2(&cK[rb * QS + c]);
+        acc[ti][0] = xa.x * sa; acc[ti][1] = xa.y * sa; acc[ti][2] = xb.x * sb; acc[ti][3] = xb.y * sb;
+      } else {
+        const float sa = sBeta[ra], sb = sBeta[rb];
+        const float2 xa = ld2(&cV[ra * VS + c - DK]), xb = ld2(&cV[rb * VS + c - DK]);
+        acc[ti][0] = xa.x * sa; acc[ti][1] = xa.y * sa; acc[ti][2] = xb.x * sb; acc[ti][3] = xb.y * sb;
       }
-      for (int bj = 0; bj < bi; ++bj) {  // + A_ij X_j
-        uint32_t a[4], bb[2];
-        lda(a, sA, AS, r0, bj * 16);
-        ldb_t1(bb, sX, XS, bj * 16, c0);
-        mma_16816<T>(acc, a, bb);
-      }
-      {
-        const int ra = r0 + gq, c = c0 + 2 * tq;
-        st2(&sX[ra * XS + c], acc[0], acc[1]);
-        st2(&sX[(ra + 8) * XS + c], acc[2], acc[3]);
-      }
-      __syncwarp();
-      {
-        uint32_t a[4], bb[2];
-        lda(a, sTd + bi * 16 * TS, TS, 0, 0);
-        ldb_t1(bb, sX, XS, r0, c0);
-        float x[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_16816<T>(x, a, bb);
-        __syncwarp();
-        const int ra = r0 + gq, c = c0 + 2 * tq;
-        st2(&sX[ra * XS + c], x[0], x[1]);
-        st2(&sX[(ra + 8) * XS + c], x[2], x[3]);
-      }
-      __syncwarp();
     }
+    for (int bj = 0; bj < bi; ++bj) {  // + A_ij X_j
+      uint32_t a[4];
+      lda(a, sA, AS, r0, bj * 16);
+#pragma unroll
+      for (int ti = 0; ti < SOLVE_T; ++ti) {
+        const int tile = warp + NW * ti;
+        if (tile >= NTILE) break;
+        uint32_t bb[2];
+        ldb_t1(bb, sX, XS, bj * 16, tile * 8);
+        mma_16816<T>(acc[ti], a, bb);
+      }
+    }
+#pragma unroll
+    for (int ti = 0; ti < SOLVE_T; ++ti) {
+      const int tile = warp + NW * ti;
+      if (tile >= NTILE) break;
+      const int c = tile * 8 + 2 * tq;
+      st2(&sX[ra * XS + c], acc[ti][0], acc[ti][1]);
+      st2(&sX[rb * XS + c], acc[ti][2], acc[ti][3]);
+    }
+    __syncwarp();
+    {
+      uint32_t a[4];
+      lda(a, sTd + bi * 16 * TS, TS, 0, 0);
+      float x[SOLVE_T][4];
+#pragma unroll
+      for (int ti = 0; ti < SOLVE_T; ++ti) {
+        const int tile = warp + NW * ti;
+        if (tile >= NTILE) break;
+        uint32_t bb[2];
+        ldb_t1(bb, sX, XS, r0, tile * 8);
+        x[ti][0] = x[ti][1] = x[ti][2] = x[ti][3] = 0.f;
+        mma_16816<T>(x[ti], a, bb);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int ti = 0; ti < SOLVE_T; ++ti) {
+        const int tile = warp + NW * ti;
+        if (tile >= NTILE) break;
+        const int c = tile * 8 + 2 * tq;
+        st2(&sX[ra * XS + c], x[ti][0], x[ti][1]);
+        st2(&sX[rb * XS + c], x[ti][2], x[ti][3]);
+      }
+    }
+    __syncwarp();
   }
   __syncthreads();
 
