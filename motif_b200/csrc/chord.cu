@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
     float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int c = 0; c < tc::kKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+    for (int c = 0; c < tc::kKeys; c += 2) mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], x[c], x[c + 1]);
     const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
     const float mb = mn == -INFINITY ? 0.f : mn;
     const float corr = ex2_approx((m - mb) * rcs);
