@@ -93,12 +93,12 @@ def kernel_work(name, cfg, B, T):
 # units, so a full launch's traffic is this figure times its units.
 #   gdn_chunk_gated : per token-head, profiles/gdn_chunk_fast_b4_t4096.txt (186.2 MB / 196608)
 #   gdn_prefill_ws  : per token-head, profiles/gdn_split_b32_t4096.txt, the three kernels of
-#                     one launch at B = 32 (5158 MB / 1572864: the chunk records written and
+#                     one launch at B = 32 (5059 MB / 1572864: the chunk records written and
 #                     read back are most of the excess over the algorithmic bytes)
 #   chord_attention : per token,      profiles/chord_tc_b4_t4096.txt (38.2 MB / 16384)
 NCU_TRAFFIC = {
     'motif_b200_gdn_chunk_gated': (186.15e6 / (4 * 4096 * 12), 'token_head'),
-    'motif_b200_gdn_prefill_ws': (5158.0e6 / (32 * 4096 * 12), 'token_head'),
+    'motif_b200_gdn_prefill_ws': (5059.3e6 / (32 * 4096 * 12), 'token_head'),
     'motif_b200_chord_attention': (38.19e6 / (4 * 4096), 'token'),
 }
 
