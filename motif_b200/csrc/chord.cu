@@ -514,7 +514,12 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     const int cmax = min(tc::kKeys - 1, min(S - 1 - k0, qpos - k0));
     const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127;  // key offset c -> tb[-c]
 #pragma unroll
-    for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(x[c], scale_s, tb[-c]);
+    for (int c = 0; c < tc::kKeys; c += 2) {
+      const float2 y = ffma2(make_float2(x[c], x[c + 1]), make_float2(scale_s, scale_s),
+                             make_float2(tb[-c], tb[-c - 1]));
+      x[c] = y.x;
+      x[c + 1] = y.y;
+    }
     if constexpr (KM) {
       const float* km = sKmw + (j & 1) * tc::kKeys;
 #pragma unroll
@@ -541,8 +546,10 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float p0 = ex2_approx(fmaf(x[cc * 8 + 2 * e], rcs, nb));
-        const float p1 = ex2_approx(fmaf(x[cc * 8 + 2 * e + 1], rcs, nb));
+        const float2 t = ffma2(make_float2(x[cc * 8 + 2 * e], x[cc * 8 + 2 * e + 1]), make_float2(rcs, rcs),
+                               make_float2(nb, nb));
+        const float p0 = ex2_approx(t.x);
+        const float p1 = ex2_approx(t.y);
         ps4[e] += p0 + p1;
         w[e] = pack2<T>(p0, p1);
       }
@@ -570,9 +577,15 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       tmem_wait_ld(r0);
       tmem_wait_ld(r1);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        o[i] = fmaf(o[i], corr, __uint_as_float(r0[i]));
-        o[32 + i] = fmaf(o[32 + i], corr, __uint_as_float(r1[i]));
+      for (int i = 0; i < 32; i += 2) {
+        const float2 a = ffma2(make_float2(o[i], o[i + 1]), make_float2(corr, corr),
+                               make_float2(__uint_as_float(r0[i]), __uint_as_float(r0[i + 1])));
+        const float2 b2 = ffma2(make_float2(o[32 + i], o[33 + i]), make_float2(corr, corr),
+                                make_float2(__uint_as_float(r1[i]), __uint_as_float(r1[i + 1])));
+        o[i] = a.x;
+        o[i + 1] = a.y;
+        o[32 + i] = b2.x;
+        o[33 + i] = b2.y;
       }
     }
     tc_fence_before();

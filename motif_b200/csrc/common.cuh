@@ -274,6 +274,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" : MB_R32(r)::"memory");
 }
+// Two independent fp32 fused multiply-adds in one instruction (sm_100 fma.rn.f32x2): each lane
+// rounds exactly as fmaf does.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
 // max of three fp32 values in one instruction (sm_100)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
