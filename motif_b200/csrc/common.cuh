@@ -55,11 +55,53 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// SiLU / sigmoid / softplus in fp32.  SiLU and sigmoid use the __expf / __fdividef
-// intrinsics (relative error ~1e-6, far below the 1e-5 fp32 bar and the 16-bit rounding);
-// softplus keeps the accurate expf / log1pf.
+// Sigmoid / SiLU / softplus in fp32.  Sigmoid uses the __expf / __fdividef intrinsics (relative
+// error ~1e-6, far below the 1e-5 fp32 bar and the 16-bit rounding); softplus keeps the
+// accurate expf / log1pf.
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
-__device__ __forceinline__ float siluf_(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float ex2f_(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcpf_(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// SiLU x / (1 + e^-x), with e^-x = 2^(-x log2 e) on the MUFU ex2 unit and the reciprocal on
+// MUFU rcp (relative error a few 1e-7); silu2_ is the same arithmetic on a channel pair with the
+// multiplies and the add packed (bit-identical per lane).
+constexpr float kNegLog2e = -1.4426950408889634f;
+__device__ __forceinline__ float siluf_(float x) { return x * rcpf_(1.0f + ex2f_(x * kNegLog2e)); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mul.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+// The causal depthwise conv of the gated delta-net preparation, one fixed evaluation order
+// (((w0 x0 + w1 x1) + w2 x2) + w3 x3, one multiply then fmas) shared by every kernel that
+// computes it, scalar or packed.
+__device__ __forceinline__ float conv4f(float w0, float w1, float w2, float w3, float x0, float x1, float x2,
+                                        float x3) {
+  return fmaf(w3, x3, fmaf(w2, x2, fmaf(w1, x1, w0 * x0)));
+}
+__device__ __forceinline__ float2 silu2_(float2 x) {
+  const float2 t = fmul2(x, make_float2(kNegLog2e, kNegLog2e));
+  const float2 d = fadd2(make_float2(ex2f_(t.x), ex2f_(t.y)), make_float2(1.0f, 1.0f));
+  return fmul2(x, make_float2(rcpf_(d.x), rcpf_(d.y)));
+}
 // scale / max(||x||, 1e-12) from ss = ||x||^2 (F.normalize's clamp), as one reciprocal square
 // root: the q / k L2 norms of the gated delta-net preparation.
 __device__ __forceinline__ float l2_scale(float ss, float scale) { return scale * rsqrtf(fmaxf(ss, 1e-24f)); }

@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(DV) gdn_decode_kernel(
     const float x = to_f(row[c]);
     const float s0 = to_f(cs[c]), s1 = to_f(cs[C + c]), s2 = to_f(cs[2 * C + c]);
     const T* w = conv_w + (int64_t)c * 4;
-    float y = to_f(w[0]) * s0 + to_f(w[1]) * s1 + to_f(w[2]) * s2 + to_f(w[3]) * x;
+    float y = conv4f(to_f(w[0]), to_f(w[1]), to_f(w[2]), to_f(w[3]), s0, s1, s2, x);
     cs[c] = from_f<T>(s1);
     cs[C + c] = from_f<T>(s2);
     cs[2 * C + c] = from_f<T>(x);
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
     const float x = to_f(row[c]);
     const float s0 = to_f(cs[c]), s1 = to_f(cs[C + c]), s2 = to_f(cs[2 * C + c]);
     const T* w = conv_w + (int64_t)c * 4;
-    const float acc = to_f(w[0]) * s0 + to_f(w[1]) * s1 + to_f(w[2]) * s2 + to_f(w[3]) * x;
+    const float acc = conv4f(to_f(w[0]), to_f(w[1]), to_f(w[2]), to_f(w[3]), s0, s1, s2, x);
     cs[c] = from_f<T>(s1);
     cs[C + c] = from_f<T>(s2);
     cs[2 * C + c] = from_f<T>(x);
@@ -318,8 +318,8 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(
     for (int r = 0; r < QPL; ++r) {
       const float xq = cq[r] >= 0 ? to_f(row[cq[r]]) : 0.f;
       const float xk = ck[r] >= 0 ? to_f(row[ck[r]]) : 0.f;
-      float a = wq[r][0] * hq[r][0] + wq[r][1] * hq[r][1] + wq[r][2] * hq[r][2] + wq[r][3] * xq;
-      float c = wk[r][0] * hk[r][0] + wk[r][1] * hk[r][1] + wk[r][2] * hk[r][2] + wk[r][3] * xk;
+      float a = conv4f(wq[r][0], wq[r][1], wq[r][2], wq[r][3], hq[r][0], hq[r][1], hq[r][2], xq);
+      float c = conv4f(wk[r][0], wk[r][1], wk[r][2], wk[r][3], hk[r][0], hk[r][1], hk[r][2], xk);
       hq[r][0] = hq[r][1]; hq[r][1] = hq[r][2]; hq[r][2] = xq;
       hk[r][0] = hk[r][1]; hk[r][1] = hk[r][2]; hk[r][2] = xk;
       yq[r] = cq[r] >= 0 ? to_f(from_f<T>(siluf_(to_f(from_f<T>(a))))) : 0.f;
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(
 #pragma unroll
     for (int r = 0; r < VPL; ++r) {
       const float xv = cv[r] >= 0 ? to_f(row[cv[r]]) : 0.f;
-      float a = wv[r][0] * hv[r][0] + wv[r][1] * hv[r][1] + wv[r][2] * hv[r][2] + wv[r][3] * xv;
+      float a = conv4f(wv[r][0], wv[r][1], wv[r][2], wv[r][3], hv[r][0], hv[r][1], hv[r][2], xv);
       hv[r][0] = hv[r][1]; hv[r][1] = hv[r][2]; hv[r][2] = xv;
       yv[r] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
     }
@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(256) gdn_prep_run_kernel(
       const float x1 = to_f(reinterpret_cast<const T*>(&raw[r + 1])[i]);
       const float x2 = to_f(reinterpret_cast<const T*>(&raw[r + 2])[i]);
       const float x3 = to_f(reinterpret_cast<const T*>(&raw[r + 3])[i]);
-      const float a = w[i][0] * x0 + w[i][1] * x1 + w[i][2] * x2 + w[i][3] * x3;
+      const float a = conv4f(w[i][0], w[i][1], w[i][2], w[i][3], x0, x1, x2, x3);
       y[i] = to_f(from_f<T>(siluf_(to_f(from_f<T>(a)))));
       ss += y[i] * y[i];
     }

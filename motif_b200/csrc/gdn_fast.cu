@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_fast_kernel(
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               const float4 w = *reinterpret_cast<const float4*>(sCw + (cl + j) * 4);
-              const float a = w.x * to_f(e3[j]) + w.y * to_f(e2[j]) + w.z * to_f(e1[j]) + w.w * to_f(e0[j]);
+              const float a = conv4f(w.x, w.y, w.z, w.w, to_f(e3[j]), to_f(e2[j]), to_f(e1[j]), to_f(e0[j]));
               y[j] = ok ? to_f(from_f<T>(siluf_(to_f(from_f<T>(a))))) : 0.f;
             }
             if (is_last && pa.conv_out) {  // raw inputs at L-3 .. L-1 become the carried conv state

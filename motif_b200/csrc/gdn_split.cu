@@ -220,18 +220,19 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       float y[8];
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {  // channel pairs: packed roundings
-        float a[2];
+      for (int i = 0; i < 8; i += 2) {  // channel pairs: packed fp32 math and roundings
+        float2 xv[4];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float x0 = to_f(reinterpret_cast<const T*>(&raw[r])[i + e]);
-          const float x1 = to_f(reinterpret_cast<const T*>(&raw[r + 1])[i + e]);
-          const float x2 = to_f(reinterpret_cast<const T*>(&raw[r + 2])[i + e]);
-          const float x3 = to_f(reinterpret_cast<const T*>(&raw[r + 3])[i + e]);
-          a[e] = w[i + e][0] * x0 + w[i + e][1] * x1 + w[i + e][2] * x2 + w[i + e][3] * x3;
-        }
-        const float2 t = round2<T>(a[0], a[1]);
-        const float2 yy = round2<T>(siluf_(t.x), siluf_(t.y));
+        for (int tap = 0; tap < 4; ++tap)
+          xv[tap] = make_float2(to_f(reinterpret_cast<const T*>(&raw[r + tap])[i]),
+                                to_f(reinterpret_cast<const T*>(&raw[r + tap])[i + 1]));
+        // conv4f's order: ((w0 x0 + w1 x1) + w2 x2) + w3 x3 as one multiply and three fmas
+        float2 a = fmul2(make_float2(w[i][0], w[i + 1][0]), xv[0]);
+        a = ffma2(make_float2(w[i][1], w[i + 1][1]), xv[1], a);
+        a = ffma2(make_float2(w[i][2], w[i + 1][2]), xv[2], a);
+        a = ffma2(make_float2(w[i][3], w[i + 1][3]), xv[3], a);
+        const float2 sv = silu2_(round2<T>(a.x, a.y));
+        const float2 yy = round2<T>(sv.x, sv.y);
         y[i] = yy.x;
         y[i + 1] = yy.y;
         ss += yy.x * yy.x;

@@ -67,7 +67,8 @@ def test_small_chunked_prefill_matches_full():
         for s in range(0, 200, 70):
             out = m(ids[:, s:s + 70], cache=cache)
             cache = out.cache
-            assert rel_err(out.logits, full[:, s:s + 70]) < 1e-5
+            # the reference's bar for this check (tests/test_unified_cache.py:185-187)
+            assert (out.logits - full[:, s:s + 70]).abs().max().item() < 1e-4
         assert cache.seq_len == 200
 
 
