@@ -225,15 +225,29 @@ __global__ void attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, co
 #pragma unroll
       for (int e = 0; e < 8; ++e) qw[v][e] = to_f(q8[e]) * to_f(w8[e]);
     }
-    // Online softmax over the sources: h accumulates exp(l_s - m) x_s.
+    // Online softmax over the sources: h accumulates exp(l_s - m) x_s.  The next source's row
+    // is requested before this one is reduced, so two rows are in flight per warp.
     float m = -INFINITY, den = 0.f;
+    uint4 nxt[NV];
+    {
+      const T* xr = static_cast<const T*>(src.p[0]) + row * srs;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) nxt[v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+    }
     for (int s = 0; s < n_src; ++s) {
-      const T* xr = static_cast<const T*>(src.p[s]) + row * srs;
+      uint4 cur[NV];
+#pragma unroll
+      for (int v = 0; v < NV; ++v) cur[v] = nxt[v];
+      if (s + 1 < n_src) {
+        const T* xn = static_cast<const T*>(src.p[s + 1]) + row * srs;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) nxt[v] = *reinterpret_cast<const uint4*>(xn + (v * 32 + lane) * 8);
+      }
       float x[NV][8];
       float ss = 0.f, dot = 0.f;
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
-        uint4 raw = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+        const uint4 raw = cur[v];
         const T* e8 = reinterpret_cast<const T*>(&raw);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
