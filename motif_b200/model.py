@@ -709,18 +709,29 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
     N_in = proj.shape[1]
     if cache is None:
         cache = KVLayerCache()  # no layer cache (training-mode forward): attend to this chunk only
-    if cache.wide:
-        raise NotImplementedError('wide KV caches (an export-only layout) are not used by the fused path')
     if cache._kbuf is not None and (cache._kbuf.dtype != dt or cache._kbuf.device != dev):
         cache.to(device=dev, dtype=dt)
     cached = cache.length
     q_start = position if position != 0 else cached
-    cache.reserve(cached + T, like=proj, shape=(B, Hkv, D))
-    cap = cache._kbuf.shape[2]
     qb = torch.empty((M, d), dtype=dt, device=dev)
-    _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
-              _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cap, None, cached, B, T, H, Hkv, D, NORM_EPS, dc, st)
-    cache.length = cached + T
+    if cache.wide:
+        # a wide cache (`cache.py:42-70`) stores every key / value head once per query head: the
+        # new keys / values are prepared narrow, widened by the cache's own update, and the
+        # attention then reads one kv head per query head (the same arithmetic as grouped)
+        kt = torch.empty((B, Hkv, T, D), dtype=dt, device=dev)
+        vt = torch.empty_like(kt)
+        _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
+                  _lib.ptr(kt), _lib.ptr(vt), T, None, 0, B, T, H, Hkv, D, NORM_EPS, dc, st)
+        cache.update(kt, vt)
+        cache.reserve(cache.length, like=proj, shape=(B, H, D))
+        Hkv = H
+    else:
+        cache.reserve(cached + T, like=proj, shape=(B, Hkv, D))
+        _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
+                  _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cache._kbuf.shape[2], None, cached, B, T, H, Hkv, D,
+                  NORM_EPS, dc, st)
+        cache.length = cached + T
+    cap = cache._kbuf.shape[2]
     S = cache.length
     attn = torch.empty((M, d), dtype=dt, device=dev)
     scale = D ** -0.5

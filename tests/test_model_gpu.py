@@ -210,3 +210,31 @@ def test_masked_bf16_d64_matches_oracle():
     err_m = (got[1, 100:] - ref_m[1, 100:].float()).abs().max().item()
     err_p = (plain[1, 100:] - ref_p[1, 100:].float()).abs().max().item()
     assert err_m < max(2 * err_p, 2e-2), (err_m, err_p)
+
+
+@pytest.mark.parametrize('functional,wide', [(True, False), (False, True), (True, True)])
+def test_functional_and_wide_caches_match_grouped(functional, wide):
+    """`create_cache(functional=..., wide_kv=...)` (`cache.py:42-70,255-302`) on the fused path:
+    prefill + decode logits equal those with the default grouped in-place cache, and a wide
+    cache holds one copy of every kv head per query head."""
+    m = build(MotifChordConfig(**SMALL), jitter=0.1)
+    ids = torch.randint(0, 512, (2, 30), generator=torch.Generator().manual_seed(11)).cuda()
+    with torch.no_grad():
+        ref = m(ids[:, :24], cache=m.create_cache())
+        got = m(ids[:, :24], cache=m.create_cache(functional=functional, wide_kv=wide))
+        assert rel_err(got.logits, ref.logits) < 1e-5
+        rc, gc = ref.cache, got.cache
+        for t in range(24, 30):
+            r = m(ids[:, t:t + 1], cache=rc)
+            g = m(ids[:, t:t + 1], cache=gc)
+            rc, gc = r.cache, g.cache
+            assert rel_err(g.logits, r.logits) < 1e-5
+    from motif_b200.cache import KVLayerCache
+    kv = [lc for bc in gc for lc in bc.attn if isinstance(lc, KVLayerCache)]
+    H = m.config.num_heads
+    for lc in kv:
+        assert lc.length == 30
+        if wide:
+            assert lc.k.shape[1] == H
+            G = H // m.config.kv_heads
+            assert torch.equal(lc.k[:, 0], lc.k[:, G - 1])  # copies of kv head 0
