@@ -291,21 +291,24 @@ MB_API int motif_b200_chord_decode_noalloc(const void* q, const void* k_cache, c
  * reference. */
 MB_API int motif_b200_wait_timeouts(uint32_t* count);
 
-/* out = a * sigmoid(gate) + m over [rows, N] (row strides given).
- * Replaces chord_attn.py:254,313 (o_proj(out) * G) + decoder.py:208 (attn + mlp). */
 /* Y[M, N] = X[M, K] . W[N, K]^T for a small token count (decode: 1 <= M <= 64), 16-bit
- * operands, fp32 accumulation, row strides ldx / ldw / ldy (elements; K, ldx, ldw multiples
- * of 8, X and W 16-byte aligned).  Streams W once; when N is small, K is split across CTAs
- * and the partial tiles are summed in a fixed order by the last CTA of each feature block.
- * `workspace` (motif_b200_skinny_gemm_workspace_bytes bytes, may be 0 / NULL when that is 0)
- * must be zero-filled once before first use and is left zeroed; calls sharing one workspace
- * must not overlap on the GPU.  Replaces the decode-time nn.Linear products (decoder.py,
- * mlp.py, motif.py lm_head) that cuBLAS runs as weight-bandwidth-bound small-M GEMMs. */
+ * operands, fp32 accumulation, row strides ldx / ldw / ldy (elements; K a multiple of 64,
+ * ldx and ldw multiples of 8, X and W 16-byte aligned; other K: MB_ERR_UNSUPPORTED).
+ * Streams W once on the tensor cores; when N is small, K is split across the CTAs of a
+ * cluster and the partial tiles are summed in a fixed order through distributed shared
+ * memory, so results are deterministic.  Needs no workspace: the workspace query returns 0
+ * and `workspace` / `workspace_bytes` are accepted and ignored (kept for callers that pass
+ * one).  Launched with programmatic dependent launch: W may stream while the previous
+ * kernel on the stream finishes; X is read and Y written only after it has ended.
+ * Replaces the decode-time nn.Linear products (decoder.py, mlp.py, motif.py lm_head) that
+ * cuBLAS runs as weight-bandwidth-bound small-M GEMMs. */
 MB_API int64_t motif_b200_skinny_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                            int64_t ldy, int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
                            int64_t workspace_bytes, void* stream);
 
+/* out = a * sigmoid(gate) + m over [rows, N] (row strides given).
+ * Replaces chord_attn.py:254,313 (o_proj(out) * G) + decoder.py:208 (attn + mlp). */
 MB_API int motif_b200_gate_residual(const void* a, int64_t a_stride, const void* gate,
                              int64_t gate_stride, const void* m, int64_t m_stride, void* out,
                              int64_t out_stride, int64_t rows, int64_t N, int dtype, void* stream);

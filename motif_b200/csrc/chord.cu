@@ -1789,6 +1789,7 @@ extern "C" int motif_b200_chord_decode_noalloc(const void* q, const void* k_cach
 
 namespace mb {
 int read_and_clear_gdn_timeouts(unsigned int* count);
+int read_and_clear_skinny_timeouts(unsigned int* count);
 }
 
 extern "C" int motif_b200_wait_timeouts(uint32_t* count) {
@@ -1797,8 +1798,10 @@ extern "C" int motif_b200_wait_timeouts(uint32_t* count) {
   if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess ||
       cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
     return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
-  const int rc = mb::read_and_clear_gdn_timeouts(&gdn);
+  unsigned int sk = 0;
+  int rc = mb::read_and_clear_gdn_timeouts(&gdn);
+  if (!rc) rc = mb::read_and_clear_skinny_timeouts(&sk);
   if (rc) return rc;
-  *count = v + gdn;
+  *count = v + gdn + sk;
   return MB_OK;
 }

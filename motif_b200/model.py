@@ -494,22 +494,9 @@ class MotifChordModel(nn.Module):
 
 # ============================================================================ engine
 # Largest M routed to motif_b200_skinny_gemm.  0: every product runs on cuBLAS — the skinny
-# kernel is correct (tests) but measured slower than cuBLAS at decode sizes (30-48 us vs
-# ~8 us per product at M = 64), so the model does not use it.
+# kernel is correct (tests) but measured slower than cuBLAS at the decode shapes (7.4-11.8 us
+# vs 3.4-10.9 us per product at M = 64), so the model does not use it.
 SKINNY_MAX_M = 0
-_SKINNY_WS: Dict[int, torch.Tensor] = {}
-
-
-def _skinny_ws(dev, nbytes: int) -> torch.Tensor:
-    """A zero-filled workspace for motif_b200_skinny_gemm per device, grown on demand (first
-    grown by a warm-up step, outside any graph capture).  The kernel leaves it zeroed; the
-    model's GEMMs run one after another on one stream, so they share it."""
-    key = dev.index
-    ws = _SKINNY_WS.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
-        _SKINNY_WS[key] = ws
-    return ws
 
 
 def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
@@ -517,15 +504,12 @@ def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Ten
     skinny GEMM, everything else on cuBLAS (plain library GEMM; timed as 'cublas_gemm')."""
     M, K = a.shape
     N = w.shape[0]
-    if (M <= SKINNY_MAX_M and a.dtype in (torch.bfloat16, torch.float16) and w.dtype == a.dtype and K % 8 == 0
+    if (M <= SKINNY_MAX_M and a.dtype in (torch.bfloat16, torch.float16) and w.dtype == a.dtype and K % 64 == 0
             and a.stride(1) == 1 and w.stride(1) == 1 and a.stride(0) % 8 == 0 and w.stride(0) % 8 == 0
             and a.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0):
         y = out if out is not None else torch.empty((M, N), dtype=a.dtype, device=a.device)
-        nbytes = _lib.load().motif_b200_skinny_gemm_workspace_bytes(M, N, K)
-        ws = _skinny_ws(a.device, nbytes) if nbytes > 0 else None
         _lib.call('motif_b200_skinny_gemm', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(),
-                  y.stride(0), M, N, K, _lib.dtype_code(a.dtype), _lib.ptr(ws), nbytes,
-                  _lib.stream_ptr(a.device))
+                  y.stride(0), M, N, K, _lib.dtype_code(a.dtype), None, 0, _lib.stream_ptr(a.device))
         return y
     tr = _lib._tracker
     if tr is None:

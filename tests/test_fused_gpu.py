@@ -313,7 +313,7 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
 
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize('M,N,K', [(1, 768, 768), (7, 8728, 768), (64, 768, 3584), (64, 6016, 768),
-                                   (33, 768, 2048), (64, 32000, 768), (5, 100, 40)])
+                                   (33, 768, 2048), (64, 32000, 768), (5, 100, 64), (64, 129, 128)])
 def test_skinny_gemm_vs_torch(dtype, M, N, K):
     g = torch.Generator().manual_seed(M + N + K)
     x = (0.5 * torch.randn(M, K, generator=g)).to(dtype).cuda()
@@ -352,6 +352,10 @@ def test_skinny_gemm_rejects_bad_shapes():
     with pytest.raises(ValueError):  # M > 64
         _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, w.data_ptr(), 64, y.data_ptr(), 64, 65, 64, 64,
                   _lib.MB_BF16, None, 0, st())
+    with pytest.raises(NotImplementedError):  # K not a multiple of the 64-wide chunk
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, w.data_ptr(), 64, y.data_ptr(), 64, 8, 64, 40,
+                  _lib.MB_BF16, None, 0, st())
+    assert _lib.wait_timeouts() == 0
 
 
 # ------------------------------------------------------------------ attention masks
