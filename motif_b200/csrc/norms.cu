@@ -138,6 +138,9 @@ inline unsigned flat_grid(int64_t total, int threads) {
 
 // ---------------------------------------------------------------------------- attn-res
 constexpr int kMaxSrc = 8;
+// Up to this many rows the fused attn-res read runs one CTA per row (sources in parallel);
+// above it, one warp per row streams the sources (the prefill shape, HBM-bound either way).
+constexpr int64_t kSrcParallelRows = 2048;
 struct SrcPtrs {
   const void* p[kMaxSrc];
   int64_t sb[kMaxSrc];
@@ -292,6 +295,105 @@ __global__ void attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, co
     }
     if (h_out) *reinterpret_cast<uint4*>(h_out + row * ors + (v * 32 + lane) * 8) = *reinterpret_cast<uint4*>(o8);
     *reinterpret_cast<uint4*>(hn_out + row * ors + (v * 32 + lane) * 8) = *reinterpret_cast<uint4*>(n8);
+  }
+}
+
+// Few-row (decode) form of the fused read: one CTA per row, warp s loads source s, so all
+// sources of the row are in flight at once instead of one after another in a single warp.
+// The logits meet in shared memory; thread g < D/8 then sums its 8-element group over the
+// sources in order, and the output RMSNorm reduces across the CTA.
+template <typename T, int NV>
+__global__ void __launch_bounds__(32 * kMaxSrc) attn_res_norm_src_kernel(
+    SrcPtrs src, int n_src, int64_t srs, const T* __restrict__ w, const T* __restrict__ q,
+    T* __restrict__ h_out, T* __restrict__ hn_out, int64_t ors, float eps_src, float eps_out) {
+  constexpr int D = 256 * NV, G = D / 8;
+  __shared__ uint4 xs[kMaxSrc][G];
+  __shared__ float lg[kMaxSrc], red[kMaxSrc];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x;
+  const bool mix = q != nullptr && n_src > 1;
+  if (warp < n_src) {
+    const T* xr = static_cast<const T*>(src.p[warp]) + row * srs;
+    uint4 raw[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) raw[v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+    float ss = 0.f, dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      xs[warp][v * 32 + lane] = raw[v];
+      if (mix) {
+        uint4 rq = *reinterpret_cast<const uint4*>(q + (v * 32 + lane) * 8);
+        uint4 rw = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
+        const T* q8 = reinterpret_cast<const T*>(&rq);
+        const T* w8 = reinterpret_cast<const T*>(&rw);
+        const T* e8 = reinterpret_cast<const T*>(&raw[v]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x = to_f(e8[e]);
+          ss += x * x;
+          dot += to_f(q8[e]) * to_f(w8[e]) * x;
+        }
+      }
+    }
+    if (mix) {
+      ss = warp_sum(ss);
+      dot = warp_sum(dot);
+      if (lane == 0) lg[warp] = dot * rsqrtf(ss / (float)D + eps_src);
+    }
+  }
+  __syncthreads();
+  float pw[kMaxSrc];
+  float inv = 1.f;
+  if (mix) {
+    float m = -INFINITY, den = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxSrc; ++s)
+      if (s < n_src) m = fmaxf(m, lg[s]);
+#pragma unroll
+    for (int s = 0; s < kMaxSrc; ++s) {
+      pw[s] = s < n_src ? expf(lg[s] - m) : 0.f;
+      den += pw[s];
+    }
+    inv = 1.f / den;
+  } else {
+#pragma unroll
+    for (int s = 0; s < kMaxSrc; ++s) pw[s] = 1.f;
+  }
+  float h[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) h[e] = 0.f;
+  float ss = 0.f;
+  if (tid < G) {
+#pragma unroll
+    for (int s = 0; s < kMaxSrc; ++s) {
+      if (s >= n_src) break;
+      const uint4 raw = xs[s][tid];
+      const T* e8 = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = fmaf(pw[s], to_f(e8[e]), h[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      h[e] *= inv;
+      ss += h[e] * h[e];
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxSrc; ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)D + eps_out);
+  if (tid < G) {
+    T o8[8], n8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o8[e] = from_f<T>(h[e]);
+      n8[e] = from_f<T>(h[e] * r);
+    }
+    if (h_out) *reinterpret_cast<uint4*>(h_out + row * ors + tid * 8) = *reinterpret_cast<uint4*>(o8);
+    *reinterpret_cast<uint4*>(hn_out + row * ors + tid * 8) = *reinterpret_cast<uint4*>(n8);
   }
 }
 
@@ -526,7 +628,22 @@ extern "C" int motif_b200_attn_res_norm(const void* const* sources, int n_src, i
     const int blk = 32 * kWarpsPerBlock;
     cudaStream_t st = (cudaStream_t)stream;
     const bool vec = aligned && sizeof(Tt) == 2 && D % 256 == 0 && D / 256 <= 4;
-    if (vec && D == 256)
+    if (vec && rows <= kSrcParallelRows) {  // decode-sized: one CTA per row, sources in parallel
+      const unsigned g = (unsigned)rows;
+      const int bs = 32 * kMaxSrc;
+      if (D == 256)
+        attn_res_norm_src_kernel<Tt, 1><<<g, bs, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                          (Tt*)h_out, (Tt*)hn_out, ors, eps_src, eps_out);
+      else if (D == 512)
+        attn_res_norm_src_kernel<Tt, 2><<<g, bs, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                          (Tt*)h_out, (Tt*)hn_out, ors, eps_src, eps_out);
+      else if (D == 768)
+        attn_res_norm_src_kernel<Tt, 3><<<g, bs, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                          (Tt*)h_out, (Tt*)hn_out, ors, eps_src, eps_out);
+      else
+        attn_res_norm_src_kernel<Tt, 4><<<g, bs, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
+                                                          (Tt*)h_out, (Tt*)hn_out, ors, eps_src, eps_out);
+    } else if (vec && D == 256)
       attn_res_norm_vec_kernel<Tt, 1><<<grid, blk, 0, st>>>(sp, n_src, srs, (const Tt*)weight, (const Tt*)query,
                                                              (Tt*)h_out, (Tt*)hn_out, ors, rows, eps_src, eps_out);
     else if (vec && D == 512)

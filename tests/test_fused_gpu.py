@@ -30,9 +30,9 @@ TOL = {torch.float32: 1e-5, torch.bfloat16: 1.5e-2}
 @pytest.mark.parametrize('D', [64, 256, 768])
 @pytest.mark.parametrize('n', [1, 2, 4, 5])
 @pytest.mark.parametrize('mode', ['softmax', 'sum'])
-def test_attn_res_norm(dtype, D, n, mode):
+@pytest.mark.parametrize('rows', [37, 2500])  # one CTA per row (decode) / one warp per row
+def test_attn_res_norm(dtype, D, n, mode, rows):
     g = torch.Generator().manual_seed(D + n)
-    rows = 37
     srcs = [torch.randn(rows, D, generator=g).to(dtype) for _ in range(n)]
     w = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype)
     qv = (torch.randn(D, generator=g) / D ** 0.5).to(dtype)
