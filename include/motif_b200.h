@@ -228,6 +228,18 @@ MB_API int motif_b200_gdn_decode(const void* proj, int64_t proj_stride, const vo
                           float* state, const void* gate, const void* onorm_w, void* out,
                           int64_t out_stride, int64_t B, int64_t H, int64_t Dk, int64_t Dv,
                           float eps, int dtype, void* stream);
+/* motif_b200_gdn_decode plus the decoder's SwiGLU MLP activation in the same launch:
+ * act[b, :hid] = gu[b, :hid] * silu(gu[b, hid:2 hid]) (motif/ops/swiglu.py:252-253), rows of
+ * gu / act strided by gu_stride / act_stride elements.  The two are independent (both read
+ * the packed projection row), so extra CTAs of the GDN launch compute the activation; when
+ * that is not possible (fp32, unaligned rows, a shape without the split kernel) a separate
+ * SwiGLU launch follows, with the same results.  Replaces decoder.py:203-207's GDN step and
+ * mlp.py's activation. */
+MB_API int motif_b200_gdn_decode_swiglu(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
+                                 const void* dt_bias, void* conv_state, float* state, const void* gate,
+                                 const void* onorm_w, void* out, int64_t os, int64_t B, int64_t H,
+                                 int64_t Dk, int64_t Dv, float eps, const void* gu, int64_t gu_stride,
+                                 void* act, int64_t act_stride, int64_t hid, int dtype, void* stream);
 
 /* Chord input preparation: per token, RMSNorm each q head (weight qn_w [D]) and each k
  * head (kn_w [D]) of `proj` rows [q (H*D) | k (Hkv*D) | v (Hkv*D) | ...]; writes q
@@ -238,6 +250,14 @@ MB_API int motif_b200_chord_prep(const void* proj, int64_t proj_stride, const vo
                           const void* kn_w, void* q, void* k_cache, void* v_cache, int64_t cap,
                           const int32_t* pos_dev, int64_t pos_host, int64_t B, int64_t T,
                           int64_t H, int64_t Hkv, int64_t D, float eps, int dtype, void* stream);
+/* motif_b200_chord_prep plus the decoder's SwiGLU MLP activation over the B*T rows in the
+ * same launch (as motif_b200_gdn_decode_swiglu; a separate SwiGLU launch follows when the
+ * vector kernel cannot run). */
+MB_API int motif_b200_chord_prep_swiglu(const void* proj, int64_t proj_stride, const void* qn_w,
+                                 const void* kn_w, void* q, void* k_cache, void* v_cache, int64_t cap,
+                                 const int32_t* pos_dev, int64_t pos_host, int64_t B, int64_t T, int64_t H,
+                                 int64_t Hkv, int64_t D, float eps, const void* gu, int64_t gu_stride,
+                                 void* act, int64_t act_stride, int64_t hid, int dtype, void* stream);
 
 /* Chord decode/short-query attention over a cache whose length is read on the device:
  * S = *len_dev (+ T new tokens already appended), q_start = S - T.  Same math as

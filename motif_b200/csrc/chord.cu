@@ -1644,26 +1644,37 @@ extern "C" int motif_b200_chord_decode_masked(const void* q, const void* k_cache
 
 // Vectorised preparation for 16-bit rows with D in {32, 64, 128}: a group of D/8 lanes owns
 // one (token, slot) row (slot = q head | k head | v head) as 16-byte vectors; the q / k RMS
-// norms reduce over the group's lanes.  A warp walks one token's H + 2 Hkv slots.
+// norms reduce over the group's lanes.  A warp takes one token's group of 32 / (D/8) slots,
+// so all H + 2 Hkv slots of a token are read at once (decode has few tokens: one warp per
+// token walking its slots in turn left the launch latency-bound).
 template <typename T, int D>
 __global__ void __launch_bounds__(256) chord_prep_vec_kernel(const T* __restrict__ proj, int64_t ps,
                                                              const T* __restrict__ qn_w, const T* __restrict__ kn_w,
                                                              T* __restrict__ qo, T* __restrict__ kc, T* __restrict__ vc,
                                                              int64_t cap, const int32_t* __restrict__ pos_dev,
                                                              int64_t pos_host, int64_t rows, int Tn, int H, int Hkv,
-                                                             float eps) {
+                                                             float eps, SwigluRole<T> sw, int main_blocks) {
   constexpr int LPS = D / 8;       // lanes per slot
   constexpr int SPI = 32 / LPS;    // slots per warp iteration
+  if ((int)blockIdx.x >= main_blocks) {  // trailing CTAs: the decoder's SwiGLU activation
+    swiglu_role_run<T>(sw, (int64_t)(blockIdx.x - main_blocks) * 256 + threadIdx.x,
+                       (int64_t)(gridDim.x - main_blocks) * 256);
+    return;
+  }
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPS, grp = lane / LPS;
-  const int64_t tok = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  // one warp per (token, group of SPI slots): every slot of a token is read at once
+  const int slots = H + 2 * Hkv;
+  const int nchunk = (slots + SPI - 1) / SPI;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t tok = wid / nchunk;
   if (tok >= rows) return;
+  const int s0 = (int)(wid % nchunk) * SPI;
   const int b = (int)(tok / Tn), t = (int)(tok % Tn);
   const int64_t pos = (pos_dev ? (int64_t)*pos_dev : pos_host) + t;
   const bool pos_ok = pos >= 0 && pos < cap;  // a device-side position past the capacity skips the cache write
-  const int slots = H + 2 * Hkv;
   const T* src_row = proj + tok * ps;
-  for (int s0 = 0; s0 < slots; s0 += SPI) {
+  {
     const int slot = s0 + grp;
     const bool act = slot < slots;  // lanes past the last slot still join the reductions
     uint4 raw = make_uint4(0, 0, 0, 0);
@@ -1678,13 +1689,13 @@ __global__ void __launch_bounds__(256) chord_prep_vec_kernel(const T* __restrict
     }
 #pragma unroll
     for (int o2 = 1; o2 < LPS; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
-    if (!act) continue;
+    if (!act) return;
     if (slot >= H + Hkv) {  // value: plain copy into the cache
       if (pos_ok) {
         const int kvh = slot - H - Hkv;
         *reinterpret_cast<uint4*>(vc + (((int64_t)b * Hkv + kvh) * cap + pos) * D + sub * 8) = raw;
       }
-      continue;
+      return;
     }
     const float r = rsqrtf(ss / (float)D + eps);
     const T* w = (slot < H ? qn_w : kn_w) + sub * 8;
@@ -1702,28 +1713,45 @@ __global__ void __launch_bounds__(256) chord_prep_vec_kernel(const T* __restrict
   }
 }
 
-extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, const void* qn_w, const void* kn_w,
-                                     void* q, void* k_cache, void* v_cache, int64_t cap, const int32_t* pos_dev,
-                                     int64_t pos_host, int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t D,
-                                     float eps, int dtype, void* stream) {
+namespace mb {
+namespace {
+// q/k RMSNorm + cache append, with the decoder's SwiGLU activation in the same launch when
+// `hid` > 0 and the vector kernel runs (otherwise a separate motif_b200_swiglu launch follows).
+int chord_prep_impl(const void* proj, int64_t proj_stride, const void* qn_w, const void* kn_w, void* q,
+                    void* k_cache, void* v_cache, int64_t cap, const int32_t* pos_dev, int64_t pos_host, int64_t B,
+                    int64_t T, int64_t H, int64_t Hkv, int64_t D, float eps, int dtype, void* stream, const void* gu,
+                    int64_t gs, void* act, int64_t as, int64_t hid) {
   MB_REQUIRE(proj && qn_w && kn_w && q && k_cache && v_cache, MB_ERR_ARG, "chord_prep: null pointer");
   MB_REQUIRE(B >= 0 && T >= 0 && H > 0 && Hkv > 0 && D > 0, MB_ERR_SHAPE, "chord_prep: bad shape");
   MB_REQUIRE(pos_dev != nullptr || pos_host + T <= cap, MB_ERR_SHAPE, "chord_prep: cache capacity %lld exceeded",
              (long long)cap);
+  MB_REQUIRE(hid == 0 || (gu && act && hid > 0 && hid <= (1 << 24)), MB_ERR_ARG, "chord_prep_swiglu: bad MLP args");
   const int64_t rows = B * T;
   if (rows == 0) return MB_OK;
   const bool vec = dtype != MB_F32 && (D == 32 || D == 64 || D == 128) && proj_stride % 8 == 0 &&
                    ((uintptr_t)proj | (uintptr_t)qn_w | (uintptr_t)kn_w | (uintptr_t)q | (uintptr_t)k_cache |
                     (uintptr_t)v_cache) % 16 == 0;
-  return dispatch_dtype(dtype, [&](auto t) {
+  bool fused = false;
+  const int rc = dispatch_dtype(dtype, [&](auto t) {
     using Tt = decltype(t);
     if constexpr (sizeof(Tt) == 2) {
       if (vec) {
         auto go = [&](auto dc) {
           constexpr int DD = decltype(dc)::value;
-          chord_prep_vec_kernel<Tt, DD><<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+          constexpr int SPI = 32 / (DD / 8);
+          const int64_t warps = rows * ((H + 2 * Hkv + SPI - 1) / SPI);
+          const int64_t main_blocks = (warps + 7) / 8;
+          SwigluRole<Tt> sw{(const Tt*)gu, gs, (Tt*)act, as, rows, 0};
+          int64_t extra = 0;
+          if (swiglu_role_ok(gu, gs, act, as, hid)) {
+            sw.hid = (int)hid;
+            extra = swiglu_role_blocks(rows, hid, 256);
+            fused = true;
+          }
+          MB_REQUIRE(main_blocks + extra < (1LL << 31), MB_ERR_SHAPE, "chord_prep: too many rows");
+          chord_prep_vec_kernel<Tt, DD><<<(unsigned)(main_blocks + extra), 256, 0, (cudaStream_t)stream>>>(
               (const Tt*)proj, proj_stride, (const Tt*)qn_w, (const Tt*)kn_w, (Tt*)q, (Tt*)k_cache, (Tt*)v_cache,
-              cap, pos_dev, pos_host, rows, (int)T, (int)H, (int)Hkv, eps);
+              cap, pos_dev, pos_host, rows, (int)T, (int)H, (int)Hkv, eps, sw, (int)main_blocks);
           return check_launch("chord_prep");
         };
         if (D == 32) return go(std::integral_constant<int, 32>{});
@@ -1737,6 +1765,29 @@ extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, cons
         pos_dev, pos_host, rows, (int)T, (int)H, (int)Hkv, (int)D, eps);
     return check_launch("chord_prep");
   });
+  if (rc || hid == 0 || fused) return rc;
+  return motif_b200_swiglu(gu, act, rows, hid, gs, as, dtype, stream);
+}
+}  // namespace
+}  // namespace mb
+
+extern "C" int motif_b200_chord_prep(const void* proj, int64_t proj_stride, const void* qn_w, const void* kn_w,
+                                     void* q, void* k_cache, void* v_cache, int64_t cap, const int32_t* pos_dev,
+                                     int64_t pos_host, int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t D,
+                                     float eps, int dtype, void* stream) {
+  return mb::chord_prep_impl(proj, proj_stride, qn_w, kn_w, q, k_cache, v_cache, cap, pos_dev, pos_host, B, T, H,
+                             Hkv, D, eps, dtype, stream, nullptr, 0, nullptr, 0, 0);
+}
+
+extern "C" int motif_b200_chord_prep_swiglu(const void* proj, int64_t proj_stride, const void* qn_w,
+                                            const void* kn_w, void* q, void* k_cache, void* v_cache, int64_t cap,
+                                            const int32_t* pos_dev, int64_t pos_host, int64_t B, int64_t T,
+                                            int64_t H, int64_t Hkv, int64_t D, float eps, const void* gu,
+                                            int64_t gu_stride, void* act, int64_t act_stride, int64_t hid,
+                                            int dtype, void* stream) {
+  MB_REQUIRE(gu && act && hid > 0, MB_ERR_ARG, "chord_prep_swiglu: null MLP pointer or hid <= 0");
+  return mb::chord_prep_impl(proj, proj_stride, qn_w, kn_w, q, k_cache, v_cache, cap, pos_dev, pos_host, B, T, H,
+                             Hkv, D, eps, dtype, stream, gu, gu_stride, act, act_stride, hid);
 }
 
 // ------------------------------------------------------------------ allocation-free decode

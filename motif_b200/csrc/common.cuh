@@ -351,4 +351,52 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// ------------------------------------------------------------------ fused SwiGLU role
+// The SwiGLU MLP activation act[r, :] = gu[r, :hid] * round(silu(gu[r, hid:2 hid]))
+// (motif/ops/swiglu.py:252-253), one 8-element (16-byte) group per thread.  Decode kernels
+// whose launch would otherwise be followed by a separate SwiGLU launch append
+// swiglu_role_blocks() CTAs to their grid that run this instead (the two are independent:
+// both read the same packed projection row), saving one launch per decoder.
+// Needs hid % 8 == 0, 16-byte aligned rows and strides that are multiples of 8.
+template <typename T>
+struct SwigluRole {
+  const T* gu;   // [rows, 2 hid] value | gate, row stride gs
+  int64_t gs;
+  T* act;        // [rows, hid], row stride as
+  int64_t as;
+  int64_t rows;
+  int hid;       // 0: no SwiGLU role
+};
+template <typename T>
+__device__ __forceinline__ void swiglu_group(const T* __restrict__ x, int64_t xs, T* __restrict__ y, int64_t ys,
+                                             int N, int64_t i) {
+  const int nv = N / 8;
+  const int64_t row = i / nv;
+  const int c = (int)(i % nv) * 8;
+  const T* xr = x + row * xs;
+  const uint4 rv = *reinterpret_cast<const uint4*>(xr + c);
+  const uint4 rg = *reinterpret_cast<const uint4*>(xr + N + c);
+  const T* v8 = reinterpret_cast<const T*>(&rv);
+  const T* g8 = reinterpret_cast<const T*>(&rg);
+  __align__(16) T o8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float sg = to_f(from_f<T>(siluf_(to_f(g8[e]))));
+    o8[e] = from_f<T>(to_f(v8[e]) * sg);
+  }
+  *reinterpret_cast<uint4*>(y + row * ys + c) = *reinterpret_cast<const uint4*>(o8);
+}
+// Thread `first` of the role's CTAs, `stride` role threads in all.
+template <typename T>
+__device__ __forceinline__ void swiglu_role_run(const SwigluRole<T>& sw, int64_t first, int64_t stride) {
+  const int64_t total = sw.rows * (sw.hid / 8);
+  for (int64_t i = first; i < total; i += stride) swiglu_group<T>(sw.gu, sw.gs, sw.act, sw.as, sw.hid, i);
+}
+inline int64_t swiglu_role_blocks(int64_t rows, int64_t hid, int threads) {
+  return hid > 0 ? (rows * (hid / 8) + threads - 1) / threads : 0;
+}
+inline bool swiglu_role_ok(const void* gu, int64_t gs, const void* act, int64_t as, int64_t hid) {
+  return hid > 0 && hid % 8 == 0 && gs % 8 == 0 && as % 8 == 0 && ((uintptr_t)gu | (uintptr_t)act) % 16 == 0;
+}
+
 }  // namespace mb

@@ -159,9 +159,14 @@ __global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
     const T* __restrict__ proj, int64_t ps, const T* __restrict__ conv_w, const T* __restrict__ A_log,
     const T* __restrict__ dt_bias, T* __restrict__ conv_state, float* __restrict__ state,
     const T* __restrict__ gate, const T* __restrict__ onw, T* __restrict__ out, int64_t os, int H,
-    float eps) {
+    float eps, SwigluRole<T> sw, int main_blocks) {
   static_assert(DV == 2 * DK, "one conv channel per thread needs Dv == 2 Dk");
   constexpr int NT = 2 * DV, HR = DK / 2;
+  if ((int)blockIdx.x >= main_blocks) {  // trailing CTAs: the decoder's SwiGLU activation
+    swiglu_role_run<T>(sw, (int64_t)(blockIdx.x - main_blocks) * NT + threadIdx.x,
+                       (int64_t)(gridDim.x - main_blocks) * NT);
+    return;
+  }
   const int b = blockIdx.x / H, h = blockIdx.x % H;
   const int tid = threadIdx.x;
   const int j = tid % DV, half = tid / DV;
@@ -560,16 +565,22 @@ extern "C" int motif_b200_gdn_recurrent(const void* q, const void* k, const void
   });
 }
 
-extern "C" int motif_b200_gdn_decode(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
-                                     const void* dt_bias, void* conv_state, float* state, const void* gate,
-                                     const void* onorm_w, void* out, int64_t os, int64_t B, int64_t H,
-                                     int64_t Dk, int64_t Dv, float eps, int dtype, void* stream) {
+namespace mb {
+namespace {
+// The L == 1 step, with the decoder's SwiGLU activation in the same launch when `hid` > 0 and
+// the split kernel runs (otherwise a separate motif_b200_swiglu launch follows).
+int gdn_decode_impl(const void* proj, int64_t ps, const void* conv_w, const void* A_log, const void* dt_bias,
+                    void* conv_state, float* state, const void* gate, const void* onorm_w, void* out, int64_t os,
+                    int64_t B, int64_t H, int64_t Dk, int64_t Dv, float eps, int dtype, void* stream,
+                    const void* gu, int64_t gs, void* act, int64_t as, int64_t hid) {
   MB_REQUIRE(proj && conv_w && A_log && dt_bias && conv_state && state && gate && onorm_w && out,
              MB_ERR_ARG, "gdn_decode: null pointer");
   MB_REQUIRE(B >= 0 && H > 0 && B * H < 2147483647LL, MB_ERR_SHAPE, "gdn_decode: bad shape");
   MB_REQUIRE(Dv >= Dk, MB_ERR_UNSUPPORTED, "gdn_decode: needs Dv >= Dk");
+  MB_REQUIRE(hid == 0 || (gu && act && hid > 0 && hid <= (1 << 24)), MB_ERR_ARG, "gdn_decode_swiglu: bad MLP args");
   if (B == 0) return MB_OK;
-  return dispatch_dtype(dtype, [&](auto t) {
+  bool fused = false;
+  const int rc = dispatch_dtype(dtype, [&](auto t) {
     using T = decltype(t);
     return dispatch_dk(Dk, [&](auto dkc) {
       constexpr int DK = decltype(dkc)::value;
@@ -578,9 +589,16 @@ extern "C" int motif_b200_gdn_decode(const void* proj, int64_t ps, const void* c
         if constexpr (DV < DK) {
           return set_error(MB_ERR_UNSUPPORTED, "gdn_decode: needs Dv >= Dk");
         } else if constexpr (DV == 2 * DK && DK % 32 == 0 && 2 * DV <= 512) {
-          gdn_decode_split_kernel<T, DK, DV><<<(unsigned)(B * H), 2 * DV, 0, (cudaStream_t)stream>>>(
+          SwigluRole<T> sw{(const T*)gu, gs, (T*)act, as, B, 0};
+          int64_t extra = 0;
+          if (sizeof(T) == 2 && swiglu_role_ok(gu, gs, act, as, hid)) {
+            sw.hid = (int)hid;
+            extra = swiglu_role_blocks(B, hid, 2 * DV);
+            fused = true;
+          }
+          gdn_decode_split_kernel<T, DK, DV><<<(unsigned)(B * H + extra), 2 * DV, 0, (cudaStream_t)stream>>>(
               (const T*)proj, ps, (const T*)conv_w, (const T*)A_log, (const T*)dt_bias, (T*)conv_state,
-              state, (const T*)gate, (const T*)onorm_w, (T*)out, os, (int)H, eps);
+              state, (const T*)gate, (const T*)onorm_w, (T*)out, os, (int)H, eps, sw, (int)(B * H));
           return check_launch("gdn_decode");
         } else {
           gdn_decode_kernel<T, DK, DV><<<(unsigned)(B * H), DV, 0, (cudaStream_t)stream>>>(
@@ -591,6 +609,28 @@ extern "C" int motif_b200_gdn_decode(const void* proj, int64_t ps, const void* c
       });
     });
   });
+  if (rc || hid == 0 || fused) return rc;
+  return motif_b200_swiglu(gu, act, B, hid, gs, as, dtype, stream);
+}
+}  // namespace
+}  // namespace mb
+
+extern "C" int motif_b200_gdn_decode(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
+                                     const void* dt_bias, void* conv_state, float* state, const void* gate,
+                                     const void* onorm_w, void* out, int64_t os, int64_t B, int64_t H,
+                                     int64_t Dk, int64_t Dv, float eps, int dtype, void* stream) {
+  return mb::gdn_decode_impl(proj, ps, conv_w, A_log, dt_bias, conv_state, state, gate, onorm_w, out, os, B, H, Dk,
+                             Dv, eps, dtype, stream, nullptr, 0, nullptr, 0, 0);
+}
+
+extern "C" int motif_b200_gdn_decode_swiglu(const void* proj, int64_t ps, const void* conv_w, const void* A_log,
+                                            const void* dt_bias, void* conv_state, float* state, const void* gate,
+                                            const void* onorm_w, void* out, int64_t os, int64_t B, int64_t H,
+                                            int64_t Dk, int64_t Dv, float eps, const void* gu, int64_t gu_stride,
+                                            void* act, int64_t act_stride, int64_t hid, int dtype, void* stream) {
+  MB_REQUIRE(gu && act && hid > 0, MB_ERR_ARG, "gdn_decode_swiglu: null MLP pointer or hid <= 0");
+  return mb::gdn_decode_impl(proj, ps, conv_w, A_log, dt_bias, conv_state, state, gate, onorm_w, out, os, B, H, Dk,
+                             Dv, eps, dtype, stream, gu, gu_stride, act, act_stride, hid);
 }
 
 extern "C" int motif_b200_gdn_prep(const void* proj, int64_t ps, const void* conv_w, const void* A_log,

@@ -82,24 +82,9 @@ __global__ void swiglu_kernel(const T* __restrict__ x, T* __restrict__ y, int64_
 template <typename T>
 __global__ void swiglu_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int64_t xs,
                                   int64_t ys) {
-  const int nv = N / 8;
-  const int64_t total = M * nv;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / nv;
-    const int c = (int)(i % nv) * 8;
-    const T* xr = x + row * xs;
-    uint4 rv = *reinterpret_cast<const uint4*>(xr + c);
-    uint4 rg = *reinterpret_cast<const uint4*>(xr + N + c);
-    const T* v8 = reinterpret_cast<const T*>(&rv);
-    const T* g8 = reinterpret_cast<const T*>(&rg);
-    T o8[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float sg = to_f(from_f<T>(siluf_(to_f(g8[e]))));
-      o8[e] = from_f<T>(to_f(v8[e]) * sg);
-    }
-    *reinterpret_cast<uint4*>(y + row * ys + c) = *reinterpret_cast<const uint4*>(o8);
-  }
+  const int64_t total = M * (N / 8);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    swiglu_group<T>(x, xs, y, ys, N, i);
 }
 
 template <typename T>

@@ -223,12 +223,12 @@ class GraphDecoder:
         H, dk, dv, hid = pk.H, pk.dk, pk.dv, pk.hid
         N_in = proj.shape[1]
         cat = torch.empty((B, H * dv + hid), dtype=dt, device=dev)
-        _lib.call('motif_b200_gdn_decode', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+        # the recurrent step and the MLP activation in one launch
+        _lib.call('motif_b200_gdn_decode_swiglu', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
                   _lib.ptr(pk.dt_bias), _lib.ptr(slot.conv), _lib.ptr(slot.state),
                   proj.data_ptr() + pk.off_g * proj.element_size(), _lib.ptr(pk.onorm_w), _lib.ptr(cat),
-                  cat.stride(0), B, H, dk, dv, NORM_EPS, dc, st)
-        _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
-                  cat.data_ptr() + H * dv * cat.element_size(), B, hid, N_in, cat.stride(0), dc, st)
+                  cat.stride(0), B, H, dk, dv, NORM_EPS, proj.data_ptr() + pk.off_gu * proj.element_size(), N_in,
+                  cat.data_ptr() + H * dv * cat.element_size(), cat.stride(0), hid, dc, st)
         return _mm(cat, pk.w_out)
 
     def _chord(self, pk, proj, lc: KVLayerCache, dc, st):
@@ -238,18 +238,18 @@ class GraphDecoder:
         N_in = proj.shape[1]
         cap = lc._kbuf.shape[2]
         qb = torch.empty((B, d), dtype=dt, device=dev)
+        act = torch.empty((B, hid), dtype=dt, device=dev)
         lens_ptr = self.lens.data_ptr()
-        _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
-                  _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap, lens_ptr, 0, B, 1, H, Hkv, D, NORM_EPS, dc, st)
+        # q/k norms + cache append and the MLP activation in one launch
+        _lib.call('motif_b200_chord_prep_swiglu', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w),
+                  _lib.ptr(qb), _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap, lens_ptr, 0, B, 1, H, Hkv, D, NORM_EPS,
+                  proj.data_ptr() + pk.off_gu * proj.element_size(), N_in, _lib.ptr(act), hid, hid, dc, st)
         attn = torch.empty((B, d), dtype=dt, device=dev)
         ws_bytes = _lib.load().motif_b200_chord_decode_workspace_bytes(B, H, 1, D, self.splits)
         ws = torch.empty((max(ws_bytes, 4) // 4,), dtype=torch.float32, device=dev)
         _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap,
                   lens_ptr + 4, 0, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax),
                   _lib.ptr(attn), d, B, H, Hkv, 1, D, D ** -0.5, GGD_EPS, self.splits, _lib.ptr(ws), ws_bytes, dc, st)
-        act = torch.empty((B, hid), dtype=dt, device=dev)
-        _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), B, hid,
-                  N_in, hid, dc, st)
         f = _mm(act, pk.w_down)
         a = _mm(attn, pk.w_o)
         _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(),

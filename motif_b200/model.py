@@ -617,9 +617,12 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
         # gdn_attn.py:198-199: the L == 1 step is the recurrence, fused with conv and o_norm.
         state = state_in if state_in is not None else torch.zeros((B, H, dk, dv), dtype=torch.float32, device=dev)
         conv = conv_in if conv_in is not None else torch.zeros((B, 3, C), dtype=dt, device=dev)
-        _lib.call('motif_b200_gdn_decode', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
+        # ... and with the MLP activation in the same launch
+        _lib.call('motif_b200_gdn_decode_swiglu', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
                   _lib.ptr(pk.dt_bias), _lib.ptr(conv), _lib.ptr(state), proj.data_ptr() + pk.off_g * proj.element_size(),
-                  _lib.ptr(pk.onorm_w), _lib.ptr(cat), cat.stride(0), B, H, dk, dv, eps, dc, st)
+                  _lib.ptr(pk.onorm_w), _lib.ptr(cat), cat.stride(0), B, H, dk, dv, eps,
+                  proj.data_ptr() + pk.off_gu * proj.element_size(), N_in,
+                  cat.data_ptr() + H * dv * cat.element_size(), cat.stride(0), hid, dc, st)
         conv_out = conv
     elif dt != torch.float32 and (dk, dv) == (64, 128) and N_in % 8 == 0 and not FUSED_GDN_PREFILL:
         # three kernels: preparation fused into the parallel per-chunk UT transform (records in a
@@ -660,8 +663,9 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   _lib.ptr(g), _lib.ptr(state_in), _lib.ptr(state), _lib.ptr(cat), B, H, T, dk, dv,
                   _lib.i64_array(strides), proj.data_ptr() + pk.off_g * proj.element_size(), N_in, dv,
                   _lib.ptr(pk.onorm_w), eps, dc, _lib.ptr(ws), max(ws_bytes, 0), st)
-    _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
-              cat.data_ptr() + H * dv * cat.element_size(), M, hid, N_in, cat.stride(0), dc, st)
+    if T != 1:
+        _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
+                  cat.data_ptr() + H * dv * cat.element_size(), M, hid, N_in, cat.stride(0), dc, st)
     f = _mm(cat, pk.w_out)
     if cache is not None:
         cache._split = (H * dk, H * dk, H * dv)
@@ -698,6 +702,8 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
     cached = cache.length
     q_start = position if position != 0 else cached
     qb = torch.empty((M, d), dtype=dt, device=dev)
+    act = torch.empty((M, hid), dtype=dt, device=dev)
+    act_done = False
     if cache.wide:
         # a wide cache (`cache.py:42-70`) stores every key / value head once per query head: the
         # new keys / values are prepared narrow, widened by the cache's own update, and the
@@ -711,9 +717,12 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
         Hkv = H
     else:
         cache.reserve(cached + T, like=proj, shape=(B, Hkv, D))
-        _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
-                  _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cache._kbuf.shape[2], None, cached, B, T, H, Hkv, D,
-                  NORM_EPS, dc, st)
+        # q/k norms + cache append and the MLP activation in one launch
+        _lib.call('motif_b200_chord_prep_swiglu', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w),
+                  _lib.ptr(qb), _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cache._kbuf.shape[2], None, cached, B,
+                  T, H, Hkv, D, NORM_EPS, proj.data_ptr() + pk.off_gu * proj.element_size(), N_in, _lib.ptr(act),
+                  hid, hid, dc, st)
+        act_done = True
         cache.length = cached + T
     cap = cache._kbuf.shape[2]
     S = cache.length
@@ -746,9 +755,9 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
                       _lib.ptr(cache._vbuf), _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu),
                       _lib.ptr(pk.ssmax), _lib.ptr(log_n), _lib.ptr(attn), B, H, Hkv, T, S, D, q_start, scale,
                       GGD_EPS, _lib.i64_array(strides), _lib.ptr(key_bias), key_bias.stride(0), dc, st)
-    act = torch.empty((M, hid), dtype=dt, device=dev)
-    _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid, N_in,
-              hid, dc, st)
+    if not act_done:
+        _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid,
+                  N_in, hid, dc, st)
     f = _mm(act, pk.w_down)
     a = _mm(attn, pk.w_o)
     _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(), N_in,

@@ -134,6 +134,76 @@ def test_gdn_decode(dtype, B, H, dk, dv):
 
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('B,H,dk,dv,hid', [(64, 12, 64, 128, 2816), (3, 12, 64, 128, 24), (2, 4, 16, 32, 40),
+                                           (5, 12, 64, 128, 20)])
+def test_gdn_decode_swiglu_matches_separate_launches(dtype, B, H, dk, dv, hid):
+    """The fused GDN step + SwiGLU launch gives bit-identical state, conv cache, GDN output and
+    MLP activation to motif_b200_gdn_decode followed by motif_b200_swiglu (hid = 20 is not a
+    multiple of 8: the entry falls back to a separate SwiGLU launch)."""
+    proj, conv_w, A_log, dt_bias, conv_in, C, _ = gdn_setup(B, 1, H, dk, dv, dtype, seed=B + hid)
+    g = torch.Generator().manual_seed(5)
+    N = C + 2 * H + H * dv + 2 * hid
+    proj = torch.cat([proj[..., :C + 2 * H], torch.randn(B, 1, H * dv + 2 * hid, generator=g).to(dtype)], -1)
+    proj = proj.view(B, N).cuda()
+    state = (0.1 * torch.randn(B, H, dk, dv, generator=g)).cuda()
+    onw = (1 + 0.1 * torch.randn(dv, generator=g)).to(dtype).cuda()
+    cw, al, db, ci = (t.cuda() for t in (conv_w, A_log, dt_bias, conv_in))
+    outs = []
+    for fused in (False, True):
+        sd, cc = state.clone(), ci.clone()
+        cat = torch.full((B, H * dv + hid), 7, dtype=dtype, device='cuda')
+        gate = proj.data_ptr() + (C + 2 * H) * proj.element_size()
+        gu = proj.data_ptr() + (C + 2 * H + H * dv) * proj.element_size()
+        act = cat.data_ptr() + H * dv * cat.element_size()
+        if fused:
+            _lib.call('motif_b200_gdn_decode_swiglu', _lib.ptr(proj), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db),
+                      _lib.ptr(cc), _lib.ptr(sd), gate, _lib.ptr(onw), _lib.ptr(cat), cat.stride(0), B, H, dk, dv,
+                      1e-6, gu, N, act, cat.stride(0), hid, _lib.dtype_code(dtype), st())
+        else:
+            _lib.call('motif_b200_gdn_decode', _lib.ptr(proj), N, _lib.ptr(cw), _lib.ptr(al), _lib.ptr(db),
+                      _lib.ptr(cc), _lib.ptr(sd), gate, _lib.ptr(onw), _lib.ptr(cat), cat.stride(0), B, H, dk, dv,
+                      1e-6, _lib.dtype_code(dtype), st())
+            _lib.call('motif_b200_swiglu', gu, act, B, hid, N, cat.stride(0), _lib.dtype_code(dtype), st())
+        outs.append((sd, cc, cat))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    v, gt = proj[:, C + 2 * H + H * dv:].float().split(hid, -1)
+    ref = v * F.silu(gt)
+    assert rel_err(outs[1][2][:, H * dv:].float(), ref) < (1e-5 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('B,T,H,Hkv,D,hid', [(64, 1, 12, 3, 64, 2816), (2, 5, 12, 3, 64, 48), (3, 1, 4, 2, 32, 12)])
+def test_chord_prep_swiglu_matches_separate_launches(dtype, B, T, H, Hkv, D, hid):
+    """The fused Chord prep + SwiGLU launch writes bit-identical q, cache rows and MLP
+    activation to motif_b200_chord_prep followed by motif_b200_swiglu."""
+    g = torch.Generator().manual_seed(B + hid)
+    N = (H + 2 * Hkv) * D + 2 * hid
+    proj = torch.randn(B * T, N, generator=g).to(dtype).cuda()
+    qw = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype).cuda()
+    kw = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype).cuda()
+    cap, pos = T + 9, 4
+    gu = proj.data_ptr() + (H + 2 * Hkv) * D * proj.element_size()
+    outs = []
+    for fused in (False, True):
+        qo = torch.empty(B * T, H * D, dtype=dtype, device='cuda')
+        kc = torch.zeros(B, Hkv, cap, D, dtype=dtype, device='cuda')
+        vc = torch.zeros_like(kc)
+        act = torch.full((B * T, hid), 3, dtype=dtype, device='cuda')
+        if fused:
+            _lib.call('motif_b200_chord_prep_swiglu', _lib.ptr(proj), N, _lib.ptr(qw), _lib.ptr(kw), _lib.ptr(qo),
+                      _lib.ptr(kc), _lib.ptr(vc), cap, None, pos, B, T, H, Hkv, D, 1e-6, gu, N, _lib.ptr(act), hid,
+                      hid, _lib.dtype_code(dtype), st())
+        else:
+            _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N, _lib.ptr(qw), _lib.ptr(kw), _lib.ptr(qo),
+                      _lib.ptr(kc), _lib.ptr(vc), cap, None, pos, B, T, H, Hkv, D, 1e-6, _lib.dtype_code(dtype), st())
+            _lib.call('motif_b200_swiglu', gu, _lib.ptr(act), B * T, hid, N, hid, _lib.dtype_code(dtype), st())
+        outs.append((qo, kc, vc, act))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize('B,T,H,Hkv,D,pos', [(2, 5, 12, 3, 64, 0), (3, 1, 4, 2, 16, 17), (1, 33, 8, 8, 32, 4)])
 def test_chord_prep(dtype, B, T, H, Hkv, D, pos):
     g = torch.Generator().manual_seed(T + pos)
