@@ -14,12 +14,12 @@
 // When the feature blocks alone cannot fill the GPU (768 outputs at K up to 3584), K is split
 // across the CTAs of a thread-block cluster (up to 16 along y).  Each CTA reads its
 // accumulator back with tcgen05.ld (thread = feature, one register per token) into a fp32
-// [token][feature] tile in its own shared memory; after a cluster barrier CTA r sums 1/nsplit
-// of the tile over all CTAs' tiles through distributed shared memory, in split order (a fixed
-// order: results do not depend on timing), and writes its part of Y.  A second cluster
-// barrier keeps every tile alive until its readers are done.  No workspace, no atomics, and
-// an unsplit launch (a cluster of one) takes the same path, which turns the epilogue into
-// coalesced row writes of Y.
+// [token][feature] tile in its own shared memory.  The tile's float4 groups are cut into
+// nsplit slices, CTA p owning slice p: after a cluster barrier every CTA sends slice p of
+// its tile to CTA p with one shared::cta -> shared::cluster bulk copy (completion counted on
+// p's receive barrier), then sums its own slice over the splits in split order (a fixed
+// order: results do not depend on timing) and writes it to Y.  No workspace, no atomics.
+// An unsplit launch (a cluster of one) writes Y straight from the accumulator registers.
 // Every mbarrier wait is bounded; a CTA whose wait runs out counts itself
 // (motif_b200_wait_timeouts), drains what it issued and still takes both cluster barriers.
 #include <algorithm>
@@ -58,8 +58,9 @@ constexpr int kXAtom = kMaxM * kBK * 2;    // 8 KB
 constexpr int kWBytes = kAtoms * kWAtom;
 constexpr int kStageBytes = kAtoms * (kWAtom + kXAtom);
 constexpr int kTileBytes = kMaxM * kBN * 4;  // fp32 partial tile, reuses the ring
-static_assert(kTileBytes <= kStages * kStageBytes, "partial tile must fit the ring");
-constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 8 + 16 + 1024;  // + 1024-byte alignment
+// the partial tile and the receive buffer of the split-K exchange both reuse the ring
+static_assert(2 * kTileBytes <= kStages * kStageBytes, "partial tile and receive buffer must fit the ring");
+constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 16 + 16 + 1024;  // + 1024-byte alignment
 constexpr uint32_t kWait = 1u << 22;
 constexpr uint32_t kTmemCols = 64;
 
@@ -75,13 +76,6 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
   return r;
 }
-// Generic address of the same shared-memory location in CTA `rank` of this cluster.
-__device__ __forceinline__ const float4* map_rank(const float4* p, uint32_t rank) {
-  uint64_t r;
-  asm("mapa.u64 %0, %1, %2;\n" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
-  return reinterpret_cast<const float4*>(r);
-}
-
 template <typename T>
 __global__ void __launch_bounds__(128, SK_MINB) skinny_tc_kernel(const __grid_constant__ CUtensorMap tmW,
                                                            const __grid_constant__ CUtensorMap tmX,
@@ -95,7 +89,8 @@ __global__ void __launch_bounds__(128, SK_MINB) skinny_tc_kernel(const __grid_co
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * kStageBytes);
   uint64_t* empty = full + kStages;
   uint64_t* done = empty + kStages;
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* recvbar = done + 1;  // split-K: the other splits' slices of this CTA's part of the tile
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(recvbar + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = blockIdx.x, ks = blockIdx.y, nsplit = gridDim.y;
   const int n0 = nb * kBN;
@@ -117,7 +112,13 @@ __global__ void __launch_bounds__(128, SK_MINB) skinny_tc_kernel(const __grid_co
       mbar_init(&empty[i], 1);
     }
     mbar_init(done, 1);
+    mbar_init(recvbar, 1);
     mbar_init_fence();
+    if (nsplit > 1) {  // the bytes the other nsplit - 1 CTAs of the cluster will send here
+      const int G = M * (kBN / 4), r = (int)cluster_rank();
+      const int len = (r + 1) * G / nsplit - r * G / nsplit;
+      mbar_arrive_expect_tx(recvbar, (uint32_t)((nsplit - 1) * len * 16));
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -221,63 +222,73 @@ __global__ void __launch_bounds__(128, SK_MINB) skinny_tc_kernel(const __grid_co
     return;
   }
   float* tile = reinterpret_cast<float*>(sm);  // [token][feature] partial, the ring is free now
+  float* recv = tile + kMaxM * kBN;            // [nsplit][slice] received partials
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     if (i < M) tile[i * kBN + f] = have ? __uint_as_float(r0[i]) : 0.f;
     if (32 + i < M) tile[(32 + i) * kBN + f] = have ? __uint_as_float(r1[i]) : 0.f;
   }
-  cluster_sync_all();  // every CTA's partial tile is written
-  // CTA r sums float4 groups r*128 + tid + j*nsplit*128 over all split tiles, in split order;
-  // loads of four splits x four groups are in flight together.
-  const float4* mine = reinterpret_cast<const float4*>(tile);
+  fence_proxy_async_smem();  // the tile is read by bulk copies (async proxy)
+  // every CTA of the cluster has written its tile and is done with its ring (so its receive
+  // buffer may be written), and its receive barrier is initialised
+  cluster_sync_all();
+  // Reduce-scatter through distributed shared memory: the float4 groups of the [M][128] tile
+  // are cut into nsplit contiguous slices; CTA p owns slice p.  Thread 0 sends slice p of
+  // this tile to CTA p with one bulk copy each (the copy engine moves the bytes, completion
+  // counted on p's receive barrier); then every CTA sums its slice over the splits in split
+  // order (deterministic) and writes it to Y.
   const int rank = (int)cluster_rank();
-  const int ngroups = M * (kBN / 4), stride = nsplit * 128;
-  for (int g0 = rank * 128 + tid; g0 < ngroups; g0 += 4 * stride) {
-    float4 acc[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp0 = 0; sp0 < nsplit; sp0 += 4) {
-      float4 v[4][4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float4* src = map_rank(mine, (uint32_t)min(sp0 + u, nsplit - 1));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int g = g0 + j * stride;
-          v[u][j] = (sp0 + u < nsplit && g < ngroups) ? src[g] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (sp0 + u < nsplit) {
-            acc[j].x += v[u][j].x;
-            acc[j].y += v[u][j].y;
-            acc[j].z += v[u][j].z;
-            acc[j].w += v[u][j].w;
-          }
+  const int G = M * (kBN / 4);
+  auto g_lo = [&](int p) { return p * G / nsplit; };
+  if (tid == 0) {
+    const uint32_t tile_a = smem_u32(tile), recv_a = smem_u32(recv), bar_a = smem_u32(recvbar);
+    for (int p = 0; p < nsplit; ++p) {
+      if (p == rank) continue;
+      const int lo = g_lo(p), len = g_lo(p + 1) - lo;
+      uint32_t dst, bar;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(dst) : "r"(recv_a + (uint32_t)(rank * len * 16)),
+                   "r"(p));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(bar) : "r"(bar_a), "r"(p));
+      asm volatile(
+          "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+          "r"(tile_a + (uint32_t)(lo * 16)), "r"((uint32_t)(len * 16)), "r"(bar)
+          : "memory");
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int g = g0 + j * stride;
-      if (g >= ngroups) continue;
+    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+  }
+  const bool got = mbar_wait_bounded(recvbar, 0, kWait);
+  if (tid == 0 && !got) atomicAdd(&g_sk_wait_timeouts, 1u);
+  {
+    const int lo = g_lo(rank), len = g_lo(rank + 1) - lo;
+    const float4* t4 = reinterpret_cast<const float4*>(tile);
+    const float4* r4 = reinterpret_cast<const float4*>(recv);
+    for (int gi = tid; gi < len; gi += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < nsplit; ++sp) {
+        const float4 v = sp == rank ? t4[lo + gi] : r4[sp * len + gi];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int g = lo + gi;
       const int m = g / (kBN / 4), n = n0 + (g % (kBN / 4)) * 4;
       T* yrow = Y + (int64_t)m * ldy;
       if (vec_store && n < N) {  // n % 4 == 0, N % 4 == 0, 8-byte aligned rows
         uint2 pk;
-        pk.x = pack2<T>(acc[j].x, acc[j].y);
-        pk.y = pack2<T>(acc[j].z, acc[j].w);
+        pk.x = pack2<T>(acc.x, acc.y);
+        pk.y = pack2<T>(acc.z, acc.w);
         *reinterpret_cast<uint2*>(yrow + n) = pk;
       } else {
-        if (n < N) yrow[n] = from_f<T>(acc[j].x);
-        if (n + 1 < N) yrow[n + 1] = from_f<T>(acc[j].y);
-        if (n + 2 < N) yrow[n + 2] = from_f<T>(acc[j].z);
-        if (n + 3 < N) yrow[n + 3] = from_f<T>(acc[j].w);
+        if (n < N) yrow[n] = from_f<T>(acc.x);
+        if (n + 1 < N) yrow[n + 1] = from_f<T>(acc.y);
+        if (n + 2 < N) yrow[n + 2] = from_f<T>(acc.z);
+        if (n + 3 < N) yrow[n + 3] = from_f<T>(acc.w);
       }
     }
   }
-  cluster_sync_all();  // no CTA leaves while another still reads its tile
+  // this CTA's outgoing copies have finished reading its tile before it exits
+  if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
 }
 
 }  // namespace

@@ -494,8 +494,8 @@ class MotifChordModel(nn.Module):
 
 # ============================================================================ engine
 # Largest M routed to motif_b200_skinny_gemm.  0: every product runs on cuBLAS — the skinny
-# kernel is correct (tests) but measured slower than cuBLAS at the decode shapes (7.4-11.8 us
-# vs 3.4-10.9 us per product at M = 64), so the model does not use it.
+# kernel is correct (tests) but measured slower than cuBLAS at the decode shapes (5.7-11.9 us
+# vs 3.3-10.9 us per product at M = 64), so the model does not use it.
 SKINNY_MAX_M = 0
 
 
