@@ -1253,6 +1253,42 @@ __global__ void __launch_bounds__(128) chord_merge_kernel(const float* __restric
   const int t = (int)(bt % Tn), b = (int)(bt / Tn);
   const int64_t split_stride = (int64_t)B * H * Tn * (D + 2);
   const float* base = ws + (((int64_t)b * H + h) * Tn + t) * (D + 2);
+  if (nsplit <= 32) {
+    // Lane sp holds split sp's (m, l) and weight; the partial rows are then read eight splits
+    // at a time with all loads in flight, and summed in split order (the same arithmetic as
+    // the general loop below).
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < nsplit) {
+      ms = base[lane * split_stride + D];
+      ls = base[lane * split_stride + D + 1];
+    }
+    const float mx = warp_max(ms);
+    const float mb = mx == -INFINITY ? 0.f : mx;
+    const float w = lane < nsplit ? exp2f(ms - mb) : 0.f;
+    const float den = warp_sum(ls * w);
+    float acc[OD];
+#pragma unroll
+    for (int d = 0; d < OD; ++d) acc[d] = 0.f;
+    for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
+      float v[8][OD];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int d = 0; d < OD; ++d) v[u][d] = sp0 + u < nsplit ? base[(sp0 + u) * split_stride + lane * OD + d] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wu = __shfl_sync(0xffffffffu, w, (sp0 + u) & 31);
+        if (sp0 + u < nsplit)
+#pragma unroll
+          for (int d = 0; d < OD; ++d) acc[d] = fmaf(wu, v[u][d], acc[d]);
+      }
+    }
+    const float inv = 1.f / fmaxf(den, 1e-20f);
+    T* dst = out + ((int64_t)b * Tn + t) * os + (int64_t)h * D;
+#pragma unroll
+    for (int d = 0; d < OD; ++d) dst[lane * OD + d] = from_f<T>(acc[d] * inv);
+    return;
+  }
   float mmax = -INFINITY;
   for (int sp = lane; sp < nsplit; sp += 32) mmax = fmaxf(mmax, base[sp * split_stride + D]);
   mmax = warp_max(mmax);

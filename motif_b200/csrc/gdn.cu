@@ -180,6 +180,10 @@ __global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
   float Sr[HR];
 #pragma unroll
   for (int i = 0; i < HR; ++i) Sr[i] = S[i * DV];
+  // every other input of the step is requested now too, so the CTA waits for memory once
+  const T a_raw = row[2 * H * DK + H * DV + h], b_raw = row[2 * H * DK + H * DV + H + h];
+  const T alog_raw = A_log[h], dtb_raw = dt_bias[h];
+  const T gate_raw = gate[(int64_t)b * ps + h * DV + j], onw_raw = onw[j];
 
   // conv + SiLU of this thread's channel (gdn_attn.py:116-136)
   const int c = tid < DK ? h * DK + tid : tid < 2 * DK ? H * DK + h * DK + (tid - DK) : 2 * H * DK + h * DV + (tid - 2 * DK);
@@ -213,10 +217,8 @@ __global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
   } else {
     sv[tid - 2 * DK] = y;
   }
-  const float a = to_f(row[2 * H * DK + H * DV + h]);
-  const float bsc = to_f(row[2 * H * DK + H * DV + H + h]);
-  const float bt = sigmoidf_(bsc);
-  const float gg = -expf(to_f(A_log[h])) * softplusf_(a + to_f(dt_bias[h]));
+  const float bt = sigmoidf_(to_f(b_raw));
+  const float gg = -expf(to_f(alog_raw)) * softplusf_(to_f(a_raw) + to_f(dtb_raw));
   const float e = expf(gg);
   __syncthreads();
 
@@ -251,9 +253,8 @@ __global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
     for (int w = 0; w < DV / 32; ++w) ss += red[w];
     const float r = rsqrtf(ss / (float)DV + eps);
     float yo = to_f(from_f<T>(ov * r));
-    yo = to_f(from_f<T>(yo * to_f(onw[j])));
-    const float gt = to_f(gate[(int64_t)b * ps + h * DV + j]);
-    out[(int64_t)b * os + h * DV + j] = from_f<T>(yo * to_f(from_f<T>(siluf_(gt))));
+    yo = to_f(from_f<T>(yo * to_f(onw_raw)));
+    out[(int64_t)b * os + h * DV + j] = from_f<T>(yo * to_f(from_f<T>(siluf_(to_f(gate_raw)))));
   }
 }
 

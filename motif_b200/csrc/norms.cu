@@ -447,18 +447,42 @@ __global__ void gate_residual_kernel(const T* __restrict__ a, int64_t as, const 
   }
 }
 
-template <typename T>
+// VEC (16-bit rows, V and the row stride multiples of 8, 16-byte aligned): each thread reads
+// 8 logits per 16-byte load, four loads in flight, visiting its indices in increasing order
+// like the scalar loop, so the first maximum still wins.
+template <typename T, bool VEC>
 __global__ void argmax_kernel(const T* __restrict__ x, int64_t V, int64_t rs, int64_t* __restrict__ ids) {
   const int64_t row = blockIdx.x;
   const T* xr = x + row * rs;
   float best = -INFINITY;
   int64_t bi = 0x7fffffffffffffffLL;
-  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = to_f(xr[i]);
+  auto visit = [&](float v, int64_t i) {
     if (v > best || (v == best && i < bi) || (isnan(v) && !isnan(best))) {
       best = v;
       bi = i;
     }
+  };
+  if constexpr (VEC) {
+    const int64_t nv = V / 8;
+    for (int64_t g0 = threadIdx.x; g0 < nv; g0 += 4 * (int64_t)blockDim.x) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t g = g0 + u * (int64_t)blockDim.x;
+        if (g < nv) r[u] = *reinterpret_cast<const uint4*>(xr + g * 8);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t g = g0 + u * (int64_t)blockDim.x;
+        if (g < nv) {
+          const T* e8 = reinterpret_cast<const T*>(&r[u]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) visit(to_f(e8[e]), g * 8 + e);
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) visit(to_f(xr[i]), i);
   }
   __shared__ float sv[32];
   __shared__ int64_t si[32];
@@ -675,7 +699,10 @@ extern "C" int motif_b200_argmax(const void* logits, int64_t rows, int64_t V, in
   if (rows == 0) return MB_OK;
   return dispatch(dtype, [&](auto t) {
     using T = decltype(t);
-    argmax_kernel<T><<<(unsigned)rows, 1024, 0, (cudaStream_t)stream>>>((const T*)logits, V, rs, ids);
+    if (sizeof(T) == 2 && V % 8 == 0 && rs % 8 == 0 && vec16_ok(logits))
+      argmax_kernel<T, true><<<(unsigned)rows, 1024, 0, (cudaStream_t)stream>>>((const T*)logits, V, rs, ids);
+    else
+      argmax_kernel<T, false><<<(unsigned)rows, 1024, 0, (cudaStream_t)stream>>>((const T*)logits, V, rs, ids);
     return check_launch("argmax");
   });
 }

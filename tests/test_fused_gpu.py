@@ -287,6 +287,16 @@ def test_gate_residual_argmax_embed():
     xc = x.cuda()
     _lib.call('motif_b200_argmax', _lib.ptr(xc), 5, 32000, 32000, _lib.ptr(ids), _lib.MB_F32, st())
     assert torch.equal(ids.cpu(), x.argmax(-1))
+    # 16-bit rows take the vectorised path (V and stride multiples of 8) or the scalar one
+    for V, rs in ((32000, 32000), (32000, 32008), (1003, 1003), (40, 48)):
+        xb = torch.randn(7, rs, generator=g).to(torch.bfloat16)
+        xb[3, 5] = xb[3, V - 2] = xb[3, :V].max() + 1  # tie across a thread's groups
+        xb[4, 8] = xb[4, 16] = xb[4, :V].max() + 2
+        xb[:, V:] = 100  # past V: never read
+        xbc = xb.cuda()
+        idb = torch.empty(7, dtype=torch.int64, device='cuda')
+        _lib.call('motif_b200_argmax', _lib.ptr(xbc), 7, V, rs, _lib.ptr(idb), _lib.MB_BF16, st())
+        assert torch.equal(idb.cpu(), xb[:, :V].float().argmax(-1)), (V, rs)
     table = torch.randn(100, 48, generator=g)
     tok = torch.randint(0, 100, (70000,), generator=g)
     out = torch.empty(70000, 48, device='cuda')
