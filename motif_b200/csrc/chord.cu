@@ -1713,8 +1713,9 @@ __global__ void __launch_bounds__(256) chord_prep_vec_kernel(const T* __restrict
   {
     const int slot = s0 + grp;
     const bool act = slot < slots;  // lanes past the last slot still join the reductions
-    uint4 raw = make_uint4(0, 0, 0, 0);
+    uint4 raw = make_uint4(0, 0, 0, 0), wr = make_uint4(0, 0, 0, 0);
     if (act) raw = *reinterpret_cast<const uint4*>(src_row + (int64_t)slot * D + sub * 8);
+    if (slot < H + Hkv) wr = *reinterpret_cast<const uint4*>((slot < H ? qn_w : kn_w) + sub * 8);  // with the row
     const T* e = reinterpret_cast<const T*>(&raw);
     float x[8];
     float ss = 0.f;
@@ -1734,8 +1735,6 @@ __global__ void __launch_bounds__(256) chord_prep_vec_kernel(const T* __restrict
       return;
     }
     const float r = rsqrtf(ss / (float)D + eps);
-    const T* w = (slot < H ? qn_w : kn_w) + sub * 8;
-    const uint4 wr = *reinterpret_cast<const uint4*>(w);
     const T* we = reinterpret_cast<const T*>(&wr);
     uint4 outv;
     T* oe = reinterpret_cast<T*>(&outv);

@@ -299,18 +299,22 @@ __global__ void __launch_bounds__(32 * kMaxSrc) attn_res_norm_src_kernel(
   const bool mix = q != nullptr && n_src > 1;
   if (warp < n_src) {
     const T* xr = static_cast<const T*>(src.p[warp]) + row * srs;
-    uint4 raw[NV];
+    uint4 raw[NV], rq[NV], rw[NV];  // the row and (when mixing) q and w, all requested at once
 #pragma unroll
-    for (int v = 0; v < NV; ++v) raw[v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+    for (int v = 0; v < NV; ++v) {
+      raw[v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+      if (mix) {
+        rq[v] = *reinterpret_cast<const uint4*>(q + (v * 32 + lane) * 8);
+        rw[v] = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
+      }
+    }
     float ss = 0.f, dot = 0.f;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       xs[warp][v * 32 + lane] = raw[v];
       if (mix) {
-        uint4 rq = *reinterpret_cast<const uint4*>(q + (v * 32 + lane) * 8);
-        uint4 rw = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
-        const T* q8 = reinterpret_cast<const T*>(&rq);
-        const T* w8 = reinterpret_cast<const T*>(&rw);
+        const T* q8 = reinterpret_cast<const T*>(&rq[v]);
+        const T* w8 = reinterpret_cast<const T*>(&rw[v]);
         const T* e8 = reinterpret_cast<const T*>(&raw[v]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
