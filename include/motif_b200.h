@@ -338,6 +338,14 @@ MB_API int motif_b200_gate_residual(const void* a, int64_t a_stride, const void*
 MB_API int motif_b200_argmax(const void* logits, int64_t rows, int64_t V, int64_t row_stride,
                       int64_t* ids, int dtype, void* stream);
 
+/* End of a CUDA-graph decode step in one launch: tokens[*step_idx, :B] = ids[:B] (a
+ * [max_steps, B] int64 log; skipped when *step_idx is outside [0, max_steps)), then
+ * *step_idx += 1 and lens[0 .. nlens) += 1 (int32 cache lengths, nlens <= 64).  Replaces
+ * the token append and position advance of the reference's generation loop
+ * (motif/model/generate.py:138-171) inside the captured step. */
+MB_API int motif_b200_decode_advance(const int64_t* ids, int64_t B, int64_t* tokens, int64_t max_steps,
+                              int64_t* step_idx, int32_t* lens, int64_t nlens, void* stream);
+
 /* One sampled token per row (Sampler.__call__, motif/model/sampler.py:151-219, without the
  * grammar constraint, whose mask the caller applies to the logits first): repetition penalty
  * over the distinct ids of history[r, :hist_len] (negative ids ignored) -> temperature

@@ -48,6 +48,7 @@ SIGNATURES = {
                                    _F, _I, _P]),
     'motif_b200_chord_prep': (_I, [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64,
                                    _I64, _F, _I, _P]),
+    'motif_b200_decode_advance': (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P]),
     'motif_b200_chord_prep_swiglu': (_I, [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64,
                                           _I64, _F, _P, _I64, _P, _I64, _I64, _I, _P]),
     'motif_b200_gdn_decode_swiglu': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,

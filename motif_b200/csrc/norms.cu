@@ -522,6 +522,23 @@ __global__ void argmax_kernel(const T* __restrict__ x, int64_t V, int64_t rs, in
   }
 }
 
+// End-of-step bookkeeping of the CUDA-graph decoder in one launch: the step's ids into row
+// step_idx of the token log, then step_idx and the cache lengths advance by one.  One CTA:
+// every thread reads step_idx before thread 0 advances it.
+__global__ void __launch_bounds__(256) decode_advance_kernel(const int64_t* __restrict__ ids, int64_t B,
+                                                             int64_t* __restrict__ tokens, int64_t max_steps,
+                                                             int64_t* __restrict__ step_idx,
+                                                             int32_t* __restrict__ lens, int nlens) {
+  const int64_t s = *step_idx;
+  if (s >= 0 && s < max_steps)
+    for (int64_t b = threadIdx.x; b < B; b += blockDim.x) tokens[s * B + b] = ids[b];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *step_idx = s + 1;
+    for (int i = 0; i < nlens; ++i) lens[i] += 1;
+  }
+}
+
 template <typename T>
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const T* __restrict__ table,
                              T* __restrict__ out, int64_t rows, int D, int64_t V) {
@@ -722,4 +739,12 @@ extern "C" int motif_b200_embed(const int64_t* ids, const void* table, void* out
     embed_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>(ids, (const T*)table, (T*)out, rows, (int)D, V);
     return check_launch("embed");
   });
+}
+
+extern "C" int motif_b200_decode_advance(const int64_t* ids, int64_t B, int64_t* tokens, int64_t max_steps,
+                                         int64_t* step_idx, int32_t* lens, int64_t nlens, void* stream) {
+  MB_REQUIRE(ids && tokens && step_idx && (lens || nlens == 0), MB_ERR_ARG, "decode_advance: null pointer");
+  MB_REQUIRE(B >= 0 && max_steps >= 0 && nlens >= 0 && nlens <= 64, MB_ERR_SHAPE, "decode_advance: bad shape");
+  decode_advance_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(ids, B, tokens, max_steps, step_idx, lens, (int)nlens);
+  return check_launch("decode_advance");
 }

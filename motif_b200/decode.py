@@ -214,9 +214,9 @@ class GraphDecoder:
             self.ids.copy_(torch.where(self.finished, self.fill, self.ids))
             self.finished.logical_or_(torch.isin(self.ids, self.eos))
             self.all_done.index_copy_(0, self.step_idx, self.finished.all().view(1))
-        self.tokens.index_copy_(0, self.step_idx, self.ids.view(1, B))
-        self.step_idx.add_(1)
-        self.lens.add_(1)
+        # token log, step counter and cache lengths in one launch
+        _lib.call('motif_b200_decode_advance', _lib.ptr(self.ids), B, _lib.ptr(self.tokens), self.max_steps,
+                  _lib.ptr(self.step_idx), _lib.ptr(self.lens), self.lens.numel(), st)
 
     def _gdn(self, pk, proj, slot: _GDNSlot, dc, st):
         B, dt, dev = self.B, self.dt, self.dev

@@ -273,6 +273,27 @@ def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, monkeypatch):
     assert _lib.wait_timeouts() == 0
 
 
+def test_decode_advance_matches_torch_ops():
+    """One launch = tokens.index_copy_(0, step_idx, ids) + step_idx += 1 + lens += 1, over
+    several steps, and no log write once step_idx is past the log."""
+    B, steps = 70, 3
+    ids = torch.randint(0, 32000, (B,), device='cuda')
+    tokens = torch.zeros(steps, B, dtype=torch.int64, device='cuda')
+    step_idx = torch.zeros(1, dtype=torch.int64, device='cuda')
+    lens = torch.tensor([8192, 8193], dtype=torch.int32, device='cuda')
+    ref_tokens = tokens.clone()
+    for s in range(steps + 1):
+        _lib.call('motif_b200_decode_advance', _lib.ptr(ids), B, _lib.ptr(tokens), steps, _lib.ptr(step_idx),
+                  _lib.ptr(lens), 2, st())
+        if s < steps:
+            ref_tokens[s] = ids
+        ids = ids + 1
+    torch.cuda.synchronize()
+    assert torch.equal(tokens, ref_tokens)
+    assert step_idx.item() == steps + 1
+    assert lens.tolist() == [8192 + steps + 1, 8193 + steps + 1]
+
+
 def test_gate_residual_argmax_embed():
     g = torch.Generator().manual_seed(0)
     a, gt, m = (torch.randn(70000, 24, generator=g) for _ in range(3))
