@@ -746,14 +746,20 @@ __global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, i
       for (int o2 = 1; o2 < LPR; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
       if (!ok[u]) continue;
       const float r = rsqrtf(ss / (float)DV + eps);
-      uint4 res;
-      T* re = reinterpret_cast<T*>(&res);
+      // two elements per packed fp32 op / bf16x2 conversion (the same roundings as one at a time)
+      uint32_t res[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float y = to_f(from_f<T>(to_f(from_f<T>(x[i] * r)) * wf[i]));
-        re[i] = from_f<T>(y * to_f(from_f<T>(siluf_(to_f(ge[i])))));
+      for (int i = 0; i < 8; i += 2) {
+        const float2 xn = fmul2(make_float2(x[i], x[i + 1]), make_float2(r, r));
+        const float2 xr = round2<T>(xn.x, xn.y);
+        const float2 yw = fmul2(xr, make_float2(wf[i], wf[i + 1]));
+        const float2 y = round2<T>(yw.x, yw.y);
+        const float2 sg = silu2_(make_float2(to_f(ge[i]), to_f(ge[i + 1])));
+        const float2 sgr = round2<T>(sg.x, sg.y);
+        const float2 o2 = fmul2(y, sgr);
+        res[i / 2] = pack2<T>(o2.x, o2.y);
       }
-      *op[u] = res;
+      *op[u] = make_uint4(res[0], res[1], res[2], res[3]);
     }
   }
 }
