@@ -538,9 +538,9 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     const float corr = ex2_approx((m - mb) * rcs);
     const float nb = -mb * rcs;
     m = mn;
-    float ps4[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 ps4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     // P row -> shared memory, swizzled: key chunk cc (8 keys) in atom cc / 8 at 16-byte slot
-    // (cc % 8) ^ (row % 8)
+    // (cc % 8) ^ (row % 8); the row sum accumulates in eight packed lanes
 #pragma unroll
     for (int cc = 0; cc < tc::kKeys / 8; ++cc) {
       uint32_t w[4];
@@ -550,13 +550,16 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
                                make_float2(nb, nb));
         const float p0 = ex2_approx(t.x);
         const float p1 = ex2_approx(t.y);
-        ps4[e] += p0 + p1;
+        ps4[e] = fadd2(ps4[e], make_float2(p0, p1));
         w[e] = pack2<T>(p0, p1);
       }
       unsigned char* dst = sPw + (cc >> 3) * tc::kTileBytes + wt * 128 + (((cc & 7) ^ (wt & 7)) << 4);
       *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    l = l * corr + ((ps4[0] + ps4[1]) + (ps4[2] + ps4[3]));
+    {
+      const float2 q = fadd2(fadd2(ps4[0], ps4[1]), fadd2(ps4[2], ps4[3]));
+      l = l * corr + (q.x + q.y);
+    }
     fence_proxy_async_smem();
     tc_fence_before();
     if (wg_sync_or(1 + wg, !ok || failed)) {
