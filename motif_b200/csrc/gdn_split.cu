@@ -213,6 +213,15 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       }
     }
     const float qscale = rsqrtf((float)DK);
+    // Sliding window of the converted inputs: xw[p][tap] holds channel pair p of row r + tap,
+    // so each raw element is converted to fp32 once, not once per tap.
+    float2 xw[4][4];
+#pragma unroll
+    for (int tap = 0; tap < 3; ++tap)
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+        xw[p][tap + 1] = make_float2(to_f(reinterpret_cast<const T*>(&raw[tap])[2 * p]),
+                                     to_f(reinterpret_cast<const T*>(&raw[tap])[2 * p + 1]));
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       const int row = run * 8 + r;
@@ -221,11 +230,13 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; i += 2) {  // channel pairs: packed fp32 math and roundings
-        float2 xv[4];
-#pragma unroll
-        for (int tap = 0; tap < 4; ++tap)
-          xv[tap] = make_float2(to_f(reinterpret_cast<const T*>(&raw[r + tap])[i]),
-                                to_f(reinterpret_cast<const T*>(&raw[r + tap])[i + 1]));
+        const int p = i / 2;
+        xw[p][0] = xw[p][1];
+        xw[p][1] = xw[p][2];
+        xw[p][2] = xw[p][3];
+        xw[p][3] = make_float2(to_f(reinterpret_cast<const T*>(&raw[r + 3])[i]),
+                               to_f(reinterpret_cast<const T*>(&raw[r + 3])[i + 1]));
+        const float2* xv = xw[p];
         // conv4f's order: ((w0 x0 + w1 x1) + w2 x2) + w3 x3 as one multiply and three fmas
         float2 a = fmul2(make_float2(w[i][0], w[i + 1][0]), xv[0]);
         a = ffma2(make_float2(w[i][1], w[i + 1][1]), xv[1], a);
