@@ -1114,6 +1114,30 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
     }
     // logits in log2 units with the GGD bias, masking, online softmax
     float rmax[2] = {-INFINITY, -INFINITY};
+    if constexpr (RH == 1) {
+      // one query row per thread: its two adjacent keys per n8 tile as packed fp32 pairs
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int kl = warp * 16 + nt * 8 + 2 * t4;
+        const int j = j0 + kl;
+        const float2 d = make_float2((float)(rqa[0] - j), (float)(rqa[0] - j - 1));
+        float2 t = fadd2(d, make_float2(rmu[0], rmu[0]));  // |-delta - mu| + eps
+        t = fadd2(make_float2(fabsf(t.x), fabsf(t.y)), make_float2(eps, eps));
+        const float2 pw = fmul2(make_float2(__log2f(t.x), __log2f(t.y)), make_float2(rbe[0], rbe[0]));
+        const float2 bias = fmul2(make_float2(ex2f_(pw.x), ex2f_(pw.y)), make_float2(-ral[0], -ral[0]));
+        float2 xx = fmul2(ffma2(make_float2(sacc[nt][0], sacc[nt][1]), make_float2(scale, scale), bias),
+                          make_float2(rrc[0], rrc[0]));
+        if (kmask) {  // key bias (mask)
+          if (kl < nk) xx.x = fmaf(kmask[(int64_t)b * kms + j], kLog2e, xx.x);
+          if (kl + 1 < nk) xx.y = fmaf(kmask[(int64_t)b * kms + j + 1], kLog2e, xx.y);
+        }
+        const float x0 = rv[0] && kl < nk && j <= rqa[0] ? xx.x : -INFINITY;
+        const float x1 = rv[0] && kl + 1 < nk && j + 1 <= rqa[0] ? xx.y : -INFINITY;
+        sacc[nt][0] = x0;
+        sacc[nt][1] = x1;
+        rmax[0] = fmax3(rmax[0], x0, x1);
+      }
+    } else {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
@@ -1131,6 +1155,7 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
         rmax[ri] = fmaxf(rmax[ri], x);
       }
     }
+    }
     float mb[2] = {0.f, 0.f};
 #pragma unroll
     for (int ri = 0; ri < RH; ++ri) {
@@ -1143,14 +1168,23 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
       l[ri] *= corr;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        o[i][2 * ri] *= corr;
-        o[i][2 * ri + 1] *= corr;
+        const float2 oc = fmul2(make_float2(o[i][2 * ri], o[i][2 * ri + 1]), make_float2(corr, corr));
+        o[i][2 * ri] = oc.x;
+        o[i][2 * ri + 1] = oc.y;
       }
     }
     uint32_t pa[4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      const float p0 = exp2f(sacc[nt][0] - mb[0]), p1 = exp2f(sacc[nt][1] - mb[0]);
+      float p0, p1;
+      if constexpr (RH == 1) {
+        const float2 a = fadd2(make_float2(sacc[nt][0], sacc[nt][1]), make_float2(-mb[0], -mb[0]));
+        p0 = ex2f_(a.x);
+        p1 = ex2f_(a.y);
+      } else {
+        p0 = exp2f(sacc[nt][0] - mb[0]);
+        p1 = exp2f(sacc[nt][1] - mb[0]);
+      }
       l[0] += p0 + p1;
       pa[2 * nt] = pack2<T>(p0, p1);
       if constexpr (RH == 2) {
