@@ -1099,17 +1099,19 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
     float sacc[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-    const uint32_t* Kw = reinterpret_cast<const uint32_t*>(sK + s * TILE_BYTES);
+    // B fragments by ldmatrix: lane l addresses key row 8 nt + (l & 7) of this warp's slice at
+    // 16-byte chunk 4 kp + (l >> 3) (swizzled), so matrix i of the x4 load is chunk 4 kp + i
+    // and registers {0, 1} / {2, 3} are the fragments of k-steps 2 kp / 2 kp + 1
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      const int kr = warp * 16 + nt * 8 + g8;
-      const uint32_t* krow = Kw + kr * 32;
+      const int kr = warp * 16 + nt * 8 + (lane & 7);
+      const unsigned char* krow = sK + s * TILE_BYTES + kr * 128;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t bb[2];
-        bb[0] = krow[(((2 * kk) ^ (kr & 7)) << 2) + t4];
-        bb[1] = krow[(((2 * kk + 1) ^ (kr & 7)) << 2) + t4];
-        mma_16816<T>(sacc[nt], qf[kk], bb);
+      for (int kp = 0; kp < 2; ++kp) {
+        uint32_t bb[4];
+        ldmatrix_x4(bb, krow + (((4 * kp + (lane >> 3)) ^ (kr & 7)) << 4));
+        mma_16816<T>(sacc[nt], qf[2 * kp], &bb[0]);
+        mma_16816<T>(sacc[nt], qf[2 * kp + 1], &bb[2]);
       }
     }
     // logits in log2 units with the GGD bias, masking, online softmax
