@@ -29,6 +29,8 @@
 #include "gdn_mma.cuh"
 
 namespace mb {
+// Two adjacent fp32 values from shared memory (8-byte aligned).
+__device__ __forceinline__ float2 ld2f(const float* p) { return *reinterpret_cast<const float2*>(p); }
 namespace {
 using namespace gdnk;
 
@@ -227,7 +229,7 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       const int row = run * 8 + r;
       const bool ok = t0 + r < L;
       float y[8];
-      float ss = 0.f;
+      float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < 8; i += 2) {  // channel pairs: packed fp32 math and roundings
         const int p = i / 2;
@@ -246,17 +248,19 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
         const float2 yy = round2<T>(sv.x, sv.y);
         y[i] = yy.x;
         y[i + 1] = yy.y;
-        ss += yy.x * yy.x;
-        ss += yy.y * yy.y;
+        ss2 = ffma2(yy, yy, ss2);
       }
+      float ss = ss2.x + ss2.y;
 #pragma unroll
       for (int o2 = 1; o2 < 8; o2 <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
       const float sc = (kind == 2 ? 1.f : l2_scale(ss, kind == 0 ? qscale : 1.f)) * (ok ? 1.f : 0.f);
-      uint4 pk;
-      pk.x = pack2<T>(y[0] * sc, y[1] * sc);
-      pk.y = pack2<T>(y[2] * sc, y[3] * sc);
-      pk.z = pack2<T>(y[4] * sc, y[5] * sc);
-      pk.w = pack2<T>(y[6] * sc, y[7] * sc);
+      uint32_t pkw[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const float2 ys = fmul2(make_float2(y[i], y[i + 1]), make_float2(sc, sc));
+        pkw[i / 2] = pack2<T>(ys.x, ys.y);
+      }
+      const uint4 pk = make_uint4(pkw[0], pkw[1], pkw[2], pkw[3]);
       T* dst = kind == 0 ? cQ + row * QS + cl : (kind == 1 ? cK + row * QS + (cl - DK) : cV + row * VS + (cl - 2 * DK));
       *reinterpret_cast<uint4*>(dst) = pk;
     }
@@ -315,12 +319,22 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       float* ad = sAd + warp * 16 * 17;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
+        // -beta_i k_i.k_j e^(gamma_i - gamma_j) below the diagonal, in packed fp32 pairs
+        // (e^x as 2^(x log2 e) on the MUFU)
         const int j = nt * 8 + 2 * tq;
-        const float gj0 = sGam[j], gj1 = sGam[j + 1];
-        const float a00 = j < i0 ? b0 * acc[nt][0] * __expf(gi0 - gj0) : 0.f;
-        const float a01 = j + 1 < i0 ? b0 * acc[nt][1] * __expf(gi0 - gj1) : 0.f;
-        const float a10 = j < i1 ? b1 * acc[nt][2] * __expf(gi1 - gj0) : 0.f;
-        const float a11 = j + 1 < i1 ? b1 * acc[nt][3] * __expf(gi1 - gj1) : 0.f;
+        const float2 gj = ld2f(&sGam[j]);
+        const float2 e0 = fmul2(fadd2(make_float2(gi0, gi0), make_float2(-gj.x, -gj.y)),
+                                make_float2(-kNegLog2e, -kNegLog2e));
+        const float2 e1 = fmul2(fadd2(make_float2(gi1, gi1), make_float2(-gj.x, -gj.y)),
+                                make_float2(-kNegLog2e, -kNegLog2e));
+        const float2 v0 = fmul2(fmul2(make_float2(b0, b0), make_float2(acc[nt][0], acc[nt][1])),
+                                make_float2(ex2f_(e0.x), ex2f_(e0.y)));
+        const float2 v1 = fmul2(fmul2(make_float2(b1, b1), make_float2(acc[nt][2], acc[nt][3])),
+                                make_float2(ex2f_(e1.x), ex2f_(e1.y)));
+        const float a00 = j < i0 ? v0.x : 0.f;
+        const float a01 = j + 1 < i0 ? v0.y : 0.f;
+        const float a10 = j < i1 ? v1.x : 0.f;
+        const float a11 = j + 1 < i1 ? v1.y : 0.f;
         st2(&sA[i0 * AS + j], a00, a01);
         st2(&sA[i1 * AS + j], a10, a11);
         if ((nt >> 1) == warp) {  // this warp's diagonal block, kept in fp32
@@ -348,13 +362,17 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
       }
     } else {
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < 8; ++nt) {  // q_i.k_j e^(gamma_i - gamma_j) on and below the diagonal
         const int j = nt * 8 + 2 * tq;
-        const float gj0 = sGam[j], gj1 = sGam[j + 1];
-        st2(&sAq[i0 * AS + j], j <= i0 ? acc[nt][0] * __expf(gi0 - gj0) : 0.f,
-            j + 1 <= i0 ? acc[nt][1] * __expf(gi0 - gj1) : 0.f);
-        st2(&sAq[i1 * AS + j], j <= i1 ? acc[nt][2] * __expf(gi1 - gj0) : 0.f,
-            j + 1 <= i1 ? acc[nt][3] * __expf(gi1 - gj1) : 0.f);
+        const float2 gj = ld2f(&sGam[j]);
+        const float2 e0 = fmul2(fadd2(make_float2(gi0, gi0), make_float2(-gj.x, -gj.y)),
+                                make_float2(-kNegLog2e, -kNegLog2e));
+        const float2 e1 = fmul2(fadd2(make_float2(gi1, gi1), make_float2(-gj.x, -gj.y)),
+                                make_float2(-kNegLog2e, -kNegLog2e));
+        const float2 v0 = fmul2(make_float2(acc[nt][0], acc[nt][1]), make_float2(ex2f_(e0.x), ex2f_(e0.y)));
+        const float2 v1 = fmul2(make_float2(acc[nt][2], acc[nt][3]), make_float2(ex2f_(e1.x), ex2f_(e1.y)));
+        st2(&sAq[i0 * AS + j], j <= i0 ? v0.x : 0.f, j + 1 <= i0 ? v0.y : 0.f);
+        st2(&sAq[i1 * AS + j], j <= i1 ? v1.x : 0.f, j + 1 <= i1 ? v1.y : 0.f);
       }
     }
   }
