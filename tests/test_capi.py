@@ -24,6 +24,26 @@ def test_header_and_binding_agree():
     assert declared() == sorted(_lib.SIGNATURES), set(declared()) ^ set(_lib.SIGNATURES)
 
 
+def declared_arity():
+    """{entry point: parameter count} from the header's MB_API declarations."""
+    src = open(os.path.join(ROOT, 'include', 'motif_b200.h')).read()
+    src = re.sub(r'/\*.*?\*/', ' ', src, flags=re.S)
+    out = {}
+    for name, params in re.findall(r'MB_API[^;(]*?\b(motif_b200_[a-z0-9_]+)\s*\(([^;]*?)\)\s*;', src, flags=re.S):
+        params = params.strip()
+        out[name] = 0 if params in ('', 'void') else params.count(',') + 1
+    return out
+
+
+def test_binding_parameter_counts_match_header():
+    """Every ctypes signature has as many parameters as the C declaration (an argument added
+    on one side only would shift every later argument of the call)."""
+    arity = declared_arity()
+    assert sorted(arity) == declared()
+    bad = {n: (arity[n], len(_lib.SIGNATURES[n][1])) for n in arity if arity[n] != len(_lib.SIGNATURES[n][1])}
+    assert not bad, bad
+
+
 def test_library_exports_every_symbol():
     lib = ctypes.CDLL(_lib.LIB_PATH)
     for name in declared():
