@@ -43,7 +43,7 @@ __device__ __forceinline__ float ggd_bias(float alpha, float beta, float mu, flo
 template <typename T>
 __device__ __forceinline__ float ggd_bias_decode(float alpha, float beta, float mu, float delta, float eps) {
   if constexpr (sizeof(T) == 2) {
-    return -alpha * exp2f(beta * __log2f(fabsf(-delta - mu) + eps));
+    return -alpha * ex2f_(beta * __log2f(fabsf(-delta - mu) + eps));
   } else {
     return ggd_bias(alpha, beta, mu, delta, eps);
   }
