@@ -3,18 +3,24 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
-One step = one `MotifChordModel.forward` over this rank's 32 x 4096-token batch (weak
-scaling: N ranks process 32·N independent sequences, no collective on the hot path), logits
-over all positions included.  `--global-batch G` instead splits G sequences across the
-ranks (strong scaling).  Prints ONE JSON line on rank 0.
+One step = one `MotifChordModel.forward` over this rank's share of config 4's batch: the 32 x
+4096-token batch is split by sequence across the N ranks (32/N each; strong scaling, no
+collective on the hot path), logits over all positions included.  `--weak` instead gives every
+rank 32 sequences.  Config 5's decode splits its 64 requests the same way.  Prints ONE JSON
+line on rank 0.
 
 * `value`      — whole-job prefill tokens/s, inputs resident in HBM, device time (CUDA
                  events on the launching stream), max over ranks.
 * `e2e`        — the same metric through the public API with host buffers: pinned int64
                  ids -> device, forward, greedy next token -> host, every step.
 * `roofline`   — the dominant kernel of this library (by time), its algorithmic work per
-                 launch over its CUDA-event duration inside the timed region.
+                 launch over its CUDA-event duration inside the timed region (tensor fraction
+                 against the sustained bf16 peak: the kernel runs inside a long step).
 * `kernels`    — per-kernel breakdown of one instrumented step (CUDA events per call).
+* `ops`        — configs 2 and 3 (the GDN and Chord ops alone), each with its roofline.
+* `decode`     — config 5 (64 requests at context 8192, greedy CUDA-graph steps).
+* `reference_gpu` — the reference's own GPU path (its Triton kernels, from `baseline/_ref`)
+                 timed on the same box, configs 2-4, when that package is present.
 * `cpu_baseline` — the CPU oracle (the reference's torch algorithm restated) timed on this
                  box's host cores on a bounded sample (B=1 x T=4096), rank 0 at N=1.
 * `--impl reference` times that CPU implementation alone on the same metric.
@@ -33,7 +39,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-GLOBAL_BATCH = 32   # sequences per rank
+GLOBAL_BATCH = 32   # config 4: sequences per step, split across the ranks
 SEQ_LEN = 4096
 METRIC = 'prefill_tokens_per_s'
 UNIT = 'tokens/s'
@@ -257,8 +263,8 @@ def run_ours(args, world, rank, local):
     torch.cuda.set_device(dev)
     cfg = config_172m()
     from motif_b200 import runner
-    weak = args.global_batch is None
-    gb = GLOBAL_BATCH * world if weak else args.global_batch
+    weak = args.weak
+    gb = args.global_batch * world if weak else args.global_batch
     lo, hi = runner.shard_range(gb, world, rank)
     B = hi - lo
     if B == 0:
@@ -355,8 +361,10 @@ def run_ours(args, world, rank, local):
         kernels['cublas_gemm']['tflops'] = round(gf / (summ['cublas_gemm'][1] / 1000.0) / 1e12, 1)
     flops, byts = kernel_work(dominant, cfg, B, T)
     avg_s = dom[1] / max(dom[0], 1) / 1000.0
-    if flops and flops / max(byts, 1) > pk['bf16_tflops'] * 1e12 / (pk['hbm_gbs'] * 1e9):
-        roof = {'bound': 'tensor', 'achieved': flops / avg_s / 1e12, 'peak': pk['bf16_tflops'], 'unit': 'TFLOP/s'}
+    # the kernel runs inside a long step under the power cap: the sustained bf16 peak applies
+    tpk = pk['bf16_tflops_sustained']
+    if flops and flops / max(byts, 1) > tpk * 1e12 / (pk['hbm_gbs'] * 1e9):
+        roof = {'bound': 'tensor', 'achieved': flops / avg_s / 1e12, 'peak': tpk, 'unit': 'TFLOP/s'}
     else:
         roof = {'bound': 'hbm', 'achieved': byts / avg_s / 1e9, 'peak': pk['hbm_gbs'], 'unit': 'GB/s'}
     roof['frac'] = roof['achieved'] / roof['peak']
@@ -364,12 +372,14 @@ def run_ours(args, world, rank, local):
     roof['kernel'] = dominant
     roof['launches_timed'] = dom[0]
     roof['avg_launch_ms'] = avg_s * 1000.0
+    roof['algorithmic_bytes'] = byts
     if flops:
+        roof['algorithmic_flops'] = flops
         roof['tflops'] = flops / avg_s / 1e12
-        roof['tensor_frac_of_measured_bf16'] = roof['tflops'] / pk['bf16_tflops']
+        roof['tensor_frac_of_measured_sustained_bf16'] = roof['tflops'] / tpk
     roof['gbs'] = byts / avg_s / 1e9
     roof['hbm_frac_of_measured'] = roof['gbs'] / pk['hbm_gbs']
-    roof['peak_source'] = pk['source']
+    roof['peak_source'] = pk['source'] + (' (sustained bf16 peak)' if roof['bound'] == 'tensor' else ' (copy peak)')
 
     result = {
         'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
@@ -378,7 +388,7 @@ def run_ours(args, world, rank, local):
         'dtype': 'bf16', 'data': 'synthetic',
         'config': {'workload': '172M-class MotifChord prefill, logits over all positions (config 4)',
                    'global_batch': gb, 'seq_len': T, 'per_rank_batch': B,
-                   'parallelism': f'sequence-sharded replicas x{world}, no hot-path collective',
+                   'parallelism': f'sequence-sharded replicas x{world} ({"weak: " + str(B) + " per rank" if weak else "strong: the batch split " + str(gb) + "/" + str(world)}), no hot-path collective',
                    'l2': 'inputs larger than L2 (every activation >= 200 MB at B=32)'},
         'e2e': {'value': tokens / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': ids_host.numel() * 8,
                 'd2h_bytes_per_step': int(tok.numel() * 8)},
@@ -390,6 +400,10 @@ def run_ours(args, world, rank, local):
     }
     if args.decode_steps > 0:
         result['decode'] = run_decode(model, cfg, args, world, rank, local, dev, stream, pk)
+    if not args.no_ops:
+        result['ops'] = run_ops(dev, pk, args)
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        result['reference_gpu'] = run_reference_gpu(dev, args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, threads, dt = cpu_oracle_rate(seq_len=args.ref_seq_len)
         result['cpu_baseline'] = {'value': rate, 'unit': UNIT, 'cores': threads, 'kind': 'port',
@@ -399,8 +413,149 @@ def run_ours(args, world, rank, local):
         print(json.dumps(result), flush=True)
 
 
+# ---------------------------------------------------------------- ops (configs 2 and 3)
+def _time_ms(fn, warm=3, iters=10):
+    """Mean device time of fn() over `iters` calls after `warm` calls (CUDA events on the current
+    stream, synchronised on both sides)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def op_inputs(dev, which, dtype=torch.bfloat16):
+    """Seeded synthetic inputs of config 2 ('gdn') or config 3 ('chord'), on `dev`."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(0)
+    B, H, T, D = 8, 12, 4096, 64
+    if which == 'gdn':
+        q = F.normalize(torch.randn(B, H, T, D, generator=g), dim=-1)
+        k = F.normalize(torch.randn(B, H, T, D, generator=g), dim=-1)
+        v = torch.randn(B, H, T, D, generator=g)
+        beta = torch.sigmoid(torch.randn(B, H, T, generator=g))
+        gg = -F.softplus(torch.randn(B, H, T, generator=g)) * 0.1
+        return [t.to(dev, dtype) for t in (q, k, v)] + [beta.to(dev), gg.to(dev)]
+    q, k, v = (torch.randn(B, H, T, D, generator=g).to(dev, dtype) for _ in range(3))
+    alpha = (0.5 + 1.5 * torch.rand(H, generator=g)).to(dev)
+    beta = torch.rand(H, generator=g).to(dev)
+    mu = torch.ones(H, device=dev)
+    ssmax = torch.ones(H, device=dev)
+    log_n = torch.log(torch.arange(1, T + 1, dtype=torch.float32)).view(1, T).expand(B, T).contiguous().to(dev)
+    return [q, k, v, alpha, beta, mu, ssmax, log_n]
+
+
+OP_WORK = {
+    # config 2: per token-head flops of the chunked delta rule (C = dk = dv = 64); bytes = q, k, v,
+    # o bf16 + beta, g fp32 + the final state fp32
+    'gdn': (8 * 12 * 4096 * (3 * 2 * 64 * 64 + 2 * 2 * 64 * 64 + 3 * 2 * 64 * 64),
+            4 * 8 * 12 * 4096 * 64 * 2 + 2 * 8 * 12 * 4096 * 4 + 8 * 12 * 64 * 64 * 4),
+    # config 3: causal half of QK^T and PV; bytes = q, k, v, o bf16
+    'chord': (4 * 8 * 12 * 64 * 4096 * 4097 / 2, 4 * 8 * 12 * 4096 * 64 * 2),
+}
+
+
+def run_ops(dev, pk, args):
+    """Configs 2 and 3 through the public ops (`motif_b200.ops`), timed alone (burst peaks)."""
+    from motif_b200 import ops
+    out = {}
+    a = op_inputs(dev, 'gdn')
+    ms = _time_ms(lambda: ops.chunk_gated_delta_rule(*a))
+    f, b = OP_WORK['gdn']
+    out['gdn_op'] = {'config': 'B=8 H=12 T=4096 dk=dv=64 chunk 64, bf16 q/k/v, fp32 beta/g/state (config 2)',
+                     'ms': ms, 'tokens_per_s': 8 * 4096 / (ms / 1000.0),
+                     'roofline': {'bound': 'hbm', 'achieved': b / (ms / 1000.0) / 1e9, 'peak': pk['hbm_gbs'],
+                                  'unit': 'GB/s', 'frac': b / (ms / 1000.0) / 1e9 / pk['hbm_gbs'],
+                                  'algorithmic_bytes': b, 'algorithmic_flops': f,
+                                  'tflops': f / (ms / 1000.0) / 1e12,
+                                  'tensor_frac_of_measured_bf16': f / (ms / 1000.0) / 1e12 / pk['bf16_tflops']}}
+    del a
+    a = op_inputs(dev, 'chord')
+    ms = _time_ms(lambda: ops.apply_chord_attention(*a))
+    f, b = OP_WORK['chord']
+    out['chord_op'] = {'config': 'B=8 H=12 (kv 12) T=4096 D=64 bf16, GGD bias in-kernel (config 3)',
+                       'ms': ms, 'tokens_per_s': 8 * 4096 / (ms / 1000.0),
+                       'roofline': {'bound': 'tensor', 'achieved': f / (ms / 1000.0) / 1e12,
+                                    'peak': pk['bf16_tflops'], 'unit': 'TFLOP/s',
+                                    'frac': f / (ms / 1000.0) / 1e12 / pk['bf16_tflops'],
+                                    'algorithmic_flops': f, 'algorithmic_bytes': b,
+                                    'gbs': b / (ms / 1000.0) / 1e9}}
+    del a
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------- the reference's GPU path
+REF_DIR = os.path.join(ROOT, 'baseline', '_ref')
+
+
+def run_reference_gpu(dev, args):
+    """The reference's own GPU path, unmodified, from the package installed in `baseline/_ref`
+    (its Triton kernels: `chunk_gated_delta_rule_triton`, `apply_chord_attention`, and
+    `MotifChordModel.forward`, which dispatches to them on CUDA), on configs 2, 3 and 4.  The
+    reference's GDN layer runs its delta rule in fp32 (`gdn_attn.py:197`), so config 2 is timed
+    on fp32 inputs there; config 4 runs at B = 4 x 4096 (its per-token rate)."""
+    if not os.path.isdir(os.path.join(REF_DIR, 'motif')):
+        return {'unavailable': 'baseline/_ref is not installed'}
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    res = {'source': 'baseline/_ref (reference package, Triton GPU path)'}
+    try:
+        from motif.ops.chord_attention import apply_chord_attention as ref_chord
+        from motif.ops.gated_deltanet import chunk_gated_delta_rule_triton as ref_gdn
+    except Exception as e:  # noqa: BLE001 - reported, not raised
+        return {'unavailable': f'import failed: {type(e).__name__}: {e}'}
+    with torch.no_grad():
+        try:
+            a = op_inputs(dev, 'gdn', dtype=torch.float32)
+            ms = _time_ms(lambda: ref_gdn(*a), warm=2, iters=5)
+            res['gdn_op'] = {'ms': ms, 'tokens_per_s': 8 * 4096 / (ms / 1000.0), 'dtype': 'fp32'}
+            del a
+        except Exception as e:  # noqa: BLE001
+            res['gdn_op'] = {'unavailable': f'{type(e).__name__}: {e}'[:300]}
+        torch.cuda.empty_cache()
+        try:
+            a = op_inputs(dev, 'chord')
+            ms = _time_ms(lambda: ref_chord(*a), warm=2, iters=5)
+            res['chord_op'] = {'ms': ms, 'tokens_per_s': 8 * 4096 / (ms / 1000.0), 'dtype': 'bf16',
+                               'tflops': OP_WORK['chord'][0] / (ms / 1000.0) / 1e12}
+            del a
+        except Exception as e:  # noqa: BLE001
+            res['chord_op'] = {'unavailable': f'{type(e).__name__}: {e}'[:300]}
+        torch.cuda.empty_cache()
+        try:
+            from motif.model.config import MotifChordConfig as RefConfig
+            from motif.model.motif import MotifChordModel as RefModel
+            from motif_b200.config import config_172m
+            from motif_b200.init import init_params
+            c = config_172m()
+            rcfg = RefConfig(vocab_size=c.vocab_size, model_dim=c.model_dim, num_heads=c.num_heads,
+                             num_kv_heads=c.num_kv_heads, head_k_dim=c.head_k_dim, block=tuple(c.block),
+                             block_n=c.block_n)
+            torch.manual_seed(0)
+            rm = RefModel(rcfg)
+            init_params(rm, seed=0)
+            rm = rm.to(dev, torch.bfloat16).eval()
+            Bref = 4
+            ids = torch.randint(0, c.vocab_size, (Bref, SEQ_LEN), generator=torch.Generator().manual_seed(0)).to(dev)
+            ms = _time_ms(lambda: rm(ids), warm=2, iters=3)
+            res['prefill_172m'] = {'ms': ms, 'batch': Bref, 'seq_len': SEQ_LEN,
+                                   'tokens_per_s': Bref * SEQ_LEN / (ms / 1000.0), 'dtype': 'bf16'}
+            del rm, ids
+        except Exception as e:  # noqa: BLE001
+            res['prefill_172m'] = {'unavailable': f'{type(e).__name__}: {e}'[:300]}
+        torch.cuda.empty_cache()
+    return res
+
+
 # ---------------------------------------------------------------- decode (config 5)
-DECODE_BATCH = 64      # sequences per rank
+DECODE_BATCH = 64      # config 5: requests, split across the ranks
 DECODE_CONTEXT = 8192
 
 
@@ -428,6 +583,18 @@ def decode_step_bytes(model, B, S):
     return wb + kv + gdn + B * d * 2 + 2 * B * cfg.vocab_size * 2
 
 
+def _decode_kernels(brk, graph_ms):
+    """Per-kernel share of the decode step: eager event times averaged over 32 steps (which
+    include launch gaps the graph does not have), normalised so the shares sum to 1 and scaled to
+    the graph step's measured time."""
+    tot = sum(t for _, t in brk.values()) or 1.0
+    out = {'_note': 'eager steps (32, events per launch) scaled to the graph step: ms = share x graph ms/step'}
+    for k, (c, t) in sorted(brk.items(), key=lambda kv: -kv[1][1]):
+        out[k.replace('motif_b200_', '')] = {'calls_per_step': c, 'eager_ms': round(t, 4), 'share': round(t / tot, 4),
+                                             'ms': round(t / tot * graph_ms, 4)}
+    return out
+
+
 def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
     """Config 5: B=64 sequences per GPU at context 8192, then `--decode-steps` greedy steps,
     one CUDA-graph replay per step.  The caches are filled directly with seeded random
@@ -435,14 +602,18 @@ def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
     64 x 8192 tokens would leave them."""
     from motif_b200 import _lib
     from motif_b200.decode import GraphDecoder, fill_cache_random
-    B, L, n = args.decode_batch, DECODE_CONTEXT, args.decode_steps
+    from motif_b200 import runner
+    gbd = args.decode_batch * world if args.weak else args.decode_batch
+    lo, hi = runner.shard_range(gbd, world, rank)
+    B, L, n = hi - lo, DECODE_CONTEXT, args.decode_steps
     cache = fill_cache_random(model, model.create_cache(), B, L, L + 2 * n, seed=rank)
     dec = GraphDecoder(model, cache, max_steps=2 * n)
     g = torch.Generator().manual_seed(rank)
     first_host = torch.randint(0, cfg.vocab_size, (B, 1), generator=g).pin_memory()
     first = first_host.to(dev)
-    # per-kernel breakdown of one step, run eagerly with events (outside the timed region)
-    brk = dec.breakdown(first)
+    # per-kernel breakdown, 32 eager steps with events around every launch (outside the timed
+    # region); reported as shares of the graph step
+    brk = dec.breakdown(first, steps=32)
     # warm-up replays (also the first touch of every cache page), then the caches' lengths
     # are rewound so the timed steps start at context 8192
     dec.run(first, min(3, n))
@@ -471,14 +642,14 @@ def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
-    total_tok = B * n * world
+    total_tok = gbd * n
     byts = sum(decode_step_bytes(model, B, L + i) for i in range(n))
     gbs = byts / (ms / 1000.0) / 1e9
     out = {
         'metric': 'decode_tokens_per_s', 'value': total_tok / (ms / 1000.0), 'unit': 'tokens/s',
-        'higher_is_better': True, 'scaling': 'weak', 'steps': n, 'ms_per_step': ms / n,
+        'higher_is_better': True, 'scaling': 'weak' if args.weak else 'strong', 'steps': n, 'ms_per_step': ms / n,
         'config': {'workload': '172M-class greedy decode (config 5), one CUDA-graph replay per token',
-                   'per_rank_batch': B, 'global_batch': B * world, 'context': L,
+                   'per_rank_batch': B, 'global_batch': gbd, 'context': L,
                    'cache_fill': 'seeded random KV / GDN states at length 8192 (stands in for the prefill)',
                    'l2': 'working set per step > 2 GB, larger than L2'},
         'hbm': {'achieved_gbs_per_gpu': gbs, 'peak': pk['hbm_gbs'], 'frac': gbs / pk['hbm_gbs'],
@@ -486,8 +657,7 @@ def run_decode(model, cfg, args, world, rank, local, dev, stream, pk):
         'e2e': {'value': total_tok / (e2e_ms / 1000.0), 'unit': 'tokens/s',
                 'h2d_bytes_per_step': first_host.numel() * 8 / n, 'd2h_bytes_per_step': toks.numel() * 8 / n},
         'gpu_launches': dec.launches_per_step * n,
-        'kernels': {k.replace('motif_b200_', ''): {'calls': c, 'ms': round(t, 4)}
-                    for k, (c, t) in sorted(brk.items(), key=lambda kv: -kv[1][1])},
+        'kernels': _decode_kernels(brk, ms / n),
         'clocks': clk.summary(),
     }
     dec.release()
@@ -502,15 +672,20 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--seq-len', type=int, default=SEQ_LEN)
-    ap.add_argument('--global-batch', type=int, default=None,
-                    help='sequences per step over all ranks, split across them (strong scaling); the default is '
-                         f'{GLOBAL_BATCH} per rank (weak scaling); small values are for profiling captures')
+    ap.add_argument('--global-batch', type=int, default=GLOBAL_BATCH,
+                    help=f'config-4 sequences per step, split across the ranks (default {GLOBAL_BATCH}); small '
+                         'values are for profiling captures')
+    ap.add_argument('--weak', action='store_true',
+                    help='weak scaling: every rank runs --global-batch prefill sequences and --decode-batch requests')
+    ap.add_argument('--no-ops', action='store_true', help='skip the op-level lines (configs 2 and 3)')
+    ap.add_argument('--no-reference-gpu', action='store_true',
+                    help="skip timing the reference's own GPU (Triton) path from baseline/_ref")
     ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--mode', choices=['all', 'decode'], default='all',
                     help="'decode' runs only the config-5 decode measurement (for profiling)")
     ap.add_argument('--decode-batch', type=int, default=DECODE_BATCH,
-                    help=f'decode sequences per rank (the benchmark config is {DECODE_BATCH})')
+                    help=f'config-5 decode requests, split across the ranks (default {DECODE_BATCH})')
     ap.add_argument('--decode-steps', type=int, default=256,
                     help='greedy decode steps of the config-5 decode measurement (0 skips it)')
     args = ap.parse_args()

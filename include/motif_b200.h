@@ -362,6 +362,24 @@ MB_API int motif_b200_sample(const void* logits, int64_t ld, int64_t B, int64_t 
                       const int64_t* offset_dev, int64_t* out, float* probs_out, int64_t probs_ld,
                       int dtype, void* stream);
 
+/* Testing hook, no counterpart in the reference: forces one of the kernels that a shape or
+ * dtype also selects onto calls the default routing sends elsewhere, so tests can compare
+ * two kernels on the same inputs.  Every knob is off at load; the setting is process-wide
+ * and read at each launch.  Not for production use.
+ *   MB_FORCE_CHORD_MMA_SYNC  16-bit D = 64 Chord prefill on the mma.sync kernel (D = 16 / 32's)
+ *   MB_FORCE_DECODE_SCALAR   16-bit D = 64 Chord decode on the CUDA-core kernel (fp32's)
+ *   MB_FORCE_GDN_PRECISE     16-bit chunked delta rule on the 3xTF32 kernel (fp32's)
+ *   MB_FORCE_GDN_FUSED       16-bit chunked delta rule with a workspace on the single fused
+ *                            kernel (the no-workspace path) */
+enum {
+  MB_FORCE_CHORD_MMA_SYNC = 0,
+  MB_FORCE_DECODE_SCALAR = 1,
+  MB_FORCE_GDN_PRECISE = 2,
+  MB_FORCE_GDN_FUSED = 3,
+  MB_FORCE_COUNT = 4
+};
+MB_API int motif_b200_testing_force(int knob, int value);
+
 /* Token embedding gather: out[r] = table[ids[r]] ([V, D] rows), motif/model/motif.py:604. */
 MB_API int motif_b200_embed(const int64_t* ids, const void* table, void* out, int64_t rows, int64_t D,
                      int64_t V, int dtype, void* stream);

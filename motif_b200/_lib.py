@@ -17,6 +17,8 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'libmotif_b2
 
 MB_OK, MB_ERR_ARG, MB_ERR_SHAPE, MB_ERR_DTYPE, MB_ERR_ALIGN, MB_ERR_UNSUPPORTED, MB_ERR_CUDA = range(7)
 MB_F32, MB_F16, MB_BF16 = 0, 1, 2
+# testing knobs of motif_b200_testing_force (include/motif_b200.h)
+FORCE_CHORD_MMA_SYNC, FORCE_DECODE_SCALAR, FORCE_GDN_PRECISE, FORCE_GDN_FUSED = range(4)
 ABI_VERSION = 1
 
 _P = ctypes.c_void_p
@@ -68,6 +70,7 @@ SIGNATURES = {
     'motif_b200_sample': (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _F, _F, _I64, _F, _P, ctypes.c_uint64,
                                ctypes.c_uint64, _P, _P, _P, _I64, _I, _P]),
     'motif_b200_wait_timeouts': (_I, [_P]),
+    'motif_b200_testing_force': (_I, [_I, _I]),
     'motif_b200_skinny_gemm_workspace_bytes': (_I64, [_I64, _I64, _I64]),
     'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _I64, _P]),
     'motif_b200_gdn_prefill_ws': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64,
@@ -137,7 +140,7 @@ KERNELS_PER_CALL = {n: 1 for n in SIGNATURES}
 KERNELS_PER_CALL.update({'motif_b200_last_error': 0, 'motif_b200_abi_version': 0,
                          'motif_b200_chord_workspace_bytes': 0, 'motif_b200_chord_decode_workspace_bytes': 0,
                          'motif_b200_skinny_gemm_workspace_bytes': 0, 'motif_b200_gdn_chunk_workspace_bytes': 0,
-                         'motif_b200_wait_timeouts': 0,
+                         'motif_b200_wait_timeouts': 0, 'motif_b200_testing_force': 0,
                          'motif_b200_chord_decode': 2, 'motif_b200_chord_decode_noalloc': 2,
                          'motif_b200_chord_decode_masked': 2,
                          'motif_b200_gdn_chunk_gated_ws': 3, 'motif_b200_gdn_prefill_ws': 3})
@@ -208,3 +211,19 @@ def wait_timeouts() -> int:
     n = ctypes.c_uint32(0)
     call('motif_b200_wait_timeouts', ctypes.addressof(n))
     return int(n.value)
+
+
+class forced:
+    """Test-only context manager: switch a testing knob of the library on for the block
+    (`with _lib.forced(_lib.FORCE_DECODE_SCALAR): ...`), off again on exit."""
+
+    def __init__(self, knob: int):
+        self.knob = knob
+
+    def __enter__(self):
+        call('motif_b200_testing_force', self.knob, 1)
+        return self
+
+    def __exit__(self, *exc):
+        call('motif_b200_testing_force', self.knob, 0)
+        return False

@@ -24,6 +24,7 @@ import json
 import os
 import re
 from dataclasses import asdict, dataclass, field, fields
+from enum import Enum, auto
 from typing import Any, Dict, List, Optional, Tuple
 
 import torch
@@ -210,14 +211,34 @@ def _from_mapping(obj, path: str) -> LoadedCheckpoint:
     raise ValueError(f'cannot find model weights in {path!r}: the mapping has keys {sorted(obj)[:8]}.')
 
 
+class PipelinePhase(Enum):
+    """Stand-in for the training pipeline's phase enum.  A pipeline checkpoint's training state
+    holds one of its members, pickled under the name `motif.pipeline.base.PipelinePhase`; the
+    class is registered under that name for `weights_only` loading so such a checkpoint loads
+    without importing the training pipeline and without the full unpickler (the reference does
+    the same, `motif/model/checkpoint.py:27-60`).  The member names are the pickle contract."""
+
+    INIT = auto()
+    SETUP = auto()
+    TRAINING = auto()
+    EVALUATING = auto()
+    FINISHED = auto()
+    INTERRUPTED = auto()
+    FAILED = auto()
+
+
+_SAFE_GLOBALS = [(PipelinePhase, 'motif.pipeline.base.PipelinePhase')]
+
+
 def _torch_load(path: str, map_location):
     errors = []
-    for kw in ({'weights_only': True, 'mmap': True}, {'weights_only': True}, {'weights_only': False, 'mmap': True},
-               {'weights_only': False}):
-        try:
-            return torch.load(path, map_location=map_location, **kw)
-        except Exception as e:  # noqa: BLE001 - every form is tried, the errors are reported together
-            errors.append(f'{kw}: {type(e).__name__}: {e}')
+    with torch.serialization.safe_globals(_SAFE_GLOBALS):
+        for kw in ({'weights_only': True, 'mmap': True}, {'weights_only': True}, {'weights_only': False, 'mmap': True},
+                   {'weights_only': False}):
+            try:
+                return torch.load(path, map_location=map_location, **kw)
+            except Exception as e:  # noqa: BLE001 - every form is tried, the errors are reported together
+                errors.append(f'{kw}: {type(e).__name__}: {e}')
     raise RuntimeError(f'failed to load {path!r} with torch.load:\n  ' + '\n  '.join(errors))
 
 

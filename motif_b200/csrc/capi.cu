@@ -1,7 +1,10 @@
 // Status / error plumbing shared by every C-ABI entry point.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -69,7 +72,46 @@ int encode_tile_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
   return encode_tile_map(map, base, elem_bytes, 2, dims, strides, box, swizzle_bytes);
 }
 
+// Per-(kernel, device) one-time set-up, e.g. the dynamic shared-memory limit that
+// cudaFuncSetAttribute must raise before the first launch on each device.  The set-up runs
+// under one process-wide lock, so host threads launching on the same device at once neither
+// race on the bookkeeping nor launch before the attribute is in place; a failed set-up is
+// not recorded and is retried by the next call.
+static std::mutex g_once_mu;
+static std::map<std::pair<const void*, int>, bool> g_once_done;
+
+int once_per_device(const void* key, int (*setup)(const void*, int), int arg) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(MB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(g_once_mu);
+  auto it = g_once_done.find({key, dev});
+  if (it != g_once_done.end()) return MB_OK;
+  const int rc = setup(key, arg);
+  if (rc == MB_OK) g_once_done[{key, dev}] = true;
+  return rc;
+}
+
+static int set_smem_attr(const void* func, int bytes) {
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return check_launch("cudaFuncSetAttribute (dynamic shared memory)");
+  return MB_OK;
+}
+
+int ensure_smem_attr(const void* func, int bytes) { return once_per_device(func, set_smem_attr, bytes); }
+
+// Testing hooks (motif_b200_testing_force): off unless a test turns them on.
+static std::atomic<int> g_force[MB_FORCE_COUNT];
+
+bool forced(int knob) { return knob >= 0 && knob < MB_FORCE_COUNT && g_force[knob].load(std::memory_order_relaxed); }
+
 }  // namespace mb
+
+extern "C" int motif_b200_testing_force(int knob, int value) {
+  MB_REQUIRE(knob >= 0 && knob < MB_FORCE_COUNT, MB_ERR_ARG, "testing_force: unknown knob %d", knob);
+  mb::g_force[knob].store(value ? 1 : 0, std::memory_order_relaxed);
+  return MB_OK;
+}
 
 extern "C" const char* motif_b200_last_error(void) { return mb::g_last_error; }
 extern "C" int motif_b200_abi_version(void) { return 1; }

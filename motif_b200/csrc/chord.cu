@@ -728,12 +728,9 @@ __global__ void __launch_bounds__(128) chord_fwd_simple_kernel(
 //                accumulates D/32 output dims over the tile's keys.
 // Partials: ws[((split * B + b) * H + h) * Tn + t][D + 2] = (o[0..D), m, l) for the merge.
 constexpr int kDecTile = 64;
-// MOTIF_B200_DECODE_SCALAR=1 routes 16-bit D = 64 decode through the CUDA-core kernel (the
-// tensor-core kernel is the default); used to cross-check the two in tests.
-static bool force_scalar_decode() {
-  const char* e = getenv("MOTIF_B200_DECODE_SCALAR");
-  return e && e[0] == '1';
-}
+// The testing knob MB_FORCE_DECODE_SCALAR routes 16-bit D = 64 decode through the CUDA-core
+// kernel (the tensor-core kernel is the default) so tests can cross-check the two.
+static bool force_scalar_decode() { return forced(MB_FORCE_DECODE_SCALAR); }
 #ifndef CD_STAGES
 #define CD_STAGES 3
 #endif
@@ -1225,12 +1222,25 @@ __global__ void __launch_bounds__(128) chord_decode_mma_kernel(
   float* sL = sM + 64;                       // [4][16]
   float* sO = sL + 64;                       // [4][16][64]
   if (failed) {
+    __shared__ int drained;
     if (tid == 0) {
       atomicAdd(&g_wait_timeouts, 1u);
+      bool all = true;
       for (int u = t; u < nissued; ++u)
-        mbar_wait_bounded(&bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit);
+        all = mbar_wait_bounded(&bar[u % kDecStages], (uint32_t)((u / kDecStages) & 1), kDecWaitLimit) && all;
+      drained = all ? 1 : 0;
     }
     __syncthreads();
+    if (!drained) {
+      // A copy may still land in the stages: leave shared memory alone and write this
+      // split's rows as empty partials (m = -inf, l = 0, o = 0) straight to the workspace.
+      for (int idx = tid; idx < R * (D + 2); idx += 128) {
+        const int r = idx / (D + 2), d = idx % (D + 2);
+        const int h = kvh * G + r / Tn, tt = r % Tn;
+        ws[((((int64_t)split * B + b) * H + h) * Tn + tt) * (D + 2) + d] = d == D ? -INFINITY : 0.f;
+      }
+      return;
+    }
 #pragma unroll
     for (int ri = 0; ri < 2; ++ri) {
       m[ri] = -INFINITY;
@@ -1457,12 +1467,9 @@ extern "C" int64_t motif_b200_chord_workspace_bytes(int64_t, int64_t, int64_t, i
   return 0;
 }
 
-// MOTIF_B200_CHORD_TC=0 keeps 16-bit D = 64 prefill on the mma.sync kernel (the tcgen05
-// kernel is the default); used to cross-check the two in tests.
-static bool chord_tc_disabled() {
-  const char* e = getenv("MOTIF_B200_CHORD_TC");
-  return e && e[0] == '0';
-}
+// The testing knob MB_FORCE_CHORD_MMA_SYNC keeps 16-bit D = 64 prefill on the mma.sync kernel
+// (the tcgen05 kernel is the default) so tests can cross-check the two.
+static bool chord_tc_disabled() { return forced(MB_FORCE_CHORD_MMA_SYNC); }
 
 template <typename T, int G, bool KM>
 int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha, const float* beta, const float* mu,
@@ -1488,14 +1495,7 @@ int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha,
     if (rc) return rc;
   }
   auto kern = chord_tc_kernel<T, G, KM>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::alloc) != cudaSuccess)
-      return check_launch("chord_attention (shared memory attribute)");
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int rc = ensure_smem_attr((const void*)kern, Lay::alloc)) return rc;
   const int GS = (int)(H / Hkv);
   dim3 grid((unsigned)((L + 2 * Lay::BMQ - 1) / (2 * Lay::BMQ)), (unsigned)(Hkv * (GS / G)), (unsigned)B);
   kern<<<grid, 256, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
@@ -1640,14 +1640,7 @@ static int chord_decode_impl(const void* q, const void* k_cache, const void* v_c
           const int smem = 2 * kDecStages * kDecTile * DD * 2 + kDecStages * 8 + 1024;
           auto launch_mma = [&](auto rhc) {  // RH = 1: every query row is in the first 8 MMA rows
             auto kern = chord_decode_mma_kernel<Tt, decltype(rhc)::value>;
-            static bool attr_set[64] = {};
-            int dev = 0;
-            cudaGetDevice(&dev);
-            if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-              if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-                return check_launch("chord_decode (shared memory attribute)");
-              if (dev >= 0 && dev < 64) attr_set[dev] = true;
-            }
+            if (int rc2 = ensure_smem_attr((const void*)kern, smem)) return rc2;
             kern<<<grid, 128, smem, st>>>(tmK, tmV, (const Tt*)q, cap, len_dev, (int)len_host, alpha, beta, mu,
                                           ssmax, (float*)workspace, (int)B, (int)H, (int)Hkv, (int)T, max_splits,
                                           scale, eps, kmask, kms);
@@ -1664,14 +1657,7 @@ static int chord_decode_impl(const void* q, const void* k_cache, const void* v_c
         constexpr int RM = decltype(rmc)::value;
         auto kern = chord_decode_kernel<Tt, DD, RM>;
         const int smem = (int)sizeof(DecodeSmem<Tt, DD, RM>);
-        static bool attr_set[64] = {};  // per instantiation and device
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-          if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return check_launch("chord_decode (shared memory attribute)");
-          if (dev >= 0 && dev < 64) attr_set[dev] = true;
-        }
+        if (int rc2 = ensure_smem_attr((const void*)kern, smem)) return rc2;
         kern<<<grid, 128, smem, st>>>((const Tt*)q, (const Tt*)k_cache, (const Tt*)v_cache, cap, len_dev,
                                       (int)len_host, alpha, beta, mu, ssmax, (float*)workspace, (int)B, (int)H,
                                       (int)Hkv, (int)T, max_splits, scale, eps, kmask, kms);
@@ -1876,28 +1862,17 @@ namespace {
 constexpr int64_t kNoAllocScratchBytes = 8LL << 20;  // 8 MiB, held by every GPU that loads the library
 __device__ __align__(256) float g_decode_scratch[kNoAllocScratchBytes / sizeof(float)];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-float* g_scratch_dev[kMaxDevices] = {};
-
-// Device address of g_decode_scratch on the current device.  In host code the array's
-// name is only a host-side stand-in, so the address is looked up once per device (with
-// that device current) and cached.
+// Device address of g_decode_scratch in the current device's context.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up with the device
+// current, on every call: the query is cheap, and a cached address would go stale if the
+// context were torn down and recreated (cudaDeviceReset) with the module loaded elsewhere.
+// The first call on a device may load the module; make it before any stream capture.
 int scratch_on_current_device(float** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(MB_ERR_CUDA, "chord_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices)
-    return set_error(MB_ERR_UNSUPPORTED, "chord_decode_noalloc: device ordinal %d >= %d", dev, kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_dev[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(MB_ERR_CUDA, "chord_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_scratch_dev[dev] = static_cast<float*>(p);
-  }
-  *out = g_scratch_dev[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(MB_ERR_CUDA, "chord_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  *out = static_cast<float*>(p);
   return MB_OK;
 }
 

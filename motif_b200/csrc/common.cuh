@@ -24,6 +24,13 @@ int encode_tile_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
 int encode_tile_map(CUtensorMap* map, const void* base, int elem_bytes, int rank, const uint64_t* dims,
                     const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes);
 
+// Runs `setup(key, arg)` once per (key, current device) under a process-wide lock.
+int once_per_device(const void* key, int (*setup)(const void*, int), int arg);
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device (thread-safe).
+int ensure_smem_attr(const void* func, int bytes);
+// True while a test has switched testing knob `knob` on (motif_b200_testing_force).
+bool forced(int knob);
+
 #define MB_REQUIRE(cond, code, ...)                  \
   do {                                               \
     if (!(cond)) return ::mb::set_error((code), __VA_ARGS__); \

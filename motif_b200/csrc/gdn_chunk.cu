@@ -546,21 +546,11 @@ int launch_dims(int64_t Dk, int64_t Dv, const void* q, const void* k, const void
                    (long long)Dv);
 }
 
-// MOTIF_B200_GDN_PRECISE=1 routes 16-bit inputs through the 3xTF32 kernel (validation aid).
-bool force_precise() {
-  static const bool v = [] {
-    const char* e = getenv("MOTIF_B200_GDN_PRECISE");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
-// MOTIF_B200_GDN_FUSED=1 keeps 16-bit calls that bring a workspace on the single fused kernel
-// (the two-kernel split is the default when a workspace is given); used to cross-check them.
-bool force_fused() {
-  const char* e = getenv("MOTIF_B200_GDN_FUSED");
-  return e && e[0] == '1';
-}
+// Testing knobs: MB_FORCE_GDN_PRECISE routes 16-bit inputs through the 3xTF32 kernel;
+// MB_FORCE_GDN_FUSED keeps 16-bit calls that bring a workspace on the single fused kernel (the
+// two-kernel split is the default when a workspace is given).  Tests cross-check with them.
+bool force_precise() { return forced(MB_FORCE_GDN_PRECISE); }
+bool force_fused() { return forced(MB_FORCE_GDN_FUSED); }
 
 int gdn_chunk_impl(const void* q, const void* k, const void* v, const float* beta, const float* g,
                    const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, int64_t Dk,

@@ -802,15 +802,8 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
   using RL = RecLayout<T, DK, DV>;
   auto k1 = gdn_wy_kernel<T, DK, DV, PREP>;
   auto k2 = gdn_rec_kernel<T, DK, DV>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WL::bytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RL::bytes);
-    if (e != cudaSuccess) return set_error(MB_ERR_CUDA, "gdn_chunk (split): smem attribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int rc0 = ensure_smem_attr((const void*)k1, (int)WL::bytes)) return rc0;
+  if (int rc0 = ensure_smem_attr((const void*)k2, (int)RL::bytes)) return rc0;
   const int64_t nchunks = (L + C - 1) / C;
   k1<<<dim3((unsigned)nchunks, (unsigned)(B * H)), NT, WL::bytes, stream>>>(
       (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws, pin);

@@ -23,6 +23,7 @@
 // Every mbarrier wait is bounded; a CTA whose wait runs out counts itself
 // (motif_b200_wait_timeouts), drains what it issued and still takes both cluster barriers.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -337,10 +338,14 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* w,
     using T = decltype(t);
     auto kern = skinny_tc_kernel<T>;
     // per device, once: attributes, and how many clusters of each size 1..16 fit at a time
+    // guarded by one lock: host threads launching on the same device at once see the table
+    // only after it is complete
     static int active[64][kMaxSplit + 1] = {};
+    static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
       return set_error(MB_ERR_CUDA, "skinny_gemm: no device");
+    std::unique_lock<std::mutex> lock(mu);
     if (!active[dev][0]) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess ||
           cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
@@ -365,6 +370,7 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* w,
       if (active[dev][1] <= 0) return set_error(MB_ERR_CUDA, "skinny_gemm: kernel cannot be resident");
       active[dev][0] = 1;
     }
+    lock.unlock();
     // the most K slices whose clusters all fit in one wave
     const int nblk = (int)((N + kBN - 1) / kBN);
     const int kchunks = (int)((K / kBK + kAtoms - 1) / kAtoms);

@@ -194,6 +194,7 @@ class GraphDecoder:
                                                              model.blocks[b + 1].features[0].attn_norm.eps))
             x = x_next
         logits = _mm(hn, self.lm)
+        self.logits = logits  # the step's [B, V] logits buffer: after a replay, the last step's
         sp = self.sampler
         if sp is None:
             _lib.call('motif_b200_argmax', _lib.ptr(logits), B, cfg.vocab_size, logits.stride(0),
@@ -359,26 +360,32 @@ class GraphDecoder:
         for bc in self.cache:
             bc.attn_res.seq_len = self.seq_start + self.taken
 
-    def breakdown(self, first_ids: torch.Tensor):
-        """Run one step eagerly (outside the graph) with CUDA events around every launch and
-        return `{entry point or 'cublas_gemm': (calls, ms)}`; the states, positions and
-        step counter are put back afterwards, so the decoder is unchanged."""
+    def breakdown(self, first_ids: torch.Tensor, steps: int = 32):
+        """Run `steps` decode steps eagerly (outside the graph) with CUDA events around every
+        launch and return `{entry point or 'cublas_gemm': (calls per step, ms per step)}`,
+        averaged over the steps after one untimed warm step.  The states, positions and step
+        counter are put back afterwards, so the decoder is unchanged.  Eager launches leave
+        gaps the graph does not have, so these times explain the graph step's SHARES; their
+        sum exceeds the graph step."""
         snap = self._snapshot()
         lens = self.lens.clone()
         step_idx = self.step_idx.clone()
         self.ids.copy_(first_ids.reshape(-1).to(self.dev, torch.int64))
-        tr = _lib.Tracker(timed=None)
+        self._step()  # warm: the first eager step after capture touches every buffer once
         torch.cuda.synchronize(self.dev)
+        tr = _lib.Tracker(timed=None)
         _lib.set_tracker(tr)
         try:
-            self._step()
+            for _ in range(max(1, int(steps))):
+                self._step()
         finally:
             _lib.set_tracker(None)
         torch.cuda.synchronize(self.dev)
         self._restore(snap)
         self.lens.copy_(lens)
         self.step_idx.copy_(step_idx)
-        return tr.summary()
+        n = max(1, int(steps))
+        return {k: (c / n, t / n) for k, (c, t) in tr.summary().items()}
 
     def release(self):
         """Free the graph (and its memory pool)."""

@@ -94,3 +94,48 @@ def test_loaded_model_logits_match_reference(name):
         lg = m(d['ids'].cuda()).logits.float().cpu()
     err = ((lg - d['logits']).abs().max() / d['logits'].abs().max()).item()
     assert err < 1e-5, err
+
+
+def test_pipeline_checkpoint_with_phase_enum_loads_weights_only(tmp_path, monkeypatch):
+    """A pipeline checkpoint whose training state holds a `motif.pipeline.base.PipelinePhase`
+    member loads through the `weights_only` unpickler (the class is allowlisted under that
+    name), without the training pipeline importable and without the full unpickler."""
+    import enum
+    import sys
+    import types
+    from motif_b200 import checkpoint as ck
+
+    # write the file the way the training pipeline did: the enum pickled under its own module
+    mod = types.ModuleType('motif.pipeline.base')
+
+    class PipelinePhase(enum.Enum):
+        INIT = 1
+        SETUP = 2
+        TRAINING = 3
+        EVALUATING = 4
+        FINISHED = 5
+        INTERRUPTED = 6
+        FAILED = 7
+
+    PipelinePhase.__module__ = 'motif.pipeline.base'
+    PipelinePhase.__qualname__ = 'PipelinePhase'
+    mod.PipelinePhase = PipelinePhase
+    for name in ('motif', 'motif.pipeline'):
+        monkeypatch.setitem(sys.modules, name, sys.modules.get(name) or types.ModuleType(name))
+    monkeypatch.setitem(sys.modules, 'motif.pipeline.base', mod)
+    sd = {'embed.weight': torch.randn(8, 4), 'lm_head.weight': torch.randn(8, 4)}
+    path = str(tmp_path / 'phase.pt')
+    torch.save({'__pipeline__': 'pretrain', 'model': sd, 'state': {'phase': PipelinePhase.FINISHED, 'step': 7}}, path)
+    monkeypatch.delitem(sys.modules, 'motif.pipeline.base')
+
+    # the weights_only form must succeed on its own: fail the test if the full unpickler runs
+    real = torch.load
+
+    def guarded(*a, **kw):
+        assert kw.get('weights_only', True), 'fell back to the full unpickler'
+        return real(*a, **kw)
+
+    monkeypatch.setattr(torch, 'load', guarded)
+    ld = ck.load_checkpoint(path)
+    assert set(ld.state_dict) == set(sd)
+    assert all(torch.equal(ld.state_dict[k], sd[k]) for k in sd)

@@ -122,18 +122,38 @@ def test_tiny_config_graph_greedy64_matches_reference():
     assert torch.equal(gen, d['greedy']), (gen != d['greedy']).nonzero()
 
 
-def test_random_filled_cache_decode_172m_shapes():
+def test_random_filled_cache_decode_172m_matches_eager():
+    """The benchmark's decode set-up (172M shapes, bf16, caches filled with seeded random
+    contents at length 1000): the CUDA-graph steps equal the eager T = 1 forward fed the same
+    tokens on a copy of the same caches (same kernels, split count pinned), token for token
+    and logit for logit; cache lengths advance by one per step."""
+    import copy
     from motif_b200.config import config_172m
     from motif_b200.decode import GraphDecoder, fill_cache_random
     m = build(config_172m(), dtype=torch.bfloat16)
     B, L, steps = 4, 1000, 8
     cache = fill_cache_random(m, m.create_cache(), B, L, L + steps)
-    dec = GraphDecoder(m, cache, max_steps=steps)
-    first = torch.zeros((B, 1), dtype=torch.int64, device='cuda')
-    toks = dec.run(first, steps)
-    torch.cuda.synchronize()
-    assert toks.shape == (B, steps)
-    assert int(toks.min()) >= 0 and int(toks.max()) < m.config.vocab_size
+    m.decode_splits = 6
+    twin = copy.deepcopy(cache)
+    with torch.no_grad():
+        dec = GraphDecoder(m, cache, max_steps=steps)
+        first = torch.arange(B, dtype=torch.int64, device='cuda').view(B, 1) * 7
+        tok, g_toks, g_logits = first, [], []
+        for _ in range(steps):
+            tok = dec.run(tok, 1)
+            torch.cuda.synchronize()
+            g_toks.append(tok.clone())
+            g_logits.append(dec.logits.float().clone())
+        tok, e_toks, e_logits = first, [], []
+        for _ in range(steps):
+            out = m(tok, cache=twin)
+            twin = out.cache
+            e_logits.append(out.logits[:, 0].float())
+            tok = out.next_token()
+            e_toks.append(tok)
+    m.decode_splits = None
+    assert torch.equal(torch.cat(g_toks, 1), torch.cat(e_toks, 1))
+    assert torch.equal(torch.stack(g_logits), torch.stack(e_logits))
     assert all(lc.length == L + steps for bc in cache for lc in bc.attn)
 
 

@@ -237,12 +237,13 @@ def test_chord_prep(dtype, B, T, H, Hkv, D, pos):
                                                   (2, 8, 2, 2, 8448, 64, 12), (1, 12, 3, 1, 64, 64, 3),
                                                   (1, 16, 2, 2, 777, 64, 5)])
 @pytest.mark.parametrize('scalar', [False, True])
-def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, monkeypatch):
-    # 16-bit D = 64 runs the tensor-core kernel unless MOTIF_B200_DECODE_SCALAR=1
+def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, request):
+    # 16-bit D = 64 runs the tensor-core kernel unless the FORCE_DECODE_SCALAR testing knob is on
     if scalar:
         if dtype == torch.float32 or D != 64:
             pytest.skip('the CUDA-core kernel is the only path for this case')
-        monkeypatch.setenv('MOTIF_B200_DECODE_SCALAR', '1')
+        _lib.call('motif_b200_testing_force', _lib.FORCE_DECODE_SCALAR, 1)
+        request.addfinalizer(lambda: _lib.call('motif_b200_testing_force', _lib.FORCE_DECODE_SCALAR, 0))
     g = torch.Generator().manual_seed(S + T)
     cap = S + 10
     q = torch.randn(B, T, H, D, generator=g).to(dtype)

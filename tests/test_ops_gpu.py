@@ -184,15 +184,15 @@ def test_chord_16bit_vs_oracle(ops, dtype, B, H, Hkv, L, S, D):
 
 
 @pytest.mark.parametrize('B,H,Hkv,L,S', [(2, 12, 3, 300, 300), (1, 8, 8, 70, 500), (2, 16, 2, 200, 260)])
-def test_chord_tcgen05_matches_mma_sync(ops, monkeypatch, B, H, Hkv, L, S):
+def test_chord_tcgen05_matches_mma_sync(ops, B, H, Hkv, L, S):
     """16-bit D = 64 prefill: the tcgen05 kernel (default) against the mma.sync kernel."""
     q, k, v, alpha, beta, mu, ssmax, log_n, qs = chord_inputs(B, H, Hkv, L, S, 64, seed=L + 7 * S,
                                                               dtype=torch.bfloat16)
     args = cuda(q, k, v, alpha, beta, mu, ssmax, log_n)
     tc = ops.apply_chord_attention(*args)
-    monkeypatch.setenv('MOTIF_B200_CHORD_TC', '0')
-    ms = ops.apply_chord_attention(*args)
     from motif_b200 import _lib
+    with _lib.forced(_lib.FORCE_CHORD_MMA_SYNC):
+        ms = ops.apply_chord_attention(*args)
     assert _lib.wait_timeouts() == 0
     ref = oo.chord_attention(q.float(), k.float(), v.float(), alpha, beta, mu, ssmax, log_n, qs)
     assert rel_err(tc.float(), ref) < 1e-2 and rel_err(ms.float(), ref) < 1e-2
