@@ -274,6 +274,11 @@ def run_ours(args, world, rank, local):
     model = MotifChordModel(cfg)
     init_params(model, seed=0)
     model = model.to(dev, torch.bfloat16).eval()
+    if args.mode == 'ops':
+        # the op-level lines alone (configs 2 and 3, the projection shapes): for profiling
+        if rank == 0:
+            print(json.dumps({'metric': 'ops', 'ops': run_ops(dev, peaks(), args)}), flush=True)
+        return
     if args.mode == 'decode':
         # decode measurement alone, printed as the line's headline (profiling captures)
         d = run_decode(model, cfg, args, world, rank, local, dev, torch.cuda.current_stream(dev), peaks())
@@ -488,6 +493,75 @@ def run_ops(dev, pk, args):
                                     'gbs': b / (ms / 1000.0) / 1e9}}
     del a
     torch.cuda.empty_cache()
+    out['gemm_shapes'] = run_gemm_shapes(dev, pk)
+    return out
+
+
+# config 4's projection shapes (M = 32 x 4096 tokens): name -> (N, K)
+GEMM_SHAPES = {'gdn_in_proj': (8728, 768), 'gdn_out_proj': (768, 3584), 'chord_in_proj': (6016, 768),
+               'chord_down_proj': (768, 2048), 'lm_head': (32000, 768)}
+
+
+def run_gemm_shapes(dev, pk, M=32 * 4096):
+    """The tcgen05 projection kernel (`motif_b200_gemm`, plain store epilogue) against the library
+    GEMM (torch.mm -> cuBLAS) on config 4's shapes, bf16, alone (burst peak)."""
+    from motif_b200 import _lib
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    for name, (N, K) in GEMM_SHAPES.items():
+        a = torch.randn((M, K), device=dev, generator=g).bfloat16()
+        w = (torch.randn((N, K), device=dev, generator=g) * K ** -0.5).bfloat16()
+        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+
+        def ours():
+            _lib.call('motif_b200_gemm', a.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K, _lib.MB_BF16,
+                      _lib.stream_ptr(dev))
+
+        ms_o = _time_ms(ours, warm=2, iters=5)
+        ms_c = _time_ms(lambda: torch.mm(a, w.t(), out=y), warm=2, iters=5)
+        f = 2.0 * M * N * K
+        res[name] = {'M': M, 'N': N, 'K': K, 'ours_ms': ms_o, 'cublas_ms': ms_c,
+                     'ours_tflops': f / (ms_o / 1000.0) / 1e12, 'cublas_tflops': f / (ms_c / 1000.0) / 1e12,
+                     'ours_frac_of_measured_bf16': f / (ms_o / 1000.0) / 1e12 / pk['bf16_tflops']}
+        del a, w, y
+    torch.cuda.empty_cache()
+    res['gdn_in_proj_fused'] = run_gdn_prep_shape(dev, M)
+    return res
+
+
+def run_gdn_prep_shape(dev, M):
+    """The GDN input projection as the model runs it (`motif_b200_gemm_gdn_prep`: conv, SiLU,
+    norms, beta / g and SwiGLU in the epilogue) at config 4's shape."""
+    from motif_b200 import _lib
+    from motif_b200.config import config_172m
+    cfg = config_172m()
+    H, dk, dv, hid, d = cfg.num_heads, cfg.gdn_dk, cfg.gdn_dv, cfg.mlp_hidden, cfg.model_dim
+    B, T = M // SEQ_LEN, SEQ_LEN
+    n = 2 * H * dk + 2 * H * dv + 2 * H + 2 * hid
+    C = H * (2 * dk + dv)
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn((M, d), device=dev, generator=g).bfloat16()
+    w = (torch.randn((n, d), device=dev, generator=g) * d ** -0.5).bfloat16()
+    cw = torch.randn((C, 4), device=dev, generator=g).bfloat16()
+    al, db = torch.rand(H, device=dev, generator=g).bfloat16(), torch.rand(H, device=dev, generator=g).bfloat16()
+    q = torch.empty((M, H * dk), device=dev, dtype=torch.bfloat16)
+    k, v, gate = torch.empty_like(q), torch.empty((M, H * dv), device=dev, dtype=torch.bfloat16), torch.empty(
+        (M, H * dv), device=dev, dtype=torch.bfloat16)
+    be, gg = torch.empty((M, H), device=dev), torch.empty((M, H), device=dev)
+    act = torch.empty((M, hid), device=dev, dtype=torch.bfloat16)
+    co = torch.empty((B, 3, C), device=dev, dtype=torch.bfloat16)
+
+    def run():
+        _lib.call('motif_b200_gemm_gdn_prep', x.data_ptr(), d, w.data_ptr(), d, B, T, d, H, dk, dv, hid, cw.data_ptr(),
+                  al.data_ptr(), db.data_ptr(), None, co.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                  be.data_ptr(), gg.data_ptr(), gate.data_ptr(), act.data_ptr(), hid, _lib.MB_BF16,
+                  _lib.stream_ptr(dev))
+
+    ms = _time_ms(run, warm=2, iters=5)
+    f = 2.0 * M * n * d
+    out = {'M': M, 'N': n, 'K': d, 'ours_ms': ms, 'ours_tflops': f / (ms / 1000.0) / 1e12}
+    del x, w, q, k, v, gate, act
+    torch.cuda.empty_cache()
     return out
 
 
@@ -682,8 +756,9 @@ def main():
                     help="skip timing the reference's own GPU (Triton) path from baseline/_ref")
     ap.add_argument('--ref-seq-len', type=int, default=SEQ_LEN)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--mode', choices=['all', 'decode'], default='all',
-                    help="'decode' runs only the config-5 decode measurement (for profiling)")
+    ap.add_argument('--mode', choices=['all', 'decode', 'ops'], default='all',
+                    help="'decode' runs only the config-5 decode measurement, 'ops' only the op-level lines "
+                         "(configs 2 and 3, the projection shapes); both for profiling")
     ap.add_argument('--decode-batch', type=int, default=DECODE_BATCH,
                     help=f'config-5 decode requests, split across the ranks (default {DECODE_BATCH})')
     ap.add_argument('--decode-steps', type=int, default=256,

@@ -327,6 +327,49 @@ MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* w, int
                            int64_t ldy, int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
                            int64_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ dense projections
+ * Y = X . W^T for 16-bit X [M, K] and W [N, K] (row strides ldx / ldw in elements, multiples of
+ * 8, 16-byte aligned; K a multiple of 64, else MB_ERR_UNSUPPORTED), fp32 accumulation on the
+ * tensor cores (tcgen05, one persistent CTA per SM), output in the input dtype.  fp32 models
+ * keep the library GEMM (these kernels are 16-bit only: MB_ERR_UNSUPPORTED).
+ * Replaces the prefill-time nn.Linear products of the reference's layers
+ * (block/attention/gdn_attn.py:88-94, chord_attn.py:88-96, block/mlp.py:52-53,
+ * model/motif.py:184 lm_head), each with the elementwise step that follows it fused in. */
+MB_API int motif_b200_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                           int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+/* The packed input projection of a decoder with its MLP activation fused: W holds n_plain
+ * projection rows, then the MLP's gate_up rows regrouped in blocks of 256 (128 value rows, then
+ * the 128 gate rows of the same hidden units; hid a multiple of 128).  y[:, :n_plain] = X . W[:
+ * n_plain]^T, and act[:, :hid] = SwiGLU of the gate_up product with the reference's rounding
+ * points: round(round(v) * round(silu(round(g)))) (block/mlp.py:52-53 + ops/swiglu.py:252-253).
+ * n_plain or hid may be 0. */
+MB_API int motif_b200_gemm_proj_swiglu(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t M,
+                                       int64_t K, int64_t n_plain, void* y, int64_t ldy, int64_t hid, void* act,
+                                       int64_t ld_act, int dtype, void* stream);
+/* The gated delta-net layer's packed input projection with the layer's preparation and the MLP
+ * activation in its epilogue.  W rows: q (H*dk) | k (H*dk) | v (H*dv) | a (H) | b (H) |
+ * g (H*dv) | gate_up (2*hid, regrouped as for motif_b200_gemm_proj_swiglu).  X is [B*T, K], the
+ * rows of B sequences of T tokens.  Outputs (token-major, contiguous): q, k [B*T, H*dk] after the
+ * causal depthwise conv (kernel 4, carried state conv_in [B, 3, C] or zeros; C = H*(2dk+dv)),
+ * SiLU and the per-head L2 norm (q also times dk^-1/2); v [B*T, H*dv] after conv + SiLU;
+ * beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) as fp32 [B*T, H]; gate [B*T, H*dv]
+ * (the g projection, for the gated norm); act (row stride ld_act) the SwiGLU; conv_out
+ * [B, 3, C] (optional) the raw inputs of each sequence's last three tokens.  Rounding points as
+ * the reference's bf16 layer.  dk = 64, dv a multiple of 32, H <= 16, T >= 3, hid a multiple
+ * of 128.  Replaces gdn_attn.py:88-94 (projections), :116-136 (_conv), :183-197 (normalise,
+ * beta, g) and block/mlp.py:52-53. */
+MB_API int motif_b200_gemm_gdn_prep(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t B, int64_t T,
+                                    int64_t K, int64_t H, int64_t dk, int64_t dv, int64_t hid, const void* conv_w,
+                                    const void* A_log, const void* dt_bias, const void* conv_in, void* conv_out,
+                                    void* q, void* k, void* v, float* beta, float* g, void* gate, void* act,
+                                    int64_t ld_act, int dtype, void* stream);
+/* The Chord output projection with the gate and the parallel residual fused:
+ * out = round(round(round(X . W^T) * round(sigmoid(gate))) + res) over [M, N]; out may alias res.
+ * Replaces chord_attn.py:254,313 (o_proj(out) * G) and decoder.py:208 (attn + mlp). */
+MB_API int motif_b200_gemm_gate_residual(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                         const void* gate, int64_t ldg, const void* res, int64_t ldr, void* out,
+                                         int64_t ldo, int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+
 /* out = a * sigmoid(gate) + m over [rows, N] (row strides given).
  * Replaces chord_attn.py:254,313 (o_proj(out) * G) + decoder.py:208 (attn + mlp). */
 MB_API int motif_b200_gate_residual(const void* a, int64_t a_stride, const void* gate,

@@ -71,6 +71,12 @@ SIGNATURES = {
                                ctypes.c_uint64, _P, _P, _P, _I64, _I, _P]),
     'motif_b200_wait_timeouts': (_I, [_P]),
     'motif_b200_testing_force': (_I, [_I, _I]),
+    'motif_b200_gemm': (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    'motif_b200_gemm_proj_swiglu': (_I, [_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _I64, _I, _P]),
+    'motif_b200_gemm_gdn_prep': (_I, [_P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P,
+                                      _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I, _P]),
+    'motif_b200_gemm_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I,
+                                           _P]),
     'motif_b200_skinny_gemm_workspace_bytes': (_I64, [_I64, _I64, _I64]),
     'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _I64, _P]),
     'motif_b200_gdn_prefill_ws': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64,

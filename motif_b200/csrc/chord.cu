@@ -1905,6 +1905,7 @@ extern "C" int motif_b200_chord_decode_noalloc(const void* q, const void* k_cach
 namespace mb {
 int read_and_clear_gdn_timeouts(unsigned int* count);
 int read_and_clear_skinny_timeouts(unsigned int* count);
+int read_and_clear_gemm_timeouts(unsigned int* count);
 }
 
 extern "C" int motif_b200_wait_timeouts(uint32_t* count) {
@@ -1913,10 +1914,11 @@ extern "C" int motif_b200_wait_timeouts(uint32_t* count) {
   if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess ||
       cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
     return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
-  unsigned int sk = 0;
+  unsigned int sk = 0, gm = 0;
   int rc = mb::read_and_clear_gdn_timeouts(&gdn);
   if (!rc) rc = mb::read_and_clear_skinny_timeouts(&sk);
+  if (!rc) rc = mb::read_and_clear_gemm_timeouts(&gm);
   if (rc) return rc;
-  *count = v + gdn + sk;
+  *count = v + gdn + sk + gm;
   return MB_OK;
 }

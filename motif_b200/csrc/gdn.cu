@@ -487,19 +487,14 @@ __global__ void __launch_bounds__(256) gdn_prep_run_kernel(
   // the run holding T-1 writes the raw inputs at T-3 .. T-1 as the carried conv state
   const int last = Tn - 1 - t0;
   if (active && conv_out && last >= 0 && last < TR) {
+    // raw[j] holds token t0 - 3 + j = Tn - 3 + slot: the window rows before t0 (j < 3) are
+    // included, since a last run of one or two tokens leaves the earlier slots there (and
+    // positions before 0 hold conv_in or zeros)
 #pragma unroll
-    for (int j = 3; j < TR + 3; ++j) {
-      const int slot = j - last - 1;  // raw[j] holds token t0 - 3 + j = Tn - 3 + slot
+    for (int j = 0; j < TR + 3; ++j) {
+      const int slot = j - last - 1;
       if (slot >= 0 && slot < 3)
         *reinterpret_cast<uint4*>(conv_out + ((int64_t)b * 3 + slot) * C + c0) = raw[j];
-    }
-    if (Tn < 3) {  // positions before 0 come from conv_in (or zeros)
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int slot = j - last - 1;
-        if (slot >= 0 && slot < 3)
-          *reinterpret_cast<uint4*>(conv_out + ((int64_t)b * 3 + slot) * C + c0) = raw[j];
-      }
     }
   }
 }

@@ -269,8 +269,10 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
     if (pin.conv_out && last >= 0 && last < 8) {
 #pragma unroll
       for (int j = 0; j < 11; ++j) {
-        const int slot = j - last - 1;  // raw[j] holds token t0 - 3 + j = L - 3 + slot
-        if (slot >= 0 && slot < 3 && (j >= 3 || L < 3))
+        // raw[j] holds token t0 - 3 + j = L - 3 + slot; the window rows before the run (j < 3)
+        // matter when the last run holds fewer than three tokens
+        const int slot = j - last - 1;
+        if (slot >= 0 && slot < 3)
           *reinterpret_cast<uint4*>(pin.conv_out + ((int64_t)b * 3 + slot) * Ct + cg) = raw[j];
       }
     }

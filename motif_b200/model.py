@@ -251,6 +251,13 @@ def greedy_next(last_logits: torch.Tensor) -> torch.Tensor:
 
 
 # ============================================================================ packing
+def _interleave_gate_up(gu: torch.Tensor, hid: int) -> torch.Tensor:
+    """gate_up rows `[values (hid) | gates (hid)]` regrouped in blocks of 256: 128 value rows, then
+    the 128 gate rows of the same hidden units (the layout `motif_b200_gemm_proj_swiglu` reads)."""
+    v, g = gu[:hid].view(hid // 128, 128, -1), gu[hid:].view(hid // 128, 128, -1)
+    return torch.cat([v, g], 1).reshape(2 * hid, -1)
+
+
 @dataclass
 class _GDNPack:
     w_in: torch.Tensor      # [N_in, d]: q | k | v | a | b | g | gate_up, norm weights folded in
@@ -265,6 +272,7 @@ class _GDNPack:
     hid: int
     off_g: int
     off_gu: int
+    w_in_il: Optional[torch.Tensor] = None  # w_in with gate_up regrouped for the fused SwiGLU
 
 
 @dataclass
@@ -284,6 +292,7 @@ class _ChordPack:
     hid: int
     off_g: int
     off_gu: int
+    w_in_il: Optional[torch.Tensor] = None  # w_in with gate_up regrouped for the fused SwiGLU
 
 
 @torch.no_grad()
@@ -297,23 +306,28 @@ def _pack_decoder(dec: Decoder):
         parts = [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.g_proj.weight]
         off_g = a.hidden_size + 2 * a.kv_dim
         w_in = torch.cat([p * wa for p in parts] + [gu], 0).contiguous()
+        w_in_il = (torch.cat([w_in[:off_g + a.hidden_size], _interleave_gate_up(w_in[off_g + a.hidden_size:], hid)],
+                             0).contiguous() if hid % 128 == 0 else None)
         al, be, mu = a._ggd_parameters()
         return _ChordPack(w_in=w_in, qn_w=a.q_norm.weight.detach().contiguous(),
                           kn_w=a.k_norm.weight.detach().contiguous(), w_o=a.o_proj.weight.detach().contiguous(),
                           w_down=dec.mlp.down_proj.weight.detach().contiguous(), alpha=al.contiguous(),
                           beta=be.contiguous(), mu=mu.contiguous(), ssmax=a.ssmax_s.detach().float().contiguous(),
                           H=a.num_heads, Hkv=a.num_kv_heads, D=a.head_dim, hid=hid, off_g=off_g,
-                          off_gu=off_g + a.hidden_size)
+                          off_gu=off_g + a.hidden_size, w_in_il=w_in_il)
     H, dk, dv = a.num_heads, a.dk, a.dv
     parts = [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.a_proj.weight, a.b_proj.weight, a.g_proj.weight]
     off_g = 2 * H * dk + H * dv + 2 * H
     w_in = torch.cat([p * wa for p in parts] + [gu], 0).contiguous()
+    off_gu = off_g + H * dv
+    w_in_il = (torch.cat([w_in[:off_gu], _interleave_gate_up(w_in[off_gu:], hid)], 0).contiguous()
+               if hid % 128 == 0 else None)
     conv_w = torch.cat([a.q_conv.weight.reshape(-1, CONV_SIZE), a.k_conv.weight.reshape(-1, CONV_SIZE),
                         a.v_conv.weight.reshape(-1, CONV_SIZE)], 0).contiguous()
     w_out = torch.cat([a.o_proj.weight, dec.mlp.down_proj.weight], 1).contiguous()
     return _GDNPack(w_in=w_in, conv_w=conv_w, A_log=a.A_log.detach().contiguous(),
                     dt_bias=a.dt_bias.detach().contiguous(), onorm_w=a.o_norm.weight.detach().contiguous(),
-                    w_out=w_out, H=H, dk=dk, dv=dv, hid=hid, off_g=off_g, off_gu=off_g + H * dv)
+                    w_out=w_out, H=H, dk=dk, dv=dv, hid=hid, off_g=off_g, off_gu=off_gu, w_in_il=w_in_il)
 
 
 # ============================================================================ model
@@ -523,6 +537,47 @@ def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Ten
     return r
 
 
+def _tc_ok(*ts: torch.Tensor) -> bool:
+    """The tcgen05 projection kernels take 16-bit operands with 16-byte aligned rows and K a
+    multiple of 64; fp32 (the parity mode) stays on the library GEMM."""
+    a = ts[0]
+    return (a.dtype in (torch.bfloat16, torch.float16) and a.shape[1] % 64 == 0
+            and all(t.dtype == a.dtype and t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+                    for t in ts))
+
+
+# Row counts up to this stay on the library GEMM: decode-sized products stream the weights once
+# and the persistent 128-row tiles would leave most of the GPU idle.
+TC_MIN_M = 65
+
+
+def _gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """a [M, K] @ w[N, K]^T: prefill-sized 16-bit products on the tcgen05 projection kernel
+    (`motif_b200_gemm`), decode-sized or fp32 ones on `_mm`."""
+    M, K = a.shape
+    N = w.shape[0]
+    if M >= TC_MIN_M and _tc_ok(a, w) and (out is None or (out.stride(1) == 1 and out.dtype == a.dtype)):
+        y = out if out is not None else torch.empty((M, N), dtype=a.dtype, device=a.device)
+        _lib.call('motif_b200_gemm', _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(y), y.stride(0),
+                  M, N, K, _lib.dtype_code(a.dtype), _lib.stream_ptr(a.device))
+        return y
+    return _mm(a, w, out)
+
+
+def _proj_fused(pk, hn: torch.Tensor, act: torch.Tensor):
+    """The decoder's packed input projection with its SwiGLU fused (`motif_b200_gemm_proj_swiglu`)
+    when the shapes allow it: returns the [M, off_gu] projection (q | k | v | ... | g) and writes
+    the MLP activation into `act`; else None."""
+    M = hn.shape[0]
+    if pk.w_in_il is None or M < TC_MIN_M or not _tc_ok(hn, pk.w_in_il, act):
+        return None
+    proj = torch.empty((M, pk.off_gu), dtype=hn.dtype, device=hn.device)
+    _lib.call('motif_b200_gemm_proj_swiglu', _lib.ptr(hn), hn.stride(0), _lib.ptr(pk.w_in_il), pk.w_in_il.stride(0),
+              M, hn.shape[1], pk.off_gu, _lib.ptr(proj), proj.stride(0), pk.hid, _lib.ptr(act), act.stride(0),
+              _lib.dtype_code(hn.dtype), _lib.stream_ptr(hn.device))
+    return proj
+
+
 def _norm_read(sources: List[torch.Tensor], query, weight, h_out, hn_out, eps_src=NORM_EPS, eps_out=NORM_EPS):
     x0 = sources[0]
     rows, d = x0.shape
@@ -566,17 +621,16 @@ def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, posit
                 _norm_read([x] + fs, block.pseudo_queries[i].detach(), block.attn_res_norms[i].weight.detach(),
                            None, hn, eps_src=block.attn_res_norms[i].eps)
             pk = decs[b][i]
-            proj = _mm(hn, pk.w_in)
             layer_cache = bc.attn[i] if use_cache else None
             if dec.attn_type == 'chord':
                 if layer_cache is not None and not isinstance(layer_cache, KVLayerCache):
                     raise TypeError(f'ChordAttention requires KVLayerCache, got {type(layer_cache).__name__}')
-                f = _chord_decoder(model, pk, proj, B, T, layer_cache, position, dt, dev, dc, st, key_bias)
+                f = _chord_decoder(model, pk, hn, B, T, layer_cache, position, dt, dev, dc, st, key_bias)
             else:
                 if layer_cache is not None and not isinstance(layer_cache, GatedDeltaAttentionLayerCache):
                     raise TypeError(f'GatedDeltaAttention requires GatedDeltaAttentionLayerCache, '
                                     f'got {type(layer_cache).__name__}')
-                f = _gdn_decoder(pk, proj, B, T, layer_cache, dt, dev, dc, st)
+                f = _gdn_decoder(pk, hn, B, T, layer_cache, dt, dev, dc, st)
             fs.append(f)
         # block output = sum of the increments (decoder.py:215-217), and its RMSNorm for the
         # next block's first decoder (or the final norm before lm_head)
@@ -588,24 +642,22 @@ def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, posit
         ar.partial_block = x_next.view(B, T, d)
         ar.seq_len = max(ar.seq_len, T)
         x = x_next
-    logits = _mm(hn, lm)
+    logits = _gemm(hn, lm)
     return logits.view(B, T, cfg.vocab_size), x.view(B, T, d)
 
 
-_PREFILL_DIMS = ((32, 64), (64, 64), (64, 128))
-# motif_b200_gdn_prefill (conv / norms inside the chunk kernel) is correct but slower than the
-# separate high-occupancy prep kernel + chunk kernel, whose per-chunk critical path it would
-# lengthen; the model uses the two-kernel path unless this is switched on.
-FUSED_GDN_PREFILL = False
-
-
-def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLayerCache], dt, dev, dc, st):
+def _gdn_decoder(pk: _GDNPack, hn, B, T, cache: Optional[GatedDeltaAttentionLayerCache], dt, dev, dc, st):
     """`GatedDeltaAttention.forward` + the SwiGLU MLP + the parallel residual (decoder.py:203-208)."""
     M = B * T
     H, dk, dv, hid = pk.H, pk.dk, pk.dv, pk.hid
     C = H * (2 * dk + dv)
-    N_in = proj.shape[1]
     cat = torch.empty((M, H * dv + hid), dtype=dt, device=dev)  # [gated-normed o | act]
+    # prefill: the input projection with the MLP activation fused, written into cat's right half
+    proj = _proj_fused(pk, hn, cat[:, H * dv:]) if T > 1 else None
+    act_done = proj is not None
+    if proj is None:
+        proj = _mm(hn, pk.w_in)
+    N_in = proj.shape[1]
     state_in = cache.state if cache is not None else None
     conv_in = cache._conv if cache is not None else None
     if state_in is not None and (state_in.dtype != torch.float32 or not state_in.is_contiguous()):
@@ -624,7 +676,7 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   proj.data_ptr() + pk.off_gu * proj.element_size(), N_in,
                   cat.data_ptr() + H * dv * cat.element_size(), cat.stride(0), hid, dc, st)
         conv_out = conv
-    elif dt != torch.float32 and (dk, dv) == (64, 128) and N_in % 8 == 0 and not FUSED_GDN_PREFILL:
+    elif dt != torch.float32 and (dk, dv) == (64, 128) and N_in % 8 == 0:
         # three kernels: preparation fused into the parallel per-chunk UT transform (records in a
         # workspace), the state scan, the gated norm
         conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)
@@ -635,13 +687,6 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   _lib.ptr(pk.dt_bias), _lib.ptr(conv_in), _lib.ptr(conv_out), _lib.ptr(state_in), _lib.ptr(state),
                   _lib.ptr(pk.onorm_w), eps, _lib.ptr(cat), cat.stride(0), B, T, H, dk, dv, dc, _lib.ptr(ws), ws_bytes,
                   st)
-    elif FUSED_GDN_PREFILL and dt != torch.float32 and (dk, dv) in _PREFILL_DIMS and N_in % 8 == 0:
-        # one kernel: conv + SiLU + norms + beta/g + chunked delta rule + GatedRMSNorm
-        conv_out = torch.empty((B, 3, C), dtype=dt, device=dev)
-        state = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
-        _lib.call('motif_b200_gdn_prefill', _lib.ptr(proj), N_in, _lib.ptr(pk.conv_w), _lib.ptr(pk.A_log),
-                  _lib.ptr(pk.dt_bias), _lib.ptr(conv_in), _lib.ptr(conv_out), _lib.ptr(state_in), _lib.ptr(state),
-                  _lib.ptr(pk.onorm_w), eps, _lib.ptr(cat), cat.stride(0), B, T, H, dk, dv, dc, st)
     else:
         qb = torch.empty((M, H * dk), dtype=dt, device=dev)
         kb = torch.empty((M, H * dk), dtype=dt, device=dev)
@@ -663,10 +708,10 @@ def _gdn_decoder(pk: _GDNPack, proj, B, T, cache: Optional[GatedDeltaAttentionLa
                   _lib.ptr(g), _lib.ptr(state_in), _lib.ptr(state), _lib.ptr(cat), B, H, T, dk, dv,
                   _lib.i64_array(strides), proj.data_ptr() + pk.off_g * proj.element_size(), N_in, dv,
                   _lib.ptr(pk.onorm_w), eps, dc, _lib.ptr(ws), max(ws_bytes, 0), st)
-    if T != 1:
+    if T != 1 and not act_done:
         _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
                   cat.data_ptr() + H * dv * cat.element_size(), M, hid, N_in, cat.stride(0), dc, st)
-    f = _mm(cat, pk.w_out)
+    f = _gemm(cat, pk.w_out)
     if cache is not None:
         cache._split = (H * dk, H * dk, H * dv)
         cache.update(state, conv_out, steps=T)
@@ -687,13 +732,20 @@ def _decode_splits(model, B, Hkv, S):
     return int(max(1, min(want, 64, (S + 255) // 256)))
 
 
-def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCache], position, dt, dev, dc, st,
+def _chord_decoder(model, pk: _ChordPack, hn, B, T, cache: Optional[KVLayerCache], position, dt, dev, dc, st,
                    key_bias: Optional[torch.Tensor] = None):
     """`ChordAttention.forward` (fused path) + SwiGLU MLP + parallel residual.  `key_bias`
     ([B, S] fp32, natural-log units) is the attention mask as an additive key bias."""
     M = B * T
     H, Hkv, D, hid = pk.H, pk.Hkv, pk.D, pk.hid
     d = H * D
+    act = torch.empty((M, hid), dtype=dt, device=dev)
+    # prefill: the input projection with the MLP activation fused
+    proj = _proj_fused(pk, hn, act) if T > 1 else None
+    act_done = proj is not None
+    fused_proj = act_done
+    if proj is None:
+        proj = _mm(hn, pk.w_in)
     N_in = proj.shape[1]
     if cache is None:
         cache = KVLayerCache()  # no layer cache (training-mode forward): attend to this chunk only
@@ -702,8 +754,6 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
     cached = cache.length
     q_start = position if position != 0 else cached
     qb = torch.empty((M, d), dtype=dt, device=dev)
-    act = torch.empty((M, hid), dtype=dt, device=dev)
-    act_done = False
     if cache.wide:
         # a wide cache (`cache.py:42-70`) stores every key / value head once per query head: the
         # new keys / values are prepared narrow, widened by the cache's own update, and the
@@ -715,6 +765,13 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
         cache.update(kt, vt)
         cache.reserve(cache.length, like=proj, shape=(B, H, D))
         Hkv = H
+    elif act_done:
+        cache.reserve(cached + T, like=proj, shape=(B, Hkv, D))
+        # q/k norms + cache append (the MLP activation came with the projection)
+        _lib.call('motif_b200_chord_prep', _lib.ptr(proj), N_in, _lib.ptr(pk.qn_w), _lib.ptr(pk.kn_w), _lib.ptr(qb),
+                  _lib.ptr(cache._kbuf), _lib.ptr(cache._vbuf), cache._kbuf.shape[2], None, cached, B, T, H, Hkv, D,
+                  NORM_EPS, dc, st)
+        cache.length = cached + T
     else:
         cache.reserve(cached + T, like=proj, shape=(B, Hkv, D))
         # q/k norms + cache append and the MLP activation in one launch
@@ -758,7 +815,14 @@ def _chord_decoder(model, pk: _ChordPack, proj, B, T, cache: Optional[KVLayerCac
     if not act_done:
         _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid,
                   N_in, hid, dc, st)
-    f = _mm(act, pk.w_down)
+    f = _gemm(act, pk.w_down)
+    gate = proj[:, pk.off_g:pk.off_g + d]
+    if fused_proj and _tc_ok(attn, pk.w_o, gate, f):
+        # o_proj with the gate and the parallel residual in its epilogue: f = attn_o * sigmoid(g) + f
+        _lib.call('motif_b200_gemm_gate_residual', _lib.ptr(attn), attn.stride(0), _lib.ptr(pk.w_o),
+                  pk.w_o.stride(0), _lib.ptr(gate), gate.stride(0), _lib.ptr(f), f.stride(0), _lib.ptr(f),
+                  f.stride(0), M, d, d, dc, st)
+        return f
     a = _mm(attn, pk.w_o)
     _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(), N_in,
               _lib.ptr(f), d, _lib.ptr(f), d, M, d, dc, st)

@@ -328,7 +328,8 @@ def test_gate_residual_argmax_embed():
 
 
 @pytest.mark.parametrize('B,T,H,dk,dv,with_state', [(2, 150, 12, 64, 128, True), (1, 64, 4, 32, 64, False),
-                                                    (3, 2, 2, 64, 64, True), (1, 300, 3, 64, 128, False)])
+                                                    (3, 2, 2, 64, 64, True), (1, 300, 3, 64, 128, False),
+                                                    (2, 130, 12, 64, 128, True), (1, 129, 4, 64, 128, False)])
 def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
     """motif_b200_gdn_prefill == gdn_prep + gdn_chunk_gated, and both track the fp32 oracle."""
     dtype = torch.bfloat16

@@ -246,3 +246,21 @@ def test_functional_and_wide_caches_match_grouped(functional, wide):
             assert lc.k.shape[1] == H
             G = H // m.config.kv_heads
             assert torch.equal(lc.k[:, 0], lc.k[:, G - 1])  # copies of kv head 0
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('T', [129, 130, 131, 67])
+def test_conv_state_after_prefill_of_any_length(dtype, T):
+    """The carried conv state (the raw inputs of the last three tokens) after a prefill whose
+    length leaves one or two tokens in the last 8-token run: decoding the next token must give
+    the logits of a full prefill that includes it (d = 256, dk = 64, dv = 128)."""
+    cfg = MotifChordConfig(vocab_size=512, model_dim=256, num_heads=4, num_kv_heads=2, head_k_dim=64,
+                           block=('gdn', 'gdn', 'gdn', 'chord'), block_n=1)
+    m = build(cfg, jitter=0.1, dtype=dtype)
+    ids = torch.randint(0, 512, (2, T + 1), generator=torch.Generator().manual_seed(T)).cuda()
+    with torch.no_grad():
+        full = m(ids).logits[:, -1].float()
+        out = m(ids[:, :T])
+        step = m(ids[:, T:], cache=out.cache).logits[:, -1].float()
+    tol = 1e-5 if dtype == torch.float32 else 3e-2
+    assert rel_err(step, full) < tol, rel_err(step, full)
