@@ -674,6 +674,224 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   }
 }
 
+// ----------------------------------------------------------------------------- CTA pairs
+// The non-preparation projections run on pairs of CTAs (a cluster of two) that share each
+// 256 x 256 output tile: CTA r holds X rows m0 + 128 r (its 128 accumulator rows) and the r-th
+// half of the tile's W rows; the pair's leader issues tcgen05.mma.cta_group::2 (M = 256), which
+// reads A and B from both CTAs' shared memory.  Per SM that halves the W traffic through shared
+// memory and L2 against a one-CTA 128 x 256 tile, so a 6-stage ring of 32 KB stages (twice the
+// bytes in flight per unit of work) covers the L2 latency that starved the one-CTA pipeline.
+//   * both producers load into their own ring and complete transaction bytes on the LEADER's
+//     stage barrier (the leader expects the pair's bytes); each refills a stage when its own
+//     empty barrier says the leader's MMAs have read it;
+//   * the leader's MMA thread commits each stage's release and each finished accumulator to the
+//     barriers of both CTAs (one commit per CTA);
+//   * each CTA's epilogue drains its own TMEM rows and arrives on the leader's "accumulator
+//     free" barrier (remote arrive from the peer).
+constexpr int kStages2 = 6;
+constexpr int kHalfBBytes = (kBN / 2) * kBK * 2;   // 16 KB: this CTA's half of the W tile
+constexpr int kStage2Bytes = kABytes + kHalfBBytes; // 32 KB
+static_assert(kStages2 * kStage2Bytes <= kStages * kStageBytes, "the pair ring fits the one-CTA ring's space");
+
+__device__ __forceinline__ uint32_t cluster_rank2() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync2() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// shared::cluster address of `local` (a shared::cta address) in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_rank(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// X / W box into this CTA's shared memory, transaction bytes completed on the barrier at
+// shared::cluster address `bar` (the leader's)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive (once) on the barrier at shared::cluster address `bar` when every MMA this thread issued has completed
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                               const __grid_constant__ CUtensorMap tmB2,
+                                                               const __grid_constant__ GemmParams p) {
+  constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  extern __shared__ unsigned char gemm_smem_raw[];
+  unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
+  unsigned char* epi_smem = sm + kStages * kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * kStageBytes + kEpiSmem);
+  uint64_t* empty = full + kStages2;
+  uint64_t* tfull = empty + kStages2;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mdone = tempty + 2;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(mdone + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank2();
+  const bool leader = rank == 0;
+  if (warp == 0) tmem_alloc_pair(sTmem, 512);
+  if (tid == 32) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB2);
+    for (int i = 0; i < kStages2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * kEpiWarps);  // the epilogue warps of both CTAs
+    }
+    mbar_init(mdone, 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync2();  // both CTAs' barriers exist before any copy or arrive crosses the pair
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const int npairs = gridDim.x >> 1, pair = blockIdx.x >> 1;
+  const int ntiles = p.m_tiles * p.n_tiles;
+  bool failed = false;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int t = pair; t < ntiles && !failed; t += npairs) {
+        const TileInfo ti = tile_info<false>(p, t);
+        const int m0 = (t / p.n_tiles) * (2 * kBM);
+        const int nmma = (ti.nvalid + 15) & ~15;
+        const int a_row = m0 + kBM * (int)rank, b_row = ti.wrow + (int)rank * (nmma / 2);
+        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+          const int s = it % kStages2;
+          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((it / kStages2) & 1) ^ 1), kWait)) {
+            failed = true;
+            break;
+          }
+          unsigned char* st = sm + s * kStage2Bytes;
+          const uint32_t lead_full = map_rank(smem_u32(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * kStage2Bytes);
+          tma_load_2d_pair(st, &tmA, kb * kBK, a_row, lead_full);
+          tma_load_2d_pair(st + kABytes, &tmB2, kb * kBK, b_row, lead_full);
+        }
+      }
+      if (failed) {
+        atomicAdd(&g_gemm_wait_timeouts, 1u);
+        if (leader)  // the pair's copies complete on the leader's barriers
+          for (int u = max(0, it - kStages2); u < it; ++u)
+            mbar_wait_bounded(&full[u % kStages2], (uint32_t)((u / kStages2) & 1), kWait);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int it = 0, jl = 0;
+      for (int t = pair; t < ntiles && !failed; t += npairs, ++jl) {
+        const TileInfo ti = tile_info<false>(p, t);
+        const int acc = jl & 1;
+        if (!mbar_wait_bounded(&tempty[acc], (uint32_t)(((jl >> 1) & 1) ^ 1), kWait)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const int nmma = (ti.nvalid + 15) & ~15;
+        const uint32_t idesc = umma_idesc_f16(ab_fmt, 2 * kBM, nmma, 0, 0);
+        const uint32_t d = tmem + (uint32_t)(acc * kBN);
+        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+          const int s = it % kStages2;
+          if (!mbar_wait_bounded(&full[s], (uint32_t)((it / kStages2) & 1), kWait)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sm + s * kStage2Bytes), b_addr = a_addr + kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_pair(d, umma_desc_sw128(a_addr + k * 32, 16, 1024), umma_desc_sw128(b_addr + k * 32, 16, 1024), idesc,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          const uint32_t e_local = smem_u32(&empty[s]);
+          umma_commit_pair(e_local);
+          umma_commit_pair(map_rank(e_local, 1));
+        }
+        if (failed) break;
+        const uint32_t f_local = smem_u32(&tfull[acc]);
+        umma_commit_pair(f_local);
+        umma_commit_pair(map_rank(f_local, 1));
+      }
+      umma_commit_pair(smem_u32(mdone));  // every MMA issued above, also on the failure path
+      if (!mbar_wait_bounded(mdone, 0, kWait)) failed = true;
+      if (failed) atomicAdd(&g_gemm_wait_timeouts, 1u);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int hcol = (warp - 2) >> 2;
+    unsigned char* mine = epi_smem + (warp - 2) * kEpiWarpSmem;
+    T* cws = reinterpret_cast<T*>(mine);
+    Stager sgr{mine + kCwBytes, 0};
+    int jl = 0;
+    for (int t = pair; t < ntiles; t += npairs, ++jl) {
+      TileInfo ti = tile_info<false>(p, t);
+      ti.m0 = (t / p.n_tiles) * (2 * kBM) + kBM * (int)rank;  // this CTA's 128 rows of the pair tile
+      const int acc = jl & 1;
+      const bool ok = mbar_wait_bounded(&tfull[acc], (uint32_t)((jl >> 1) & 1), kWait);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) atomicAdd(&g_gemm_wait_timeouts, 1u);
+        break;
+      }
+      tc_fence_after();
+      epilogue_tile<T, false>(p, ti, tmem + (uint32_t)(acc * kBN) + ((uint32_t)(q * 32) << 16), q, hcol, lane, cws,
+                              sgr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&tempty[acc]);
+        else
+          mbar_arrive_remote(map_rank(smem_u32(&tempty[acc]), 0));
+      }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync2();  // every MMA, copy and cross-CTA arrive of the pair is done
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
 int sm_count() {
   static int count[64] = {};
   static std::mutex mu;
@@ -710,14 +928,37 @@ int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t 
     MB_REQUIRE(sg.tma || sg.kind == EPI_STORE || sg.kind == EPI_GATE_RES || sg.kind == EPI_BETA_G, MB_ERR_ALIGN,
                "gemm: segment %d output needs 16-byte aligned rows (row stride a multiple of 8)", sidx);
   }
-  auto kern = p.prep ? gemm_tc_kernel<T, true> : gemm_tc_kernel<T, false>;
-  if (int e = ensure_smem_attr((const void*)kern, kSmemBytes)) return e;
   p.M = (int)M;
-  const int rows_per_tile = p.prep ? kPrepRows : kBM;
-  p.m_tiles = (int)((M + rows_per_tile - 1) / rows_per_tile);
   p.kblocks = (int)(K / kBK);
   p.n_tiles = 0;
   for (int s = 0; s < p.nseg; ++s) p.n_tiles += p.seg[s].tiles;
+  if (!p.prep) {  // CTA pairs on 256 x 256 tiles
+    CUtensorMap tmB2;
+    rc = encode_tile_map_2d(&tmB2, w, 2, (uint64_t)K, (uint64_t)wrows, (uint64_t)ldw * 2, kBK, kBN / 2, 128);
+    if (rc) return rc;
+    auto kern = gemm_pair_kernel<T>;
+    if (int e = ensure_smem_attr((const void*)kern, kSmemBytes)) return e;
+    p.m_tiles = (int)((M + 2 * kBM - 1) / (2 * kBM));
+    const int64_t ntiles = (int64_t)p.m_tiles * p.n_tiles;
+    const int npairs = (int)std::min<int64_t>(ntiles, sm_count() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(2 * npairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, tmA, tmB2, p);
+    return check_launch("gemm (CTA pairs)");
+  }
+  auto kern = gemm_tc_kernel<T, true>;
+  if (int e = ensure_smem_attr((const void*)kern, kSmemBytes)) return e;
+  p.m_tiles = (int)((M + kPrepRows - 1) / kPrepRows);
   const int64_t ntiles = (int64_t)p.m_tiles * p.n_tiles;
   const int grid = (int)std::min<int64_t>(ntiles, sm_count());
   kern<<<grid, kThreads, kSmemBytes, st>>>(tmA, tmA4, tmB, p);
