@@ -95,17 +95,17 @@ def kernel_work(name, cfg, B, T):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per unit of work, from one ncu
-# capture of each kernel on a smaller case of the same layer; traffic grows in proportion to the
-# units, so a full launch's traffic is this figure times its units.
+# capture of each kernel on a smaller case of the same layer (B = 4 x T = 4096); traffic grows in
+# proportion to the units, so a full launch's traffic is this figure times its units.
+#   gdn_prefill_ws  : per token-head, the layer's three kernels at B = 4
+#                     (profiles/gdn_split_b4_t4096.txt: UT transform 216.9 MB + state scan
+#                     202.6 MB + gated norm 114.4 MB = 533.9 MB / 196608)
 #   gdn_chunk_gated : per token-head, profiles/gdn_chunk_fast_b4_t4096.txt (186.2 MB / 196608)
-#   gdn_prefill_ws  : per token-head, profiles/gdn_split_b32_t4096.txt, the three kernels of
-#                     one launch at B = 32 (5059 MB / 1572864: the chunk records written and
-#                     read back are most of the excess over the algorithmic bytes)
-#   chord_attention : per token,      profiles/chord_tc_b4_t4096.txt (38.2 MB / 16384)
+#   chord_attention : per token, profiles/chord_tc_b4_t4096.txt (38.35 MB / 16384)
 NCU_TRAFFIC = {
     'motif_b200_gdn_chunk_gated': (186.15e6 / (4 * 4096 * 12), 'token_head'),
-    'motif_b200_gdn_prefill_ws': (5059.3e6 / (32 * 4096 * 12), 'token_head'),
-    'motif_b200_chord_attention': (38.19e6 / (4 * 4096), 'token'),
+    'motif_b200_gdn_prefill_ws': (533.9e6 / (4 * 4096 * 12), 'token_head'),
+    'motif_b200_chord_attention': (38.35e6 / (4 * 4096), 'token'),
 }
 
 

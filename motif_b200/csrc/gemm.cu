@@ -387,14 +387,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
   }
   if (sg.kind == EPI_SWIGLU) {
     // value columns [0, 128) and gate columns [128, 256) of the accumulator; this warp's outputs
-    // are its slice of [0, 128)
+    // are its slice of [0, 128).  The next chunk's TMEM columns load while this chunk is stored.
+    const int s_lo = h * (kBN / 2 / kColSplit), s_hi = (h + 1) * (kBN / 2 / kColSplit);
+    uint32_t rv[32], rg[32];
+    tmem_ld32(taddr + s_lo, rv);
+    tmem_ld32(taddr + kBN / 2 + s_lo, rg);
+    tmem_wait_ld(rv);
+    tmem_wait_ld(rg);
 #pragma unroll 1
-    for (int c = h * (kBN / 2 / kColSplit); c < (h + 1) * (kBN / 2 / kColSplit); c += 32) {
-      uint32_t rv[32], rg[32];
-      tmem_ld32(taddr + c, rv);
-      tmem_ld32(taddr + kBN / 2 + c, rg);
-      tmem_wait_ld(rv);
-      tmem_wait_ld(rg);
+    for (int c = s_lo; c < s_hi; c += 32) {
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -407,28 +408,35 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
         }
         w[i] = pack2<T>(o2[0], o2[1]);
       }
+      const bool more = c + 32 < s_hi;
+      if (more) {
+        tmem_ld32(taddr + c + 32, rv);
+        tmem_ld32(taddr + kBN / 2 + c + 32, rg);
+      }
       emit_chunk<PREP>(sgr, omap, ti.j * (kBN / 2) + c, y_box, w, lane);
+      if (more) {
+        tmem_wait_ld(rv);
+        tmem_wait_ld(rg);
+      }
     }
     return;
   }
   const int col0 = ti.j * kBN;
   T* dst = reinterpret_cast<T*>(sg.out) + (int64_t)r * sg.ldo + col0;
   const bool vec = (sg.ldo % 8 == 0) && (((uintptr_t)sg.out) % 16 == 0);
-  if (sg.kind == EPI_STORE && sg.tma) {
+  if (sg.kind == EPI_STORE && sg.tma) {  // the next chunk's TMEM columns load while this one is stored
+    if (c_lo >= c_hi) return;
+    uint32_t ra[32];
+    tmem_ld32(taddr + c_lo, ra);
+    tmem_wait_ld(ra);
 #pragma unroll 1
-    for (int c = c_lo; c < c_hi; c += 64) {
-      uint32_t r0[32], r1[32];
-      tmem_ld32(taddr + c, r0);
-      tmem_ld32(taddr + c + 32, r1);
-      tmem_wait_ld(r0);
-      tmem_wait_ld(r1);
+    for (int c = c_lo; c < c_hi; c += 32) {
       uint32_t w[16];
-      pack32<T>(r0, w);
+      pack32<T>(ra, w);
+      const bool more = c + 32 < c_hi;
+      if (more) tmem_ld32(taddr + c + 32, ra);
       emit_chunk<PREP>(sgr, omap, col0 + c, y_box, w, lane);
-      if (c + 32 < c_hi) {
-        pack32<T>(r1, w);
-        emit_chunk<PREP>(sgr, omap, col0 + c + 32, y_box, w, lane);
-      }
+      if (more) tmem_wait_ld(ra);
     }
     return;
   }
