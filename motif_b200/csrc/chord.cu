@@ -287,15 +287,38 @@ __global__ void __launch_bounds__(128) chord_fwd_mma_kernel(
 namespace tc {
 constexpr int kKeys = 128, kD = 64;
 constexpr int kTileBytes = 128 * kD * 2;  // 16 KB: 128 rows of 128 bytes
-constexpr int kStages = 3;
+constexpr int kStages = 4;  // a stage is released one tile late (after P V of that tile completes)
 constexpr uint32_t kWait = 1u << 22;
-constexpr uint32_t kTmemCols = 512;  // S: 2 x 128 columns, O: 2 x 64
+constexpr uint32_t kTmemCols = 512;  // per warpgroup: S 128 columns, P 64, O 64
 }  // namespace tc
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
+}
+// 32 consecutive 32-bit columns of this thread's TMEM lane (warp w of a warpgroup writes lanes
+// 32w .. 32w+31); complete after tmem_wait_st().
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// D[tmem] (+)= A[tmem] * B[smem]: A read from TMEM (K-major, two 16-bit values per column,
+// one row per lane), issued by one thread.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 // Barrier over the 128 threads of one warpgroup (ids 1 and 2; 0 is __syncthreads).
 __device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;\n" ::"r"(id) : "memory"); }
@@ -317,8 +340,7 @@ struct TcSmemLayout {
   static constexpr int offQ = 0;                          // 2 warpgroup tiles
   static constexpr int offK = offQ + 2 * tc::kTileBytes;  // kStages
   static constexpr int offV = offK + tc::kStages * tc::kTileBytes;
-  static constexpr int offP = offV + tc::kStages * tc::kTileBytes;  // 2 warpgroups x 2 atoms of 64 keys
-  static constexpr int offBias = offP + 4 * tc::kTileBytes;         // 2 warpgroups x 2 tiles
+  static constexpr int offBias = offV + tc::kStages * tc::kTileBytes;  // 2 warpgroups x 2 tiles
   static constexpr int offKm = offBias + 4 * G * TBLS * 4;          // key bias: 2 warpgroups x 2 tiles
   static constexpr int offBar = offKm + 4 * tc::kKeys * 4;
   static constexpr int nBar = 1 + tc::kStages + 6;  // q, kv[], s[2], o[2], drain[2]
@@ -391,7 +413,6 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   const float inv_rcs = 1.f / rcs;  // a key bias m (natural log) enters x as m log2(e) / |rc|
 
   unsigned char* sQw = sQ + wg * tc::kTileBytes;
-  unsigned char* sPw = sm + Lay::offP + wg * 2 * tc::kTileBytes;
   float* sBw = reinterpret_cast<float*>(sm + Lay::offBias) + wg * 2 * G * TBLS;
   float* sKmw = reinterpret_cast<float*>(sm + Lay::offKm) + wg * 2 * tc::kKeys;
 
@@ -408,7 +429,8 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sTmem;
-  const uint32_t colS = wg * tc::kKeys, colO = 2 * tc::kKeys + wg * tc::kD;
+  // TMEM columns of this warpgroup: S (128 fp32) | P (128 16-bit keys, 64 columns) | O (64 fp32)
+  const uint32_t colS = wg * 256, colP = colS + tc::kKeys, colO = colP + tc::kKeys / 2;
 
   auto issue_kv = [&](int j) {  // one thread
     const int s = j % NS;
@@ -425,12 +447,12 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
                   idS, ks > 0);
     umma_commit(&barS[wg]);
   };
-  auto issue_o = [&](int j) {  // warpgroup issuer: O_t = P_w V_j
-    const uint32_t pa = smem_u32(sPw), va = smem_u32(sV + (j % NS) * tc::kTileBytes);
+  auto issue_o = [&](int j) {  // warpgroup issuer: O (+)= P_w V_j, P from this warpgroup's TMEM
+    const uint32_t va = smem_u32(sV + (j % NS) * tc::kTileBytes);
 #pragma unroll
     for (int ks = 0; ks < tc::kKeys / 16; ++ks)
-      umma_f16_ss(tmem + colO, umma_desc_sw128(pa + (ks >> 2) * tc::kTileBytes + (ks & 3) * 32, 16, 1024),
-                  umma_desc_sw128(va + ks * 16 * 128, tc::kTileBytes, 1024), idO, ks > 0);
+      umma_f16_ts(tmem + colO, tmem + colP + ks * 8, umma_desc_sw128(va + ks * 16 * 128, tc::kTileBytes, 1024), idO,
+                  (j > 0 || ks > 0) ? 1u : 0u);
     umma_commit(&barO[wg]);
   };
   auto fill_bias = [&](int j) {  // warpgroup: table of tile j into buffer j & 1
@@ -466,11 +488,25 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
   }
 
-  float o[tc::kD];
-#pragma unroll
-  for (int i = 0; i < tc::kD; ++i) o[i] = 0.f;
-  float m = -INFINITY, l = 0.f;
+  // O accumulates in TMEM (P V with accumulate), exponentiated against a reference row max
+  // m_ref that is raised only when the tile's max exceeds it by more than 2^8 in the exponent:
+  // P entries stay below 256 (exact enough in 16 bits, far from fp32 overflow) and O is rescaled
+  // in TMEM on those rare tiles instead of every tile.
+  constexpr float kRescale = 8.f;
+  float m_ref = -INFINITY, l = 0.f;
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+  // the issuer releases the K/V stage of tile j once P V(j) has completed (checked at tile j + 1)
+  auto release = [&](int j) {
+    const int s = j % NS;
+    const int need = (j < nA) + (j < nB);
+    __threadfence_block();
+    const int prev = atomicAdd(&cnt[s], 1);
+    __threadfence_block();
+    if (prev + 1 == need) {
+      cnt[s] = 0;
+      if (j + NS < nall) issue_kv(j + NS);
+    }
+  };
 
   for (int j = 0; j < nmine; ++j) {
     bool ok = failed ? false : mbar_wait_bounded(&barS[wg], (uint32_t)(j & 1), tc::kWait);
@@ -533,34 +569,61 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int c = 0; c < tc::kKeys; c += 2) mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], x[c], x[c + 1]);
-    const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
-    const float mb = mn == -INFINITY ? 0.f : mn;
-    const float corr = ex2_approx((m - mb) * rcs);
-    const float nb = -mb * rcs;
-    m = mn;
+    const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+    // raise the reference max on the first visible key, or when this tile exceeds it by > 2^8
+    const bool raise = mt > m_ref && (m_ref == -INFINITY || (mt - m_ref) * rcs > kRescale);
+    float corr = 1.f;
+    if (raise) {
+      corr = m_ref == -INFINITY ? 0.f : ex2_approx((m_ref - mt) * rcs);
+      m_ref = mt;
+    }
+    const float nb = -(m_ref == -INFINITY ? 0.f : m_ref) * rcs;
     float2 ps4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-    // P row -> shared memory, swizzled: key chunk cc (8 keys) in atom cc / 8 at 16-byte slot
-    // (cc % 8) ^ (row % 8); the row sum accumulates in eight packed lanes
+    uint32_t pw0[32], pw1[32];  // P row packed in 16-bit pairs: keys 0..63, 64..127
 #pragma unroll
-    for (int cc = 0; cc < tc::kKeys / 8; ++cc) {
-      uint32_t w[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 t = ffma2(make_float2(x[cc * 8 + 2 * e], x[cc * 8 + 2 * e + 1]), make_float2(rcs, rcs),
-                               make_float2(nb, nb));
-        const float p0 = ex2_approx(t.x);
-        const float p1 = ex2_approx(t.y);
-        ps4[e] = fadd2(ps4[e], make_float2(p0, p1));
-        w[e] = pack2<T>(p0, p1);
-      }
-      unsigned char* dst = sPw + (cc >> 3) * tc::kTileBytes + wt * 128 + (((cc & 7) ^ (wt & 7)) << 4);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int c = 0; c < tc::kKeys; c += 2) {
+      const float2 t = ffma2(make_float2(x[c], x[c + 1]), make_float2(rcs, rcs), make_float2(nb, nb));
+      const float p0 = ex2_approx(t.x);
+      const float p1 = ex2_approx(t.y);
+      ps4[(c >> 1) & 3] = fadd2(ps4[(c >> 1) & 3], make_float2(p0, p1));
+      if (c < 64)
+        pw0[c >> 1] = pack2<T>(p0, p1);
+      else
+        pw1[(c - 64) >> 1] = pack2<T>(p0, p1);
     }
     {
       const float2 q = fadd2(fadd2(ps4[0], ps4[1]), fadd2(ps4[2], ps4[3]));
       l = l * corr + (q.x + q.y);
     }
-    fence_proxy_async_smem();
+    // P V(j - 1) has completed: its P columns may be overwritten, O may be rescaled, and its K/V
+    // stage released
+    if (j > 0) {
+      if (!mbar_wait_bounded(&barO[wg], (uint32_t)((j - 1) & 1), tc::kWait)) ok = false;
+      tc_fence_after();
+      if (issuer && !failed) release(j - 1);
+      if (__any_sync(0xffffffffu, raise)) {  // warp-collective: rows without a raise scale by 1
+        uint32_t o0[32], o1[32];
+        const uint32_t ta = tmem + lane_base + colO;
+        tmem_ld32(ta, o0);
+        tmem_ld32(ta + 32, o1);
+        tmem_wait_ld(o0);
+        tmem_wait_ld(o1);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float2 u0 = fmul2(make_float2(__uint_as_float(o0[i]), __uint_as_float(o0[i + 1])), make_float2(corr, corr));
+          const float2 u1 = fmul2(make_float2(__uint_as_float(o1[i]), __uint_as_float(o1[i + 1])), make_float2(corr, corr));
+          o0[i] = __float_as_uint(u0.x);
+          o0[i + 1] = __float_as_uint(u0.y);
+          o1[i] = __float_as_uint(u1.x);
+          o1[i + 1] = __float_as_uint(u1.y);
+        }
+        tmem_st32(ta, o0);
+        tmem_st32(ta + 32, o1);
+      }
+    }
+    tmem_st32(tmem + lane_base + colP, pw0);
+    tmem_st32(tmem + lane_base + colP + 32, pw1);
+    tmem_wait_st();
     tc_fence_before();
     if (wg_sync_or(1 + wg, !ok || failed)) {
       failed = true;
@@ -570,44 +633,15 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       tc_fence_after();
       issue_o(j);
     }
-    ok = mbar_wait_bounded(&barO[wg], (uint32_t)(j & 1), tc::kWait);
-    tc_fence_after();
-    {
-      uint32_t r0[32], r1[32];
-      const uint32_t ta = tmem + lane_base + colO;
-      tmem_ld32(ta, r0);
-      tmem_ld32(ta + 32, r1);
-      tmem_wait_ld(r0);
-      tmem_wait_ld(r1);
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const float2 a = ffma2(make_float2(o[i], o[i + 1]), make_float2(corr, corr),
-                               make_float2(__uint_as_float(r0[i]), __uint_as_float(r0[i + 1])));
-        const float2 b2 = ffma2(make_float2(o[32 + i], o[33 + i]), make_float2(corr, corr),
-                                make_float2(__uint_as_float(r1[i]), __uint_as_float(r1[i + 1])));
-        o[i] = a.x;
-        o[i + 1] = a.y;
-        o[32 + i] = b2.x;
-        o[33 + i] = b2.y;
-      }
-    }
-    tc_fence_before();
-    if (!ok) failed = true;  // reported at the next barrier
-    // this warpgroup is done with stage j % NS (its MMAs up to O_t(j) have completed); the
-    // last of the warpgroups that use tile j refills the stage
-    if (issuer && !failed) {
-      const int s = j % NS;
-      const int need = (j < nA) + (j < nB);
-      __threadfence_block();
-      const int prev = atomicAdd(&cnt[s], 1);
-      __threadfence_block();
-      if (prev + 1 == need) {
-        cnt[s] = 0;
-        if (j + NS < nall) issue_kv(j + NS);
-      }
-    }
   }
-  failed = __syncthreads_or(failed);
+  // the last P V of this warpgroup, then its stage
+  bool okO = true;
+  if (!failed && nmine > 0) {
+    okO = mbar_wait_bounded(&barO[wg], (uint32_t)((nmine - 1) & 1), tc::kWait);
+    tc_fence_after();
+    if (issuer && okO) release(nmine - 1);
+  }
+  failed = __syncthreads_or(failed || !okO);
   if (failed) {
     if (issuer) {  // every MMA this warpgroup issued
       umma_commit(&barDrain[wg]);
@@ -621,18 +655,31 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
         if (stage_tile[s] >= 0)
           mbar_wait_bounded(&barKV[s], (uint32_t)((stage_tile[s] / NS) & 1), tc::kWait);
     }
-  } else if (row_ok) {
-    const float inv = 1.f / fmaxf(l, 1e-20f);
+  } else if (nmine > 0) {
+    uint32_t o0[32], o1[32];
+    const uint32_t ta = tmem + lane_base + colO;
+    tmem_ld32(ta, o0);
+    tmem_ld32(ta + 32, o1);
+    tmem_wait_ld(o0);
+    tmem_wait_ld(o1);
+    if (row_ok) {
+      const float inv = 1.f / fmaxf(l, 1e-20f);
+      T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11];
+#pragma unroll
+      for (int c8 = 0; c8 < tc::kD / 8; ++c8) {
+        const uint32_t* src = c8 < 4 ? &o0[c8 * 8] : &o1[(c8 - 4) * 8];
+        uint4 v;
+        v.x = pack2<T>(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+        v.y = pack2<T>(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+        v.z = pack2<T>(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+        v.w = pack2<T>(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        *reinterpret_cast<uint4*>(orow + c8 * 8) = v;
+      }
+    }
+  } else if (row_ok) {  // no visible key (cannot happen for q_start >= 0): zeros
     T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11];
 #pragma unroll
-    for (int c8 = 0; c8 < tc::kD / 8; ++c8) {
-      uint4 v;
-      v.x = pack2<T>(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
-      v.y = pack2<T>(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
-      v.z = pack2<T>(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
-      v.w = pack2<T>(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
-      *reinterpret_cast<uint4*>(orow + c8 * 8) = v;
-    }
+    for (int c8 = 0; c8 < tc::kD / 8; ++c8) *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(0, 0, 0, 0);
   }
   tc_fence_before();
   __syncthreads();
