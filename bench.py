@@ -494,7 +494,63 @@ def run_ops(dev, pk, args):
     del a
     torch.cuda.empty_cache()
     out['gemm_shapes'] = run_gemm_shapes(dev, pk)
+    out['decode_gemm_shapes'] = {f'M={m}': run_decode_gemm_shapes(dev, pk, M=m) for m in (64, 8)}
     return out
+
+
+# config 5's products (M = 64 requests): name -> (N, K)
+DECODE_GEMM_SHAPES = {'gdn_in_proj': (8728, 768), 'gdn_out_proj': (768, 3584), 'chord_in_proj': (6016, 768),
+                      'chord_o_proj': (768, 768), 'chord_down_proj': (768, 2048), 'lm_head': (32000, 768)}
+
+
+def run_decode_gemm_shapes(dev, pk, M=64, reps=24):
+    """The skinny GEMM (`motif_b200_skinny_gemm` on fragment-packed weights) against the library
+    GEMM (torch.mm -> cuBLAS) on config 5's decode products at M rows (64: one GPU; 8: eight GPUs
+    of the strong split), bf16: each timed as a CUDA graph of
+    `reps` back-to-back products whose weights rotate through enough copies to exceed L2 twice
+    (every product streams its weight from HBM, as in the decode step)."""
+    from motif_b200 import _lib
+    from motif_b200.model import _skinny_packed
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    l2 = 126 << 20
+    for name, (N, K) in DECODE_GEMM_SHAPES.items():
+        wbytes = N * K * 2
+        copies = max(2, -(-2 * l2 // wbytes))
+        ws = [(torch.randn((N, K), device=dev, generator=g) * K ** -0.5).bfloat16() for _ in range(copies)]
+        ps = [_skinny_packed(w) for w in ws]
+        x = torch.randn((M, K), device=dev, generator=g).bfloat16()
+        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+
+        def ours():
+            for i in range(reps):
+                _lib.call('motif_b200_skinny_gemm', x.data_ptr(), K, ps[i % copies].data_ptr(), y.data_ptr(), N, M, N,
+                          K, 0, 0, _lib.MB_BF16, _lib.stream_ptr(dev))
+
+        def lib():
+            for i in range(reps):
+                torch.mm(x, ws[i % copies].t(), out=y)
+
+        r = {'M': M, 'N': N, 'K': K, 'weight_bytes': wbytes}
+        for tag, fn in (('ours', ours), ('cublas', lib)):
+            s_ = torch.cuda.Stream(dev)
+            s_.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s_):
+                fn()
+                torch.cuda.synchronize(dev)
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=s_):
+                    fn()
+            torch.cuda.current_stream(dev).wait_stream(s_)
+            ms = _time_ms(gr.replay, warm=3, iters=10) / reps
+            r[f'{tag}_us'] = ms * 1000.0
+            r[f'{tag}_weight_gbs'] = wbytes / (ms / 1000.0) / 1e9
+            del gr
+        r['ours_frac_of_measured_hbm'] = r['ours_weight_gbs'] / pk['hbm_gbs']
+        res[name] = r
+        del ws, ps, x, y
+        torch.cuda.empty_cache()
+    return res
 
 
 # config 4's projection shapes (M = 32 x 4096 tokens): name -> (N, K)

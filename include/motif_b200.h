@@ -311,21 +311,29 @@ MB_API int motif_b200_chord_decode_noalloc(const void* q, const void* k_cache, c
  * reference. */
 MB_API int motif_b200_wait_timeouts(uint32_t* count);
 
-/* Y[M, N] = X[M, K] . W[N, K]^T for a small token count (decode: 1 <= M <= 64), 16-bit
- * operands, fp32 accumulation, row strides ldx / ldw / ldy (elements; K a multiple of 64,
- * ldx and ldw multiples of 8, X and W 16-byte aligned; other K: MB_ERR_UNSUPPORTED).
- * Streams W once on the tensor cores; when N is small, K is split across the CTAs of a
- * cluster and the partial tiles are summed in a fixed order through distributed shared
- * memory, so results are deterministic.  Needs no workspace: the workspace query returns 0
- * and `workspace` / `workspace_bytes` are accepted and ignored (kept for callers that pass
- * one).  Launched with programmatic dependent launch: W may stream while the previous
- * kernel on the stream finishes; X is read and Y written only after it has ended.
- * Replaces the decode-time nn.Linear products (decoder.py, mlp.py, motif.py lm_head) that
- * cuBLAS runs as weight-bandwidth-bound small-M GEMMs. */
-MB_API int64_t motif_b200_skinny_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
-MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
-                           int64_t ldy, int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
-                           int64_t workspace_bytes, void* stream);
+/* Decode-sized products Y[M, N] = X[M, K] . W[N, K]^T, 1 <= M <= 64, 16-bit operands, fp32
+ * accumulation, on a weight packed once in tensor-core fragment order.
+ *
+ * motif_b200_skinny_packed_bytes(N, K): size of the packed copy of W (N rounded up to 32
+ *   features; -1 if K is not a positive multiple of 16).
+ * motif_b200_skinny_pack: W [N, K] (row stride ldw elements, even, W 4-byte aligned) into
+ *   `packed` (16-byte aligned, motif_b200_skinny_packed_bytes(N, K) bytes).  Asynchronous on
+ *   `stream`.  Pack again after changing W.
+ * motif_b200_skinny_gemm: Y (row stride ldy; N and ldy multiples of 4, Y 8-byte aligned) from
+ *   X (row stride ldx, a multiple of 8, 16-byte aligned) and the packed W; K a multiple of 16.
+ *   Each warp loads its weight blocks straight from HBM into the registers the MMA reads
+ *   before waiting on the previous kernel (programmatic dependent launch); K is split across
+ *   the warps of a CTA and across the CTAs of a cluster (at most 8), with the partial tiles
+ *   summed in a fixed order, so results are deterministic.  k_warps (1, 2 or 4) and split_k
+ *   (1 .. 8) force the split; 0 lets the library choose.  Other shapes: MB_ERR_UNSUPPORTED.
+ * Replaces the decode-time nn.Linear products (gdn_attn.py:88-94, chord_attn.py:88-96,
+ * mlp.py:52-53, the decoders' o_proj / down_proj, motif.py lm_head) that cuBLAS runs as
+ * weight-bandwidth-bound small-M GEMMs. */
+MB_API int64_t motif_b200_skinny_packed_bytes(int64_t N, int64_t K);
+MB_API int motif_b200_skinny_pack(const void* w, int64_t ldw, int64_t N, int64_t K, void* packed, int dtype,
+                                  void* stream);
+MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* packed, void* y, int64_t ldy, int64_t M,
+                                  int64_t N, int64_t K, int k_warps, int split_k, int dtype, void* stream);
 
 /* ------------------------------------------------------------------ dense projections
  * Y = X . W^T for 16-bit X [M, K] and W [N, K] (row strides ldx / ldw in elements, multiples of

@@ -77,8 +77,9 @@ SIGNATURES = {
                                       _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I, _P]),
     'motif_b200_gemm_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I,
                                            _P]),
-    'motif_b200_skinny_gemm_workspace_bytes': (_I64, [_I64, _I64, _I64]),
-    'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _I64, _P]),
+    'motif_b200_skinny_packed_bytes': (_I64, [_I64, _I64]),
+    'motif_b200_skinny_pack': (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
+    'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P]),
     'motif_b200_gdn_prefill_ws': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64,
                                        _I64, _I64, _I, _P, _I64, _P]),
     'motif_b200_gdn_chunk_workspace_bytes': (_I64, [_I64, _I64, _I64, _I64, _I64, _I]),
@@ -145,7 +146,7 @@ def ptr(t):
 KERNELS_PER_CALL = {n: 1 for n in SIGNATURES}
 KERNELS_PER_CALL.update({'motif_b200_last_error': 0, 'motif_b200_abi_version': 0,
                          'motif_b200_chord_workspace_bytes': 0, 'motif_b200_chord_decode_workspace_bytes': 0,
-                         'motif_b200_skinny_gemm_workspace_bytes': 0, 'motif_b200_gdn_chunk_workspace_bytes': 0,
+                         'motif_b200_skinny_packed_bytes': 0, 'motif_b200_gdn_chunk_workspace_bytes': 0,
                          'motif_b200_wait_timeouts': 0, 'motif_b200_testing_force': 0,
                          'motif_b200_chord_decode': 2, 'motif_b200_chord_decode_noalloc': 2,
                          'motif_b200_chord_decode_masked': 2,

@@ -1341,6 +1341,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(128) chord_merge_kernel(const float* __restrict__ ws, T* __restrict__ out,
                                                           int64_t os, int B, int H, int Tn, int nsplit) {
   constexpr int OD = D / 32;
+  allow_dependent_launch();  // the decoder's down / output projections may start fetching weights
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);  // (b * Tn + t) * H + h
   if (row >= (int64_t)B * Tn * H) return;

@@ -116,6 +116,14 @@ __device__ __forceinline__ float l2_scale(float ss, float scale) { return scale 
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 // ------------------------------------------------------------------ PTX wrappers
+// Programmatic dependent launch: a kernel launched after this one with the programmatic
+// stream serialization attribute (the decode-time skinny GEMM) may start now, on the SMs this
+// kernel leaves free; it fetches its weights and then waits (griddepcontrol.wait) for this
+// kernel to complete before it reads anything this kernel writes.  No effect on a dependent
+// launched without the attribute.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

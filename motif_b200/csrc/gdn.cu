@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(2 * DV) gdn_decode_split_kernel(
     float eps, SwigluRole<T> sw, int main_blocks) {
   static_assert(DV == 2 * DK, "one conv channel per thread needs Dv == 2 Dk");
   constexpr int NT = 2 * DV, HR = DK / 2;
+  allow_dependent_launch();  // the decoder's output projection may start fetching its weights
   if ((int)blockIdx.x >= main_blocks) {  // trailing CTAs: the decoder's SwiGLU activation
     swiglu_role_run<T>(sw, (int64_t)(blockIdx.x - main_blocks) * NT + threadIdx.x,
                        (int64_t)(gridDim.x - main_blocks) * NT);

@@ -294,6 +294,7 @@ __global__ void __launch_bounds__(32 * kMaxSrc) attn_res_norm_src_kernel(
   constexpr int D = 256 * NV, G = D / 8;
   __shared__ uint4 xs[kMaxSrc][G];
   __shared__ float lg[kMaxSrc], red[kMaxSrc];
+  allow_dependent_launch();  // the decoder's input projection may start fetching its weights
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = blockIdx.x;
   const bool mix = q != nullptr && n_src > 1;

@@ -1,73 +1,59 @@
 // Y[M, N] = X[M, K] . W[N, K]^T for a small token count M (decode: one row per sequence,
 // M <= 64), 16-bit operands, fp32 accumulation.  At decode every nn.Linear of the model is
-// such a product and its cost is streaming W once from HBM (the activations are a few
-// hundred KB and stay in L2).
+// such a product and its cost is streaming W once from HBM: the activations are a few hundred
+// KB and stay in L2, the weights (1-49 MB per product) do not.
 //
-// The product is computed transposed on the 5th-generation tensor cores: Y^T = W . X^T, so a
-// CTA's 128 output features are the MMA's M = 128 rows and the (up to 64) tokens its N.  A
-// CTA owns 128 consecutive rows of W and one slice of K; thread 0 streams 64-wide K chunks of
-// W (128 x 64) and X (64 x 64) by tiled TMA (128-byte swizzle, rows past N or M read as zeros)
-// into a 4-stage ring and issues four tcgen05.mma (K = 16 each) per chunk into a 64-column
-// TMEM accumulator; a stage is refilled once the MMAs that read it have completed
-// (tcgen05.commit on the stage's mbarrier).
+// * W is packed once (motif_b200_skinny_pack) in the register order of the mma.m16n8k16 A
+//   operand: for each block of 16 features x 16 K, lane l's four A registers are 16 contiguous
+//   bytes.  A warp's run of k-tiles of one feature block is one contiguous range, fetched by ONE
+//   bulk copy (the TMA engine, not the load/store unit) into shared memory, from where each lane
+//   reads its fragment with one conflict-free 16-byte load.
+// * Y^T = W . X^T: features are the MMA's M (a warp owns 2 blocks = 32 features), tokens its N
+//   (M / 8 n-tiles).  X rows of the CTA's K range arrive by bulk copies too, and X^T fragments
+//   are read by ldmatrix.
+// * The W copies are issued first, before the kernel waits on its predecessor (programmatic
+//   dependent launch: W is a weight and does not depend on earlier kernels), so the HBM latency
+//   overlaps the end of the previous kernel; X is fetched after the wait.
+// * K is split two ways so that every shape fills the GPU with enough bytes in flight: across
+//   the 1, 2 or 4 warps of a CTA that share its features (summed in shared memory), and across
+//   the CTAs of a thread-block cluster (up to 8 along y).  Between CTAs, CTA r owns a slice of
+//   the tile's token rows: after one cluster barrier it reads that slice of every CTA's partial
+//   through distributed shared memory, all S reads of a vector in flight together, and adds
+//   them in split order.  The summation order is fixed, so results do not depend on timing.
 //
-// When the feature blocks alone cannot fill the GPU (768 outputs at K up to 3584), K is split
-// across the CTAs of a thread-block cluster (up to 16 along y).  Each CTA reads its
-// accumulator back with tcgen05.ld (thread = feature, one register per token) into a fp32
-// [token][feature] tile in its own shared memory.  The tile's float4 groups are cut into
-// nsplit slices, CTA p owning slice p: after a cluster barrier every CTA sends slice p of
-// its tile to CTA p with one shared::cta -> shared::cluster bulk copy (completion counted on
-// p's receive barrier), then sums its own slice over the splits in split order (a fixed
-// order: results do not depend on timing) and writes it to Y.  No workspace, no atomics.
-// An unsplit launch (a cluster of one) writes Y straight from the accumulator registers.
-// Every mbarrier wait is bounded; a CTA whose wait runs out counts itself
-// (motif_b200_wait_timeouts), drains what it issued and still takes both cluster barriers.
+// The host picks the split that runs in the fewest waves with the most CTAs (ties: more
+// features per CTA, then fewer splits); callers may force it (k_warps, split_k).  Every wait on
+// a copy is bounded: a CTA whose wait runs out counts itself (motif_b200_wait_timeouts), waits
+// once more for its copies and carries on with what it has.
+// Replaces the decode-time nn.Linear products (gdn_attn.py:88-94, chord_attn.py:88-96,
+// mlp.py:52-53, decoder.py o_proj / down_proj, motif.py lm_head), which cuBLAS runs as
+// weight-bandwidth-bound small-M GEMMs.
 #include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
+#include "gdn_mma.cuh"
 
 namespace mb {
 
 __device__ unsigned int g_sk_wait_timeouts = 0;
 
+int read_and_clear_skinny_timeouts(unsigned int* count) {
+  unsigned int zero = 0;
+  if (cudaMemcpyFromSymbol(count, g_sk_wait_timeouts, sizeof(*count)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_sk_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
+    return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
+  return MB_OK;
+}
+
 namespace {
 
-constexpr int kBN = 128;        // output features per CTA (MMA M)
-constexpr int kBK = 64;         // K per swizzle atom: one 128-byte row
-constexpr int kMaxM = 64;       // tokens (MMA N)
-#ifndef SK_STAGES
-#define SK_STAGES 4
-#endif
-#ifndef SK_ATOMS
-#define SK_ATOMS 1
-#endif
-#ifndef SK_MINB
-#define SK_MINB 2
-#endif
-#ifndef SK_ROT
-#define SK_ROT 1
-#endif
-#ifndef SK_PDL
-#define SK_PDL 1
-#endif
-constexpr int kStages = SK_STAGES;
-constexpr int kAtoms = SK_ATOMS;  // 64-wide K atoms per stage (one TMA box each)
-constexpr int kMaxSplit = 16;   // cluster size limit (16 needs the non-portable opt-in)
-constexpr int kWAtom = kBN * kBK * 2;      // 16 KB
-constexpr int kXAtom = kMaxM * kBK * 2;    // 8 KB
-constexpr int kWBytes = kAtoms * kWAtom;
-constexpr int kStageBytes = kAtoms * (kWAtom + kXAtom);
-constexpr int kTileBytes = kMaxM * kBN * 4;  // fp32 partial tile, reuses the ring
-// the partial tile and the receive buffer of the split-K exchange both reuse the ring
-static_assert(2 * kTileBytes <= kStages * kStageBytes, "partial tile and receive buffer must fit the ring");
-constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 16 + 16 + 1024;  // + 1024-byte alignment
+constexpr int kWarps = 4;           // warps per CTA
+constexpr int kThreads = kWarps * 32;
+constexpr int kKtw = 12;            // most k-tiles (16 deep) one warp takes
+constexpr int kMaxCluster = 8;      // portable cluster size
 constexpr uint32_t kWait = 1u << 22;
-constexpr uint32_t kTmemCols = 64;
 
-__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
-  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
-}
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
@@ -77,329 +63,391 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
   return r;
 }
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+// Pack W [N, K] (row stride ldw) into A-fragment order: block (fb, kt) of 16 features x 16 K
+// at element offset (fb * KT + kt) * 256; lane l (g = l / 4, t = l % 4) holds
+//   W[16 fb + g][16 kt + 2t .. +1], W[16 fb + g + 8][16 kt + 2t .. +1],
+//   W[16 fb + g][16 kt + 2t + 8 .. +9], W[16 fb + g + 8][16 kt + 2t + 8 .. +9].
+// Features past N (up to the next multiple of 32) are zeros.
 template <typename T>
-__global__ void __launch_bounds__(128, SK_MINB) skinny_tc_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                           const __grid_constant__ CUtensorMap tmX,
-                                                           T* __restrict__ Y, int64_t ldy, int M, int N,
-                                                           int kchunks_per_split, int kchunks, int katoms,
-                                                           int vec_store) {
-  constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  constexpr uint32_t idesc = umma_idesc_f16(ab_fmt, kBN, kMaxM, 0, 0);
-  extern __shared__ unsigned char sk_smem_raw[];
-  unsigned char* sm = sk_smem_raw + ((1024u - (smem_u32(sk_smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* done = empty + kStages;
-  uint64_t* recvbar = done + 1;  // split-K: the other splits' slices of this CTA's part of the tile
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(recvbar + 1);
+__global__ void skinny_pack_kernel(const T* __restrict__ w, int64_t ldw, int N, int KT, int NB, uint4* __restrict__ out) {
+  const int64_t total = (int64_t)NB * KT * 32;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int lane = (int)(i & 31);
+    const int64_t blk = i >> 5;
+    const int kt = (int)(blk % KT), fb = (int)(blk / KT);
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = fb * 16 + g, r1 = r0 + 8;
+    const int c0 = kt * 16 + 2 * t, c1 = c0 + 8;
+    auto pair = [&](int r, int c) -> uint32_t {
+      if (r >= N) return 0u;
+      return *reinterpret_cast<const uint32_t*>(w + (int64_t)r * ldw + c);
+    };
+    out[i] = make_uint4(pair(r0, c0), pair(r1, c0), pair(r0, c1), pair(r1, c1));
+  }
+}
+
+// Shared-memory plan of one launch (bytes): [W: kWarps x 2 x kwn blocks | X: ROWS x XS] with the
+// partial tiles [wk][ROWS][PF] fp32 over them once the products are done, then the barriers.
+struct Plan {
+  int rows, kwn, xs, pf;
+  size_t off_x, off_bar, bytes;
+};
+__host__ __device__ inline Plan make_plan(int ntt, int M, int wk, int kc, int S) {
+  Plan p;
+  p.rows = ntt < 2 ? 16 : ntt * 8;  // token rows staged (x4 ldmatrix reads 16)
+  p.kwn = (kc + wk - 1) / wk;
+  p.xs = kc * 16 + 8;               // X row stride (elements): rows on distinct 16-byte bank groups
+  p.pf = (kWarps / wk) * 32 + 4;    // partial row stride (floats): conflict-free fragment stores
+  const size_t wb = (size_t)kWarps * 2 * p.kwn * 512;
+  p.off_x = wb;
+  const size_t ab = wb + (size_t)p.rows * p.xs * 2;
+  const size_t pb = (size_t)wk * p.rows * p.pf * 4;
+  p.off_bar = ((ab > pb ? ab : pb) + 15) / 16 * 16;
+  p.bytes = p.off_bar + (kWarps + 1) * 8;
+  return p;
+}
+
+// One CTA: kWarps / wk feature groups of 32 (warp w: group w % wf, K part w / wf) over the
+// CTA's K range [s kc, s kc + kc) of split s = blockIdx.y (the cluster's rank).
+template <typename T, int NTT>
+__global__ void __launch_bounds__(kThreads)
+    skinny_kernel(const T* __restrict__ X, int64_t ldx, const uint4* __restrict__ P, int KT, int NG,
+                  T* __restrict__ Y, int64_t ldy, int M, int N, int wk, int kc) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = gridDim.y, s = blockIdx.y;
+  const Plan pl = make_plan(NTT, M, wk, kc, S);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nb = blockIdx.x, ks = blockIdx.y, nsplit = gridDim.y;
-  const int n0 = nb * kBN;
-  const int c_begin = ks * kchunks_per_split, c_end = min(kchunks, c_begin + kchunks_per_split);
-  const int nc = max(0, c_end - c_begin);
+  const int gq = lane >> 2, tq = lane & 3;
+  const int wf = kWarps / wk;
+  const int fw = warp % wf, kw = warp / wf;
+  const int group = blockIdx.x * wf + fw;
+  const int kbeg = s * kc, kend = min(KT, kbeg + kc);
+  const int wbeg = kbeg + kw * pl.kwn, wend = min(kend, wbeg + pl.kwn);
+  const int nk = group < NG ? max(0, wend - wbeg) : 0;
+  uint4* sW = reinterpret_cast<uint4*>(smem) + (size_t)warp * 2 * pl.kwn * 32;  // this warp's [2][kwn][32]
+  T* sX = reinterpret_cast<T*>(smem + pl.off_x);
+  uint64_t* wbar = reinterpret_cast<uint64_t*>(smem + pl.off_bar);
+  uint64_t* xbar = wbar + kWarps;
 
-  // Programmatic dependent launch: the next kernel in the stream may start its own prologue
-  // now; this kernel waits for its predecessor only before the first read of X (W is a
-  // weight, independent of earlier kernels).
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  if (tid == 0) {
-    prefetch_tmap(&tmW);
-    prefetch_tmap(&tmX);
-  }
-  if (warp == 0) tmem_alloc(sTmem, kTmemCols);
-  if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    mbar_init(done, 1);
-    mbar_init(recvbar, 1);
+  // every CTA of the cluster has started before any reads of another's shared memory (the
+  // matching wait is just before the exchange)
+  if (S > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+  // 1. this warp's W: two contiguous runs (its two feature blocks), one bulk copy each; each
+  //    warp initialises its own barrier (warp 0 also the one of X), so nothing waits for the CTA
+  if (lane == 0) {
+    mbar_init(&wbar[warp], 1);
+    if (warp == 0) mbar_init(xbar, 1);
     mbar_init_fence();
-    if (nsplit > 1) {  // the bytes the other nsplit - 1 CTAs of the cluster will send here
-      const int G = M * (kBN / 4), r = (int)cluster_rank();
-      const int len = (r + 1) * G / nsplit - r * G / nsplit;
-      mbar_arrive_expect_tx(recvbar, (uint32_t)((nsplit - 1) * len * 16));
+    if (nk > 0) {
+      const uint4* src = P + ((int64_t)(2 * group) * KT + wbeg) * 32;
+      mbar_arrive_expect_tx(&wbar[warp], (uint32_t)(2 * nk * 512));
+      bulk_load(sW, src, (uint32_t)(nk * 512), &wbar[warp]);
+      bulk_load(sW + pl.kwn * 32, src + (int64_t)KT * 32, (uint32_t)(nk * 512), &wbar[warp]);
+    } else {
+      mbar_arrive_expect_tx(&wbar[warp], 0u);
     }
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *sTmem;
-
-  // Two single-thread roles: thread 0 of warp 0 streams chunks into the ring (a stage is
-  // refilled as soon as the MMAs that read it complete), thread 0 of warp 1 issues the MMAs.
-  // The other lanes of both warps park at __syncwarp rather than spinning in a divergent branch.
-  bool failed = false;
-  // Feature blocks start their K walk at different chunks (block nb at nb mod nc), so the CTAs
-  // in flight read different column ranges of W at any moment instead of all hitting the same
-  // 128-byte column of every row.  The order is fixed per block: results stay deterministic.
-  const int rot = SK_ROT ? nb % max(nc, 1) : 0;
-  auto chunk_of = [&](int c) { return c_begin + (c + rot) % nc; };
-  auto atoms_of = [&](int c) { return min(kAtoms, katoms - chunk_of(c) * kAtoms); };
-  if (tid == 0) {
-    // the first ring's worth of W before waiting on the predecessor grid, then its X
-    const int first = min(nc, kStages);
-    for (int c = 0; c < first; ++c) {
-      const int na = atoms_of(c), a0 = chunk_of(c) * kAtoms;
-      mbar_arrive_expect_tx(&full[c], (uint32_t)(na * (kWAtom + kXAtom)));
-      for (int a = 0; a < na; ++a) tma_load_2d(sm + c * kStageBytes + a * kWAtom, &tmW, (a0 + a) * kBK, n0, &full[c]);
-    }
-    asm volatile("griddepcontrol.wait;\n" ::: "memory");
-    for (int c = 0; c < first; ++c) {
-      const int na = atoms_of(c), a0 = chunk_of(c) * kAtoms;
-      for (int a = 0; a < na; ++a)
-        tma_load_2d(sm + c * kStageBytes + kWBytes + a * kXAtom, &tmX, (a0 + a) * kBK, 0, &full[c]);
-    }
-    int issued = first;
-    for (; issued < nc; ++issued) {
-      const int s = issued % kStages;
-      if (!mbar_wait_bounded(&empty[s], (uint32_t)((issued / kStages - 1) & 1), kWait)) {
-        failed = true;
-        break;
-      }
-      unsigned char* st = sm + s * kStageBytes;
-      const int na = atoms_of(issued), a0 = chunk_of(issued) * kAtoms;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(na * (kWAtom + kXAtom)));
-      for (int a = 0; a < na; ++a) tma_load_2d(st + a * kWAtom, &tmW, (a0 + a) * kBK, n0, &full[s]);
-      for (int a = 0; a < na; ++a) tma_load_2d(st + kWBytes + a * kXAtom, &tmX, (a0 + a) * kBK, 0, &full[s]);
-    }
-    // the last copy into each stage has landed before the ring is reused (bounded)
-    for (int u = max(0, issued - kStages); u < issued; ++u)
-      if (!mbar_wait_bounded(&full[u % kStages], (uint32_t)((u / kStages) & 1), kWait)) failed = true;
-  } else if (tid == 32) {
-    for (int c = 0; c < nc; ++c) {
-      const int s = c % kStages;
-      if (!mbar_wait_bounded(&full[s], (uint32_t)((c / kStages) & 1), kWait)) {
-        failed = true;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t wa = smem_u32(sm + s * kStageBytes), xa = wa + kWBytes;
-      const int na = atoms_of(c);
-      for (int a = 0; a < na; ++a)
-#pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)
-          umma_f16_ss(tmem, umma_desc_sw128(wa + a * kWAtom + k * 32, 16, 1024),
-                      umma_desc_sw128(xa + a * kXAtom + k * 32, 16, 1024), idesc, (c > 0 || a > 0 || k > 0) ? 1u : 0u);
-      umma_commit(&empty[s]);
-    }
-    umma_commit(done);  // every MMA issued above (a failed CTA drains them here too)
-  }
-  if (warp < 2) __syncwarp();
-  if (failed) atomicAdd(&g_sk_wait_timeouts, 1u);
-  // the accumulator is complete (or the CTA failed and drains)
-  const bool ok = mbar_wait_bounded(done, 0, kWait);
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");  // Y is written only after the predecessor ends
-  failed = __syncthreads_or(failed || !ok);
-  tc_fence_after();
-  const int f = warp * 32 + lane;  // this thread's feature within the block (TMEM lane)
-  const bool have = nc > 0 && !failed;
-  uint32_t r0[32], r1[32];
-  {
-    const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
-    tmem_ld32(ta, r0);
-    tmem_ld32(ta + 32, r1);
-    tmem_wait_ld(r0);
-    tmem_wait_ld(r1);
-  }
-  tc_fence_before();
-  __syncthreads();
+  // 2. the predecessor's output (X) is complete past this point; let the next kernel start
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  // 3. X rows [0, M) x the CTA's K range (rows past M are never stored, so they stay as they are)
   if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    const uint32_t rb = (uint32_t)(kend - kbeg) * 32;
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(xbar, rb * (uint32_t)M);
+    __syncwarp();
+    for (int r = lane; r < M; r += 32) bulk_load(sX + (size_t)r * pl.xs, X + (int64_t)r * ldx + (int64_t)kbeg * 16, rb, xbar);
   }
-  if (tid == 0 && !ok) atomicAdd(&g_sk_wait_timeouts, 1u);
+  __syncthreads();  // the barriers' initialisation is visible to every warp before it waits
+  bool ok = mbar_wait_bounded(xbar, 0, kWait);
+  ok = mbar_wait_bounded(&wbar[warp], 0, kWait) && ok;
+  if (!ok) {  // count it, then give the copies one more bounded wait before the memory is reused
+    if (lane == 0) atomicAdd(&g_sk_wait_timeouts, 1u);
+    mbar_wait_bounded(xbar, 0, kWait);
+    mbar_wait_bounded(&wbar[warp], 0, kWait);
+  }
 
-  if (nsplit == 1) {  // unsplit: each thread writes its feature's column, a warp 32 adjacent features
-    const int n = n0 + f;
-    if (n < N) {
+  // 4. the products: acc[f][n] = Y^T block (16 features of block f) x (8 tokens of n-tile n)
+  float acc[2][NTT][4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < M) Y[(int64_t)i * ldy + n] = from_f<T>(have ? __uint_as_float(r0[i]) : 0.f);
+  for (int f = 0; f < 2; ++f)
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (32 + i < M) Y[(int64_t)(32 + i) * ldy + n] = from_f<T>(have ? __uint_as_float(r1[i]) : 0.f);
+    for (int n = 0; n < NTT; ++n) acc[f][n][0] = acc[f][n][1] = acc[f][n][2] = acc[f][n][3] = 0.f;
+  const int kofs = (wbeg - kbeg) * 16;
+  for (int j = 0; j < nk; ++j) {
+    uint32_t b[NTT < 2 ? 2 : NTT][2];
+#pragma unroll
+    for (int n = 0; n < (NTT < 2 ? 2 : NTT); n += 2) {
+      uint32_t r[4];
+      gdnk::ldb_n(r, sX, pl.xs, kofs + j * 16, n * 8);
+      b[n][0] = r[0];
+      b[n][1] = r[1];
+      b[n + 1][0] = r[2];
+      b[n + 1][1] = r[3];
     }
+#pragma unroll
+    for (int f = 0; f < 2; ++f) {
+      const uint4 w4 = sW[(f * pl.kwn + j) * 32 + lane];
+      const uint32_t a[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int n = 0; n < NTT; ++n) mma_16816<T>(acc[f][n], a, b[n]);
+    }
+  }
+  __syncthreads();  // every warp is done with W and X before the partial tiles overwrite them
+
+  // 5. partial tiles [wk][ROWS][PF] (token-major), the CTA's K parts summed into part 0 in order
+  const int PF = pl.pf, ROWS = pl.rows;
+  float* sP = reinterpret_cast<float*>(smem);
+  {
+    float* part = sP + (size_t)kw * ROWS * PF;
+#pragma unroll
+    for (int f = 0; f < 2; ++f)
+#pragma unroll
+      for (int n = 0; n < NTT; ++n) {
+        const int fl = fw * 32 + f * 16 + gq, t0 = n * 8 + 2 * tq;
+        part[t0 * PF + fl] = acc[f][n][0];
+        part[(t0 + 1) * PF + fl] = acc[f][n][1];
+        part[t0 * PF + fl + 8] = acc[f][n][2];
+        part[(t0 + 1) * PF + fl + 8] = acc[f][n][3];
+      }
+  }
+  __syncthreads();
+  const int VR = wf * 8;  // float4 vectors per token row of the tile
+  const int V = M * VR;
+  auto tile_vec = [&](int v) {
+    const int t = v / VR, c = (v % VR) * 4;
+    float4 a = *reinterpret_cast<const float4*>(&sP[t * PF + c]);
+    for (int p = 1; p < wk; ++p) {
+      const float4 q = *reinterpret_cast<const float4*>(&sP[(size_t)p * ROWS * PF + t * PF + c]);
+      a.x += q.x;
+      a.y += q.y;
+      a.z += q.z;
+      a.w += q.w;
+    }
+    return a;
+  };
+  const int n0 = blockIdx.x * wf * 32;
+  auto store = [&](int t, int c, float4 a) {
+    if (n0 + c >= N) return;
+    uint2 o;
+    o.x = pack2<T>(a.x, a.y);
+    o.y = pack2<T>(a.z, a.w);
+    *reinterpret_cast<uint2*>(Y + (int64_t)t * ldy + n0 + c) = o;
+  };
+  if (S == 1) {
+    for (int v = tid; v < V; v += kThreads) store(v / VR, (v % VR) * 4, tile_vec(v));
     return;
   }
-  float* tile = reinterpret_cast<float*>(sm);  // [token][feature] partial, the ring is free now
-  float* recv = tile + kMaxM * kBN;            // [nsplit][slice] received partials
+  // 6. exchange: CTA r owns token rows [r M / S, (r + 1) M / S) of the tile; after one cluster
+  //    barrier it reads those rows of every CTA's summed partial (its own included) and adds
+  //    them in split order.  Each thread fetches all S copies of its vectors before adding, so
+  //    the remote reads overlap instead of paying one round trip each.
+  if (wk > 1) {  // the CTA's own K parts summed into part 0 first
+    for (int v = tid; v < V; v += kThreads) {
+      const int t = v / VR, c = (v % VR) * 4;
+      *reinterpret_cast<float4*>(&sP[t * PF + c]) = tile_vec(v);
+    }
+  }
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");  // every CTA has started
+  cluster_sync_all();  // every CTA's part 0 is complete
+  const int r = (int)cluster_rank();
+  const int ta = r * M / S, tb = (r + 1) * M / S;
+  for (int v0 = ta * VR + tid; v0 < tb * VR; v0 += 2 * kThreads) {
+    float4 q[2][kMaxCluster];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    if (i < M) tile[i * kBN + f] = have ? __uint_as_float(r0[i]) : 0.f;
-    if (32 + i < M) tile[(32 + i) * kBN + f] = have ? __uint_as_float(r1[i]) : 0.f;
-  }
-  fence_proxy_async_smem();  // the tile is read by bulk copies (async proxy)
-  // every CTA of the cluster has written its tile and is done with its ring (so its receive
-  // buffer may be written), and its receive barrier is initialised
-  cluster_sync_all();
-  // Reduce-scatter through distributed shared memory: the float4 groups of the [M][128] tile
-  // are cut into nsplit contiguous slices; CTA p owns slice p.  Thread 0 sends slice p of
-  // this tile to CTA p with one bulk copy each (the copy engine moves the bytes, completion
-  // counted on p's receive barrier); then every CTA sums its slice over the splits in split
-  // order (deterministic) and writes it to Y.
-  const int rank = (int)cluster_rank();
-  const int G = M * (kBN / 4);
-  auto g_lo = [&](int p) { return p * G / nsplit; };
-  if (tid == 0) {
-    const uint32_t tile_a = smem_u32(tile), recv_a = smem_u32(recv), bar_a = smem_u32(recvbar);
-    for (int p = 0; p < nsplit; ++p) {
-      if (p == rank) continue;
-      const int lo = g_lo(p), len = g_lo(p + 1) - lo;
-      uint32_t dst, bar;
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(dst) : "r"(recv_a + (uint32_t)(rank * len * 16)),
-                   "r"(p));
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(bar) : "r"(bar_a), "r"(p));
-      asm volatile(
-          "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-          "r"(tile_a + (uint32_t)(lo * 16)), "r"((uint32_t)(len * 16)), "r"(bar)
-          : "memory");
-    }
-    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
-  }
-  const bool got = mbar_wait_bounded(recvbar, 0, kWait);
-  if (tid == 0 && !got) atomicAdd(&g_sk_wait_timeouts, 1u);
-  {
-    const int lo = g_lo(rank), len = g_lo(rank + 1) - lo;
-    const float4* t4 = reinterpret_cast<const float4*>(tile);
-    const float4* r4 = reinterpret_cast<const float4*>(recv);
-    for (int gi = tid; gi < len; gi += 128) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float4 v = sp == rank ? t4[lo + gi] : r4[sp * len + gi];
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    for (int u = 0; u < 2; ++u) {
+      const int v = v0 + u * kThreads;
+      if (v < tb * VR) {
+        const uint32_t addr = smem_u32(&sP[(v / VR) * PF + (v % VR) * 4]);
+#pragma unroll
+        for (int p = 0; p < kMaxCluster; ++p)
+          if (p < S) q[u][p] = ld_dsmem_f4(addr, (uint32_t)p);
       }
-      const int g = lo + gi;
-      const int m = g / (kBN / 4), n = n0 + (g % (kBN / 4)) * 4;
-      T* yrow = Y + (int64_t)m * ldy;
-      if (vec_store && n < N) {  // n % 4 == 0, N % 4 == 0, 8-byte aligned rows
-        uint2 pk;
-        pk.x = pack2<T>(acc.x, acc.y);
-        pk.y = pack2<T>(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(yrow + n) = pk;
-      } else {
-        if (n < N) yrow[n] = from_f<T>(acc.x);
-        if (n + 1 < N) yrow[n + 1] = from_f<T>(acc.y);
-        if (n + 2 < N) yrow[n + 2] = from_f<T>(acc.z);
-        if (n + 3 < N) yrow[n + 3] = from_f<T>(acc.w);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int v = v0 + u * kThreads;
+      if (v < tb * VR) {
+        float4 a = q[u][0];
+#pragma unroll
+        for (int p = 1; p < kMaxCluster; ++p)
+          if (p < S) {
+            a.x += q[u][p].x;
+            a.y += q[u][p].y;
+            a.z += q[u][p].z;
+            a.w += q[u][p].w;
+          }
+        store(v / VR, (v % VR) * 4, a);
       }
     }
   }
-  // this CTA's outgoing copies have finished reading its tile before it exits
-  if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+  // no CTA leaves while the others read its tile.  Relaxed: every remote value this thread read
+  // has been added (consumed) before the arrive issues, and the Y stores need no ordering here
+  // (a release would wait for them to reach L2).
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
 }
+
+struct Split {
+  int wk, S, kc;
+};
 
 }  // namespace
-
-int read_and_clear_skinny_timeouts(unsigned int* count) {
-  unsigned int v = 0, zero = 0;
-  if (cudaMemcpyFromSymbol(&v, g_sk_wait_timeouts, sizeof(v)) != cudaSuccess ||
-      cudaMemcpyToSymbol(g_sk_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
-    return set_error(MB_ERR_CUDA, "wait_timeouts: %s", cudaGetErrorString(cudaGetLastError()));
-  *count = v;
-  return MB_OK;
-}
-
 }  // namespace mb
 
-extern "C" int64_t motif_b200_skinny_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  (void)M;
-  (void)N;
-  (void)K;
-  return 0;  // the split-K reduction runs through distributed shared memory
+using namespace mb;
+
+extern "C" int64_t motif_b200_skinny_packed_bytes(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0 || K % 16 != 0) return -1;
+  return (N + 31) / 32 * 32 * K * 2;
 }
 
-extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
-                                      int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
-                                      int64_t workspace_bytes, void* stream) {
-  using namespace mb;
-  (void)workspace;
-  (void)workspace_bytes;
-  MB_REQUIRE(x && w && y, MB_ERR_ARG, "skinny_gemm: null pointer");
-  MB_REQUIRE(M > 0 && M <= kMaxM && N > 0 && K > 0 && N < (1LL << 31) && K < (1LL << 31), MB_ERR_SHAPE,
-             "skinny_gemm: M must be in 1..%d (got %lld)", kMaxM, (long long)M);
-  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "skinny_gemm: 16-bit dtypes only");
-  MB_REQUIRE(K % kBK == 0, MB_ERR_UNSUPPORTED, "skinny_gemm: K must be a multiple of %d (got %lld)", kBK,
-             (long long)K);
-  MB_REQUIRE(ldx % 8 == 0 && ldw % 8 == 0 && ldx >= K && ldw >= K && ldy >= N &&
-                 ((uintptr_t)x | (uintptr_t)w) % 16 == 0 && (uintptr_t)y % 2 == 0,
-             MB_ERR_ALIGN, "skinny_gemm: rows must be 16-byte aligned (ldx, ldw multiples of 8)");
-  MB_REQUIRE((N + kBN - 1) / kBN < 65536LL * 32, MB_ERR_SHAPE, "skinny_gemm: N too large");
-  CUtensorMap tmW, tmX;
-  int rc = encode_tile_map_2d(&tmW, w, 2, (uint64_t)K, (uint64_t)N, (uint64_t)ldw * 2, kBK, kBN, 128);
-  if (!rc) rc = encode_tile_map_2d(&tmX, x, 2, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, kBK, kMaxM, 128);
-  if (rc) return rc;
-  const int vec_store = (ldy % 4 == 0 && N % 4 == 0 && (uintptr_t)y % 8 == 0) ? 1 : 0;
+extern "C" int motif_b200_skinny_pack(const void* w, int64_t ldw, int64_t N, int64_t K, void* packed, int dtype,
+                                      void* stream) {
+  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "skinny_pack: 16-bit weights only");
+  MB_REQUIRE(N > 0 && K > 0 && N < (1LL << 30) && K < (1LL << 24), MB_ERR_SHAPE, "skinny_pack: N %lld K %lld",
+             (long long)N, (long long)K);
+  MB_REQUIRE(K % 16 == 0, MB_ERR_UNSUPPORTED, "skinny_pack: K (%lld) must be a multiple of 16", (long long)K);
+  MB_REQUIRE(ldw >= K && ldw % 2 == 0 && (uintptr_t)w % 4 == 0, MB_ERR_ARG,
+             "skinny_pack: ldw must be >= K and even, W 4-byte aligned");
+  MB_REQUIRE(w != nullptr && packed != nullptr && (uintptr_t)packed % 16 == 0, MB_ERR_ARG,
+             "skinny_pack: null or unaligned pointer");
+  const int KT = (int)(K / 16), NB = (int)((N + 31) / 32 * 2);
+  const int64_t total = (int64_t)NB * KT * 32;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
   cudaStream_t st = (cudaStream_t)stream;
-  auto go = [&](auto t) {
+  if (dtype == MB_BF16)
+    skinny_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)w, ldw, (int)N, KT, NB,
+                                                               (uint4*)packed);
+  else
+    skinny_pack_kernel<__half><<<blocks, 256, 0, st>>>((const __half*)w, ldw, (int)N, KT, NB, (uint4*)packed);
+  return check_launch("skinny_pack");
+}
+
+extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* packed, void* y, int64_t ldy,
+                                      int64_t M, int64_t N, int64_t K, int k_warps, int split_k, int dtype,
+                                      void* stream) {
+  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "skinny_gemm: 16-bit operands only");
+  MB_REQUIRE(M >= 1 && M <= 64, MB_ERR_UNSUPPORTED, "skinny_gemm: M (%lld) must be in 1..64", (long long)M);
+  MB_REQUIRE(N > 0 && K > 0 && N < (1LL << 30) && K < (1LL << 24), MB_ERR_SHAPE, "skinny_gemm: N %lld K %lld",
+             (long long)N, (long long)K);
+  MB_REQUIRE(K % 16 == 0, MB_ERR_UNSUPPORTED, "skinny_gemm: K (%lld) must be a multiple of 16", (long long)K);
+  MB_REQUIRE(N % 4 == 0 && ldy % 4 == 0 && ldy >= N && (uintptr_t)y % 8 == 0, MB_ERR_UNSUPPORTED,
+             "skinny_gemm: N and ldy must be multiples of 4 (Y 8-byte aligned)");
+  MB_REQUIRE(ldx % 8 == 0 && ldx >= K && (uintptr_t)x % 16 == 0 && (uintptr_t)packed % 16 == 0, MB_ERR_UNSUPPORTED,
+             "skinny_gemm: ldx must be a multiple of 8 (X and the packed weight 16-byte aligned)");
+  MB_REQUIRE(k_warps == 0 || k_warps == 1 || k_warps == 2 || k_warps == 4, MB_ERR_ARG,
+             "skinny_gemm: k_warps must be 0 (automatic), 1, 2 or 4");
+  MB_REQUIRE(split_k >= 0 && split_k <= kMaxCluster, MB_ERR_ARG, "skinny_gemm: split_k must be 0 (automatic) .. %d",
+             kMaxCluster);
+  const int KT = (int)(K / 16), NG = (int)((N + 31) / 32);
+  const int ntt = M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8));
+  int dev = 0, sms = 148, smem_sm = 228 * 1024;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(MB_ERR_CUDA, "skinny_gemm: no device");
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  constexpr size_t kMaxSmem = 227 * 1024;
+
+  // registers per thread of the instance (once per device and instance): CTAs per SM
+  static int regs_of[4] = {0, 0, 0, 0};
+  static std::mutex regs_mu;
+  const int ni = ntt == 1 ? 0 : (ntt == 2 ? 1 : (ntt == 4 ? 2 : 3));
+  int regs = 0;
+  {
+    std::lock_guard<std::mutex> lock(regs_mu);
+    if (!regs_of[ni]) {
+      cudaFuncAttributes fa = {};
+      const void* f = ntt == 1 ? (const void*)skinny_kernel<__nv_bfloat16, 1>
+                    : ntt == 2 ? (const void*)skinny_kernel<__nv_bfloat16, 2>
+                    : ntt == 4 ? (const void*)skinny_kernel<__nv_bfloat16, 4>
+                               : (const void*)skinny_kernel<__nv_bfloat16, 8>;
+      regs_of[ni] = cudaFuncGetAttributes(&fa, f) == cudaSuccess && fa.numRegs > 0 ? fa.numRegs : 255;
+    }
+    regs = regs_of[ni];
+  }
+  const long reg_ctas = std::max(1, 65536 / (kThreads * ((regs + 7) / 8 * 8)));
+
+  // The split with the least estimated time.  Per CTA: its W bytes at an SM's share of HBM
+  // bandwidth (~44 KB/us), its X bytes from L2 (~110 KB/us), and its partial tile read by the
+  // cluster (~10 KB/us through distributed shared memory); the CTAs sharing an SM add up; each
+  // wave pays ~2 us of latency.  The constants are measured orders of magnitude on B200; the
+  // model only has to rank the candidates.
+  Split best = {0, 0, 0};
+  double best_us = 0.0;
+  size_t best_smem = 0;
+  for (int wk : {1, 2, 4}) {
+    if (k_warps && wk != k_warps) continue;
+    for (int S = 1; S <= kMaxCluster; ++S) {
+      if (split_k && S != split_k) continue;
+      const int kc = (KT + S - 1) / S;
+      if ((kc + wk - 1) / wk > kKtw) continue;
+      const Split sp = {wk, (KT + kc - 1) / kc, kc};
+      if (!split_k && sp.S != S) continue;  // the same split as a smaller S
+      const Plan pl = make_plan(ntt, (int)M, wk, kc, sp.S);
+      if (pl.bytes > kMaxSmem) continue;
+      const long per_sm = std::min<long>(reg_ctas, (long)smem_sm / (long)(pl.bytes + 1024));
+      if (per_sm < 1) continue;
+      const int F = (kWarps / wk) * 32;
+      const long ctas = (long)((NG + kWarps / wk - 1) / (kWarps / wk)) * sp.S;
+      const long slots = per_sm * sms, waves = (ctas + slots - 1) / slots;
+      const long share = (std::min(ctas, slots) + sms - 1) / sms;
+      const double w_kb = (double)F * kc * 32 / 1024.0, x_kb = (double)M * kc * 32 / 1024.0;
+      const double e_kb = sp.S > 1 ? (double)M * F * 4 * (sp.S - 1) / sp.S / 1024.0 : 0.0;
+      const double us = (double)waves * (2.0 + (double)share * (w_kb / 44.0 + x_kb / 110.0 + e_kb / 10.0));
+      if (best.wk == 0 || us < best_us) {
+        best = sp;
+        best_us = us;
+        best_smem = pl.bytes;
+      }
+    }
+  }
+  MB_REQUIRE(best.wk != 0, MB_ERR_UNSUPPORTED,
+             "skinny_gemm: no split of K = %lld fits (k_warps %d, split_k %d; at most %d k-tiles per warp)",
+             (long long)K, k_warps, split_k, kKtw);
+  const int wf = kWarps / best.wk;
+  cudaStream_t st = (cudaStream_t)stream;
+  auto go = [&](auto t, auto ntt_c) -> int {
     using T = decltype(t);
-    auto kern = skinny_tc_kernel<T>;
-    // per device, once: attributes, and how many clusters of each size 1..16 fit at a time
-    // guarded by one lock: host threads launching on the same device at once see the table
-    // only after it is complete
-    static int active[64][kMaxSplit + 1] = {};
-    static std::mutex mu;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
-      return set_error(MB_ERR_CUDA, "skinny_gemm: no device");
-    std::unique_lock<std::mutex> lock(mu);
-    if (!active[dev][0]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess ||
-          cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-        return check_launch("skinny_gemm (function attributes)");
-      for (int cs = 1; cs <= kMaxSplit; ++cs) {
-        cudaLaunchConfig_t q = {};
-        cudaLaunchAttribute qa[1];
-        qa[0].id = cudaLaunchAttributeClusterDimension;
-        qa[0].val.clusterDim.x = 1;
-        qa[0].val.clusterDim.y = (unsigned)cs;
-        qa[0].val.clusterDim.z = 1;
-        q.gridDim = dim3(1, (unsigned)cs);
-        q.blockDim = dim3(128);
-        q.dynamicSmemBytes = kSmemBytes;
-        q.attrs = qa;
-        q.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess) n = 0;
-        active[dev][cs] = n;
-      }
-      cudaGetLastError();
-      if (active[dev][1] <= 0) return set_error(MB_ERR_CUDA, "skinny_gemm: kernel cannot be resident");
-      active[dev][0] = 1;
-    }
-    lock.unlock();
-    // the most K slices whose clusters all fit in one wave
-    const int nblk = (int)((N + kBN - 1) / kBN);
-    const int kchunks = (int)((K / kBK + kAtoms - 1) / kAtoms);
-    int nsplit = 1, per = kchunks;
-    for (int want = std::min(kMaxSplit, kchunks); want > 1; --want) {
-      const int p = (kchunks + want - 1) / want, ns = (kchunks + p - 1) / p;
-      if (nblk <= active[dev][ns]) {
-        nsplit = ns;
-        per = p;
-        break;
-      }
-    }
+    constexpr int NTT = decltype(ntt_c)::value;
+    auto kern = skinny_kernel<T, NTT>;
+    const int rc = ensure_smem_attr((const void*)kern, (int)kMaxSmem);
+    if (rc != MB_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = (unsigned)nsplit;
+    at[0].val.clusterDim.y = (unsigned)best.S;
     at[0].val.clusterDim.z = 1;
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)nblk, (unsigned)nsplit);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.gridDim = dim3((unsigned)((NG + wf - 1) / wf), (unsigned)best.S);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = best_smem;
     cfg.stream = st;
     cfg.attrs = at;
-    cfg.numAttrs = SK_PDL ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, per,
-                       (int)((K / kBK + kAtoms - 1) / kAtoms), (int)(K / kBK), vec_store);
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, kern, (const T*)x, ldx, (const uint4*)packed, KT, NG, (T*)y, ldy, (int)M, (int)N,
+                       best.wk, best.kc);
     return check_launch("skinny_gemm");
   };
-  return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+  auto by_n = [&](auto t) -> int {
+    switch (ntt) {
+      case 1: return go(t, std::integral_constant<int, 1>{});
+      case 2: return go(t, std::integral_constant<int, 2>{});
+      case 4: return go(t, std::integral_constant<int, 4>{});
+      default: return go(t, std::integral_constant<int, 8>{});
+    }
+  };
+  return dtype == MB_BF16 ? by_n(__nv_bfloat16{}) : by_n(__half{});
 }

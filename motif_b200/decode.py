@@ -180,7 +180,7 @@ class GraphDecoder:
                     _norm_read([x] + fs, block.pseudo_queries[i].detach(), block.attn_res_norms[i].weight.detach(),
                                None, hn, eps_src=block.attn_res_norms[i].eps)
                 pk = self.decs[b][i]
-                proj = _mm(hn, pk.w_in)
+                proj = _mm(hn, pk.w_in, wp=pk.w_in_sk)
                 if dec.attn_type == 'chord':
                     f = self._chord(pk, proj, self.kv[kv_i], dc, st)
                     kv_i += 1
@@ -193,7 +193,7 @@ class GraphDecoder:
             _norm_read(fs, None, None, x_next, hn, eps_out=(model.norm.eps if b == len(model.blocks) - 1 else
                                                              model.blocks[b + 1].features[0].attn_norm.eps))
             x = x_next
-        logits = _mm(hn, self.lm)
+        logits = _mm(hn, self.lm, wp=model._lm_sk)
         self.logits = logits  # the step's [B, V] logits buffer: after a replay, the last step's
         sp = self.sampler
         if sp is None:
@@ -230,7 +230,7 @@ class GraphDecoder:
                   proj.data_ptr() + pk.off_g * proj.element_size(), _lib.ptr(pk.onorm_w), _lib.ptr(cat),
                   cat.stride(0), B, H, dk, dv, NORM_EPS, proj.data_ptr() + pk.off_gu * proj.element_size(), N_in,
                   cat.data_ptr() + H * dv * cat.element_size(), cat.stride(0), hid, dc, st)
-        return _mm(cat, pk.w_out)
+        return _mm(cat, pk.w_out, wp=pk.w_out_sk)
 
     def _chord(self, pk, proj, lc: KVLayerCache, dc, st):
         B, dt, dev = self.B, self.dt, self.dev
@@ -251,8 +251,8 @@ class GraphDecoder:
         _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap,
                   lens_ptr + 4, 0, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax),
                   _lib.ptr(attn), d, B, H, Hkv, 1, D, D ** -0.5, GGD_EPS, self.splits, _lib.ptr(ws), ws_bytes, dc, st)
-        f = _mm(act, pk.w_down)
-        a = _mm(attn, pk.w_o)
+        f = _mm(act, pk.w_down, wp=pk.w_down_sk)
+        a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
         _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(),
                   N_in, _lib.ptr(f), d, _lib.ptr(f), d, B, d, dc, st)
         return f

@@ -273,6 +273,8 @@ class _GDNPack:
     off_g: int
     off_gu: int
     w_in_il: Optional[torch.Tensor] = None  # w_in with gate_up regrouped for the fused SwiGLU
+    w_in_sk: Optional[torch.Tensor] = None  # decode-sized products: w_in / w_out packed for the skinny GEMM
+    w_out_sk: Optional[torch.Tensor] = None
 
 
 @dataclass
@@ -293,6 +295,24 @@ class _ChordPack:
     off_g: int
     off_gu: int
     w_in_il: Optional[torch.Tensor] = None  # w_in with gate_up regrouped for the fused SwiGLU
+    w_in_sk: Optional[torch.Tensor] = None  # decode-sized products: packed for the skinny GEMM
+    w_o_sk: Optional[torch.Tensor] = None
+    w_down_sk: Optional[torch.Tensor] = None
+
+
+def _skinny_packed(w: torch.Tensor) -> Optional[torch.Tensor]:
+    """w [N, K] in the skinny GEMM's fragment order (`motif_b200_skinny_pack`), or None where
+    that kernel does not apply (CPU, fp32, K not a multiple of 16)."""
+    if not w.is_cuda or w.dtype not in (torch.bfloat16, torch.float16) or w.dim() != 2:
+        return None
+    N, K = w.shape
+    if K % 16 or N % 4 or w.stride(1) != 1 or w.stride(0) % 2 or w.data_ptr() % 4:
+        return None
+    nbytes = _lib.load().motif_b200_skinny_packed_bytes(N, K)
+    out = torch.empty(nbytes // w.element_size(), dtype=w.dtype, device=w.device)
+    _lib.call('motif_b200_skinny_pack', w.data_ptr(), w.stride(0), N, K, out.data_ptr(), _lib.dtype_code(w.dtype),
+              _lib.stream_ptr(w.device))
+    return out
 
 
 @torch.no_grad()
@@ -309,12 +329,14 @@ def _pack_decoder(dec: Decoder):
         w_in_il = (torch.cat([w_in[:off_g + a.hidden_size], _interleave_gate_up(w_in[off_g + a.hidden_size:], hid)],
                              0).contiguous() if hid % 128 == 0 else None)
         al, be, mu = a._ggd_parameters()
+        w_o = a.o_proj.weight.detach().contiguous()
+        w_down = dec.mlp.down_proj.weight.detach().contiguous()
         return _ChordPack(w_in=w_in, qn_w=a.q_norm.weight.detach().contiguous(),
-                          kn_w=a.k_norm.weight.detach().contiguous(), w_o=a.o_proj.weight.detach().contiguous(),
-                          w_down=dec.mlp.down_proj.weight.detach().contiguous(), alpha=al.contiguous(),
+                          kn_w=a.k_norm.weight.detach().contiguous(), w_o=w_o, w_down=w_down, alpha=al.contiguous(),
                           beta=be.contiguous(), mu=mu.contiguous(), ssmax=a.ssmax_s.detach().float().contiguous(),
                           H=a.num_heads, Hkv=a.num_kv_heads, D=a.head_dim, hid=hid, off_g=off_g,
-                          off_gu=off_g + a.hidden_size, w_in_il=w_in_il)
+                          off_gu=off_g + a.hidden_size, w_in_il=w_in_il, w_in_sk=_skinny_packed(w_in),
+                          w_o_sk=_skinny_packed(w_o), w_down_sk=_skinny_packed(w_down))
     H, dk, dv = a.num_heads, a.dk, a.dv
     parts = [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.a_proj.weight, a.b_proj.weight, a.g_proj.weight]
     off_g = 2 * H * dk + H * dv + 2 * H
@@ -327,7 +349,8 @@ def _pack_decoder(dec: Decoder):
     w_out = torch.cat([a.o_proj.weight, dec.mlp.down_proj.weight], 1).contiguous()
     return _GDNPack(w_in=w_in, conv_w=conv_w, A_log=a.A_log.detach().contiguous(),
                     dt_bias=a.dt_bias.detach().contiguous(), onorm_w=a.o_norm.weight.detach().contiguous(),
-                    w_out=w_out, H=H, dk=dk, dv=dv, hid=hid, off_g=off_g, off_gu=off_gu, w_in_il=w_in_il)
+                    w_out=w_out, H=H, dk=dk, dv=dv, hid=hid, off_g=off_g, off_gu=off_gu, w_in_il=w_in_il,
+                    w_in_sk=_skinny_packed(w_in), w_out_sk=_skinny_packed(w_out))
 
 
 # ============================================================================ model
@@ -346,6 +369,7 @@ class MotifChordModel(nn.Module):
             self.embed.weight = self.lm_head.weight
         self.sampler = None
         self._packed = None
+        self._lm_sk = None
         self.decode_splits = None  # split-KV count override for the decode attention
 
     # ------------------------------------------------------------------ bookkeeping
@@ -365,6 +389,7 @@ class MotifChordModel(nn.Module):
             with torch.no_grad():
                 decs = [[_pack_decoder(dec) for dec in blk.features] for blk in self.blocks]
                 lm = (self.lm_head.weight * self.norm.weight[None, :]).contiguous()
+                self._lm_sk = _skinny_packed(lm)
             self._packed = (decs, lm)
         return self._packed
 
@@ -507,23 +532,25 @@ class MotifChordModel(nn.Module):
 
 
 # ============================================================================ engine
-# Largest M routed to motif_b200_skinny_gemm.  0: every product runs on cuBLAS — the skinny
-# kernel is correct (tests) but measured slower than cuBLAS at the decode shapes (5.7-11.9 us
-# vs 3.3-10.9 us per product at M = 64), so the model does not use it.
-SKINNY_MAX_M = 0
+# Largest M routed to motif_b200_skinny_gemm (decode: one row per sequence).  Measured on the
+# 172M decode step (context 8192, CUDA graph): 0.365 vs 0.447 ms per step at 8 rows, 0.443 vs
+# 0.503 at 16, 0.548 vs 0.565 at 32, but 0.908 vs 0.747 at 64, where the legacy-MMA products
+# and the cluster's partial-tile exchange cost more than the latency the kernel hides.
+SKINNY_MAX_M = 32
 
 
-def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
-    """a [M, K] @ w[N, K]^T: decode-sized M (<= 64, 16-bit, aligned rows) on the weight-streaming
-    skinny GEMM, everything else on cuBLAS (plain library GEMM; timed as 'cublas_gemm')."""
+def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, wp: torch.Tensor = None) -> torch.Tensor:
+    """a [M, K] @ w[N, K]^T: decode-sized M (<= 64, 16-bit) on the weight-streaming skinny GEMM
+    when `wp` (w packed by `_skinny_packed`) is given, everything else on cuBLAS (plain library
+    GEMM; timed as 'cublas_gemm')."""
     M, K = a.shape
     N = w.shape[0]
-    if (M <= SKINNY_MAX_M and a.dtype in (torch.bfloat16, torch.float16) and w.dtype == a.dtype and K % 64 == 0
-            and a.stride(1) == 1 and w.stride(1) == 1 and a.stride(0) % 8 == 0 and w.stride(0) % 8 == 0
-            and a.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0):
+    if (wp is not None and M <= SKINNY_MAX_M and a.dtype == w.dtype and a.stride(1) == 1
+            and a.stride(0) % 8 == 0 and a.data_ptr() % 16 == 0
+            and (out is None or (out.stride(1) == 1 and out.stride(0) % 4 == 0 and out.data_ptr() % 8 == 0))):
         y = out if out is not None else torch.empty((M, N), dtype=a.dtype, device=a.device)
-        _lib.call('motif_b200_skinny_gemm', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(),
-                  y.stride(0), M, N, K, _lib.dtype_code(a.dtype), None, 0, _lib.stream_ptr(a.device))
+        _lib.call('motif_b200_skinny_gemm', a.data_ptr(), a.stride(0), wp.data_ptr(), y.data_ptr(), y.stride(0), M, N,
+                  K, 0, 0, _lib.dtype_code(a.dtype), _lib.stream_ptr(a.device))
         return y
     tr = _lib._tracker
     if tr is None:
@@ -551,9 +578,9 @@ def _tc_ok(*ts: torch.Tensor) -> bool:
 TC_MIN_M = 65
 
 
-def _gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+def _gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, wp: torch.Tensor = None) -> torch.Tensor:
     """a [M, K] @ w[N, K]^T: prefill-sized 16-bit products on the tcgen05 projection kernel
-    (`motif_b200_gemm`), decode-sized or fp32 ones on `_mm`."""
+    (`motif_b200_gemm`), decode-sized or fp32 ones on `_mm` (`wp`: w packed for the skinny GEMM)."""
     M, K = a.shape
     N = w.shape[0]
     if M >= TC_MIN_M and _tc_ok(a, w) and (out is None or (out.stride(1) == 1 and out.dtype == a.dtype)):
@@ -561,7 +588,7 @@ def _gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None) -> torch.T
         _lib.call('motif_b200_gemm', _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(y), y.stride(0),
                   M, N, K, _lib.dtype_code(a.dtype), _lib.stream_ptr(a.device))
         return y
-    return _mm(a, w, out)
+    return _mm(a, w, out, wp)
 
 
 def _proj_fused(pk, hn: torch.Tensor, act: torch.Tensor):
@@ -642,7 +669,7 @@ def _forward(model: MotifChordModel, ids: torch.Tensor, cache: ModelCache, posit
         ar.partial_block = x_next.view(B, T, d)
         ar.seq_len = max(ar.seq_len, T)
         x = x_next
-    logits = _gemm(hn, lm)
+    logits = _gemm(hn, lm, wp=model._lm_sk)
     return logits.view(B, T, cfg.vocab_size), x.view(B, T, d)
 
 
@@ -656,7 +683,7 @@ def _gdn_decoder(pk: _GDNPack, hn, B, T, cache: Optional[GatedDeltaAttentionLaye
     proj = _proj_fused(pk, hn, cat[:, H * dv:]) if T > 1 else None
     act_done = proj is not None
     if proj is None:
-        proj = _mm(hn, pk.w_in)
+        proj = _mm(hn, pk.w_in, wp=pk.w_in_sk)
     N_in = proj.shape[1]
     state_in = cache.state if cache is not None else None
     conv_in = cache._conv if cache is not None else None
@@ -711,7 +738,7 @@ def _gdn_decoder(pk: _GDNPack, hn, B, T, cache: Optional[GatedDeltaAttentionLaye
     if T != 1 and not act_done:
         _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(),
                   cat.data_ptr() + H * dv * cat.element_size(), M, hid, N_in, cat.stride(0), dc, st)
-    f = _gemm(cat, pk.w_out)
+    f = _gemm(cat, pk.w_out, wp=pk.w_out_sk)
     if cache is not None:
         cache._split = (H * dk, H * dk, H * dv)
         cache.update(state, conv_out, steps=T)
@@ -745,7 +772,7 @@ def _chord_decoder(model, pk: _ChordPack, hn, B, T, cache: Optional[KVLayerCache
     act_done = proj is not None
     fused_proj = act_done
     if proj is None:
-        proj = _mm(hn, pk.w_in)
+        proj = _mm(hn, pk.w_in, wp=pk.w_in_sk)
     N_in = proj.shape[1]
     if cache is None:
         cache = KVLayerCache()  # no layer cache (training-mode forward): attend to this chunk only
@@ -815,7 +842,7 @@ def _chord_decoder(model, pk: _ChordPack, hn, B, T, cache: Optional[KVLayerCache
     if not act_done:
         _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid,
                   N_in, hid, dc, st)
-    f = _gemm(act, pk.w_down)
+    f = _gemm(act, pk.w_down, wp=pk.w_down_sk)
     gate = proj[:, pk.off_g:pk.off_g + d]
     if fused_proj and _tc_ok(attn, pk.w_o, gate, f):
         # o_proj with the gate and the parallel residual in its epilogue: f = attn_o * sigmoid(g) + f
@@ -823,7 +850,7 @@ def _chord_decoder(model, pk: _ChordPack, hn, B, T, cache: Optional[KVLayerCache
                   pk.w_o.stride(0), _lib.ptr(gate), gate.stride(0), _lib.ptr(f), f.stride(0), _lib.ptr(f),
                   f.stride(0), M, d, d, dc, st)
         return f
-    a = _mm(attn, pk.w_o)
+    a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
     _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(), N_in,
               _lib.ptr(f), d, _lib.ptr(f), d, M, d, dc, st)
     return f

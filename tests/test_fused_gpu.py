@@ -414,51 +414,144 @@ def test_gdn_prefill_fused_matches_two_kernel_path(B, T, H, dk, dv, with_state):
     assert rel_err(S1, S) < 2e-2, rel_err(S1, S)
 
 
+def skinny_pack(w):
+    N, K = w.shape
+    nbytes = _lib.load().motif_b200_skinny_packed_bytes(N, K)
+    assert nbytes == (N + 31) // 32 * 32 * K * 2
+    p = torch.empty(nbytes // 2, dtype=w.dtype, device=w.device)
+    _lib.call('motif_b200_skinny_pack', w.data_ptr(), w.stride(0), N, K, p.data_ptr(), _lib.dtype_code(w.dtype), st())
+    return p
+
+
+def skinny(x, p, N, y=None, k_warps=0, split_k=0):
+    M, K = x.shape
+    y = y if y is not None else torch.empty(M, N, dtype=x.dtype, device=x.device)
+    _lib.call('motif_b200_skinny_gemm', x.data_ptr(), x.stride(0), p.data_ptr(), y.data_ptr(), y.stride(0), M, N, K,
+              k_warps, split_k, _lib.dtype_code(x.dtype), st())
+    return y
+
+
+def within_fp32_product(y, x, w):
+    """The kernel accumulates in fp32 and rounds once to the output dtype: each element is
+    within one 16-bit rounding of the fp32 product plus a summation-order term."""
+    ref = x.float() @ w.float().t()
+    err = (y.float() - ref).abs()
+    tol = 2.0 ** -7 * ref.abs() + 1e-3 * ref.abs().max()
+    return bool((err <= tol).all()), err.max().item()
+
+
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize('M,N,K', [(1, 768, 768), (7, 8728, 768), (64, 768, 3584), (64, 6016, 768),
-                                   (33, 768, 2048), (64, 32000, 768), (5, 100, 64), (64, 129, 128)])
-def test_skinny_gemm_vs_torch(dtype, M, N, K):
+                                   (33, 768, 2048), (64, 32000, 768), (5, 100, 64), (64, 132, 128), (16, 8728, 768),
+                                   (9, 768, 16)])
+def test_skinny_gemm_vs_fp32_product(dtype, M, N, K):
     g = torch.Generator().manual_seed(M + N + K)
     x = (0.5 * torch.randn(M, K, generator=g)).to(dtype).cuda()
-    w = (0.05 * torch.randn(N, K, generator=g)).to(dtype).cuda()
-    ref = x.float() @ w.float().t()
-    # split-K is summed through distributed shared memory: no workspace is asked for
-    assert _lib.load().motif_b200_skinny_gemm_workspace_bytes(M, N, K) == 0
+    w = (K ** -0.5 * torch.randn(N, K, generator=g)).to(dtype).cuda()
+    p = skinny_pack(w)
     outs = []
     for _ in range(2):  # a call leaves no state behind: a repeat gives the same bits
-        y = torch.empty(M, N, dtype=dtype, device='cuda')
-        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K,
-                  _lib.dtype_code(dtype), None, 0, st())
-        assert rel_err(y.float(), ref) < 1e-2, rel_err(y.float(), ref)
+        y = skinny(x, p, N)
+        torch.cuda.synchronize()
+        ok, e = within_fp32_product(y, x, w)
+        assert ok, e
         outs.append(y)
     assert torch.equal(outs[0], outs[1])
 
 
-def test_skinny_gemm_consecutive_shapes():
-    """Back-to-back calls of the decode step's shapes on one stream (split and unsplit
-    launches, clusters of different sizes)."""
+@pytest.mark.parametrize('k_warps,split_k', [(1, 1), (1, 4), (2, 3), (4, 1), (4, 8), (2, 8), (1, 7)])
+def test_skinny_gemm_every_split(k_warps, split_k):
+    """Forced splits of K across the warps of a CTA (1, 2, 4) and the CTAs of a cluster (1..8),
+    including ragged last parts, all within the fp32 product's bound."""
+    M, N, K = 40, 1000, 1536
+    g = torch.Generator().manual_seed(k_warps * 10 + split_k)
+    x = torch.randn(M, K, generator=g).bfloat16().cuda()
+    w = (K ** -0.5 * torch.randn(N, K, generator=g)).bfloat16().cuda()
+    p = skinny_pack(w)
+    if (K // 16 + split_k - 1) // split_k > 12 * k_warps:
+        with pytest.raises(NotImplementedError, match='no split'):
+            skinny(x, p, N, k_warps=k_warps, split_k=split_k)
+        return
+    y = skinny(x, p, N, k_warps=k_warps, split_k=split_k)
+    torch.cuda.synchronize()
+    ok, e = within_fp32_product(y, x, w)
+    assert ok, e
+
+
+def test_skinny_gemm_strided_rows_and_slices():
+    """X a column slice of a wider buffer (ldx > K), Y written into a column slice (ldy > N):
+    the columns around the slice are left alone."""
+    M, N, K = 64, 768, 2048
+    g = torch.Generator().manual_seed(11)
+    big_x = torch.randn(M, K + 1536, generator=g).bfloat16().cuda()
+    x = big_x[:, 1536:]
+    w = (K ** -0.5 * torch.randn(N, K, generator=g)).bfloat16().cuda()
+    big_y = torch.full((M, N + 16), 3.0, dtype=torch.bfloat16, device='cuda')
+    y = skinny(x, skinny_pack(w), N, y=big_y[:, 8:8 + N])
+    torch.cuda.synchronize()
+    ok, e = within_fp32_product(y, x, w)
+    assert ok, e
+    assert bool((big_y[:, :8] == 3).all()) and bool((big_y[:, 8 + N:] == 3).all())
+
+
+def test_skinny_gemm_decode_shapes_in_a_cuda_graph():
+    """The decode step's products back to back on one stream, captured in a CUDA graph (the
+    launches carry programmatic-dependent-launch edges there) and replayed: each replay equals
+    the eager calls bit for bit, and each product feeds the next (a chain of dependencies)."""
     g = torch.Generator().manual_seed(3)
-    shapes = [(2, 768, 3584), (2, 6016, 768), (2, 768, 2048), (2, 8728, 768), (2, 768, 3584)]
-    for M, N, K in shapes * 2:
-        x = torch.randn(M, K, generator=g).bfloat16().cuda()
-        w = (0.05 * torch.randn(N, K, generator=g)).bfloat16().cuda()
-        y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
-        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, M, N, K,
-                  _lib.MB_BF16, None, 0, st())
-        assert rel_err(y.float(), x.float() @ w.float().t()) < 1e-2
+    M = 64
+    shapes = [(8728, 768), (768, 3584), (6016, 768), (768, 2048), (768, 768), (32000, 768)]
+    ws = [(K ** -0.5 * torch.randn(N, K, generator=g)).bfloat16().cuda() for N, K in shapes]
+    ps = [skinny_pack(w) for w in ws]
+    x0 = torch.randn(M, 768, generator=g).bfloat16().cuda()
+    bufs = [torch.empty(M, N, dtype=torch.bfloat16, device='cuda') for N, _ in shapes]
+
+    def chain():  # each product reads a column slice of the previous one's output (N >= next K)
+        h = x0
+        for (N, K), p, out in zip(shapes, ps, bufs):
+            skinny(h[:, :K], p, N, y=out)
+            h = out
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain()
+        torch.cuda.synchronize()
+        eager = [b.clone() for b in bufs]
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            chain()
+    torch.cuda.current_stream().wait_stream(s)
+    for b in bufs:
+        b.zero_()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    for i, b in enumerate(bufs):
+        assert torch.equal(b, eager[i]), i
+    ok, e = within_fp32_product(eager[1], eager[0][:, :3584], ws[1])
+    assert ok, e
+    del graph
 
 
-def test_skinny_gemm_rejects_bad_shapes():
+def test_skinny_gemm_rejects_bad_arguments():
     x = torch.zeros(65, 64, dtype=torch.bfloat16, device='cuda')
     w = torch.zeros(64, 64, dtype=torch.bfloat16, device='cuda')
+    p = skinny_pack(w)
     y = torch.zeros(65, 64, dtype=torch.bfloat16, device='cuda')
-    with pytest.raises(ValueError):  # M > 64
-        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, w.data_ptr(), 64, y.data_ptr(), 64, 65, 64, 64,
-                  _lib.MB_BF16, None, 0, st())
-    with pytest.raises(NotImplementedError):  # K not a multiple of the 64-wide chunk
-        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, w.data_ptr(), 64, y.data_ptr(), 64, 8, 64, 40,
-                  _lib.MB_BF16, None, 0, st())
-    assert _lib.wait_timeouts() == 0
+    with pytest.raises(NotImplementedError, match='M'):  # M > 64
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, p.data_ptr(), y.data_ptr(), 64, 65, 64, 64, 0, 0,
+                  _lib.MB_BF16, st())
+    with pytest.raises(NotImplementedError, match='multiple of 16'):
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, p.data_ptr(), y.data_ptr(), 64, 8, 64, 40, 0, 0,
+                  _lib.MB_BF16, st())
+    with pytest.raises(ValueError, match='k_warps'):
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, p.data_ptr(), y.data_ptr(), 64, 8, 64, 64, 3, 0,
+                  _lib.MB_BF16, st())
+    with pytest.raises(NotImplementedError, match='16-bit'):
+        _lib.call('motif_b200_skinny_gemm', x.data_ptr(), 64, p.data_ptr(), y.data_ptr(), 64, 8, 64, 64, 0, 0,
+                  _lib.MB_F32, st())
+    assert _lib.load().motif_b200_skinny_packed_bytes(64, 40) == -1
 
 
 # ------------------------------------------------------------------ attention masks
