@@ -335,6 +335,49 @@ MB_API int motif_b200_skinny_pack(const void* w, int64_t ldw, int64_t N, int64_t
 MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* packed, void* y, int64_t ldy, int64_t M,
                                   int64_t N, int64_t K, int k_warps, int split_k, int dtype, void* stream);
 
+/* ------------------------------------------------------------------ backward (training)
+ * Gradients of the three hot-path ops, fp32 arithmetic on CUDA cores (16-bit inputs widened on
+ * load), asynchronous on `stream`.
+ *
+ * motif_b200_chord_backward: dq [B,H,L,D], dk / dv [B,Hkv,S,D] (summed over each kv head's
+ *   query heads) from q, k, v, the forward output `out` and `dout`, with the forward's
+ *   arguments; `strides` holds the (b, head, t) element strides of q, k, v, out, dout, dq, dk,
+ *   dv and the (b, t) strides of log_n (26 values; unit inner strides).  Each row's
+ *   log-sum-exp is recomputed.  `param_partials` [B][H][ceil(L/32)][4] fp64 receives per-tile
+ *   partial gradients of alpha, beta, mu, ssmax (the caller sums over batch and tiles).
+ *   `workspace`: motif_b200_chord_backward_workspace_bytes(B, H, L), 16-byte aligned.
+ *   D in {16, 32, 64, 128}.  Replaces `_chord_backward_impl` / `_chord_bwd_dq_kernel` /
+ *   `_chord_bwd_dkdv_kernel` (motif/ops/chord_attention.py:518-958, 1348-1445).
+ * motif_b200_attn_res_backward: the gradient of every source (d_sources, same layout: rows of
+ *   D elements, row stride `row_stride`) and, in z_partials [partial_rows][D] fp32, partial
+ *   sums Z of which dquery = weight * sum(Z) and dweight = query * sum(Z); one launch of
+ *   `partial_rows` CTAs.  Replaces `_AttnResFunction.backward` (motif/ops/attn_res.py:188-364,
+ *   425-463).
+ * motif_b200_gdn_backward: dq, dk [B,H,L,Dk], dv [B,H,L,Dv], dbeta, dg [B,H,L] and (when
+ *   d_state_in is not null) the initial state's gradient, from grad_out [B,H,L,Dv] and
+ *   grad_state (the final state's gradient, or null); all fp32 and contiguous.  The states are
+ *   rebuilt from checkpoints every 64 steps in `workspace`
+ *   (motif_b200_gdn_backward_workspace_bytes).  (Dk, Dv) in {(16,32), (32,32), (32,64),
+ *   (64,64), (64,128), (128,128)}.  Replaces the backward of `_PrepareChunksFunction` and
+ *   `_FusedScanFunction` (motif/ops/gated_deltanet.py:180-284, 427-611, 726-765). */
+MB_API int64_t motif_b200_chord_backward_workspace_bytes(int64_t B, int64_t H, int64_t L);
+MB_API int motif_b200_chord_backward(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                                     const float* alpha, const float* beta, const float* mu, const float* ssmax,
+                                     const float* log_n, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                                     int64_t Hkv, int64_t L, int64_t S, int64_t D, int64_t q_start, float scale,
+                                     float eps, const int64_t* strides, void* workspace, int64_t workspace_bytes,
+                                     double* param_partials, int dtype, void* stream);
+MB_API int motif_b200_attn_res_backward(const void* const* sources, void* const* d_sources, int n_src, int64_t rows,
+                                        int64_t row_stride, int64_t D, const void* weight, const void* query,
+                                        float eps, const void* grad_out, int64_t grad_stride, float* z_partials,
+                                        int64_t partial_rows, int dtype, void* stream);
+MB_API int64_t motif_b200_gdn_backward_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, int64_t Dv);
+MB_API int motif_b200_gdn_backward(const float* q, const float* k, const float* v, const float* beta, const float* g,
+                                   const float* state_in, const float* grad_out, const float* grad_state, float* dq,
+                                   float* dk, float* dv, float* dbeta, float* dg, float* d_state_in, int64_t B,
+                                   int64_t H, int64_t L, int64_t Dk, int64_t Dv, void* workspace,
+                                   int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ dense projections
  * Y = X . W^T for 16-bit X [M, K] and W [N, K] (row strides ldx / ldw in elements, multiples of
  * 8, 16-byte aligned; K a multiple of 64, else MB_ERR_UNSUPPORTED), fp32 accumulation on the

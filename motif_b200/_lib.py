@@ -78,6 +78,11 @@ SIGNATURES = {
     'motif_b200_gemm_gate_residual': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I,
                                            _P]),
     'motif_b200_skinny_packed_bytes': (_I64, [_I64, _I64]),
+    'motif_b200_chord_backward_workspace_bytes': (_I64, [_I64, _I64, _I64]),
+    'motif_b200_chord_backward': (_I, [_P] * 13 + [_I64] * 7 + [_F, _F, _P, _P, _I64, _P, _I, _P]),
+    'motif_b200_attn_res_backward': (_I, [_P, _P, _I, _I64, _I64, _I64, _P, _P, _F, _P, _I64, _P, _I64, _I, _P]),
+    'motif_b200_gdn_backward_workspace_bytes': (_I64, [_I64] * 5),
+    'motif_b200_gdn_backward': (_I, [_P] * 14 + [_I64] * 5 + [_P, _I64, _P]),
     'motif_b200_skinny_pack': (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
     'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P]),
     'motif_b200_gdn_prefill_ws': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64,
@@ -147,6 +152,8 @@ KERNELS_PER_CALL = {n: 1 for n in SIGNATURES}
 KERNELS_PER_CALL.update({'motif_b200_last_error': 0, 'motif_b200_abi_version': 0,
                          'motif_b200_chord_workspace_bytes': 0, 'motif_b200_chord_decode_workspace_bytes': 0,
                          'motif_b200_skinny_packed_bytes': 0, 'motif_b200_gdn_chunk_workspace_bytes': 0,
+                         'motif_b200_chord_backward_workspace_bytes': 0, 'motif_b200_gdn_backward_workspace_bytes': 0,
+                         'motif_b200_chord_backward': 2,
                          'motif_b200_wait_timeouts': 0, 'motif_b200_testing_force': 0,
                          'motif_b200_chord_decode': 2, 'motif_b200_chord_decode_noalloc': 2,
                          'motif_b200_chord_decode_masked': 2,

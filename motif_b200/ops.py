@@ -2,9 +2,11 @@
 
 Same names, argument meanings, return values and exception types as
 `motif/ops/__init__.py:1-10` (plus `apply_block_attn_res`, `motif/ops/attn_res.py:596`),
-computed by the sm_100a kernels of `libmotif_b200.so`.  Forward only: inputs that require
-a gradient raise (autograd is not part of this inference path).  CPU tensors raise
-`ValueError`; there is no eager fallback.
+computed by the sm_100a kernels of `libmotif_b200.so`.  The delta rule, Chord attention and
+the attn-res read take gradients the way the reference's do (autograd Functions over the
+backward kernels, `motif_b200.autograd`); the norm / SwiGLU modules are forward-only and raise
+for inputs that require a gradient.  CPU tensors raise `ValueError`; there is no eager
+fallback.
 """
 
 from typing import Optional, Sequence
@@ -13,6 +15,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
+from .autograd import AttnResFunction, ChordAttentionFunction, GatedDeltaRuleFunction, needs_grad
 from .sampler import Sampler, make_sampler  # noqa: F401  (install targets)
 
 __all__ = [
@@ -48,7 +51,6 @@ def _last_contig(t):
 def _delta_args(q, k, v, beta, g, S):
     for n, t in (('q', q), ('k', k), ('v', v), ('beta', beta), ('g', g)):
         _cuda(n, t)
-    _no_grad(q, k, v, beta, g, S)
     if q.dim() != 4 or k.shape != q.shape or v.dim() != 4 or v.shape[:3] != q.shape[:3]:
         raise ValueError(f'q/k [B,H,L,Dk] and v [B,H,L,Dv] expected, got {tuple(q.shape)}, {tuple(k.shape)}, '
                          f'{tuple(v.shape)}')
@@ -91,13 +93,21 @@ def _delta_call(entry, q, k, v, beta, g, S):
     return o, S_out.to(q.dtype)
 
 
+def _delta_dispatch(entry, q, k, v, beta, g, S):
+    """The forward kernel, under the autograd Function when an input requires a gradient."""
+    if needs_grad(q, k, v, beta, g, S):
+        _delta_args(q, k, v, beta, g, S)  # validate before recording the graph
+        return GatedDeltaRuleFunction.apply(lambda *a: _delta_call(entry, *a), q, k, v, beta, g, S)
+    return _delta_call(entry, q, k, v, beta, g, S)
+
+
 def recurrent_gated_delta_rule(q, k, v, beta, g, S=None):
     """Token-by-token gated delta rule (`motif/ops/gated_deltanet.py:26-59`).
 
     Returns `(o [B,H,L,Dv], S [B,H,Dk,Dv])`; the state is carried in fp32 inside the kernel
     and returned in q's dtype, as the reference returns it.
     """
-    return _delta_call('motif_b200_gdn_recurrent', q, k, v, beta, g, S)
+    return _delta_dispatch('motif_b200_gdn_recurrent', q, k, v, beta, g, S)
 
 
 def chunk_gated_delta_rule(q, k, v, beta, g, S=None, chunk_size=64):
@@ -108,14 +118,14 @@ def chunk_gated_delta_rule(q, k, v, beta, g, S=None, chunk_size=64):
     """
     if int(chunk_size) < 1:
         raise ValueError(f'chunk_size must be positive, got {chunk_size}')
-    return _delta_call('motif_b200_gdn_chunk', q, k, v, beta, g, S)
+    return _delta_dispatch('motif_b200_gdn_chunk', q, k, v, beta, g, S)
 
 
 def chunk_gated_delta_rule_triton(q, k, v, beta, g, S=None, chunk_size=64):
     """`chunk_gated_delta_rule_triton` (`motif/ops/gated_deltanet.py:796-834`), same kernel."""
     if int(chunk_size) < 16:
         raise NotImplementedError('chunk_size must be >= 16 (the K-dimension lower bound of tl.dot)')
-    return _delta_call('motif_b200_gdn_chunk', q, k, v, beta, g, S)
+    return _delta_dispatch('motif_b200_gdn_chunk', q, k, v, beta, g, S)
 
 
 # -------------------------------------------------------------------- chord attention
@@ -169,7 +179,6 @@ def apply_chord_attention(q, k, v, alpha, beta, mu, ssmax, log_n, q_start: Optio
     """Chord attention forward (`motif/ops/chord_attention.py:1557-1625`)."""
     B, H, L, D, Hkv, S = _check_chord(q, k, v, log_n)
     _check_params(alpha, beta, mu, ssmax, H)
-    _no_grad(q, k, v, alpha, beta, mu, ssmax)
     if softmax_scale is None:
         softmax_scale = D ** -0.5
     if q_start is None:
@@ -177,6 +186,15 @@ def apply_chord_attention(q, k, v, alpha, beta, mu, ssmax, log_n, q_start: Optio
     q_start = int(q_start)
     if q_start < 0:
         raise ValueError(f'q_start must not be negative, got {q_start}')
+    if needs_grad(q, k, v, alpha, beta, mu, ssmax):
+        return ChordAttentionFunction.apply(_chord_forward, q, k, v, alpha, beta, mu, ssmax, log_n, q_start,
+                                            float(softmax_scale), float(eps))
+    return _chord_forward(q, k, v, alpha, beta, mu, ssmax, log_n, q_start, float(softmax_scale), float(eps))
+
+
+def _chord_forward(q, k, v, alpha, beta, mu, ssmax, log_n, q_start, softmax_scale, eps):
+    B, H, L, D = q.shape
+    Hkv, S = k.shape[1], k.shape[2]
     out = torch.empty((B, H, L, D), dtype=q.dtype, device=q.device)
     if L == 0:
         return out
@@ -211,7 +229,12 @@ def attn_res_block(sources: Sequence[torch.Tensor], weight: torch.Tensor, query:
     """Fused cross-block attention residual (`motif/ops/attn_res.py:518-540`)."""
     if not can_use_triton_attn_res(sources, weight, query):
         raise ValueError('attn_res_block: unsupported sources / weight / query')
-    _no_grad(weight, query, *sources)
+    if needs_grad(weight, query, *sources):
+        return AttnResFunction.apply(_attn_res_forward, weight, query, float(eps), *sources)
+    return _attn_res_forward(sources, weight, query, eps)
+
+
+def _attn_res_forward(sources, weight, query, eps):
     sources = [_last_contig(s) for s in sources]
     B, T, D = sources[0].shape
     dt = sources[0].dtype
