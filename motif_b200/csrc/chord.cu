@@ -265,25 +265,27 @@ __global__ void __launch_bounds__(128) chord_fwd_mma_kernel(
 }
 
 // ------------------------------------------------------------------ tcgen05 prefill (16-bit, D = 64)
-// One CTA = two warpgroups, each owning a tile of 128 query rows = G heads of one GQA group x
-// BMQ = 128/G positions (row r of warpgroup w <-> position t0 + w*BMQ + r / G, head
-// h0 + r % G; thread r of the warpgroup owns that row, which is TMEM lane r of its
-// accumulators).  Both tiles read the same 128-key K/V tiles, loaded once per CTA by tiled
-// TMA (128-byte swizzle) into a ring of kStages stages; each warpgroup runs its own loop and
-// the two interleave on the tensor core (while one does its softmax, the other's MMAs run).
-// Per warpgroup and key tile j:
-//   S = Q Kᵀ   tcgen05.mma M=128 N=128 K=64 into the warpgroup's S columns, issued for tile
-//              j+1 as soon as every row has read S(j), so it overlaps the softmax of tile j;
-//   softmax    each row reads its S (tcgen05.ld), applies scale, the GGD bias (per-tile table
-//              over the BMQ + 127 distances the tile spans, per head), mask and log-n scaling,
-//              updates its running max / sum and writes P (16-bit) into shared memory in the
-//              swizzled K-major layout;
-//   O_t = P V  tcgen05.mma M=128 N=64 K=128; the rows read it back and accumulate
-//              o = o * corr + O_t in registers.
-// The warpgroup's first thread issues its MMAs; a K/V stage is refilled by whichever
-// warpgroup finishes with it last.  All waits are bounded: a CTA whose wait runs out counts
-// itself in g_wait_timeouts, drains what it issued, frees its TMEM and leaves its rows
-// unwritten.
+// One CTA = two query tiles of 128 rows = G heads of one GQA group x BMQ = 128/G positions
+// (row r of tile t <-> position t0 + t*BMQ + r / G, head h0 + r % G; row r is TMEM lane r of the
+// tile's accumulators), each served by two warpgroups: thread r of warpgroup `half` takes row r
+// and keys 64 half .. 64 half + 63 of every 128-key tile, so a row's softmax runs on two
+// threads and an SM runs 16 softmax warps.  Both tiles read the same 128-key K/V tiles, loaded
+// once per CTA by tiled TMA (128-byte swizzle) into a ring of kStages stages; each query tile
+// runs its own loop and the two interleave on the tensor core.  Per query tile and key tile j:
+//   S = Q Kᵀ   tcgen05.mma M=128 N=128 K=64 into the tile's S columns, issued for tile j+1 once
+//              every row has read S(j);
+//   softmax    each thread reads its half row of S (tcgen05.ld), applies scale, the GGD bias
+//              (per-tile table over the BMQ + 127 distances the tile spans, per head), mask and
+//              log-n scaling; the two halves' maxima meet in shared memory at the barrier that
+//              also frees S; P (16-bit) goes to the tile's P columns in TMEM (tcgen05.st),
+//              each half its 32 columns;
+//   O += P V   tcgen05.mma M=128 N=64 K=128 with A = P read from TMEM, O accumulated in TMEM
+//              against a reference row max that is raised only when a tile exceeds it by more
+//              than 2^8 (O is then rescaled in TMEM, each half its 32 columns).
+// The halves' row sums are added once, at the end.  The tile's first thread issues its MMAs; a
+// K/V stage is released once P V of both tiles that read it completed.  All waits are bounded:
+// a CTA whose wait runs out counts itself in g_wait_timeouts, drains what it issued, frees its
+// TMEM and leaves its rows unwritten.
 namespace tc {
 constexpr int kKeys = 128, kD = 64;
 constexpr int kTileBytes = 128 * kD * 2;  // 16 KB: 128 rows of 128 bytes
@@ -321,11 +323,12 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 // Barrier over the 128 threads of one warpgroup (ids 1 and 2; 0 is __syncthreads).
-__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;\n" ::"r"(id) : "memory"); }
-__device__ __forceinline__ bool wg_sync_or(int id, bool pred) {
+// Named barriers of one query tile's two warpgroups (256 threads).
+__device__ __forceinline__ void qt_sync(int id) { asm volatile("bar.sync %0, 256;\n" ::"r"(id) : "memory"); }
+__device__ __forceinline__ bool qt_sync_or(int id, bool pred) {
   uint32_t r;
   asm volatile(
-      "{\n .reg .pred ip, op;\n setp.ne.u32 ip, %1, 0;\n bar.red.or.pred op, %2, 128, ip;\n selp.u32 %0, 1, 0, op;\n}\n"
+      "{\n .reg .pred ip, op;\n setp.ne.u32 ip, %1, 0;\n bar.red.or.pred op, %2, 256, ip;\n selp.u32 %0, 1, 0, op;\n}\n"
       : "=r"(r)
       : "r"((uint32_t)pred), "r"(id)
       : "memory");
@@ -341,8 +344,9 @@ struct TcSmemLayout {
   static constexpr int offK = offQ + 2 * tc::kTileBytes;  // kStages
   static constexpr int offV = offK + tc::kStages * tc::kTileBytes;
   static constexpr int offBias = offV + tc::kStages * tc::kTileBytes;  // 2 warpgroups x 2 tiles
-  static constexpr int offKm = offBias + 4 * G * TBLS * 4;          // key bias: 2 warpgroups x 2 tiles
-  static constexpr int offBar = offKm + 4 * tc::kKeys * 4;
+  static constexpr int offKm = offBias + 4 * G * TBLS * 4;          // key bias: 2 query tiles x 2 tiles
+  static constexpr int offX = offKm + 4 * tc::kKeys * 4;            // row exchange [2 query tiles][2 halves][128]
+  static constexpr int offBar = offX + 2 * 2 * 128 * 4;
   static constexpr int nBar = 1 + tc::kStages + 6;  // q, kv[], s[2], o[2], drain[2]
   static constexpr int offCnt = offBar + nBar * 8;   // per-stage release count, last tile issued
   static constexpr int offTmem = offCnt + 2 * tc::kStages * 4;
@@ -353,7 +357,7 @@ struct TcSmemLayout {
 // KM: an additive key bias kmask[b * kms + key] (natural-log units, -inf drops the key) is
 // added to every logit, as the attention mask of chord_attn.py:347-356.
 template <typename T, int G, bool KM>
-__global__ void __launch_bounds__(256, 1) chord_tc_kernel(
+__global__ void __launch_bounds__(512, 1) chord_tc_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const float* __restrict__ alpha, const float* __restrict__ beta,
     const float* __restrict__ mu, const float* __restrict__ ssmax, const float* __restrict__ log_n,
@@ -377,8 +381,11 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
 
   const int64_t* st = sv.s;
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int wg = tid >> 7, wt = tid & 127;
-  const bool issuer = wt == 0;
+  // four warpgroups: two per 128-row query tile (qt), each taking one half of every 128-key tile
+  // (keys 64 half .. +63) for the same rows, so a row's softmax runs on two threads
+  const int wg = tid >> 7, qt = wg >> 1, half = wg & 1, wt = tid & 127;
+  const int ht = half * 128 + wt;  // thread index within the query tile's 256
+  const bool issuer = wt == 0 && half == 0;
   const int GS = H / Hkv;
   const int groups_per_kv = GS / G;
   const int kvh = blockIdx.y / groups_per_kv;
@@ -392,8 +399,8 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   };
   const int nA = tiles_from(tpair), nB = tiles_from(tpair + BMQ);
   const int nall = max(nA, nB);
-  const int t0w = tpair + wg * BMQ;
-  const int nmine = wg ? nB : nA;
+  const int t0w = tpair + qt * BMQ;
+  const int nmine = qt ? nB : nA;
 
   // this thread's row
   const int tl = wt / G, hg = wt % G;
@@ -412,9 +419,10 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   const float scale_s = sgn * scale;
   const float inv_rcs = 1.f / rcs;  // a key bias m (natural log) enters x as m log2(e) / |rc|
 
-  unsigned char* sQw = sQ + wg * tc::kTileBytes;
-  float* sBw = reinterpret_cast<float*>(sm + Lay::offBias) + wg * 2 * G * TBLS;
-  float* sKmw = reinterpret_cast<float*>(sm + Lay::offKm) + wg * 2 * tc::kKeys;
+  unsigned char* sQw = sQ + qt * tc::kTileBytes;
+  float* sBw = reinterpret_cast<float*>(sm + Lay::offBias) + qt * 2 * G * TBLS;
+  float* sKmw = reinterpret_cast<float*>(sm + Lay::offKm) + qt * 2 * tc::kKeys;
+  float* sXq = reinterpret_cast<float*>(sm + Lay::offX) + qt * 2 * 128;  // [half][row]
 
   if (warp == 0) tmem_alloc(sTmem, tc::kTmemCols);
   if (tid == 0) {
@@ -429,8 +437,9 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sTmem;
-  // TMEM columns of this warpgroup: S (128 fp32) | P (128 16-bit keys, 64 columns) | O (64 fp32)
-  const uint32_t colS = wg * 256, colP = colS + tc::kKeys, colO = colP + tc::kKeys / 2;
+  // TMEM columns of the query tile: S (128 fp32) | P (128 16-bit keys, 64 columns) | O (64 fp32);
+  // this half reads S columns 64 half .., writes P columns 32 half .., rescales O columns 32 half ..
+  const uint32_t colS = qt * 256, colP = colS + tc::kKeys, colO = colP + tc::kKeys / 2;
 
   auto issue_kv = [&](int j) {  // one thread
     const int s = j % NS;
@@ -445,7 +454,7 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     for (int ks = 0; ks < tc::kD / 16; ++ks)
       umma_f16_ss(tmem + colS, umma_desc_sw128(qa + ks * 32, 16, 1024), umma_desc_sw128(ka + ks * 32, 16, 1024),
                   idS, ks > 0);
-    umma_commit(&barS[wg]);
+    umma_commit(&barS[qt]);
   };
   auto issue_o = [&](int j) {  // warpgroup issuer: O (+)= P_w V_j, P from this warpgroup's TMEM
     const uint32_t va = smem_u32(sV + (j % NS) * tc::kTileBytes);
@@ -453,20 +462,22 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     for (int ks = 0; ks < tc::kKeys / 16; ++ks)
       umma_f16_ts(tmem + colO, tmem + colP + ks * 8, umma_desc_sw128(va + ks * 16 * 128, tc::kTileBytes, 1024), idO,
                   (j > 0 || ks > 0) ? 1u : 0u);
-    umma_commit(&barO[wg]);
+    umma_commit(&barO[qt]);
   };
-  auto fill_bias = [&](int j) {  // warpgroup: table of tile j into buffer j & 1
+  auto fill_bias = [&](int j) {  // the query tile's 256 threads: table of tile j into buffer j & 1
     float* tb = sBw + (j & 1) * G * TBLS;
     const int base = q_start + t0w - j * tc::kKeys - 127;  // distance of entry 0
-    for (int e = wt; e < G * TBL; e += 128) {
+    for (int e = ht; e < G * TBL; e += 256) {
       const int g = e / TBL, ee = e % TBL;
       const int hh = h0 + g;
       const float b0 = ggd_bias_decode<T>(alpha[hh], beta[hh], mu[hh], (float)(base + ee), eps);
       tb[g * TBLS + ee] = ssmax[hh] < 0.f ? -b0 : b0;
     }
     if constexpr (KM) {  // the tile's key bias in log2 units
-      const int key = j * tc::kKeys + wt;
-      sKmw[(j & 1) * tc::kKeys + wt] = key < S ? kmask[(int64_t)b * kms + key] * kLog2e : 0.f;
+      if (half == 0) {
+        const int key = j * tc::kKeys + wt;
+        sKmw[(j & 1) * tc::kKeys + wt] = key < S ? kmask[(int64_t)b * kms + key] * kLog2e : 0.f;
+      }
     }
   };
 
@@ -508,31 +519,57 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
   };
 
+  constexpr int HK = tc::kKeys / 2;  // keys of one half
   for (int j = 0; j < nmine; ++j) {
-    bool ok = failed ? false : mbar_wait_bounded(&barS[wg], (uint32_t)(j & 1), tc::kWait);
+    bool ok = failed ? false : mbar_wait_bounded(&barS[qt], (uint32_t)(j & 1), tc::kWait);
     tc_fence_after();
-    float x[tc::kKeys];
+    float x[HK];
     {
-      uint32_t r0[32], r1[32], r2[32], r3[32];
-      const uint32_t ta = tmem + lane_base + colS;
+      uint32_t r0[32], r1[32];
+      const uint32_t ta = tmem + lane_base + colS + (uint32_t)(half * HK);
       tmem_ld32(ta, r0);
       tmem_ld32(ta + 32, r1);
-      tmem_ld32(ta + 64, r2);
-      tmem_ld32(ta + 96, r3);
       tmem_wait_ld(r0);
       tmem_wait_ld(r1);
-      tmem_wait_ld(r2);
-      tmem_wait_ld(r3);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         x[i] = __uint_as_float(r0[i]);
         x[32 + i] = __uint_as_float(r1[i]);
-        x[64 + i] = __uint_as_float(r2[i]);
-        x[96 + i] = __uint_as_float(r3[i]);
       }
     }
     tc_fence_before();
-    wg_sync(1 + wg);  // every row holds S(j): the columns may take S(j + 1)
+
+    // x = +-(s * scale + bias) (sign of ssmax folded in); keys past the row's last visible key
+    // (causal, or at / past S) are set to -inf only on the tiles that contain such keys
+    const int k0 = j * tc::kKeys + half * HK;
+    const int cmax = min(HK - 1, min(S - 1 - k0, qpos - k0));
+    const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127 - half * HK;  // key offset c -> tb[-c]
+#pragma unroll
+    for (int c = 0; c < HK; c += 2) {
+      const float2 y = ffma2(make_float2(x[c], x[c + 1]), make_float2(scale_s, scale_s),
+                             make_float2(tb[-c], tb[-c - 1]));
+      x[c] = y.x;
+      x[c + 1] = y.y;
+    }
+    if constexpr (KM) {
+      const float* km = sKmw + (j & 1) * tc::kKeys + half * HK;
+#pragma unroll
+      for (int c = 0; c < HK; ++c) x[c] = fmaf(km[c], inv_rcs, x[c]);
+    }
+    if (cmax < HK - 1) {
+#pragma unroll
+      for (int c = 0; c < HK; ++c)
+        if (c > cmax) x[c] = -INFINITY;
+    }
+    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int c = 0; c < HK; c += 2) mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], x[c], x[c + 1]);
+    float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+    // the row's two halves meet: every thread of the query tile holds S(j) (the columns may take
+    // S(j + 1)) and has its half's max in the exchange
+    sXq[half * 128 + wt] = mt;
+    qt_sync(1 + qt);
+    mt = fmaxf(mt, sXq[(half ^ 1) * 128 + wt]);
     if (issuer && !failed && j + 1 < nmine) {
       const int jn = j + 1;
       if (mbar_wait_bounded(&barKV[jn % NS], (uint32_t)((jn / NS) & 1), tc::kWait)) {
@@ -544,33 +581,8 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
     if (j + 1 < nmine) fill_bias(j + 1);
 
-    // x = +-(s * scale + bias) (sign of ssmax folded in); keys past the row's last visible key
-    // (causal, or at / past S) are set to -inf only on the tiles that contain such keys
-    const int k0 = j * tc::kKeys;
-    const int cmax = min(tc::kKeys - 1, min(S - 1 - k0, qpos - k0));
-    const float* tb = sBw + (j & 1) * G * TBLS + hg * TBLS + tl + 127;  // key offset c -> tb[-c]
-#pragma unroll
-    for (int c = 0; c < tc::kKeys; c += 2) {
-      const float2 y = ffma2(make_float2(x[c], x[c + 1]), make_float2(scale_s, scale_s),
-                             make_float2(tb[-c], tb[-c - 1]));
-      x[c] = y.x;
-      x[c + 1] = y.y;
-    }
-    if constexpr (KM) {
-      const float* km = sKmw + (j & 1) * tc::kKeys;
-#pragma unroll
-      for (int c = 0; c < tc::kKeys; ++c) x[c] = fmaf(km[c], inv_rcs, x[c]);
-    }
-    if (cmax < tc::kKeys - 1) {
-#pragma unroll
-      for (int c = 0; c < tc::kKeys; ++c)
-        if (c > cmax) x[c] = -INFINITY;
-    }
-    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-    for (int c = 0; c < tc::kKeys; c += 2) mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], x[c], x[c + 1]);
-    const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
     // raise the reference max on the first visible key, or when this tile exceeds it by > 2^8
+    // (both halves of a row take the same decision: the same mt and m_ref)
     const bool raise = mt > m_ref && (m_ref == -INFINITY || (mt - m_ref) * rcs > kRescale);
     float corr = 1.f;
     if (raise) {
@@ -579,53 +591,43 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
     }
     const float nb = -(m_ref == -INFINITY ? 0.f : m_ref) * rcs;
     float2 ps4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-    uint32_t pw0[32], pw1[32];  // P row packed in 16-bit pairs: keys 0..63, 64..127
+    uint32_t pw[32];  // this half's P row packed in 16-bit pairs
 #pragma unroll
-    for (int c = 0; c < tc::kKeys; c += 2) {
+    for (int c = 0; c < HK; c += 2) {
       const float2 t = ffma2(make_float2(x[c], x[c + 1]), make_float2(rcs, rcs), make_float2(nb, nb));
       const float p0 = ex2_approx(t.x);
       const float p1 = ex2_approx(t.y);
       ps4[(c >> 1) & 3] = fadd2(ps4[(c >> 1) & 3], make_float2(p0, p1));
-      if (c < 64)
-        pw0[c >> 1] = pack2<T>(p0, p1);
-      else
-        pw1[(c - 64) >> 1] = pack2<T>(p0, p1);
+      pw[c >> 1] = pack2<T>(p0, p1);
     }
     {
       const float2 q = fadd2(fadd2(ps4[0], ps4[1]), fadd2(ps4[2], ps4[3]));
-      l = l * corr + (q.x + q.y);
+      l = l * corr + (q.x + q.y);  // this half's share of the row sum
     }
     // P V(j - 1) has completed: its P columns may be overwritten, O may be rescaled, and its K/V
     // stage released
     if (j > 0) {
-      if (!mbar_wait_bounded(&barO[wg], (uint32_t)((j - 1) & 1), tc::kWait)) ok = false;
+      if (!mbar_wait_bounded(&barO[qt], (uint32_t)((j - 1) & 1), tc::kWait)) ok = false;
       tc_fence_after();
       if (issuer && !failed) release(j - 1);
       if (__any_sync(0xffffffffu, raise)) {  // warp-collective: rows without a raise scale by 1
-        uint32_t o0[32], o1[32];
-        const uint32_t ta = tmem + lane_base + colO;
+        uint32_t o0[32];
+        const uint32_t ta = tmem + lane_base + colO + (uint32_t)(half * 32);
         tmem_ld32(ta, o0);
-        tmem_ld32(ta + 32, o1);
         tmem_wait_ld(o0);
-        tmem_wait_ld(o1);
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const float2 u0 = fmul2(make_float2(__uint_as_float(o0[i]), __uint_as_float(o0[i + 1])), make_float2(corr, corr));
-          const float2 u1 = fmul2(make_float2(__uint_as_float(o1[i]), __uint_as_float(o1[i + 1])), make_float2(corr, corr));
           o0[i] = __float_as_uint(u0.x);
           o0[i + 1] = __float_as_uint(u0.y);
-          o1[i] = __float_as_uint(u1.x);
-          o1[i + 1] = __float_as_uint(u1.y);
         }
         tmem_st32(ta, o0);
-        tmem_st32(ta + 32, o1);
       }
     }
-    tmem_st32(tmem + lane_base + colP, pw0);
-    tmem_st32(tmem + lane_base + colP + 32, pw1);
+    tmem_st32(tmem + lane_base + colP + (uint32_t)(half * 32), pw);
     tmem_wait_st();
     tc_fence_before();
-    if (wg_sync_or(1 + wg, !ok || failed)) {
+    if (qt_sync_or(3 + qt, !ok || failed)) {
       failed = true;
       break;
     }
@@ -634,18 +636,18 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       issue_o(j);
     }
   }
-  // the last P V of this warpgroup, then its stage
+  // the last P V of this query tile, then its stage
   bool okO = true;
   if (!failed && nmine > 0) {
-    okO = mbar_wait_bounded(&barO[wg], (uint32_t)((nmine - 1) & 1), tc::kWait);
+    okO = mbar_wait_bounded(&barO[qt], (uint32_t)((nmine - 1) & 1), tc::kWait);
     tc_fence_after();
     if (issuer && okO) release(nmine - 1);
   }
   failed = __syncthreads_or(failed || !okO);
   if (failed) {
-    if (issuer) {  // every MMA this warpgroup issued
-      umma_commit(&barDrain[wg]);
-      mbar_wait_bounded(&barDrain[wg], 0, tc::kWait);
+    if (issuer) {  // every MMA this query tile issued
+      umma_commit(&barDrain[qt]);
+      mbar_wait_bounded(&barDrain[qt], 0, tc::kWait);
     }
     __syncthreads();
     if (tid == 0) {  // every copy issued (the latest into each stage is the only one pending)
@@ -656,18 +658,21 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
           mbar_wait_bounded(&barKV[s], (uint32_t)((stage_tile[s] / NS) & 1), tc::kWait);
     }
   } else if (nmine > 0) {
-    uint32_t o0[32], o1[32];
-    const uint32_t ta = tmem + lane_base + colO;
+    // the row sum: this half's share plus the other half's (the exchange is free again: every
+    // thread passed the last loop barrier after its reads)
+    sXq[half * 128 + wt] = l;
+    qt_sync(1 + qt);
+    const float lt = l + sXq[(half ^ 1) * 128 + wt];
+    uint32_t o0[32];
+    const uint32_t ta = tmem + lane_base + colO + (uint32_t)(half * 32);
     tmem_ld32(ta, o0);
-    tmem_ld32(ta + 32, o1);
     tmem_wait_ld(o0);
-    tmem_wait_ld(o1);
     if (row_ok) {
-      const float inv = 1.f / fmaxf(l, 1e-20f);
-      T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11];
+      const float inv = 1.f / fmaxf(lt, 1e-20f);
+      T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11] + half * 32;
 #pragma unroll
-      for (int c8 = 0; c8 < tc::kD / 8; ++c8) {
-        const uint32_t* src = c8 < 4 ? &o0[c8 * 8] : &o1[(c8 - 4) * 8];
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const uint32_t* src = &o0[c8 * 8];
         uint4 v;
         v.x = pack2<T>(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
         v.y = pack2<T>(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
@@ -677,9 +682,9 @@ __global__ void __launch_bounds__(256, 1) chord_tc_kernel(
       }
     }
   } else if (row_ok) {  // no visible key (cannot happen for q_start >= 0): zeros
-    T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11];
+    T* orow = out + b * st[9] + (int64_t)h * st[10] + (int64_t)pos * st[11] + half * 32;
 #pragma unroll
-    for (int c8 = 0; c8 < tc::kD / 8; ++c8) *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(0, 0, 0, 0);
+    for (int c8 = 0; c8 < 4; ++c8) *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(0, 0, 0, 0);
   }
   tc_fence_before();
   __syncthreads();
@@ -1546,7 +1551,7 @@ int launch_tc_g(const void* q, const void* k, const void* v, const float* alpha,
   if (int rc = ensure_smem_attr((const void*)kern, Lay::alloc)) return rc;
   const int GS = (int)(H / Hkv);
   dim3 grid((unsigned)((L + 2 * Lay::BMQ - 1) / (2 * Lay::BMQ)), (unsigned)(Hkv * (GS / G)), (unsigned)B);
-  kern<<<grid, 256, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
+  kern<<<grid, 512, Lay::alloc, st>>>(tmQ, tmK, tmV, alpha, beta, mu, ssmax, log_n, (T*)out, (int)H, (int)Hkv, (int)L,
                                      (int)S, (int)q_start, scale, eps, sv, kmask, kms);
   return check_launch("chord_attention (tcgen05)");
 }
