@@ -464,13 +464,16 @@ MB_API int motif_b200_sample(const void* logits, int64_t ld, int64_t B, int64_t 
  *   MB_FORCE_DECODE_SCALAR   16-bit D = 64 Chord decode on the CUDA-core kernel (fp32's)
  *   MB_FORCE_GDN_PRECISE     16-bit chunked delta rule on the 3xTF32 kernel (fp32's)
  *   MB_FORCE_GDN_FUSED       16-bit chunked delta rule with a workspace on the single fused
- *                            kernel (the no-workspace path) */
+ *                            kernel (the no-workspace path)
+ *   MB_FORCE_GDN_WIDE        the split path's state scan on 64-column value slices even for small
+ *                            batches (which take 32-column slices; the results are identical) */
 enum {
   MB_FORCE_CHORD_MMA_SYNC = 0,
   MB_FORCE_DECODE_SCALAR = 1,
   MB_FORCE_GDN_PRECISE = 2,
   MB_FORCE_GDN_FUSED = 3,
-  MB_FORCE_COUNT = 4
+  MB_FORCE_GDN_WIDE = 4,
+  MB_FORCE_COUNT = 5
 };
 MB_API int motif_b200_testing_force(int knob, int value);
 

@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'libmotif_b2
 MB_OK, MB_ERR_ARG, MB_ERR_SHAPE, MB_ERR_DTYPE, MB_ERR_ALIGN, MB_ERR_UNSUPPORTED, MB_ERR_CUDA = range(7)
 MB_F32, MB_F16, MB_BF16 = 0, 1, 2
 # testing knobs of motif_b200_testing_force (include/motif_b200.h)
-FORCE_CHORD_MMA_SYNC, FORCE_DECODE_SCALAR, FORCE_GDN_PRECISE, FORCE_GDN_FUSED = range(4)
+FORCE_CHORD_MMA_SYNC, FORCE_DECODE_SCALAR, FORCE_GDN_PRECISE, FORCE_GDN_FUSED, FORCE_GDN_WIDE = range(5)
 ABI_VERSION = 1
 
 _P = ctypes.c_void_p

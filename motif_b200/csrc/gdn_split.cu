@@ -39,9 +39,9 @@ using namespace gdnk;
 // slice of the scan reads, then one U plane per slice of SW value columns:
 //   Qs [C][QS] = q e^gamma | Kd [C][QS] = k e^{gamma_L - gamma} | W [C][QS] | Aq [C][AS] (T) |
 //   e^{gamma_L} (fp32, padded to 16 bytes) | U_0 [C][US] | U_1 [C][US] | ...
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, int SWP = 64>
 struct WsRec {
-  static constexpr int SW = DV < 64 ? DV : 64;  // value columns per scan slice
+  static constexpr int SW = DV < SWP ? DV : SWP;  // value columns per scan slice
   static constexpr int NSL = DV / SW;
   static_assert(DV % SW == 0, "value columns split into equal slices");
   static constexpr int QS = DK + 8, AS = C + 8, US = SW + 8;
@@ -107,13 +107,13 @@ __device__ __forceinline__ void wy_gamma(int lane, float x0, float x1, float b0,
   sBeta[lane + 32] = b1;
 }
 
-template <typename T, int DK, int DV, bool PREP>
+template <typename T, int DK, int DV, bool PREP, int SWP>
 __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                     const T* __restrict__ v, const float* __restrict__ beta,
                                                     const float* __restrict__ g, int H, int L, Strides18 sv,
                                                     unsigned char* __restrict__ ws, PrepIn<T> pin) {
   using Lay = WyLayout<T, DK, DV>;
-  using Rec = WsRec<T, DK, DV>;
+  using Rec = WsRec<T, DK, DV, SWP>;
   constexpr int QS = Lay::QS, VS = Lay::VS, AS = Lay::AS, XS = Lay::XS, TS = Lay::TS;
   constexpr int NTILE = (DK + DV) / 8;
   constexpr int SOLVE_T = (NTILE + NW - 1) / NW;
@@ -516,9 +516,9 @@ __global__ void __launch_bounds__(NT, 2) gdn_wy_kernel(const T* __restrict__ q, 
   }
 }
 
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, int SWP>
 struct RecLayout {
-  using Rec = WsRec<T, DK, DV>;
+  using Rec = WsRec<T, DK, DV, SWP>;
   static constexpr int SS = Rec::SW + 8;  // state slice row stride (elements)
   static constexpr size_t stage_bytes = Rec::shared_bytes + Rec::u_bytes;
   static constexpr size_t off_stage = 0;  // 2 stages: the shared part + this slice's U plane
@@ -536,12 +536,12 @@ __device__ unsigned int g_gdn_wait_timeouts = 0;
 // independently (X = U - W S, o = Qs S + Aq X and S' = e^gL S + Kd^T X act column by column),
 // so each slice scans its own DK x SW block of the state.  Adjacent CTAs are the slices of one
 // (sequence, head) and read the record's shared part at about the same time, from L2.
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, int SWP>
 __global__ void __launch_bounds__(NT, 2) gdn_rec_kernel(const unsigned char* __restrict__ ws,
                                                         const float* __restrict__ s_in, float* __restrict__ s_out,
                                                         T* __restrict__ o, int H, int L, Strides18 sv) {
-  using Lay = RecLayout<T, DK, DV>;
-  using Rec = WsRec<T, DK, DV>;
+  using Lay = RecLayout<T, DK, DV, SWP>;
+  using Rec = WsRec<T, DK, DV, SWP>;
   constexpr int QS = Rec::QS, AS = Rec::AS, US = Rec::US, SW = Rec::SW, SS = Lay::SS;
   constexpr int SM_T = DK / 16;
   constexpr int HT = SW / 16;  // n8 tiles per warp (two column groups of SW / 2)
@@ -795,15 +795,26 @@ __global__ void __launch_bounds__(256) gdn_gate_norm_kernel(T* __restrict__ o, i
   }
 }
 
-template <typename T, int DK, int DV, bool PREP = false>
-int launch_split(const void* q, const void* k, const void* v, const float* beta, const float* g,
-                 const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, const Strides18& sv,
-                 const void* gate, int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, void* ws,
-                 cudaStream_t stream, PrepIn<T> pin = PrepIn<T>{}) {
+// Value-column slices of the state scan: 64 wide, or 32 when the 64-wide slicing would occupy at
+// most half of the SMs (tiny batches: 1-2 sequences x 12 heads), so the latency-bound chunk
+// chains spread over more SMs.  Measured on the 172M prefill at T = 4096: 3.60 vs 3.96 ms at
+// B = 1, 5.76 vs 6.08 at B = 2, equal at B = 4; wider batches (4 x 12 heads at Dv = 128 and the
+// 8 x 12 x 64 op) are 5-7 % faster on 64-column slices.
+bool narrow_slices(int64_t B, int64_t H, int64_t Dv) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return Dv >= 64 && 2 * B * H * (Dv / 64) <= (int64_t)sms && !forced(MB_FORCE_GDN_WIDE);
+}
+
+template <typename T, int DK, int DV, bool PREP, int SWP>
+int launch_split_sw(const void* q, const void* k, const void* v, const float* beta, const float* g,
+                    const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, const Strides18& sv,
+                    const void* gate, int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, void* ws,
+                    cudaStream_t stream, PrepIn<T> pin) {
   using WL = WyLayout<T, DK, DV>;
-  using RL = RecLayout<T, DK, DV>;
-  auto k1 = gdn_wy_kernel<T, DK, DV, PREP>;
-  auto k2 = gdn_rec_kernel<T, DK, DV>;
+  using RL = RecLayout<T, DK, DV, SWP>;
+  auto k1 = gdn_wy_kernel<T, DK, DV, PREP, SWP>;
+  auto k2 = gdn_rec_kernel<T, DK, DV, SWP>;
   if (int rc0 = ensure_smem_attr((const void*)k1, (int)WL::bytes)) return rc0;
   if (int rc0 = ensure_smem_attr((const void*)k2, (int)RL::bytes)) return rc0;
   const int64_t nchunks = (L + C - 1) / C;
@@ -811,7 +822,7 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
       (const T*)q, (const T*)k, (const T*)v, beta, g, (int)H, (int)L, sv, (unsigned char*)ws, pin);
   int rc = check_launch("gdn_chunk (UT transform)");
   if (rc) return rc;
-  k2<<<(unsigned)(B * H * WsRec<T, DK, DV>::NSL), NT, RL::bytes, stream>>>((const unsigned char*)ws, s_in, s_out,
+  k2<<<(unsigned)(B * H * WsRec<T, DK, DV, SWP>::NSL), NT, RL::bytes, stream>>>((const unsigned char*)ws, s_in, s_out,
                                                                              (T*)o, (int)H, (int)L, sv);
   rc = check_launch("gdn_chunk (state scan)");
   if (rc || gate == nullptr) return rc;
@@ -826,6 +837,18 @@ int launch_split(const void* q, const void* k, const void* v, const float* beta,
   return check_launch("gdn_chunk (gated norm)");
 }
 
+template <typename T, int DK, int DV, bool PREP = false>
+int launch_split(const void* q, const void* k, const void* v, const float* beta, const float* g,
+                 const float* s_in, float* s_out, void* o, int64_t B, int64_t H, int64_t L, const Strides18& sv,
+                 const void* gate, int64_t gate_rs, int64_t gate_hs, const void* onorm_w, float eps, void* ws,
+                 cudaStream_t stream, PrepIn<T> pin = PrepIn<T>{}) {
+  if (narrow_slices(B, H, DV))
+    return launch_split_sw<T, DK, DV, PREP, 32>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs, gate_hs,
+                                               onorm_w, eps, ws, stream, pin);
+  return launch_split_sw<T, DK, DV, PREP, 64>(q, k, v, beta, g, s_in, s_out, o, B, H, L, sv, gate, gate_rs, gate_hs,
+                                             onorm_w, eps, ws, stream, pin);
+}
+
 }  // namespace
 
 // Workspace bytes of the split path for (Dk, Dv), or 0 when no split kernel exists.
@@ -833,9 +856,10 @@ int64_t gdn_split_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t Dk, i
   if (dtype != MB_BF16 && dtype != MB_F16) return 0;
   const int64_t nchunks = (L + C - 1) / C;
   int64_t rec = 0;
-  if (Dk == 32 && Dv == 64) rec = WsRec<__nv_bfloat16, 32, 64>::bytes;
-  if (Dk == 64 && Dv == 64) rec = WsRec<__nv_bfloat16, 64, 64>::bytes;
-  if (Dk == 64 && Dv == 128) rec = WsRec<__nv_bfloat16, 64, 128>::bytes;
+  const bool nar = narrow_slices(B, H, Dv);
+  if (Dk == 32 && Dv == 64) rec = nar ? WsRec<__nv_bfloat16, 32, 64, 32>::bytes : WsRec<__nv_bfloat16, 32, 64>::bytes;
+  if (Dk == 64 && Dv == 64) rec = nar ? WsRec<__nv_bfloat16, 64, 64, 32>::bytes : WsRec<__nv_bfloat16, 64, 64>::bytes;
+  if (Dk == 64 && Dv == 128) rec = nar ? WsRec<__nv_bfloat16, 64, 128, 32>::bytes : WsRec<__nv_bfloat16, 64, 128>::bytes;
   return B * H * nchunks * rec;
 }
 

@@ -659,3 +659,62 @@ def test_chord_masked_all_keys_dropped_gives_zeros():
               _lib.ptr(kb.cuda()), S, _lib.dtype_code(torch.bfloat16), st())
     assert bool((out[:, :, :4] == 0).all()) and torch.isfinite(out).all()
     assert bool((out[:, :, 4:].abs().sum(-1) > 0).all())
+
+
+@pytest.mark.parametrize('B,H,T,dk,dv,with_state', [(2, 12, 300, 64, 128, True), (1, 12, 4096, 64, 128, False),
+                                                    (1, 3, 70, 64, 128, True)])
+def test_gdn_split_narrow_slices_equal_wide(B, H, T, dk, dv, with_state):
+    """Tiny batches scan 32-column value slices (twice the CTAs of the 64-column ones); the
+    columns of the state evolve independently, so both slicings give the same bits, for the
+    whole-layer prefill (preparation fused) and the split call on prepared inputs."""
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(B * T + dv)
+    C = H * (2 * dk + dv)
+    N = C + 2 * H + H * dv
+    N += (-N) % 8
+    proj = (0.5 * torch.randn(B * T, N, generator=g)).to(dtype).cuda()
+    conv_w = (0.3 * torch.randn(C, 4, generator=g)).to(dtype).cuda()
+    A_log = torch.log(1 + 15 * torch.rand(H, generator=g)).to(dtype).cuda()
+    dt_bias = (0.1 * torch.randn(H, generator=g)).to(dtype).cuda()
+    conv_in = (0.5 * torch.randn(B, 3, C, generator=g)).to(dtype).cuda()
+    s_in = (0.1 * torch.randn(B, H, dk, dv, generator=g)).cuda() if with_state else None
+    onw = (1 + 0.1 * torch.randn(dv, generator=g)).to(dtype).cuda()
+    dc, s = _lib.MB_BF16, st()
+    M = B * T
+
+    def layer():
+        ws_bytes = _lib.load().motif_b200_gdn_chunk_workspace_bytes(B, H, T, dk, dv, dc)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda')
+        out = torch.empty(M, H * dv, dtype=dtype, device='cuda')
+        co = torch.empty(B, 3, C, dtype=dtype, device='cuda')
+        S = torch.empty(B, H, dk, dv, device='cuda')
+        _lib.call('motif_b200_gdn_prefill_ws', _lib.ptr(proj), N, _lib.ptr(conv_w), _lib.ptr(A_log),
+                  _lib.ptr(dt_bias), _lib.ptr(conv_in), _lib.ptr(co), _lib.ptr(s_in), _lib.ptr(S), _lib.ptr(onw), 1e-6,
+                  _lib.ptr(out), H * dv, B, T, H, dk, dv, dc, _lib.ptr(ws), ws_bytes, s)
+        torch.cuda.synchronize()
+        return out, S
+
+    narrow = layer()
+    with _lib.forced(_lib.FORCE_GDN_WIDE):
+        wide = layer()
+    assert torch.equal(narrow[0], wide[0]) and torch.equal(narrow[1], wide[1])
+    assert _lib.wait_timeouts() == 0
+
+
+@pytest.mark.parametrize('B,H,L,dk,dv', [(2, 4, 300, 64, 64), (2, 12, 1000, 64, 64), (1, 2, 130, 32, 64)])
+def test_gdn_chunk_op_narrow_slices_equal_wide(B, H, L, dk, dv):
+    """The chunked delta-rule op (config 2's shape family) through the split path: 32- and
+    64-column scan slices give the same bits."""
+    from motif_b200 import ops
+    g = torch.Generator().manual_seed(L + B)
+    q = torch.nn.functional.normalize(torch.randn(B, H, L, dk, generator=g), dim=-1).bfloat16().cuda()
+    k = torch.nn.functional.normalize(torch.randn(B, H, L, dk, generator=g), dim=-1).bfloat16().cuda()
+    v = torch.randn(B, H, L, dv, generator=g).bfloat16().cuda()
+    beta = torch.rand(B, H, L, generator=g).cuda()
+    gg = (-0.2 * torch.rand(B, H, L, generator=g)).cuda()
+    S0 = (0.1 * torch.randn(B, H, dk, dv, generator=g)).cuda()
+    o1, s1 = ops.chunk_gated_delta_rule(q, k, v, beta, gg, S0)
+    with _lib.forced(_lib.FORCE_GDN_WIDE):
+        o2, s2 = ops.chunk_gated_delta_rule(q, k, v, beta, gg, S0)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
