@@ -306,7 +306,8 @@ def _skinny_packed(w: torch.Tensor) -> Optional[torch.Tensor]:
     if not w.is_cuda or w.dtype not in (torch.bfloat16, torch.float16) or w.dim() != 2:
         return None
     N, K = w.shape
-    if K % 16 or N % 4 or w.stride(1) != 1 or w.stride(0) % 2 or w.data_ptr() % 4:
+    # K up to 8 cluster splits x 4 warps x 12 k-tiles of 16 (the kernel's split limits)
+    if K % 16 or K > 8 * 4 * 12 * 16 or N % 4 or w.stride(1) != 1 or w.stride(0) % 2 or w.data_ptr() % 4:
         return None
     nbytes = _lib.load().motif_b200_skinny_packed_bytes(N, K)
     out = torch.empty(nbytes // w.element_size(), dtype=w.dtype, device=w.device)
