@@ -504,9 +504,10 @@ DECODE_GEMM_SHAPES = {'gdn_in_proj': (8728, 768), 'gdn_out_proj': (768, 3584), '
 
 
 def run_decode_gemm_shapes(dev, pk, M=64, reps=24):
-    """The skinny GEMM (`motif_b200_skinny_gemm` on fragment-packed weights) against the library
-    GEMM (torch.mm -> cuBLAS) on config 5's decode products at M rows (64: one GPU; 8: eight GPUs
-    of the strong split), bf16: each timed as a CUDA graph of
+    """The skinny GEMM (`motif_b200_skinny_gemm` on fragment-packed weights, 'ours') and the
+    tensor-core decode GEMM (`motif_b200_skinny_gemm_tc`, 'tc') against the library GEMM (torch.mm
+    -> cuBLAS) on config 5's decode products at M rows (64: one GPU; 8: eight GPUs of the strong
+    split), bf16: each timed as a CUDA graph of
     `reps` back-to-back products whose weights rotate through enough copies to exceed L2 twice
     (every product streams its weight from HBM, as in the decode step)."""
     from motif_b200 import _lib
@@ -531,8 +532,13 @@ def run_decode_gemm_shapes(dev, pk, M=64, reps=24):
             for i in range(reps):
                 torch.mm(x, ws[i % copies].t(), out=y)
 
+        def ours_tc():
+            for i in range(reps):
+                _lib.call('motif_b200_skinny_gemm_tc', x.data_ptr(), K, ws[i % copies].data_ptr(), K, y.data_ptr(), N,
+                          M, N, K, 0, _lib.MB_BF16, _lib.stream_ptr(dev))
+
         r = {'M': M, 'N': N, 'K': K, 'weight_bytes': wbytes}
-        for tag, fn in (('ours', ours), ('cublas', lib)):
+        for tag, fn in (('ours', ours), ('tc', ours_tc), ('cublas', lib)):
             s_ = torch.cuda.Stream(dev)
             s_.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(s_):
@@ -547,6 +553,7 @@ def run_decode_gemm_shapes(dev, pk, M=64, reps=24):
             r[f'{tag}_weight_gbs'] = wbytes / (ms / 1000.0) / 1e9
             del gr
         r['ours_frac_of_measured_hbm'] = r['ours_weight_gbs'] / pk['hbm_gbs']
+        r['tc_frac_of_measured_hbm'] = r['tc_weight_gbs'] / pk['hbm_gbs']
         res[name] = r
         del ws, ps, x, y
         torch.cuda.empty_cache()

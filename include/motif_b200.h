@@ -335,6 +335,20 @@ MB_API int motif_b200_skinny_pack(const void* w, int64_t ldw, int64_t N, int64_t
 MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* packed, void* y, int64_t ldy, int64_t M,
                                   int64_t N, int64_t K, int k_warps, int split_k, int dtype, void* stream);
 
+/* Decode-sized products on the tensor cores: Y[M, N] = X[M, K] . W[N, K]^T for 1 <= M <= 64
+ * (the one-GPU decode batch), 16-bit operands, fp32 accumulation, on the weight itself (no
+ * packing).  X and W rows 16-byte aligned (ldx, ldw multiples of 8), K a multiple of 64; Y row
+ * stride ldy, N and ldy multiples of 4, Y 8-byte aligned.  Each CTA streams one 128-feature
+ * tile of W over a run of K by tiled TMA, requested before the kernel waits on the previous
+ * kernel (programmatic dependent launch), into tcgen05.mma with a TMEM accumulator; K is split
+ * across the CTAs of a cluster (at most 8) whose fp32 partial tiles are exchanged by bulk
+ * copies between their shared memories and summed in a fixed order (deterministic).  split_k
+ * (1 .. 8) forces the split; 0 lets the library choose.  Asynchronous on `stream`.
+ * Replaces the same decode-time nn.Linear products as motif_b200_skinny_gemm
+ * (gdn_attn.py:88-94, chord_attn.py:88-96, mlp.py:52-53, the decoders' o_proj / down_proj). */
+MB_API int motif_b200_skinny_gemm_tc(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                                     int64_t M, int64_t N, int64_t K, int split_k, int dtype, void* stream);
+
 /* ------------------------------------------------------------------ backward (training)
  * Gradients of the three hot-path ops, fp32 arithmetic on CUDA cores (16-bit inputs widened on
  * load), asynchronous on `stream`.

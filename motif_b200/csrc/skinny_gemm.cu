@@ -29,7 +29,9 @@
 // mlp.py:52-53, decoder.py o_proj / down_proj, motif.py lm_head), which cuBLAS runs as
 // weight-bandwidth-bound small-M GEMMs.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 #include "gdn_mma.cuh"
@@ -450,4 +452,362 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* pa
     }
   };
   return dtype == MB_BF16 ? by_n(__nv_bfloat16{}) : by_n(__half{});
+}
+
+// ----------------------------------------------------------------------------------------
+// Tensor-core variant for 33 .. 64 token rows (one GPU's decode batch of the 172M model: 64
+// requests).  At these row counts the legacy-MMA kernel above spends as long on its MMAs and
+// on the cluster exchange of wide partial tiles as on the weight stream, so:
+//   * Y^T tile = W tile (128 features, the MMA's M) x X^T (64 token columns, the MMA's N) as
+//     tcgen05.mma kind::f16 into a 64-column TMEM accumulator, both operands staged by tiled
+//     TMA (128-byte swizzle) in 64-deep K blocks; tokens past M are the tensor map's zero fill;
+//   * a CTA takes one feature tile and a contiguous run of K blocks (split s = blockIdx.y of a
+//     cluster of S along y); every W block of its ring is requested before the kernel waits on
+//     its predecessor (programmatic dependent launch), X after the wait;
+//   * the split-K partials (fp32, token-major [64][128]) stay in each CTA's shared memory;
+//     after one cluster barrier CTA r reads the token rows it owns from all S partials through
+//     distributed shared memory, every read of a thread in flight at once, and adds them in rank
+//     order (deterministic) before storing them.
+// Every wait is bounded (counted in motif_b200_wait_timeouts); every CTA passes the same
+// cluster barriers whatever happened, so no CTA of the cluster waits for one that left.
+namespace mb {
+namespace {
+
+constexpr int kTcF = 128;                       // features per CTA
+constexpr int kTcTok = 64;                      // token columns of the accumulator
+constexpr int kTcBK = 64;                       // K per ring stage
+constexpr int kTcWBytes = kTcF * kTcBK * 2;     // 16 KB
+constexpr int kTcXBytes = kTcTok * kTcBK * 2;   // 8 KB
+constexpr int kTcStage = kTcWBytes + kTcXBytes; // 24 KB
+constexpr int kTcMaxStages = 8;
+constexpr int kTcThreads = 128;
+constexpr int kTcRow = kTcF * 4;                // bytes of one token row of a partial tile
+constexpr int kTcMaxCluster = 8;
+
+struct TcPlan {
+  size_t off_bar, bytes;
+};
+// [ring: R stages of W | X, the partial tile [64][128] fp32 over it once drained][barriers]
+__host__ __device__ inline TcPlan make_tc_plan(int R) {
+  TcPlan p;
+  const size_t ring = (size_t)R * kTcStage;
+  const size_t ptile = (size_t)kTcTok * kTcRow;  // 32 KB
+  p.off_bar = ring > ptile ? ring : ptile;
+  p.bytes = p.off_bar + (2 * kTcMaxStages + 4) * 8 + 1024;  // barriers, TMEM address, 1 KB alignment slack
+  return p;
+}
+
+__device__ __forceinline__ void tc_prefetch_tmap(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                               const __grid_constant__ CUtensorMap tmX,
+                                                               T* __restrict__ Y, int64_t ldy, int M, int N,
+                                                               int kb_total, int kbc, int R) {
+  constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  extern __shared__ unsigned char tc_smem_raw[];
+  unsigned char* sm = tc_smem_raw + ((1024u - (smem_u32(tc_smem_raw) & 1023u)) & 1023u);
+  const int S = gridDim.y, s = blockIdx.y;
+  const TcPlan pl = make_tc_plan(R);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + pl.off_bar);
+  uint64_t* empty = full + kTcMaxStages;
+  uint64_t* mdone = empty + kTcMaxStages;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(mdone + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb0 = s * kbc;
+  const int nkb = min(kb_total, kb0 + kbc) - kb0;  // >= 1 (the host sizes the split)
+  const int f0 = blockIdx.x * kTcF;
+  const int ta = s * M / S, tb = (s + 1) * M / S;  // token rows this CTA sums and stores
+  const int nfirst = min(R, nkb);
+  auto load_w = [&](int st, int kb) { tma_load_2d(sm + st * kTcStage, &tmW, kb * kTcBK, f0, &full[st]); };
+
+  if (tid == 0) {
+    tc_prefetch_tmap(&tmW);
+    tc_prefetch_tmap(&tmX);
+    for (int i = 0; i < kTcMaxStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(mdone, 1);
+    mbar_init_fence();
+    // the weights do not depend on the previous kernel: request the whole first ring now
+    for (int i = 0; i < nfirst; ++i) {
+      mbar_arrive_expect_tx(&full[i], (uint32_t)kTcStage);
+      load_w(i, kb0 + i);
+    }
+  }
+  if (warp == 1) tmem_alloc(sTmem, kTcTok);
+  // X is the previous kernel's output; let the next kernel start its own weight fetch
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  if (tid == 0)
+    for (int i = 0; i < nfirst; ++i) tma_load_2d(sm + i * kTcStage + kTcWBytes, &tmX, (kb0 + i) * kTcBK, 0, &full[i]);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {  // refills past the first ring
+    for (int i = nfirst; i < nkb && ok; ++i) {
+      const int st = i % R;
+      if (!mbar_wait_bounded(&empty[st], (uint32_t)((i / R - 1) & 1), kWait)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&full[st], (uint32_t)kTcStage);
+      load_w(st, kb0 + i);
+      tma_load_2d(sm + st * kTcStage + kTcWBytes, &tmX, (kb0 + i) * kTcBK, 0, &full[st]);
+    }
+  } else if (warp == 1 && lane == 0) {  // the MMAs
+    const uint32_t idesc = umma_idesc_f16(ab_fmt, kTcF, kTcTok, 0, 0);
+    for (int i = 0; i < nkb; ++i) {
+      const int st = i % R;
+      if (!mbar_wait_bounded(&full[st], (uint32_t)((i / R) & 1), kWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a = smem_u32(sm + st * kTcStage), b = a + kTcWBytes;
+#pragma unroll
+      for (int k = 0; k < kTcBK / 16; ++k)
+        umma_f16_ss(tmem, umma_desc_sw128(a + k * 32, 16, 1024), umma_desc_sw128(b + k * 32, 16, 1024), idesc,
+                    (i > 0 || k > 0) ? 1u : 0u);
+      if (i + R < nkb) umma_commit(&empty[st]);
+    }
+    umma_commit(mdone);  // also on the failure path: every MMA issued above completes first
+  }
+  __syncwarp();
+  ok = mbar_wait_bounded(mdone, 0, kWait) && ok;
+  if (!ok) {  // count it; the copies still in flight get one more bounded wait before the ring is reused
+    if (lane == 0) atomicAdd(&g_sk_wait_timeouts, 1u);
+    if (tid == 0)
+      for (int i = 0; i < nfirst; ++i) mbar_wait_bounded(&full[i], (uint32_t)(((nkb - 1 - i) / R) & 1), kWait);
+  }
+  tc_fence_after();
+
+  // accumulator -> partial tile P [token][feature] fp32 over the drained ring
+  float* P = reinterpret_cast<float*>(sm);
+  {
+    const int fl = warp * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+    uint32_t acc[32];
+#pragma unroll
+    for (int h = 0; h < kTcTok / 32; ++h) {
+      tmem_ld32(taddr + (uint32_t)(h * 32), acc);
+      tmem_wait_ld(acc);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) P[(h * 32 + j) * kTcF + fl] = __uint_as_float(acc[j]);
+    }
+  }
+  auto store = [&](int t, int c, float4 a) {
+    if (f0 + c >= N) return;
+    uint2 o;
+    o.x = pack2<T>(a.x, a.y);
+    o.y = pack2<T>(a.z, a.w);
+    *reinterpret_cast<uint2*>(Y + (int64_t)t * ldy + f0 + c) = o;
+  };
+  constexpr int VR = kTcF / 4;  // float4 vectors per token row
+  if (S == 1) {
+    __syncthreads();
+    // every load of the thread in flight before its stores (a dependent load -> store chain
+    // per vector would cost one shared-memory round trip each)
+    constexpr int U = kTcTok * VR / kTcThreads;  // 16 vectors per thread at M = 64
+    float4 q[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = tid + u * kTcThreads;
+      if (v < M * VR) q[u] = *reinterpret_cast<const float4*>(&P[(v / VR) * kTcF + (v % VR) * 4]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = tid + u * kTcThreads;
+      if (v < M * VR) store(v / VR, (v % VR) * 4, q[u]);
+    }
+  } else {
+    // every CTA's partial is in its shared memory before any CTA reads it
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+    const uint32_t pbase = smem_u32(P);
+    const int nv = (tb - ta) * VR;
+    constexpr int U = 4;
+    for (int v0 = tid; v0 < nv; v0 += U * kTcThreads) {
+      float4 q[U][kTcMaxCluster];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * kTcThreads;
+        if (v < nv) {
+          const uint32_t addr = pbase + (uint32_t)(((ta + v / VR) * kTcF + (v % VR) * 4) * 4);
+#pragma unroll
+          for (int p = 0; p < kTcMaxCluster; ++p)
+            if (p < S) q[u][p] = ld_dsmem_f4(addr, (uint32_t)p);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * kTcThreads;
+        if (v < nv) {
+          float4 a = q[u][0];
+#pragma unroll
+          for (int p = 1; p < kTcMaxCluster; ++p)  // rank order: the sum does not depend on timing
+            if (p < S) {
+              a.x += q[u][p].x;
+              a.y += q[u][p].y;
+              a.z += q[u][p].z;
+              a.w += q[u][p].w;
+            }
+          store(ta + v / VR, (v % VR) * 4, a);
+        }
+      }
+    }
+    // no CTA leaves while another reads its partial (every value read above has been used)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcTok);
+  }
+}
+
+struct TcChoice {
+  int S, kbc, R;
+  size_t bytes;
+};
+
+}  // namespace
+}  // namespace mb
+
+namespace mb {
+namespace {
+// Clusters of S CTAs (kTcThreads threads, `bytes` of shared memory each) that can be resident at
+// once on the current device (cached per device and shape; 0 if the query fails).
+int tc_max_clusters(const void* kern, int S, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, S, bytes);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = (unsigned)S;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(1, (unsigned)S);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = bytes;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int64_t M,
+                     int64_t N, int64_t K, int split_k, int dtype, void* stream) {
+  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "skinny_gemm_tc: 16-bit operands only");
+  MB_REQUIRE(M >= 1 && M <= kTcTok, MB_ERR_UNSUPPORTED, "skinny_gemm_tc: M (%lld) must be in 1..64", (long long)M);
+  MB_REQUIRE(N > 0 && K > 0 && N < (1LL << 30) && K < (1LL << 24), MB_ERR_SHAPE, "skinny_gemm_tc: N %lld K %lld",
+             (long long)N, (long long)K);
+  MB_REQUIRE(K % kTcBK == 0, MB_ERR_UNSUPPORTED, "skinny_gemm_tc: K (%lld) must be a multiple of 64", (long long)K);
+  MB_REQUIRE(x && w && y, MB_ERR_ARG, "skinny_gemm_tc: null operand");
+  MB_REQUIRE(N % 4 == 0 && ldy % 4 == 0 && ldy >= N && (uintptr_t)y % 8 == 0, MB_ERR_UNSUPPORTED,
+             "skinny_gemm_tc: N and ldy must be multiples of 4 (Y 8-byte aligned)");
+  MB_REQUIRE(ldx % 8 == 0 && ldw % 8 == 0 && ldx >= K && ldw >= K && ((uintptr_t)x | (uintptr_t)w) % 16 == 0,
+             MB_ERR_ALIGN, "skinny_gemm_tc: X / W rows must be 16-byte aligned (row strides multiples of 8)");
+  MB_REQUIRE(split_k >= 0 && split_k <= kTcMaxCluster, MB_ERR_ARG, "skinny_gemm_tc: split_k must be 0 (automatic) .. %d",
+             kTcMaxCluster);
+  constexpr size_t kMaxSmem = 227 * 1024;
+  const int kbt = (int)(K / kTcBK);
+  const int tiles = (int)((N + kTcF - 1) / kTcF);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(MB_ERR_CUDA, "skinny_gemm_tc: no device");
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // The split.  One CTA streams its W run at roughly 40-55 GB/s (measured: bounded by the
+  // copies a CTA keeps in flight), so the weight has to be spread over every SM: the grid is
+  // sized to one CTA per SM (the shared-memory request is raised so that the block scheduler
+  // cannot stack two CTAs on one SM while others idle) unless it needs more CTAs than SMs, in
+  // which case two fit per SM.  Among the splits whose clusters all fit in one wave (asked of
+  // the occupancy calculator), the fewest parts that reach 90 % of the SMs, else the most
+  // CTAs; at most 8 parts (a portable cluster).  Ring depth: the CTA's whole run when it fits.
+  auto kern_bf16 = skinny_tc_kernel<__nv_bfloat16>;
+  auto kern_f16 = skinny_tc_kernel<__half>;
+  if (int e = ensure_smem_attr((const void*)kern_bf16, (int)kMaxSmem)) return e;
+  if (int e = ensure_smem_attr((const void*)kern_f16, (int)kMaxSmem)) return e;
+  constexpr size_t kOnePerSm = 114 * 1024;  // more than half an SM's shared memory
+  TcChoice ch = {0, 0, 0, 0};
+  long ch_ctas = 0;
+  for (int S = 1; S <= kTcMaxCluster; ++S) {
+    if (split_k && S != split_k) continue;
+    const int kbc = (kbt + S - 1) / S;
+    const int Se = (kbt + kbc - 1) / kbc;
+    if (Se != S) continue;  // the same split as a smaller S
+    const long ctas = (long)tiles * S;
+    int R = std::min(kbc, kTcMaxStages);
+    while (R > 1 && make_tc_plan(R).bytes > kMaxSmem) --R;
+    if (ctas > sms)
+      while (R > 2 && make_tc_plan(R).bytes > kMaxSmem / 2) --R;
+    size_t bytes = make_tc_plan(R).bytes;
+    if (bytes > kMaxSmem) continue;
+    if (ctas <= sms) bytes = std::max(bytes, kOnePerSm);
+    const int cap = tc_max_clusters((const void*)kern_bf16, S, bytes);
+    const bool one_wave = cap > 0 && (long)tiles <= cap;
+    if (split_k) {
+      ch = {S, kbc, R, bytes};
+      break;
+    }
+    if (!one_wave && ch.S != 0) continue;
+    if (ch.S == 0 || ctas > ch_ctas) {
+      ch = {S, kbc, R, bytes};
+      ch_ctas = ctas;
+    }
+    if (one_wave && ctas >= sms * 9 / 10) break;
+  }
+  MB_REQUIRE(ch.S != 0, MB_ERR_UNSUPPORTED, "skinny_gemm_tc: no split of K = %lld into %d parts", (long long)K,
+             split_k);
+  CUtensorMap tmW, tmX;
+  int rc = encode_tile_map_2d(&tmW, w, 2, (uint64_t)K, (uint64_t)N, (uint64_t)ldw * 2, kTcBK, kTcF, 128);
+  if (!rc) rc = encode_tile_map_2d(&tmX, x, 2, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, kTcBK, kTcTok, 128);
+  if (rc) return rc;
+  auto go = [&](auto t) -> int {
+    using T = decltype(t);
+    auto kern = skinny_tc_kernel<T>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = (unsigned)ch.S;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)ch.S);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = ch.bytes;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt, ch.kbc, ch.R);
+    return check_launch("skinny_gemm_tc");
+  };
+  return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+}
+
+}  // namespace
+}  // namespace mb
+
+extern "C" int motif_b200_skinny_gemm_tc(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                                         int64_t M, int64_t N, int64_t K, int split_k, int dtype, void* stream) {
+  return mb::skinny_tc_launch(x, ldx, w, ldw, y, ldy, M, N, K, split_k, dtype, stream);
 }

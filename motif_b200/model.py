@@ -538,14 +538,38 @@ class MotifChordModel(nn.Module):
 # 0.503 at 16, 0.548 vs 0.565 at 32, but 0.908 vs 0.747 at 64, where the legacy-MMA products
 # and the cluster's partial-tile exchange cost more than the latency the kernel hides.
 SKINNY_MAX_M = 32
+# Row counts SKINNY_MAX_M < M <= SKINNY_TC_MAX_M run on the tensor-core decode GEMM
+# (motif_b200_skinny_gemm_tc, the weight as it is) for the shapes where it measured faster than
+# the library GEMM at 64 rows (CUDA graphs of back-to-back products, weights streamed from HBM):
+# long K (the decoders' output and down projections, K >= 2048: e.g. N 768 x K 2816 5.8 vs
+# 6.3 us) and the lm_head (N >= 16384: 10.5 vs 10.9 us).  The wide K = 768 input projections
+# stay on the library GEMM (N 8728: 7.5 vs 5.1 us): one CTA streams its weight run at only
+# ~40-55 GB/s, so they would need more split-K parts than the exchange of the partials allows.
+SKINNY_TC_MAX_M = 64
+
+
+def _tc_skinny_ok(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]) -> bool:
+    M, K = a.shape
+    N = w.shape[0]
+    return (SKINNY_MAX_M < M <= SKINNY_TC_MAX_M and (K >= 2048 or N >= 16384)
+            and a.dtype in (torch.bfloat16, torch.float16) and w.dtype == a.dtype
+            and K % 64 == 0 and N % 4 == 0 and a.stride(1) == 1 and w.stride(1) == 1
+            and a.stride(0) % 8 == 0 and w.stride(0) % 8 == 0 and a.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0
+            and (out is None or (out.stride(1) == 1 and out.stride(0) % 4 == 0 and out.data_ptr() % 8 == 0)))
 
 
 def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, wp: torch.Tensor = None) -> torch.Tensor:
     """a [M, K] @ w[N, K]^T: decode-sized M (<= 64, 16-bit) on the weight-streaming skinny GEMM
-    when `wp` (w packed by `_skinny_packed`) is given, everything else on cuBLAS (plain library
-    GEMM; timed as 'cublas_gemm')."""
+    when `wp` (w packed by `_skinny_packed`) is given and M <= SKINNY_MAX_M, on the tensor-core
+    decode GEMM for the larger decode batches, everything else on cuBLAS (plain library GEMM;
+    timed as 'cublas_gemm')."""
     M, K = a.shape
     N = w.shape[0]
+    if _tc_skinny_ok(a, w, out):
+        y = out if out is not None else torch.empty((M, N), dtype=a.dtype, device=a.device)
+        _lib.call('motif_b200_skinny_gemm_tc', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(),
+                  y.stride(0), M, N, K, 0, _lib.dtype_code(a.dtype), _lib.stream_ptr(a.device))
+        return y
     if (wp is not None and M <= SKINNY_MAX_M and a.dtype == w.dtype and a.stride(1) == 1
             and a.stride(0) % 8 == 0 and a.data_ptr() % 16 == 0
             and (out is None or (out.stride(1) == 1 and out.stride(0) % 4 == 0 and out.data_ptr() % 8 == 0))):
