@@ -4,6 +4,8 @@
 // All are one warp per row: the row is streamed once from HBM into registers (fp32),
 // reduced with warp shuffles and written once.  Rows of up to 8 * 32 * MAXV elements stay
 // in registers; the generic path re-reads the row (it is L1-resident by then).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace mb {
@@ -177,7 +179,7 @@ __global__ void attn_res_kernel(SrcPtrs src, int n_src, const T* __restrict__ w,
 // Fused attn-res read + RMSNorm of the result for the model path (token-major rows, all
 // sources share one row stride).  NV 16-byte vectors of 8 elements per lane: D = 256 * NV.
 template <typename T, int NV>
-__global__ void attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, const T* __restrict__ w,
+__global__ void __launch_bounds__(32 * kWarpsPerBlock, 2) attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, const T* __restrict__ w,
                                          const T* __restrict__ q, T* __restrict__ h_out,
                                          T* __restrict__ hn_out, int64_t ors, int64_t rows,
                                          float eps_src, float eps_out) {
@@ -191,16 +193,29 @@ __global__ void attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, co
 #pragma unroll
     for (int e = 0; e < 8; ++e) h[v][e] = 0.f;
 
+  // The rows of up to kGroup sources are requested together before any is reduced, so a warp
+  // keeps kGroup rows (4 x 1.5 KB at D = 768) in flight instead of one or two.
+  constexpr int kGroup = 4;
   if (q == nullptr || n_src == 1) {
-    for (int s = 0; s < n_src; ++s) {
-      const T* xr = static_cast<const T*>(src.p[s]) + row * srs;
+    for (int s0 = 0; s0 < n_src; s0 += kGroup) {
+      uint4 raw[kGroup][NV];
 #pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        uint4 raw = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
-        const T* e8 = reinterpret_cast<const T*>(&raw);
+      for (int u = 0; u < kGroup; ++u)
+        if (s0 + u < n_src) {
+          const T* xr = static_cast<const T*>(src.p[s0 + u]) + row * srs;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) h[v][e] += to_f(e8[e]);
-      }
+          for (int v = 0; v < NV; ++v) raw[u][v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+        }
+#pragma unroll
+      for (int u = 0; u < kGroup; ++u)
+        if (s0 + u < n_src) {
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            const T* e8 = reinterpret_cast<const T*>(&raw[u][v]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[v][e] += to_f(e8[e]);
+          }
+        }
     }
   } else {
     float qw[NV][8];
@@ -213,49 +228,56 @@ __global__ void attn_res_norm_vec_kernel(SrcPtrs src, int n_src, int64_t srs, co
 #pragma unroll
       for (int e = 0; e < 8; ++e) qw[v][e] = to_f(q8[e]) * to_f(w8[e]);
     }
-    // Online softmax over the sources: h accumulates exp(l_s - m) x_s.  The next source's row
-    // is requested before this one is reduced, so two rows are in flight per warp.
+    // Online softmax over the sources: h accumulates exp(l_s - m) x_s, group by group.
     float m = -INFINITY, den = 0.f;
-    uint4 nxt[NV];
-    {
-      const T* xr = static_cast<const T*>(src.p[0]) + row * srs;
+    for (int s0 = 0; s0 < n_src; s0 += kGroup) {
+      uint4 raw[kGroup][NV];
 #pragma unroll
-      for (int v = 0; v < NV; ++v) nxt[v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
-    }
-    for (int s = 0; s < n_src; ++s) {
-      uint4 cur[NV];
+      for (int u = 0; u < kGroup; ++u)
+        if (s0 + u < n_src) {
+          const T* xr = static_cast<const T*>(src.p[s0 + u]) + row * srs;
 #pragma unroll
-      for (int v = 0; v < NV; ++v) cur[v] = nxt[v];
-      if (s + 1 < n_src) {
-        const T* xn = static_cast<const T*>(src.p[s + 1]) + row * srs;
+          for (int v = 0; v < NV; ++v) raw[u][v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+        }
+      float ss[kGroup], dot[kGroup];
 #pragma unroll
-        for (int v = 0; v < NV; ++v) nxt[v] = *reinterpret_cast<const uint4*>(xn + (v * 32 + lane) * 8);
-      }
-      float x[NV][8];
-      float ss = 0.f, dot = 0.f;
+      for (int u = 0; u < kGroup; ++u) {
+        ss[u] = 0.f;
+        dot[u] = 0.f;
+        if (s0 + u < n_src) {
 #pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        const uint4 raw = cur[v];
-        const T* e8 = reinterpret_cast<const T*>(&raw);
+          for (int v = 0; v < NV; ++v) {
+            const T* e8 = reinterpret_cast<const T*>(&raw[u][v]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          x[v][e] = to_f(e8[e]);
-          ss += x[v][e] * x[v][e];
-          dot += qw[v][e] * x[v][e];
+            for (int e = 0; e < 8; ++e) {
+              const float x = to_f(e8[e]);
+              ss[u] += x * x;
+              dot[u] += qw[v][e] * x;
+            }
+          }
         }
       }
-      ss = warp_sum(ss);
-      dot = warp_sum(dot);
-      const float l = dot * rsqrtf(ss / (float)D + eps_src);
-      const float mn = fmaxf(m, l);
-      const float sc = expf(m - mn);  // 0 on the first source (m = -inf)
-      const float p = expf(l - mn);
-      den = den * sc + p;
 #pragma unroll
-      for (int v = 0; v < NV; ++v)
+      for (int u = 0; u < kGroup; ++u) {
+        ss[u] = warp_sum(ss[u]);
+        dot[u] = warp_sum(dot[u]);
+      }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) h[v][e] = h[v][e] * sc + p * x[v][e];
-      m = mn;
+      for (int u = 0; u < kGroup; ++u)
+        if (s0 + u < n_src) {  // sources in order: the same sums as one source at a time
+          const float l = dot[u] * rsqrtf(ss[u] / (float)D + eps_src);
+          const float mn = fmaxf(m, l);
+          const float sc = expf(m - mn);  // 0 on the first source (m = -inf)
+          const float p = expf(l - mn);
+          den = den * sc + p;
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            const T* e8 = reinterpret_cast<const T*>(&raw[u][v]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[v][e] = h[v][e] * sc + p * to_f(e8[e]);
+          }
+          m = mn;
+        }
     }
     const float inv = 1.f / den;
 #pragma unroll
