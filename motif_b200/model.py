@@ -4,22 +4,28 @@ generation API (`motif/model/motif.py`, `motif/block/decoder.py`, `motif/block/m
 
 The parameters are stored exactly as the reference stores them, so `state_dict()` /
 `load_state_dict()` interoperate with the reference in both directions.  The forward does
-not walk the modules one by one; per decoder it runs
+not walk the modules one by one; per decoder a prefill runs
 
-    attn-res read + RMSNorm            motif_b200_attn_res_norm   (one pass over the sources)
-    one GEMM for every input projection  cuBLAS, norm weights folded into the packed weight
-    GDN:   conv + SiLU + L2 norms + beta/g   motif_b200_gdn_prep
-           delta rule + GatedRMSNorm          motif_b200_gdn_chunk_gated   (decode: gdn_decode)
-           SwiGLU                             motif_b200_swiglu
+    attn-res read + RMSNorm                motif_b200_attn_res_norm (one pass over the sources)
+    every input projection as ONE GEMM, norm weights folded into the packed weight, the MLP's
+    SwiGLU in its epilogue                 motif_b200_gemm_proj_swiglu (tcgen05)
+    GDN:   conv + SiLU + L2 norms + beta / g, UT transform, state scan, GatedRMSNorm
+                                           motif_b200_gdn_prefill_ws
            o_proj + down_proj as ONE GEMM over [o | act] (the parallel residual is a sum of
            two products, so it is one product over the concatenated K dimension)
-    Chord: q/k RMSNorm + cache append         motif_b200_chord_prep
-           biased flash attention             motif_b200_chord_attention  (decode: chord_decode)
-           o_proj, down_proj GEMMs, then f = attn * sigmoid(g) + mlp   motif_b200_gate_residual
+                                           motif_b200_gemm
+    Chord: q/k RMSNorm + cache append      motif_b200_chord_prep
+           biased flash attention          motif_b200_chord_attention (tcgen05)
+           down_proj, then o_proj with f = attn * sigmoid(g) + mlp in its epilogue
+                                           motif_b200_gemm, motif_b200_gemm_gate_residual
 
-and the block output / final norm with the same fused read (sum mode).  Packed weights
-are derived from the parameters on first use and rebuilt after `load_state_dict`, `.to()`
-or an explicit `invalidate_packed()` (call it after editing parameters in place).
+and a decode step the same reads with the decode kernels (motif_b200_gdn_decode_swiglu,
+motif_b200_chord_prep_swiglu, motif_b200_chord_decode, motif_b200_gate_residual) and the
+decode-sized products of `_mm` (weight-streaming GEMMs, the library GEMM for the K = 768 input
+projections at 33-64 rows); the block output / final norm use the same fused read (sum mode).
+Packed weights are derived from the parameters on first use and rebuilt after
+`load_state_dict`, `.to()` or an explicit `invalidate_packed()` (call it after editing
+parameters in place).
 """
 
 import builtins
