@@ -348,6 +348,17 @@ MB_API int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* packed
  * (gdn_attn.py:88-94, chord_attn.py:88-96, mlp.py:52-53, the decoders' o_proj / down_proj). */
 MB_API int motif_b200_skinny_gemm_tc(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
                                      int64_t M, int64_t N, int64_t K, int split_k, int dtype, void* stream);
+/* motif_b200_skinny_gemm_tc with the Chord decoder's parallel residual in the epilogue:
+ *   y = round(round(a * round(sigmoid(g))) + round(x . w^T))
+ * (the MLP's down projection plus the gated attention output; a [M, N] is the o_proj output,
+ * g [M, N] the gate projection, both 16-bit with rows 8-byte aligned and strides multiples of
+ * 4; y must not overlap them).  Bit-identical to motif_b200_skinny_gemm_tc followed by
+ * motif_b200_gate_residual.  Replaces chord_attn.py:254,313 (o_proj(out) * G) and the parallel
+ * residual of decoder.py:208 for decode-sized batches. */
+MB_API int motif_b200_skinny_gemm_tc_add_gated(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                               const void* a, int64_t lda, const void* g, int64_t ldg, void* y,
+                                               int64_t ldy, int64_t M, int64_t N, int64_t K, int split_k,
+                                               int dtype, void* stream);
 
 /* ------------------------------------------------------------------ backward (training)
  * Gradients of the three hot-path ops, fp32 arithmetic on CUDA cores (16-bit inputs widened on

@@ -464,6 +464,10 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* pa
 //   * a CTA takes one feature tile and a contiguous run of K blocks (split s = blockIdx.y of a
 //     cluster of S along y); every W block of its ring is requested before the kernel waits on
 //     its predecessor (programmatic dependent launch), X after the wait;
+//   * optional epilogue (the Chord decoder's parallel residual, chord_attn.py:254,313 and
+//     decoder.py:208): Y = round(round(A * round(sigmoid(G))) + round(X W^T)) with A the
+//     attention output after o_proj and G the gate, at the rounding points of the separate
+//     gate-residual kernel, so the fused result is bit-identical to the product followed by it;
 //   * the split-K partials (fp32, token-major [64][128]) stay in each CTA's shared memory;
 //     after one cluster barrier CTA r reads the token rows it owns from all S partials through
 //     distributed shared memory, every read of a thread in flight at once, and adds them in rank
@@ -505,7 +509,9 @@ template <typename T>
 __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_constant__ CUtensorMap tmW,
                                                                const __grid_constant__ CUtensorMap tmX,
                                                                T* __restrict__ Y, int64_t ldy, int M, int N,
-                                                               int kb_total, int kbc, int R) {
+                                                               int kb_total, int kbc, int R,
+                                                               const T* __restrict__ ga, int64_t lda,
+                                                               const T* __restrict__ gg, int64_t ldg) {
   constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   extern __shared__ unsigned char tc_smem_raw[];
   unsigned char* sm = tc_smem_raw + ((1024u - (smem_u32(tc_smem_raw) & 1023u)) & 1023u);
@@ -604,6 +610,20 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
   }
   auto store = [&](int t, int c, float4 a) {
     if (f0 + c >= N) return;
+    if (ga != nullptr) {  // y = round(round(A round(sigmoid(G))) + round(product))
+      const uint2 av = *reinterpret_cast<const uint2*>(ga + (int64_t)t * lda + f0 + c);
+      const uint2 gv = *reinterpret_cast<const uint2*>(gg + (int64_t)t * ldg + f0 + c);
+      const T* a4 = reinterpret_cast<const T*>(&av);
+      const T* g4 = reinterpret_cast<const T*>(&gv);
+      float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float gate = to_f(from_f<T>(sigmoidf_(to_f(g4[e]))));
+        const float att = to_f(from_f<T>(to_f(a4[e]) * gate));
+        v[e] = att + to_f(from_f<T>(v[e]));
+      }
+      a = make_float4(v[0], v[1], v[2], v[3]);
+    }
     uint2 o;
     o.x = pack2<T>(a.x, a.y);
     o.y = pack2<T>(a.z, a.w);
@@ -716,7 +736,8 @@ int tc_max_clusters(const void* kern, int S, size_t bytes) {
 }
 
 int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int64_t M,
-                     int64_t N, int64_t K, int split_k, int dtype, void* stream) {
+                     int64_t N, int64_t K, int split_k, int dtype, void* stream, const void* ga = nullptr,
+                     int64_t lda = 0, const void* gg = nullptr, int64_t ldg = 0) {
   MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "skinny_gemm_tc: 16-bit operands only");
   MB_REQUIRE(M >= 1 && M <= kTcTok, MB_ERR_UNSUPPORTED, "skinny_gemm_tc: M (%lld) must be in 1..64", (long long)M);
   MB_REQUIRE(N > 0 && K > 0 && N < (1LL << 30) && K < (1LL << 24), MB_ERR_SHAPE, "skinny_gemm_tc: N %lld K %lld",
@@ -798,7 +819,8 @@ int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, voi
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = at;
     cfg.numAttrs = 2;
-    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt, ch.kbc, ch.R);
+    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt, ch.kbc, ch.R, (const T*)ga, lda,
+                       (const T*)gg, ldg);
     return check_launch("skinny_gemm_tc");
   };
   return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
@@ -810,4 +832,14 @@ int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, voi
 extern "C" int motif_b200_skinny_gemm_tc(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
                                          int64_t M, int64_t N, int64_t K, int split_k, int dtype, void* stream) {
   return mb::skinny_tc_launch(x, ldx, w, ldw, y, ldy, M, N, K, split_k, dtype, stream);
+}
+
+extern "C" int motif_b200_skinny_gemm_tc_add_gated(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                                   const void* a, int64_t lda, const void* g, int64_t ldg, void* y,
+                                                   int64_t ldy, int64_t M, int64_t N, int64_t K, int split_k,
+                                                   int dtype, void* stream) {
+  MB_REQUIRE(a && g, MB_ERR_ARG, "skinny_gemm_tc_add_gated: null attention output or gate");
+  MB_REQUIRE(lda % 4 == 0 && ldg % 4 == 0 && lda >= N && ldg >= N && ((uintptr_t)a | (uintptr_t)g) % 8 == 0,
+             MB_ERR_ALIGN, "skinny_gemm_tc_add_gated: A / G rows must be 8-byte aligned (row strides multiples of 4)");
+  return mb::skinny_tc_launch(x, ldx, w, ldw, y, ldy, M, N, K, split_k, dtype, stream, a, lda, g, ldg);
 }

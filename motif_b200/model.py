@@ -595,6 +595,26 @@ def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, wp: torch.Te
     return r
 
 
+def _down_add_gated(act: torch.Tensor, w_down: torch.Tensor, a: torch.Tensor,
+                    gate: torch.Tensor) -> Optional[torch.Tensor]:
+    """The Chord decoder's `down_proj(act) + o_proj(out) * sigmoid(g)` for decode-sized batches
+    (`chord_attn.py:254,313`, `decoder.py:208`) as ONE launch: the tensor-core decode GEMM with
+    the gated residual in its epilogue (`motif_b200_skinny_gemm_tc_add_gated`), given the o_proj
+    output `a`; None when that kernel does not take the shapes."""
+    M, K = act.shape
+    N = w_down.shape[0]
+    if not (_tc_skinny_ok(act, w_down, None) and a.shape == (M, N) and gate.shape == (M, N)
+            and a.dtype == gate.dtype == act.dtype and a.stride(1) == 1 and gate.stride(1) == 1
+            and a.stride(0) % 4 == 0 and gate.stride(0) % 4 == 0 and a.data_ptr() % 8 == 0
+            and gate.data_ptr() % 8 == 0):
+        return None
+    y = torch.empty((M, N), dtype=act.dtype, device=act.device)
+    _lib.call('motif_b200_skinny_gemm_tc_add_gated', act.data_ptr(), act.stride(0), w_down.data_ptr(),
+              w_down.stride(0), a.data_ptr(), a.stride(0), gate.data_ptr(), gate.stride(0), y.data_ptr(),
+              y.stride(0), M, N, K, 0, _lib.dtype_code(act.dtype), _lib.stream_ptr(act.device))
+    return y
+
+
 def _tc_ok(*ts: torch.Tensor) -> bool:
     """The tcgen05 projection kernels take 16-bit operands with 16-byte aligned rows and K a
     multiple of 64; fp32 (the parity mode) stays on the library GEMM."""
@@ -873,15 +893,22 @@ def _chord_decoder(model, pk: _ChordPack, hn, B, T, cache: Optional[KVLayerCache
     if not act_done:
         _lib.call('motif_b200_swiglu', proj.data_ptr() + pk.off_gu * proj.element_size(), _lib.ptr(act), M, hid,
                   N_in, hid, dc, st)
-    f = _gemm(act, pk.w_down, wp=pk.w_down_sk)
     gate = proj[:, pk.off_g:pk.off_g + d]
+    a = None
+    if not fused_proj:  # decode-sized: o_proj first, then down_proj with the gated residual fused
+        a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
+        f = _down_add_gated(act, pk.w_down, a, gate)
+        if f is not None:
+            return f
+    f = _gemm(act, pk.w_down, wp=pk.w_down_sk)
     if fused_proj and _tc_ok(attn, pk.w_o, gate, f):
         # o_proj with the gate and the parallel residual in its epilogue: f = attn_o * sigmoid(g) + f
         _lib.call('motif_b200_gemm_gate_residual', _lib.ptr(attn), attn.stride(0), _lib.ptr(pk.w_o),
                   pk.w_o.stride(0), _lib.ptr(gate), gate.stride(0), _lib.ptr(f), f.stride(0), _lib.ptr(f),
                   f.stride(0), M, d, d, dc, st)
         return f
-    a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
+    if a is None:
+        a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
     _lib.call('motif_b200_gate_residual', _lib.ptr(a), d, proj.data_ptr() + pk.off_g * proj.element_size(), N_in,
               _lib.ptr(f), d, _lib.ptr(f), d, M, d, dc, st)
     return f

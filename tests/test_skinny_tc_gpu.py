@@ -153,3 +153,39 @@ def test_skinny_tc_rejects_bad_arguments():
     with pytest.raises(ValueError, match='aligned'):
         call(8, 64, 128, ldx=130)
 
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize('M,K,split_k', [(64, 2048, 0), (40, 2048, 3), (64, 768, 0), (33, 2816, 8)])
+def test_skinny_tc_add_gated_equals_product_then_gate_residual(dtype, M, K, split_k):
+    """The Chord decoder's down_proj with the gated residual in the epilogue gives the same bits
+    as the product followed by the separate gate-residual kernel, with the gate a column slice
+    of a wider projection row (as in the model), on two calls in a row."""
+    N, N_in, off_g = 768, 6016, 1152
+    g = torch.Generator().manual_seed(M * 7 + K)
+    x = torch.randn(M, K, generator=g).to(dtype).cuda()
+    w = (K ** -0.5 * torch.randn(N, K, generator=g)).to(dtype).cuda()
+    a = torch.randn(M, N, generator=g).to(dtype).cuda()
+    proj = (2 * torch.randn(M, N_in, generator=g)).to(dtype).cuda()
+    gate = proj[:, off_g:off_g + N]
+    ref = tc(x, w, split_k=split_k)
+    _lib.call('motif_b200_gate_residual', a.data_ptr(), N, gate.data_ptr(), N_in, ref.data_ptr(), N, ref.data_ptr(), N,
+              M, N, _lib.dtype_code(dtype), st())
+    for _ in range(2):
+        y = torch.full((M, N), float('nan'), dtype=dtype, device='cuda')
+        _lib.call('motif_b200_skinny_gemm_tc_add_gated', x.data_ptr(), K, w.data_ptr(), K, a.data_ptr(), N,
+                  gate.data_ptr(), N_in, y.data_ptr(), N, M, N, K, split_k, _lib.dtype_code(dtype), st())
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+    assert _lib.wait_timeouts() == 0
+
+
+def test_skinny_tc_add_gated_rejects_misaligned_gate():
+    x = torch.zeros(64, 2048, dtype=torch.bfloat16, device='cuda')
+    w = torch.zeros(768, 2048, dtype=torch.bfloat16, device='cuda')
+    a = torch.zeros(64, 768, dtype=torch.bfloat16, device='cuda')
+    proj = torch.zeros(64, 6016, dtype=torch.bfloat16, device='cuda')
+    y = torch.zeros(64, 768, dtype=torch.bfloat16, device='cuda')
+    with pytest.raises(ValueError, match='aligned'):  # the gate starts 2 bytes past an 8-byte boundary
+        _lib.call('motif_b200_skinny_gemm_tc_add_gated', x.data_ptr(), 2048, w.data_ptr(), 2048, a.data_ptr(), 768,
+                  proj.data_ptr() + 2, 6016, y.data_ptr(), 768, 64, 768, 2048, 0, _lib.MB_BF16, st())
