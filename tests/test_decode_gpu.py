@@ -122,16 +122,19 @@ def test_tiny_config_graph_greedy64_matches_reference():
     assert torch.equal(gen, d['greedy']), (gen != d['greedy']).nonzero()
 
 
-def test_random_filled_cache_decode_172m_matches_eager():
+@pytest.mark.parametrize('B', [4, 48])
+def test_random_filled_cache_decode_172m_matches_eager(B):
     """The benchmark's decode set-up (172M shapes, bf16, caches filled with seeded random
     contents at length 1000): the CUDA-graph steps equal the eager T = 1 forward fed the same
     tokens on a copy of the same caches (same kernels, split count pinned), token for token
-    and logit for logit; cache lengths advance by one per step."""
+    and logit for logit; cache lengths advance by one per step.  4 requests take the
+    weight-streaming legacy-MMA products, 48 the tensor-core decode GEMM and its fused gated
+    residual."""
     import copy
     from motif_b200.config import config_172m
     from motif_b200.decode import GraphDecoder, fill_cache_random
     m = build(config_172m(), dtype=torch.bfloat16)
-    B, L, steps = 4, 1000, 8
+    L, steps = 1000, 8
     cache = fill_cache_random(m, m.create_cache(), B, L, L + steps)
     m.decode_splits = 6
     twin = copy.deepcopy(cache)
