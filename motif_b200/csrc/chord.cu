@@ -1355,19 +1355,27 @@ __global__ void __launch_bounds__(128) chord_merge_kernel(const float* __restric
   const int t = (int)(bt % Tn), b = (int)(bt / Tn);
   const int64_t split_stride = (int64_t)B * H * Tn * (D + 2);
   const float* base = ws + (((int64_t)b * H + h) * Tn + t) * (D + 2);
-  if (nsplit <= 32) {
-    // Lane sp holds split sp's (m, l) and weight; the partial rows are then read eight splits
-    // at a time with all loads in flight, and summed in split order (the same arithmetic as
-    // the general loop below).
-    float ms = -INFINITY, ls = 0.f;
+  if (nsplit <= 64) {
+    // Lane sp holds splits sp and sp + 32's (m, l) and weights; the partial rows are then read
+    // eight splits at a time with all loads in flight, and summed in split order (the same
+    // arithmetic as the general loop below, whose lanes also take splits sp, sp + 32).
+    float ms0 = -INFINITY, ls0 = 0.f, ms1 = -INFINITY, ls1 = 0.f;
     if (lane < nsplit) {
-      ms = base[lane * split_stride + D];
-      ls = base[lane * split_stride + D + 1];
+      ms0 = base[lane * split_stride + D];
+      ls0 = base[lane * split_stride + D + 1];
     }
-    const float mx = warp_max(ms);
+    if (lane + 32 < nsplit) {
+      ms1 = base[(lane + 32) * split_stride + D];
+      ls1 = base[(lane + 32) * split_stride + D + 1];
+    }
+    const float mx = warp_max(fmaxf(ms0, ms1));
     const float mb = mx == -INFINITY ? 0.f : mx;
-    const float w = lane < nsplit ? exp2f(ms - mb) : 0.f;
-    const float den = warp_sum(ls * w);
+    const float w0 = lane < nsplit ? exp2f(ms0 - mb) : 0.f;
+    const float w1 = lane + 32 < nsplit ? exp2f(ms1 - mb) : 0.f;
+    float dpart = 0.f;
+    if (lane < nsplit) dpart += ls0 * w0;
+    if (lane + 32 < nsplit) dpart += ls1 * w1;
+    const float den = warp_sum(dpart);
     float acc[OD];
 #pragma unroll
     for (int d = 0; d < OD; ++d) acc[d] = 0.f;
@@ -1379,7 +1387,7 @@ __global__ void __launch_bounds__(128) chord_merge_kernel(const float* __restric
         for (int d = 0; d < OD; ++d) v[u][d] = sp0 + u < nsplit ? base[(sp0 + u) * split_stride + lane * OD + d] : 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float wu = __shfl_sync(0xffffffffu, w, (sp0 + u) & 31);
+        const float wu = __shfl_sync(0xffffffffu, sp0 + u < 32 ? w0 : w1, (sp0 + u) & 31);
         if (sp0 + u < nsplit)
 #pragma unroll
           for (int d = 0; d < OD; ++d) acc[d] = fmaf(wu, v[u][d], acc[d]);

@@ -235,7 +235,7 @@ def test_chord_prep(dtype, B, T, H, Hkv, D, pos):
 @pytest.mark.parametrize('B,H,Hkv,T,S,D,splits', [(2, 12, 3, 1, 1000, 64, 7), (3, 4, 2, 2, 33, 32, 4),
                                                   (1, 8, 8, 1, 5000, 64, 64), (2, 4, 1, 4, 300, 32, 1),
                                                   (2, 8, 2, 2, 8448, 64, 12), (1, 12, 3, 1, 64, 64, 3),
-                                                  (1, 16, 2, 2, 777, 64, 5)])
+                                                  (1, 16, 2, 2, 777, 64, 5), (2, 12, 3, 1, 8448, 64, 33)])
 @pytest.mark.parametrize('scalar', [False, True])
 def test_chord_decode(dtype, B, H, Hkv, T, S, D, splits, scalar, request):
     # 16-bit D = 64 runs the tensor-core kernel unless the FORCE_DECODE_SCALAR testing knob is on
