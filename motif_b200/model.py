@@ -554,10 +554,15 @@ SKINNY_MAX_M = 32
 SKINNY_TC_MAX_M = 64
 
 
-def _tc_skinny_ok(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]) -> bool:
+def _tc_skinny_ok(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor], fused: bool = False) -> bool:
+    """The tensor-core decode GEMM takes the product: above SKINNY_MAX_M rows for the long-K
+    products and the lm_head; at SKINNY_MAX_M rows or fewer only the lm_head (at 8 rows 10.6 us
+    against 12.2 on the legacy-MMA kernel) and, with `fused`, the Chord down projection that
+    carries the gated residual in its epilogue (one launch instead of two)."""
     M, K = a.shape
     N = w.shape[0]
-    return (SKINNY_MAX_M < M <= SKINNY_TC_MAX_M and (K >= 2048 or N >= 16384)
+    small_ok = fused or N >= 16384
+    return (0 < M <= SKINNY_TC_MAX_M and (M > SKINNY_MAX_M or small_ok) and (K >= 2048 or N >= 16384)
             and a.dtype in (torch.bfloat16, torch.float16) and w.dtype == a.dtype
             and K % 64 == 0 and N % 4 == 0 and a.stride(1) == 1 and w.stride(1) == 1
             and a.stride(0) % 8 == 0 and w.stride(0) % 8 == 0 and a.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0
@@ -603,7 +608,7 @@ def _down_add_gated(act: torch.Tensor, w_down: torch.Tensor, a: torch.Tensor,
     output `a`; None when that kernel does not take the shapes."""
     M, K = act.shape
     N = w_down.shape[0]
-    if not (_tc_skinny_ok(act, w_down, None) and a.shape == (M, N) and gate.shape == (M, N)
+    if not (_tc_skinny_ok(act, w_down, None, fused=True) and a.shape == (M, N) and gate.shape == (M, N)
             and a.dtype == gate.dtype == act.dtype and a.stride(1) == 1 and gate.stride(1) == 1
             and a.stride(0) % 4 == 0 and gate.stride(0) % 4 == 0 and a.data_ptr() % 8 == 0
             and gate.data_ptr() % 8 == 0):
