@@ -380,11 +380,13 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* pa
   }
   const long reg_ctas = std::max(1, 65536 / (kThreads * ((regs + 7) / 8 * 8)));
 
-  // The split with the least estimated time.  Per CTA: its W bytes at an SM's share of HBM
-  // bandwidth (~44 KB/us), its X bytes from L2 (~110 KB/us), and its partial tile read by the
-  // cluster (~10 KB/us through distributed shared memory); the CTAs sharing an SM add up; each
-  // wave pays ~2 us of latency.  The constants are measured orders of magnitude on B200; the
-  // model only has to rank the candidates.
+  // The split with the least estimated time.  Each wave pays ~1.5 us of latency; a CTA streams
+  // its W bytes at ~70 KB/us and its X bytes from L2 at ~110 KB/us, and the CTAs sharing an SM
+  // add up; a split across a cluster costs ~0.8 us plus ~0.1 us per part for the barrier and the
+  // exchange, plus its partial bytes at ~10 KB/us; and no split moves the weight faster than HBM
+  // (~6.5 GB/ms).  Fitted to forced-split sweeps of the 172M model's decode products on B200 at
+  // 8-32 rows (the exchange's fixed cost is what makes a split-free CTA of four K-splitting
+  // warps the fastest choice for the K = 768 products: 2.9 instead of 5.0 us for N 6016).
   Split best = {0, 0, 0};
   double best_us = 0.0;
   size_t best_smem = 0;
@@ -406,7 +408,9 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* pa
       const long share = (std::min(ctas, slots) + sms - 1) / sms;
       const double w_kb = (double)F * kc * 32 / 1024.0, x_kb = (double)M * kc * 32 / 1024.0;
       const double e_kb = sp.S > 1 ? (double)M * F * 4 * (sp.S - 1) / sp.S / 1024.0 : 0.0;
-      const double us = (double)waves * (2.0 + (double)share * (w_kb / 44.0 + x_kb / 110.0 + e_kb / 10.0));
+      double us = (double)waves * (1.5 + (double)share * (w_kb / 70.0 + x_kb / 110.0)) +
+                  (sp.S > 1 ? 0.8 + 0.1 * sp.S + e_kb / 10.0 : 0.0);
+      us = std::max(us, (double)N * K * 2 / 1024.0 / 6500.0);
       if (best.wk == 0 || us < best_us) {
         best = sp;
         best_us = us;
