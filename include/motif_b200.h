@@ -359,6 +359,18 @@ MB_API int motif_b200_skinny_gemm_tc_add_gated(const void* x, int64_t ldx, const
                                                const void* a, int64_t lda, const void* g, int64_t ldg, void* y,
                                                int64_t ldy, int64_t M, int64_t N, int64_t K, int split_k,
                                                int dtype, void* stream);
+/* The Chord decoder's whole tail in one launch on the tensor-core decode GEMM:
+ *   y = round(round(round(x1 . w1^T) * round(sigmoid(g))) + round(x2 . w2^T))
+ * with x1 [M, K1] the attention output and w1 [N, K1] o_proj, x2 [M, K2] the MLP activation
+ * and w2 [N, K2] down_proj, g [M, N] the gate (rows 8-byte aligned, stride a multiple of 4).
+ * The cluster's ranks split the K of both products; each product's partials are summed apart
+ * in rank order (deterministic).  Same operand rules as motif_b200_skinny_gemm_tc; y must not
+ * overlap the inputs.  Replaces chord_attn.py:254,313 (o_proj(out) * G) with the MLP's down
+ * projection (mlp.py:63) and the parallel residual (decoder.py:208) for decode-sized batches. */
+MB_API int motif_b200_skinny_gemm_tc_chord_tail(const void* x1, int64_t ldx1, const void* w1, int64_t ldw1,
+                                                int64_t K1, const void* x2, int64_t ldx2, const void* w2,
+                                                int64_t ldw2, int64_t K2, const void* g, int64_t ldg, void* y,
+                                                int64_t ldy, int64_t M, int64_t N, int dtype, void* stream);
 
 /* ------------------------------------------------------------------ backward (training)
  * Gradients of the three hot-path ops, fp32 arithmetic on CUDA cores (16-bit inputs widened on

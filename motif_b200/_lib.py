@@ -86,6 +86,8 @@ SIGNATURES = {
     'motif_b200_skinny_pack': (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
     'motif_b200_skinny_gemm': (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P]),
     'motif_b200_skinny_gemm_tc': (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I, _P]),
+    'motif_b200_skinny_gemm_tc_chord_tail': (_I, [_P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _P,
+                                                   _I64, _I64, _I64, _I, _P]),
     'motif_b200_skinny_gemm_tc_add_gated': (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64,
                                                   _I, _I, _P]),
     'motif_b200_gdn_prefill_ws': (_I, [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64,

@@ -472,6 +472,11 @@ extern "C" int motif_b200_skinny_gemm(const void* x, int64_t ldx, const void* pa
 //     decoder.py:208): Y = round(round(A * round(sigmoid(G))) + round(X W^T)) with A the
 //     attention output after o_proj and G the gate, at the rounding points of the separate
 //     gate-residual kernel, so the fused result is bit-identical to the product followed by it;
+//   * two products in one launch (the Chord decoder's tail, motif_b200_skinny_gemm_tc_chord_tail):
+//     the cluster's first S1 ranks split the K of product 1 (the o_proj of the attention
+//     output), the others the K of product 2 (the MLP's down_proj); each CTA still has one
+//     accumulator, the exchange sums the two groups of partials apart, and the epilogue applies
+//     Y = round(round(round(P1) * round(sigmoid(G))) + round(P2));
 //   * the split-K partials (fp32, token-major [64][128]) stay in each CTA's shared memory;
 //     after one cluster barrier CTA r reads the token rows it owns from all S partials through
 //     distributed shared memory, every read of a thread in flight at once, and adds them in rank
@@ -515,7 +520,10 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
                                                                T* __restrict__ Y, int64_t ldy, int M, int N,
                                                                int kb_total, int kbc, int R,
                                                                const T* __restrict__ ga, int64_t lda,
-                                                               const T* __restrict__ gg, int64_t ldg) {
+                                                               const T* __restrict__ gg, int64_t ldg,
+                                                               const __grid_constant__ CUtensorMap tmW2,
+                                                               const __grid_constant__ CUtensorMap tmX2,
+                                                               int kb_total2, int S1) {
   constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   extern __shared__ unsigned char tc_smem_raw[];
   unsigned char* sm = tc_smem_raw + ((1024u - (smem_u32(tc_smem_raw) & 1023u)) & 1023u);
@@ -526,16 +534,20 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
   uint64_t* mdone = empty + kTcMaxStages;
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(mdone + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kb0 = s * kbc;
-  const int nkb = min(kb_total, kb0 + kbc) - kb0;  // >= 1 (the host sizes the split)
+  // ranks [0, S1) run product 1 (tmW, tmX), ranks [S1, S) product 2 (tmW2, tmX2)
+  const bool second = s >= S1;
+  const CUtensorMap* mW = second ? &tmW2 : &tmW;
+  const CUtensorMap* mX = second ? &tmX2 : &tmX;
+  const int kb0 = (second ? s - S1 : s) * kbc;
+  const int nkb = min(second ? kb_total2 : kb_total, kb0 + kbc) - kb0;  // >= 1 (the host sizes the split)
   const int f0 = blockIdx.x * kTcF;
   const int ta = s * M / S, tb = (s + 1) * M / S;  // token rows this CTA sums and stores
   const int nfirst = min(R, nkb);
-  auto load_w = [&](int st, int kb) { tma_load_2d(sm + st * kTcStage, &tmW, kb * kTcBK, f0, &full[st]); };
+  auto load_w = [&](int st, int kb) { tma_load_2d(sm + st * kTcStage, mW, kb * kTcBK, f0, &full[st]); };
 
   if (tid == 0) {
-    tc_prefetch_tmap(&tmW);
-    tc_prefetch_tmap(&tmX);
+    tc_prefetch_tmap(mW);
+    tc_prefetch_tmap(mX);
     for (int i = 0; i < kTcMaxStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -553,7 +565,7 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   if (tid == 0)
-    for (int i = 0; i < nfirst; ++i) tma_load_2d(sm + i * kTcStage + kTcWBytes, &tmX, (kb0 + i) * kTcBK, 0, &full[i]);
+    for (int i = 0; i < nfirst; ++i) tma_load_2d(sm + i * kTcStage + kTcWBytes, mX, (kb0 + i) * kTcBK, 0, &full[i]);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -569,7 +581,7 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
       }
       mbar_arrive_expect_tx(&full[st], (uint32_t)kTcStage);
       load_w(st, kb0 + i);
-      tma_load_2d(sm + st * kTcStage + kTcWBytes, &tmX, (kb0 + i) * kTcBK, 0, &full[st]);
+      tma_load_2d(sm + st * kTcStage + kTcWBytes, mX, (kb0 + i) * kTcBK, 0, &full[st]);
     }
   } else if (warp == 1 && lane == 0) {  // the MMAs
     const uint32_t idesc = umma_idesc_f16(ab_fmt, kTcF, kTcTok, 0, 0);
@@ -612,9 +624,22 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
       for (int j = 0; j < 32; ++j) P[(h * 32 + j) * kTcF + fl] = __uint_as_float(acc[j]);
     }
   }
-  auto store = [&](int t, int c, float4 a) {
+  const bool dual = S1 < S;
+  auto store = [&](int t, int c, float4 a, float4 d) {
     if (f0 + c >= N) return;
-    if (ga != nullptr) {  // y = round(round(A round(sigmoid(G))) + round(product))
+    if (dual) {  // y = round(round(round(product 1) round(sigmoid(G))) + round(product 2))
+      const uint2 gv = *reinterpret_cast<const uint2*>(gg + (int64_t)t * ldg + f0 + c);
+      const T* g4 = reinterpret_cast<const T*>(&gv);
+      const float v1[4] = {a.x, a.y, a.z, a.w}, v2[4] = {d.x, d.y, d.z, d.w};
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float gate = to_f(from_f<T>(sigmoidf_(to_f(g4[e]))));
+        const float att = to_f(from_f<T>(to_f(from_f<T>(v1[e])) * gate));
+        v[e] = att + to_f(from_f<T>(v2[e]));
+      }
+      a = make_float4(v[0], v[1], v[2], v[3]);
+    } else if (ga != nullptr) {  // y = round(round(A round(sigmoid(G))) + round(product))
       const uint2 av = *reinterpret_cast<const uint2*>(ga + (int64_t)t * lda + f0 + c);
       const uint2 gv = *reinterpret_cast<const uint2*>(gg + (int64_t)t * ldg + f0 + c);
       const T* a4 = reinterpret_cast<const T*>(&av);
@@ -648,7 +673,7 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int v = tid + u * kTcThreads;
-      if (v < M * VR) store(v / VR, (v % VR) * 4, q[u]);
+      if (v < M * VR) store(v / VR, (v % VR) * 4, q[u], q[u]);
     }
   } else {
     // every CTA's partial is in its shared memory before any CTA reads it
@@ -673,16 +698,29 @@ __global__ void __launch_bounds__(kTcThreads) skinny_tc_kernel(const __grid_cons
       for (int u = 0; u < U; ++u) {
         const int v = v0 + u * kTcThreads;
         if (v < nv) {
-          float4 a = q[u][0];
+          // rank order within each product: the sums do not depend on timing
+          float4 a = q[u][0], d = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int p = 1; p < kTcMaxCluster; ++p)  // rank order: the sum does not depend on timing
-            if (p < S) {
+          for (int p = 1; p < kTcMaxCluster; ++p)
+            if (p < S1) {
               a.x += q[u][p].x;
               a.y += q[u][p].y;
               a.z += q[u][p].z;
               a.w += q[u][p].w;
             }
-          store(ta + v / VR, (v % VR) * 4, a);
+#pragma unroll
+          for (int p = 1; p < kTcMaxCluster; ++p)
+            if (p >= S1 && p < S) {
+              if (p == S1) {
+                d = q[u][p];
+              } else {
+                d.x += q[u][p].x;
+                d.y += q[u][p].y;
+                d.z += q[u][p].z;
+                d.w += q[u][p].w;
+              }
+            }
+          store(ta + v / VR, (v % VR) * 4, a, d);
         }
       }
     }
@@ -824,7 +862,7 @@ int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, voi
     cfg.attrs = at;
     cfg.numAttrs = 2;
     cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt, ch.kbc, ch.R, (const T*)ga, lda,
-                       (const T*)gg, ldg);
+                       (const T*)gg, ldg, tmW, tmX, 0, ch.S);
     return check_launch("skinny_gemm_tc");
   };
   return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
@@ -846,4 +884,86 @@ extern "C" int motif_b200_skinny_gemm_tc_add_gated(const void* x, int64_t ldx, c
   MB_REQUIRE(lda % 4 == 0 && ldg % 4 == 0 && lda >= N && ldg >= N && ((uintptr_t)a | (uintptr_t)g) % 8 == 0,
              MB_ERR_ALIGN, "skinny_gemm_tc_add_gated: A / G rows must be 8-byte aligned (row strides multiples of 4)");
   return mb::skinny_tc_launch(x, ldx, w, ldw, y, ldy, M, N, K, split_k, dtype, stream, a, lda, g, ldg);
+}
+
+extern "C" int motif_b200_skinny_gemm_tc_chord_tail(const void* x1, int64_t ldx1, const void* w1, int64_t ldw1,
+                                                    int64_t K1, const void* x2, int64_t ldx2, const void* w2,
+                                                    int64_t ldw2, int64_t K2, const void* g, int64_t ldg, void* y,
+                                                    int64_t ldy, int64_t M, int64_t N, int dtype, void* stream) {
+  using namespace mb;
+  MB_REQUIRE(dtype == MB_BF16 || dtype == MB_F16, MB_ERR_UNSUPPORTED, "skinny_gemm_tc_chord_tail: 16-bit operands only");
+  MB_REQUIRE(M >= 1 && M <= kTcTok, MB_ERR_UNSUPPORTED, "skinny_gemm_tc_chord_tail: M (%lld) must be in 1..64",
+             (long long)M);
+  MB_REQUIRE(N > 0 && N < (1LL << 30) && K1 > 0 && K2 > 0 && K1 < (1LL << 24) && K2 < (1LL << 24), MB_ERR_SHAPE,
+             "skinny_gemm_tc_chord_tail: N %lld K1 %lld K2 %lld", (long long)N, (long long)K1, (long long)K2);
+  MB_REQUIRE(K1 % kTcBK == 0 && K2 % kTcBK == 0, MB_ERR_UNSUPPORTED,
+             "skinny_gemm_tc_chord_tail: K1 and K2 must be multiples of 64");
+  MB_REQUIRE(x1 && w1 && x2 && w2 && g && y, MB_ERR_ARG, "skinny_gemm_tc_chord_tail: null operand");
+  MB_REQUIRE(N % 4 == 0 && ldy % 4 == 0 && ldy >= N && (uintptr_t)y % 8 == 0, MB_ERR_UNSUPPORTED,
+             "skinny_gemm_tc_chord_tail: N and ldy must be multiples of 4 (Y 8-byte aligned)");
+  MB_REQUIRE(ldx1 % 8 == 0 && ldw1 % 8 == 0 && ldx2 % 8 == 0 && ldw2 % 8 == 0 && ldx1 >= K1 && ldw1 >= K1 &&
+                 ldx2 >= K2 && ldw2 >= K2 && ((uintptr_t)x1 | (uintptr_t)w1 | (uintptr_t)x2 | (uintptr_t)w2) % 16 == 0,
+             MB_ERR_ALIGN, "skinny_gemm_tc_chord_tail: X / W rows must be 16-byte aligned (row strides multiples of 8)");
+  MB_REQUIRE(ldg % 4 == 0 && ldg >= N && (uintptr_t)g % 8 == 0, MB_ERR_ALIGN,
+             "skinny_gemm_tc_chord_tail: G rows must be 8-byte aligned (row stride a multiple of 4)");
+  constexpr size_t kMaxSmem = 227 * 1024;
+  constexpr size_t kOnePerSm = 114 * 1024;
+  const int kbt1 = (int)(K1 / kTcBK), kbt2 = (int)(K2 / kTcBK);
+  const int tiles = (int)((N + kTcF - 1) / kTcF);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(MB_ERR_CUDA, "skinny_gemm_tc_chord_tail: no device");
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  auto kern_bf16 = skinny_tc_kernel<__nv_bfloat16>;
+  auto kern_f16 = skinny_tc_kernel<__half>;
+  if (int e = ensure_smem_attr((const void*)kern_bf16, (int)kMaxSmem)) return e;
+  if (int e = ensure_smem_attr((const void*)kern_f16, (int)kMaxSmem)) return e;
+  // K blocks per CTA, the same for both products: the smallest (the most CTAs) whose
+  // S1 + S2 <= 8 parts fit a cluster and whose clusters fit in one wave
+  TcChoice ch = {0, 0, 0, 0};
+  int S1 = 0;
+  for (int kbc = 1; kbc <= std::max(kbt1, kbt2); ++kbc) {
+    const int s1 = (kbt1 + kbc - 1) / kbc, s2 = (kbt2 + kbc - 1) / kbc;
+    const int S = s1 + s2;
+    if (S > kTcMaxCluster) continue;
+    int R = std::min(kbc, kTcMaxStages);
+    while (R > 1 && make_tc_plan(R).bytes > kMaxSmem) --R;
+    size_t bytes = make_tc_plan(R).bytes;
+    if (bytes > kMaxSmem) continue;
+    if ((long)tiles * S <= sms) bytes = std::max(bytes, kOnePerSm);
+    const int cap = tc_max_clusters((const void*)kern_bf16, S, bytes);
+    if (cap <= 0 || tiles > cap) continue;
+    ch = {S, kbc, R, bytes};
+    S1 = s1;
+    break;
+  }
+  MB_REQUIRE(ch.S != 0, MB_ERR_UNSUPPORTED, "skinny_gemm_tc_chord_tail: no split of K1 = %lld, K2 = %lld fits",
+             (long long)K1, (long long)K2);
+  CUtensorMap tmW, tmX, tmW2, tmX2;
+  int rc = encode_tile_map_2d(&tmW, w1, 2, (uint64_t)K1, (uint64_t)N, (uint64_t)ldw1 * 2, kTcBK, kTcF, 128);
+  if (!rc) rc = encode_tile_map_2d(&tmX, x1, 2, (uint64_t)K1, (uint64_t)M, (uint64_t)ldx1 * 2, kTcBK, kTcTok, 128);
+  if (!rc) rc = encode_tile_map_2d(&tmW2, w2, 2, (uint64_t)K2, (uint64_t)N, (uint64_t)ldw2 * 2, kTcBK, kTcF, 128);
+  if (!rc) rc = encode_tile_map_2d(&tmX2, x2, 2, (uint64_t)K2, (uint64_t)M, (uint64_t)ldx2 * 2, kTcBK, kTcTok, 128);
+  if (rc) return rc;
+  auto go = [&](auto t) -> int {
+    using T = decltype(t);
+    auto kern = skinny_tc_kernel<T>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = (unsigned)ch.S;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)ch.S);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = ch.bytes;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt1, ch.kbc, ch.R, (const T*)nullptr,
+                       (int64_t)0, (const T*)g, ldg, tmW2, tmX2, kbt2, S1);
+    return check_launch("skinny_gemm_tc_chord_tail");
+  };
+  return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
 }

@@ -33,7 +33,7 @@ import torch
 from . import _lib
 from .cache import GatedDeltaAttentionLayerCache, KVLayerCache, ModelCache
 from .config import GGD_EPS, NORM_EPS
-from .model import _decode_splits, _down_add_gated, _mm, _norm_read
+from .model import _chord_tail, _decode_splits, _down_add_gated, _mm, _norm_read
 
 __all__ = ['GraphDecoder', 'fill_cache_random']
 
@@ -251,8 +251,12 @@ class GraphDecoder:
         _lib.call('motif_b200_chord_decode', _lib.ptr(qb), _lib.ptr(lc._kbuf), _lib.ptr(lc._vbuf), cap,
                   lens_ptr + 4, 0, _lib.ptr(pk.alpha), _lib.ptr(pk.beta), _lib.ptr(pk.mu), _lib.ptr(pk.ssmax),
                   _lib.ptr(attn), d, B, H, Hkv, 1, D, D ** -0.5, GGD_EPS, self.splits, _lib.ptr(ws), ws_bytes, dc, st)
+        gate = proj[:, pk.off_g:pk.off_g + d]
+        f = _chord_tail(attn, pk.w_o, act, pk.w_down, gate)
+        if f is not None:  # o_proj, down_proj and the gated residual in one launch
+            return f
         a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
-        f = _down_add_gated(act, pk.w_down, a, proj[:, pk.off_g:pk.off_g + d])
+        f = _down_add_gated(act, pk.w_down, a, gate)
         if f is not None:  # the gated residual in the down projection's epilogue
             return f
         f = _mm(act, pk.w_down, wp=pk.w_down_sk)

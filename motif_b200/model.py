@@ -620,6 +620,34 @@ def _down_add_gated(act: torch.Tensor, w_down: torch.Tensor, a: torch.Tensor,
     return y
 
 
+# Decode-sized Chord decoders run their o_proj, down_proj and gated residual as one launch
+# (motif_b200_skinny_gemm_tc_chord_tail).
+CHORD_TAIL_ONE_LAUNCH = True
+
+
+def _chord_tail(attn: torch.Tensor, w_o: torch.Tensor, act: torch.Tensor, w_down: torch.Tensor,
+                gate: torch.Tensor) -> Optional[torch.Tensor]:
+    """The Chord decoder's `o_proj(out) * sigmoid(g) + down_proj(act)` (`chord_attn.py:254,313`,
+    `mlp.py:63`, `decoder.py:208`) for decode-sized batches as ONE launch on the tensor-core decode
+    GEMM; None when that kernel does not take the shapes."""
+    M, K1 = attn.shape
+    K2 = act.shape[1]
+    N = w_o.shape[0]
+    ts = (attn, w_o, act, w_down)
+    if not (CHORD_TAIL_ONE_LAUNCH and 0 < M <= SKINNY_TC_MAX_M and act.shape[0] == M and w_down.shape[0] == N
+            and attn.dtype in (torch.bfloat16, torch.float16) and all(t.dtype == attn.dtype for t in ts + (gate,))
+            and K1 % 64 == 0 and K2 % 64 == 0 and N % 4 == 0 and w_o.shape[1] == K1 and w_down.shape[1] == K2
+            and all(t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0 for t in ts)
+            and gate.shape == (M, N) and gate.stride(1) == 1 and gate.stride(0) % 4 == 0 and gate.data_ptr() % 8 == 0):
+        return None
+    y = torch.empty((M, N), dtype=attn.dtype, device=attn.device)
+    _lib.call('motif_b200_skinny_gemm_tc_chord_tail', attn.data_ptr(), attn.stride(0), w_o.data_ptr(), w_o.stride(0),
+              K1, act.data_ptr(), act.stride(0), w_down.data_ptr(), w_down.stride(0), K2, gate.data_ptr(),
+              gate.stride(0), y.data_ptr(), y.stride(0), M, N, _lib.dtype_code(attn.dtype),
+              _lib.stream_ptr(attn.device))
+    return y
+
+
 def _tc_ok(*ts: torch.Tensor) -> bool:
     """The tcgen05 projection kernels take 16-bit operands with 16-byte aligned rows and K a
     multiple of 64; fp32 (the parity mode) stays on the library GEMM."""
@@ -903,7 +931,10 @@ def _chord_decoder(model, pk: _ChordPack, hn, B, T, cache: Optional[KVLayerCache
                   N_in, hid, dc, st)
     gate = proj[:, pk.off_g:pk.off_g + d]
     a = None
-    if not fused_proj:  # decode-sized: o_proj first, then down_proj with the gated residual fused
+    if not fused_proj:  # decode-sized: the whole tail in one launch, else o_proj then down + residual
+        f = _chord_tail(attn, pk.w_o, act, pk.w_down, gate)
+        if f is not None:
+            return f
         a = _mm(attn, pk.w_o, wp=pk.w_o_sk)
         f = _down_add_gated(act, pk.w_down, a, gate)
         if f is not None:

@@ -189,3 +189,39 @@ def test_skinny_tc_add_gated_rejects_misaligned_gate():
     with pytest.raises(ValueError, match='aligned'):  # the gate starts 2 bytes past an 8-byte boundary
         _lib.call('motif_b200_skinny_gemm_tc_add_gated', x.data_ptr(), 2048, w.data_ptr(), 2048, a.data_ptr(), 768,
                   proj.data_ptr() + 2, 6016, y.data_ptr(), 768, 64, 768, 2048, 0, _lib.MB_BF16, st())
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize('M', [64, 33, 8, 1])
+def test_skinny_tc_chord_tail(dtype, M):
+    """The Chord decoder's tail in one launch, y = o_proj(attn) * sigmoid(g) + down_proj(act) with
+    the unfused path's rounding points, against the fp32 products rounded where the separate
+    kernels round (each product within one 16-bit rounding plus a summation-order term), on
+    two calls in a row that give the same bits."""
+    N, K1, K2, N_in, off_g = 768, 768, 2048, 6016, 1152
+    g = torch.Generator().manual_seed(M + 5)
+    x1 = torch.randn(M, K1, generator=g).to(dtype).cuda()
+    w1 = (K1 ** -0.5 * torch.randn(N, K1, generator=g)).to(dtype).cuda()
+    x2 = torch.randn(M, K2, generator=g).to(dtype).cuda()
+    w2 = (K2 ** -0.5 * torch.randn(N, K2, generator=g)).to(dtype).cuda()
+    proj = (2 * torch.randn(M, N_in, generator=g)).to(dtype).cuda()
+    gate = proj[:, off_g:off_g + N]
+    outs = []
+    for _ in range(2):
+        y = torch.full((M, N), float('nan'), dtype=dtype, device='cuda')
+        _lib.call('motif_b200_skinny_gemm_tc_chord_tail', x1.data_ptr(), K1, w1.data_ptr(), K1, K1, x2.data_ptr(), K2,
+                  w2.data_ptr(), K2, K2, gate.data_ptr(), N_in, y.data_ptr(), N, M, N, _lib.dtype_code(dtype), st())
+        torch.cuda.synchronize()
+        outs.append(y)
+    assert torch.equal(outs[0], outs[1])
+    p1 = x1.float() @ w1.float().t()
+    p2 = x2.float() @ w2.float().t()
+    sg = torch.sigmoid(gate.float()).to(dtype).float()
+    att = (p1.to(dtype).float() * sg).to(dtype).float()
+    mlp = p2.to(dtype).float()
+    ref = att + mlp
+    err = (outs[0].float() - ref).abs()
+    # a few 16-bit roundings of each part (the sum may cancel, so the bound follows the parts)
+    tol = 2.0 ** -6 * (att.abs() + mlp.abs()) + 1e-3
+    assert bool((err <= tol).all()), err.max().item()
+    assert _lib.wait_timeouts() == 0
