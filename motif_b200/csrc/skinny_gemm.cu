@@ -777,6 +777,36 @@ int tc_max_clusters(const void* kern, int S, size_t bytes) {
   return n;
 }
 
+// One launch of skinny_tc_kernel: `tiles` feature tiles x ch.S cluster ranks (a cluster along
+// y), programmatic dependent launch allowed.  Product 2 (tmW2, tmX2, kbt2) runs on ranks
+// [S1, ch.S); with S1 == ch.S there is one product.
+int launch_tc(int dtype, const TcChoice& ch, int tiles, void* stream, const CUtensorMap& tmW, const CUtensorMap& tmX,
+              void* y, int64_t ldy, int64_t M, int64_t N, int kbt, const void* ga, int64_t lda, const void* gg,
+              int64_t ldg, const CUtensorMap& tmW2, const CUtensorMap& tmX2, int kbt2, int S1, const char* what) {
+  auto go = [&](auto t) -> int {
+    using T = decltype(t);
+    auto kern = skinny_tc_kernel<T>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = (unsigned)ch.S;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)ch.S);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = ch.bytes;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt, ch.kbc, ch.R, (const T*)ga, lda,
+                       (const T*)gg, ldg, tmW2, tmX2, kbt2, S1);
+    return check_launch(what);
+  };
+  return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+}
+
 int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int64_t M,
                      int64_t N, int64_t K, int split_k, int dtype, void* stream, const void* ga = nullptr,
                      int64_t lda = 0, const void* gg = nullptr, int64_t ldg = 0) {
@@ -844,28 +874,8 @@ int skinny_tc_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, voi
   int rc = encode_tile_map_2d(&tmW, w, 2, (uint64_t)K, (uint64_t)N, (uint64_t)ldw * 2, kTcBK, kTcF, 128);
   if (!rc) rc = encode_tile_map_2d(&tmX, x, 2, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, kTcBK, kTcTok, 128);
   if (rc) return rc;
-  auto go = [&](auto t) -> int {
-    using T = decltype(t);
-    auto kern = skinny_tc_kernel<T>;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = (unsigned)ch.S;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)tiles, (unsigned)ch.S);
-    cfg.blockDim = dim3(kTcThreads);
-    cfg.dynamicSmemBytes = ch.bytes;
-    cfg.stream = (cudaStream_t)stream;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt, ch.kbc, ch.R, (const T*)ga, lda,
-                       (const T*)gg, ldg, tmW, tmX, 0, ch.S);
-    return check_launch("skinny_gemm_tc");
-  };
-  return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+  return launch_tc(dtype, ch, tiles, stream, tmW, tmX, y, ldy, M, N, kbt, ga, lda, gg, ldg, tmW, tmX, 0, ch.S,
+                   "skinny_gemm_tc");
 }
 
 }  // namespace
@@ -944,26 +954,6 @@ extern "C" int motif_b200_skinny_gemm_tc_chord_tail(const void* x1, int64_t ldx1
   if (!rc) rc = encode_tile_map_2d(&tmW2, w2, 2, (uint64_t)K2, (uint64_t)N, (uint64_t)ldw2 * 2, kTcBK, kTcF, 128);
   if (!rc) rc = encode_tile_map_2d(&tmX2, x2, 2, (uint64_t)K2, (uint64_t)M, (uint64_t)ldx2 * 2, kTcBK, kTcTok, 128);
   if (rc) return rc;
-  auto go = [&](auto t) -> int {
-    using T = decltype(t);
-    auto kern = skinny_tc_kernel<T>;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = (unsigned)ch.S;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)tiles, (unsigned)ch.S);
-    cfg.blockDim = dim3(kTcThreads);
-    cfg.dynamicSmemBytes = ch.bytes;
-    cfg.stream = (cudaStream_t)stream;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    cudaLaunchKernelEx(&cfg, kern, tmW, tmX, (T*)y, ldy, (int)M, (int)N, kbt1, ch.kbc, ch.R, (const T*)nullptr,
-                       (int64_t)0, (const T*)g, ldg, tmW2, tmX2, kbt2, S1);
-    return check_launch("skinny_gemm_tc_chord_tail");
-  };
-  return dtype == MB_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+  return launch_tc(dtype, ch, tiles, stream, tmW, tmX, y, ldy, M, N, kbt1, nullptr, 0, g, ldg, tmW2, tmX2, kbt2, S1,
+                   "skinny_gemm_tc_chord_tail");
 }
